@@ -1,0 +1,298 @@
+"""Benchmark of the qwen35moe MoE hot path on B200.
+
+Default workload: decode of one token through 40 stacked MoE layers of the config-0
+shapes (H 2048, 256 experts of FFN 512, top-8, Q4_K gate/up + Q6_K down, shared expert), residual + RMSNorm
+between layers, all 20.9 GB of expert weights resident in HBM. One step = one token through the 40 layers.
+Metric: tokens/s; the roofline line reports the expert-weight HBM bandwidth against the measured copy peak.
+At N > 1 GPUs (torchrun) every rank serves its own token stream with its own full store (decode does not shard:
+"replicas only"), value = total tokens/s over all ranks, time = max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode40|prefill4096]
+
+--impl reference times the CPU restatement of willow's own CPU path (the oracle port; willow's code cannot run
+on the GPU box) on the host cores, on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+HIDDEN, FFN, EXPERTS, TOP_K = 2048, 512, 256, 8
+EXPERT_BYTES = 2 * FFN * HIDDEN // 256 * 144 + HIDDEN * FFN // 256 * 210   # 2,039,808
+ROUTER_BYTES = EXPERTS * HIDDEN * 4 + HIDDEN * 4                           # router + shared gate, fp32
+LAYERS = 40
+SEED = 0
+METRIC = "MoE decode tokens/s (40-layer qwen35moe stack, 1 token per step)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def setup_model(device: int):
+    """The 40-layer model on the GPU: synthetic routed experts generated in HBM, router/shared weights uploaded."""
+    import torch
+    from willow_v2_b200 import moe, synth
+    ctx = moe.Context(device)
+    store = moe.ExpertStore(LAYERS, EXPERTS, HIDDEN, FFN, ctx=ctx)
+    store.fill_synthetic(SEED)
+    layers = []
+    for l in range(LAYERS):
+        layers.append(moe.LayerWeights(
+            router_w=torch.from_numpy(synth.router_weight(SEED, l)).cuda(),
+            shared_gate=torch.from_numpy(synth.shared_gate_weight(SEED, l)).cuda(),
+            shared_gate_up=torch.from_numpy(synth.expert_gate_up(SEED, l, EXPERTS).reshape(-1)).cuda(),
+            shared_down=torch.from_numpy(synth.expert_down(SEED, l, EXPERTS).reshape(-1)).cuda()))
+    torch.cuda.synchronize()
+    return ctx, store, layers
+
+
+def run_decode40(args, rank: int, world: int, dist):
+    import torch
+    from willow_v2_b200 import moe, synth
+    device = torch.cuda.current_device()
+    ctx, store, layers = setup_model(device)
+    K, W = args.steps, args.warmup
+    # a new token per step (different routing every step); inputs resident before the timed region
+    h_all = torch.from_numpy(np.concatenate([synth.hidden(SEED + 1000 * rank, 1, step=s) for s in range(K + W)])).cuda()
+    out = torch.empty(HIDDEN, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    for s in range(W):
+        moe.decode_stack(store, layers, h_all[s], 1e-6, out=out)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        ev0.record(stream)
+        for s in range(K):
+            moe.decode_stack(store, layers, h_all[W + s], 1e-6, out=out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    gpu_launches = ctx.launches - launches0
+    ms = ev0.elapsed_time(ev1) / K
+    ctx.check_device()
+
+    # end to end through the public API: pinned host input -> device, decode, result -> pinned host, every step
+    h_host = torch.from_numpy(np.concatenate([synth.hidden(SEED + 7 + 1000 * rank, 1, step=s) for s in range(K)])).pin_memory()
+    o_host = torch.empty(K, HIDDEN, dtype=torch.float32).pin_memory()
+    h_dev = torch.empty(HIDDEN, dtype=torch.float32, device="cuda")
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(K):
+        h_dev.copy_(h_host[s], non_blocking=True)
+        moe.decode_stack(store, layers, h_dev, 1e-6, out=out)
+        o_host[s].copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+
+    times = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = times.tolist()
+    hbm, _, peak_kind = peaks()
+    expert_bytes = LAYERS * (TOP_K + 1) * EXPERT_BYTES
+    achieved = expert_bytes / (ms * 1e-3) / 1e9
+    result = {
+        "metric": METRIC, "value": world * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks with the config-0 distributions; random-init router)",
+        "config": {"workload": "configs[1]: decode 1 token x 40 MoE layers, all experts resident", "hidden": HIDDEN,
+                   "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": LAYERS, "tokens_per_step": 1,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: 734 MB of expert weights per step, a new token (new routing) each step"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": expert_bytes,
+                     "frac_of_8TBps": achieved / 8000.0,
+                     "all_bytes_per_launch": expert_bytes + LAYERS * ROUTER_BYTES},
+        "e2e": {"value": world * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": HIDDEN * 4,
+                "d2h_bytes_per_step": HIDDEN * 4},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks.summary(),
+    }
+    return result, (ctx, store, layers)
+
+
+def cpu_baseline(sample_layers: int = 2):
+    """willow's CPU path restated (the oracle port) timed on the host cores: dequantise the token's routed and
+    shared experts from their GGUF bytes and run route / expert FFN / combine in float32, one layer at a time.
+    Returns tokens/s scaled to the 40-layer token from the sampled layers."""
+    import oracle.moe_oracle as ora
+    from willow_v2_b200 import synth
+    h = synth.hidden(SEED, 1, step=123)
+    total = 0.0
+    for l in range(sample_layers):
+        x = ora.rms_norm(h)
+        router = synth.router_weight(SEED, l)
+        sel = ora.route(x @ router.T)[1][0]
+        raw = {int(e): (synth.expert_gate_up(SEED, l, int(e)), synth.expert_down(SEED, l, int(e)))
+               for e in list(sel) + [EXPERTS]}  # bytes as the store would hold them (not timed)
+        gate = synth.shared_gate_weight(SEED, l)
+
+        def experts(e):
+            gu, dn = raw[e]
+            return ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN)), ora.dequantize(dn, "Q6_K", (HIDDEN, FFN))
+
+        t0 = time.perf_counter()
+        out = ora.moe(x, router, experts, experts(EXPERTS), gate)[0]
+        total += time.perf_counter() - t0
+        h = h + out
+    per_layer = total / sample_layers
+    return {"value": 1.0 / (per_layer * LAYERS), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{sample_layers} of the 40 layers of one decode token (dequantise 9 experts + route + FFN + "
+                      f"combine per layer, float32 numpy), scaled to 40 layers"}
+
+
+def run_reference(args, rank, world):
+    """The reference arm: the CPU restatement of willow's CPU path on the host cores, rank 0 only."""
+    if rank != 0:
+        return None
+    import oracle.moe_oracle as ora
+    from willow_v2_b200 import synth
+    K, W = args.steps, args.warmup
+    # each step: one layer's router + top-k on a new token, then one of that layer's 9 experts (8 routed + shared)
+    # dequantised from its GGUF bytes and run; a token = 40 x (router + 9 experts)
+    t_route, t_expert = [], []
+    routers = [synth.router_weight(SEED, l) for l in range(LAYERS)]
+    for s in range(W + K):
+        layer = s % LAYERS
+        x = ora.rms_norm(synth.hidden(SEED, 1, step=10_000 + s))
+        t0 = time.perf_counter()
+        w, sel = ora.route(x @ routers[layer].T)
+        t1 = time.perf_counter()
+        e = int(sel[0, s % TOP_K]) if s % (TOP_K + 1) != TOP_K else EXPERTS
+        gu, dn = synth.expert_gate_up(SEED, layer, e), synth.expert_down(SEED, layer, e)  # the store's bytes
+        t2 = time.perf_counter()
+        y = ora.expert_gate(x @ ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN)).T) @ ora.dequantize(dn, "Q6_K", (HIDDEN, FFN)).T
+        y = y * w[0, 0]
+        t3 = time.perf_counter()
+        if s >= W:
+            t_route.append(t1 - t0)
+            t_expert.append(t3 - t2)
+    sec = LAYERS * (statistics.mean(t_route) + (TOP_K + 1) * statistics.mean(t_expert))
+    value = 1.0 / sec
+    return {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "configs[1]: decode 1 token x 40 MoE layers", "hidden": HIDDEN, "experts": EXPERTS,
+                       "ffn": FFN, "top_k": TOP_K, "layers": LAYERS},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": "each step: one layer's router + top-8 and one of its 9 experts dequantised "
+                                       "from GGUF bytes and run (numpy float32); token time = 40 x (router + "
+                                       "9 x expert)"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode40", choices=["decode40"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as d
+        d.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                             device_id=torch.device("cuda", local))
+        dist = d
+    result, _keep = run_decode40(args, rank, world, dist)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * wmoe.h - C ABI of libwmoe.so, the B200 (sm_100a) MoE block of willow's qwen35moe engine.
+ *
+ * Plain C: device pointers, sizes and a CUDA stream passed as void*. Every function returns WMOE_OK (0) or a
+ * negative WMOE_ERR_* code; wmoe_last_error() gives the message of the last failure on a context. Nothing
+ * aborts or exits. A context is used from one host thread.
+ *
+ * Each entry point names the willow interface it replaces (paths within the willow-v2 project):
+ *   wmoe_dequant             gguf/quants.py:207-227 dequantize (Q4_K 73-92, Q6_K 104-116);
+ *                            gguf/metal.py:217-228,357-363 dequant_<type> / dequantize_gpu
+ *   wmoe_route               engines/base.py:91-97 route (+ the router linear, base.py:305-306,448,
+ *                            and the shared-expert gate of base.py:104-107)
+ *   wmoe_dispatch            engines/base.py:456-467,555-566 (selected.cpu / unique / nonzero grouping),
+ *                            gguf/store.py:482-484 record_usage
+ *   wmoe_moe_forward         engines/base.py:445-490 Engine.moe (each_expert 534-591,
+ *                            batched_decode_experts 492-532, combine_decode_experts 431-443)
+ *   wmoe_decode_stack        engines/qwen36/model.py:17-22 MoEEngine.forward's per-layer
+ *                            x + moe(rms_norm(x)) for one decode token, all layers in one launch
+ *   wmoe_store_*             gguf/store.py:41-536 ExpertStore (slabs, LRU, load_batches, prefetch,
+ *                            record_usage) and gguf/mps_shared.mm:10-20 shared_empty (host staging)
+ *   wmoe_gemv_batch          gguf/metal.py:239-261,336-343 gemv_batch (several experts x one token)
+ */
+#ifndef WMOE_H
+#define WMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WMOE_OK 0
+#define WMOE_ERR_INVALID (-1)     /* bad argument (null pointer, shape, dtype, alignment) */
+#define WMOE_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define WMOE_ERR_CAPACITY (-3)    /* the expert store's cap cannot hold what one call needs */
+#define WMOE_ERR_DEVICE (-4)      /* a kernel reported a bad index or a wait that ran out (device status) */
+#define WMOE_ERR_UNSUPPORTED (-5) /* shape or type this build has no kernel for */
+#define WMOE_ERR_IO (-6)          /* a host-side copy into the store failed or was short */
+
+/* element types of activations */
+#define WMOE_F32 0
+#define WMOE_BF16 1
+#define WMOE_F16 2
+
+/* ggml type ids (gguf/reader.py:14-48) */
+#define WMOE_GGML_Q4_K 12
+#define WMOE_GGML_Q6_K 14
+
+typedef struct wmoe_ctx wmoe_ctx;
+typedef struct wmoe_store wmoe_store;
+
+/* ---- context ---------------------------------------------------------------------------------------- */
+
+/* Creates a context on a CUDA device (made current). Owns scratch buffers, grown on demand. */
+int wmoe_init(int device, wmoe_ctx** out);
+void wmoe_destroy(wmoe_ctx* ctx);
+const char* wmoe_last_error(const wmoe_ctx* ctx);
+/* Number of kernels this context has launched so far (for benchmark accounting). */
+uint64_t wmoe_launch_count(const wmoe_ctx* ctx);
+/* enable = 1 (default): wmoe_moe_forward runs single-token calls on an uncapped store with the persistent
+ * decode kernel; 0: with the multi-launch GEMV path. Returns the previous setting. */
+int wmoe_set_decode_kernel(wmoe_ctx* ctx, int enable);
+/* Reads and clears the device status word: 0, or the first WMOE_ERR_DEVICE cause a kernel recorded
+ * (1 = expert id out of range, 2 = expert not resident, 3 = grid barrier timed out, 4 = bad segment). */
+int wmoe_device_status(wmoe_ctx* ctx, int* status, void* stream);
+
+/* ---- quantised weights ------------------------------------------------------------------------------ */
+
+/* Dequantises nblocks ggml super-blocks (Q4_K: 144 B, Q6_K: 210 B each, 256 values) to out_dtype.
+ * F32 output is bit-identical to gguf/quants.py:dequantize; BF16/F16 are that value rounded to nearest even. */
+int wmoe_dequant(wmoe_ctx* ctx, int ggml_type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype,
+                 void* stream);
+
+/* ---- router ----------------------------------------------------------------------------------------- */
+
+/* logits = x . router_w^T (+ router_bias); softmax over experts, top_k largest, renormalised to sum 1
+ * (norm_topk_prob); shared_s = sigmoid(x . shared_gate) when shared_gate is not null.
+ * x: [T, hidden] of x_dtype. router_w: f32 [experts, hidden]. Outputs: topk_w f32 [T, top_k],
+ * topk_idx int32 [T, top_k] (descending weight), shared_s f32 [T] (nullable), logits f32 [T, experts]
+ * (nullable). */
+int wmoe_route(wmoe_ctx* ctx, const void* x, int x_dtype, int T, int hidden, int experts, int top_k,
+               const float* router_w, const float* router_bias, const float* shared_gate, float* topk_w,
+               int32_t* topk_idx, float* shared_s, float* logits, void* stream);
+
+/* Groups the T*top_k (token, slot) picks by expert, stably in token order: counts int32 [experts],
+ * offsets int32 [experts + 1], perm int32 [T*top_k] (token*top_k + slot, expert-major), usage (nullable)
+ * int64 [experts] += counts. */
+int wmoe_dispatch(wmoe_ctx* ctx, const int32_t* topk_idx, int T, int top_k, int experts, int32_t* counts,
+                  int32_t* offsets, int32_t* perm, int64_t* usage, void* stream);
+
+/* ---- expert store ----------------------------------------------------------------------------------- */
+
+/* An HBM store of layers x experts expert blobs (gate_up bytes then down bytes, the pack layout of
+ * gguf/compiler.py:139-197). cap_bytes = 0: every blob resident. Otherwise at most cap_bytes of device slots;
+ * blobs live in pinned host memory and are copied in on a side stream, least recently used evicted first.
+ * gate_up is Q4_K [2*ffn, hidden]; down is Q6_K [hidden, ffn]. */
+int wmoe_store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, size_t cap_bytes,
+                      wmoe_store** out);
+void wmoe_store_destroy(wmoe_store* store);
+/* Copies one blob (gate_up then down, size wmoe_store_blob_bytes) from host memory into the store. */
+int wmoe_store_upload(wmoe_store* store, int layer, int expert, const void* host_src, void* stream);
+/* Generates every blob of layers [layer_begin, layer_end) on the device from a seed (the generator of
+ * willow_v2_b200/synth.py), in the store's resident slots or its host copy when capped. */
+int wmoe_store_fill_synthetic(wmoe_store* store, uint64_t seed, int layer_begin, int layer_end, void* stream);
+size_t wmoe_store_blob_bytes(const wmoe_store* store);
+/* Makes the given experts of a layer resident (copies misses from the host copy on the store's side stream;
+ * the compute stream waits for them). Returns WMOE_ERR_CAPACITY if they cannot all fit at once. */
+int wmoe_store_prepare(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream);
+/* Copies one blob back to host memory (from its slot, or the host copy of a capped store); synchronous. */
+int wmoe_store_download(wmoe_store* store, int layer, int expert, void* host_dst, void* stream);
+/* Device address of a resident blob, or null. */
+const uint8_t* wmoe_store_blob(const wmoe_store* store, int layer, int expert);
+/* Counters: hits, misses (copies), bytes copied host->device, evictions. */
+int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, uint64_t* bytes_in,
+                     uint64_t* evictions);
+
+/* ---- the MoE block ---------------------------------------------------------------------------------- */
+
+/* One MoE block on T tokens: out = sum over each token's top_k experts (ascending expert id) of
+ * w * down(silu(gate x) * up x), plus sigmoid(x . shared_gate) * shared(x).
+ * x: [T, hidden] (x_dtype F32 or BF16). router_w f32 [experts, hidden]; router_bias f32 [experts] (nullable);
+ * shared_gate f32 [hidden]; shared_gate_up / shared_down: the shared expert's Q4_K / Q6_K bytes on the device.
+ * out: [T, hidden] of out_dtype (F32 or BF16). topk_idx_out int32 [T, top_k] and topk_w_out f32 [T, top_k]
+ * are optional copies of the routing. Routed experts come from the store (all must be resident, or the store
+ * must be able to stream them: capped stores synchronise on the routing once per call). */
+int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                     const float* router_w, const float* router_bias, const float* shared_gate,
+                     const uint8_t* shared_gate_up, const uint8_t* shared_down, void* out, int out_dtype,
+                     int32_t* topk_idx_out, float* topk_w_out, void* stream);
+
+/* Per-layer weights of a decode stack, in device memory: one entry per layer. */
+typedef struct wmoe_layer_weights {
+    const float* router_w;          /* f32 [experts, hidden] */
+    const float* router_bias;       /* f32 [experts] or null */
+    const float* shared_gate;       /* f32 [hidden] */
+    const uint8_t* shared_gate_up;  /* Q4_K [2*ffn, hidden] */
+    const uint8_t* shared_down;     /* Q6_K [hidden, ffn] */
+} wmoe_layer_weights;
+
+/* One decode token through layers [layer_begin, layer_begin + n_layers) of the store:
+ * h <- h + moe_l(rms_norm(h)) per layer (eps, unit weight), in one persistent launch per 64 layers.
+ * h_in / h_out: f32 [hidden] on the device (may alias). layers: HOST array of n_layers entries whose pointers
+ * are device pointers. topk_idx_out: optional int32 [n_layers, top_k]. Needs every routed expert resident
+ * (cap 0). */
+int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
+                      const wmoe_layer_weights* layers, float eps, const float* h_in, float* h_out,
+                      int32_t* topk_idx_out, void* stream);
+
+/* Several experts' [rows, k] Q4_K or Q6_K weights times one token: y[i] = W_i x for i < n.
+ * weights: device array of n device pointers; x f32 [k]; y f32 [n, rows]. */
+int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, int n, int rows, int k,
+                    const float* x, float* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WMOE_H */

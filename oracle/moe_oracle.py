@@ -88,7 +88,8 @@ def route(logits: np.ndarray, top_k: int = 8, normalize: bool = True):
 
 
 def silu(x: np.ndarray) -> np.ndarray:
-    return x / (np.float32(1) + np.exp(-x))
+    with np.errstate(over="ignore"):  # exp(-x) -> inf for very negative x gives the right limit, -0
+        return x / (np.float32(1) + np.exp(-x))
 
 
 def expert_gate(gate_up: np.ndarray) -> np.ndarray:
@@ -98,7 +99,8 @@ def expert_gate(gate_up: np.ndarray) -> np.ndarray:
 
 
 def sigmoid(x: np.ndarray) -> np.ndarray:
-    return np.float32(1) / (np.float32(1) + np.exp(-x))
+    with np.errstate(over="ignore"):
+        return np.float32(1) / (np.float32(1) + np.exp(-x))
 
 
 def shared_expert(x, gate_w, up_w, down_w, shared_gate_w):

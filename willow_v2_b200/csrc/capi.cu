@@ -1,0 +1,403 @@
+// The C ABI of include/wmoe.h: argument checks, scratch planning and the order of launches. Kernels live in
+// dequant.cu, route.cu, dispatch.cu, gemv.cu, decode.cu and store.cu.
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "../../include/wmoe.h"
+#include "common.cuh"
+#include "kernels.cuh"
+#include "store.h"
+
+using namespace wmoe;
+
+int ctx_fail(wmoe_ctx* ctx, int code, const std::string& msg) {
+  if (ctx) ctx->error = msg;
+  return code;
+}
+
+void ctx_count_launch(wmoe_ctx* ctx, int n) {
+  if (ctx) ctx->launches += uint64_t(n);
+}
+
+static int cuda_fail(wmoe_ctx* ctx, cudaError_t e, const char* where) {
+  return ctx_fail(ctx, WMOE_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+#define WMOE_CHECK_CUDA(ctx, expr, where)              \
+  do {                                                 \
+    const cudaError_t e_ = (expr);                     \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_, where); \
+  } while (0)
+
+// Bump allocator over the context's scratch buffer (256-byte aligned pieces).
+struct Plan {
+  size_t bytes = 0;
+  template <typename T>
+  size_t take(size_t count) {
+    const size_t off = bytes;
+    bytes += (count * sizeof(T) + 255) / 256 * 256;
+    return off;
+  }
+};
+
+static int ensure_scratch(wmoe_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->scratch_bytes) return WMOE_OK;
+  if (ctx->scratch) {
+    WMOE_CHECK_CUDA(ctx, cudaDeviceSynchronize(), "scratch resize");
+    cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+  }
+  const size_t grown = std::max(bytes, size_t(1) << 20);
+  WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->scratch, grown), "scratch allocation");
+  ctx->scratch_bytes = grown;
+  return WMOE_OK;
+}
+
+template <typename T>
+static T* at(wmoe_ctx* ctx, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(ctx->scratch) + off);
+}
+
+extern "C" {
+
+int wmoe_init(int device, wmoe_ctx** out) {
+  if (!out) return WMOE_ERR_INVALID;
+  *out = nullptr;
+  auto* ctx = new wmoe_ctx();
+  ctx->device = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    delete ctx;
+    return WMOE_ERR_CUDA;
+  }
+  ctx->decode_ctas = decode_num_ctas(device);
+  *out = ctx;
+  return WMOE_OK;
+}
+
+void wmoe_destroy(wmoe_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  cudaFree(ctx->scratch);
+  cudaFree(ctx->d_status);
+  delete ctx;
+}
+
+const char* wmoe_last_error(const wmoe_ctx* ctx) { return ctx ? ctx->error.c_str() : "null context"; }
+
+uint64_t wmoe_launch_count(const wmoe_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int wmoe_set_decode_kernel(wmoe_ctx* ctx, int enable) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  const int prev = ctx->use_decode_kernel ? 1 : 0;
+  ctx->use_decode_kernel = enable != 0;
+  return prev;
+}
+
+int wmoe_device_status(wmoe_ctx* ctx, int* status, void* stream) {
+  if (!ctx || !status) return WMOE_ERR_INVALID;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(&v, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, st), "status read");
+  WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "status read");
+  WMOE_CHECK_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, sizeof(int), st), "status clear");
+  *status = v;
+  return WMOE_OK;
+}
+
+int wmoe_dequant(wmoe_ctx* ctx, int ggml_type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype,
+                 void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (ggml_type != WMOE_GGML_Q4_K && ggml_type != WMOE_GGML_Q6_K)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_dequant: only Q4_K and Q6_K are supported");
+  if (out_dtype != WMOE_F32 && out_dtype != WMOE_BF16 && out_dtype != WMOE_F16)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_dequant: bad output dtype");
+  if (nblocks && (!blocks || !out)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_dequant: null pointer");
+  WMOE_CHECK_CUDA(ctx, dequant(ggml_type, blocks, nblocks, out, out_dtype, static_cast<cudaStream_t>(stream)),
+                  "wmoe_dequant");
+  ctx->launches += nblocks ? 1 : 0;
+  return WMOE_OK;
+}
+
+int wmoe_route(wmoe_ctx* ctx, const void* x, int x_dtype, int T, int hidden, int experts, int top_k,
+               const float* router_w, const float* router_bias, const float* shared_gate, float* topk_w,
+               int32_t* topk_idx, float* shared_s, float* logits, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (T < 0 || hidden <= 0 || hidden % 128 || experts <= 0 || experts > 512 || top_k <= 0 || top_k > 32 ||
+      top_k > experts)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_route: bad shape");
+  if (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_route: bad dtype");
+  if (T == 0) return WMOE_OK;
+  if (!x || !router_w || !topk_w || !topk_idx || (shared_s && !shared_gate))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_route: null pointer");
+  Plan plan;
+  const size_t o_logits = plan.take<float>(size_t(T) * (experts + 1));
+  if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int n = 0;
+  float* lg = at<float>(ctx, o_logits);
+  WMOE_CHECK_CUDA(ctx, router_logits(x, x_dtype, T, hidden, experts, router_w, shared_gate, lg, st, &n), "router");
+  WMOE_CHECK_CUDA(ctx, router_topk(lg, T, experts, top_k, router_bias, topk_w, topk_idx, shared_s, logits, st, &n),
+                  "top-k");
+  ctx->launches += uint64_t(n);
+  return WMOE_OK;
+}
+
+int wmoe_dispatch(wmoe_ctx* ctx, const int32_t* topk_idx, int T, int top_k, int experts, int32_t* counts,
+                  int32_t* offsets, int32_t* perm, int64_t* usage, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (T < 0 || top_k <= 0 || experts <= 0 || experts > 992) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_dispatch: bad shape");
+  if (!counts || !offsets || (T > 0 && (!topk_idx || !perm)))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_dispatch: null pointer");
+  Plan plan;
+  const size_t o_disp = plan.bytes;
+  plan.bytes += (dispatch_scratch_bytes(T, experts) + 255) / 256 * 256;
+  const size_t o_pos = plan.take<int32_t>(size_t(T) * top_k + 1);
+  const size_t o_used = plan.take<int32_t>(size_t(experts) + 1);
+  const size_t o_seg = plan.take<int32_t>(size_t(experts) + 2);
+  const size_t o_nused = plan.take<int32_t>(1);
+  if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
+  int n = 0;
+  WMOE_CHECK_CUDA(ctx,
+                  dispatch(topk_idx, T, top_k, experts, at<void>(ctx, o_disp), counts, offsets, perm,
+                           at<int32_t>(ctx, o_pos), at<int32_t>(ctx, o_used), at<int32_t>(ctx, o_seg),
+                           at<int32_t>(ctx, o_nused), usage, ctx->d_status, static_cast<cudaStream_t>(stream), &n),
+                  "wmoe_dispatch");
+  ctx->launches += uint64_t(n);
+  return WMOE_OK;
+}
+
+int wmoe_store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, size_t cap_bytes,
+                      wmoe_store** out) {
+  if (!ctx || !out || layers <= 0 || experts <= 0 || hidden <= 0 || ffn <= 0 || hidden % 256 || ffn % 256)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_create: bad arguments");
+  *out = nullptr;
+  return store_create(ctx, layers, experts, hidden, ffn, cap_bytes, out);
+}
+
+void wmoe_store_destroy(wmoe_store* store) { store_destroy(store); }
+
+int wmoe_store_upload(wmoe_store* store, int layer, int expert, const void* host_src, void* stream) {
+  if (!store) return WMOE_ERR_INVALID;
+  return store_upload(store, layer, expert, host_src, static_cast<cudaStream_t>(stream));
+}
+
+int wmoe_store_fill_synthetic(wmoe_store* store, uint64_t seed, int layer_begin, int layer_end, void* stream) {
+  if (!store) return WMOE_ERR_INVALID;
+  return store_fill_synthetic(store, seed, layer_begin, layer_end, static_cast<cudaStream_t>(stream));
+}
+
+size_t wmoe_store_blob_bytes(const wmoe_store* store) { return store ? store->blob_bytes : 0; }
+
+int wmoe_store_prepare(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream) {
+  if (!store || (n > 0 && !experts)) return WMOE_ERR_INVALID;
+  return store_prepare(store, layer, experts, n, static_cast<cudaStream_t>(stream));
+}
+
+int wmoe_store_download(wmoe_store* store, int layer, int expert, void* host_dst, void* stream) {
+  if (!store) return WMOE_ERR_INVALID;
+  wmoe_ctx* ctx = store->ctx;
+  if (layer < 0 || layer >= store->layers || expert < 0 || expert >= store->experts || !host_dst)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_download: bad arguments");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t key = size_t(layer) * store->experts + expert;
+  const int slot = store->slot_of[key];
+  if (slot >= 0) {
+    WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(host_dst, store->d_slab + size_t(slot) * store->slot_stride,
+                                         store->blob_bytes, cudaMemcpyDeviceToHost, st),
+                    "wmoe_store_download");
+    WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "wmoe_store_download");
+  } else if (store->h_master) {
+    WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "wmoe_store_download");
+    memcpy(host_dst, store->h_master + key * store->blob_bytes, store->blob_bytes);
+  } else {
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_download: blob not present");
+  }
+  return WMOE_OK;
+}
+
+const uint8_t* wmoe_store_blob(const wmoe_store* store, int layer, int expert) {
+  if (!store || layer < 0 || layer >= store->layers || expert < 0 || expert >= store->experts) return nullptr;
+  const int slot = store->slot_of[size_t(layer) * store->experts + expert];
+  return slot < 0 ? nullptr : store->d_slab + size_t(slot) * store->slot_stride;
+}
+
+int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, uint64_t* bytes_in,
+                     uint64_t* evictions) {
+  if (!store) return WMOE_ERR_INVALID;
+  if (hits) *hits = store->hits;
+  if (misses) *misses = store->misses;
+  if (bytes_in) *bytes_in = store->bytes_in;
+  if (evictions) *evictions = store->evictions;
+  return WMOE_OK;
+}
+
+int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                     const float* router_w, const float* router_bias, const float* shared_gate,
+                     const uint8_t* shared_gate_up, const uint8_t* shared_down, void* out, int out_dtype,
+                     int32_t* topk_idx_out, float* topk_w_out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!store) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: null store");
+  if (store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: store belongs to another context");
+  const int H = store->hidden, F = store->ffn, E = store->experts;
+  if (layer < 0 || layer >= store->layers || T < 0 || top_k <= 0 || top_k > E)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: bad layer, token count or top_k");
+  if ((x_dtype != WMOE_F32 && x_dtype != WMOE_BF16) || (out_dtype != WMOE_F32 && out_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: activations must be F32 or BF16");
+  if (H != 2048 || F != 512 || top_k != 8 || E > 512)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_moe_forward: this build runs hidden 2048, ffn 512, top-8");
+  if (T == 0) return WMOE_OK;
+  if (!x || !router_w || !shared_gate || !shared_gate_up || !shared_down || !out)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: null pointer");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 1 && !store->capped && ctx->use_decode_kernel && ctx->decode_ctas > 0 && E == 256) {
+    // one token, every expert resident: the persistent decode kernel (one launch, no host synchronisation)
+    if (int rc = ensure_scratch(ctx, decode_scratch_bytes(H, F, E, ctx->decode_ctas))) return rc;
+    DecodeLayer dl{router_w, router_bias, shared_gate, shared_gate_up, shared_down};
+    int n = 0;
+    const cudaError_t e = decode_persistent(store_source(store, shared_gate_up, shared_down), layer, 1, &dl, H, F, E,
+                                            top_k, 0.f, false, x, x_dtype, out, out_dtype, topk_idx_out, topk_w_out,
+                                            ctx->scratch, ctx->decode_ctas, ctx->d_status, st, &n);
+    ctx->launches += uint64_t(n);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel");
+    return WMOE_OK;
+  }
+  const int k = top_k, P = T * (k + 1);
+  Plan plan;
+  const size_t o_logits = plan.take<float>(size_t(T) * (E + 1));
+  const size_t o_w = plan.take<float>(size_t(T) * k);
+  const size_t o_idx = plan.take<int32_t>(size_t(T) * k);
+  const size_t o_s = plan.take<float>(size_t(T));
+  const size_t o_counts = plan.take<int32_t>(size_t(E));
+  const size_t o_offsets = plan.take<int32_t>(size_t(E) + 1);
+  const size_t o_perm = plan.take<int32_t>(size_t(T) * k);
+  const size_t o_pos = plan.take<int32_t>(size_t(T) * k);
+  const size_t o_used = plan.take<int32_t>(size_t(E) + 1);
+  const size_t o_seg = plan.take<int32_t>(size_t(E) + 2);
+  const size_t o_nused = plan.take<int32_t>(1);
+  const size_t o_disp = plan.bytes;
+  plan.bytes += (dispatch_scratch_bytes(T, E) + 255) / 256 * 256;
+  const size_t o_xq = plan.take<int16_t>(size_t(T) * H);
+  const size_t o_xs = plan.take<float>(size_t(T) * H / 32);
+  const size_t o_xsum = plan.take<int32_t>(size_t(T) * H / 16);
+  const size_t o_h = plan.take<float>(size_t(P) * F);
+  const size_t o_hq = plan.take<int16_t>(size_t(P) * F);
+  const size_t o_hs = plan.take<float>(size_t(P) * F / 32);
+  const size_t o_hsum = plan.take<int32_t>(size_t(P) * F / 16);
+  const size_t o_y = plan.take<float>(size_t(P) * H);
+  if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
+
+  int n = 0;
+  float* topk_w = at<float>(ctx, o_w);
+  int32_t* topk_idx = at<int32_t>(ctx, o_idx);
+  float* shared_s = at<float>(ctx, o_s);
+  WMOE_CHECK_CUDA(ctx, router_logits(x, x_dtype, T, H, E, router_w, shared_gate, at<float>(ctx, o_logits), st, &n),
+                  "router");
+  WMOE_CHECK_CUDA(ctx, router_topk(at<float>(ctx, o_logits), T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr,
+                                   st, &n),
+                  "top-k");
+  std::vector<int32_t> experts_used;
+  if (store->capped) {
+    // the store must copy this call's experts in first: one wait for the routing (engines/base.py:456-460 does
+    // the same with selected.cpu())
+    std::vector<int32_t> sel(size_t(T) * k);
+    WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(sel.data(), topk_idx, sel.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+                    "routing read-back");
+    WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "routing read-back");
+    experts_used = sel;
+    std::sort(experts_used.begin(), experts_used.end());
+    experts_used.erase(std::unique(experts_used.begin(), experts_used.end()), experts_used.end());
+    if (int rc = store_prepare(store, layer, experts_used.data(), int(experts_used.size()), st)) return rc;
+  }
+  PairMap pm;
+  pm.T = T;
+  pm.k = k;
+  pm.E = E;
+  pm.perm = at<int32_t>(ctx, o_perm);
+  pm.pos = at<int32_t>(ctx, o_pos);
+  pm.used = at<int32_t>(ctx, o_used);
+  pm.seg = at<int32_t>(ctx, o_seg);
+  pm.n_used = at<int32_t>(ctx, o_nused);
+  WMOE_CHECK_CUDA(ctx,
+                  dispatch(topk_idx, T, k, E, at<void>(ctx, o_disp), at<int32_t>(ctx, o_counts),
+                           at<int32_t>(ctx, o_offsets), at<int32_t>(ctx, o_perm), at<int32_t>(ctx, o_pos),
+                           at<int32_t>(ctx, o_used), at<int32_t>(ctx, o_seg), at<int32_t>(ctx, o_nused), nullptr,
+                           ctx->d_status, st, &n),
+                  "dispatch");
+  const ExpertSource src = store_source(store, shared_gate_up, shared_down);
+  int16_t* xq = at<int16_t>(ctx, o_xq);
+  float* xs = at<float>(ctx, o_xs);
+  int32_t* xsum = at<int32_t>(ctx, o_xsum);
+  WMOE_CHECK_CUDA(ctx, quant_rows(x, x_dtype, T, H, xq, xs, xsum, st, &n), "activation quantisation");
+  float* h = at<float>(ctx, o_h);
+  WMOE_CHECK_CUDA(ctx, gate_up_gemv(src, layer, pm, H, F, xq, xs, xsum, h, ctx->d_status, st, &n), "gate_up");
+  int16_t* hq = at<int16_t>(ctx, o_hq);
+  float* hs = at<float>(ctx, o_hs);
+  int32_t* hsum = at<int32_t>(ctx, o_hsum);
+  WMOE_CHECK_CUDA(ctx, quant_rows(h, WMOE_F32, P, F, hq, hs, hsum, st, &n), "hidden quantisation");
+  float* y = at<float>(ctx, o_y);
+  WMOE_CHECK_CUDA(ctx, down_gemv(src, layer, pm, H, F, hq, hs, hsum, y, ctx->d_status, st, &n), "down");
+  WMOE_CHECK_CUDA(ctx, combine(pm, H, topk_w, shared_s, y, nullptr, out, out_dtype, st, &n), "combine");
+  if (topk_idx_out)
+    WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_idx_out, topk_idx, size_t(T) * k * sizeof(int32_t),
+                                         cudaMemcpyDeviceToDevice, st),
+                    "routing copy");
+  if (topk_w_out)
+    WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_w_out, topk_w, size_t(T) * k * sizeof(float), cudaMemcpyDeviceToDevice, st),
+                    "routing copy");
+  ctx->launches += uint64_t(n);
+  if (store->capped)
+    if (int rc = store_mark_used(store, layer, experts_used.data(), int(experts_used.size()), st)) return rc;
+  return WMOE_OK;
+}
+
+int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
+                      const wmoe_layer_weights* layers, float eps, const float* h_in, float* h_out,
+                      int32_t* topk_idx_out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack: bad store");
+  if (store->capped) return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_decode_stack: needs every expert resident");
+  if (layer_begin < 0 || n_layers <= 0 || layer_begin + n_layers > store->layers || !layers || !h_in || !h_out)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack: bad arguments");
+  if (store->hidden != 2048 || store->ffn != 512 || store->experts != 256)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_decode_stack: this build runs hidden 2048, ffn 512, 256 experts");
+  if (ctx->decode_ctas <= 0)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_decode_stack: the persistent kernel cannot be co-resident here");
+  for (int i = 0; i < n_layers; ++i)
+    if (!layers[i].router_w || !layers[i].shared_gate || !layers[i].shared_gate_up || !layers[i].shared_down)
+      return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack: null weight pointer in layers[]");
+  const size_t need = decode_scratch_bytes(store->hidden, store->ffn, store->experts, ctx->decode_ctas);
+  if (int rc = ensure_scratch(ctx, need)) return rc;
+  int n = 0;
+  const ExpertSource src = store_source(store, nullptr, nullptr);
+  const cudaError_t e = decode_persistent(src, layer_begin, n_layers, reinterpret_cast<const DecodeLayer*>(layers),
+                                          store->hidden, store->ffn, store->experts, 8, eps, true, h_in, WMOE_F32,
+                                          h_out, WMOE_F32, topk_idx_out, nullptr, ctx->scratch, ctx->decode_ctas,
+                                          ctx->d_status, static_cast<cudaStream_t>(stream), &n);
+  ctx->launches += uint64_t(n);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack");
+  return WMOE_OK;
+}
+
+int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, int n, int rows, int k,
+                    const float* x, float* y, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (ggml_type != WMOE_GGML_Q4_K && ggml_type != WMOE_GGML_Q6_K)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv_batch: only Q4_K and Q6_K");
+  if (n < 0 || rows < 0 || k <= 0 || k % 256) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: bad shape");
+  if (n == 0 || rows == 0) return WMOE_OK;
+  if (!weights || !x || !y) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: null pointer");
+  int c = 0;
+  WMOE_CHECK_CUDA(ctx, gemv_batch(ggml_type, weights, n, rows, k, x, y, static_cast<cudaStream_t>(stream), &c),
+                  "wmoe_gemv_batch");
+  ctx->launches += uint64_t(c);
+  return WMOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,91 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wmoe {
+
+constexpr int kF32 = 0, kBF16 = 1, kF16 = 2;  // WMOE_F32/BF16/F16
+constexpr int kGgmlQ4K = 12, kGgmlQ6K = 14;
+
+// Where a layer's routed experts live: a slab of fixed-size slots and a [layers, experts] slot table
+// (-1: not resident). The shared expert (id == experts) comes from its own pointers.
+struct ExpertSource {
+  const uint8_t* slab;
+  const int32_t* slot_of;
+  uint64_t slot_bytes;
+  uint64_t gate_up_bytes;  // offset of down within a slot
+  int experts;
+  const uint8_t* shared_gate_up;
+  const uint8_t* shared_down;
+};
+
+// Result of dispatch for T tokens with top-k routing, plus the shared expert as an extra segment.
+// Positions 0..T*k-1 hold the routed (token, slot) pairs grouped by expert (ascending id, tokens ascending
+// within an expert); positions T*k..T*k+T-1 are the shared expert's rows, one per token.
+struct PairMap {
+  int T, k, E;
+  const int32_t* perm;    // [T*k] pair id (token*k + slot) at each position
+  const int32_t* pos;     // [T*k] inverse: position of pair id
+  const int32_t* used;    // [E+1] expert id of segment u; the last used segment is the shared expert (id E)
+  const int32_t* seg;     // [E+2] first position of segment u; seg[n_used] = T*(k+1)
+  const int32_t* n_used;  // [1]
+};
+
+__device__ __forceinline__ int pair_token(const PairMap& m, int p) {
+  return p < m.T * m.k ? m.perm[p] / m.k : p - m.T * m.k;
+}
+
+// dequant.cu
+cudaError_t dequant(int type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype, cudaStream_t st);
+
+// route.cu: logits [T, E+1] (column E = shared gate) then top-k
+cudaError_t router_logits(const void* x, int x_dtype, int T, int H, int E, const float* router_w,
+                          const float* shared_gate, float* logits, cudaStream_t st, int* launches);
+cudaError_t router_topk(const float* logits, int T, int E, int k, const float* bias, float* topk_w,
+                        int32_t* topk_idx, float* shared_s, float* logits_out, cudaStream_t st, int* launches);
+
+// dispatch.cu
+size_t dispatch_scratch_bytes(int T, int E);
+cudaError_t dispatch(const int32_t* topk_idx, int T, int k, int E, void* scratch, int32_t* counts,
+                     int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* used, int32_t* seg, int32_t* n_used,
+                     int64_t* usage, int* status, cudaStream_t st, int* launches);
+
+// gemv.cu (small token counts per expert)
+cudaError_t quant_rows(const void* x, int x_dtype, int rows, int K, int16_t* q, float* scale, int32_t* sum16,
+                       cudaStream_t st, int* launches);
+cudaError_t gate_up_gemv(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const int16_t* xq,
+                         const float* xs, const int32_t* xsum16, float* h, int* status, cudaStream_t st,
+                         int* launches);
+cudaError_t down_gemv(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const int16_t* hq,
+                      const float* hs, const int32_t* hsum16, float* y, int* status, cudaStream_t st,
+                      int* launches);
+cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* shared_s, const float* y,
+                    const float* residual, void* out, int out_dtype, cudaStream_t st, int* launches);
+cudaError_t gemv_batch(int type, const uint8_t* const* weights, int n, int rows, int k, const float* x, float* y,
+                       cudaStream_t st, int* launches);
+
+// decode.cu: persistent one-token decode (one layer or a stack)
+struct DecodeLayer {
+  const float* router_w;
+  const float* router_bias;
+  const float* shared_gate;
+  const uint8_t* shared_gate_up;
+  const uint8_t* shared_down;
+};
+size_t decode_scratch_bytes(int H, int F, int E, int num_ctas);
+int decode_num_ctas(int device);
+cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_layers, const DecodeLayer* layers,
+                              int H, int F, int E, int k, float eps, bool stack, const void* x_in, int x_dtype,
+                              void* out,
+                              int out_dtype, int32_t* topk_idx_out, float* topk_w_out, void* scratch,
+                              int num_ctas, int* status, cudaStream_t st, int* launches);
+
+// store.cu: device generator
+cudaError_t fill_synthetic(uint8_t* dst, uint64_t seed, const int32_t* layer_expert /*[n][2]*/, int n,
+                           uint64_t dst_stride, int hidden, int ffn, cudaStream_t st);
+cudaError_t fill_synthetic_one(uint8_t* dst, uint64_t seed, int layer, int expert, int hidden, int ffn,
+                               cudaStream_t st);
+
+}  // namespace wmoe

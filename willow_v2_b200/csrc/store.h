@@ -1,0 +1,57 @@
+// Host-side state behind the opaque wmoe_ctx / wmoe_store handles of include/wmoe.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstring>
+#include <list>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+
+struct wmoe_ctx {
+  int device = 0;
+  int sm_count = 0;
+  std::string error;
+  uint64_t launches = 0;
+  int* d_status = nullptr;  // device status word (see wmoe::DeviceStatus)
+  void* scratch = nullptr;  // grown on demand
+  size_t scratch_bytes = 0;
+  int decode_ctas = 0;      // CTAs of the persistent decode kernel (all co-resident)
+  bool use_decode_kernel = true;
+};
+
+struct wmoe_store {
+  static constexpr int kRing = 64;
+  wmoe_ctx* ctx = nullptr;
+  int layers = 0, experts = 0, hidden = 0, ffn = 0;
+  size_t gate_up_bytes = 0, down_bytes = 0, blob_bytes = 0, slot_stride = 0;
+  bool capped = false;
+  int n_slots = 0;
+  uint8_t* d_slab = nullptr;
+  int32_t* d_slot_of = nullptr;   // [layers * experts] slot or -1
+  std::vector<int32_t> slot_of;   // host mirror
+  uint8_t* h_master = nullptr;    // pinned host copy of every blob (capped stores)
+  std::vector<int64_t> slot_key;  // (layer * experts + expert) held by each slot, -1 free
+  std::vector<uint64_t> slot_use; // sequence number of the last call that read the slot
+  std::list<int> lru;             // slots, least recently used first
+  std::vector<std::list<int>::iterator> lru_pos;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ring[kRing] = {};
+  cudaEvent_t copied = nullptr;
+  uint64_t seq = 0;
+  uint64_t hits = 0, misses = 0, bytes_in = 0, evictions = 0;
+};
+
+int ctx_fail(wmoe_ctx* ctx, int code, const std::string& msg);
+void ctx_count_launch(wmoe_ctx* ctx, int n = 1);
+
+int store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, size_t cap_bytes, wmoe_store** out);
+void store_destroy(wmoe_store* s);
+int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cudaStream_t st);
+int store_fill_synthetic(wmoe_store* s, uint64_t seed, int layer_begin, int layer_end, cudaStream_t st);
+int store_prepare(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st);
+int store_mark_used(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st);
+wmoe::ExpertSource store_source(const wmoe_store* s, const uint8_t* shared_gate_up, const uint8_t* shared_down);

@@ -1,0 +1,74 @@
+"""ctypes binding of libwmoe.so (include/wmoe.h). Importing this module loads the library and fails loudly when it
+is missing: there is no CPU fallback. Build it with ``python -m willow_v2_b200.build``."""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libwmoe.so")
+
+OK = 0
+ERR_INVALID, ERR_CUDA, ERR_CAPACITY, ERR_DEVICE, ERR_UNSUPPORTED, ERR_IO = -1, -2, -3, -4, -5, -6
+F32, BF16, F16 = 0, 1, 2
+GGML_Q4_K, GGML_Q6_K = 12, 14
+STATUS_NAMES = {1: "expert id out of range", 2: "expert not resident", 3: "grid barrier timed out",
+                4: "bad segment"}
+
+# every symbol include/wmoe.h declares, with (restype, argtypes)
+_p, _i, _sz, _u64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_float
+_pp = ctypes.POINTER(ctypes.c_void_p)
+SIGNATURES = {
+    "wmoe_init": (_i, [_i, _pp]),
+    "wmoe_destroy": (None, [_p]),
+    "wmoe_last_error": (ctypes.c_char_p, [_p]),
+    "wmoe_launch_count": (_u64, [_p]),
+    "wmoe_set_decode_kernel": (_i, [_p, _i]),
+    "wmoe_device_status": (_i, [_p, ctypes.POINTER(_i), _p]),
+    "wmoe_dequant": (_i, [_p, _i, _p, _sz, _p, _i, _p]),
+    "wmoe_route": (_i, [_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "wmoe_dispatch": (_i, [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p]),
+    "wmoe_store_create": (_i, [_p, _i, _i, _i, _i, _sz, _pp]),
+    "wmoe_store_destroy": (None, [_p]),
+    "wmoe_store_upload": (_i, [_p, _i, _i, _p, _p]),
+    "wmoe_store_fill_synthetic": (_i, [_p, _u64, _i, _i, _p]),
+    "wmoe_store_blob_bytes": (_sz, [_p]),
+    "wmoe_store_prepare": (_i, [_p, _i, _p, _i, _p]),
+    "wmoe_store_download": (_i, [_p, _i, _i, _p, _p]),
+    "wmoe_store_blob": (_p, [_p, _i, _i]),
+    "wmoe_store_stats": (_i, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_u64), ctypes.POINTER(_u64),
+                              ctypes.POINTER(_u64)]),
+    "wmoe_moe_forward": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _i, _p, _p, _p]),
+    "wmoe_decode_stack": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
+    "wmoe_gemv_batch": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
+}
+
+
+class LayerWeights(ctypes.Structure):
+    """wmoe_layer_weights: device pointers of one layer's router, bias, shared gate and shared expert."""
+    _fields_ = [("router_w", _p), ("router_bias", _p), ("shared_gate", _p), ("shared_gate_up", _p),
+                ("shared_down", _p)]
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m willow_v2_b200.build`")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+class WmoeError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+def check(ctx, code: int):
+    if code != OK:
+        msg = lib.wmoe_last_error(ctx)
+        raise WmoeError(code, msg.decode() if msg else "unknown error")

@@ -1,0 +1,274 @@
+"""The host side of the B200 MoE block: thin PyTorch-facing wrappers over libwmoe.so that mirror willow's own
+interfaces, so willow's engine can call them unchanged.
+
+  dequantize(raw, type_name, shape, dtype)   gguf/quants.py:207-227 (Q4_K, Q6_K), on the GPU
+  route(x, router_w, top_k, ...)             engines/base.py:91-97 route, after the router linear (base.py:448)
+  dispatch(selected, experts)                engines/base.py:456-467 grouping + store.py:482-484 record_usage
+  ExpertStore                                gguf/store.py:41-536 (HBM slots; capped LRU over pinned host memory)
+  moe_forward / CudaMoE.moe                  engines/base.py:445-490 Engine.moe
+  decode_stack                               engines/qwen36/model.py:17-22, the per-layer x + moe(rms_norm(x))
+
+Tensors are torch CUDA tensors; kernels run on torch's current stream. Errors raise WmoeError with the library's
+message (willow raises Python exceptions the same way: quants.py:214-216, store.py:77-81).
+"""
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import lib as _lib
+from .lib import check, lib
+
+_DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+_GGML = {"Q4_K": (_lib.GGML_Q4_K, 144), "Q6_K": (_lib.GGML_Q6_K, 210)}
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class Context:
+    """One libwmoe context on a CUDA device (scratch buffers, device status word, launch counter)."""
+
+    def __init__(self, device: Optional[int] = None):
+        self.device = torch.cuda.current_device() if device is None else int(device)
+        handle = ctypes.c_void_p()
+        code = lib.wmoe_init(self.device, ctypes.byref(handle))
+        if code != _lib.OK:
+            raise _lib.WmoeError(code, f"wmoe_init failed on device {self.device}")
+        self.handle = handle
+
+    @property
+    def launches(self) -> int:
+        return int(lib.wmoe_launch_count(self.handle))
+
+    def set_decode_kernel(self, enable: bool) -> bool:
+        return bool(lib.wmoe_set_decode_kernel(self.handle, int(enable)))
+
+    def device_status(self) -> int:
+        """Reads and clears the device status word (0 = fine; see lib.STATUS_NAMES)."""
+        v = ctypes.c_int()
+        check(self.handle, lib.wmoe_device_status(self.handle, ctypes.byref(v), _stream()))
+        return v.value
+
+    def check_device(self):
+        v = self.device_status()
+        if v:
+            raise _lib.WmoeError(_lib.ERR_DEVICE, _lib.STATUS_NAMES.get(v, f"device status {v}"))
+
+    def close(self):
+        if self.handle:
+            lib.wmoe_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default_ctx = {}
+
+
+def default_context() -> Context:
+    dev = torch.cuda.current_device()
+    if dev not in _default_ctx:
+        _default_ctx[dev] = Context(dev)
+    return _default_ctx[dev]
+
+
+def dequantize(raw: torch.Tensor, type_name: str, shape: tuple, dtype: torch.dtype = torch.bfloat16,
+               ctx: Optional[Context] = None) -> torch.Tensor:
+    """raw: uint8 CUDA tensor holding one Q4_K or Q6_K tensor's bytes -> a new tensor of shape and dtype
+    (float32 bit-identical to gguf/quants.py:dequantize; bf16/f16 rounded to nearest even from it)."""
+    ctx = ctx or default_context()
+    if type_name not in _GGML:
+        raise NotImplementedError(f"ggml type {type_name} is not supported (supported: Q4_K, Q6_K)")
+    gtype, block = _GGML[type_name]
+    assert raw.is_cuda and raw.dtype == torch.uint8 and raw.is_contiguous()
+    nblocks = raw.numel() // block
+    assert nblocks * block == raw.numel() and nblocks * 256 == int(np.prod(shape)), (type_name, shape, raw.shape)
+    out = torch.empty(shape, dtype=dtype, device=raw.device)
+    check(ctx.handle, lib.wmoe_dequant(ctx.handle, gtype, _ptr(raw), nblocks, _ptr(out), _DTYPES[dtype], _stream()))
+    return out
+
+
+def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int = 8, bias: Optional[torch.Tensor] = None,
+          shared_gate: Optional[torch.Tensor] = None, ctx: Optional[Context] = None):
+    """x [T, H] (f32/bf16) -> (weights f32 [T, top_k], selected int32 [T, top_k], shared gate sigmoid f32 [T] or
+    None, logits f32 [T, E]). The router linear in fp32, softmax, top-k and renormalisation of engines/base.py:91-97
+    (norm_topk_prob=True)."""
+    ctx = ctx or default_context()
+    T, H = x.shape
+    E = router_w.shape[0]
+    w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    sel = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    s = torch.empty(T, dtype=torch.float32, device=x.device) if shared_gate is not None else None
+    logits = torch.empty(T, E, dtype=torch.float32, device=x.device)
+    check(ctx.handle, lib.wmoe_route(ctx.handle, _ptr(x.contiguous()), _DTYPES[x.dtype], T, H, E, top_k,
+                                     _ptr(router_w), _ptr(bias), _ptr(shared_gate), _ptr(w), _ptr(sel), _ptr(s),
+                                     _ptr(logits), _stream()))
+    return w, sel, s, logits
+
+
+def dispatch(selected: torch.Tensor, experts: int, usage: Optional[torch.Tensor] = None,
+             ctx: Optional[Context] = None):
+    """selected int32 [T, k] -> (counts int32 [E], offsets int32 [E+1], perm int32 [T*k]): the picks grouped by
+    expert, tokens ascending within an expert; perm holds token*k + slot. usage (int64 [E]) accumulates counts."""
+    ctx = ctx or default_context()
+    T, k = selected.shape
+    dev = selected.device
+    counts = torch.empty(experts, dtype=torch.int32, device=dev)
+    offsets = torch.empty(experts + 1, dtype=torch.int32, device=dev)
+    perm = torch.empty(T * k, dtype=torch.int32, device=dev)
+    check(ctx.handle, lib.wmoe_dispatch(ctx.handle, _ptr(selected.contiguous()), T, k, experts, _ptr(counts),
+                                        _ptr(offsets), _ptr(perm), _ptr(usage), _stream()))
+    return counts, offsets, perm
+
+
+class ExpertStore:
+    """Routed experts of every layer in HBM (the role of gguf/store.py:ExpertStore). Each expert is one blob, the
+    pack layout: gate_up (Q4_K [2F, H], gate rows then up rows) followed by down (Q6_K [H, F]).
+    cap_bytes = 0 keeps every blob resident; otherwise at most cap_bytes of device slots, the blobs in pinned
+    host memory, misses copied on a side stream with least-recently-used eviction."""
+
+    def __init__(self, layers: int, experts: int = 256, hidden: int = 2048, ffn: int = 512, cap_bytes: int = 0,
+                 ctx: Optional[Context] = None):
+        self.ctx = ctx or default_context()
+        self.layers, self.experts, self.hidden, self.ffn = layers, experts, hidden, ffn
+        handle = ctypes.c_void_p()
+        check(self.ctx.handle, lib.wmoe_store_create(self.ctx.handle, layers, experts, hidden, ffn, cap_bytes,
+                                                     ctypes.byref(handle)))
+        self.handle = handle
+        self.blob_bytes = int(lib.wmoe_store_blob_bytes(handle))
+        self.gate_up_bytes = 2 * ffn * hidden // 256 * 144
+        self.capped = cap_bytes != 0 and cap_bytes < layers * experts * ((self.blob_bytes + 255) // 256 * 256)
+
+    def upload(self, layer: int, expert: int, blob):
+        """blob: the expert's bytes (numpy uint8 / bytes, or a CPU uint8 tensor), blob_bytes long."""
+        arr = np.ascontiguousarray(np.frombuffer(blob, dtype=np.uint8) if isinstance(blob, (bytes, bytearray))
+                                   else (blob.numpy() if isinstance(blob, torch.Tensor) else blob), dtype=np.uint8)
+        if arr.size != self.blob_bytes:
+            raise ValueError(f"expert blob is {arr.size} bytes, expected {self.blob_bytes}")
+        check(self.ctx.handle, lib.wmoe_store_upload(self.handle, layer, expert,
+                                                     arr.ctypes.data_as(ctypes.c_void_p), _stream()))
+        torch.cuda.current_stream().synchronize()  # the host buffer may be freed after this returns
+
+    def fill_synthetic(self, seed: int, layer_begin: int = 0, layer_end: Optional[int] = None):
+        """Generates every blob of the layer range on the device (the generator of willow_v2_b200.synth)."""
+        end = self.layers if layer_end is None else layer_end
+        check(self.ctx.handle, lib.wmoe_store_fill_synthetic(self.handle, seed, layer_begin, end, _stream()))
+
+    def load_many(self, layer: int, experts):
+        """Makes the experts of a layer resident (store.py:132-137's role); a no-op when nothing is capped."""
+        ids = np.ascontiguousarray(np.asarray(list(experts), dtype=np.int32))
+        check(self.ctx.handle, lib.wmoe_store_prepare(self.handle, layer, ids.ctypes.data_as(ctypes.c_void_p),
+                                                      int(ids.size), _stream()))
+
+    def download(self, layer: int, expert: int) -> np.ndarray:
+        """The expert's bytes as the store holds them (uint8 [blob_bytes])."""
+        out = np.empty(self.blob_bytes, dtype=np.uint8)
+        check(self.ctx.handle, lib.wmoe_store_download(self.handle, layer, expert,
+                                                       out.ctypes.data_as(ctypes.c_void_p), _stream()))
+        return out
+
+    def blob_ptr(self, layer: int, expert: int) -> Optional[int]:
+        return lib.wmoe_store_blob(self.handle, layer, expert)
+
+    def stats(self) -> dict:
+        vals = [ctypes.c_uint64() for _ in range(4)]
+        check(self.ctx.handle, lib.wmoe_store_stats(self.handle, *[ctypes.byref(v) for v in vals]))
+        return dict(zip(("hits", "misses", "bytes_in", "evictions"), (v.value for v in vals)))
+
+    def close(self):
+        if self.handle:
+            lib.wmoe_store_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class LayerWeights:
+    """One layer's non-routed MoE weights on the GPU: router f32 [E, H], optional routing bias f32 [E], shared
+    expert gate vector f32 [H], shared expert gate_up (Q4_K bytes, uint8) and down (Q6_K bytes, uint8)."""
+    router_w: torch.Tensor
+    shared_gate: torch.Tensor
+    shared_gate_up: torch.Tensor
+    shared_down: torch.Tensor
+    router_bias: Optional[torch.Tensor] = None
+
+    def as_struct(self) -> _lib.LayerWeights:
+        return _lib.LayerWeights(self.router_w.data_ptr(), None if self.router_bias is None else self.router_bias.data_ptr(),
+                                 self.shared_gate.data_ptr(), self.shared_gate_up.data_ptr(), self.shared_down.data_ptr())
+
+
+def moe_forward(store: ExpertStore, layer: int, x: torch.Tensor, lw: LayerWeights, top_k: int = 8,
+                out_dtype: Optional[torch.dtype] = None, return_routing: bool = False):
+    """One MoE block (engines/base.py:445-490) on x [T, H] (f32 or bf16) -> out [T, H] (x's dtype by default);
+    with return_routing also (weights f32 [T, k], selected int32 [T, k])."""
+    ctx = store.ctx
+    x = x.contiguous()
+    T = x.shape[0]
+    out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    sel = torch.empty(T, top_k, dtype=torch.int32, device=x.device) if return_routing else None
+    w = torch.empty(T, top_k, dtype=torch.float32, device=x.device) if return_routing else None
+    check(ctx.handle, lib.wmoe_moe_forward(ctx.handle, store.handle, layer, _ptr(x), _DTYPES[x.dtype], T, top_k,
+                                           _ptr(lw.router_w), _ptr(lw.router_bias), _ptr(lw.shared_gate),
+                                           _ptr(lw.shared_gate_up), _ptr(lw.shared_down), _ptr(out),
+                                           _DTYPES[out.dtype], _ptr(sel), _ptr(w), _stream()))
+    return (out, w, sel) if return_routing else out
+
+
+def decode_stack(store: ExpertStore, layers: list, h: torch.Tensor, eps: float = 1e-6, layer_begin: int = 0,
+                 out: Optional[torch.Tensor] = None, return_routing: bool = False):
+    """One decode token through len(layers) stacked blocks, h <- h + moe(rms_norm(h)) per layer, in one persistent
+    launch. h: f32 [H] (or [1, H]) on the GPU."""
+    ctx = store.ctx
+    h = h.reshape(-1).contiguous()
+    assert h.dtype == torch.float32
+    out = torch.empty_like(h) if out is None else out
+    arr = (_lib.LayerWeights * len(layers))(*[lw.as_struct() for lw in layers])
+    sel = torch.empty(len(layers), 8, dtype=torch.int32, device=h.device) if return_routing else None
+    check(ctx.handle, lib.wmoe_decode_stack(ctx.handle, store.handle, layer_begin, len(layers),
+                                            ctypes.cast(arr, ctypes.c_void_p), ctypes.c_float(eps), _ptr(h),
+                                            _ptr(out), _ptr(sel), _stream()))
+    return (out, sel) if return_routing else out
+
+
+class CudaMoE:
+    """Mixin that replaces willow's Engine.moe (engines/base.py:445-490) with the B200 kernels:
+
+        class B200Qwen35(CudaMoE, Qwen35MoEEngine): ...
+
+    It reads the layer's weights by willow's names through self.w(...): the router
+    ``{prefix}layers.{L}.mlp.gate.weight`` and ``.mlp.shared_expert_gate.weight`` (f32, on the GPU), and the shared
+    expert as raw GGUF bytes on the GPU, ``.mlp.shared_expert.gate_up_proj.qweight`` (Q4_K, gate rows then up rows)
+    and ``.mlp.shared_expert.down_proj.qweight`` (Q6_K). Routed experts come from self.experts, an ExpertStore of
+    this module. ``.mlp.gate.bias`` (optional, f32 [E]) is added to the logits. Returns the block's output in x's
+    dtype, like Engine.moe; residual is accepted for the signature (the next-layer guess it feeds in willow only
+    drives SSD prefetching, which an HBM-resident store does not need)."""
+
+    top_k = 8
+
+    def moe(self, x: torch.Tensor, layer: int, residual: torch.Tensor = None) -> torch.Tensor:
+        p = f"{self.prefix}layers.{layer}.mlp"
+        lw = LayerWeights(router_w=self.w(p + ".gate.weight"),
+                          shared_gate=self.w(p + ".shared_expert_gate.weight").reshape(-1),
+                          shared_gate_up=self.w(p + ".shared_expert.gate_up_proj.qweight"),
+                          shared_down=self.w(p + ".shared_expert.down_proj.qweight"),
+                          router_bias=self.weights.get(p + ".gate.bias"))
+        shape = x.shape
+        out = moe_forward(self.experts, layer, x.reshape(-1, shape[-1]), lw, self.top_k)
+        return out.view(shape)
