@@ -61,6 +61,13 @@ uint64_t wmoe_launch_count(const wmoe_ctx* ctx);
 /* enable = 1 (default): wmoe_moe_forward runs single-token calls on an uncapped store with the persistent
  * decode kernel; 0: with the multi-launch GEMV path. Returns the previous setting. */
 int wmoe_set_decode_kernel(wmoe_ctx* ctx, int enable);
+/* Phase tracing of the persistent decode kernel (the role of willow's per-section Engine.tick timings,
+ * engines/base.py:384-390): with trace non-null, each CTA writes %globaltimer nanoseconds at WMOE_TRACE_POINTS
+ * points of every layer into trace[(layer * WMOE_TRACE_POINTS + point) * ctas + cta] (device memory of at least
+ * layers * WMOE_TRACE_POINTS * ctas entries; ctas from wmoe_decode_ctas). Null turns it off. */
+#define WMOE_TRACE_POINTS 12
+int wmoe_set_trace(wmoe_ctx* ctx, uint64_t* trace, size_t entries);
+int wmoe_decode_ctas(const wmoe_ctx* ctx);
 /* Reads and clears the device status word: 0, or the first WMOE_ERR_DEVICE cause a kernel recorded
  * (1 = expert id out of range, 2 = expert not resident, 3 = grid barrier timed out, 4 = bad segment). */
 int wmoe_device_status(wmoe_ctx* ctx, int* status, void* stream);
@@ -129,14 +136,23 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
                      const uint8_t* shared_gate_up, const uint8_t* shared_down, void* out, int out_dtype,
                      int32_t* topk_idx_out, float* topk_w_out, void* stream);
 
-/* Per-layer weights of a decode stack, in device memory: one entry per layer. */
+/* Per-layer weights of a decode stack (device pointers): one entry per layer. */
 typedef struct wmoe_layer_weights {
     const float* router_w;          /* f32 [experts, hidden] */
     const float* router_bias;       /* f32 [experts] or null */
     const float* shared_gate;       /* f32 [hidden] */
     const uint8_t* shared_gate_up;  /* Q4_K [2*ffn, hidden] */
     const uint8_t* shared_down;     /* Q6_K [hidden, ffn] */
+    const float* router_packed;     /* f32 [hidden, WMOE_ROUTER_STRIDE] from wmoe_pack_router, or null */
 } wmoe_layer_weights;
+
+/* The router and the shared-expert gate transposed into one [hidden, WMOE_ROUTER_STRIDE] f32 matrix: column e < experts
+ * is router row e, column experts is the shared gate, the rest zero. A layout transform done once at load (like
+ * willow's pack step, gguf/compiler.py:90-137); with it every CTA of the decode kernel reads its slice of rows as one
+ * contiguous block. out: device memory of hidden * WMOE_ROUTER_STRIDE floats. experts <= 263. */
+#define WMOE_ROUTER_STRIDE 264
+int wmoe_pack_router(wmoe_ctx* ctx, const float* router_w, const float* shared_gate, int experts, int hidden,
+                     float* out, void* stream);
 
 /* One decode token through layers [layer_begin, layer_begin + n_layers) of the store:
  * h <- h + moe_l(rms_norm(h)) per layer (eps, unit weight), in one persistent launch per 64 layers.

@@ -39,7 +39,7 @@ def test_library_rejects_bad_arguments_without_a_gpu():
 
 def test_layer_weights_struct_matches_header():
     from willow_v2_b200 import lib as L
-    assert ctypes.sizeof(L.LayerWeights) == 5 * ctypes.sizeof(ctypes.c_void_p)
+    assert ctypes.sizeof(L.LayerWeights) == 6 * ctypes.sizeof(ctypes.c_void_p)
 
 
 def f64_to_f16_rne(v: float) -> int:

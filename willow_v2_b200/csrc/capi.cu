@@ -93,6 +93,15 @@ const char* wmoe_last_error(const wmoe_ctx* ctx) { return ctx ? ctx->error.c_str
 
 uint64_t wmoe_launch_count(const wmoe_ctx* ctx) { return ctx ? ctx->launches : 0; }
 
+int wmoe_set_trace(wmoe_ctx* ctx, uint64_t* trace, size_t entries) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  ctx->trace = entries ? trace : nullptr;
+  ctx->trace_entries = trace ? entries : 0;
+  return WMOE_OK;
+}
+
+int wmoe_decode_ctas(const wmoe_ctx* ctx) { return ctx ? ctx->decode_ctas : 0; }
+
 int wmoe_set_decode_kernel(wmoe_ctx* ctx, int enable) {
   if (!ctx) return WMOE_ERR_INVALID;
   const int prev = ctx->use_decode_kernel ? 1 : 0;
@@ -146,6 +155,18 @@ int wmoe_route(wmoe_ctx* ctx, const void* x, int x_dtype, int T, int hidden, int
   WMOE_CHECK_CUDA(ctx, router_topk(lg, T, experts, top_k, router_bias, topk_w, topk_idx, shared_s, logits, st, &n),
                   "top-k");
   ctx->launches += uint64_t(n);
+  return WMOE_OK;
+}
+
+int wmoe_pack_router(wmoe_ctx* ctx, const float* router_w, const float* shared_gate, int experts, int hidden,
+                     float* out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (experts <= 0 || experts >= WMOE_ROUTER_STRIDE || hidden <= 0)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_pack_router: bad shape");
+  if (!router_w || !shared_gate || !out) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_pack_router: null pointer");
+  WMOE_CHECK_CUDA(ctx, pack_router(router_w, shared_gate, experts, hidden, out, static_cast<cudaStream_t>(stream)),
+                  "wmoe_pack_router");
+  ctx->launches += 1;
   return WMOE_OK;
 }
 
@@ -263,7 +284,8 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
     int n = 0;
     const cudaError_t e = decode_persistent(store_source(store, shared_gate_up, shared_down), layer, 1, &dl, H, F, E,
                                             top_k, 0.f, false, x, x_dtype, out, out_dtype, topk_idx_out, topk_w_out,
-                                            ctx->scratch, ctx->decode_ctas, ctx->d_status, st, &n);
+                                            ctx->scratch, ctx->decode_ctas, ctx->d_status, ctx->trace,
+                                            ctx->trace_entries, st, &n);
     ctx->launches += uint64_t(n);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel");
     return WMOE_OK;
@@ -379,7 +401,8 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
   const cudaError_t e = decode_persistent(src, layer_begin, n_layers, reinterpret_cast<const DecodeLayer*>(layers),
                                           store->hidden, store->ffn, store->experts, 8, eps, true, h_in, WMOE_F32,
                                           h_out, WMOE_F32, topk_idx_out, nullptr, ctx->scratch, ctx->decode_ctas,
-                                          ctx->d_status, static_cast<cudaStream_t>(stream), &n);
+                                          ctx->d_status, ctx->trace, ctx->trace_entries,
+                                          static_cast<cudaStream_t>(stream), &n);
   ctx->launches += uint64_t(n);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack");
   return WMOE_OK;

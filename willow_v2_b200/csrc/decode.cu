@@ -1,19 +1,28 @@
 // Persistent one-token decode of the MoE block: one cooperative launch (one CTA per SM, all co-resident) runs
 // every layer of a stack, h <- h + moe_l(rms_norm(h)) (engines/qwen36/model.py:17-22), or a single MoE block.
 //
-// Per layer, three phases separated by grid barriers:
-//   A  x (the residual stream, or the caller's normalised input) -> shared memory, RMS-normalised for a stack,
-//      quantised to int16 per 32 values; the E router rows and the shared-expert gate row are split over the
-//      CTAs (fp32 dot products, 16 warps per row) -> logits in global memory.
-//   B  every CTA reads the E+1 logits and forms the same top-k routing (softmax over the picks, renormalised);
-//      the (k routed + 1 shared) x F SwiGLU outputs are split over CTAs and warps: each warp computes a gate row
-//      and its up row from the Q4_K blocks (dp2a on the 4-bit codes, layout of gemv.cu) -> h in global memory.
-//   C  every CTA quantises all k+1 h vectors into shared memory and owns a slice of the H output rows: for each
-//      of its rows, the k+1 Q6_K down dot products (8 lanes each), then the combine in ascending expert id plus
-//      the shared expert times its sigmoid gate, plus the residual for a stack.
-// Data written by other CTAs is read with ld.global.cg (L2), never from a possibly stale L1 line.
-// The barrier spins are bounded (1 s of %globaltimer); a timeout sets the device status word and every CTA
-// returns early instead of hanging.
+// A layer has two grid-wide exchanges, the minimum its data flow allows (every logit needs all of x; every down
+// row needs all of an expert's h):
+//   S1  x_l is complete in global memory, and so are the router sums S_l[e] = sum_r R_l[e, r] x_l[r] (plus the
+//       shared-expert gate row), accumulated in float64 by the CTAs that produced the rows of x_l, into 16
+//       replicas (CTA c adds into replica c % 16) so that no cache line takes more than ~10 of the adds.
+//   B   every CTA reads x_l (its own RMS scale r = 1/sqrt(mean(x^2) + eps) from it), sums the replicas in a
+//       fixed order and quantises x to int16; warp 0 forms logits r*S + bias and the same top-k routing on every
+//       CTA and its lanes at once issue TMA bulk copies (cp.async.bulk, mbarrier completion) of this CTA's 32
+//       gate/up row pairs in two chunks. CTA c < 144 owns h block c: 32 consecutive h values of one expert slot.
+//       Once the first chunk lands, this CTA's slice of down rows of all k+1 experts follows, streaming while
+//       gate_up computes. Warps compute gate and up rows (dp2a on the 4-bit codes) -> SwiGLU; warp 0 quantises
+//       the block's 32 h values to int16 once and writes them to global memory in the order the down lanes read;
+//       the other warps unpack their Q6_K down codes into registers (independent of h).
+//   S2  all h blocks complete.
+//   C   every CTA copies the quantised h into shared memory, finishes its rows of the k+1 down products (dp2a on
+//       the unpacked codes), combines them in ascending expert id plus the gated shared expert (+ the residual),
+//       writes x_{l+1} rows, and adds its rows' share of the next layer's router sums S_{l+1}.
+// The router is linear in x, so the RMS normalisation is applied to the sums afterwards (logits = r * S).
+// Data written by other CTAs is read through L2 (ld.global.cg). The float64 replicas keep the logits
+// independent of the order in which CTAs add their parts (to far below float32 resolution).
+// Barrier and mbarrier waits are bounded (1 s of %globaltimer): a timeout sets the device status word and
+// every CTA returns instead of hanging (by then every copy it issued has long completed).
 #include <algorithm>
 
 #include "common.cuh"
@@ -27,7 +36,17 @@ constexpr int kH = 2048, kF = 512, kE = 256, kK = 8;
 constexpr int kSlots = kK + 1;  // routed experts + the shared one
 constexpr int kThreads = 512, kWarps = kThreads / 32;
 constexpr int kMaxLayers = 64;
-constexpr unsigned long long kBarrierTimeoutNs = 1000000000ull;
+constexpr int kMaxRows = 32;                      // output rows per CTA
+constexpr int kRowBytesQ4 = kH / 256 * Q4K_BYTES;  // 1152
+constexpr int kRowBytesQ6 = kF / 256 * Q6K_BYTES;  // 420
+constexpr int kHBlocks = kSlots * kF / 32;        // 144 h blocks of 32 values: one per CTA
+constexpr int kChunkBytes = 16 * 2 * kRowBytesQ4;  // 16 gate rows + 16 up rows
+constexpr int kReplicas = 16;
+constexpr int kSaccStride = 264;                  // doubles per replica (>= kE + 1)
+constexpr int kSaccRot = kReplicas * kSaccStride;  // doubles per rotation buffer
+constexpr int kMaxPairs = 2;                      // (row, slot) down pairs per 8-lane group
+constexpr unsigned long long kTimeoutNs = 1000000000ull;
+constexpr int kTracePoints = 12;  // WMOE_TRACE_POINTS
 
 struct DecodeParams {
   ExpertSource src;
@@ -40,23 +59,19 @@ struct DecodeParams {
   int out_dtype;
   int32_t* topk_idx_out;
   float* topk_w_out;
-  float* xbuf;     // [2][H] residual stream between layers
-  float* logits;   // [E+1]
-  float* hbuf;     // [kSlots][F]
-  unsigned* bar;   // [64]: count at 0, generation at 32 (separate 128-byte lines)
+  float* xbuf;      // [2][H] residual stream between layers
+  double* sacc;     // [3][kReplicas][kSaccStride] router sums, rotating by layer
+  int16_t* hq;      // [kSlots][F] quantised h, down lane order
+  float* hs;        // [kSlots][F / 32] its scales
+  int32_t* hsum;    // [kSlots][F / 16] its per-16 sums
+  unsigned* bar;    // grid barrier counter (own 128-byte line)
   int* status;
+  int dn_chunk;     // bytes reserved per slot for this CTA's down rows
+  unsigned long long* trace;  // phase timestamps [layer][point][cta], or null
   DecodeLayer layers[kMaxLayers];
 };
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+// ---------------------------------------------------------------- synchronisation primitives
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
@@ -64,96 +79,129 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
-// Returns false (for every thread of the CTA) when the wait ran out.
-__device__ bool grid_barrier(unsigned* bar, int* status, int* abort_flag) {
-  __syncthreads();
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Monotonic-counter grid barrier: the epoch-th barrier of this launch completes when the counter reaches
+// epoch * gridDim.x. Split into arrive (one thread, after the CTA's writes that others will read; the fence
+// makes them visible first) and wait (every thread), so that independent work can run in between.
+__device__ __forceinline__ void grid_arrive(unsigned* counter) {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+}
+
+// Returns false on every thread of the CTA if the wait ran out.
+__device__ bool grid_wait(unsigned* counter, unsigned epoch, int* status, volatile int* abort_flag) {
   if (threadIdx.x == 0) {
-    unsigned* count = bar;
-    unsigned* gen = bar + 32;
-    const unsigned g = ld_acquire(gen);
-    __threadfence();
-    const unsigned arrived = atomicAdd(count, 1u);
-    if (arrived == gridDim.x - 1) {
-      atomicExch(count, 0u);
-      st_release(gen, g + 1);
-    } else {
-      const unsigned long long t0 = globaltimer();
-      while (ld_acquire(gen) == g) {
-        if (globaltimer() - t0 > kBarrierTimeoutNs) {
-          set_status(status, kStatusBarrierTimeout);
-          *abort_flag = 1;
-          break;
-        }
+    const unsigned target = epoch * gridDim.x;
+    const unsigned long long t0 = globaltimer();
+    while (int(ld_acquire(counter) - target) < 0) {
+      if (globaltimer() - t0 > kTimeoutNs) {
+        set_status(status, kStatusBarrierTimeout);
+        *abort_flag = 1;
+        break;
       }
     }
-    __threadfence();
   }
   __syncthreads();
   return *abort_flag == 0;
 }
 
-struct Smem {
-  float x[kH];                 // input row (normalised for a stack)
-  float resid[kH];             // residual (stack)
-  int16_t xq[kH];              // quantised x
-  float xs[kH / 32];           // per-32 scales
-  int32_t xsum[kH / 16];       // per-16 sums of xq
-  int16_t hq[kSlots][kF];      // quantised h of each slot
-  float hs[kSlots][kF / 32];
-  int32_t hsum[kSlots][kF / 16];
-  float ys[32][kSlots];        // down outputs of this CTA's rows (at most 32: needs >= 64 CTAs)
-  float red[kWarps];
-  float red2[kWarps][2];
-  int sel[kSlots];             // expert id of each slot (slot kK: shared = kE)
-  float w[kSlots];             // routing weight of each slot (slot kK: sigmoid gate)
-  int order[kK];               // routed slots in ascending expert id
-  float norm;
-  int abort_flag;
-};
-
-// Quantise 32 floats (shared memory) to int16 with their scale and per-16 sums.
-__device__ __forceinline__ void quant32(const float* v, int16_t* q, float* scale, int32_t* sum16) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
-  int s0 = 0, s1 = 0;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    int a = __float2int_rn(v[i] * inv);
-    a = max(-32767, min(32767, a));
-    q[i] = int16_t(a);
-    if (i < 16) s0 += a; else s1 += a;
-  }
-  *scale = amax / 32767.f;
-  sum16[0] = s0;
-  sum16[1] = s1;
+__device__ bool grid_barrier(unsigned* counter, unsigned epoch, int* status, volatile int* abort_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) grid_arrive(counter);
+  return grid_wait(counter, epoch, status, abort_flag);
 }
 
-struct Q4L {
-  float A0, B0, A1, B1;
-  uint4 q0, q1;
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity; false if it ran out (status and abort flag set).
+__device__ bool mbar_wait(uint64_t* bar, unsigned parity, int* status, volatile int* abort_flag) {
+  if (!mbar_try_wait(bar, parity)) {
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        set_status(status, kStatusBarrierTimeout);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// global -> shared bulk copy (16-byte aligned addresses, size a multiple of 16), completing on an mbarrier. The
+// destination's earlier readers have all passed a CTA barrier before the copy is issued (their loads are
+// complete), so the copy's async-proxy writes cannot overtake them.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------- shared memory layout
+
+struct Small {
+  uint64_t mbar_gu[2], mbar_dn, mbar_rs;
+  alignas(16) float x[kH];        // x_l as read (raw residual for a stack)
+  alignas(16) int16_t xq[kH];     // quantised x, in gate_up lane order (see xq_offset)
+  float xs[kH / 32];
+  int32_t xsum[kH / 16];
+  alignas(16) int16_t hq[kSlots][kF];  // quantised h, in down lane order (see hq_offset)
+  float hs[kSlots][kF / 32];
+  int32_t hsum[kSlots][kF / 16];
+  float ys[kMaxRows][kSlots];
+  float xn[kMaxRows];             // this CTA's rows of x_{l+1}
+  alignas(16) float rs[kMaxRows][kRouterStride];  // packed router rows r0..r1-1 of the next layer
+  float logit[kE + 1];            // summed router sums S (before the RMS factor)
+  int slot_row[2][kE];            // the store slot of each expert, by layer parity
+  float bias[2][kE];              // the routing bias (zero without one), by layer parity
+  float hblk[32];                 // this CTA's 32 h values
+  float red[kWarps];
+  const uint8_t* dn_ptr[kSlots];
+  int sel[kSlots];
+  float w[kSlots];
+  int order[kK];
+  float rscale;
+  int abort_flag;
+  int dn_off;                     // offset of row r0 within each slot's down chunk
 };
 
-__device__ __forceinline__ Q4L q4_load(const uint8_t* block, int g) {
-  Q4L r;
-  const uint4 hd = ldg_nc_v4(block);
-  r.q0 = ldg_nc_v4(block + 16 + 32 * g);
-  r.q1 = ldg_nc_v4(block + 32 + 32 * g);
+__device__ __forceinline__ float q4_dot_smem(const uint8_t* block, int g, const uint32_t* xw, float sx0, float sx1,
+                                             float sum0, float sum1) {
+  const uint4 hd = *reinterpret_cast<const uint4*>(block);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(block + 16 + 32 * g);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(block + 32 + 32 * g);
   const float d = f16_to_f32(uint16_t(hd.x & 0xFFFF)), dmin = f16_to_f32(uint16_t(hd.x >> 16));
   int sc0, mn0, sc1, mn1;
   q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * g, sc0, mn0);
   q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * g + 1, sc1, mn1);
-  r.A0 = d * float(sc0);
-  r.B0 = dmin * float(mn0);
-  r.A1 = d * float(sc1);
-  r.B1 = dmin * float(mn1);
-  return r;
-}
-
-__device__ __forceinline__ float q4_dot(const Q4L& w, const uint32_t* xw, float sx0, float sx1, float sum0,
-                                        float sum1) {
-  const uint32_t qw[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
   int a0 = 0, a1 = 0;
 #pragma unroll
   for (int m = 0; m < 8; ++m) {
@@ -163,236 +211,428 @@ __device__ __forceinline__ float q4_dot(const Q4L& w, const uint32_t* xw, float 
     a1 = dp2a_lo(xw[16 + 2 * m], hi, a1);
     a1 = dp2a_hi(xw[17 + 2 * m], hi, a1);
   }
-  return sx0 * (w.A0 * float(a0) - w.B0 * sum0) + sx1 * (w.A1 * float(a1) - w.B1 * sum1);
+  return sx0 * ((d * float(sc0)) * float(a0) - (dmin * float(mn0)) * sum0) +
+         sx1 * ((d * float(sc1)) * float(a1) - (dmin * float(mn1)) * sum1);
+}
+
+// Where x position pos lives in sm.xq: the gate_up lane (super-block pos/256, nibble group (pos%256)/64) reads its
+// 64 values as 8 runs of 8, run m of every lane adjacent (conflict-free 16-byte loads).
+__device__ __forceinline__ int xq_offset(int pos) {
+  const int lanex = (pos / 256) * 4 + (pos % 256) / 64, k = pos % 64;
+  return ((k / 8) * 32 + lanex) * 8 + k % 8;
+}
+
+// Where h position pos lives within a slot's quantised h: the down lane task t8 = (super-block, half, 16-run)
+// reads quarter s of its positions as two runs of 8, the eight tasks' runs adjacent.
+__device__ __forceinline__ int hq_offset(int pos) {
+  const int sb = pos / 256, hh = (pos % 256) / 128, r = pos % 128, s = r / 32, p = r % 32;
+  const int t8 = sb * 4 + hh * 2 + p / 16, e16 = p % 16;
+  return ((s * 2 + e16 / 8) * 8 + t8) * 8 + e16 % 8;
+}
+
+// Warp-cooperative int16 quantisation of 32 values (lane i holds value i of the block): q[offset], the block's
+// scale and its two per-16 sums, with single-instruction warp reductions (redux.sync).
+__device__ __forceinline__ void quant32_warp(float v, int lane, int16_t* q, int offset, float* scale,
+                                             int32_t* sum16) {
+  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
+  const float inv = amax > 0.f ? 32767.f / amax : 0.f;
+  int a = __float2int_rn(v * inv);
+  a = max(-32767, min(32767, a));
+  q[offset] = int16_t(a);
+  const int all = __reduce_add_sync(0xffffffffu, a);
+  const int lo = __reduce_add_sync(0xffffffffu, lane < 16 ? a : 0);
+  if (lane == 0) {
+    *scale = amax / 32767.f;
+    sum16[0] = lo;
+    sum16[1] = all - lo;
+  }
+}
+
+// This CTA's rows [r0, r1) of x (in sm.xn) times the packed router slice in sm.rs, added into its float64 replica.
+__device__ void add_router_part(Small& sm, double* replica, int nrows) {
+  const int e = threadIdx.x;
+  if (e <= kE) {
+    float acc = 0.f;
+    for (int i = 0; i < nrows; ++i) acc = fmaf(sm.rs[i][e], sm.xn[i], acc);
+    atomicAdd(replica + e, double(acc));
+  }
+}
+
+// Router rows r0..r1-1 (transposed: [row][expert], shared gate at column kE) of layer L into sm.rs: one bulk copy
+// of the packed router (thread 0 issues; mbar_rs completes), or plain loads from the [E, H] router when no packed
+// copy exists (every thread; then the caller's __syncthreads completes it). Returns true if a copy was issued.
+__device__ bool fetch_router_slice(Small& sm, const DecodeLayer& L, int r0, int nrows) {
+  if (L.router_packed) {
+    if (threadIdx.x == 0) {
+      const unsigned bytes = unsigned(nrows) * kRouterStride * 4;
+      mbar_arrive_expect_tx(&sm.mbar_rs, bytes);
+      bulk_g2s(&sm.rs[0][0], L.router_packed + size_t(r0) * kRouterStride, bytes, &sm.mbar_rs);
+    }
+    return true;
+  }
+  for (int idx = threadIdx.x; idx < (kE + 1) * nrows; idx += kThreads) {
+    const int e = idx / nrows, i = idx % nrows;
+    const float* row = e < kE ? L.router_w + size_t(e) * kH : L.shared_gate;
+    sm.rs[i][e] = __ldg(row + r0 + i);
+  }
+  return false;
+}
+
+// Layer li's slot-table row and routing bias into shared memory (buffer li % 2, read by that layer's top-k).
+__device__ void fetch_layer_meta(Small& sm, const DecodeParams& p, int li) {
+  const int t = threadIdx.x, layer = p.layer_begin + li;
+  if (t < kE)
+    sm.slot_row[li % 2][t] = p.src.slot_of[size_t(layer) * kE + t];
+  else if (t < 2 * kE)
+    sm.bias[li % 2][t - kE] = p.layers[li].router_bias ? p.layers[li].router_bias[t - kE] : 0.f;
+}
+
+// int16 quantisation of 2048 values by 512 threads, 4 each (thread t holds positions 4t..4t+3 in v): a 32-value
+// block is 8 adjacent threads (amax and per-16 sums by xor shuffles within the group). q written in xq_offset
+// order (4 adjacent positions stay adjacent).
+__device__ __forceinline__ void quant_x(float4 v, int16_t* q, float* scale, int32_t* sum16) {
+  const int t = threadIdx.x;
+  float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  const float inv = amax > 0.f ? 32767.f * __frcp_rn(amax) : 0.f;
+  const int a = max(-32767, min(32767, __float2int_rn(v.x * inv)));
+  const int b = max(-32767, min(32767, __float2int_rn(v.y * inv)));
+  const int cc = max(-32767, min(32767, __float2int_rn(v.z * inv)));
+  const int d = max(-32767, min(32767, __float2int_rn(v.w * inv)));
+  *reinterpret_cast<uint2*>(q + xq_offset(4 * t)) =
+      make_uint2((uint32_t(a) & 0xFFFFu) | (uint32_t(b) << 16), (uint32_t(cc) & 0xFFFFu) | (uint32_t(d) << 16));
+  int s = a + b + cc + d;
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);  // sum of 16 values (4 threads)
+  if ((t & 7) == 0) scale[t / 8] = amax / 32767.f;
+  if ((t & 3) == 0) sum16[t / 4] = s;
+}
+
+// Order-preserving map of a float onto unsigned (larger float -> larger integer); 0 is below every float.
+__device__ __forceinline__ uint32_t ordered(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float unordered(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+
+// Unpacked Q6_K codes of one (row, slot) pair for one lane: quarter s, positions 4m..4m+3 in q[s][m].
+struct DownPair {
+  uint32_t q[4][4];
+  float D[4];
+};
+
+__device__ __forceinline__ void down_unpack(const uint8_t* blk, int hh, int pq, DownPair& dp) {
+  const uint4 ql0 = lds_u2_16(blk + hh * 64 + pq), ql1 = lds_u2_16(blk + hh * 64 + 32 + pq);
+  const uint4 qh = lds_u2_16(blk + 128 + hh * 32 + pq), sc = lds_u2_16(blk + 192);
+  const float d = f16_to_f32(*reinterpret_cast<const uint16_t*>(blk + 208));
+  const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
+  const uint32_t l0[4] = {ql0.x, ql0.y, ql0.z, ql0.w}, l1[4] = {ql1.x, ql1.y, ql1.z, ql1.w};
+  const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int si = hh * 8 + 2 * s + pq / 16;
+    dp.D[s] = d * float(int8_t((scw[si / 4] >> (8 * (si % 4))) & 0xFF));
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t lw = (s % 2 == 0) ? l0[m] : l1[m];
+      dp.q[s][m] = ((lw >> (4 * (s / 2))) & 0x0F0F0F0Fu) | (((hw[m] >> (2 * s)) & 0x03030303u) << 4);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
-  __shared__ Smem sm;
+  extern __shared__ __align__(128) uint8_t dyn[];
+  Small& sm = *reinterpret_cast<Small*>(dyn);
+  uint8_t* gu_buf = dyn + (sizeof(Small) + 127) / 128 * 128;  // [chunk][gate rows 16][up rows 16]
+  uint8_t* dn_buf = gu_buf + 2 * kChunkBytes;
+  const int dn_chunk = p.dn_chunk;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int nc = gridDim.x, c = blockIdx.x;
-  if (tid == 0) sm.abort_flag = 0;
+  const int r0 = int((long long)c * kH / nc), r1 = int((long long)(c + 1) * kH / nc), nrows = r1 - r0;
+  const bool has_block = c < kHBlocks;  // h block c: slot c / 16, h indices 32 (c % 16) .. + 31
+  const int blk_slot = c / 16, blk_j0 = 32 * (c % 16);
+  const int replica = c % kReplicas;
+  unsigned epoch = 0;
+  unsigned rs_phase = 0;  // parity of the next mbar_rs phase
+#define WMOE_TRACE(li, pt)                                                                        \
+  do {                                                                                            \
+    if (p.trace && tid == 0) p.trace[(size_t(li) * kTracePoints + (pt)) * nc + c] = globaltimer(); \
+  } while (0)
+  if (tid == 0) {
+    sm.abort_flag = 0;
+    mbar_init(&sm.mbar_gu[0], 1);
+    mbar_init(&sm.mbar_gu[1], 1);
+    mbar_init(&sm.mbar_dn, 1);
+    mbar_init(&sm.mbar_rs, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    sm.dn_off = int(unsigned(r0) * kRowBytesQ6 % 16);
+  }
   __syncthreads();
+
+  // ---------------- prologue: the first layer's router sums from the input rows of this CTA
+  {
+    const DecodeLayer& L = p.layers[0];
+    for (int i = tid; i < nrows; i += kThreads) {
+      float v;
+      if (p.x_dtype == kF32)
+        v = __ldcg(static_cast<const float*>(p.x_in) + r0 + i);
+      else
+        v = __bfloat162float(static_cast<const __nv_bfloat16*>(p.x_in)[r0 + i]);
+      sm.xn[i] = v;
+    }
+    fetch_layer_meta(sm, p, 0);
+    if (fetch_router_slice(sm, L, r0, nrows)) {
+      if (!mbar_wait(&sm.mbar_rs, rs_phase, p.status, &sm.abort_flag)) return;
+      rs_phase ^= 1u;
+    }
+    __syncthreads();
+    add_router_part(sm, p.sacc + replica * kSaccStride, nrows);
+  }
+  if (!grid_barrier(p.bar, ++epoch, p.status, &sm.abort_flag)) return;
 
   for (int li = 0; li < p.n_layers; ++li) {
     const int layer = p.layer_begin + li;
     const DecodeLayer& L = p.layers[li];
+    const unsigned parity = unsigned(li & 1);
+    const double* S = p.sacc + (li % 3) * kSaccRot;
+    const bool last = li + 1 == p.n_layers;
 
-    // ---------------- phase A: input row, normalisation, quantisation, router logits
-    if (li == 0) {
-      if (p.x_dtype == kF32) {
-        const float* xi = static_cast<const float*>(p.x_in);
-        for (int i = tid; i < kH; i += kThreads) sm.resid[i] = __ldcg(xi + i);
+    // ---------------- phase B: x_l, RMS scale, router sums, routing, copies, gate_up
+    WMOE_TRACE(li, 0);
+    {
+      float4 v;
+      if (li == 0 && p.x_dtype != kF32) {
+        const uint2 b = reinterpret_cast<const uint2*>(p.x_in)[tid];
+        v = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xFFFF0000u), __uint_as_float(b.y << 16),
+                        __uint_as_float(b.y & 0xFFFF0000u));
       } else {
-        const __nv_bfloat16* xi = static_cast<const __nv_bfloat16*>(p.x_in);
-        for (int i = tid; i < kH; i += kThreads) sm.resid[i] = __bfloat162float(xi[i]);
+        const float* xi = li == 0 ? static_cast<const float*>(p.x_in) : p.xbuf + (li % 2) * kH;
+        v = __ldcg(reinterpret_cast<const float4*>(xi) + tid);
       }
-    } else {
-      const float* xi = p.xbuf + (li % 2) * kH;
-      for (int i = tid; i < kH; i += kThreads) sm.resid[i] = __ldcg(xi + i);
-    }
-    __syncthreads();
-    if (p.stack) {
-      float ss = 0.f;
-      for (int i = tid; i < kH; i += kThreads) ss = fmaf(sm.resid[i], sm.resid[i], ss);
+      reinterpret_cast<float4*>(sm.x)[tid] = v;
+      float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
       ss = warp_sum(ss);
       if (lane == 0) sm.red[warp] = ss;
-      __syncthreads();
-      if (tid == 0) {
-        float t = 0.f;
-        for (int i = 0; i < kWarps; ++i) t += sm.red[i];
-        sm.norm = 1.0f / sqrtf(t / float(kH) + p.eps);
+      quant_x(v, sm.xq, sm.xs, sm.xsum);  // the RMS factor is applied to the scales later
+      if (tid <= kE) {
+        double acc = 0.0;
+#pragma unroll
+        for (int r = 0; r < kReplicas; ++r) acc += __ldcg(S + r * kSaccStride + tid);
+        sm.logit[tid] = float(acc);
       }
-      __syncthreads();
-      for (int i = tid; i < kH; i += kThreads) sm.x[i] = sm.resid[i] * sm.norm;
-    } else {
-      for (int i = tid; i < kH; i += kThreads) sm.x[i] = sm.resid[i];
+      if (c == 0)  // this rotation buffer is next added into two layers on
+        for (int i = tid; i < kSaccRot; i += kThreads) p.sacc[((li + 2) % 3) * kSaccRot + i] = 0.0;
     }
     __syncthreads();
-    if (tid < kH / 32) quant32(sm.x + 32 * tid, sm.xq + 32 * tid, sm.xs + tid, sm.xsum + 2 * tid);
-    // router rows r = c, c + nc, ... of [R; g]: 16 warps split K, one float4 per lane
-    for (int r = c; r <= kE; r += nc) {
-      const float* row = r < kE ? L.router_w + size_t(r) * kH : L.shared_gate;
-      const int k0 = warp * (kH / kWarps) + lane * 4;
-      const float4 wv = __ldg(reinterpret_cast<const float4*>(row + k0));
-      float acc = wv.x * sm.x[k0];
-      acc = fmaf(wv.y, sm.x[k0 + 1], acc);
-      acc = fmaf(wv.z, sm.x[k0 + 2], acc);
-      acc = fmaf(wv.w, sm.x[k0 + 3], acc);
-      acc = warp_sum(acc);
-      __syncthreads();  // sm.red is reused across rows
-      if (lane == 0) sm.red[warp] = acc;
-      __syncthreads();
-      if (tid == 0) {
-        float t = 0.f;
-        for (int i = 0; i < kWarps; ++i) t += sm.red[i];
-        p.logits[r] = t;
-      }
+    WMOE_TRACE(li, 1);
+    // the next layer's slot row and bias, loaded now into a register and stored in phase C
+    int next_meta = 0;
+    if (!last) {
+      const int layer1 = layer + 1;
+      if (tid < kE)
+        next_meta = p.src.slot_of[size_t(layer1) * kE + tid];
+      else if (tid < 2 * kE && p.layers[li + 1].router_bias)
+        next_meta = __float_as_int(p.layers[li + 1].router_bias[tid - kE]);
     }
-    if (!grid_barrier(p.bar, p.status, &sm.abort_flag)) return;
-
-    // ---------------- phase B: routing (every CTA), gate_up + SwiGLU
     if (warp == 0) {
-      float v[kE / 32];
+      float t = 0.f;
+      for (int i = 0; i < kWarps; ++i) t += sm.red[i];
+      const float rsc = p.stack ? 1.0f / sqrtf(t / float(kH) + p.eps) : 1.0f;
+      // top-k by k rounds of two single-instruction warp reductions: the largest logit, then the smallest expert
+      // id holding it (ties go to the lower id)
+      uint32_t key[kE / 32];
 #pragma unroll
       for (int i = 0; i < kE / 32; ++i) {
         const int e = lane + 32 * i;
-        float l = __ldcg(p.logits + e);
-        if (L.router_bias) l += L.router_bias[e];
-        v[i] = l;
+        key[i] = ordered(sm.logit[e] * rsc + sm.bias[li % 2][e]);
       }
-      float top0 = 0.f, sum = 0.f, my_ex = 0.f;
-      int my_e = 0;
+      uint32_t my_key = 0;
+      int my_e = kE;  // lane kK keeps the shared expert's id
       for (int r = 0; r < kK; ++r) {
-        float best = -INFINITY;
-        int be = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < kE / 32; ++i) {
-          const int e = lane + 32 * i;
-          if (v[i] > best || (v[i] == best && e < be)) {
-            best = v[i];
-            be = e;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-          const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-          if (ob > best || (ob == best && oe < be)) {
-            best = ob;
-            be = oe;
-          }
-        }
+        // local maximum as a tree; ties keep the lower expert id (smaller i)
+        uint32_t m01 = key[0] >= key[1] ? key[0] : key[1], m23 = key[2] >= key[3] ? key[2] : key[3];
+        uint32_t m45 = key[4] >= key[5] ? key[4] : key[5], m67 = key[6] >= key[7] ? key[6] : key[7];
+        int i01 = key[0] >= key[1] ? 0 : 1, i23 = key[2] >= key[3] ? 2 : 3;
+        int i45 = key[4] >= key[5] ? 4 : 5, i67 = key[6] >= key[7] ? 6 : 7;
+        const uint32_t ma = m01 >= m23 ? m01 : m23, mb = m45 >= m67 ? m45 : m67;
+        const int ia = m01 >= m23 ? i01 : i23, ib = m45 >= m67 ? i45 : i67;
+        const uint32_t lm = ma >= mb ? ma : mb;
+        const int le = lane + 32 * (ma >= mb ? ia : ib);
+        const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
+        const int be = int(__reduce_min_sync(0xffffffffu, lm == m ? uint32_t(le) : 0xffffffffu));
 #pragma unroll
         for (int i = 0; i < kE / 32; ++i)
-          if (lane + 32 * i == be) v[i] = -INFINITY;
-        if (r == 0) top0 = best;
-        const float ex = expf(best - top0);
-        sum += ex;
+          if (lane + 32 * i == be) key[i] = 0u;
         if (lane == r) {
-          my_ex = ex;
+          my_key = m;
           my_e = be;
         }
       }
-      if (lane < kK) {
+      // renormalised weights of the k picks: exp(l_i - l_0) / sum_j exp(l_j - l_0)
+      const float top0 = unordered(__shfl_sync(0xffffffffu, my_key, 0));
+      const float my_ex = lane < kK ? expf(unordered(my_key) - top0) : 0.f;
+      float sum = my_ex;
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);  // lanes 0..7
+      WMOE_TRACE(li, 2);
+      // expert addresses of the k+1 slots (lane s holds slot s)
+      const uint8_t *gu = nullptr, *dn = nullptr;
+      if (lane < kSlots) {
+        if (my_e == kE) {
+          gu = L.shared_gate_up;
+          dn = L.shared_down;
+        } else {
+          const int s = sm.slot_row[li % 2][my_e];
+          if (s >= 0) {
+            gu = p.src.slab + size_t(s) * p.src.slot_bytes;
+            dn = gu + p.src.gate_up_bytes;
+          } else {
+            set_status(p.status, kStatusNotResident);
+          }
+        }
+        sm.dn_ptr[lane] = dn;
         sm.sel[lane] = my_e;
+      }
+      // this CTA's 32 gate/up row pairs: lanes 0-3 issue the four copies at once (chunk = 16 pairs)
+      const unsigned long long gu_blk =
+          __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(gu), has_block ? blk_slot : 0);
+      if (lane < 2) mbar_arrive_expect_tx(&sm.mbar_gu[lane], has_block && gu_blk ? kChunkBytes : 0u);
+      __syncwarp();
+      if (has_block && gu_blk && lane < 4) {
+        const int ch = lane / 2, up = lane % 2;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(gu_blk) +
+                             size_t(up * kF + blk_j0 + 16 * ch) * kRowBytesQ4;
+        bulk_g2s(gu_buf + ch * kChunkBytes + up * (kChunkBytes / 2), src, kChunkBytes / 2, &sm.mbar_gu[ch]);
+      }
+      WMOE_TRACE(li, 3);
+      if (lane < kK) {
         sm.w[lane] = my_ex / sum;
         if (c == 0 && p.topk_idx_out) p.topk_idx_out[li * kK + lane] = my_e;
         if (c == 0 && p.topk_w_out) p.topk_w_out[li * kK + lane] = my_ex / sum;
-        // rank of this slot in ascending expert id
         int rank = 0;
-        for (int o = 0; o < kK; ++o) {
-          const int oe = __shfl_sync(0x000000ffu, my_e, o);
-          rank += oe < my_e ? 1 : 0;
-        }
+        for (int o = 0; o < kK; ++o) rank += __shfl_sync(0x000000ffu, my_e, o) < my_e ? 1 : 0;
         sm.order[rank] = lane;
       }
       if (lane == 0) {
-        sm.sel[kK] = kE;
-        sm.w[kK] = 1.0f / (1.0f + expf(-__ldcg(p.logits + kE)));
+        sm.rscale = rsc;
+        sm.w[kK] = 1.0f / (1.0f + expf(-sm.logit[kE] * rsc));
       }
     }
     __syncthreads();
-    {
-      // the lane's 64 activations (super-block lane/4, nibble group lane%4) stay in registers
+    WMOE_TRACE(li, 4);
+    // the next layer's router slice, overlapping the copies (waited for before it is used in phase C)
+    const bool rs_copy = p.stack && !last && fetch_router_slice(sm, p.layers[li + 1], r0, nrows);
+    if (!mbar_wait(&sm.mbar_gu[0], parity, p.status, &sm.abort_flag)) return;
+    WMOE_TRACE(li, 5);
+    if (tid == 0) {
+      // down rows [r0, r1) of every slot, aligned outward to 16 bytes, after the first gate_up chunk
+      const unsigned lo = unsigned(r0) * kRowBytesQ6 / 16 * 16;
+      const unsigned hi = (unsigned(r1) * kRowBytesQ6 + 15) / 16 * 16;
+      int present = 0;
+      for (int s = 0; s < kSlots; ++s) present += sm.dn_ptr[s] ? 1 : 0;
+      mbar_arrive_expect_tx(&sm.mbar_dn, unsigned(present) * (hi - lo));
+      for (int s = 0; s < kSlots; ++s)
+        if (sm.dn_ptr[s]) bulk_g2s(dn_buf + size_t(s) * dn_chunk, sm.dn_ptr[s] + lo, hi - lo, &sm.mbar_dn);
+    }
+    if (has_block) {
       const int sb = lane / 4, g = lane % 4;
       uint32_t xw[32];
-      const uint4* xp = reinterpret_cast<const uint4*>(sm.xq + sb * 256 + 64 * g);
+      const uint4* xp = reinterpret_cast<const uint4*>(sm.xq) + lane;  // run m of this lane at (m * 32 + lane)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint4 v = xp[i];
+        const uint4 v = xp[i * 32];
         xw[4 * i] = v.x, xw[4 * i + 1] = v.y, xw[4 * i + 2] = v.z, xw[4 * i + 3] = v.w;
       }
-      const float sx0 = sm.xs[sb * 8 + 2 * g], sx1 = sm.xs[sb * 8 + 2 * g + 1];
+      const float rsc = sm.rscale;
+      const float sx0 = sm.xs[sb * 8 + 2 * g] * rsc, sx1 = sm.xs[sb * 8 + 2 * g + 1] * rsc;
       const float sum0 = float(sm.xsum[sb * 16 + 4 * g] + sm.xsum[sb * 16 + 4 * g + 1]);
       const float sum1 = float(sm.xsum[sb * 16 + 4 * g + 2] + sm.xsum[sb * 16 + 4 * g + 3]);
-      constexpr int kUnits = kSlots * kF, kRowBytes = kH / 256 * Q4K_BYTES;
-      const int u0 = int((long long)c * kUnits / nc), u1 = int((long long)(c + 1) * kUnits / nc);
-      for (int u = u0 + warp; u < u1; u += kWarps) {
-        const int slot = u / kF, j = u % kF;
-        const int e = sm.sel[slot];
-        const uint8_t* w;
-        if (e == kE) {
-          w = L.shared_gate_up;
-        } else {
-          const int s = p.src.slot_of[size_t(layer) * kE + e];
-          if (s < 0) {
-            set_status(p.status, kStatusNotResident);
-            continue;
-          }
-          w = p.src.slab + size_t(s) * p.src.slot_bytes;
-        }
-        const Q4L gw = q4_load(w + size_t(j) * kRowBytes + sb * Q4K_BYTES, g);
-        const Q4L uw = q4_load(w + size_t(kF + j) * kRowBytes + sb * Q4K_BYTES, g);
-        float gs = q4_dot(gw, xw, sx0, sx1, sum0, sum1);
-        float us = q4_dot(uw, xw, sx0, sx1, sum0, sum1);
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        if (ch == 1 && !mbar_wait(&sm.mbar_gu[1], parity, p.status, &sm.abort_flag)) return;
+        const uint8_t* gate = gu_buf + ch * kChunkBytes + warp * kRowBytesQ4 + sb * Q4K_BYTES;
+        const uint8_t* up = gate + kChunkBytes / 2;
+        float gs = q4_dot_smem(gate, g, xw, sx0, sx1, sum0, sum1);
+        float us = q4_dot_smem(up, g, xw, sx0, sx1, sum0, sum1);
         gs = warp_sum(gs);
         us = warp_sum(us);
-        if (lane == 0) p.hbuf[slot * kF + j] = silu(gs) * us;
+        if (lane == 0) sm.hblk[16 * ch + warp] = silu(gs) * us;
       }
-    }
-    if (!grid_barrier(p.bar, p.status, &sm.abort_flag)) return;
-
-    // ---------------- phase C: down for this CTA's rows, combine, residual
-    for (int b = tid; b < kSlots * kF / 32; b += kThreads) {
-      const int slot = b / (kF / 32), blk = b % (kF / 32);
-      float v[32];
-      const float4* hp = reinterpret_cast<const float4*>(p.hbuf + slot * kF + 32 * blk);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 f = __ldcg(hp + i);
-        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
-      }
-      quant32(v, &sm.hq[slot][32 * blk], &sm.hs[slot][blk], &sm.hsum[slot][2 * blk]);
     }
     __syncthreads();
-    const int r0 = int((long long)c * kH / nc), r1 = int((long long)(c + 1) * kH / nc);
-    const int nrows = r1 - r0;
-    {
-      const int grp = tid / 8, t8 = tid % 8;
-      const unsigned gmask = 0xFFu << (8 * (lane / 8));
-      const int sb = t8 / 4, hh = (t8 / 2) % 2, pq = 16 * (t8 % 2);
-      const int base = sb * 256 + hh * 128 + pq;
-      for (int pr = grp; pr < nrows * kSlots; pr += kThreads / 8) {
+    WMOE_TRACE(li, 6);
+    // the block's h, quantised once, in the order the down lanes read it; then this CTA arrives at S2
+    if (warp == 0) {
+      if (has_block) {
+        const int pos = blk_j0 + lane, blk = blk_j0 / 32;
+        quant32_warp(sm.hblk[lane], lane, p.hq + blk_slot * kF, hq_offset(pos), p.hs + blk_slot * (kF / 32) + blk,
+                     p.hsum + blk_slot * (kF / 16) + 2 * blk);
+      }
+      __syncwarp();
+      if (lane == 0) grid_arrive(p.bar);
+    }
+    ++epoch;
+    // down codes of this thread's (row, slot) pairs, unpacked while S2 completes
+    const int grp = tid / 8, t8 = tid % 8;
+    const int sb = t8 / 4, hh = (t8 / 2) % 2, pq = 16 * (t8 % 2);
+    const int base = sb * 256 + hh * 128 + pq;
+    DownPair dp[kMaxPairs];
+    if (!mbar_wait(&sm.mbar_dn, parity, p.status, &sm.abort_flag)) return;
+#pragma unroll
+    for (int k = 0; k < kMaxPairs; ++k) {
+      const int pr = grp + k * (kThreads / 8);
+      if (pr < nrows * kSlots) {
         const int rl = pr / kSlots, slot = pr % kSlots;
-        const int e = sm.sel[slot];
-        const uint8_t* w;
-        bool ok = true;
-        if (e == kE) {
-          w = L.shared_down;
-        } else {
-          const int s = p.src.slot_of[size_t(layer) * kE + e];
-          ok = s >= 0;
-          w = p.src.slab + size_t(ok ? s : 0) * p.src.slot_bytes + p.src.gate_up_bytes;
-        }
+        down_unpack(dn_buf + size_t(slot) * dn_chunk + sm.dn_off + rl * kRowBytesQ6 + sb * Q6K_BYTES, hh, pq, dp[k]);
+      }
+    }
+    WMOE_TRACE(li, 7);
+    if (!grid_wait(p.bar, epoch, p.status, &sm.abort_flag)) return;
+    WMOE_TRACE(li, 8);
+
+    // ---------------- phase C: h, down rows of this CTA, combine, next layer's router sums
+    if (!last) {  // the next layer's slot row and bias (read by its top-k after S1)
+      if (tid < kE)
+        sm.slot_row[(li + 1) % 2][tid] = next_meta;
+      else if (tid < 2 * kE)
+        sm.bias[(li + 1) % 2][tid - kE] = __int_as_float(next_meta);
+    }
+    {
+      constexpr int kVec = kSlots * kF / 8;  // 576 runs of 8 int16
+      const uint4* src = reinterpret_cast<const uint4*>(p.hq);
+      uint4* dst = reinterpret_cast<uint4*>(&sm.hq[0][0]);
+      for (int i = tid; i < kVec; i += kThreads) dst[i] = __ldcg(src + i);
+      for (int i = tid; i < kSlots * kF / 32; i += kThreads) (&sm.hs[0][0])[i] = __ldcg(p.hs + i);
+      for (int i = tid; i < kSlots * kF / 16; i += kThreads) (&sm.hsum[0][0])[i] = __ldcg(p.hsum + i);
+    }
+    __syncthreads();
+    WMOE_TRACE(li, 9);
+    {
+      const unsigned gmask = 0xFFu << (8 * (lane / 8));
+#pragma unroll
+      for (int k = 0; k < kMaxPairs; ++k) {
+        const int pr = grp + k * (kThreads / 8);
+        if (pr >= nrows * kSlots) break;  // uniform within the 8-lane group
+        const int rl = pr / kSlots, slot = pr % kSlots;
         float part = 0.f;
-        if (ok) {
-          const uint8_t* blk = w + size_t(r0 + rl) * (kF / 256 * Q6K_BYTES) + sb * Q6K_BYTES;
-          const uint4 ql0 = ldg_u2_16(blk + hh * 64 + pq), ql1 = ldg_u2_16(blk + hh * 64 + 32 + pq);
-          const uint4 qh = ldg_u2_16(blk + 128 + hh * 32 + pq), sc = ldg_u2_16(blk + 192);
-          const float d = f16_to_f32(__ldg(reinterpret_cast<const unsigned short*>(blk + 208)));
-          const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
-          const uint32_t l0[4] = {ql0.x, ql0.y, ql0.z, ql0.w}, l1[4] = {ql1.x, ql1.y, ql1.z, ql1.w};
-          const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            const int si = hh * 8 + 2 * s + pq / 16;
-            const float D = d * float(int8_t((scw[si / 4] >> (8 * (si % 4))) & 0xFF));
-            const uint4* xp = reinterpret_cast<const uint4*>(&sm.hq[slot][base + 32 * s]);
-            const uint4 xa = xp[0], xb = xp[1];
-            const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-            int acc = 0;
+        for (int s = 0; s < 4; ++s) {
+          // runs of 8 of this lane task: (s, 0) and (s, 1), each group's eight tasks adjacent
+          const uint4* xp = reinterpret_cast<const uint4*>(sm.hq[slot]) + (s * 2) * 8 + t8;
+          const uint4 xa = xp[0], xb = xp[8];
+          const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+          int acc = 0;
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              const uint32_t lw = (s % 2 == 0) ? l0[m] : l1[m];
-              const uint32_t q = ((lw >> (4 * (s / 2))) & 0x0F0F0F0Fu) | (((hw[m] >> (2 * s)) & 0x03030303u) << 4);
-              acc = dp2a_lo(xw[2 * m], q, acc);
-              acc = dp2a_hi(xw[2 * m + 1], q, acc);
-            }
-            const int pos = base + 32 * s;
-            part += sm.hs[slot][pos / 32] * (D * float(acc - 32 * sm.hsum[slot][pos / 16]));
+          for (int m = 0; m < 4; ++m) {
+            acc = dp2a_lo(xw[2 * m], dp[k].q[s][m], acc);
+            acc = dp2a_hi(xw[2 * m + 1], dp[k].q[s][m], acc);
           }
-        } else {
-          set_status(p.status, kStatusNotResident);
+          const int pos = base + 32 * s;
+          part += sm.hs[slot][pos / 32] * (dp[k].D[s] * float(acc - 32 * sm.hsum[slot][pos / 16]));
         }
         part += __shfl_xor_sync(gmask, part, 4);
         part += __shfl_xor_sync(gmask, part, 2);
@@ -401,6 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       }
     }
     __syncthreads();
+    WMOE_TRACE(li, 10);
     if (tid < nrows) {
       const int r = r0 + tid;
       float acc = 0.f;
@@ -410,8 +651,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         acc = __fadd_rn(acc, __fmul_rn(sm.ys[tid][slot], sm.w[slot]));
       }
       acc = __fadd_rn(acc, __fmul_rn(sm.w[kK], sm.ys[tid][kK]));
-      if (p.stack) acc = __fadd_rn(sm.resid[r], acc);
-      if (li + 1 < p.n_layers) {
+      if (p.stack) acc = __fadd_rn(sm.x[r], acc);
+      sm.xn[tid] = acc;
+      if (!last) {
         p.xbuf[((li + 1) % 2) * kH + r] = acc;
       } else if (p.out_dtype == kF32) {
         static_cast<float*>(p.out)[r] = acc;
@@ -419,38 +661,66 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         static_cast<__nv_bfloat16*>(p.out)[r] = __float2bfloat16_rn(acc);
       }
     }
-    if (li + 1 < p.n_layers)
-      if (!grid_barrier(p.bar, p.status, &sm.abort_flag)) return;
+    if (!last) {
+      if (rs_copy && !mbar_wait(&sm.mbar_rs, rs_phase, p.status, &sm.abort_flag)) return;
+      if (rs_copy) rs_phase ^= 1u;
+      __syncthreads();
+      add_router_part(sm, p.sacc + ((li + 1) % 3) * kSaccRot + replica * kSaccStride, nrows);
+      WMOE_TRACE(li, 11);
+      if (!grid_barrier(p.bar, ++epoch, p.status, &sm.abort_flag)) return;
+    }
   }
+#undef WMOE_TRACE
+}
+
+// one slot's down rows of a CTA, aligned outward to 16 bytes, plus the 4 bytes a funnel-shift load may read past
+int down_chunk_bytes(int nc) { return ((kH + nc - 1) / nc * kRowBytesQ6 + 32 + 15) / 16 * 16; }
+
+size_t smem_bytes(int nc) {
+  return (sizeof(Small) + 127) / 128 * 128 + 2 * size_t(kChunkBytes) + size_t(kSlots) * down_chunk_bytes(nc) + 64;
 }
 
 }  // namespace
 
 size_t decode_scratch_bytes(int H, int F, int E, int) {
-  return size_t(2 * H + (E + 1) + kSlots * F) * sizeof(float) + 64 * sizeof(unsigned) + 1024;
+  // barrier line, x ping-pong, router sums, then quantised h with its scales and per-16 sums
+  return 256 + size_t(2 * H) * sizeof(float) + 3 * size_t(kSaccRot) * sizeof(double) +
+         size_t(kSlots * F) * sizeof(int16_t) + size_t(kSlots * F / 32) * sizeof(float) +
+         size_t(kSlots * F / 16) * sizeof(int32_t) + 256;
 }
 
 int decode_num_ctas(int device) {
   int coop = 0, sms = 0, per_sm = 0;
   if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device) != cudaSuccess || !coop) return 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, kThreads, 0) != cudaSuccess) return 0;
-  return per_sm >= 1 && sms >= 64 ? sms : 0;
+  // one h block per CTA; every CTA at most kMaxRows output rows and kMaxPairs (row, slot) pairs per 8-lane group
+  if (sms < kHBlocks || (kH + sms - 1) / sms > kMaxRows || (kH + sms - 1) / sms * kSlots > kMaxPairs * (kThreads / 8))
+    return 0;
+  const size_t smem = smem_bytes(sms);
+  if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, kThreads, smem) != cudaSuccess) return 0;
+  return per_sm >= 1 ? sms : 0;
 }
 
 cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_layers, const DecodeLayer* layers,
                               int H, int F, int E, int k, float eps, bool stack, const void* x_in, int x_dtype,
-                              void* out,
-                              int out_dtype, int32_t* topk_idx_out, float* topk_w_out, void* scratch,
-                              int num_ctas, int* status, cudaStream_t st, int* launches) {
-  if (H != kH || F != kF || E != kE || k != kK || num_ctas <= 0) return cudaErrorInvalidValue;
+                              void* out, int out_dtype, int32_t* topk_idx_out, float* topk_w_out, void* scratch,
+                              int num_ctas, int* status, uint64_t* trace, size_t trace_entries, cudaStream_t st,
+                              int* launches) {
+  if (H != kH || F != kF || E != kE || k != kK || num_ctas < kHBlocks) return cudaErrorInvalidValue;
+  // the trace covers the first launch's layers when it is large enough, else it is off
+  if (trace && trace_entries < size_t(std::min(n_layers, kMaxLayers)) * kTracePoints * size_t(num_ctas))
+    trace = nullptr;
   char* base = static_cast<char*>(scratch);
   unsigned* bar = reinterpret_cast<unsigned*>(base);
   float* xbuf = reinterpret_cast<float*>(base + 256);
-  float* logits = xbuf + 2 * kH;
-  float* hbuf = logits + (kE + 1 + 63) / 64 * 64;
-  cudaError_t e = cudaMemsetAsync(bar, 0, 64 * sizeof(unsigned), st);
-  if (e != cudaSuccess) return e;
+  double* sacc = reinterpret_cast<double*>(xbuf + 2 * kH);
+  int16_t* hq = reinterpret_cast<int16_t*>(sacc + 3 * kSaccRot);
+  float* hs = reinterpret_cast<float*>(hq + kSlots * kF);
+  int32_t* hsum = reinterpret_cast<int32_t*>(hs + kSlots * kF / 32);
+  const size_t smem = smem_bytes(num_ctas);
+  cudaError_t e = cudaSuccess;
   for (int l0 = 0; l0 < n_layers; l0 += kMaxLayers) {
     DecodeParams p{};
     p.src = src;
@@ -465,14 +735,22 @@ cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_la
     p.topk_idx_out = topk_idx_out ? topk_idx_out + l0 * kK : nullptr;
     p.topk_w_out = topk_w_out ? topk_w_out + l0 * kK : nullptr;
     p.xbuf = xbuf;
-    p.logits = logits;
-    p.hbuf = hbuf;
+    p.sacc = sacc;
+    p.hq = hq;
+    p.hs = hs;
+    p.hsum = hsum;
     p.bar = bar;
     p.status = status;
+    p.dn_chunk = down_chunk_bytes(num_ctas);
+    p.trace = l0 == 0 ? reinterpret_cast<unsigned long long*>(trace) : nullptr;
     for (int i = 0; i < p.n_layers; ++i) p.layers[i] = layers[l0 + i];
+    // barrier counter and the router sums start at zero for every launch
+    e = cudaMemsetAsync(base, 0, 256, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(sacc, 0, 3 * size_t(kSaccRot) * sizeof(double), st);
+    if (e != cudaSuccess) return e;
     void* args[] = {&p};
     e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(decode_kernel), dim3(num_ctas), dim3(kThreads),
-                                    args, 0, st);
+                                    args, smem, st);
     if (e != cudaSuccess) return e;
     ++*launches;
   }

@@ -73,14 +73,18 @@ struct DecodeLayer {
   const float* shared_gate;
   const uint8_t* shared_gate_up;
   const uint8_t* shared_down;
+  const float* router_packed;  // [H][kRouterStride] or null
 };
+constexpr int kRouterStride = 264;
+cudaError_t pack_router(const float* router_w, const float* shared_gate, int E, int H, float* out, cudaStream_t st);
 size_t decode_scratch_bytes(int H, int F, int E, int num_ctas);
 int decode_num_ctas(int device);
 cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_layers, const DecodeLayer* layers,
                               int H, int F, int E, int k, float eps, bool stack, const void* x_in, int x_dtype,
                               void* out,
                               int out_dtype, int32_t* topk_idx_out, float* topk_w_out, void* scratch,
-                              int num_ctas, int* status, cudaStream_t st, int* launches);
+                              int num_ctas, int* status, uint64_t* trace, size_t trace_entries, cudaStream_t st,
+                              int* launches);
 
 // store.cu: device generator
 cudaError_t fill_synthetic(uint8_t* dst, uint64_t seed, const int32_t* layer_expert /*[n][2]*/, int n,

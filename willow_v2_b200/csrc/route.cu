@@ -204,6 +204,30 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
   if (lane == 0 && shared_s) shared_s[t] = 1.0f / (1.0f + expf(-row[E]));
 }
 
+// out[h][e] = R[e][h] for e < E, out[h][E] = g[h], zero up to the stride: 32 x 32 tiles through shared memory.
+__global__ void pack_router_kernel(const float* __restrict__ R, const float* __restrict__ g, int E, int H,
+                                   float* __restrict__ out) {
+  __shared__ float tile[32][33];
+  const int e0 = blockIdx.y * 32, h0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int e = e0 + i, h = h0 + threadIdx.x;
+    float v = 0.f;
+    if (h < H) v = e < E ? R[size_t(e) * H + h] : (e == E ? g[h] : 0.f);
+    tile[i][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int h = h0 + i, e = e0 + threadIdx.x;
+    if (h < H && e < kRouterStride) out[size_t(h) * kRouterStride + e] = tile[threadIdx.x][i];
+  }
+}
+
+cudaError_t pack_router(const float* router_w, const float* shared_gate, int E, int H, float* out, cudaStream_t st) {
+  const dim3 grid(unsigned((H + 31) / 32), unsigned((kRouterStride + 31) / 32));
+  pack_router_kernel<<<grid, dim3(32, 8), 0, st>>>(router_w, shared_gate, E, H, out);
+  return cudaGetLastError();
+}
+
 cudaError_t router_topk(const float* logits, int T, int E, int k, const float* bias, float* topk_w,
                         int32_t* topk_idx, float* shared_s, float* logits_out, cudaStream_t st, int* launches) {
   const unsigned grid = unsigned((T + 7) / 8);

@@ -21,6 +21,8 @@ struct wmoe_ctx {
   size_t scratch_bytes = 0;
   int decode_ctas = 0;      // CTAs of the persistent decode kernel (all co-resident)
   bool use_decode_kernel = true;
+  uint64_t* trace = nullptr;  // decode phase timestamps (device), or null
+  size_t trace_entries = 0;
 };
 
 struct wmoe_store {

@@ -22,10 +22,13 @@ SIGNATURES = {
     "wmoe_last_error": (ctypes.c_char_p, [_p]),
     "wmoe_launch_count": (_u64, [_p]),
     "wmoe_set_decode_kernel": (_i, [_p, _i]),
+    "wmoe_set_trace": (_i, [_p, _p, _sz]),
+    "wmoe_decode_ctas": (_i, [_p]),
     "wmoe_device_status": (_i, [_p, ctypes.POINTER(_i), _p]),
     "wmoe_dequant": (_i, [_p, _i, _p, _sz, _p, _i, _p]),
     "wmoe_route": (_i, [_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p]),
     "wmoe_dispatch": (_i, [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p]),
+    "wmoe_pack_router": (_i, [_p, _p, _p, _i, _i, _p, _p]),
     "wmoe_store_create": (_i, [_p, _i, _i, _i, _i, _sz, _pp]),
     "wmoe_store_destroy": (None, [_p]),
     "wmoe_store_upload": (_i, [_p, _i, _i, _p, _p]),
@@ -45,7 +48,10 @@ SIGNATURES = {
 class LayerWeights(ctypes.Structure):
     """wmoe_layer_weights: device pointers of one layer's router, bias, shared gate and shared expert."""
     _fields_ = [("router_w", _p), ("router_bias", _p), ("shared_gate", _p), ("shared_gate_up", _p),
-                ("shared_down", _p)]
+                ("shared_down", _p), ("router_packed", _p)]
+
+
+ROUTER_STRIDE = 264  # WMOE_ROUTER_STRIDE
 
 
 def _load():

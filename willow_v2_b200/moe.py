@@ -199,19 +199,33 @@ class ExpertStore:
             pass
 
 
+def pack_router(router_w: torch.Tensor, shared_gate: torch.Tensor, ctx: Optional[Context] = None) -> torch.Tensor:
+    """The router [E, H] and shared gate [H] transposed into one f32 [H, 264] matrix (wmoe_pack_router): the
+    decode kernel reads each CTA's rows of it as one contiguous block."""
+    ctx = ctx or default_context()
+    E, H = router_w.shape
+    out = torch.empty(H, _lib.ROUTER_STRIDE, dtype=torch.float32, device=router_w.device)
+    check(ctx.handle, lib.wmoe_pack_router(ctx.handle, _ptr(router_w.contiguous()), _ptr(shared_gate.contiguous()),
+                                           E, H, _ptr(out), _stream()))
+    return out
+
+
 @dataclass
 class LayerWeights:
     """One layer's non-routed MoE weights on the GPU: router f32 [E, H], optional routing bias f32 [E], shared
-    expert gate vector f32 [H], shared expert gate_up (Q4_K bytes, uint8) and down (Q6_K bytes, uint8)."""
+    expert gate vector f32 [H], shared expert gate_up (Q4_K bytes, uint8) and down (Q6_K bytes, uint8), and the
+    packed router (made on first use by decode_stack)."""
     router_w: torch.Tensor
     shared_gate: torch.Tensor
     shared_gate_up: torch.Tensor
     shared_down: torch.Tensor
     router_bias: Optional[torch.Tensor] = None
+    router_packed: Optional[torch.Tensor] = None
 
     def as_struct(self) -> _lib.LayerWeights:
-        return _lib.LayerWeights(self.router_w.data_ptr(), None if self.router_bias is None else self.router_bias.data_ptr(),
-                                 self.shared_gate.data_ptr(), self.shared_gate_up.data_ptr(), self.shared_down.data_ptr())
+        opt = lambda t: None if t is None else t.data_ptr()
+        return _lib.LayerWeights(self.router_w.data_ptr(), opt(self.router_bias), self.shared_gate.data_ptr(),
+                                 self.shared_gate_up.data_ptr(), self.shared_down.data_ptr(), opt(self.router_packed))
 
 
 def moe_forward(store: ExpertStore, layer: int, x: torch.Tensor, lw: LayerWeights, top_k: int = 8,
@@ -232,13 +246,16 @@ def moe_forward(store: ExpertStore, layer: int, x: torch.Tensor, lw: LayerWeight
 
 
 def decode_stack(store: ExpertStore, layers: list, h: torch.Tensor, eps: float = 1e-6, layer_begin: int = 0,
-                 out: Optional[torch.Tensor] = None, return_routing: bool = False):
+                 out: Optional[torch.Tensor] = None, return_routing: bool = False, pack: bool = True):
     """One decode token through len(layers) stacked blocks, h <- h + moe(rms_norm(h)) per layer, in one persistent
-    launch. h: f32 [H] (or [1, H]) on the GPU."""
+    launch. h: f32 [H] (or [1, H]) on the GPU. pack: give each layer a packed router first (the fast layout)."""
     ctx = store.ctx
     h = h.reshape(-1).contiguous()
     assert h.dtype == torch.float32
     out = torch.empty_like(h) if out is None else out
+    for lw in layers:
+        if pack and lw.router_packed is None:
+            lw.router_packed = pack_router(lw.router_w, lw.shared_gate, ctx)
     arr = (_lib.LayerWeights * len(layers))(*[lw.as_struct() for lw in layers])
     sel = torch.empty(len(layers), 8, dtype=torch.int32, device=h.device) if return_routing else None
     check(ctx.handle, lib.wmoe_decode_stack(ctx.handle, store.handle, layer_begin, len(layers),
