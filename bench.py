@@ -91,15 +91,15 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def setup_model(device: int):
-    """The 40-layer model on the GPU: synthetic routed experts generated in HBM, router/shared weights uploaded."""
+def setup_model(device: int, n_layers: int = LAYERS):
+    """The model on the GPU: synthetic routed experts generated in HBM, router/shared weights uploaded."""
     import torch
     from willow_v2_b200 import moe, synth
     ctx = moe.Context(device)
-    store = moe.ExpertStore(LAYERS, EXPERTS, HIDDEN, FFN, ctx=ctx)
+    store = moe.ExpertStore(n_layers, EXPERTS, HIDDEN, FFN, ctx=ctx)
     store.fill_synthetic(SEED)
     layers = []
-    for l in range(LAYERS):
+    for l in range(n_layers):
         layers.append(moe.LayerWeights(
             router_w=torch.from_numpy(synth.router_weight(SEED, l)).cuda(),
             shared_gate=torch.from_numpy(synth.shared_gate_weight(SEED, l)).cuda(),
@@ -113,7 +113,8 @@ def run_decode40(args, rank: int, world: int, dist):
     import torch
     from willow_v2_b200 import moe, synth
     device = torch.cuda.current_device()
-    ctx, store, layers = setup_model(device)
+    n_layers = args.layers
+    ctx, store, layers = setup_model(device, n_layers)
     K, W = args.steps, args.warmup
     # a new token per step (different routing every step); inputs resident before the timed region
     h_all = torch.from_numpy(np.concatenate([synth.hidden(SEED + 1000 * rank, 1, step=s) for s in range(K + W)])).cuda()
@@ -163,21 +164,23 @@ def run_decode40(args, rank: int, world: int, dist):
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms, e2e_ms = times.tolist()
     hbm, _, peak_kind = peaks()
-    expert_bytes = LAYERS * (TOP_K + 1) * EXPERT_BYTES
+    expert_bytes = n_layers * (TOP_K + 1) * EXPERT_BYTES
     achieved = expert_bytes / (ms * 1e-3) / 1e9
     result = {
         "metric": METRIC, "value": world * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks with the config-0 distributions; random-init router)",
-        "config": {"workload": "configs[1]: decode 1 token x 40 MoE layers, all experts resident", "hidden": HIDDEN,
-                   "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": LAYERS, "tokens_per_step": 1,
+        "config": {"workload": ("configs[1]: decode 1 token x 40 MoE layers, all experts resident" if n_layers == LAYERS
+                                else f"profiling case: decode 1 token x {n_layers} layers (not the benchmark)"),
+                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": n_layers,
+                   "tokens_per_step": 1,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2: 734 MB of expert weights per step, a new token (new routing) each step"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": None, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": expert_bytes,
                      "frac_of_8TBps": achieved / 8000.0,
-                     "all_bytes_per_launch": expert_bytes + LAYERS * ROUTER_BYTES},
+                     "all_bytes_per_launch": expert_bytes + n_layers * ROUTER_BYTES},
         "e2e": {"value": world * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": HIDDEN * 4,
                 "d2h_bytes_per_step": HIDDEN * 4},
         "gpu_launches": int(gpu_launches),
@@ -264,6 +267,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode40", choices=["decode40"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="stack depth (40 = the benchmark; fewer = profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
