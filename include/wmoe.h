@@ -163,6 +163,27 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
                       const wmoe_layer_weights* layers, float eps, const float* h_in, float* h_out,
                       int32_t* topk_idx_out, void* stream);
 
+/* wmoe_decode_stack for callers that cannot allocate device memory: it has no counterpart in willow. It calls no
+ * cudaMalloc/cudaFree and no allocating library routine. Its scratch is a fixed file-scope device array of
+ * WMOE_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the process exits. Shapes needing more
+ * scratch are refused with WMOE_ERR_CAPACITY.
+ *
+ * Who needs it: code that runs where allocation is not allowed or not safe, for example
+ *   - a caller issuing work while a CUDA graph is being captured on its stream (cudaMalloc there fails or breaks
+ *     the capture);
+ *   - an engine whose device memory is owned by a pool allocator it must not bypass;
+ *   - a latency-critical decode loop that must never hit a growing scratch buffer (wmoe_decode_stack grows the
+ *     context's scratch with cudaMalloc on first use).
+ *
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture. Every call on a device shares the one array, which keeps the last call's contents (the
+ * kernel zeroes what must start at zero), so calls that overlap on the GPU - on different streams, or from
+ * different contexts of one process on the same device - race and must be serialised by the caller. */
+#define WMOE_NOALLOC_SCRATCH_BYTES (160u * 1024u)
+int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
+                              const wmoe_layer_weights* layers, float eps, const float* h_in, float* h_out,
+                              int32_t* topk_idx_out, void* stream);
+
 /* Several experts' [rows, k] Q4_K or Q6_K weights times one token: y[i] = W_i x for i < n.
  * weights: device array of n device pointers; x f32 [k]; y f32 [n, rows]. */
 int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, int n, int rows, int k,

@@ -408,6 +408,48 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
   return WMOE_OK;
 }
 
+int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
+                              const wmoe_layer_weights* layers, float eps, const float* h_in, float* h_out,
+                              int32_t* topk_idx_out, void* stream) {
+  // Same work as wmoe_decode_stack; the scratch is the file-scope device array of decode.cu instead of the
+  // context's cudaMalloc'd buffer, so nothing here allocates.
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: bad store");
+  if (store->capped)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_decode_stack_noalloc: needs every expert resident");
+  if (layer_begin < 0 || n_layers <= 0 || layer_begin + n_layers > store->layers || !layers || !h_in || !h_out)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: bad arguments");
+  if (store->hidden != 2048 || store->ffn != 512 || store->experts != 256)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED,
+                    "wmoe_decode_stack_noalloc: this build runs hidden 2048, ffn 512, 256 experts");
+  if (ctx->decode_ctas <= 0)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED,
+                    "wmoe_decode_stack_noalloc: the persistent kernel cannot be co-resident here");
+  for (int i = 0; i < n_layers; ++i)
+    if (!layers[i].router_w || !layers[i].shared_gate || !layers[i].shared_gate_up || !layers[i].shared_down)
+      return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: null weight pointer in layers[]");
+  const size_t need = decode_scratch_bytes(store->hidden, store->ffn, store->experts, ctx->decode_ctas);
+  if (need > static_scratch_bytes())
+    return ctx_fail(ctx, WMOE_ERR_CAPACITY,
+                    "wmoe_decode_stack_noalloc: needs " + std::to_string(need) + " bytes of scratch, more than the " +
+                        std::to_string(static_scratch_bytes()) + "-byte static array");
+  int current = -1;
+  WMOE_CHECK_CUDA(ctx, cudaGetDevice(&current), "wmoe_decode_stack_noalloc");
+  if (current != ctx->device)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: make the context's device current first");
+  void* scratch = nullptr;
+  WMOE_CHECK_CUDA(ctx, static_scratch(ctx->device, &scratch), "wmoe_decode_stack_noalloc: static scratch address");
+  int n = 0;
+  const ExpertSource src = store_source(store, nullptr, nullptr);
+  const cudaError_t e = decode_persistent(src, layer_begin, n_layers, reinterpret_cast<const DecodeLayer*>(layers),
+                                          store->hidden, store->ffn, store->experts, 8, eps, true, h_in, WMOE_F32,
+                                          h_out, WMOE_F32, topk_idx_out, nullptr, scratch, ctx->decode_ctas,
+                                          ctx->d_status, nullptr, 0, static_cast<cudaStream_t>(stream), &n);
+  ctx->launches += uint64_t(n);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack_noalloc");
+  return WMOE_OK;
+}
+
 int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, int n, int rows, int k,
                     const float* x, float* y, void* stream) {
   if (!ctx) return WMOE_ERR_INVALID;

@@ -24,6 +24,7 @@
 // Barrier and mbarrier waits are bounded (1 s of %globaltimer): a timeout sets the device status word and
 // every CTA returns instead of hanging (by then every copy it issued has long completed).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -681,6 +682,32 @@ size_t smem_bytes(int nc) {
 }
 
 }  // namespace
+
+// Scratch of the no-allocation entry point (wmoe_decode_stack_noalloc): file-scope device memory of a fixed size,
+// one copy on every GPU that loads the library, held until the process exits. Host code cannot use the symbol as
+// a device address (it is a host-side stand-in); static_scratch() looks the address up per device.
+constexpr size_t kStaticScratchBytes = 160u * 1024u;  // WMOE_NOALLOC_SCRATCH_BYTES
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+size_t static_scratch_bytes() { return kStaticScratchBytes; }
+
+// Device address of g_static_scratch on the current device, looked up once per device (the first call on a device
+// must come before any stream capture). Returns the CUDA error of the lookup.
+cudaError_t static_scratch(int device, void** ptr) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return e;
+    addr[device] = p;
+  }
+  *ptr = addr[device];
+  return cudaSuccess;
+}
 
 size_t decode_scratch_bytes(int H, int F, int E, int) {
   // barrier line, x ping-pong, router sums, then quantised h with its scales and per-16 sums

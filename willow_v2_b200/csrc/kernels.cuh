@@ -78,6 +78,8 @@ struct DecodeLayer {
 constexpr int kRouterStride = 264;
 cudaError_t pack_router(const float* router_w, const float* shared_gate, int E, int H, float* out, cudaStream_t st);
 size_t decode_scratch_bytes(int H, int F, int E, int num_ctas);
+size_t static_scratch_bytes();
+cudaError_t static_scratch(int device, void** ptr);  // the no-allocation entry point's scratch on a device
 int decode_num_ctas(int device);
 cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_layers, const DecodeLayer* layers,
                               int H, int F, int E, int k, float eps, bool stack, const void* x_in, int x_dtype,

@@ -41,6 +41,7 @@ SIGNATURES = {
                               ctypes.POINTER(_u64)]),
     "wmoe_moe_forward": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _i, _p, _p, _p]),
     "wmoe_decode_stack": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
+    "wmoe_decode_stack_noalloc": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
     "wmoe_gemv_batch": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
 }
 
