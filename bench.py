@@ -28,6 +28,9 @@ sys.path.insert(0, REPO)
 HIDDEN, FFN, EXPERTS, TOP_K = 2048, 512, 256, 8
 EXPERT_BYTES = 2 * FFN * HIDDEN // 256 * 144 + HIDDEN * FFN // 256 * 210   # 2,039,808
 ROUTER_BYTES = EXPERTS * HIDDEN * 4 + HIDDEN * 4                           # router + shared gate, fp32
+# DRAM bytes (read + write) per layer of decode_kernel, measured by ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum) on a 4-layer launch: 82,234,880 + 1,487,360 bytes; traffic grows with the layers
+TRAFFIC_PER_LAYER = (82_234_880 + 1_487_360) / 4
 LAYERS = 40
 SEED = 0
 METRIC = "MoE decode tokens/s (40-layer qwen35moe stack, 1 token per step)"
@@ -177,7 +180,7 @@ def run_decode40(args, rank: int, world: int, dist):
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2: 734 MB of expert weights per step, a new token (new routing) each step"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": None, "peak_kind": peak_kind,
+                     "traffic": n_layers * TRAFFIC_PER_LAYER, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": expert_bytes,
                      "frac_of_8TBps": achieved / 8000.0,
                      "all_bytes_per_launch": expert_bytes + n_layers * ROUTER_BYTES},
