@@ -102,6 +102,13 @@ int wmoe_set_trace(wmoe_ctx* ctx, uint64_t* trace, size_t entries) {
 
 int wmoe_decode_ctas(const wmoe_ctx* ctx) { return ctx ? ctx->decode_ctas : 0; }
 
+int wmoe_set_prefill_threshold(wmoe_ctx* ctx, int tokens) {
+  if (!ctx || tokens < 1) return WMOE_ERR_INVALID;
+  const int prev = ctx->prefill_threshold;
+  ctx->prefill_threshold = tokens;
+  return prev;
+}
+
 int wmoe_set_decode_kernel(wmoe_ctx* ctx, int enable) {
   if (!ctx) return WMOE_ERR_INVALID;
   const int prev = ctx->use_decode_kernel ? 1 : 0;
@@ -305,6 +312,9 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
   const size_t o_nused = plan.take<int32_t>(1);
   const size_t o_disp = plan.bytes;
   plan.bytes += (dispatch_scratch_bytes(T, E) + 255) / 256 * 256;
+  // many tokens per expert: tcgen05 grouped GEMMs; few: the dequant-GEMV kernels (their buffers share the region)
+  const bool gemm_path = T >= ctx->prefill_threshold;
+  const size_t o_region = plan.bytes;
   const size_t o_xq = plan.take<int16_t>(size_t(T) * H);
   const size_t o_xs = plan.take<float>(size_t(T) * H / 32);
   const size_t o_xsum = plan.take<int32_t>(size_t(T) * H / 16);
@@ -313,6 +323,7 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
   const size_t o_hs = plan.take<float>(size_t(P) * F / 32);
   const size_t o_hsum = plan.take<int32_t>(size_t(P) * F / 16);
   const size_t o_y = plan.take<float>(size_t(P) * H);
+  if (gemm_path) plan.bytes = o_region + (prefill_scratch_bytes(T, k, E, H, F) + 255) / 256 * 256;
   if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
 
   int n = 0;
@@ -353,19 +364,26 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
                            ctx->d_status, st, &n),
                   "dispatch");
   const ExpertSource src = store_source(store, shared_gate_up, shared_down);
-  int16_t* xq = at<int16_t>(ctx, o_xq);
-  float* xs = at<float>(ctx, o_xs);
-  int32_t* xsum = at<int32_t>(ctx, o_xsum);
-  WMOE_CHECK_CUDA(ctx, quant_rows(x, x_dtype, T, H, xq, xs, xsum, st, &n), "activation quantisation");
-  float* h = at<float>(ctx, o_h);
-  WMOE_CHECK_CUDA(ctx, gate_up_gemv(src, layer, pm, H, F, xq, xs, xsum, h, ctx->d_status, st, &n), "gate_up");
-  int16_t* hq = at<int16_t>(ctx, o_hq);
-  float* hs = at<float>(ctx, o_hs);
-  int32_t* hsum = at<int32_t>(ctx, o_hsum);
-  WMOE_CHECK_CUDA(ctx, quant_rows(h, WMOE_F32, P, F, hq, hs, hsum, st, &n), "hidden quantisation");
-  float* y = at<float>(ctx, o_y);
-  WMOE_CHECK_CUDA(ctx, down_gemv(src, layer, pm, H, F, hq, hs, hsum, y, ctx->d_status, st, &n), "down");
-  WMOE_CHECK_CUDA(ctx, combine(pm, H, topk_w, shared_s, y, nullptr, out, out_dtype, st, &n), "combine");
+  if (gemm_path) {
+    WMOE_CHECK_CUDA(ctx,
+                    prefill_experts(src, layer, pm, H, F, x, x_dtype, topk_w, shared_s, out, out_dtype,
+                                    at<void>(ctx, o_region), ctx->d_status, st, &n),
+                    "grouped GEMM");
+  } else {
+    int16_t* xq = at<int16_t>(ctx, o_xq);
+    float* xs = at<float>(ctx, o_xs);
+    int32_t* xsum = at<int32_t>(ctx, o_xsum);
+    WMOE_CHECK_CUDA(ctx, quant_rows(x, x_dtype, T, H, xq, xs, xsum, st, &n), "activation quantisation");
+    float* h = at<float>(ctx, o_h);
+    WMOE_CHECK_CUDA(ctx, gate_up_gemv(src, layer, pm, H, F, xq, xs, xsum, h, ctx->d_status, st, &n), "gate_up");
+    int16_t* hq = at<int16_t>(ctx, o_hq);
+    float* hs = at<float>(ctx, o_hs);
+    int32_t* hsum = at<int32_t>(ctx, o_hsum);
+    WMOE_CHECK_CUDA(ctx, quant_rows(h, WMOE_F32, P, F, hq, hs, hsum, st, &n), "hidden quantisation");
+    float* y = at<float>(ctx, o_y);
+    WMOE_CHECK_CUDA(ctx, down_gemv(src, layer, pm, H, F, hq, hs, hsum, y, ctx->d_status, st, &n), "down");
+    WMOE_CHECK_CUDA(ctx, combine(pm, H, topk_w, shared_s, y, nullptr, out, out_dtype, st, &n), "combine");
+  }
   if (topk_idx_out)
     WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_idx_out, topk_idx, size_t(T) * k * sizeof(int32_t),
                                          cudaMemcpyDeviceToDevice, st),

@@ -66,6 +66,12 @@ cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* 
 cudaError_t gemv_batch(int type, const uint8_t* const* weights, int n, int rows, int k, const float* x, float* y,
                        cudaStream_t st, int* launches);
 
+// gemm_sm100.cu: tcgen05 grouped GEMMs for many tokens per expert (gate_up + SwiGLU, down, fp16 combine)
+size_t prefill_scratch_bytes(int T, int k, int E, int H, int F);
+cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const void* x,
+                            int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
+                            void* scratch, int* status, cudaStream_t st, int* launches);
+
 // decode.cu: persistent one-token decode (one layer or a stack)
 struct DecodeLayer {
   const float* router_w;

@@ -23,6 +23,7 @@ SIGNATURES = {
     "wmoe_launch_count": (_u64, [_p]),
     "wmoe_set_decode_kernel": (_i, [_p, _i]),
     "wmoe_set_trace": (_i, [_p, _p, _sz]),
+    "wmoe_set_prefill_threshold": (_i, [_p, _i]),
     "wmoe_decode_ctas": (_i, [_p]),
     "wmoe_device_status": (_i, [_p, ctypes.POINTER(_i), _p]),
     "wmoe_dequant": (_i, [_p, _i, _p, _sz, _p, _i, _p]),
