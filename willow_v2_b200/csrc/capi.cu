@@ -367,7 +367,7 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
   if (gemm_path) {
     WMOE_CHECK_CUDA(ctx,
                     prefill_experts(src, layer, pm, H, F, x, x_dtype, topk_w, shared_s, out, out_dtype,
-                                    at<void>(ctx, o_region), ctx->d_status, st, &n),
+                                    at<void>(ctx, o_region), ctx->sm_count, ctx->d_status, st, &n),
                     "grouped GEMM");
   } else {
     int16_t* xq = at<int16_t>(ctx, o_xq);

@@ -2,19 +2,32 @@
 // Replaces willow's dequantize-to-bf16 + matmul path for more than 8 tokens (gguf/metal.py:357-363, 404-407) and
 // the per-expert loop of Engine.each_expert (engines/base.py:534-591).
 //
-// Swap-AB: the expert's weight rows are the MMA's M (128 per tile), its tokens are N (128 per tile), K runs over the
-// hidden size (gate_up) or the FFN width (down) in blocks of 64.
-//   A  128 x 64 weight tile: 4 warps dequantise it from the raw Q4_K / Q6_K bytes in global memory (one row per
-//      thread: 48 or 100 bytes) to fp16 and store it in shared memory in the 128-byte-swizzled K-major layout the
-//      MMA reads. Values are the exact float32 dequantisation of willow (gguf/quants.py:87-116) rounded to fp16.
-//   B  128 tokens x 64 activations (fp16): one TMA tile load (128-byte swizzle) from the gathered activations.
-//   D  128 x 128 float32 accumulator in TMEM (128 columns), 4 tcgen05.mma (K = 16 each) per K block, issued by one
-//      thread; tcgen05.commit signals an mbarrier when they have read shared memory and finished.
-// gate_up tiles pair 64 gate rows with the 64 matching up rows (rows j and F + j), so the SwiGLU epilogue has both:
-// h = silu(gate) * up, stored as fp16 scaled by 1/32 (fp16 has the precision the 2e-3 bound needs - bf16 does
-// not - but not the range of raw h). down tiles write y / 32 as fp16; the combine multiplies the 32 back.
-// Waits are bounded (1 s of %globaltimer); on a timeout the CTA records the device status, waits (bounded) for its
-// outstanding MMAs, frees its TMEM and returns.
+// Swap-AB: the expert's weight rows are the MMA's M (128 per tile), its tokens are N (a chunk of up to 256 of the
+// expert's tokens; the MMA's N is the chunk rounded up to 16), K runs over the hidden size (gate_up, Q4_K) or the
+// FFN width (down, Q6_K) in blocks of 64. An item is (chunk, 128-row M tile). The kernel is persistent: one CTA
+// per SM walks the items i = blockIdx.x, + gridDim.x, ... with specialised warps:
+//   warp 0      TMA: the token tile of each K block (fp16, 128-byte swizzle) into a 3-stage ring
+//   warp 1      allocates 512 TMEM columns (two fp32 accumulators of 256 columns); one lane issues 4 tcgen05.mma
+//               (K = 16) per K block; tcgen05.commit frees the stage, and after an item's last K block marks
+//               its accumulator full
+//   warp 2      the weight bytes into shared memory. Q4_K: one super-block column (144 bytes of 128 rows) per
+//               TMA load pair, 3 deep (the expert matrices are a 3-D tensor map over the slab). Q6_K: the item's
+//               128 rows, contiguous, by one bulk copy
+//   warps 3-6   the epilogue: accumulator -> registers (tcgen05.ld), SwiGLU or scaling, fp16 stores; it works on
+//               one accumulator while the MMAs fill the other
+//   warps 7-14  dequantise the 128 x 64 weight tile of each K block from shared memory into the stage, two
+//               groups of 4 warps taking alternate K blocks (thread = tile row)
+// Dequantisation is packed fp16 arithmetic: codes are moved into the low mantissa bits of 1024.0 (low nibbles,
+// 6-bit codes) or 64.0 (high nibbles, spacing 1/16) by byte permutes and masks, the magic is subtracted exactly,
+// and one fused multiply-add applies the sub-block's d*sc and -dmin*mn rounded to fp16 (measured error on an
+// expert FFN: 5.2e-4 relative L2 against the float32 reference; bound 2e-3). The codes of a 32-bit word come out
+// as elements (0, 2, 1, 3) of its 4, so the activations are stored with the same order inside every run of 8
+// (gather and SwiGLU epilogue), which leaves every dot product unchanged.
+// gate_up tiles pair 64 gate rows with the 64 matching up rows (rows j and F + j): the epilogue forms
+// h = silu(gate) * up, stored as fp16 scaled by 1/32 (fp16 keeps the precision the 2e-3 bound needs, bf16 does not,
+// but not the range of raw h). down tiles write y / 32 as fp16; the combine multiplies the 32 back.
+// Every wait is bounded (1 s of %globaltimer) and any timeout stops every role: the CTA records the device status,
+// waits (bounded) for its copies and MMAs in flight, frees its TMEM and returns.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -24,10 +37,28 @@ namespace wmoe {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;
-constexpr int kThreads = 128;
-constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB per operand tile (fp16)
+constexpr int kBM = 128, kBN = 256, kBK = 64, kBoxRows = 128;
+constexpr int kStages = 3;
+constexpr int kWarps = 15, kThreads = kWarps * 32;
+constexpr int kTileA = kBM * kBK * 2;                 // 16 KB fp16 weights
+constexpr int kTileB = kBN * kBK * 2;                 // 32 KB fp16 tokens
+constexpr int kStageBytes = kTileA + kTileB;
+constexpr int kQ4Row = 144;                           // one Q4_K super-block of a row
+constexpr int kQ4Unit = kBM * kQ4Row;                 // 18,432 B: one super-block column of the tile
+constexpr int kQ4Depth = 3;
+constexpr int kQ6Unit = kBM * 2 * Q6K_BYTES;          // 53,760 B: 128 down rows of F = 512
+constexpr int kXbufBytes = 32 * 64 * 4;               // gate/up exchange of 32 columns
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
+
+template <int MODE>
+struct Layout {
+  static constexpr int depth = MODE == 0 ? kQ4Depth : 1;  // weight ring
+  static constexpr int unit = MODE == 0 ? kQ4Unit : kQ6Unit;
+  static constexpr int raw = kStages * kStageBytes;       // weight ring offset
+  static constexpr int xbuf = raw + depth * unit;
+  static constexpr int bytes = xbuf + (MODE == 0 ? kXbufBytes : 0) + 1024;  // + alignment slack
+};
+static_assert(Layout<0>::bytes <= 232448 && Layout<1>::bytes <= 232448, "shared memory");
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
@@ -41,6 +72,10 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
@@ -57,12 +92,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   return ok != 0;
 }
 
-__device__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+// Waits for the phase; gives up after the time limit or once another role has given up (fail set).
+__device__ bool mbar_wait(uint64_t* bar, unsigned parity, volatile int* fail) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity))
-    if (globaltimer() - t0 > kTimeoutNs) return false;
+  while (!mbar_try_wait(bar, parity)) {
+    if (*fail) return false;
+    if (globaltimer() - t0 > kTimeoutNs) {
+      *fail = 1;
+      return false;
+    }
+  }
   return true;
+}
+
+// the same, one answer for the whole warp (every lane waits; the warp continues only if all saw the phase)
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, unsigned parity, volatile int* fail) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, fail));
 }
 
 // 2-D TMA tile load (box 64 fp16 x 128 rows, 128-byte swizzle) completing on an mbarrier; x = column, y = row.
@@ -71,6 +117,22 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
           "r"(smem_u32(dst)),
       "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 3-D TMA tile load (no swizzle): x = byte column, y = row, z = slot.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -84,14 +146,15 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p) {
          | (2ull << 61);                  // SWIZZLE_128B
 }
 
-// Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator, both K-major, M = 128, N = kBN.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+// Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator, both K-major, M = 128; N at bits 17-22.
+constexpr uint32_t kIdescBase = (1u << 4) | (uint32_t(kBM >> 4) << 24);
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
           tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -124,83 +187,89 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// One Q4_K row's K block kb (elements 64 kb .. 64 kb + 63 = sub-blocks 2g, 2g + 1 of super-block kb / 4, g = kb % 4)
-// -> 64 fp16 into the row of the swizzled tile.
-__device__ __forceinline__ void dequant_q4k_row(const uint8_t* row, int kb, uint8_t* tile, int r) {
-  const uint8_t* b = row + (kb / 4) * Q4K_BYTES;
-  const int g = kb % 4;
-  const uint4 hd = ldg_nc_v4(b);
-  const uint4 qa = ldg_nc_v4(b + 16 + 32 * g), qb = ldg_nc_v4(b + 32 + 32 * g);
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+
+// Stored position of element e within its run of 8 (and back: the map is its own inverse).
+__device__ __forceinline__ int perm8(int e) { return (e & ~7) | ((e & 1) << 1) | ((e & 2) >> 1) | (e & 4); }
+
+// Q4_K K block (sub-blocks 2g and 2g + 1 of one super-block) of tile row r, from the row's 144 bytes in shared
+// memory, into the swizzled A tile. Low nibbles of quant bytes 32g .. 32g + 31 are elements 0-31, high nibbles
+// elements 32-63 (gguf/quants.py:82-98).
+__device__ __forceinline__ void dequant_q4k_block(const uint8_t* row, int g, uint8_t* tile, int r) {
+  const uint4 hd = *reinterpret_cast<const uint4*>(row);
   const float d = f16_to_f32(uint16_t(hd.x & 0xFFFF)), dmin = f16_to_f32(uint16_t(hd.x >> 16));
   int sc0, mn0, sc1, mn1;
   q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * g, sc0, mn0);
   q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * g + 1, sc1, mn1);
-  const float A0 = __fmul_rn(d, float(sc0)), B0 = __fmul_rn(dmin, float(mn0));
-  const float A1 = __fmul_rn(d, float(sc1)), B1 = __fmul_rn(dmin, float(mn1));
+  const __half2 A0 = __float2half2_rn(d * float(sc0)), A1 = __float2half2_rn(d * float(sc1));
+  const __half2 B0 = __float2half2_rn(-dmin * float(mn0)), B1 = __float2half2_rn(-dmin * float(mn1));
+  const uint4 qa = *reinterpret_cast<const uint4*>(row + 16 + 32 * g);
+  const uint4 qb = *reinterpret_cast<const uint4*>(row + 32 + 32 * g);
   const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  // chunks 0..3: sub-block 2g (low nibbles of bytes 0..31), chunks 4..7: sub-block 2g + 1 (high nibbles)
+  const __half2 k1024 = u2h(0x64006400u), k64 = u2h(0x54005400u);
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const float A = half ? A1 : A0, B = half ? B1 : B0;
+  for (int c = 0; c < 4; ++c) {
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      const uint32_t x = qw[2 * c + w];
+      const uint32_t pe = __byte_perm(x, 0, 0x4240), po = __byte_perm(x, 0, 0x4341);  // bytes (0, 2), (1, 3)
+      lo[2 * w] = h2u(__hfma2(__hsub2(u2h((pe & 0x000F000Fu) | 0x64006400u), k1024), A0, B0));
+      lo[2 * w + 1] = h2u(__hfma2(__hsub2(u2h((po & 0x000F000Fu) | 0x64006400u), k1024), A0, B0));
+      hi[2 * w] = h2u(__hfma2(__hsub2(u2h((pe & 0x00F000F0u) | 0x54005400u), k64), A1, B1));
+      hi[2 * w + 1] = h2u(__hfma2(__hsub2(u2h((po & 0x00F000F0u) | 0x54005400u), k64), A1, B1));
+    }
+    *reinterpret_cast<uint4*>(tile + sw128(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(tile + sw128(r, 4 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  }
+}
+
+// Q6_K K block kb of tile row r (64 elements of super-block kb / 4: half hh = (kb % 4) / 2, quarters 2q and 2q + 1,
+// q = kb % 2) from the row's bytes in shared memory (gguf/quants.py:120-140). Element e: ql byte hh*64 + e
+// (nibble q), qh byte 128 + hh*32 + e % 32 (bits 4q + 2 (e / 32)), scale index hh*8 + 4q + e / 16.
+__device__ __forceinline__ void dequant_q6k_block(const uint8_t* row, int kb, uint8_t* tile, int r) {
+  const uint8_t* b = row + (kb / 4) * Q6K_BYTES;
+  const int hh = (kb % 4) / 2, q = kb % 2;
+  uint32_t qh[8];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint4 v = lds_u2_16(b + 128 + hh * 32 + 16 * i);
+    qh[4 * i] = v.x, qh[4 * i + 1] = v.y, qh[4 * i + 2] = v.z, qh[4 * i + 3] = v.w;
+  }
+  const uint4 scw = lds_u2_16(b + 192);
+  const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
+  const float d = f16_to_f32(*reinterpret_cast<const uint16_t*>(b + 208));
+  __half2 D[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int si = hh * 8 + 4 * q + i;
+    D[i] = __float2half2_rn(d * float(int8_t((sw[si / 4] >> (8 * (si % 4))) & 0xFF)));
+  }
+  const __half2 k1056 = u2h(0x64206420u);  // 1024 + 32
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // elements 32 half .. 32 half + 31
+    uint32_t ql[8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 v = lds_u2_16(b + hh * 64 + 32 * half + 16 * i);
+      ql[4 * i] = v.x, ql[4 * i + 1] = v.y, ql[4 * i + 2] = v.z, ql[4 * i + 3] = v.w;
+    }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t o[4];
 #pragma unroll
       for (int w = 0; w < 2; ++w) {
-        const uint32_t word = qw[2 * c + w] >> (4 * half);
-        float v[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = __fsub_rn(__fmul_rn(A, float((word >> (8 * i)) & 0xF)), B);
-        o[2 * w] = pack_h2(v[0], v[1]);
-        o[2 * w + 1] = pack_h2(v[2], v[3]);
+        const int e0 = 8 * c + 4 * w;  // within the half
+        const uint32_t code = ((ql[e0 / 4] >> (4 * q)) & 0x0F0F0F0Fu) |
+                              (((qh[e0 / 4] >> (4 * q + 2 * half)) & 0x03030303u) << 4);  // q6, 0..63
+        const uint32_t pe = __byte_perm(code, 0x64646464u, 0x4240), po = __byte_perm(code, 0x64646464u, 0x4341);
+        const __half2 dd = D[2 * half + e0 / 16];
+        o[2 * w] = h2u(__hmul2(__hsub2(u2h(pe), k1056), dd));
+        o[2 * w + 1] = h2u(__hmul2(__hsub2(u2h(po), k1056), dd));
       }
       *reinterpret_cast<uint4*>(tile + sw128(r, 4 * half + c)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-  }
-}
-
-// One Q6_K row's K block kb (64 elements of super-block kb / 4: half hh = (kb % 4) / 2, quarters 2q and 2q + 1,
-// q = kb % 2) -> 64 fp16. Element e: ql byte hh*64 + e (nibble q), qh byte 128 + hh*32 + e % 32 (bits 4q + 2(e/32)),
-// scale index hh*8 + 4q + e / 16.
-__device__ __forceinline__ void dequant_q6k_row(const uint8_t* row, int kb, uint8_t* tile, int r) {
-  const uint8_t* b = row + (kb / 4) * Q6K_BYTES;
-  const int hh = (kb % 4) / 2, q = kb % 2;
-  uint32_t ql[16], qh[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint4 v = ldg_u2_16(b + hh * 64 + 16 * i);
-    ql[4 * i] = v.x, ql[4 * i + 1] = v.y, ql[4 * i + 2] = v.z, ql[4 * i + 3] = v.w;
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const uint4 v = ldg_u2_16(b + 128 + hh * 32 + 16 * i);
-    qh[4 * i] = v.x, qh[4 * i + 1] = v.y, qh[4 * i + 2] = v.z, qh[4 * i + 3] = v.w;
-  }
-  const uint4 scw = ldg_u2_16(b + 192);
-  const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
-  const float d = f16_to_f32(__ldg(reinterpret_cast<const unsigned short*>(b + 208)));
-  float D[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int si = hh * 8 + 4 * q + i;
-    D[i] = __fmul_rn(d, float(int8_t((sw[si / 4] >> (8 * (si % 4))) & 0xFF)));
-  }
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {  // chunk c: elements 8c .. 8c + 7
-    uint32_t o[4];
-#pragma unroll
-    for (int w = 0; w < 2; ++w) {
-      const int e0 = 8 * c + 4 * w;  // 4 elements e0..e0+3, one ql word and one qh word
-      const uint32_t lw = (ql[e0 / 4] >> (4 * q)) & 0x0F0F0F0Fu;
-      const uint32_t hw = (qh[(e0 % 32) / 4] >> (4 * q + 2 * (e0 / 32))) & 0x03030303u;
-      const uint32_t q6 = lw | (hw << 4);
-      float v[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(D[e0 / 16], float(int((q6 >> (8 * i)) & 0xFF) - 32));
-      o[2 * w] = pack_h2(v[0], v[1]);
-      o[2 * w + 1] = pack_h2(v[2], v[3]);
-    }
-    *reinterpret_cast<uint4*>(tile + sw128(r, c)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -208,184 +277,307 @@ struct GemmParams {
   ExpertSource src;
   int layer;
   PairMap pm;
-  const int2* items;     // (segment u, first token of the tile within the segment)
-  const int* n_items;
-  int mode;              // 0: gate_up + SwiGLU -> h, 1: down -> y
+  const int2* chunks;    // (segment u, first token of the chunk within the segment)
+  const int* n_chunks;
+  int n_mtiles;
   int F, H;
-  __half* out;           // mode 0: h [P][F]; mode 1: y [P][H]
+  __half* out;           // gate_up: h [P][F] (columns in run-of-8 order); down: y [P][H]
   int* status;
 };
 
-__global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_b,
-                                                                const __grid_constant__ GemmParams p) {
+struct Item {
+  int u, seg0, n0, ncols, mt;
+};
+
+__device__ __forceinline__ Item get_item(const GemmParams& p, int i) {
+  Item t;
+  const int2 c = p.chunks[i / p.n_mtiles];
+  t.mt = i % p.n_mtiles;
+  t.u = c.x;
+  t.n0 = c.y;
+  t.seg0 = p.pm.seg[t.u];
+  t.ncols = min(kBN, p.pm.seg[t.u + 1] - t.seg0 - t.n0);
+  return t;
+}
+
+// slot of the item's expert in the slab, kSharedSlot for the shared expert, -1 if not resident
+constexpr int kSharedSlot = -2;
+__device__ __forceinline__ int item_slot(const GemmParams& p, int u) {
+  const int e = p.pm.used[u];
+  if (e == p.src.experts) return kSharedSlot;
+  return p.src.slot_of[size_t(p.layer) * p.src.experts + e];
+}
+
+struct Bars {
+  uint64_t full_a[kStages], full_b[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t raw_full[kQ4Depth], raw_empty[kQ4Depth];
+  uint64_t done;
+  uint32_t tmem;
+  int fail;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_w,
+                        const __grid_constant__ CUtensorMap tmap_ws, const __grid_constant__ GemmParams p) {
+  using L = Layout<MODE>;
   extern __shared__ __align__(1024) uint8_t dyn[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
-  uint8_t* tileA = base;
-  uint8_t* tileB = base + kTileBytes;
-  __shared__ uint64_t mbar_b, mbar_mma;
-  __shared__ uint32_t tmem_base;
-  __shared__ int fail;
+  uint8_t* raw = base + L::raw;
+  __shared__ Bars bars;
 
-  const int item = blockIdx.y;
-  if (item >= *p.n_items) return;
-  const int2 it = p.items[item];
-  const int u = it.x, n0 = it.y;
-  const int e = p.pm.used[u];
-  const int seg0 = p.pm.seg[u], cnt = p.pm.seg[u + 1] - seg0;
-  const int n_valid = min(kBN, cnt - n0);
-  const int mt = blockIdx.x;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int K = p.mode == 0 ? p.H : p.F;
-
-  // the expert's weights
-  const uint8_t* w;
-  if (e == p.src.experts) {
-    w = p.mode == 0 ? p.src.shared_gate_up : p.src.shared_down;
-  } else {
-    const int s = p.src.slot_of[size_t(p.layer) * p.src.experts + e];
-    if (s < 0) {
-      if (tid == 0) set_status(p.status, kStatusNotResident);
-      return;
-    }
-    w = p.src.slab + size_t(s) * p.src.slot_bytes + (p.mode == 0 ? 0 : p.src.gate_up_bytes);
-  }
-  const size_t row_bytes = p.mode == 0 ? size_t(K / QK) * Q4K_BYTES : size_t(K / QK) * Q6K_BYTES;
-  // weight row of this thread's tile row
-  int wrow;
-  if (p.mode == 0)
-    wrow = tid < 64 ? 64 * mt + tid : p.F + 64 * mt + (tid - 64);
-  else
-    wrow = kBM * mt + tid;
-  const uint8_t* my_row = w + size_t(wrow) * row_bytes;
+  const int total = *p.n_chunks * p.n_mtiles;
+  const int K = MODE == 0 ? p.H : p.F, nk = K / kBK;
+  const int units = MODE == 0 ? K / QK : 1;  // weight units per item
 
   if (tid == 0) {
-    fail = 0;
-    mbar_init(&mbar_b, 1);
-    mbar_init(&mbar_mma, 1);
+    bars.fail = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars.full_a[s], 4);  // the 4 warps of one dequant group
+      mbar_init(&bars.full_b[s], 1);
+      mbar_init(&bars.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars.acc_full[b], 1);
+      mbar_init(&bars.acc_empty[b], 4);  // the 4 epilogue warps
+    }
+    for (int s = 0; s < L::depth; ++s) {
+      mbar_init(&bars.raw_full[s], 1);
+      mbar_init(&bars.raw_empty[s], 8);  // all 8 dequant warps
+    }
+    mbar_init(&bars.done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(kBN)
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars.tmem)),
+                 "r"(2 * kBN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem_d = tmem_base;
+  const uint32_t tmem_base = bars.tmem;
+  volatile int* fail = &bars.fail;
+  int issued_b = 0, issued_w = 0;  // copies the two producer lanes issued (for the drain after a failure)
 
-  const int nk = K / kBK;
-  int issued = 0;  // MMA groups committed
-  for (int kb = 0; kb < nk; ++kb) {
-    // B: this tile's tokens x activations kb*64 .. +63
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&mbar_b, kTileBytes);
-      tma_load_2d(tileB, &tmap_b, kb * kBK, seg0 + n0, &mbar_b);
+  if (warp == 0) {
+    // ---------------- token tiles
+    if (lane == 0) {
+      int it = 0;
+      for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
+        const Item t = get_item(p, i);
+        const int nb = t.ncols > kBoxRows ? 2 : 1;
+        for (int kb = 0; kb < nk; ++kb) {
+          const int kbg = it * nk + kb, s = kbg % kStages;
+          if (kbg >= kStages && !mbar_wait(&bars.empty[s], unsigned((kbg / kStages - 1) & 1), fail)) goto out;
+          mbar_arrive_expect_tx(&bars.full_b[s], unsigned(nb * kBoxRows * kBK * 2));
+          uint8_t* dst = base + s * kStageBytes + kTileA;
+          tma_load_2d(dst, &tmap_b, kb * kBK, t.seg0 + t.n0, &bars.full_b[s]);
+          if (nb == 2) tma_load_2d(dst + kBoxRows * 128, &tmap_b, kb * kBK, t.seg0 + t.n0 + kBoxRows, &bars.full_b[s]);
+          issued_b = kbg + 1;
+        }
+      }
     }
-    // A: 128 weight rows, dequantised
-    if (p.mode == 0)
-      dequant_q4k_row(my_row, kb, tileA, tid);
-    else
-      dequant_q6k_row(my_row, kb, tileA, tid);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> visible to the MMA
-    __syncthreads();
-    if (tid == 0) {
-      bool ok = mbar_wait(&mbar_b, unsigned(kb & 1));
-      if (ok) {
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      int it = 0;
+      for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
+        const Item t = get_item(p, i);
+        const int buf = it & 1;
+        if (it >= 2 && !mbar_wait(&bars.acc_empty[buf], unsigned((it / 2 - 1) & 1), fail)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t da = smem_desc(tileA), db = smem_desc(tileB);
+        const uint32_t idesc = kIdescBase | (uint32_t(((t.ncols + 15) & ~15) >> 3) << 17);
+        const uint32_t d = tmem_base + uint32_t(buf * kBN);
+        bool ok = true;
+        for (int kb = 0; kb < nk && ok; ++kb) {
+          const int kbg = it * nk + kb, s = kbg % kStages;
+          const unsigned ph = unsigned((kbg / kStages) & 1);
+          ok = mbar_wait(&bars.full_a[s], ph, fail) && mbar_wait(&bars.full_b[s], ph, fail);
+          if (!ok) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t da = smem_desc(base + s * kStageBytes), db = smem_desc(base + s * kStageBytes + kTileA);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)  // 32 bytes of K per MMA: +2 in the 16-byte address field
-          mma_f16(tmem_d, da + 2 * k, db + 2 * k, (kb | k) != 0 ? 1u : 0u);
-        mma_commit(&mbar_mma);
-        ++issued;
-      } else {
-        fail = 1;
-        set_status(p.status, kStatusBarrierTimeout);
-      }
-    }
-    __syncthreads();
-    if (fail) break;
-    // the tiles are rewritten next iteration: wait until the MMAs have consumed them (the decision to stop is
-    // taken after a CTA barrier, so every thread leaves the loop together)
-    if (!mbar_wait(&mbar_mma, unsigned(kb & 1))) {
-      fail = 1;
-      set_status(p.status, kStatusBarrierTimeout);
-    }
-    __syncthreads();
-    if (fail) break;
-  }
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (!fail) {
-    float* xbuf = reinterpret_cast<float*>(base);  // [32 columns][64 rows] up values, reusing the tiles
-    if (p.mode == 0) {
-      // gate rows in warps 0-1, up rows in warps 2-3; up values pass through shared memory column by column
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem_d + (uint32_t(32 * warp) << 16) + uint32_t(c0), v);
-        if (warp >= 2) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) xbuf[i * 64 + (tid - 64)] = v[i];
+          for (int k = 0; k < kBK / 16; ++k)  // 32 bytes of K per MMA: +2 in the 16-byte address field
+            mma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          mma_commit(&bars.empty[s]);
         }
-        __syncthreads();
-        if (warp < 2) {
-          const int j = 64 * mt + tid;  // h index
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c0 + i;
-            if (col < n_valid) {
-              const float up = xbuf[i * 64 + tid];
-              p.out[size_t(seg0 + n0 + col) * p.F + j] = __float2half_rn(silu(v[i]) * up * (1.0f / 32.0f));
-            }
+        if (!ok) break;
+        mma_commit(&bars.acc_full[buf]);
+      }
+      mma_commit(&bars.done);  // arrives once every MMA issued above has completed
+    }
+  } else if (warp == 2) {
+    // ---------------- weight bytes
+    if (lane == 0) {
+      int it = 0;
+      for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
+        const Item t = get_item(p, i);
+        const int slot = item_slot(p, t.u);
+        if (slot == -1 || slot >= p.src.n_slots) {
+          set_status(p.status, kStatusNotResident);
+          *fail = 1;
+          break;
+        }
+        for (int un = 0; un < units; ++un) {
+          const int ru = it * units + un, rs = ru % L::depth;
+          if (ru >= L::depth && !mbar_wait(&bars.raw_empty[rs], unsigned((ru / L::depth - 1) & 1), fail)) goto out;
+          uint8_t* dst = raw + rs * L::unit;
+          mbar_arrive_expect_tx(&bars.raw_full[rs], unsigned(L::unit));
+          if (MODE == 0) {  // gate rows 64 mt .., up rows F + 64 mt .., super-block un
+            const CUtensorMap* m = slot == kSharedSlot ? &tmap_ws : &tmap_w;
+            const int z = slot == kSharedSlot ? 0 : slot;
+            tma_load_3d(dst, m, un * kQ4Row, 64 * t.mt, z, &bars.raw_full[rs]);
+            tma_load_3d(dst + 64 * kQ4Row, m, un * kQ4Row, p.F + 64 * t.mt, z, &bars.raw_full[rs]);
+          } else {
+            const uint8_t* w = slot == kSharedSlot
+                                   ? p.src.shared_down
+                                   : p.src.slab + size_t(slot) * p.src.slot_bytes + p.src.gate_up_bytes;
+            bulk_g2s(dst, w + size_t(kQ6Unit) * t.mt, unsigned(kQ6Unit), &bars.raw_full[rs]);
           }
-        }
-        __syncthreads();
-      }
-    } else {
-      const int row = kBM * mt + tid;  // hidden row
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem_d + (uint32_t(32 * warp) << 16) + uint32_t(c0), v);
-        for (int i = 0; i < 32; ++i) {
-          const int col = c0 + i;
-          if (col < n_valid) p.out[size_t(seg0 + n0 + col) * p.H + row] = __float2half_rn(v[i]);
+          issued_w = ru + 1;
         }
       }
     }
-  } else if (issued > 0) {
-    // a wait ran out: let the MMAs already committed finish (bounded) before the accumulator is freed
-    mbar_wait(&mbar_mma, unsigned((issued - 1) & 1));
+  } else if (warp <= 6) {
+    // ---------------- epilogue (warps 3-6 cover the four TMEM lane quadrants)
+    const int quad = warp % 4, trow = 32 * quad + lane;
+    float* xbuf = reinterpret_cast<float*>(base + L::xbuf);  // [32 columns][64 rows] up values
+    int it = 0;
+    for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
+      const Item t = get_item(p, i);
+      const int buf = it & 1;
+      const bool ready = mbar_wait(&bars.acc_full[buf], unsigned((it / 2) & 1), fail) && !*fail;
+      unsigned all_ready;  // one decision for the four epilogue warps (they meet at named barrier 1)
+      asm volatile(
+          "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+          : "=r"(all_ready)
+          : "r"(unsigned(ready))
+          : "memory");
+      if (!all_ready) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t taddr = tmem_base + uint32_t(buf * kBN) + (uint32_t(32 * quad) << 16);
+      const size_t row0 = size_t(t.seg0 + t.n0);
+      for (int c0 = 0; c0 < t.ncols; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + uint32_t(c0), v);
+        if (MODE == 0) {
+          // gate rows are quadrants 0-1, up rows quadrants 2-3
+          if (quad >= 2) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) xbuf[c * 64 + (trow - 64)] = v[c];
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (quad < 2) {
+            const int j = perm8(64 * t.mt + trow);  // stored column of h index 64 mt + trow
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (c0 + c < t.ncols)
+                p.out[(row0 + c0 + c) * p.F + j] = __float2half_rn(silu(v[c]) * xbuf[c * 64 + trow] * (1.0f / 32.0f));
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        } else {
+          __half* o = p.out + (row0 + c0) * p.H + kBM * t.mt + trow;
+          const int n = min(32, t.ncols - c0);
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (c < n) o[size_t(c) * p.H] = __float2half_rn(v[c]);
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
+    }
+  } else {
+    // ---------------- dequantisation: group j takes the K blocks kb with kb % 2 == j; thread = tile row r
+    const int dw = warp - 7, j = dw / 4, r = (dw % 4) * 32 + lane;
+    int it = 0;
+    for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
+      for (int un = 0; un < units; ++un) {
+        const int ru = it * units + un, rs = ru % L::depth;
+        if (!mbar_wait_warp(&bars.raw_full[rs], unsigned((ru / L::depth) & 1), fail)) goto out;
+        const uint8_t* wrow = raw + rs * L::unit + r * (MODE == 0 ? kQ4Row : 2 * Q6K_BYTES);
+        const int kb0 = MODE == 0 ? 4 * un : 0, kb1 = MODE == 0 ? 4 * un + 4 : nk;
+        for (int kb = kb0 + j; kb < kb1; kb += 2) {
+          const int kbg = it * nk + kb, s = kbg % kStages;
+          if (kbg >= kStages && !mbar_wait_warp(&bars.empty[s], unsigned((kbg / kStages - 1) & 1), fail)) goto out;
+          if (MODE == 0)
+            dequant_q4k_block(wrow, kb % 4, base + s * kStageBytes, r);
+          else
+            dequant_q6k_block(wrow, kb, base + s * kStageBytes, r);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.full_a[s]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.raw_empty[rs]);
+      }
+    }
+  }
+out:
+  __syncwarp();
+  if (tid == 0 && *fail) set_status(p.status, kStatusBarrierTimeout);
+  {
+    // every MMA this CTA issued has completed, and after a failure every copy in flight gets a bounded wait,
+    // before the CTA frees its shared memory and TMEM
+    volatile int never = 0;
+    if (warp == 1) mbar_wait(&bars.done, 0, &never);
+    if (*fail && lane == 0) {
+      if (warp == 0)
+        for (int kbg = max(0, issued_b - kStages); kbg < issued_b; ++kbg)
+          mbar_wait(&bars.full_b[kbg % kStages], unsigned((kbg / kStages) & 1), &never);
+      if (warp == 2)
+        for (int ru = max(0, issued_w - L::depth); ru < issued_w; ++ru)
+          mbar_wait(&bars.raw_full[ru % L::depth], unsigned((ru / L::depth) & 1), &never);
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kBN) : "memory");
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kBN) : "memory");
 }
 
-// Work list: one item per (segment, 128-token tile).
-__global__ void tile_list_kernel(PairMap pm, int2* items, int* n_items) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const int n = *pm.n_used;
-  int k = 0;
-  for (int u = 0; u < n; ++u) {
-    const int cnt = pm.seg[u + 1] - pm.seg[u];
-    for (int n0 = 0; n0 < cnt; n0 += kBN) items[k++] = make_int2(u, n0);
+// Chunk list: one entry per (segment, up to 256 tokens), segments in order.
+__global__ void __launch_bounds__(512) chunk_list_kernel(PairMap pm, int2* chunks, int* n_chunks) {
+  __shared__ int warp_sum[16];
+  const int n = *pm.n_used, u = threadIdx.x, lane = u % 32, wid = u / 32;
+  const int cnt = u < n ? (pm.seg[u + 1] - pm.seg[u] + kBN - 1) / kBN : 0;
+  int incl = cnt;  // inclusive scan within the warp, then across the 16 warp totals
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += v;
   }
-  *n_items = k;
+  if (lane == 31) warp_sum[wid] = incl;
+  __syncthreads();
+  int before = 0, total = 0;
+  for (int i = 0; i < 16; ++i) {
+    before += i < wid ? warp_sum[i] : 0;
+    total += warp_sum[i];
+  }
+  const int off = before + incl - cnt;
+  for (int c = 0; c < cnt; ++c) chunks[off + c] = make_int2(u, c * kBN);
+  if (u == 0) *n_chunks = total;
 }
 
-// X_g[p] = fp16(x[token(p)]) for every pair position p (routed pairs, then the shared expert's rows).
+// X_g[p] = fp16(x[token(p)]) for every pair position p (routed pairs, then the shared expert's rows), columns in
+// run-of-8 order.
 template <typename XT>
 __global__ void gather_fp16_kernel(PairMap pm, const XT* __restrict__ x, int H, __half* __restrict__ xg) {
   const int p = blockIdx.x;
   const int t = pair_token(pm, p);
   const XT* src = x + size_t(t) * H;
   __half* dst = xg + size_t(p) * H;
-  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
-    const float a = to_f32(src[i]), b = to_f32(src[i + 1]), c = to_f32(src[i + 2]), d = to_f32(src[i + 3]);
-    *reinterpret_cast<uint2*>(dst + i) = make_uint2(pack_h2(a, b), pack_h2(c, d));
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = to_f32(src[i + j]);
+    // stored order within the run: elements 0, 2, 1, 3, 4, 6, 5, 7
+    *reinterpret_cast<uint4*>(dst + i) =
+        make_uint4(pack_h2(v[0], v[2]), pack_h2(v[1], v[3]), pack_h2(v[4], v[6]), pack_h2(v[5], v[7]));
   }
 }
 
@@ -446,42 +638,58 @@ EncodeFn encode_fn() {
   return fn;
 }
 
-// fp16 [rows, cols] row-major, tiles of 128 rows x 64 columns with the 128-byte swizzle
-cudaError_t make_tmap(CUtensorMap* map, const __half* base, uint64_t rows, uint64_t cols) {
+// fp16 [rows, cols] row-major, boxes of 128 rows x 64 columns with the 128-byte swizzle
+cudaError_t make_tmap_f16(CUtensorMap* map, const __half* ptr, uint64_t rows, uint64_t cols) {
   EncodeFn fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols * sizeof(__half)};
-  const cuuint32_t box[2] = {uint32_t(kBK), uint32_t(kBN)};
+  const cuuint32_t box[2] = {uint32_t(kBK), uint32_t(kBoxRows)};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// Two tiles, 1024-aligned (the epilogue reuses them), padded so that at most 4 CTAs share an SM: their 4 x 128
-// TMEM columns then fit the SM's 512 and tcgen05.alloc never has to wait for another CTA.
-constexpr size_t kSmem = 48 * 1024 + 1024;
+// Q4_K matrices as bytes [slots][rows][row_bytes] (slot stride slot_bytes), boxes of one super-block (144 bytes)
+// of 64 rows, no swizzle.
+cudaError_t make_tmap_q4k(CUtensorMap* map, const uint8_t* ptr, uint64_t row_bytes, uint64_t rows, uint64_t slots,
+                          uint64_t slot_bytes) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[3] = {row_bytes, rows, slots};
+  const cuuint64_t strides[2] = {row_bytes, slot_bytes};
+  const cuuint32_t box[3] = {uint32_t(kQ4Row), 64, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
 
 }  // namespace
 
 size_t prefill_scratch_bytes(int T, int k, int E, int H, int F) {
   const size_t P = size_t(T) * (k + 1);
-  const size_t items = P / kBN + size_t(E) + 2;
-  return items * sizeof(int2) + 256 + P * H * sizeof(__half) * 2 + P * F * sizeof(__half) + 4 * 256;
+  const size_t chunks = P / kBN + size_t(E) + 2;
+  return chunks * sizeof(int2) + 256 + P * H * sizeof(__half) * 2 + P * F * sizeof(__half) + 4 * 256;
 }
 
 cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const void* x,
                             int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
-                            void* scratch, int* status, cudaStream_t st, int* launches) {
-  if (H % kBK || F % kBK || F % 128 || H % 128) return cudaErrorInvalidValue;
+                            void* scratch, int num_sms, int* status, cudaStream_t st, int* launches) {
+  if (H % QK || F != 2 * QK || H % kBM || pm.E + 1 > 512 || pm.k != 8 || num_sms <= 0) return cudaErrorInvalidValue;
+  // weight rows are copied by TMA and bulk copies: the matrices must start on 16-byte boundaries
+  if (reinterpret_cast<uintptr_t>(src.shared_down) % 16 || reinterpret_cast<uintptr_t>(src.shared_gate_up) % 16 ||
+      reinterpret_cast<uintptr_t>(src.slab) % 16 || src.slot_bytes % 16 || src.gate_up_bytes % 16)
+    return cudaErrorInvalidValue;
   const size_t P = size_t(pm.T) * (pm.k + 1);
-  const size_t max_items = P / kBN + size_t(pm.E) + 2;
+  const size_t max_chunks = P / kBN + size_t(pm.E) + 2;
   char* b = static_cast<char*>(scratch);
-  int2* items = reinterpret_cast<int2*>(b);
-  b += (max_items * sizeof(int2) + 255) / 256 * 256;
-  int* n_items = reinterpret_cast<int*>(b);
+  int2* chunks = reinterpret_cast<int2*>(b);
+  b += (max_chunks * sizeof(int2) + 255) / 256 * 256;
+  int* n_chunks = reinterpret_cast<int*>(b);
   b += 256;
   __half* xg = reinterpret_cast<__half*>(b);
   b += (P * H * sizeof(__half) + 255) / 256 * 256;
@@ -489,7 +697,7 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
   b += (P * F * sizeof(__half) + 255) / 256 * 256;
   __half* ybuf = reinterpret_cast<__half*>(b);
 
-  tile_list_kernel<<<1, 32, 0, st>>>(pm, items, n_items);
+  chunk_list_kernel<<<1, 512, 0, st>>>(pm, chunks, n_chunks);
   if (x_dtype == kF32)
     gather_fp16_kernel<float><<<unsigned(P), 256, 0, st>>>(pm, static_cast<const float*>(x), H, xg);
   else
@@ -497,29 +705,41 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
   *launches += 2;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-
-  e = cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem));
-  if (e != cudaSuccess) return e;
-  CUtensorMap map_x, map_h;
-  if ((e = make_tmap(&map_x, xg, P, uint64_t(H))) != cudaSuccess) return e;
-  if ((e = make_tmap(&map_h, hbuf, P, uint64_t(F))) != cudaSuccess) return e;
+  static bool attr_set = false;  // per process: the kernels' shared memory limit does not change
+  if (!attr_set) {
+    if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Layout<0>::bytes)) != cudaSuccess)
+      return e;
+    if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Layout<1>::bytes)) != cudaSuccess)
+      return e;
+    attr_set = true;
+  }
+  const uint64_t q4_row = uint64_t(H / QK) * Q4K_BYTES;
+  CUtensorMap map_x, map_h, map_w, map_ws;
+  if ((e = make_tmap_f16(&map_x, xg, P, uint64_t(H))) != cudaSuccess) return e;
+  if ((e = make_tmap_f16(&map_h, hbuf, P, uint64_t(F))) != cudaSuccess) return e;
+  if ((e = make_tmap_q4k(&map_w, src.slab, q4_row, uint64_t(2 * F), uint64_t(src.n_slots), src.slot_bytes)) !=
+      cudaSuccess)
+    return e;
+  if ((e = make_tmap_q4k(&map_ws, src.shared_gate_up, q4_row, uint64_t(2 * F), 1, q4_row * 2 * F)) != cudaSuccess)
+    return e;
 
   GemmParams gp{};
   gp.src = src;
   gp.layer = layer;
   gp.pm = pm;
-  gp.items = items;
-  gp.n_items = n_items;
+  gp.chunks = chunks;
+  gp.n_chunks = n_chunks;
   gp.F = F;
   gp.H = H;
   gp.status = status;
-  gp.mode = 0;
+  gp.n_mtiles = F / 64;
   gp.out = hbuf;
-  grouped_gemm_kernel<<<dim3(unsigned(F / 64), unsigned(max_items)), kThreads, kSmem, st>>>(map_x, gp);
-  gp.mode = 1;
+  grouped_gemm_kernel<0><<<unsigned(num_sms), kThreads, Layout<0>::bytes, st>>>(map_x, map_w, map_ws, gp);
+  gp.n_mtiles = H / kBM;
   gp.out = ybuf;
-  grouped_gemm_kernel<<<dim3(unsigned(H / kBM), unsigned(max_items)), kThreads, kSmem, st>>>(map_h, gp);
-  if (pm.k != 8) return cudaErrorInvalidValue;
+  grouped_gemm_kernel<1><<<unsigned(num_sms), kThreads, Layout<1>::bytes, st>>>(map_h, map_w, map_ws, gp);
   combine_f16_kernel<8><<<dim3(unsigned((H + 255) / 256), unsigned(pm.T)), 256, 0, st>>>(pm, H, topk_w, shared_s, ybuf,
                                                                                          out, out_dtype);
   *launches += 3;

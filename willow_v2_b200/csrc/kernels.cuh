@@ -17,6 +17,7 @@ struct ExpertSource {
   uint64_t slot_bytes;
   uint64_t gate_up_bytes;  // offset of down within a slot
   int experts;
+  int n_slots;             // slots in the slab
   const uint8_t* shared_gate_up;
   const uint8_t* shared_down;
 };
@@ -70,7 +71,7 @@ cudaError_t gemv_batch(int type, const uint8_t* const* weights, int n, int rows,
 size_t prefill_scratch_bytes(int T, int k, int E, int H, int F);
 cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const void* x,
                             int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
-                            void* scratch, int* status, cudaStream_t st, int* launches);
+                            void* scratch, int num_sms, int* status, cudaStream_t st, int* launches);
 
 // decode.cu: persistent one-token decode (one layer or a stack)
 struct DecodeLayer {

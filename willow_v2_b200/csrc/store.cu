@@ -338,6 +338,7 @@ ExpertSource store_source(const wmoe_store* s, const uint8_t* shared_gate_up, co
   src.slot_bytes = s->slot_stride;
   src.gate_up_bytes = s->gate_up_bytes;
   src.experts = s->experts;
+  src.n_slots = s->n_slots;
   src.shared_gate_up = shared_gate_up;
   src.shared_down = shared_down;
   return src;
