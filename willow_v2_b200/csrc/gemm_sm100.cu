@@ -2,21 +2,25 @@
 // Replaces willow's dequantize-to-bf16 + matmul path for more than 8 tokens (gguf/metal.py:357-363, 404-407) and
 // the per-expert loop of Engine.each_expert (engines/base.py:534-591).
 //
-// Swap-AB: the expert's weight rows are the MMA's M (128 per tile), its tokens are N (a chunk of up to 256 of the
+// Swap-AB: the expert's weight rows are the MMA's M (128 per tile), its tokens are N (a chunk of up to 192 of the
 // expert's tokens; the MMA's N is the chunk rounded up to 16), K runs over the hidden size (gate_up, Q4_K) or the
 // FFN width (down, Q6_K) in blocks of 64. An item is (chunk, 128-row M tile). The kernel is persistent: one CTA
 // per SM walks the items i = blockIdx.x, + gridDim.x, ... with specialised warps:
-//   warp 0      TMA: the token tile of each K block (fp16, 128-byte swizzle) into a 3-stage ring
-//   warp 1      allocates 512 TMEM columns (two fp32 accumulators of 256 columns); one lane issues 4 tcgen05.mma
-//               (K = 16) per K block; tcgen05.commit frees the stage, and after an item's last K block marks
-//               its accumulator full
+//   warp 0      TMA: the token tile of each K block (fp16, 128-byte swizzle) into a shared-memory ring
+//   warp 1      allocates all 512 TMEM columns: two fp32 accumulators of 192 columns and a 4-stage ring of fp16
+//               weight tiles (32 columns each). One lane issues 4 tcgen05.mma (K = 16) per K block with A read
+//               from TMEM and B from shared memory; tcgen05.commit frees the stages, and after an item's last K
+//               block marks its accumulator full
 //   warp 2      the weight bytes into shared memory. Q4_K: one super-block column (144 bytes of 128 rows) per
 //               TMA load pair, 3 deep (the expert matrices are a 3-D tensor map over the slab). Q6_K: the item's
-//               128 rows, contiguous, by one bulk copy
+//               128 rows, contiguous, by one bulk copy, 2 deep
 //   warps 3-6   the epilogue: accumulator -> registers (tcgen05.ld), SwiGLU or scaling, fp16 stores; it works on
 //               one accumulator while the MMAs fill the other
-//   warps 7-14  dequantise the 128 x 64 weight tile of each K block from shared memory into the stage, two
-//               groups of 4 warps taking alternate K blocks (thread = tile row)
+//   warps 7-14  dequantise the 128 x 64 weight tile of each K block from the shared-memory bytes into a TMEM
+//               stage (tcgen05.st), two groups of 4 warps taking alternate K blocks; thread = tile row = TMEM lane
+// Keeping A out of shared memory matters: an M = 128 MMA already reads ~100 bytes per clock of shared memory for
+// its operands, close to the port's 128, so writing and re-reading the dequantised tile there would bound the
+// kernel by shared-memory bandwidth.
 // Dequantisation is packed fp16 arithmetic: codes are moved into the low mantissa bits of 1024.0 (low nibbles,
 // 6-bit codes) or 64.0 (high nibbles, spacing 1/16) by byte permutes and masks, the magic is subtracted exactly,
 // and one fused multiply-add applies the sub-block's d*sc and -dmin*mn rounded to fp16 (measured error on an
@@ -37,28 +41,35 @@ namespace wmoe {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kBoxRows = 128;
-constexpr int kStages = 3;
+constexpr int kBM = 128, kBN = 192, kBK = 64, kBoxRows = 64;
+constexpr int kAStages = 4;                           // weight tiles in TMEM
+constexpr int kAccCols = kBN;                         // accumulator b at columns [b * kBN, (b + 1) * kBN)
+constexpr int kACol0 = 2 * kAccCols;                  // weight stage s at columns kACol0 + 32 s
+constexpr int kTmemCols = 512;
+static_assert(kACol0 + 32 * kAStages <= kTmemCols, "TMEM columns");
+constexpr int kMaxBStages = 6;
 constexpr int kWarps = 15, kThreads = kWarps * 32;
-constexpr int kTileA = kBM * kBK * 2;                 // 16 KB fp16 weights
-constexpr int kTileB = kBN * kBK * 2;                 // 32 KB fp16 tokens
-constexpr int kStageBytes = kTileA + kTileB;
+constexpr int kTileB = kBN * kBK * 2;                 // 24 KB fp16 tokens
 constexpr int kQ4Row = 144;                           // one Q4_K super-block of a row
 constexpr int kQ4Unit = kBM * kQ4Row;                 // 18,432 B: one super-block column of the tile
-constexpr int kQ4Depth = 3;
 constexpr int kQ6Unit = kBM * 2 * Q6K_BYTES;          // 53,760 B: 128 down rows of F = 512
-constexpr int kXbufBytes = 32 * 64 * 4;               // gate/up exchange of 32 columns
+constexpr int kXbufBytes = 32 * 64 * 4;               // gate/up exchange of 32 columns (fp32)
+constexpr int kOutBytes = 32 * kBM * 2;                // one 32-column chunk of the output, token-major fp16
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
 template <int MODE>
 struct Layout {
-  static constexpr int depth = MODE == 0 ? kQ4Depth : 1;  // weight ring
+  static constexpr int bstages = MODE == 0 ? 6 : 4;      // token tile ring
+  static constexpr int depth = MODE == 0 ? 3 : 2;        // weight byte ring
   static constexpr int unit = MODE == 0 ? kQ4Unit : kQ6Unit;
-  static constexpr int raw = kStages * kStageBytes;       // weight ring offset
-  static constexpr int xbuf = raw + depth * unit;
-  static constexpr int bytes = xbuf + (MODE == 0 ? kXbufBytes : 0) + 1024;  // + alignment slack
+  static constexpr int raw = bstages * kTileB;           // weight ring offset (1024-aligned)
+  static constexpr int xbuf = raw + depth * unit;        // gate_up only
+  static constexpr int obuf = xbuf + (MODE == 0 ? kXbufBytes : 0);
+  static constexpr int bytes = obuf + kOutBytes + 1024;  // + alignment slack
 };
 static_assert(Layout<0>::bytes <= 232448 && Layout<1>::bytes <= 232448, "shared memory");
+static_assert(Layout<0>::bstages <= kMaxBStages && Layout<1>::bstages <= kMaxBStages, "barrier arrays");
+static_assert(kTileB % 1024 == 0 && kQ4Unit % 1024 == 0, "TMA destinations stay 1024-aligned");
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
@@ -149,12 +160,23 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p) {
 // Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator, both K-major, M = 128; N at bits 17-22.
 constexpr uint32_t kIdescBase = (1u << 4) | (uint32_t(kBM >> 4) << 24);
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
+// D (TMEM) += A (TMEM: 128 lanes, 8 columns of fp16 pairs) x B (shared memory descriptor)
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
   asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
           tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 16 consecutive TMEM columns of this thread's lane from registers
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
 
@@ -179,9 +201,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Byte offset of (row, 16-byte chunk c of the row's 128 bytes) in a 128-byte-swizzled K-major tile.
-__device__ __forceinline__ int sw128(int row, int c) { return (row >> 3) * 1024 + (row & 7) * 128 + ((c ^ (row & 7)) << 4); }
-
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -193,10 +212,10 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<co
 // Stored position of element e within its run of 8 (and back: the map is its own inverse).
 __device__ __forceinline__ int perm8(int e) { return (e & ~7) | ((e & 1) << 1) | ((e & 2) >> 1) | (e & 4); }
 
-// Q4_K K block (sub-blocks 2g and 2g + 1 of one super-block) of tile row r, from the row's 144 bytes in shared
-// memory, into the swizzled A tile. Low nibbles of quant bytes 32g .. 32g + 31 are elements 0-31, high nibbles
-// elements 32-63 (gguf/quants.py:82-98).
-__device__ __forceinline__ void dequant_q4k_block(const uint8_t* row, int g, uint8_t* tile, int r) {
+// Q4_K K block (sub-blocks 2g and 2g + 1 of one super-block) of one tile row, from the row's 144 bytes in shared
+// memory, into the thread's TMEM lane at taddr: 32 columns of fp16 pairs, stored position p in column p / 2. Low
+// nibbles of quant bytes 32g .. 32g + 31 are elements 0-31, high nibbles elements 32-63 (gguf/quants.py:82-98).
+__device__ __forceinline__ void dequant_q4k_block(const uint8_t* row, int g, uint32_t taddr) {
   const uint4 hd = *reinterpret_cast<const uint4*>(row);
   const float d = f16_to_f32(uint16_t(hd.x & 0xFFFF)), dmin = f16_to_f32(uint16_t(hd.x >> 16));
   int sc0, mn0, sc1, mn1;
@@ -208,27 +227,29 @@ __device__ __forceinline__ void dequant_q4k_block(const uint8_t* row, int g, uin
   const uint4 qb = *reinterpret_cast<const uint4*>(row + 32 + 32 * g);
   const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
   const __half2 k1024 = u2h(0x64006400u), k64 = u2h(0x54005400u);
+  uint32_t o[16];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t lo[4], hi[4];
+  for (int half = 0; half < 2; ++half) {  // low nibbles (elements 0-31), then high nibbles (32-63)
 #pragma unroll
-    for (int w = 0; w < 2; ++w) {
-      const uint32_t x = qw[2 * c + w];
-      const uint32_t pe = __byte_perm(x, 0, 0x4240), po = __byte_perm(x, 0, 0x4341);  // bytes (0, 2), (1, 3)
-      lo[2 * w] = h2u(__hfma2(__hsub2(u2h((pe & 0x000F000Fu) | 0x64006400u), k1024), A0, B0));
-      lo[2 * w + 1] = h2u(__hfma2(__hsub2(u2h((po & 0x000F000Fu) | 0x64006400u), k1024), A0, B0));
-      hi[2 * w] = h2u(__hfma2(__hsub2(u2h((pe & 0x00F000F0u) | 0x54005400u), k64), A1, B1));
-      hi[2 * w + 1] = h2u(__hfma2(__hsub2(u2h((po & 0x00F000F0u) | 0x54005400u), k64), A1, B1));
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t pe = __byte_perm(qw[w], 0, 0x4240), po = __byte_perm(qw[w], 0, 0x4341);  // bytes (0,2), (1,3)
+      if (half == 0) {
+        o[2 * w] = h2u(__hfma2(__hsub2(u2h((pe & 0x000F000Fu) | 0x64006400u), k1024), A0, B0));
+        o[2 * w + 1] = h2u(__hfma2(__hsub2(u2h((po & 0x000F000Fu) | 0x64006400u), k1024), A0, B0));
+      } else {
+        o[2 * w] = h2u(__hfma2(__hsub2(u2h((pe & 0x00F000F0u) | 0x54005400u), k64), A1, B1));
+        o[2 * w + 1] = h2u(__hfma2(__hsub2(u2h((po & 0x00F000F0u) | 0x54005400u), k64), A1, B1));
+      }
     }
-    *reinterpret_cast<uint4*>(tile + sw128(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4*>(tile + sw128(r, 4 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    tmem_st16(taddr + uint32_t(16 * half), o);
   }
 }
 
-// Q6_K K block kb of tile row r (64 elements of super-block kb / 4: half hh = (kb % 4) / 2, quarters 2q and 2q + 1,
-// q = kb % 2) from the row's bytes in shared memory (gguf/quants.py:120-140). Element e: ql byte hh*64 + e
-// (nibble q), qh byte 128 + hh*32 + e % 32 (bits 4q + 2 (e / 32)), scale index hh*8 + 4q + e / 16.
-__device__ __forceinline__ void dequant_q6k_block(const uint8_t* row, int kb, uint8_t* tile, int r) {
+// Q6_K K block kb of one tile row (64 elements of super-block kb / 4: half hh = (kb % 4) / 2, quarters 2q and
+// 2q + 1, q = kb % 2) from the row's bytes in shared memory (gguf/quants.py:120-140) into the thread's TMEM lane.
+// Element e: ql byte hh*64 + e (nibble q), qh byte 128 + hh*32 + e % 32 (bits 4q + 2 (e / 32)), scale index
+// hh*8 + 4q + e / 16.
+__device__ __forceinline__ void dequant_q6k_block(const uint8_t* row, int kb, uint32_t taddr) {
   const uint8_t* b = row + (kb / 4) * Q6K_BYTES;
   const int hh = (kb % 4) / 2, q = kb % 2;
   uint32_t qh[8];
@@ -255,21 +276,17 @@ __device__ __forceinline__ void dequant_q6k_block(const uint8_t* row, int kb, ui
       const uint4 v = lds_u2_16(b + hh * 64 + 32 * half + 16 * i);
       ql[4 * i] = v.x, ql[4 * i + 1] = v.y, ql[4 * i + 2] = v.z, ql[4 * i + 3] = v.w;
     }
+    uint32_t o[16];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t o[4];
-#pragma unroll
-      for (int w = 0; w < 2; ++w) {
-        const int e0 = 8 * c + 4 * w;  // within the half
-        const uint32_t code = ((ql[e0 / 4] >> (4 * q)) & 0x0F0F0F0Fu) |
-                              (((qh[e0 / 4] >> (4 * q + 2 * half)) & 0x03030303u) << 4);  // q6, 0..63
-        const uint32_t pe = __byte_perm(code, 0x64646464u, 0x4240), po = __byte_perm(code, 0x64646464u, 0x4341);
-        const __half2 dd = D[2 * half + e0 / 16];
-        o[2 * w] = h2u(__hmul2(__hsub2(u2h(pe), k1056), dd));
-        o[2 * w + 1] = h2u(__hmul2(__hsub2(u2h(po), k1056), dd));
-      }
-      *reinterpret_cast<uint4*>(tile + sw128(r, 4 * half + c)) = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int w = 0; w < 8; ++w) {  // elements 4w .. 4w + 3 of the half
+      const uint32_t code = ((ql[w] >> (4 * q)) & 0x0F0F0F0Fu) |
+                            (((qh[w] >> (4 * q + 2 * half)) & 0x03030303u) << 4);  // q6, 0..63
+      const uint32_t pe = __byte_perm(code, 0x64646464u, 0x4240), po = __byte_perm(code, 0x64646464u, 0x4341);
+      const __half2 dd = D[2 * half + w / 4];
+      o[2 * w] = h2u(__hmul2(__hsub2(u2h(pe), k1056), dd));
+      o[2 * w + 1] = h2u(__hmul2(__hsub2(u2h(po), k1056), dd));
     }
+    tmem_st16(taddr + uint32_t(16 * half), o);
   }
 }
 
@@ -309,9 +326,10 @@ __device__ __forceinline__ int item_slot(const GemmParams& p, int u) {
 }
 
 struct Bars {
-  uint64_t full_a[kStages], full_b[kStages], empty[kStages];
+  uint64_t full_a[kAStages], empty_a[kAStages];
+  uint64_t full_b[kMaxBStages], empty_b[kMaxBStages];
   uint64_t acc_full[2], acc_empty[2];
-  uint64_t raw_full[kQ4Depth], raw_empty[kQ4Depth];
+  uint64_t raw_full[3], raw_empty[3];
   uint64_t done;
   uint32_t tmem;
   int fail;
@@ -322,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_ws, const __grid_constant__ GemmParams p) {
   using L = Layout<MODE>;
+  constexpr int BS = L::bstages;
   extern __shared__ __align__(1024) uint8_t dyn[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* raw = base + L::raw;
@@ -334,10 +353,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     bars.fail = 0;
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kAStages; ++s) {
       mbar_init(&bars.full_a[s], 4);  // the 4 warps of one dequant group
+      mbar_init(&bars.empty_a[s], 1);
+    }
+    for (int s = 0; s < BS; ++s) {
       mbar_init(&bars.full_b[s], 1);
-      mbar_init(&bars.empty[s], 1);
+      mbar_init(&bars.empty_b[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars.acc_full[b], 1);
@@ -352,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars.tmem)),
-                 "r"(2 * kBN)
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -364,25 +386,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   int issued_b = 0, issued_w = 0;  // copies the two producer lanes issued (for the drain after a failure)
 
   if (warp == 0) {
-    // ---------------- token tiles
+    // ---------------- token tiles: 1-3 boxes of 64 rows per K block
     if (lane == 0) {
       int it = 0;
       for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
         const Item t = get_item(p, i);
-        const int nb = t.ncols > kBoxRows ? 2 : 1;
+        const int nbox = (t.ncols + kBoxRows - 1) / kBoxRows;
         for (int kb = 0; kb < nk; ++kb) {
-          const int kbg = it * nk + kb, s = kbg % kStages;
-          if (kbg >= kStages && !mbar_wait(&bars.empty[s], unsigned((kbg / kStages - 1) & 1), fail)) goto out;
-          mbar_arrive_expect_tx(&bars.full_b[s], unsigned(nb * kBoxRows * kBK * 2));
-          uint8_t* dst = base + s * kStageBytes + kTileA;
-          tma_load_2d(dst, &tmap_b, kb * kBK, t.seg0 + t.n0, &bars.full_b[s]);
-          if (nb == 2) tma_load_2d(dst + kBoxRows * 128, &tmap_b, kb * kBK, t.seg0 + t.n0 + kBoxRows, &bars.full_b[s]);
+          const int kbg = it * nk + kb, s = kbg % BS;
+          if (kbg >= BS && !mbar_wait(&bars.empty_b[s], unsigned((kbg / BS - 1) & 1), fail)) goto out;
+          mbar_arrive_expect_tx(&bars.full_b[s], unsigned(nbox * kBoxRows * kBK * 2));
+          uint8_t* dst = base + s * kTileB;
+          for (int bx = 0; bx < nbox; ++bx)
+            tma_load_2d(dst + bx * kBoxRows * 128, &tmap_b, kb * kBK, t.seg0 + t.n0 + bx * kBoxRows, &bars.full_b[s]);
           issued_b = kbg + 1;
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
+    // ---------------- MMA issuer: A from the TMEM ring, B from the shared-memory ring
     if (lane == 0) {
       int it = 0;
       for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
@@ -391,19 +413,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it >= 2 && !mbar_wait(&bars.acc_empty[buf], unsigned((it / 2 - 1) & 1), fail)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t idesc = kIdescBase | (uint32_t(((t.ncols + 15) & ~15) >> 3) << 17);
-        const uint32_t d = tmem_base + uint32_t(buf * kBN);
+        const uint32_t d = tmem_base + uint32_t(buf * kAccCols);
         bool ok = true;
         for (int kb = 0; kb < nk && ok; ++kb) {
-          const int kbg = it * nk + kb, s = kbg % kStages;
-          const unsigned ph = unsigned((kbg / kStages) & 1);
-          ok = mbar_wait(&bars.full_a[s], ph, fail) && mbar_wait(&bars.full_b[s], ph, fail);
+          const int kbg = it * nk + kb, sa = kbg % kAStages, sb = kbg % BS;
+          ok = mbar_wait(&bars.full_a[sa], unsigned((kbg / kAStages) & 1), fail) &&
+               mbar_wait(&bars.full_b[sb], unsigned((kbg / BS) & 1), fail);
           if (!ok) break;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t da = smem_desc(base + s * kStageBytes), db = smem_desc(base + s * kStageBytes + kTileA);
+          const uint32_t ta = tmem_base + uint32_t(kACol0 + 32 * sa);
+          const uint64_t db = smem_desc(base + sb * kTileB);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)  // 32 bytes of K per MMA: +2 in the 16-byte address field
-            mma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
-          mma_commit(&bars.empty[s]);
+          for (int k = 0; k < kBK / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, +32 bytes (+2) of B
+            mma_f16_ts(d, ta + uint32_t(8 * k), db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          mma_commit(&bars.empty_a[sa]);
+          mma_commit(&bars.empty_b[sb]);
         }
         if (!ok) break;
         mma_commit(&bars.acc_full[buf]);
@@ -443,9 +467,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp <= 6) {
-    // ---------------- epilogue (warps 3-6 cover the four TMEM lane quadrants)
-    const int quad = warp % 4, trow = 32 * quad + lane;
-    float* xbuf = reinterpret_cast<float*>(base + L::xbuf);  // [32 columns][64 rows] up values
+    // ---------------- epilogue (warps 3-6 cover the four TMEM lane quadrants). Per 32-column chunk: accumulator
+    // -> registers (thread = row), SwiGLU or scaling, fp16 into a token-major chunk in shared memory, then 16-byte
+    // stores of whole token rows.
+    const int quad = warp % 4, trow = 32 * quad + lane, e = tid - 96;
+    float* xbuf = reinterpret_cast<float*>(base + L::xbuf);     // [32 columns][64 rows] up values
+    __half* obuf = reinterpret_cast<__half*>(base + L::obuf);   // [32 columns][rows of the tile] fp16
+    constexpr int orows = MODE == 0 ? 64 : kBM;                 // output rows per tile
+    const int ld = MODE == 0 ? p.F : p.H;
     int it = 0;
     for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
       const Item t = get_item(p, i);
@@ -459,41 +488,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           : "memory");
       if (!all_ready) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t taddr = tmem_base + uint32_t(buf * kBN) + (uint32_t(32 * quad) << 16);
-      const size_t row0 = size_t(t.seg0 + t.n0);
+      const uint32_t taddr = tmem_base + uint32_t(buf * kAccCols) + (uint32_t(32 * quad) << 16);
+      __half* gout = p.out + size_t(t.seg0 + t.n0) * ld + orows * t.mt;
       for (int c0 = 0; c0 < t.ncols; c0 += 32) {
         float v[32];
         tmem_ld32(taddr + uint32_t(c0), v);
         if (MODE == 0) {
-          // gate rows are quadrants 0-1, up rows quadrants 2-3
+          // gate rows are quadrants 0-1, up rows quadrants 2-3; h index 64 mt + trow, stored in run-of-8 order
           if (quad >= 2) {
 #pragma unroll
             for (int c = 0; c < 32; ++c) xbuf[c * 64 + (trow - 64)] = v[c];
           }
           asm volatile("bar.sync 1, 128;" ::: "memory");
           if (quad < 2) {
-            const int j = perm8(64 * t.mt + trow);  // stored column of h index 64 mt + trow
+            const int j = perm8(trow);
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (c0 + c < t.ncols)
-                p.out[(row0 + c0 + c) * p.F + j] = __float2half_rn(silu(v[c]) * xbuf[c * 64 + trow] * (1.0f / 32.0f));
+            for (int c = 0; c < 32; ++c) {
+              const float g = v[c];
+              obuf[c * 64 + j] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * xbuf[c * 64 + trow] * (1.0f / 32.0f));
+            }
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
         } else {
-          __half* o = p.out + (row0 + c0) * p.H + kBM * t.mt + trow;
-          const int n = min(32, t.ncols - c0);
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (c < n) o[size_t(c) * p.H] = __float2half_rn(v[c]);
+          for (int c = 0; c < 32; ++c) obuf[c * kBM + trow] = __float2half_rn(v[c]);
         }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int n = min(32, t.ncols - c0);
+        constexpr int pieces = 32 * orows / 8;  // 16-byte pieces of the chunk
+#pragma unroll
+        for (int q = e; q < pieces; q += 128) {
+          const int c = q / (orows / 8), g = q % (orows / 8);
+          if (c < n)
+            *reinterpret_cast<uint4*>(gout + size_t(c0 + c) * ld + 8 * g) =
+                *reinterpret_cast<const uint4*>(obuf + c * orows + 8 * g);
+        }
+        if (MODE == 1) asm volatile("bar.sync 1, 128;" ::: "memory");  // obuf is rewritten by the next chunk
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
     }
   } else {
-    // ---------------- dequantisation: group j takes the K blocks kb with kb % 2 == j; thread = tile row r
-    const int dw = warp - 7, j = dw / 4, r = (dw % 4) * 32 + lane;
+    // ---------------- dequantisation: group j takes the K blocks kb with kb % 2 == j; thread = tile row = TMEM
+    // lane 32 (warp % 4) + lane (a warp reaches only its own lane quadrant)
+    const int dw = warp - 7, j = dw / 4, r = 32 * (warp % 4) + lane;
+    const uint32_t tlane = tmem_base + (uint32_t(32 * (warp % 4)) << 16);
     int it = 0;
     for (int i = blockIdx.x; i < total; i += gridDim.x, ++it) {
       for (int un = 0; un < units; ++un) {
@@ -502,13 +541,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* wrow = raw + rs * L::unit + r * (MODE == 0 ? kQ4Row : 2 * Q6K_BYTES);
         const int kb0 = MODE == 0 ? 4 * un : 0, kb1 = MODE == 0 ? 4 * un + 4 : nk;
         for (int kb = kb0 + j; kb < kb1; kb += 2) {
-          const int kbg = it * nk + kb, s = kbg % kStages;
-          if (kbg >= kStages && !mbar_wait_warp(&bars.empty[s], unsigned((kbg / kStages - 1) & 1), fail)) goto out;
+          const int kbg = it * nk + kb, s = kbg % kAStages;
+          if (kbg >= kAStages &&
+              !mbar_wait_warp(&bars.empty_a[s], unsigned((kbg / kAStages - 1) & 1), fail))
+            goto out;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t ta = tlane + uint32_t(kACol0 + 32 * s);
           if (MODE == 0)
-            dequant_q4k_block(wrow, kb % 4, base + s * kStageBytes, r);
+            dequant_q4k_block(wrow, kb % 4, ta);
           else
-            dequant_q6k_block(wrow, kb, base + s * kStageBytes, r);
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            dequant_q6k_block(wrow, kb, ta);
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars.full_a[s]);
         }
@@ -527,8 +571,8 @@ out:
     if (warp == 1) mbar_wait(&bars.done, 0, &never);
     if (*fail && lane == 0) {
       if (warp == 0)
-        for (int kbg = max(0, issued_b - kStages); kbg < issued_b; ++kbg)
-          mbar_wait(&bars.full_b[kbg % kStages], unsigned((kbg / kStages) & 1), &never);
+        for (int kbg = max(0, issued_b - BS); kbg < issued_b; ++kbg)
+          mbar_wait(&bars.full_b[kbg % BS], unsigned((kbg / BS) & 1), &never);
       if (warp == 2)
         for (int ru = max(0, issued_w - L::depth); ru < issued_w; ++ru)
           mbar_wait(&bars.raw_full[ru % L::depth], unsigned((ru / L::depth) & 1), &never);
@@ -537,10 +581,10 @@ out:
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kBN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
 }
 
-// Chunk list: one entry per (segment, up to 256 tokens), segments in order.
+// Chunk list: one entry per (segment, up to kBN tokens), segments in order.
 __global__ void __launch_bounds__(512) chunk_list_kernel(PairMap pm, int2* chunks, int* n_chunks) {
   __shared__ int warp_sum[16];
   const int n = *pm.n_used, u = threadIdx.x, lane = u % 32, wid = u / 32;
