@@ -148,6 +148,7 @@ typedef struct wmoe_layer_weights {
     const uint8_t* shared_gate_up;  /* Q4_K [2*ffn, hidden] */
     const uint8_t* shared_down;     /* Q6_K [hidden, ffn] */
     const float* router_packed;     /* f32 [hidden, WMOE_ROUTER_STRIDE] from wmoe_pack_router, or null */
+    const uint16_t* router_split;   /* bf16 [3, experts, hidden] from wmoe_split_router, or null */
 } wmoe_layer_weights;
 
 /* The router and the shared-expert gate transposed into one [hidden, WMOE_ROUTER_STRIDE] f32 matrix: column e < experts
@@ -157,6 +158,20 @@ typedef struct wmoe_layer_weights {
 #define WMOE_ROUTER_STRIDE 264
 int wmoe_pack_router(wmoe_ctx* ctx, const float* router_w, const float* shared_gate, int experts, int hidden,
                      float* out, void* stream);
+
+/* The router as three bf16 terms, R = R1 + R2 + R3 (R1 = bf16(R), R2 = bf16(R - R1), R3 = bf16(R - R1 - R2)),
+ * stored [3, experts, hidden]: a layout transform done once at load, like wmoe_pack_router. With it,
+ * wmoe_moe_forward_layer computes the router logits of bf16 tokens on the tensor cores with float32 accuracy
+ * (bf16 x R_i products are exact in the float32 accumulator); without it the router runs in float32 on the CUDA
+ * cores. out: device memory of 3 * experts * hidden bf16 values. */
+int wmoe_split_router(wmoe_ctx* ctx, const float* router_w, int experts, int hidden, uint16_t* out, void* stream);
+
+/* wmoe_moe_forward with the layer's weights as one wmoe_layer_weights (device pointers), so that prepared forms
+ * (router_split) can be used. Same semantics, arguments and errors as wmoe_moe_forward, which it generalises:
+ * the MoE block of engines/base.py:445-491 reads all of a layer's weights under one name prefix in the same way. */
+int wmoe_moe_forward_layer(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                           const wmoe_layer_weights* weights, void* out, int out_dtype, int32_t* topk_idx_out,
+                           float* topk_w_out, void* stream);
 
 /* One decode token through layers [layer_begin, layer_begin + n_layers) of the store:
  * h <- h + moe_l(rms_norm(h)) per layer (eps, unit weight), in one persistent launch per 64 layers.

@@ -38,8 +38,14 @@ def test_library_rejects_bad_arguments_without_a_gpu():
 
 
 def test_layer_weights_struct_matches_header():
+    """The ctypes mirror of wmoe_layer_weights has the header's fields, in order, all pointers."""
+    import re
     from willow_v2_b200 import lib as L
-    assert ctypes.sizeof(L.LayerWeights) == 6 * ctypes.sizeof(ctypes.c_void_p)
+    text = open(os.path.join(REPO, "include", "wmoe.h")).read()
+    body = re.search(r"typedef struct wmoe_layer_weights \{(.*?)\} wmoe_layer_weights;", text, re.S).group(1)
+    names = re.findall(r"\*\s*(\w+);", body)
+    assert names == [f[0] for f in L.LayerWeights._fields_]
+    assert ctypes.sizeof(L.LayerWeights) == len(names) * ctypes.sizeof(ctypes.c_void_p)
 
 
 def f64_to_f16_rne(v: float) -> int:

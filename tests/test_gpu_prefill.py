@@ -110,3 +110,59 @@ def test_gemm_path_config3_size(model):
     idx = [0, 2047, 4095]
     ref = ora.moe(x[idx].float().cpu().numpy(), **oracle_layer(0))[0]
     assert rel_l2(g[idx].cpu().numpy(), ref) < 1e-3
+
+
+def routing_agrees(x, lw, bias, sel_a, sel_b, w_a, w_b):
+    """Two routings of the same tokens agree: identical picks except where the float64 logits of the swapped
+    experts are within 1e-5 (the parity rule), and weights within 1e-5 where the picks agree."""
+    import torch
+    logits = x.double() @ lw.router_w.double().T
+    if bias is not None:
+        logits = logits + torch.from_numpy(bias).cuda().double()
+    a, b = sel_a.long(), sel_b.long()
+    rows = (a.sort(1).values != b.sort(1).values).any(1)
+    for t in rows.nonzero().flatten().tolist():
+        only_a = set(a[t].tolist()) - set(b[t].tolist())
+        only_b = set(b[t].tolist()) - set(a[t].tolist())
+        gap = max(abs(logits[t, i] - logits[t, j]).item() for i in only_a for j in only_b)
+        assert gap < 1e-5, (t, only_a, only_b, gap)
+    same = ~rows
+    assert torch.allclose(w_a[same], w_b[same], rtol=0, atol=1e-5)
+    return int(rows.sum())
+
+
+@pytest.mark.parametrize("T,zipf", [(4096, False), (1024, True), (37, False)])
+def test_tensor_core_router_matches_float32_router(model, T, zipf):
+    """bf16 tokens with the split router (tcgen05, K split) against the float32 CUDA-core router on the same
+    inputs: same routing (up to 1e-5 logit ties), same outputs within the path tolerance."""
+    import torch
+    from willow_v2_b200 import moe
+    ctx, store = model
+    bias = synth.zipf_bias(SEED) if zipf else None
+    lw = layer_weights(1, bias)
+    lw_tc = moe.LayerWeights(**{f: getattr(lw, f) for f in ("router_w", "shared_gate", "shared_gate_up",
+                                                             "shared_down", "router_bias")}).prepare(ctx)
+    x = torch.from_numpy(synth.hidden(SEED, T, step=70 + T)).to(torch.bfloat16).cuda()
+    g, gw, gsel = forward(ctx, store, 1, x, lw_tc, "gemm", out_dtype=torch.float32)
+    v, vw, vsel = forward(ctx, store, 1, x, lw, "gemm", out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    routing_agrees(x, lw, bias, gsel, vsel, gw, vw)
+    assert rel_l2(g.cpu().numpy(), v.cpu().numpy()) < 1e-3
+    idx = [0, T // 2, T - 1]
+    ref = ora.moe(x[idx].float().cpu().numpy(), **oracle_layer(1, bias))[0]
+    assert rel_l2(g[idx].cpu().numpy(), ref) < 1e-3
+
+
+def test_split_router_terms_sum_to_router(model):
+    """wmoe_split_router: three bf16 terms whose float64 sum is the float32 router to ~2^-24 relative."""
+    import torch
+    from willow_v2_b200 import moe
+    ctx, _ = model
+    r = torch.from_numpy(synth.router_weight(SEED, 3)).cuda()
+    s = moe.split_router(r, ctx)
+    torch.cuda.synchronize()
+    assert s.shape == (3, 256, 2048) and s.dtype == torch.bfloat16
+    assert torch.equal(s[0], r.to(torch.bfloat16))
+    total = s.double().sum(0)
+    assert ((total - r.double()).abs() <= r.double().abs() * 2.0 ** -23).all()

@@ -9,6 +9,14 @@
 #include "kernels.cuh"
 #include "store.h"
 
+#include <cstddef>
+
+// wmoe_decode_stack hands the caller's wmoe_layer_weights array to the kernels as DecodeLayer: same layout
+static_assert(sizeof(wmoe_layer_weights) == sizeof(wmoe::DecodeLayer), "layer weight layouts differ");
+static_assert(offsetof(wmoe_layer_weights, router_packed) == offsetof(wmoe::DecodeLayer, router_packed) &&
+                  offsetof(wmoe_layer_weights, router_split) == offsetof(wmoe::DecodeLayer, router_split),
+              "layer weight layouts differ");
+
 using namespace wmoe;
 
 int ctx_fail(wmoe_ctx* ctx, int code, const std::string& msg) {
@@ -177,6 +185,16 @@ int wmoe_pack_router(wmoe_ctx* ctx, const float* router_w, const float* shared_g
   return WMOE_OK;
 }
 
+int wmoe_split_router(wmoe_ctx* ctx, const float* router_w, int experts, int hidden, uint16_t* out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (experts <= 0 || hidden <= 0) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_split_router: bad shape");
+  if (!router_w || !out) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_split_router: null pointer");
+  WMOE_CHECK_CUDA(ctx, router_split(router_w, experts, hidden, out, static_cast<cudaStream_t>(stream)),
+                  "wmoe_split_router");
+  ctx->launches += 1;
+  return WMOE_OK;
+}
+
 int wmoe_dispatch(wmoe_ctx* ctx, const int32_t* topk_idx, int T, int top_k, int experts, int32_t* counts,
                   int32_t* offsets, int32_t* perm, int64_t* usage, void* stream) {
   if (!ctx) return WMOE_ERR_INVALID;
@@ -266,10 +284,11 @@ int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, 
   return WMOE_OK;
 }
 
-int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
-                     const float* router_w, const float* router_bias, const float* shared_gate,
-                     const uint8_t* shared_gate_up, const uint8_t* shared_down, void* out, int out_dtype,
-                     int32_t* topk_idx_out, float* topk_w_out, void* stream) {
+static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T,
+                            int top_k, const float* router_w, const float* router_bias, const float* shared_gate,
+                            const uint8_t* shared_gate_up, const uint8_t* shared_down, const float* router_packed,
+                            const void* router_split, void* out, int out_dtype, int32_t* topk_idx_out,
+                            float* topk_w_out, void* stream) {
   if (!ctx) return WMOE_ERR_INVALID;
   if (!store) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: null store");
   if (store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: store belongs to another context");
@@ -287,7 +306,7 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
   if (T == 1 && !store->capped && ctx->use_decode_kernel && ctx->decode_ctas > 0 && E == 256) {
     // one token, every expert resident: the persistent decode kernel (one launch, no host synchronisation)
     if (int rc = ensure_scratch(ctx, decode_scratch_bytes(H, F, E, ctx->decode_ctas))) return rc;
-    DecodeLayer dl{router_w, router_bias, shared_gate, shared_gate_up, shared_down};
+    DecodeLayer dl{router_w, router_bias, shared_gate, shared_gate_up, shared_down, router_packed, router_split};
     int n = 0;
     const cudaError_t e = decode_persistent(store_source(store, shared_gate_up, shared_down), layer, 1, &dl, H, F, E,
                                             top_k, 0.f, false, x, x_dtype, out, out_dtype, topk_idx_out, topk_w_out,
@@ -299,7 +318,11 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
   }
   const int k = top_k, P = T * (k + 1);
   Plan plan;
-  const size_t o_logits = plan.take<float>(size_t(T) * (E + 1));
+  // router logits on the tensor cores for bf16 tokens when the split router is given (partial sums of a K split),
+  // else float32 on the CUDA cores ([T][E + 1] with the shared gate as column E)
+  const bool router_tc = router_split && x_dtype == WMOE_BF16 && T >= 16 && router_tc_supported(T, H, E);
+  const size_t o_logits =
+      plan.take<float>(router_tc ? size_t(kRouterKSplit) * T * E : size_t(T) * (E + 1));
   const size_t o_w = plan.take<float>(size_t(T) * k);
   const size_t o_idx = plan.take<int32_t>(size_t(T) * k);
   const size_t o_s = plan.take<float>(size_t(T));
@@ -330,11 +353,23 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
   float* topk_w = at<float>(ctx, o_w);
   int32_t* topk_idx = at<int32_t>(ctx, o_idx);
   float* shared_s = at<float>(ctx, o_s);
-  WMOE_CHECK_CUDA(ctx, router_logits(x, x_dtype, T, H, E, router_w, shared_gate, at<float>(ctx, o_logits), st, &n),
-                  "router");
-  WMOE_CHECK_CUDA(ctx, router_topk(at<float>(ctx, o_logits), T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr,
-                                   st, &n),
-                  "top-k");
+  if (router_tc) {
+    WMOE_CHECK_CUDA(ctx,
+                    router_logits_tc(x, T, H, E, router_split, at<float>(ctx, o_logits), ctx->d_status, st, &n),
+                    "router");
+    WMOE_CHECK_CUDA(ctx,
+                    router_topk_split(at<float>(ctx, o_logits), kRouterKSplit, T, E, k, router_bias, topk_w, topk_idx,
+                                      shared_s, nullptr, x, x_dtype, shared_gate, H, st, &n),
+                    "top-k");
+  } else {
+    WMOE_CHECK_CUDA(ctx,
+                    router_logits(x, x_dtype, T, H, E, router_w, shared_gate, at<float>(ctx, o_logits), st, &n),
+                    "router");
+    WMOE_CHECK_CUDA(ctx,
+                    router_topk(at<float>(ctx, o_logits), T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr,
+                                st, &n),
+                    "top-k");
+  }
   std::vector<int32_t> experts_used;
   if (store->capped) {
     // the store must copy this call's experts in first: one wait for the routing (engines/base.py:456-460 does
@@ -395,6 +430,24 @@ int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x,
   if (store->capped)
     if (int rc = store_mark_used(store, layer, experts_used.data(), int(experts_used.size()), st)) return rc;
   return WMOE_OK;
+}
+
+int wmoe_moe_forward(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                     const float* router_w, const float* router_bias, const float* shared_gate,
+                     const uint8_t* shared_gate_up, const uint8_t* shared_down, void* out, int out_dtype,
+                     int32_t* topk_idx_out, float* topk_w_out, void* stream) {
+  return moe_forward_impl(ctx, store, layer, x, x_dtype, T, top_k, router_w, router_bias, shared_gate, shared_gate_up,
+                          shared_down, nullptr, nullptr, out, out_dtype, topk_idx_out, topk_w_out, stream);
+}
+
+int wmoe_moe_forward_layer(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                           const wmoe_layer_weights* w, void* out, int out_dtype, int32_t* topk_idx_out,
+                           float* topk_w_out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!w) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_layer: null weights");
+  return moe_forward_impl(ctx, store, layer, x, x_dtype, T, top_k, w->router_w, w->router_bias, w->shared_gate,
+                          w->shared_gate_up, w->shared_down, w->router_packed, w->router_split, out, out_dtype,
+                          topk_idx_out, topk_w_out, stream);
 }
 
 int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,

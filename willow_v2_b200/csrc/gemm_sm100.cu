@@ -36,10 +36,13 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "sm100.cuh"
 
 namespace wmoe {
 
 namespace {
+
+using namespace sm100;
 
 constexpr int kBM = 128, kBN = 192, kBK = 64, kBoxRows = 64;
 constexpr int kAStages = 4;                           // weight tiles in TMEM
@@ -55,7 +58,6 @@ constexpr int kQ4Unit = kBM * kQ4Row;                 // 18,432 B: one super-blo
 constexpr int kQ6Unit = kBM * 2 * Q6K_BYTES;          // 53,760 B: 128 down rows of F = 512
 constexpr int kXbufBytes = 32 * 64 * 4;               // gate/up exchange of 32 columns (fp32)
 constexpr int kOutBytes = 32 * kBM * 2;                // one 32-column chunk of the output, token-major fp16
-constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
 template <int MODE>
 struct Layout {
@@ -70,136 +72,6 @@ struct Layout {
 static_assert(Layout<0>::bytes <= 232448 && Layout<1>::bytes <= 232448, "shared memory");
 static_assert(Layout<0>::bstages <= kMaxBStages && Layout<1>::bstages <= kMaxBStages, "barrier arrays");
 static_assert(kTileB % 1024 == 0 && kQ4Unit % 1024 == 0, "TMA destinations stay 1024-aligned");
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Waits for the phase; gives up after the time limit or once another role has given up (fail set).
-__device__ bool mbar_wait(uint64_t* bar, unsigned parity, volatile int* fail) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*fail) return false;
-    if (globaltimer() - t0 > kTimeoutNs) {
-      *fail = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
-// the same, one answer for the whole warp (every lane waits; the warp continues only if all saw the phase)
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, unsigned parity, volatile int* fail) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, fail));
-}
-
-// 2-D TMA tile load (box 64 fp16 x 128 rows, 128-byte swizzle) completing on an mbarrier; x = column, y = row.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// 3-D TMA tile load (no swizzle): x = byte column, y = row, z = slot.
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (sm100 version 1).
-__device__ __forceinline__ uint64_t smem_desc(const void* p) {
-  const uint64_t addr = smem_u32(p);
-  return ((addr >> 4) & 0x3FFFull)        // start address
-         | (1ull << 16)                   // leading byte offset (unused for swizzled K-major): 16 B
-         | (uint64_t(1024 >> 4) << 32)    // stride byte offset: 1024 B between 8-row groups
-         | (1ull << 46)                   // descriptor version
-         | (2ull << 61);                  // SWIZZLE_128B
-}
-
-// Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator, both K-major, M = 128; N at bits 17-22.
-constexpr uint32_t kIdescBase = (1u << 4) | (uint32_t(kBM >> 4) << 24);
-
-// D (TMEM) += A (TMEM: 128 lanes, 8 columns of fp16 pairs) x B (shared memory descriptor)
-__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
-          tmem_d),
-      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// 16 consecutive TMEM columns of this thread's lane from registers
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-// 32 consecutive TMEM columns of this thread's lane (the warp's 32 lanes)
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
@@ -412,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = it & 1;
         if (it >= 2 && !mbar_wait(&bars.acc_empty[buf], unsigned((it / 2 - 1) & 1), fail)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t idesc = kIdescBase | (uint32_t(((t.ncols + 15) & ~15) >> 3) << 17);
+        const uint32_t idesc = idesc_f16(kBM, (t.ncols + 15) & ~15, false);
         const uint32_t d = tmem_base + uint32_t(buf * kAccCols);
         bool ok = true;
         for (int kb = 0; kb < nk && ok; ++kb) {
@@ -607,18 +479,33 @@ __global__ void __launch_bounds__(512) chunk_list_kernel(PairMap pm, int2* chunk
   if (u == 0) *n_chunks = total;
 }
 
+// 8 consecutive activations as float32 from one 16-byte (bf16) or two 16-byte (f32) loads
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
 // X_g[p] = fp16(x[token(p)]) for every pair position p (routed pairs, then the shared expert's rows), columns in
 // run-of-8 order.
 template <typename XT>
-__global__ void gather_fp16_kernel(PairMap pm, const XT* __restrict__ x, int H, __half* __restrict__ xg) {
+__global__ void __launch_bounds__(256) gather_fp16_kernel(PairMap pm, const XT* __restrict__ x, int H,
+                                                          __half* __restrict__ xg) {
   const int p = blockIdx.x;
   const int t = pair_token(pm, p);
   const XT* src = x + size_t(t) * H;
   __half* dst = xg + size_t(p) * H;
   for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
     float v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = to_f32(src[i + j]);
+    load8(src + i, v);
     // stored order within the run: elements 0, 2, 1, 3, 4, 6, 5, 7
     *reinterpret_cast<uint4*>(dst + i) =
         make_uint4(pack_h2(v[0], v[2]), pack_h2(v[1], v[3]), pack_h2(v[4], v[6]), pack_h2(v[5], v[7]));
@@ -626,13 +513,14 @@ __global__ void gather_fp16_kernel(PairMap pm, const XT* __restrict__ x, int H, 
 }
 
 // Combine from the fp16 down outputs (stored / 32): out[t] = sum over picks in ascending expert id of
-// w * 32 * y[pick] (engines/base.py:580-586), + s_t * 32 * y[shared row t] (base.py:481-489).
+// w * 32 * y[pick] (engines/base.py:580-586), + s_t * 32 * y[shared row t] (base.py:481-489). One CTA per token,
+// 8 consecutive outputs per thread from 16-byte loads of each picked row.
 template <int K>
 __global__ void __launch_bounds__(256) combine_f16_kernel(PairMap pm, int H, const float* __restrict__ topk_w,
                                                           const float* __restrict__ shared_s,
                                                           const __half* __restrict__ y, void* __restrict__ out,
                                                           int out_dtype) {
-  const int t = blockIdx.y;
+  const int t = blockIdx.x;
   int ps[K];
   float ws[K];
 #pragma unroll
@@ -654,32 +542,35 @@ __global__ void __launch_bounds__(256) combine_f16_kernel(PairMap pm, int H, con
       }
   const float s = shared_s[t] * 32.0f;
   const size_t shared_row = size_t(pm.T) * K + t;
-  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {
-    float acc = 0.f;
+  for (int r = threadIdx.x * 8; r < H; r += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(__half2float(y[size_t(ps[i]) * H + r]), ws[i]));
-    acc = __fadd_rn(acc, __fmul_rn(s, __half2float(y[shared_row * H + r])));
-    if (out_dtype == kF32)
-      static_cast<float*>(out)[size_t(t) * H + r] = acc;
-    else
-      static_cast<__nv_bfloat16*>(out)[size_t(t) * H + r] = __float2bfloat16_rn(acc);
+    for (int i = 0; i < K + 1; ++i) {
+      const size_t row = i < K ? size_t(ps[i]) : shared_row;
+      const float wi = i < K ? ws[i] : s;
+      const uint4 u = *reinterpret_cast<const uint4*>(y + row * H + r);
+      const uint32_t hw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[j]));
+        acc[2 * j] = __fadd_rn(acc[2 * j], i < K ? __fmul_rn(f.x, wi) : __fmul_rn(wi, f.x));
+        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], i < K ? __fmul_rn(f.y, wi) : __fmul_rn(wi, f.y));
+      }
+    }
+    if (out_dtype == kF32) {
+      float* o = static_cast<float*>(out) + size_t(t) * H + r;
+      *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint32_t b[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+        b[j] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + size_t(t) * H + r) = make_uint4(b[0], b[1], b[2], b[3]);
+    }
   }
-}
-
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeFn encode_fn() {
-  static EncodeFn fn = nullptr;
-  if (!fn) {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeFn>(f);
-  }
-  return fn;
 }
 
 // fp16 [rows, cols] row-major, boxes of 128 rows x 64 columns with the 128-byte swizzle
@@ -724,6 +615,8 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
                             int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
                             void* scratch, int num_sms, int* status, cudaStream_t st, int* launches) {
   if (H % QK || F != 2 * QK || H % kBM || pm.E + 1 > 512 || pm.k != 8 || num_sms <= 0) return cudaErrorInvalidValue;
+  // activations are read and written 16 bytes at a time
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16) return cudaErrorInvalidValue;
   // weight rows are copied by TMA and bulk copies: the matrices must start on 16-byte boundaries
   if (reinterpret_cast<uintptr_t>(src.shared_down) % 16 || reinterpret_cast<uintptr_t>(src.shared_gate_up) % 16 ||
       reinterpret_cast<uintptr_t>(src.slab) % 16 || src.slot_bytes % 16 || src.gate_up_bytes % 16)
@@ -784,8 +677,7 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
   gp.n_mtiles = H / kBM;
   gp.out = ybuf;
   grouped_gemm_kernel<1><<<unsigned(num_sms), kThreads, Layout<1>::bytes, st>>>(map_h, map_w, map_ws, gp);
-  combine_f16_kernel<8><<<dim3(unsigned((H + 255) / 256), unsigned(pm.T)), 256, 0, st>>>(pm, H, topk_w, shared_s, ybuf,
-                                                                                         out, out_dtype);
+  combine_f16_kernel<8><<<unsigned(pm.T), 256, 0, st>>>(pm, H, topk_w, shared_s, ybuf, out, out_dtype);
   *launches += 3;
   return cudaGetLastError();
 }

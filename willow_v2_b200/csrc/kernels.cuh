@@ -46,6 +46,17 @@ cudaError_t router_logits(const void* x, int x_dtype, int T, int H, int E, const
                           const float* shared_gate, float* logits, cudaStream_t st, int* launches);
 cudaError_t router_topk(const float* logits, int T, int E, int k, const float* bias, float* topk_w,
                         int32_t* topk_idx, float* shared_s, float* logits_out, cudaStream_t st, int* launches);
+cudaError_t router_topk_split(const float* logits, int splits, int T, int E, int k, const float* bias, float* topk_w,
+                              int32_t* topk_idx, float* shared_s, float* logits_out, const void* x, int x_dtype,
+                              const float* g, int H, cudaStream_t st, int* launches);
+
+// router_sm100.cu: bf16 tokens x (float32 router as three bf16 terms) on the tensor cores, K split kRouterKSplit
+// ways into partial logits [kRouterKSplit][T][E]
+constexpr int kRouterKSplit = 4;
+bool router_tc_supported(int T, int H, int E);
+cudaError_t router_split(const float* router_w, int E, int H, void* out, cudaStream_t st);
+cudaError_t router_logits_tc(const void* x_bf16, int T, int H, int E, const void* router_split3, float* partial,
+                             int* status, cudaStream_t st, int* launches);
 
 // dispatch.cu
 size_t dispatch_scratch_bytes(int T, int E);
@@ -81,6 +92,7 @@ struct DecodeLayer {
   const uint8_t* shared_gate_up;
   const uint8_t* shared_down;
   const float* router_packed;  // [H][kRouterStride] or null
+  const void* router_split;    // bf16 [3][E][H] (router as three bf16 terms) or null
 };
 constexpr int kRouterStride = 264;
 cudaError_t pack_router(const float* router_w, const float* shared_gate, int E, int H, float* out, cudaStream_t st);

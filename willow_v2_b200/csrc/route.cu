@@ -141,11 +141,14 @@ cudaError_t router_logits(const void* x, int x_dtype, int T, int H, int E, const
 }
 
 // One warp per token: k rounds of warp arg-max (larger value first, then the smaller expert id).
+// splits == 0: logits [T][E + 1], column E the shared-expert gate logit. splits > 0: `splits` partial sums
+// [splits][T][E] added in order, and the shared-expert gate logit is x[t] . g computed here.
 template <int PER_LANE>
-__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int T, int E, int k,
+__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int splits, int T, int E, int k,
                                                    const float* __restrict__ bias, float* __restrict__ topk_w,
                                                    int32_t* __restrict__ topk_idx, float* __restrict__ shared_s,
-                                                   float* __restrict__ logits_out) {
+                                                   float* __restrict__ logits_out, const void* __restrict__ x,
+                                                   int x_dtype, const float* __restrict__ g, int H) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
@@ -156,7 +159,12 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     const int e = lane + 32 * i;
     float l = -INFINITY;
     if (e < E) {
-      l = row[e];
+      if (splits == 0) {
+        l = row[e];
+      } else {
+        l = logits[size_t(t) * E + e];
+        for (int s = 1; s < splits; ++s) l += logits[(size_t(s) * T + t) * E + e];
+      }
       if (bias) l += bias[e];
       if (logits_out) logits_out[size_t(t) * E + e] = l;
     }
@@ -201,7 +209,25 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     topk_w[size_t(t) * k + lane] = sel_l / sum;
     topk_idx[size_t(t) * k + lane] = sel_e;
   }
-  if (lane == 0 && shared_s) shared_s[t] = 1.0f / (1.0f + expf(-row[E]));
+  if (shared_s) {
+    float sl;
+    if (splits == 0) {
+      sl = row[E];
+    } else {
+      float acc = 0.f;
+      for (int h = lane * 4; h < H; h += 128) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(g + h));
+        const float4 xv = x_dtype == kF32 ? load4<float>(static_cast<const float*>(x) + size_t(t) * H + h)
+                                          : load4<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x) + size_t(t) * H + h);
+        acc = fmaf(w.x, xv.x, acc);
+        acc = fmaf(w.y, xv.y, acc);
+        acc = fmaf(w.z, xv.z, acc);
+        acc = fmaf(w.w, xv.w, acc);
+      }
+      sl = warp_sum(acc);
+    }
+    if (lane == 0) shared_s[t] = 1.0f / (1.0f + expf(-sl));
+  }
 }
 
 // out[h][e] = R[e][h] for e < E, out[h][E] = g[h], zero up to the stride: 32 x 32 tiles through shared memory.
@@ -228,15 +254,24 @@ cudaError_t pack_router(const float* router_w, const float* shared_gate, int E, 
   return cudaGetLastError();
 }
 
-cudaError_t router_topk(const float* logits, int T, int E, int k, const float* bias, float* topk_w,
-                        int32_t* topk_idx, float* shared_s, float* logits_out, cudaStream_t st, int* launches) {
+cudaError_t router_topk_split(const float* logits, int splits, int T, int E, int k, const float* bias, float* topk_w,
+                              int32_t* topk_idx, float* shared_s, float* logits_out, const void* x, int x_dtype,
+                              const float* g, int H, cudaStream_t st, int* launches) {
   const unsigned grid = unsigned((T + 7) / 8);
   if (E <= 256)
-    topk_kernel<8><<<grid, 256, 0, st>>>(logits, T, E, k, bias, topk_w, topk_idx, shared_s, logits_out);
+    topk_kernel<8><<<grid, 256, 0, st>>>(logits, splits, T, E, k, bias, topk_w, topk_idx, shared_s, logits_out, x,
+                                         x_dtype, g, H);
   else
-    topk_kernel<16><<<grid, 256, 0, st>>>(logits, T, E, k, bias, topk_w, topk_idx, shared_s, logits_out);
+    topk_kernel<16><<<grid, 256, 0, st>>>(logits, splits, T, E, k, bias, topk_w, topk_idx, shared_s, logits_out, x,
+                                          x_dtype, g, H);
   ++*launches;
   return cudaGetLastError();
+}
+
+cudaError_t router_topk(const float* logits, int T, int E, int k, const float* bias, float* topk_w,
+                        int32_t* topk_idx, float* shared_s, float* logits_out, cudaStream_t st, int* launches) {
+  return router_topk_split(logits, 0, T, E, k, bias, topk_w, topk_idx, shared_s, logits_out, nullptr, kF32, nullptr,
+                           0, st, launches);
 }
 
 }  // namespace wmoe

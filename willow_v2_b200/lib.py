@@ -30,6 +30,7 @@ SIGNATURES = {
     "wmoe_route": (_i, [_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p]),
     "wmoe_dispatch": (_i, [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p]),
     "wmoe_pack_router": (_i, [_p, _p, _p, _i, _i, _p, _p]),
+    "wmoe_split_router": (_i, [_p, _p, _i, _i, _p, _p]),
     "wmoe_store_create": (_i, [_p, _i, _i, _i, _i, _sz, _pp]),
     "wmoe_store_destroy": (None, [_p]),
     "wmoe_store_upload": (_i, [_p, _i, _i, _p, _p]),
@@ -41,6 +42,7 @@ SIGNATURES = {
     "wmoe_store_stats": (_i, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_u64), ctypes.POINTER(_u64),
                               ctypes.POINTER(_u64)]),
     "wmoe_moe_forward": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _i, _p, _p, _p]),
+    "wmoe_moe_forward_layer": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _i, _p, _p, _p]),
     "wmoe_decode_stack": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
     "wmoe_decode_stack_noalloc": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
     "wmoe_gemv_batch": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
@@ -48,9 +50,10 @@ SIGNATURES = {
 
 
 class LayerWeights(ctypes.Structure):
-    """wmoe_layer_weights: device pointers of one layer's router, bias, shared gate and shared expert."""
+    """wmoe_layer_weights: device pointers of one layer's router, bias, shared gate, shared expert and the two
+    prepared router forms."""
     _fields_ = [("router_w", _p), ("router_bias", _p), ("shared_gate", _p), ("shared_gate_up", _p),
-                ("shared_down", _p), ("router_packed", _p)]
+                ("shared_down", _p), ("router_packed", _p), ("router_split", _p)]
 
 
 ROUTER_STRIDE = 264  # WMOE_ROUTER_STRIDE

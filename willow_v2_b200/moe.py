@@ -210,38 +210,58 @@ def pack_router(router_w: torch.Tensor, shared_gate: torch.Tensor, ctx: Optional
     return out
 
 
+def split_router(router_w: torch.Tensor, ctx: Optional[Context] = None) -> torch.Tensor:
+    """The router [E, H] as three bf16 terms [3, E, H] summing to it (wmoe_split_router): with it, the router
+    logits of bf16 tokens run on the tensor cores at float32 accuracy."""
+    ctx = ctx or default_context()
+    E, H = router_w.shape
+    out = torch.empty(3, E, H, dtype=torch.bfloat16, device=router_w.device)
+    check(ctx.handle, lib.wmoe_split_router(ctx.handle, _ptr(router_w.contiguous()), E, H, _ptr(out), _stream()))
+    return out
+
+
 @dataclass
 class LayerWeights:
     """One layer's non-routed MoE weights on the GPU: router f32 [E, H], optional routing bias f32 [E], shared
-    expert gate vector f32 [H], shared expert gate_up (Q4_K bytes, uint8) and down (Q6_K bytes, uint8), and the
-    packed router (made on first use by decode_stack)."""
+    expert gate vector f32 [H], shared expert gate_up (Q4_K bytes, uint8) and down (Q6_K bytes, uint8), and two
+    prepared forms of the router made once by prepare(): packed (decode) and split into bf16 terms (prefill)."""
     router_w: torch.Tensor
     shared_gate: torch.Tensor
     shared_gate_up: torch.Tensor
     shared_down: torch.Tensor
     router_bias: Optional[torch.Tensor] = None
     router_packed: Optional[torch.Tensor] = None
+    router_split: Optional[torch.Tensor] = None
+
+    def prepare(self, ctx: Optional[Context] = None, decode: bool = True, prefill: bool = True) -> "LayerWeights":
+        if decode and self.router_packed is None:
+            self.router_packed = pack_router(self.router_w, self.shared_gate, ctx)
+        if prefill and self.router_split is None:
+            self.router_split = split_router(self.router_w, ctx)
+        return self
 
     def as_struct(self) -> _lib.LayerWeights:
         opt = lambda t: None if t is None else t.data_ptr()
         return _lib.LayerWeights(self.router_w.data_ptr(), opt(self.router_bias), self.shared_gate.data_ptr(),
-                                 self.shared_gate_up.data_ptr(), self.shared_down.data_ptr(), opt(self.router_packed))
+                                 self.shared_gate_up.data_ptr(), self.shared_down.data_ptr(), opt(self.router_packed),
+                                 opt(self.router_split))
 
 
 def moe_forward(store: ExpertStore, layer: int, x: torch.Tensor, lw: LayerWeights, top_k: int = 8,
                 out_dtype: Optional[torch.dtype] = None, return_routing: bool = False):
-    """One MoE block (engines/base.py:445-490) on x [T, H] (f32 or bf16) -> out [T, H] (x's dtype by default);
-    with return_routing also (weights f32 [T, k], selected int32 [T, k])."""
+    """One MoE block (engines/base.py:445-491) on x [T, H] (f32 or bf16) -> out [T, H] (x's dtype by default);
+    with return_routing also (weights f32 [T, k], selected int32 [T, k]). Uses the prepared router forms that lw
+    holds (LayerWeights.prepare)."""
     ctx = store.ctx
     x = x.contiguous()
     T = x.shape[0]
     out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
     sel = torch.empty(T, top_k, dtype=torch.int32, device=x.device) if return_routing else None
     w = torch.empty(T, top_k, dtype=torch.float32, device=x.device) if return_routing else None
-    check(ctx.handle, lib.wmoe_moe_forward(ctx.handle, store.handle, layer, _ptr(x), _DTYPES[x.dtype], T, top_k,
-                                           _ptr(lw.router_w), _ptr(lw.router_bias), _ptr(lw.shared_gate),
-                                           _ptr(lw.shared_gate_up), _ptr(lw.shared_down), _ptr(out),
-                                           _DTYPES[out.dtype], _ptr(sel), _ptr(w), _stream()))
+    weights = lw.as_struct()
+    check(ctx.handle, lib.wmoe_moe_forward_layer(ctx.handle, store.handle, layer, _ptr(x), _DTYPES[x.dtype], T,
+                                                 top_k, ctypes.byref(weights), _ptr(out), _DTYPES[out.dtype],
+                                                 _ptr(sel), _ptr(w), _stream()))
     return (out, w, sel) if return_routing else out
 
 
@@ -279,13 +299,20 @@ class CudaMoE:
 
     top_k = 8
 
+    def moe_layer_weights(self, layer: int) -> LayerWeights:
+        """The layer's weights with their prepared router forms, made on first use and kept."""
+        cache = self.__dict__.setdefault("_wmoe_layers", {})
+        if layer not in cache:
+            p = f"{self.prefix}layers.{layer}.mlp"
+            cache[layer] = LayerWeights(router_w=self.w(p + ".gate.weight"),
+                                        shared_gate=self.w(p + ".shared_expert_gate.weight").reshape(-1),
+                                        shared_gate_up=self.w(p + ".shared_expert.gate_up_proj.qweight"),
+                                        shared_down=self.w(p + ".shared_expert.down_proj.qweight"),
+                                        router_bias=self.weights.get(p + ".gate.bias")).prepare(self.experts.ctx)
+        return cache[layer]
+
     def moe(self, x: torch.Tensor, layer: int, residual: torch.Tensor = None) -> torch.Tensor:
-        p = f"{self.prefix}layers.{layer}.mlp"
-        lw = LayerWeights(router_w=self.w(p + ".gate.weight"),
-                          shared_gate=self.w(p + ".shared_expert_gate.weight").reshape(-1),
-                          shared_gate_up=self.w(p + ".shared_expert.gate_up_proj.qweight"),
-                          shared_down=self.w(p + ".shared_expert.down_proj.qweight"),
-                          router_bias=self.weights.get(p + ".gate.bias"))
+        lw = self.moe_layer_weights(layer)
         shape = x.shape
         out = moe_forward(self.experts, layer, x.reshape(-1, shape[-1]), lw, self.top_k)
         return out.view(shape)
