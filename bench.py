@@ -9,6 +9,10 @@ At N > 1 GPUs (torchrun) every rank serves its own token stream with its own ful
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode40|prefill4096]
 
+--workload prefill4096: one MoE layer on 4096 bf16 tokens with uniform routing (~128
+tokens per expert) through the tcgen05 grouped GEMMs; tokens/s, with the dominant GEMM launch against the measured
+bf16 tensor peak. At N > 1 every rank runs its own batches (replicas).
+
 --impl reference times the CPU restatement of willow's own CPU path (the oracle port; willow's code cannot run
 on the GPU box) on the host cores, on a bounded sample of the same workload.
 """
@@ -31,9 +35,17 @@ ROUTER_BYTES = EXPERTS * HIDDEN * 4 + HIDDEN * 4                           # rou
 # DRAM bytes (read + write) per layer of decode_kernel, measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on a 4-layer launch: 82,234,880 + 1,487,360 bytes; traffic grows with the layers
 TRAFFIC_PER_LAYER = (82_234_880 + 1_487_360) / 4
+# DRAM bytes (read + write) of one grouped_gemm_kernel<0> launch at 4096 tokens, measured by ncu; None until captured
+PREFILL_GATE_UP_TRAFFIC = None
 LAYERS = 40
 SEED = 0
 METRIC = "MoE decode tokens/s (40-layer qwen35moe stack, 1 token per step)"
+PREFILL_T = 4096
+METRIC_PREFILL = "MoE prefill tokens/s (one qwen35moe MoE layer, 4096 bf16 tokens per step)"
+# useful expert-product FLOPs of one prefill layer: every token through 8 routed experts + the shared expert,
+# gate_up [2F x H] then down [H x F]
+GATE_UP_FLOPS = 2 * PREFILL_T * (TOP_K + 1) * (2 * FFN) * HIDDEN   # 154.6 GFLOP
+DOWN_FLOPS = 2 * PREFILL_T * (TOP_K + 1) * HIDDEN * FFN             # 77.3 GFLOP
 
 
 def peaks():
@@ -192,6 +204,136 @@ def run_decode40(args, rank: int, world: int, dist):
     return result, (ctx, store, layers)
 
 
+def run_prefill4096(args, rank: int, world: int, dist):
+    import torch
+    from willow_v2_b200 import lib as L
+    from willow_v2_b200 import moe, synth
+    device = torch.cuda.current_device()
+    ctx, store, layers = setup_model(device, 1)
+    lw = layers[0].prepare(ctx, decode=False)
+    K, W = args.steps, args.warmup
+    T = PREFILL_T
+    # 4 different batches of 4096 tokens cycled (each step re-routes); inputs resident before the timed region
+    xs = [torch.from_numpy(synth.hidden(SEED + 1000 * rank, T, step=b)).to(torch.bfloat16).cuda() for b in range(4)]
+    out = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(x, o):
+        weights = lw.as_struct()
+        L.check(ctx.handle, L.lib.wmoe_moe_forward_layer(ctx.handle, store.handle, 0, x.data_ptr(), L.BF16, T, TOP_K,
+                                                         L.ctypes.byref(weights), o.data_ptr(), L.BF16, None, None,
+                                                         stream.cuda_stream))
+
+    for s in range(W):
+        step(xs[s % 4], out)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    L.check(ctx.handle, L.lib.wmoe_set_profiling(ctx.handle, K))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        ev0.record(stream)
+        for s in range(K):
+            step(xs[s % 4], out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    gpu_launches = ctx.launches - launches0
+    ms = ev0.elapsed_time(ev1) / K
+    phase = {name: [] for name in L.PHASES}
+    for ago in range(K):
+        for p, name in enumerate(L.PHASES):
+            v = L.ctypes.c_float()
+            L.check(ctx.handle, L.lib.wmoe_phase_ms(ctx.handle, ago, p, L.ctypes.byref(v)))
+            phase[name].append(v.value)
+    L.check(ctx.handle, L.lib.wmoe_set_profiling(ctx.handle, 0))
+    phase_ms = {name: statistics.mean(v) for name, v in phase.items()}
+    ctx.check_device()
+
+    # end to end through the public API: pinned bf16 host batch -> device, layer, result -> pinned host, every step
+    x_host = [x.cpu().pin_memory() for x in xs]
+    o_host = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device="cuda")
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(K):
+        x_dev.copy_(x_host[s % 4], non_blocking=True)
+        step(x_dev, out)
+        o_host.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    if dist:
+        dist.barrier()
+
+    times = torch.tensor([ms, e2e_ms, phase_ms["gate_up"], phase_ms["down"]], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, gu_ms, dn_ms = times.tolist()
+    _, bf16, peak_kind = peaks()
+    gu_tflops = GATE_UP_FLOPS / (gu_ms * 1e-3) / 1e12
+    dn_tflops = DOWN_FLOPS / (dn_ms * 1e-3) / 1e12
+    layer_tflops = (GATE_UP_FLOPS + DOWN_FLOPS) / (ms * 1e-3) / 1e12
+    result = {
+        "metric": METRIC_PREFILL, "value": world * T * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 accumulation",
+        "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks with the config-0 distributions; bf16 N(0,1) tokens)",
+        "config": {"workload": "configs[3]: prefill 4096 tokens through one MoE layer, uniform routing",
+                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: 524 MB of expert weights and ~500 MB of activations per step"},
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel<0> (gate_up + SwiGLU)",
+                     "achieved": gu_tflops, "peak": bf16, "unit": "TFLOP/s", "frac": gu_tflops / bf16,
+                     "traffic": PREFILL_GATE_UP_TRAFFIC, "peak_kind": peak_kind,
+                     "algorithmic_flops_per_launch": GATE_UP_FLOPS, "launch_ms": gu_ms},
+        "roofline_down": {"kernel": "grouped_gemm_kernel<1> (down)", "achieved": dn_tflops, "frac": dn_tflops / bf16,
+                          "algorithmic_flops_per_launch": DOWN_FLOPS, "launch_ms": dn_ms},
+        "layer_tensor_frac": layer_tflops / bf16,
+        "phase_ms": phase_ms,
+        "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 2,
+                "d2h_bytes_per_step": T * HIDDEN * 2},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks.summary(),
+    }
+    return result, (ctx, store, layers)
+
+
+def cpu_baseline_prefill(sample_experts: int = 128, tokens_per_expert: int = 144):
+    """willow's CPU path restated (the oracle port) for the prefill layer, timed on the host cores: the router on
+    all 4096 tokens, and for a sample of experts the dequantisation of their GGUF bytes plus their FFN on 128
+    tokens each, scaled to the 257 experts (256 routed + shared) and 36,864 (token, expert) rows of the layer."""
+    import oracle.moe_oracle as ora
+    from willow_v2_b200 import synth
+    x = synth.hidden(SEED, PREFILL_T, step=321)
+    router = synth.router_weight(SEED, 0)
+    t0 = time.perf_counter()
+    ora.route(x @ router.T)
+    t_route = time.perf_counter() - t0
+    t_deq = t_ffn = 0.0
+    for e in range(sample_experts):
+        gu, dn = synth.expert_gate_up(SEED, 0, e), synth.expert_down(SEED, 0, e)
+        t0 = time.perf_counter()
+        wg = ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN))
+        wd = ora.dequantize(dn, "Q6_K", (HIDDEN, FFN))
+        t1 = time.perf_counter()
+        xe = x[e * tokens_per_expert:(e + 1) * tokens_per_expert]
+        ora.expert_gate(xe @ wg.T) @ wd.T
+        t_ffn += time.perf_counter() - t1
+        t_deq += t1 - t0
+    rows = PREFILL_T * (TOP_K + 1)
+    sec = t_route + t_deq / sample_experts * (EXPERTS + 1) + t_ffn / (sample_experts * tokens_per_expert) * rows
+    return {"value": PREFILL_T / sec, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"router on all {PREFILL_T} tokens; {sample_experts} experts dequantised from GGUF bytes with "
+                      f"their FFN on {tokens_per_expert} tokens each (numpy float32); scaled to 257 experts and "
+                      f"{rows} token-expert rows"}
+
+
 def cpu_baseline(sample_layers: int = 2):
     """willow's CPU path restated (the oracle port) timed on the host cores: dequantise the token's routed and
     shared experts from their GGUF bytes and run route / expert FFN / combine in float32, one layer at a time.
@@ -226,6 +368,20 @@ def run_reference(args, rank, world):
     """The reference arm: the CPU restatement of willow's CPU path on the host cores, rank 0 only."""
     if rank != 0:
         return None
+    if args.workload == "prefill4096":
+        K, W = args.steps, args.warmup
+        vals = [cpu_baseline_prefill(sample_experts=8)["value"] for _ in range(W + K)][W:]
+        value = statistics.mean(vals)
+        base = cpu_baseline_prefill(sample_experts=8)
+        return {"metric": METRIC_PREFILL, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": PREFILL_T / value * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": "configs[3]: prefill 4096 tokens through one MoE layer, uniform routing",
+                           "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
+                           "tokens_per_step": PREFILL_T},
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                 "sample": "each step: " + base["sample"]},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     import oracle.moe_oracle as ora
     from willow_v2_b200 import synth
     K, W = args.steps, args.warmup
@@ -268,7 +424,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode40", choices=["decode40"])
+    ap.add_argument("--workload", default="decode40", choices=["decode40", "prefill4096"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="stack depth (40 = the benchmark; fewer = profiling)")
     args = ap.parse_args()
@@ -291,9 +447,14 @@ def main():
         d.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                              device_id=torch.device("cuda", local))
         dist = d
-    result, _keep = run_decode40(args, rank, world, dist)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline()
+    if args.workload == "prefill4096":
+        result, _keep = run_prefill4096(args, rank, world, dist)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_prefill()
+    else:
+        result, _keep = run_decode40(args, rank, world, dist)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(result), flush=True)
     if dist:

@@ -126,6 +126,17 @@ const uint8_t* wmoe_store_blob(const wmoe_store* store, int layer, int expert);
 int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, uint64_t* bytes_in,
                      uint64_t* evictions);
 
+/* Per-phase device time of the multi-token MoE block, by CUDA events (opt-in, for benchmarks and profiling; no
+ * counterpart in willow, whose engine times phases on the host with Engine.tick, engines/base.py:445-491). After
+ * wmoe_set_profiling(ctx, calls), every wmoe_moe_forward(_layer) call with more than one token records its phase
+ * boundaries on its own stream into slot (call number % calls); calls = 0 turns it off and frees the events.
+ * wmoe_phase_ms gives phase `phase` of the call `ago` calls back (0 = the latest): 0 router + top-k, 1 dispatch,
+ * 2 gather (GEMM path) or activation quantisation (GEMV path), 3 gate_up, 4 down, 5 combine. It waits for that
+ * call's events. */
+#define WMOE_PHASES 6
+int wmoe_set_profiling(wmoe_ctx* ctx, int calls);
+int wmoe_phase_ms(wmoe_ctx* ctx, int ago, int phase, float* ms);
+
 /* ---- the MoE block ---------------------------------------------------------------------------------- */
 
 /* One MoE block on T tokens: out = sum over each token's top_k experts (ascending expert id) of

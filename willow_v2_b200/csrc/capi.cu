@@ -88,10 +88,13 @@ int wmoe_init(int device, wmoe_ctx** out) {
   return WMOE_OK;
 }
 
+static void free_profiling(wmoe_ctx* ctx);
+
 void wmoe_destroy(wmoe_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  free_profiling(ctx);
   cudaFree(ctx->scratch);
   cudaFree(ctx->d_status);
   delete ctx;
@@ -109,6 +112,45 @@ int wmoe_set_trace(wmoe_ctx* ctx, uint64_t* trace, size_t entries) {
 }
 
 int wmoe_decode_ctas(const wmoe_ctx* ctx) { return ctx ? ctx->decode_ctas : 0; }
+
+static void free_profiling(wmoe_ctx* ctx) {
+  for (cudaEvent_t e : ctx->prof_events) cudaEventDestroy(e);
+  ctx->prof_events.clear();
+  ctx->profile_calls = 0;
+  ctx->profile_seq = 0;
+}
+
+int wmoe_set_profiling(wmoe_ctx* ctx, int calls) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (calls < 0 || calls > 100000) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_set_profiling: bad call count");
+  cudaSetDevice(ctx->device);
+  free_profiling(ctx);
+  if (calls == 0) return WMOE_OK;
+  ctx->prof_events.resize(size_t(calls) * wmoe_ctx::kProfMarks, nullptr);
+  for (cudaEvent_t& e : ctx->prof_events) {
+    const cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) {
+      e = nullptr;
+      free_profiling(ctx);
+      return cuda_fail(ctx, err, "wmoe_set_profiling");
+    }
+  }
+  ctx->profile_calls = calls;
+  return WMOE_OK;
+}
+
+int wmoe_phase_ms(wmoe_ctx* ctx, int ago, int phase, float* ms) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!ms || phase < 0 || phase >= WMOE_PHASES || ctx->profile_calls == 0 || ago < 0 ||
+      uint64_t(ago) >= ctx->profile_seq || ago >= ctx->profile_calls)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_phase_ms: no such recorded call or phase");
+  const size_t slot = size_t((ctx->profile_seq - 1 - uint64_t(ago)) % uint64_t(ctx->profile_calls));
+  cudaEvent_t* ev = &ctx->prof_events[slot * wmoe_ctx::kProfMarks];
+  cudaError_t e = cudaEventSynchronize(ev[phase + 1]);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(ms, ev[phase], ev[phase + 1]);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_phase_ms");
+  return WMOE_OK;
+}
 
 int wmoe_set_prefill_threshold(wmoe_ctx* ctx, int tokens) {
   if (!ctx || tokens < 1) return WMOE_ERR_INVALID;
@@ -350,6 +392,15 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
 
   int n = 0;
+  // opt-in phase marks (wmoe_set_profiling): 0 start, 1 routed, 2 dispatched, 3-6 inside the expert products
+  cudaEvent_t* marks = ctx->profile_calls > 0
+                           ? &ctx->prof_events[size_t(ctx->profile_seq % uint64_t(ctx->profile_calls)) *
+                                               wmoe_ctx::kProfMarks]
+                           : nullptr;
+  auto mark = [&](int i) {
+    if (marks) cudaEventRecord(marks[i], st);
+  };
+  mark(0);
   float* topk_w = at<float>(ctx, o_w);
   int32_t* topk_idx = at<int32_t>(ctx, o_idx);
   float* shared_s = at<float>(ctx, o_s);
@@ -370,6 +421,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
                                 st, &n),
                     "top-k");
   }
+  mark(1);
   std::vector<int32_t> experts_used;
   if (store->capped) {
     // the store must copy this call's experts in first: one wait for the routing (engines/base.py:456-460 does
@@ -398,27 +450,34 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
                            at<int32_t>(ctx, o_used), at<int32_t>(ctx, o_seg), at<int32_t>(ctx, o_nused), nullptr,
                            ctx->d_status, st, &n),
                   "dispatch");
+  mark(2);
   const ExpertSource src = store_source(store, shared_gate_up, shared_down);
   if (gemm_path) {
     WMOE_CHECK_CUDA(ctx,
                     prefill_experts(src, layer, pm, H, F, x, x_dtype, topk_w, shared_s, out, out_dtype,
-                                    at<void>(ctx, o_region), ctx->sm_count, ctx->d_status, st, &n),
+                                    at<void>(ctx, o_region), ctx->sm_count, ctx->d_status, marks ? marks + 3 : nullptr,
+                                    st, &n),
                     "grouped GEMM");
   } else {
     int16_t* xq = at<int16_t>(ctx, o_xq);
     float* xs = at<float>(ctx, o_xs);
     int32_t* xsum = at<int32_t>(ctx, o_xsum);
     WMOE_CHECK_CUDA(ctx, quant_rows(x, x_dtype, T, H, xq, xs, xsum, st, &n), "activation quantisation");
+    mark(3);
     float* h = at<float>(ctx, o_h);
     WMOE_CHECK_CUDA(ctx, gate_up_gemv(src, layer, pm, H, F, xq, xs, xsum, h, ctx->d_status, st, &n), "gate_up");
     int16_t* hq = at<int16_t>(ctx, o_hq);
     float* hs = at<float>(ctx, o_hs);
     int32_t* hsum = at<int32_t>(ctx, o_hsum);
     WMOE_CHECK_CUDA(ctx, quant_rows(h, WMOE_F32, P, F, hq, hs, hsum, st, &n), "hidden quantisation");
+    mark(4);
     float* y = at<float>(ctx, o_y);
     WMOE_CHECK_CUDA(ctx, down_gemv(src, layer, pm, H, F, hq, hs, hsum, y, ctx->d_status, st, &n), "down");
+    mark(5);
     WMOE_CHECK_CUDA(ctx, combine(pm, H, topk_w, shared_s, y, nullptr, out, out_dtype, st, &n), "combine");
+    mark(6);
   }
+  if (marks) ++ctx->profile_seq;
   if (topk_idx_out)
     WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_idx_out, topk_idx, size_t(T) * k * sizeof(int32_t),
                                          cudaMemcpyDeviceToDevice, st),

@@ -613,7 +613,8 @@ size_t prefill_scratch_bytes(int T, int k, int E, int H, int F) {
 
 cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const void* x,
                             int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
-                            void* scratch, int num_sms, int* status, cudaStream_t st, int* launches) {
+                            void* scratch, int num_sms, int* status, const cudaEvent_t* marks, cudaStream_t st,
+                            int* launches) {
   if (H % QK || F != 2 * QK || H % kBM || pm.E + 1 > 512 || pm.k != 8 || num_sms <= 0) return cudaErrorInvalidValue;
   // activations are read and written 16 bytes at a time
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16) return cudaErrorInvalidValue;
@@ -640,6 +641,7 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
   else
     gather_fp16_kernel<__nv_bfloat16><<<unsigned(P), 256, 0, st>>>(pm, static_cast<const __nv_bfloat16*>(x), H, xg);
   *launches += 2;
+  if (marks) cudaEventRecord(marks[0], st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   static bool attr_set = false;  // per process: the kernels' shared memory limit does not change
@@ -674,10 +676,13 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
   gp.n_mtiles = F / 64;
   gp.out = hbuf;
   grouped_gemm_kernel<0><<<unsigned(num_sms), kThreads, Layout<0>::bytes, st>>>(map_x, map_w, map_ws, gp);
+  if (marks) cudaEventRecord(marks[1], st);
   gp.n_mtiles = H / kBM;
   gp.out = ybuf;
   grouped_gemm_kernel<1><<<unsigned(num_sms), kThreads, Layout<1>::bytes, st>>>(map_h, map_w, map_ws, gp);
+  if (marks) cudaEventRecord(marks[2], st);
   combine_f16_kernel<8><<<unsigned(pm.T), 256, 0, st>>>(pm, H, topk_w, shared_s, ybuf, out, out_dtype);
+  if (marks) cudaEventRecord(marks[3], st);
   *launches += 3;
   return cudaGetLastError();
 }

@@ -82,7 +82,8 @@ cudaError_t gemv_batch(int type, const uint8_t* const* weights, int n, int rows,
 size_t prefill_scratch_bytes(int T, int k, int E, int H, int F);
 cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const void* x,
                             int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
-                            void* scratch, int num_sms, int* status, cudaStream_t st, int* launches);
+                            void* scratch, int num_sms, int* status, const cudaEvent_t* marks, cudaStream_t st,
+                            int* launches);  // marks: 4 events recorded after gather, gate_up, down, combine (or null)
 
 // decode.cu: persistent one-token decode (one layer or a stack)
 struct DecodeLayer {

@@ -24,6 +24,11 @@ struct wmoe_ctx {
   int prefill_threshold = 256;  // token count from which wmoe_moe_forward uses the tcgen05 grouped GEMMs
   uint64_t* trace = nullptr;  // decode phase timestamps (device), or null
   size_t trace_entries = 0;
+  // per-phase CUDA events of the last profile_calls multi-token MoE calls (opt-in): [profile_calls][kProfMarks]
+  static constexpr int kProfMarks = 7;
+  std::vector<cudaEvent_t> prof_events;
+  int profile_calls = 0;
+  uint64_t profile_seq = 0;  // calls recorded so far
 };
 
 struct wmoe_store {

@@ -24,6 +24,8 @@ SIGNATURES = {
     "wmoe_set_decode_kernel": (_i, [_p, _i]),
     "wmoe_set_trace": (_i, [_p, _p, _sz]),
     "wmoe_set_prefill_threshold": (_i, [_p, _i]),
+    "wmoe_set_profiling": (_i, [_p, _i]),
+    "wmoe_phase_ms": (_i, [_p, _i, _i, ctypes.POINTER(_f)]),
     "wmoe_decode_ctas": (_i, [_p]),
     "wmoe_device_status": (_i, [_p, ctypes.POINTER(_i), _p]),
     "wmoe_dequant": (_i, [_p, _i, _p, _sz, _p, _i, _p]),
@@ -57,6 +59,7 @@ class LayerWeights(ctypes.Structure):
 
 
 ROUTER_STRIDE = 264  # WMOE_ROUTER_STRIDE
+PHASES = ("router", "dispatch", "gather", "gate_up", "down", "combine")  # WMOE_PHASES, in order
 
 
 def _load():
