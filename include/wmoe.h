@@ -108,6 +108,11 @@ int wmoe_dispatch(wmoe_ctx* ctx, const int32_t* topk_idx, int T, int top_k, int 
  * gate_up is Q4_K [2*ffn, hidden]; down is Q6_K [hidden, ffn]. */
 int wmoe_store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, size_t cap_bytes,
                       wmoe_store** out);
+/* A store holding only experts [expert_begin, expert_end) of each layer (the block one rank owns under expert
+ * parallelism); the others are never resident and are refused by upload / prepare / download. cap_bytes as above,
+ * over the held blobs only (so is the pinned host copy). wmoe_store_create is the range [0, experts). */
+int wmoe_store_create_range(wmoe_ctx* ctx, int layers, int experts, int expert_begin, int expert_end, int hidden,
+                            int ffn, size_t cap_bytes, wmoe_store** out);
 void wmoe_store_destroy(wmoe_store* store);
 /* Copies one blob (gate_up then down, size wmoe_store_blob_bytes) from host memory into the store. */
 int wmoe_store_upload(wmoe_store* store, int layer, int expert, const void* host_src, void* stream);
@@ -183,6 +188,39 @@ int wmoe_split_router(wmoe_ctx* ctx, const float* router_w, int experts, int hid
 int wmoe_moe_forward_layer(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
                            const wmoe_layer_weights* weights, void* out, int out_dtype, int32_t* topk_idx_out,
                            float* topk_w_out, void* stream);
+
+/* ---- expert parallelism --------------------------------------------------------------
+ * willow runs on one device and has no counterpart; these replace its single-device MoE block
+ * (engines/base.py:445-491) when `world` ranks share the experts. Rank r owns experts
+ * [r * experts / world, (r + 1) * experts / world) of every layer, in a store from wmoe_store_create_range, and
+ * routes its own T tokens. One layer on every rank:
+ *   1. wmoe_ep_route_plan: route, then for each rank d the tokens with a pick on d (send_rows[d] rows, each token
+ *      once) and those picks (send_pairs[d] pairs, (row within d's block, expert id) int32 pairs).
+ *   2. all-to-all of the counts, then of the rows (fp16 [rows][hidden], send_buf) and pair lists, blocks in rank order.
+ *   3. wmoe_ep_experts on what arrived: y rows 0 .. P_r - 1 (one fp16 row per received pair, in arrival order) and
+ *      y rows P_r .. P_r + T - 1 (the shared expert on this rank's own tokens).
+ *   4. all-to-all of y rows 0 .. P_r - 1 back to their senders (send_pairs[d] rows from rank d, in rank order).
+ *   5. wmoe_ep_combine: out[t] = sum of the token's picks in ascending expert id + the shared expert, the same
+ *      arithmetic in the same order as wmoe_moe_forward, so the output does not depend on `world`.
+ * The transfers are the caller's (willow_v2_b200.moe.moe_forward_ep uses torch.distributed over NCCL). Rows are fp16
+ * in the library's internal layout (elements permuted within runs of 8; results scaled by 1/32). */
+#define WMOE_MAX_RANKS 8
+int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int T, int top_k, int experts,
+                       int hidden, const wmoe_layer_weights* weights, float* topk_w /* [T, top_k] */,
+                       int32_t* topk_idx /* [T, top_k] */, float* shared_s /* [T] */,
+                       int32_t* send_rows /* [world] */, int32_t* send_pairs /* [world] */,
+                       int32_t* send_tok /* [T * min(top_k, world)] */, int32_t* pair_list /* [T * top_k, 2] */,
+                       int32_t* ret_index /* [T, top_k] */, uint16_t* send_buf /* fp16 [T * min(top_k, world), hidden] */,
+                       void* stream);
+/* recv_rows / recv_pairs: HOST arrays [world] (what each rank sent here); recv_buf fp16 [sum recv_rows, hidden];
+ * recv_pair_list [sum recv_pairs, 2]; x [T, hidden] this rank's own tokens; y fp16 [sum recv_pairs + T, hidden]. */
+int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, const int32_t* recv_rows,
+                    const int32_t* recv_pairs, const uint16_t* recv_buf, const int32_t* recv_pair_list,
+                    const void* x, int x_dtype, int T, const wmoe_layer_weights* weights, uint16_t* y, void* stream);
+/* y_returned fp16 [sum send_pairs, hidden] (blocks in rank order); y_shared fp16 [T, hidden] (rows P_r.. of y). */
+int wmoe_ep_combine(wmoe_ctx* ctx, int T, int top_k, int hidden, const int32_t* topk_idx, const float* topk_w,
+                    const int32_t* ret_index, const float* shared_s, const uint16_t* y_returned,
+                    const uint16_t* y_shared, void* out, int out_dtype, void* stream);
 
 /* One decode token through layers [layer_begin, layer_begin + n_layers) of the store:
  * h <- h + moe_l(rms_norm(h)) per layer (eps, unit weight), in one persistent launch per 64 layers.

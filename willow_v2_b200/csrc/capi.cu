@@ -263,10 +263,17 @@ int wmoe_dispatch(wmoe_ctx* ctx, const int32_t* topk_idx, int T, int top_k, int 
 
 int wmoe_store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, size_t cap_bytes,
                       wmoe_store** out) {
-  if (!ctx || !out || layers <= 0 || experts <= 0 || hidden <= 0 || ffn <= 0 || hidden % 256 || ffn % 256)
+  return wmoe_store_create_range(ctx, layers, experts, 0, experts, hidden, ffn, cap_bytes, out);
+}
+
+int wmoe_store_create_range(wmoe_ctx* ctx, int layers, int experts, int expert_begin, int expert_end, int hidden,
+                            int ffn, size_t cap_bytes, wmoe_store** out) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!out || layers <= 0 || experts <= 0 || hidden <= 0 || ffn <= 0 || hidden % 256 || ffn % 256 ||
+      expert_begin < 0 || expert_end > experts || expert_begin >= expert_end)
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_create: bad arguments");
   *out = nullptr;
-  return store_create(ctx, layers, experts, hidden, ffn, cap_bytes, out);
+  return store_create(ctx, layers, experts, expert_begin, expert_end, hidden, ffn, cap_bytes, out);
 }
 
 void wmoe_store_destroy(wmoe_store* store) { store_destroy(store); }
@@ -296,6 +303,7 @@ int wmoe_store_download(wmoe_store* store, int layer, int expert, void* host_dst
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t key = size_t(layer) * store->experts + expert;
   const int slot = store->slot_of[key];
+  if (!store->owns(expert)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_download: expert outside the store's range");
   if (slot >= 0) {
     WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(host_dst, store->d_slab + size_t(slot) * store->slot_stride,
                                          store->blob_bytes, cudaMemcpyDeviceToHost, st),
@@ -303,7 +311,7 @@ int wmoe_store_download(wmoe_store* store, int layer, int expert, void* host_dst
     WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "wmoe_store_download");
   } else if (store->h_master) {
     WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "wmoe_store_download");
-    memcpy(host_dst, store->h_master + key * store->blob_bytes, store->blob_bytes);
+    memcpy(host_dst, store->h_master + store->blob_index(layer, expert) * store->blob_bytes, store->blob_bytes);
   } else {
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_download: blob not present");
   }
@@ -324,6 +332,28 @@ int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, 
   if (bytes_in) *bytes_in = store->bytes_in;
   if (evictions) *evictions = store->evictions;
   return WMOE_OK;
+}
+
+// Router + top-k + shared gate of T tokens into caller buffers: for bf16 tokens with the split router, logits on the
+// tensor cores (partial sums of a K split); otherwise float32 on the CUDA cores. logits: router_logit_floats().
+static bool use_router_tc(const void* router_split, int x_dtype, int T, int H, int E) {
+  return router_split && x_dtype == WMOE_BF16 && T >= 16 && router_tc_supported(T, H, E);
+}
+static size_t router_logit_floats(bool tc, int T, int E) {
+  return tc ? size_t(kRouterKSplit) * T * E : size_t(T) * (E + 1);
+}
+static cudaError_t route_tokens(bool tc, const void* x, int x_dtype, int T, int H, int E, int k, const float* router_w,
+                                const float* router_bias, const float* shared_gate, const void* router_split,
+                                float* logits, float* topk_w, int32_t* topk_idx, float* shared_s, int* status,
+                                cudaStream_t st, int* n) {
+  cudaError_t e;
+  if (tc) {
+    if ((e = router_logits_tc(x, T, H, E, router_split, logits, status, st, n)) != cudaSuccess) return e;
+    return router_topk_split(logits, kRouterKSplit, T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr, x,
+                             x_dtype, shared_gate, H, st, n);
+  }
+  if ((e = router_logits(x, x_dtype, T, H, E, router_w, shared_gate, logits, st, n)) != cudaSuccess) return e;
+  return router_topk(logits, T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr, st, n);
 }
 
 static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T,
@@ -362,9 +392,8 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   Plan plan;
   // router logits on the tensor cores for bf16 tokens when the split router is given (partial sums of a K split),
   // else float32 on the CUDA cores ([T][E + 1] with the shared gate as column E)
-  const bool router_tc = router_split && x_dtype == WMOE_BF16 && T >= 16 && router_tc_supported(T, H, E);
-  const size_t o_logits =
-      plan.take<float>(router_tc ? size_t(kRouterKSplit) * T * E : size_t(T) * (E + 1));
+  const bool router_tc = use_router_tc(router_split, x_dtype, T, H, E);
+  const size_t o_logits = plan.take<float>(router_logit_floats(router_tc, T, E));
   const size_t o_w = plan.take<float>(size_t(T) * k);
   const size_t o_idx = plan.take<int32_t>(size_t(T) * k);
   const size_t o_s = plan.take<float>(size_t(T));
@@ -404,23 +433,10 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   float* topk_w = at<float>(ctx, o_w);
   int32_t* topk_idx = at<int32_t>(ctx, o_idx);
   float* shared_s = at<float>(ctx, o_s);
-  if (router_tc) {
-    WMOE_CHECK_CUDA(ctx,
-                    router_logits_tc(x, T, H, E, router_split, at<float>(ctx, o_logits), ctx->d_status, st, &n),
-                    "router");
-    WMOE_CHECK_CUDA(ctx,
-                    router_topk_split(at<float>(ctx, o_logits), kRouterKSplit, T, E, k, router_bias, topk_w, topk_idx,
-                                      shared_s, nullptr, x, x_dtype, shared_gate, H, st, &n),
-                    "top-k");
-  } else {
-    WMOE_CHECK_CUDA(ctx,
-                    router_logits(x, x_dtype, T, H, E, router_w, shared_gate, at<float>(ctx, o_logits), st, &n),
-                    "router");
-    WMOE_CHECK_CUDA(ctx,
-                    router_topk(at<float>(ctx, o_logits), T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr,
-                                st, &n),
-                    "top-k");
-  }
+  WMOE_CHECK_CUDA(ctx,
+                  route_tokens(router_tc, x, x_dtype, T, H, E, k, router_w, router_bias, shared_gate, router_split,
+                               at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status, st, &n),
+                  "router");
   mark(1);
   std::vector<int32_t> experts_used;
   if (store->capped) {
@@ -454,7 +470,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   const ExpertSource src = store_source(store, shared_gate_up, shared_down);
   if (gemm_path) {
     WMOE_CHECK_CUDA(ctx,
-                    prefill_experts(src, layer, pm, H, F, x, x_dtype, topk_w, shared_s, out, out_dtype,
+                    prefill_experts(src, layer, pm, topk_idx, H, F, x, x_dtype, topk_w, shared_s, out, out_dtype,
                                     at<void>(ctx, o_region), ctx->sm_count, ctx->d_status, marks ? marks + 3 : nullptr,
                                     st, &n),
                     "grouped GEMM");
@@ -507,6 +523,154 @@ int wmoe_moe_forward_layer(wmoe_ctx* ctx, wmoe_store* store, int layer, const vo
   return moe_forward_impl(ctx, store, layer, x, x_dtype, T, top_k, w->router_w, w->router_bias, w->shared_gate,
                           w->shared_gate_up, w->shared_down, w->router_packed, w->router_split, out, out_dtype,
                           topk_idx_out, topk_w_out, stream);
+}
+
+static int check_layer(wmoe_ctx* ctx, const wmoe_layer_weights* w, const char* fn) {
+  if (!w || !w->router_w || !w->shared_gate || !w->shared_gate_up || !w->shared_down)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, std::string(fn) + ": null weight pointer");
+  return WMOE_OK;
+}
+
+int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int T, int top_k, int experts,
+                       int hidden, const wmoe_layer_weights* w, float* topk_w, int32_t* topk_idx, float* shared_s,
+                       int32_t* send_rows, int32_t* send_pairs, int32_t* send_tok, int32_t* pair_list,
+                       int32_t* ret_index, uint16_t* send_buf, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (world < 1 || world > kMaxRanks || experts <= 0 || experts % world || T < 0 || top_k != 8 || hidden != 2048 ||
+      (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_route_plan: bad world, shape or dtype");
+  if (int rc = check_layer(ctx, w, "wmoe_ep_route_plan")) return rc;
+  if (!send_rows || !send_pairs || (T > 0 && (!x || !topk_w || !topk_idx || !shared_s || !send_tok || !pair_list ||
+                                              !ret_index || !send_buf)))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_route_plan: null pointer");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    WMOE_CHECK_CUDA(ctx, cudaMemsetAsync(send_rows, 0, world * sizeof(int32_t), st), "wmoe_ep_route_plan");
+    WMOE_CHECK_CUDA(ctx, cudaMemsetAsync(send_pairs, 0, world * sizeof(int32_t), st), "wmoe_ep_route_plan");
+    return WMOE_OK;
+  }
+  const bool tc = use_router_tc(w->router_split, x_dtype, T, hidden, experts);
+  Plan plan;
+  const size_t o_logits = plan.take<float>(router_logit_floats(tc, T, experts));
+  if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
+  int n = 0;
+  WMOE_CHECK_CUDA(ctx,
+                  route_tokens(tc, x, x_dtype, T, hidden, experts, top_k, w->router_w, w->router_bias, w->shared_gate,
+                               w->router_split, at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status,
+                               st, &n),
+                  "router");
+  WMOE_CHECK_CUDA(ctx,
+                  ep_plan(topk_idx, T, top_k, experts, world, send_rows, send_pairs, send_tok, pair_list, ret_index,
+                          ctx->d_status, st, &n),
+                  "wmoe_ep_route_plan: plan");
+  WMOE_CHECK_CUDA(ctx,
+                  ep_pack(x, x_dtype, hidden, send_tok, send_rows, world, T * std::min(top_k, world), send_buf, st, &n),
+                  "wmoe_ep_route_plan: rows");
+  ctx->launches += uint64_t(n);
+  return WMOE_OK;
+}
+
+int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, const int32_t* recv_rows,
+                    const int32_t* recv_pairs, const uint16_t* recv_buf, const int32_t* recv_pair_list,
+                    const void* x, int x_dtype, int T, const wmoe_layer_weights* w, uint16_t* y, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad store");
+  if (world < 1 || world > kMaxRanks || !recv_rows || !recv_pairs || layer < 0 || layer >= store->layers || T < 0 ||
+      (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad arguments");
+  if (int rc = check_layer(ctx, w, "wmoe_ep_experts")) return rc;
+  const int H = store->hidden, F = store->ffn, E = store->experts;
+  if (H != 2048 || F != 512) return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_ep_experts: this build runs hidden 2048, ffn 512");
+  long long R = 0, Pr = 0;
+  for (int s = 0; s < world; ++s) {
+    if (recv_rows[s] < 0 || recv_pairs[s] < 0) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad counts");
+    R += recv_rows[s];
+    Pr += recv_pairs[s];
+  }
+  if (Pr + T > (1ll << 30) || Pr > R * 8) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad counts");
+  if (Pr + T == 0) return WMOE_OK;
+  if (!y || (T > 0 && !x) || (Pr > 0 && (!recv_buf || !recv_pair_list)))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: null pointer");
+  const int P_r = int(Pr);
+  const size_t P = size_t(Pr) + size_t(T);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan plan;
+  const size_t o_row = plan.take<int32_t>(size_t(P_r));
+  const size_t o_exp = plan.take<int32_t>(size_t(P_r));
+  const size_t o_counts = plan.take<int32_t>(size_t(E));
+  const size_t o_offsets = plan.take<int32_t>(size_t(E) + 1);
+  const size_t o_perm = plan.take<int32_t>(size_t(P_r));
+  const size_t o_pos = plan.take<int32_t>(size_t(P_r));
+  const size_t o_used = plan.take<int32_t>(size_t(E) + 1);
+  const size_t o_seg = plan.take<int32_t>(size_t(E) + 2);
+  const size_t o_nused = plan.take<int32_t>(1);
+  const size_t o_disp = plan.take<char>(dispatch_scratch_bytes(P_r, E));
+  const size_t o_xg = plan.take<uint16_t>(P * H);
+  const size_t o_gemm = plan.take<char>(prefill_gemm_scratch_bytes(P, E, H, F));
+  if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
+  int n = 0;
+  int32_t* pair_row = at<int32_t>(ctx, o_row);
+  int32_t* pair_exp = at<int32_t>(ctx, o_exp);
+  WMOE_CHECK_CUDA(ctx, ep_fixup(recv_pair_list, P_r, world, recv_rows, recv_pairs, pair_row, pair_exp, st, &n),
+                  "wmoe_ep_experts: pair lists");
+  std::vector<int32_t> experts_used;
+  if (store->capped && P_r > 0) {
+    // the store must copy the received pairs' experts in first: one wait for the pair list
+    std::vector<int32_t> ex(static_cast<size_t>(P_r));
+    WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(ex.data(), pair_exp, ex.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+                    "pair read-back");
+    WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "pair read-back");
+    std::sort(ex.begin(), ex.end());
+    ex.erase(std::unique(ex.begin(), ex.end()), ex.end());
+    experts_used = ex;
+    if (int rc = store_prepare(store, layer, experts_used.data(), int(experts_used.size()), st)) return rc;
+  }
+  PairMap pm;
+  pm.T = P_r;
+  pm.k = 1;
+  pm.E = E;
+  pm.perm = at<int32_t>(ctx, o_perm);
+  pm.pos = at<int32_t>(ctx, o_pos);
+  pm.used = at<int32_t>(ctx, o_used);
+  pm.seg = at<int32_t>(ctx, o_seg);
+  pm.n_used = at<int32_t>(ctx, o_nused);
+  WMOE_CHECK_CUDA(ctx,
+                  dispatch_rows(pair_exp, P_r, 1, E, T, at<void>(ctx, o_disp), at<int32_t>(ctx, o_counts),
+                                at<int32_t>(ctx, o_offsets), at<int32_t>(ctx, o_perm), at<int32_t>(ctx, o_pos),
+                                at<int32_t>(ctx, o_used), at<int32_t>(ctx, o_seg), at<int32_t>(ctx, o_nused), nullptr,
+                                ctx->d_status, st, &n),
+                  "wmoe_ep_experts: dispatch");
+  __half* xg = at<__half>(ctx, o_xg);
+  WMOE_CHECK_CUDA(ctx, ep_gather(pm.perm, pair_row, P_r, recv_buf, x, x_dtype, T, H, xg, st, &n),
+                  "wmoe_ep_experts: gather");
+  const ExpertSource src = store_source(store, w->shared_gate_up, w->shared_down);
+  WMOE_CHECK_CUDA(ctx,
+                  prefill_gemms(src, layer, pm, P, H, F, xg, reinterpret_cast<__half*>(y), pm.perm, P_r,
+                                at<void>(ctx, o_gemm), ctx->sm_count, ctx->d_status, nullptr, st, &n),
+                  "wmoe_ep_experts: grouped GEMM");
+  ctx->launches += uint64_t(n);
+  if (store->capped && !experts_used.empty())
+    if (int rc = store_mark_used(store, layer, experts_used.data(), int(experts_used.size()), st)) return rc;
+  return WMOE_OK;
+}
+
+int wmoe_ep_combine(wmoe_ctx* ctx, int T, int top_k, int hidden, const int32_t* topk_idx, const float* topk_w,
+                    const int32_t* ret_index, const float* shared_s, const uint16_t* y_returned,
+                    const uint16_t* y_shared, void* out, int out_dtype, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (T < 0 || top_k != 8 || hidden <= 0 || hidden % 8 || (out_dtype != WMOE_F32 && out_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_combine: bad arguments");
+  if (T == 0) return WMOE_OK;
+  if (!topk_idx || !topk_w || !ret_index || !shared_s || !y_returned || !y_shared || !out)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_combine: null pointer");
+  int n = 0;
+  WMOE_CHECK_CUDA(ctx,
+                  combine_rows(T, top_k, hidden, topk_idx, topk_w, ret_index, shared_s,
+                               reinterpret_cast<const __half*>(y_returned), reinterpret_cast<const __half*>(y_shared),
+                               out, out_dtype, static_cast<cudaStream_t>(stream), &n),
+                  "wmoe_ep_combine");
+  ctx->launches += uint64_t(n);
+  return WMOE_OK;
 }
 
 int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,

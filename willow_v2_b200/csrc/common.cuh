@@ -148,4 +148,41 @@ __device__ __forceinline__ float to_f32<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
 
+
+// ---- fp16 activation rows of the grouped GEMMs ----
+// The GEMM operands and outputs are fp16 rows whose elements are stored in "run-of-8" order: inside every aligned
+// run of 8 values, stored position perm8(e) holds element e (order 0, 2, 1, 3, 4, 6, 5, 7), the order in which the
+// in-register dequantisation produces weights, so every dot product is unchanged.
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+
+// Stored position of element e within its run of 8 (and back: the map is its own inverse).
+__device__ __forceinline__ int perm8(int e) { return (e & ~7) | ((e & 1) << 1) | ((e & 2) >> 1) | (e & 4); }
+
+// 8 consecutive activations as float32 from one 16-byte (bf16) or two 16-byte (f32) loads
+__device__ __forceinline__ uint4 pack8_perm(const float (&v)[8]) {
+  return make_uint4(pack_h2(v[0], v[2]), pack_h2(v[1], v[3]), pack_h2(v[4], v[6]), pack_h2(v[5], v[7]));
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+
 }  // namespace wmoe

@@ -67,7 +67,7 @@ __device__ int block_exclusive_scan(int v, int* total) {
   return result;
 }
 
-__global__ void scan_kernel(const int32_t* __restrict__ tile_counts, int ntiles, int T, int k, int E,
+__global__ void scan_kernel(const int32_t* __restrict__ tile_counts, int ntiles, int T, int k, int E, int shared_rows,
                             int32_t* __restrict__ tile_base, int32_t* __restrict__ counts,
                             int32_t* __restrict__ offsets, int32_t* __restrict__ used, int32_t* __restrict__ seg,
                             int32_t* __restrict__ n_used, int64_t* __restrict__ usage) {
@@ -95,9 +95,9 @@ __global__ void scan_kernel(const int32_t* __restrict__ tile_counts, int ntiles,
   }
   if (e == 0) {
     offsets[E] = T * k;
-    used[nflag] = E;  // the shared expert's segment: one row per token
+    used[nflag] = E;  // the shared expert's segment: shared_rows rows (one per token)
     seg[nflag] = T * k;
-    seg[nflag + 1] = T * (k + 1);
+    seg[nflag + 1] = T * k + shared_rows;
     *n_used = nflag + 1;
   }
 }
@@ -132,6 +132,14 @@ __global__ void __launch_bounds__(kTile) scatter_kernel(const int32_t* __restric
 cudaError_t dispatch(const int32_t* topk_idx, int T, int k, int E, void* scratch, int32_t* counts,
                      int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* used, int32_t* seg, int32_t* n_used,
                      int64_t* usage, int* status, cudaStream_t st, int* launches) {
+  return dispatch_rows(topk_idx, T, k, E, T, scratch, counts, offsets, perm, pos, used, seg, n_used, usage, status,
+                       st, launches);
+}
+
+cudaError_t dispatch_rows(const int32_t* topk_idx, int T, int k, int E, int shared_rows, void* scratch,
+                          int32_t* counts, int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* used,
+                          int32_t* seg, int32_t* n_used, int64_t* usage, int* status, cudaStream_t st,
+                          int* launches) {
   const int ntiles = (T + kTile - 1) / kTile;
   int32_t* tile_counts = static_cast<int32_t*>(scratch);
   int32_t* tile_base = tile_counts + size_t(ntiles) * E;
@@ -140,8 +148,8 @@ cudaError_t dispatch(const int32_t* topk_idx, int T, int k, int E, void* scratch
     ++*launches;
   }
   const int threads = ((E + 31) / 32) * 32;
-  scan_kernel<<<1, threads < 64 ? 64 : threads, 0, st>>>(tile_counts, ntiles, T, k, E, tile_base, counts, offsets,
-                                                         used, seg, n_used, usage);
+  scan_kernel<<<1, threads < 64 ? 64 : threads, 0, st>>>(tile_counts, ntiles, T, k, E, shared_rows, tile_base, counts,
+                                                         offsets, used, seg, n_used, usage);
   ++*launches;
   if (T > 0) {
     scatter_kernel<<<ntiles, kTile, size_t(E) * (kTile / 32) * sizeof(uint32_t), st>>>(topk_idx, T, k, E, tile_base,

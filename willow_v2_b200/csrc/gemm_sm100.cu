@@ -73,16 +73,8 @@ static_assert(Layout<0>::bytes <= 232448 && Layout<1>::bytes <= 232448, "shared 
 static_assert(Layout<0>::bstages <= kMaxBStages && Layout<1>::bstages <= kMaxBStages, "barrier arrays");
 static_assert(kTileB % 1024 == 0 && kQ4Unit % 1024 == 0, "TMA destinations stay 1024-aligned");
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
 
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
 
-// Stored position of element e within its run of 8 (and back: the map is its own inverse).
-__device__ __forceinline__ int perm8(int e) { return (e & ~7) | ((e & 1) << 1) | ((e & 2) >> 1) | (e & 4); }
 
 // Q4_K K block (sub-blocks 2g and 2g + 1 of one super-block) of one tile row, from the row's 144 bytes in shared
 // memory, into the thread's TMEM lane at taddr: 32 columns of fp16 pairs, stored position p in column p / 2. Low
@@ -171,6 +163,8 @@ struct GemmParams {
   int n_mtiles;
   int F, H;
   __half* out;           // gate_up: h [P][F] (columns in run-of-8 order); down: y [P][H]
+  const int32_t* out_rows;  // down: y row of pair position p < n_routed is out_rows[p] (null: p)
+  int n_routed;
   int* status;
 };
 
@@ -361,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!all_ready) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t taddr = tmem_base + uint32_t(buf * kAccCols) + (uint32_t(32 * quad) << 16);
-      __half* gout = p.out + size_t(t.seg0 + t.n0) * ld + orows * t.mt;
+      const int prow0 = t.seg0 + t.n0;  // pair position of the chunk's first token
+      __half* gout = p.out + orows * t.mt;
       for (int c0 = 0; c0 < t.ncols; c0 += 32) {
         float v[32];
         tmem_ld32(taddr + uint32_t(c0), v);
@@ -390,9 +385,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int q = e; q < pieces; q += 128) {
           const int c = q / (orows / 8), g = q % (orows / 8);
-          if (c < n)
-            *reinterpret_cast<uint4*>(gout + size_t(c0 + c) * ld + 8 * g) =
+          if (c < n) {
+            int row = prow0 + c0 + c;
+            if (MODE == 1 && p.out_rows && row < p.n_routed) row = p.out_rows[row];
+            *reinterpret_cast<uint4*>(gout + size_t(row) * ld + 8 * g) =
                 *reinterpret_cast<const uint4*>(obuf + c * orows + 8 * g);
+          }
         }
         if (MODE == 1) asm volatile("bar.sync 1, 128;" ::: "memory");  // obuf is rewritten by the next chunk
       }
@@ -479,21 +477,6 @@ __global__ void __launch_bounds__(512) chunk_list_kernel(PairMap pm, int2* chunk
   if (u == 0) *n_chunks = total;
 }
 
-// 8 consecutive activations as float32 from one 16-byte (bf16) or two 16-byte (f32) loads
-__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-}
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-
 // X_g[p] = fp16(x[token(p)]) for every pair position p (routed pairs, then the shared expert's rows), columns in
 // run-of-8 order.
 template <typename XT>
@@ -506,33 +489,38 @@ __global__ void __launch_bounds__(256) gather_fp16_kernel(PairMap pm, const XT* 
   for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
     float v[8];
     load8(src + i, v);
-    // stored order within the run: elements 0, 2, 1, 3, 4, 6, 5, 7
-    *reinterpret_cast<uint4*>(dst + i) =
-        make_uint4(pack_h2(v[0], v[2]), pack_h2(v[1], v[3]), pack_h2(v[4], v[6]), pack_h2(v[5], v[7]));
+    *reinterpret_cast<uint4*>(dst + i) = pack8_perm(v);
   }
 }
 
-// Combine from the fp16 down outputs (stored / 32): out[t] = sum over picks in ascending expert id of
-// w * 32 * y[pick] (engines/base.py:580-586), + s_t * 32 * y[shared row t] (base.py:481-489). One CTA per token,
-// 8 consecutive outputs per thread from 16-byte loads of each picked row.
+// Combine from the fp16 down outputs (stored / 32): out[t] = sum over the token's picks in ascending expert id of
+// w * 32 * y_routed[rows[t][j]] (engines/base.py:580-586), + s_t * 32 * y_shared[t] (base.py:481-489). One CTA per
+// token, 8 consecutive outputs per thread from 16-byte loads of each row.
 template <int K>
-__global__ void __launch_bounds__(256) combine_f16_kernel(PairMap pm, int H, const float* __restrict__ topk_w,
-                                                          const float* __restrict__ shared_s,
-                                                          const __half* __restrict__ y, void* __restrict__ out,
-                                                          int out_dtype) {
+__global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t* __restrict__ topk_idx,
+                                                           const float* __restrict__ topk_w,
+                                                           const int32_t* __restrict__ rows,
+                                                           const float* __restrict__ shared_s,
+                                                           const __half* __restrict__ y_routed,
+                                                           const __half* __restrict__ y_shared,
+                                                           void* __restrict__ out, int out_dtype) {
   const int t = blockIdx.x;
-  int ps[K];
+  int ex[K], ps[K];
   float ws[K];
 #pragma unroll
   for (int s = 0; s < K; ++s) {
-    ps[s] = pm.pos[size_t(t) * K + s];
+    ex[s] = topk_idx[size_t(t) * K + s];
+    ps[s] = rows[size_t(t) * K + s];
     ws[s] = topk_w[size_t(t) * K + s] * 32.0f;
   }
 #pragma unroll
   for (int i = 1; i < K; ++i)
 #pragma unroll
     for (int j = i; j > 0; --j)
-      if (ps[j] < ps[j - 1]) {
+      if (ex[j] < ex[j - 1]) {
+        const int te = ex[j];
+        ex[j] = ex[j - 1];
+        ex[j - 1] = te;
         const int tp = ps[j];
         ps[j] = ps[j - 1];
         ps[j - 1] = tp;
@@ -541,20 +529,19 @@ __global__ void __launch_bounds__(256) combine_f16_kernel(PairMap pm, int H, con
         ws[j - 1] = tw;
       }
   const float s = shared_s[t] * 32.0f;
-  const size_t shared_row = size_t(pm.T) * K + t;
   for (int r = threadIdx.x * 8; r < H; r += blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < K + 1; ++i) {
-      const size_t row = i < K ? size_t(ps[i]) : shared_row;
+      const __half* src = i < K ? y_routed + size_t(ps[i]) * H : y_shared + size_t(t) * H;
       const float wi = i < K ? ws[i] : s;
-      const uint4 u = *reinterpret_cast<const uint4*>(y + row * H + r);
+      const uint4 u = *reinterpret_cast<const uint4*>(src + r);
       const uint32_t hw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[j]));
-        acc[2 * j] = __fadd_rn(acc[2 * j], i < K ? __fmul_rn(f.x, wi) : __fmul_rn(wi, f.x));
-        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], i < K ? __fmul_rn(f.y, wi) : __fmul_rn(wi, f.y));
+        acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(f.x, wi));
+        acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(f.y, wi));
       }
     }
     if (out_dtype == kF32) {
@@ -605,45 +592,40 @@ cudaError_t make_tmap_q4k(CUtensorMap* map, const uint8_t* ptr, uint64_t row_byt
 
 }  // namespace
 
-size_t prefill_scratch_bytes(int T, int k, int E, int H, int F) {
-  const size_t P = size_t(T) * (k + 1);
+size_t prefill_gemm_scratch_bytes(size_t P, int E, int H, int F) {
   const size_t chunks = P / kBN + size_t(E) + 2;
-  return chunks * sizeof(int2) + 256 + P * H * sizeof(__half) * 2 + P * F * sizeof(__half) + 4 * 256;
+  return (chunks * sizeof(int2) + 255) / 256 * 256 + 256 + (P * F * sizeof(__half) + 255) / 256 * 256;
 }
 
-cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const void* x,
-                            int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
-                            void* scratch, int num_sms, int* status, const cudaEvent_t* marks, cudaStream_t st,
-                            int* launches) {
-  if (H % QK || F != 2 * QK || H % kBM || pm.E + 1 > 512 || pm.k != 8 || num_sms <= 0) return cudaErrorInvalidValue;
-  // activations are read and written 16 bytes at a time
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16) return cudaErrorInvalidValue;
+size_t prefill_scratch_bytes(int T, int k, int E, int H, int F) {
+  const size_t P = size_t(T) * (k + 1);
+  return prefill_gemm_scratch_bytes(P, E, H, F) + 2 * ((P * H * sizeof(__half) + 255) / 256 * 256);
+}
+
+cudaError_t check_weight_alignment(const ExpertSource& src) {
   // weight rows are copied by TMA and bulk copies: the matrices must start on 16-byte boundaries
   if (reinterpret_cast<uintptr_t>(src.shared_down) % 16 || reinterpret_cast<uintptr_t>(src.shared_gate_up) % 16 ||
       reinterpret_cast<uintptr_t>(src.slab) % 16 || src.slot_bytes % 16 || src.gate_up_bytes % 16)
     return cudaErrorInvalidValue;
-  const size_t P = size_t(pm.T) * (pm.k + 1);
+  return cudaSuccess;
+}
+
+cudaError_t prefill_gemms(const ExpertSource& src, int layer, const PairMap& pm, size_t P, int H, int F,
+                          const __half* xg, __half* y, const int32_t* out_rows, int n_routed, void* scratch,
+                          int num_sms, int* status, const cudaEvent_t* marks, cudaStream_t st, int* launches) {
+  if (H % QK || F != 2 * QK || H % kBM || pm.E + 1 > 512 || num_sms <= 0) return cudaErrorInvalidValue;
+  cudaError_t e = check_weight_alignment(src);
+  if (e != cudaSuccess) return e;
   const size_t max_chunks = P / kBN + size_t(pm.E) + 2;
   char* b = static_cast<char*>(scratch);
   int2* chunks = reinterpret_cast<int2*>(b);
   b += (max_chunks * sizeof(int2) + 255) / 256 * 256;
   int* n_chunks = reinterpret_cast<int*>(b);
   b += 256;
-  __half* xg = reinterpret_cast<__half*>(b);
-  b += (P * H * sizeof(__half) + 255) / 256 * 256;
   __half* hbuf = reinterpret_cast<__half*>(b);
-  b += (P * F * sizeof(__half) + 255) / 256 * 256;
-  __half* ybuf = reinterpret_cast<__half*>(b);
 
   chunk_list_kernel<<<1, 512, 0, st>>>(pm, chunks, n_chunks);
-  if (x_dtype == kF32)
-    gather_fp16_kernel<float><<<unsigned(P), 256, 0, st>>>(pm, static_cast<const float*>(x), H, xg);
-  else
-    gather_fp16_kernel<__nv_bfloat16><<<unsigned(P), 256, 0, st>>>(pm, static_cast<const __nv_bfloat16*>(x), H, xg);
-  *launches += 2;
-  if (marks) cudaEventRecord(marks[0], st);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  ++*launches;
   static bool attr_set = false;  // per process: the kernels' shared memory limit does not change
   if (!attr_set) {
     if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -676,15 +658,55 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
   gp.n_mtiles = F / 64;
   gp.out = hbuf;
   grouped_gemm_kernel<0><<<unsigned(num_sms), kThreads, Layout<0>::bytes, st>>>(map_x, map_w, map_ws, gp);
-  if (marks) cudaEventRecord(marks[1], st);
+  if (marks) cudaEventRecord(marks[0], st);
   gp.n_mtiles = H / kBM;
-  gp.out = ybuf;
+  gp.out = y;
+  gp.out_rows = out_rows;
+  gp.n_routed = n_routed;
   grouped_gemm_kernel<1><<<unsigned(num_sms), kThreads, Layout<1>::bytes, st>>>(map_h, map_w, map_ws, gp);
-  if (marks) cudaEventRecord(marks[2], st);
-  combine_f16_kernel<8><<<unsigned(pm.T), 256, 0, st>>>(pm, H, topk_w, shared_s, ybuf, out, out_dtype);
-  if (marks) cudaEventRecord(marks[3], st);
-  *launches += 3;
+  if (marks) cudaEventRecord(marks[1], st);
+  *launches += 2;
   return cudaGetLastError();
+}
+
+cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const float* topk_w, const int32_t* rows,
+                         const float* shared_s, const __half* y_routed, const __half* y_shared, void* out,
+                         int out_dtype, cudaStream_t st, int* launches) {
+  if (k != 8 || H % 8 || reinterpret_cast<uintptr_t>(out) % 16) return cudaErrorInvalidValue;
+  if (T > 0) {
+    combine_rows_kernel<8><<<unsigned(T), 256, 0, st>>>(H, topk_idx, topk_w, rows, shared_s, y_routed, y_shared, out,
+                                                        out_dtype);
+    ++*launches;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, const int32_t* topk_idx, int H,
+                            int F, const void* x, int x_dtype, const float* topk_w, const float* shared_s, void* out,
+                            int out_dtype, void* scratch, int num_sms, int* status, const cudaEvent_t* marks,
+                            cudaStream_t st, int* launches) {
+  if (pm.k != 8) return cudaErrorInvalidValue;
+  // activations are read and written 16 bytes at a time
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16) return cudaErrorInvalidValue;
+  const size_t P = size_t(pm.T) * (pm.k + 1);
+  char* b = static_cast<char*>(scratch);
+  __half* xg = reinterpret_cast<__half*>(b);
+  b += (P * H * sizeof(__half) + 255) / 256 * 256;
+  __half* ybuf = reinterpret_cast<__half*>(b);
+  b += (P * H * sizeof(__half) + 255) / 256 * 256;
+  if (x_dtype == kF32)
+    gather_fp16_kernel<float><<<unsigned(P), 256, 0, st>>>(pm, static_cast<const float*>(x), H, xg);
+  else
+    gather_fp16_kernel<__nv_bfloat16><<<unsigned(P), 256, 0, st>>>(pm, static_cast<const __nv_bfloat16*>(x), H, xg);
+  ++*launches;
+  if (marks) cudaEventRecord(marks[0], st);
+  cudaError_t e = prefill_gemms(src, layer, pm, P, H, F, xg, ybuf, nullptr, 0, b, num_sms, status,
+                                marks ? marks + 1 : nullptr, st, launches);
+  if (e != cudaSuccess) return e;
+  e = combine_rows(pm.T, pm.k, H, topk_idx, topk_w, pm.pos, shared_s, ybuf, ybuf + size_t(pm.T) * pm.k * H, out,
+                   out_dtype, st, launches);
+  if (marks) cudaEventRecord(marks[3], st);
+  return e;
 }
 
 }  // namespace wmoe

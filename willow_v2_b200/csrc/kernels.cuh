@@ -63,6 +63,11 @@ size_t dispatch_scratch_bytes(int T, int E);
 cudaError_t dispatch(const int32_t* topk_idx, int T, int k, int E, void* scratch, int32_t* counts,
                      int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* used, int32_t* seg, int32_t* n_used,
                      int64_t* usage, int* status, cudaStream_t st, int* launches);
+// The same with a shared-expert segment of shared_rows rows (instead of T) after the T * k routed positions.
+cudaError_t dispatch_rows(const int32_t* topk_idx, int T, int k, int E, int shared_rows, void* scratch,
+                          int32_t* counts, int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* used,
+                          int32_t* seg, int32_t* n_used, int64_t* usage, int* status, cudaStream_t st,
+                          int* launches);
 
 // gemv.cu (small token counts per expert)
 cudaError_t quant_rows(const void* x, int x_dtype, int rows, int K, int16_t* q, float* scale, int32_t* sum16,
@@ -78,12 +83,36 @@ cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* 
 cudaError_t gemv_batch(int type, const uint8_t* const* weights, int n, int rows, int k, const float* x, float* y,
                        cudaStream_t st, int* launches);
 
-// gemm_sm100.cu: tcgen05 grouped GEMMs for many tokens per expert (gate_up + SwiGLU, down, fp16 combine)
+// gemm_sm100.cu: tcgen05 grouped GEMMs for many tokens per expert (gate_up + SwiGLU, down) and the fp16 combine
 size_t prefill_scratch_bytes(int T, int k, int E, int H, int F);
-cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const void* x,
-                            int x_dtype, const float* topk_w, const float* shared_s, void* out, int out_dtype,
-                            void* scratch, int num_sms, int* status, const cudaEvent_t* marks, cudaStream_t st,
-                            int* launches);  // marks: 4 events recorded after gather, gate_up, down, combine (or null)
+size_t prefill_gemm_scratch_bytes(size_t P, int E, int H, int F);
+// The whole multi-token expert stage: gather, both GEMMs, combine. marks: 4 events recorded after gather, gate_up,
+// down, combine (or null).
+cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, const int32_t* topk_idx, int H,
+                            int F, const void* x, int x_dtype, const float* topk_w, const float* shared_s, void* out,
+                            int out_dtype, void* scratch, int num_sms, int* status, const cudaEvent_t* marks,
+                            cudaStream_t st, int* launches);
+// The two GEMMs over P gathered fp16 rows xg (run-of-8 order): y [P][H] fp16 (= down output / 32); routed pair
+// positions p < n_routed are written at row out_rows[p] when out_rows is given. marks: 2 events (or null).
+cudaError_t prefill_gemms(const ExpertSource& src, int layer, const PairMap& pm, size_t P, int H, int F,
+                          const __half* xg, __half* y, const int32_t* out_rows, int n_routed, void* scratch,
+                          int num_sms, int* status, const cudaEvent_t* marks, cudaStream_t st, int* launches);
+// out[t] = sum over picks in ascending expert id of w * 32 * y_routed[rows[t][j]] + s_t * 32 * y_shared[t]
+cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const float* topk_w, const int32_t* rows,
+                         const float* shared_s, const __half* y_routed, const __half* y_shared, void* out,
+                         int out_dtype, cudaStream_t st, int* launches);
+
+// ep.cu: expert parallelism over up to kMaxRanks ranks (contiguous expert blocks)
+constexpr int kMaxRanks = 8;
+cudaError_t ep_plan(const int32_t* topk_idx, int T, int k, int E, int world, int32_t* send_rows, int32_t* send_pairs,
+                    int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, int* status, cudaStream_t st,
+                    int* launches);
+cudaError_t ep_pack(const void* x, int x_dtype, int H, const int32_t* send_tok, const int32_t* send_rows, int world,
+                    int max_rows, void* send_buf, cudaStream_t st, int* launches);
+cudaError_t ep_fixup(const int32_t* pair_list, int P, int world, const int32_t* recv_rows, const int32_t* recv_pairs,
+                     int32_t* pair_row, int32_t* pair_expert, cudaStream_t st, int* launches);
+cudaError_t ep_gather(const int32_t* perm, const int32_t* pair_row, int P_r, const void* recv, const void* x,
+                      int x_dtype, int T, int H, void* xg, cudaStream_t st, int* launches);
 
 // decode.cu: persistent one-token decode (one layer or a stack)
 struct DecodeLayer {

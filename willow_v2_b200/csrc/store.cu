@@ -112,20 +112,24 @@ static void push_update(wmoe_store* s, SlotUpdates& u, int index, int value, cud
   ++u.n;
 }
 
-int store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, size_t cap_bytes, wmoe_store** out) {
+int store_create(wmoe_ctx* ctx, int layers, int experts, int expert_begin, int expert_end, int hidden, int ffn,
+                 size_t cap_bytes, wmoe_store** out) {
   auto* s = new wmoe_store();
   s->ctx = ctx;
   s->layers = layers;
   s->experts = experts;
+  s->expert_begin = expert_begin;
+  s->expert_end = expert_end;
   s->hidden = hidden;
   s->ffn = ffn;
   s->gate_up_bytes = size_t(2 * ffn) * hidden / QK * Q4K_BYTES;
   s->down_bytes = size_t(hidden) * ffn / QK * Q6K_BYTES;
   s->blob_bytes = s->gate_up_bytes + s->down_bytes;
   s->slot_stride = (s->blob_bytes + 255) / 256 * 256;
-  const size_t total = size_t(layers) * experts;
-  s->capped = cap_bytes != 0 && cap_bytes < total * s->slot_stride;
-  s->n_slots = s->capped ? int(cap_bytes / s->slot_stride) : int(total);
+  const size_t total = size_t(layers) * experts;          // slot table entries (every expert id)
+  const size_t held = size_t(layers) * s->owned();         // blobs this store holds
+  s->capped = cap_bytes != 0 && cap_bytes < held * s->slot_stride;
+  s->n_slots = s->capped ? int(std::min(cap_bytes / s->slot_stride, held)) : int(held);
   if (s->n_slots <= 0) {
     delete s;
     return ctx_fail(ctx, -3, "expert store cap is smaller than one expert");
@@ -137,14 +141,15 @@ int store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, si
     e = cudaEventCreateWithFlags(&s->ring[i], cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->copied, cudaEventDisableTiming);
   s->slot_of.assign(total, -1);
-  if (e == cudaSuccess && s->capped) e = cudaHostAlloc(&s->h_master, total * s->blob_bytes, cudaHostAllocDefault);
+  if (e == cudaSuccess && s->capped) e = cudaHostAlloc(&s->h_master, held * s->blob_bytes, cudaHostAllocDefault);
   if (e != cudaSuccess) {
     const std::string msg = std::string("expert store allocation: ") + cudaGetErrorString(e);
     store_destroy(s);
     return ctx_fail(ctx, -2, msg);
   }
   if (!s->capped) {
-    for (size_t i = 0; i < total; ++i) s->slot_of[i] = int32_t(i);
+    for (int l = 0; l < layers; ++l)
+      for (int x = expert_begin; x < expert_end; ++x) s->slot_of[size_t(l) * experts + x] = int32_t(s->blob_index(l, x));
   } else {
     s->slot_key.assign(size_t(s->n_slots), -1);
     s->slot_use.assign(size_t(s->n_slots), 0);
@@ -176,13 +181,14 @@ void store_destroy(wmoe_store* s) {
 int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cudaStream_t st) {
   if (layer < 0 || layer >= s->layers || expert < 0 || expert >= s->experts || !host_src)
     return store_fail(s, -1, "wmoe_store_upload: bad layer/expert/source");
+  if (!s->owns(expert)) return store_fail(s, -1, "wmoe_store_upload: expert outside the store's range");
   const size_t key = size_t(layer) * s->experts + expert;
   cudaError_t e;
   if (s->capped) {
     // the host copy is the master; drop any resident copy so the next prepare reloads it
     e = cudaStreamSynchronize(st);
     if (e == cudaSuccess) {
-      memcpy(s->h_master + key * s->blob_bytes, host_src, s->blob_bytes);
+      memcpy(s->h_master + s->blob_index(layer, expert) * s->blob_bytes, host_src, s->blob_bytes);
       const int slot = s->slot_of[key];
       if (slot >= 0) {
         SlotUpdates u{};
@@ -203,30 +209,30 @@ int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cud
 int store_fill_synthetic(wmoe_store* s, uint64_t seed, int layer_begin, int layer_end, cudaStream_t st) {
   if (layer_begin < 0 || layer_end > s->layers || layer_begin > layer_end)
     return store_fail(s, -1, "wmoe_store_fill_synthetic: bad layer range");
-  const int E = s->experts;
-  std::vector<int32_t> le(size_t(2) * E);
+  const int E = s->experts, n = int(s->owned());
+  std::vector<int32_t> le(size_t(2) * n);
   int32_t* d_le = nullptr;
   uint8_t* staging = nullptr;
   cudaError_t e = cudaMalloc(&d_le, le.size() * sizeof(int32_t));
-  if (e == cudaSuccess && s->capped) e = cudaMalloc(&staging, size_t(E) * s->blob_bytes);
+  if (e == cudaSuccess && s->capped) e = cudaMalloc(&staging, size_t(n) * s->blob_bytes);
   for (int layer = layer_begin; layer < layer_end && e == cudaSuccess; ++layer) {
-    for (int x = 0; x < E; ++x) {
-      le[size_t(2) * x] = layer;
-      le[size_t(2) * x + 1] = x;
+    for (int i = 0; i < n; ++i) {
+      le[size_t(2) * i] = layer;
+      le[size_t(2) * i + 1] = s->expert_begin + i;
     }
     e = cudaMemcpyAsync(d_le, le.data(), le.size() * sizeof(int32_t), cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) break;
     if (!s->capped) {
-      // uncapped slots are laid out layer-major with identity slots: one launch covers the layer
-      e = fill_synthetic(s->d_slab + size_t(layer) * E * s->slot_stride, seed, d_le, E, s->slot_stride, s->hidden,
-                         s->ffn, st);
+      // uncapped slots hold the owned experts layer-major in id order: one launch covers the layer
+      e = fill_synthetic(s->d_slab + s->blob_index(layer, s->expert_begin) * s->slot_stride, seed, d_le, n,
+                         s->slot_stride, s->hidden, s->ffn, st);
       ctx_count_launch(s->ctx);
     } else {
-      e = fill_synthetic(staging, seed, d_le, E, s->blob_bytes, s->hidden, s->ffn, st);
+      e = fill_synthetic(staging, seed, d_le, n, s->blob_bytes, s->hidden, s->ffn, st);
       ctx_count_launch(s->ctx);
       if (e == cudaSuccess)
-        e = cudaMemcpyAsync(s->h_master + size_t(layer) * E * s->blob_bytes, staging, size_t(E) * s->blob_bytes,
-                            cudaMemcpyDeviceToHost, st);
+        e = cudaMemcpyAsync(s->h_master + s->blob_index(layer, s->expert_begin) * s->blob_bytes, staging,
+                            size_t(n) * s->blob_bytes, cudaMemcpyDeviceToHost, st);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // le is reused for the next layer
   }
@@ -253,8 +259,10 @@ int store_fill_synthetic(wmoe_store* s, uint64_t seed, int layer_begin, int laye
 
 int store_prepare(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st) {
   if (layer < 0 || layer >= s->layers || n < 0) return store_fail(s, -1, "wmoe_store_prepare: bad layer");
-  for (int i = 0; i < n; ++i)
+  for (int i = 0; i < n; ++i) {
     if (experts[i] < 0 || experts[i] >= s->experts) return store_fail(s, -1, "wmoe_store_prepare: bad expert id");
+    if (!s->owns(experts[i])) return store_fail(s, -1, "wmoe_store_prepare: expert outside the store's range");
+  }
   if (!s->capped) {
     s->hits += uint64_t(n);
     return 0;
@@ -301,8 +309,8 @@ int store_prepare(wmoe_store* s, int layer, const int32_t* experts, int n, cudaS
       if (e != cudaSuccess) break;
     }
     const size_t key = size_t(layer) * E + size_t(x);
-    e = cudaMemcpyAsync(s->d_slab + size_t(slot) * s->slot_stride, s->h_master + key * s->blob_bytes, s->blob_bytes,
-                        cudaMemcpyHostToDevice, s->side);
+    e = cudaMemcpyAsync(s->d_slab + size_t(slot) * s->slot_stride, s->h_master + s->blob_index(layer, x) * s->blob_bytes,
+                        s->blob_bytes, cudaMemcpyHostToDevice, s->side);
     if (e != cudaSuccess) break;
     ++s->misses;
     s->bytes_in += s->blob_bytes;

@@ -35,6 +35,11 @@ struct wmoe_store {
   static constexpr int kRing = 64;
   wmoe_ctx* ctx = nullptr;
   int layers = 0, experts = 0, hidden = 0, ffn = 0;
+  int expert_begin = 0, expert_end = 0;  // the experts of each layer this store holds (expert parallelism)
+  bool owns(int e) const { return e >= expert_begin && e < expert_end; }
+  size_t owned() const { return size_t(expert_end - expert_begin); }
+  // index of an owned blob among the store's blobs (layer-major), e.g. into the pinned host copy
+  size_t blob_index(int layer, int e) const { return size_t(layer) * owned() + size_t(e - expert_begin); }
   size_t gate_up_bytes = 0, down_bytes = 0, blob_bytes = 0, slot_stride = 0;
   bool capped = false;
   int n_slots = 0;
@@ -56,7 +61,8 @@ struct wmoe_store {
 int ctx_fail(wmoe_ctx* ctx, int code, const std::string& msg);
 void ctx_count_launch(wmoe_ctx* ctx, int n = 1);
 
-int store_create(wmoe_ctx* ctx, int layers, int experts, int hidden, int ffn, size_t cap_bytes, wmoe_store** out);
+int store_create(wmoe_ctx* ctx, int layers, int experts, int expert_begin, int expert_end, int hidden, int ffn,
+                 size_t cap_bytes, wmoe_store** out);
 void store_destroy(wmoe_store* s);
 int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cudaStream_t st);
 int store_fill_synthetic(wmoe_store* s, uint64_t seed, int layer_begin, int layer_end, cudaStream_t st);

@@ -34,6 +34,7 @@ SIGNATURES = {
     "wmoe_pack_router": (_i, [_p, _p, _p, _i, _i, _p, _p]),
     "wmoe_split_router": (_i, [_p, _p, _i, _i, _p, _p]),
     "wmoe_store_create": (_i, [_p, _i, _i, _i, _i, _sz, _pp]),
+    "wmoe_store_create_range": (_i, [_p, _i, _i, _i, _i, _i, _i, _sz, _pp]),
     "wmoe_store_destroy": (None, [_p]),
     "wmoe_store_upload": (_i, [_p, _i, _i, _p, _p]),
     "wmoe_store_fill_synthetic": (_i, [_p, _u64, _i, _i, _p]),
@@ -48,6 +49,9 @@ SIGNATURES = {
     "wmoe_decode_stack": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
     "wmoe_decode_stack_noalloc": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
     "wmoe_gemv_batch": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
+    "wmoe_ep_route_plan": (_i, [_p, _i, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "wmoe_ep_experts": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p]),
+    "wmoe_ep_combine": (_i, [_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _i, _p]),
 }
 
 
@@ -60,6 +64,7 @@ class LayerWeights(ctypes.Structure):
 
 ROUTER_STRIDE = 264  # WMOE_ROUTER_STRIDE
 PHASES = ("router", "dispatch", "gather", "gate_up", "down", "combine")  # WMOE_PHASES, in order
+MAX_RANKS = 8  # WMOE_MAX_RANKS
 
 
 def _load():

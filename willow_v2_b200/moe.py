@@ -140,16 +140,21 @@ class ExpertStore:
     host memory, misses copied on a side stream with least-recently-used eviction."""
 
     def __init__(self, layers: int, experts: int = 256, hidden: int = 2048, ffn: int = 512, cap_bytes: int = 0,
-                 ctx: Optional[Context] = None):
+                 ctx: Optional[Context] = None, expert_range: Optional[tuple] = None):
+        """expert_range (begin, end): hold only those experts of every layer (one rank's block under expert
+        parallelism, wmoe_store_create_range); default all."""
         self.ctx = ctx or default_context()
         self.layers, self.experts, self.hidden, self.ffn = layers, experts, hidden, ffn
+        self.expert_range = tuple(expert_range) if expert_range is not None else (0, experts)
+        held = self.expert_range[1] - self.expert_range[0]
         handle = ctypes.c_void_p()
-        check(self.ctx.handle, lib.wmoe_store_create(self.ctx.handle, layers, experts, hidden, ffn, cap_bytes,
-                                                     ctypes.byref(handle)))
+        check(self.ctx.handle, lib.wmoe_store_create_range(self.ctx.handle, layers, experts, self.expert_range[0],
+                                                           self.expert_range[1], hidden, ffn, cap_bytes,
+                                                           ctypes.byref(handle)))
         self.handle = handle
         self.blob_bytes = int(lib.wmoe_store_blob_bytes(handle))
         self.gate_up_bytes = 2 * ffn * hidden // 256 * 144
-        self.capped = cap_bytes != 0 and cap_bytes < layers * experts * ((self.blob_bytes + 255) // 256 * 256)
+        self.capped = cap_bytes != 0 and cap_bytes < layers * held * ((self.blob_bytes + 255) // 256 * 256)
 
     def upload(self, layer: int, expert: int, blob):
         """blob: the expert's bytes (numpy uint8 / bytes, or a CPU uint8 tensor), blob_bytes long."""
@@ -263,6 +268,124 @@ def moe_forward(store: ExpertStore, layer: int, x: torch.Tensor, lw: LayerWeight
                                                  top_k, ctypes.byref(weights), _ptr(out), _DTYPES[out.dtype],
                                                  _ptr(sel), _ptr(w), _stream()))
     return (out, w, sel) if return_routing else out
+
+
+@dataclass
+class EPPlan:
+    """A rank's routing and send plan for one layer under expert parallelism (wmoe_ep_route_plan)."""
+    topk_w: torch.Tensor       # f32 [T, k]
+    topk_idx: torch.Tensor     # int32 [T, k]
+    shared_s: torch.Tensor     # f32 [T]
+    counts: torch.Tensor       # int32 [2, world]: rows, pairs to each rank
+    send_buf: torch.Tensor     # fp16 [T * min(k, world), H] (first sum(rows) used)
+    pair_list: torch.Tensor    # int32 [T * k, 2] (first sum(pairs) used)
+    ret_index: torch.Tensor    # int32 [T, k]
+
+
+def ep_route_plan(ctx: Context, world: int, x: torch.Tensor, lw: LayerWeights, experts: int = 256,
+                  top_k: int = 8) -> EPPlan:
+    """Step 1 of an expert-parallel layer on one rank (see include/wmoe.h): route x [T, H] and build what goes to
+    each of the world ranks."""
+    x = x.contiguous()
+    T, H = x.shape
+    dev = x.device
+    rows = T * min(top_k, world)
+    plan = EPPlan(topk_w=torch.empty(T, top_k, dtype=torch.float32, device=dev),
+                  topk_idx=torch.empty(T, top_k, dtype=torch.int32, device=dev),
+                  shared_s=torch.empty(T, dtype=torch.float32, device=dev),
+                  counts=torch.zeros(2, world, dtype=torch.int32, device=dev),
+                  send_buf=torch.empty(rows, H, dtype=torch.float16, device=dev),
+                  pair_list=torch.empty(T * top_k, 2, dtype=torch.int32, device=dev),
+                  ret_index=torch.empty(T, top_k, dtype=torch.int32, device=dev))
+    weights = lw.as_struct()
+    send_tok = torch.empty(max(rows, 1), dtype=torch.int32, device=dev)
+    check(ctx.handle, lib.wmoe_ep_route_plan(ctx.handle, world, _ptr(x), _DTYPES[x.dtype], T, top_k, experts, H,
+                                             ctypes.byref(weights), _ptr(plan.topk_w), _ptr(plan.topk_idx),
+                                             _ptr(plan.shared_s), _ptr(plan.counts[0]), _ptr(plan.counts[1]),
+                                             _ptr(send_tok), _ptr(plan.pair_list), _ptr(plan.ret_index),
+                                             _ptr(plan.send_buf), _stream()))
+    return plan
+
+
+def ep_experts(store: ExpertStore, layer: int, world: int, recv_rows, recv_pairs, recv_buf: torch.Tensor,
+               recv_pair_list: torch.Tensor, x: torch.Tensor, lw: LayerWeights) -> torch.Tensor:
+    """Step 3: this rank's experts on the received rows (recv_rows / recv_pairs: per-source counts, host ints),
+    plus the shared expert on its own tokens x. -> y fp16 [sum(recv_pairs) + T, H]."""
+    ctx = store.ctx
+    x = x.contiguous()
+    T, H = x.shape
+    rr = (ctypes.c_int32 * world)(*[int(v) for v in recv_rows])
+    rp = (ctypes.c_int32 * world)(*[int(v) for v in recv_pairs])
+    y = torch.empty(sum(int(v) for v in recv_pairs) + T, H, dtype=torch.float16, device=x.device)
+    weights = lw.as_struct()
+    check(ctx.handle, lib.wmoe_ep_experts(ctx.handle, store.handle, layer, world, rr, rp, _ptr(recv_buf),
+                                          _ptr(recv_pair_list), _ptr(x), _DTYPES[x.dtype], T, ctypes.byref(weights),
+                                          _ptr(y), _stream()))
+    return y
+
+
+def ep_combine(ctx: Context, plan: EPPlan, y_returned: torch.Tensor, y_shared: torch.Tensor,
+               out_dtype: torch.dtype) -> torch.Tensor:
+    """Step 5: the rank's outputs from the returned result rows and its shared-expert rows."""
+    T, k = plan.topk_idx.shape
+    H = y_shared.shape[1]
+    out = torch.empty(T, H, dtype=out_dtype, device=y_shared.device)
+    check(ctx.handle, lib.wmoe_ep_combine(ctx.handle, T, k, H, _ptr(plan.topk_idx), _ptr(plan.topk_w),
+                                          _ptr(plan.ret_index), _ptr(plan.shared_s), _ptr(y_returned),
+                                          _ptr(y_shared), _ptr(out), _DTYPES[out_dtype], _stream()))
+    return out
+
+
+class GpuEPOps:
+    """The three per-rank steps of an expert-parallel layer, on this library's kernels."""
+
+    @staticmethod
+    def route_plan(store: ExpertStore, x: torch.Tensor, lw: LayerWeights, world: int, top_k: int) -> EPPlan:
+        return ep_route_plan(store.ctx, world, x, lw, store.experts, top_k)
+
+    @staticmethod
+    def experts(store: ExpertStore, layer: int, world: int, recv_rows, recv_pairs, recv_buf, recv_pair_list, x, lw):
+        return ep_experts(store, layer, world, recv_rows, recv_pairs, recv_buf, recv_pair_list, x, lw)
+
+    @staticmethod
+    def combine(store: ExpertStore, plan: EPPlan, y_returned, y_shared, out_dtype):
+        return ep_combine(store.ctx, plan, y_returned, y_shared, out_dtype)
+
+
+def moe_forward_ep(store, layer: int, x: torch.Tensor, lw: LayerWeights, group=None, top_k: int = 8,
+                   out_dtype: Optional[torch.dtype] = None, return_routing: bool = False, ops=GpuEPOps):
+    """One MoE block on this rank's tokens x [T, H] with the experts split over the ranks of `group`
+    (torch.distributed; NCCL on GPUs): store holds this rank's block (ExpertStore(expert_range=...)). Same result
+    as moe_forward on one GPU with every expert. The exchange: counts, then rows and pair lists, then result rows
+    back, each one all_to_all_single."""
+    import torch.distributed as dist
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    per = store.experts // world
+    if tuple(store.expert_range) != (rank * per, (rank + 1) * per):
+        raise ValueError(f"rank {rank} of {world} must hold experts [{rank * per}, {(rank + 1) * per})")
+    x = x.contiguous()
+    plan = ops.route_plan(store, x, lw, world, top_k)
+    # counts: what this rank sends to each rank -> what each rank sends here (one host read for the sizes)
+    send_counts = plan.counts.t().contiguous()  # [world, (rows, pairs)]
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    c = torch.cat([send_counts, recv_counts]).cpu()
+    s_rows, s_pairs = c[:world, 0].tolist(), c[:world, 1].tolist()
+    r_rows, r_pairs = c[world:, 0].tolist(), c[world:, 1].tolist()
+    H = x.shape[1]
+    recv_buf = plan.send_buf.new_empty(sum(r_rows), *plan.send_buf.shape[1:])
+    recv_pairs = plan.pair_list.new_empty(sum(r_pairs), 2)
+    dist.all_to_all_single(recv_buf, plan.send_buf[:sum(s_rows)], output_split_sizes=r_rows,
+                           input_split_sizes=s_rows, group=group)
+    dist.all_to_all_single(recv_pairs, plan.pair_list[:sum(s_pairs)], output_split_sizes=r_pairs,
+                           input_split_sizes=s_pairs, group=group)
+    y = ops.experts(store, layer, world, r_rows, r_pairs, recv_buf, recv_pairs, x, lw)
+    P_r = sum(r_pairs)
+    y_ret = y.new_empty(sum(s_pairs), H)
+    dist.all_to_all_single(y_ret, y[:P_r].contiguous(), output_split_sizes=s_pairs, input_split_sizes=r_pairs,
+                           group=group)
+    out = ops.combine(store, plan, y_ret, y[P_r:], out_dtype or x.dtype)
+    return (out, plan.topk_w, plan.topk_idx) if return_routing else out
 
 
 def decode_stack(store: ExpertStore, layers: list, h: torch.Tensor, eps: float = 1e-6, layer_begin: int = 0,
