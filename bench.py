@@ -11,7 +11,8 @@ At N > 1 GPUs (torchrun) every rank serves its own token stream with its own ful
 
 --workload prefill4096: one MoE layer on 4096 bf16 tokens with uniform routing (~128
 tokens per expert) through the tcgen05 grouped GEMMs; tokens/s, with the dominant GEMM launch against the measured
-bf16 tensor peak. At N > 1 every rank runs its own batches (replicas).
+bf16 tensor peak. At N > 1 it is expert-parallel (rank r holds 256/N experts, 4096 tokens per rank per step,
+NCCL all-to-all dispatch and combine).
 
 --impl reference times the CPU restatement of willow's own CPU path (the oracle port; willow's code cannot run
 on the GPU box) on the host cores, on a bounded sample of the same workload.
@@ -204,10 +205,108 @@ def run_decode40(args, rank: int, world: int, dist):
     return result, (ctx, store, layers)
 
 
+def run_prefill4096_ep(args, rank: int, world: int, dist):
+    """configs[3] expert-parallel: rank r holds experts [r * 256 / N, (r + 1) * 256 / N) and routes its own 4096
+    tokens per step (weak scaling); dispatch and combine are NCCL all-to-alls (moe_forward_ep)."""
+    import torch
+    from willow_v2_b200 import moe, synth
+    device = torch.cuda.current_device()
+    ctx = moe.Context(device)
+    per = EXPERTS // world
+    store = moe.ExpertStore(1, EXPERTS, HIDDEN, FFN, ctx=ctx, expert_range=(rank * per, (rank + 1) * per))
+    store.fill_synthetic(SEED)
+    lw = moe.LayerWeights(router_w=torch.from_numpy(synth.router_weight(SEED, 0)).cuda(),
+                          shared_gate=torch.from_numpy(synth.shared_gate_weight(SEED, 0)).cuda(),
+                          shared_gate_up=torch.from_numpy(synth.expert_gate_up(SEED, 0, EXPERTS).reshape(-1)).cuda(),
+                          shared_down=torch.from_numpy(synth.expert_down(SEED, 0, EXPERTS).reshape(-1)).cuda()
+                          ).prepare(ctx, decode=False)
+    K, W = args.steps, args.warmup
+    T = PREFILL_T
+    xs = [torch.from_numpy(synth.hidden(SEED + 1000 * rank, T, step=b)).to(torch.bfloat16).cuda() for b in range(4)]
+    stream = torch.cuda.current_stream()
+    for s in range(W):
+        moe.moe_forward_ep(store, 0, xs[s % 4], lw)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    stats = [dict() for _ in range(K)]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        ev0.record(stream)
+        for s in range(K):
+            moe.moe_forward_ep(store, 0, xs[s % 4], lw, stats=stats[s])
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    gpu_launches = ctx.launches - launches0
+    ms = ev0.elapsed_time(ev1) / K
+    stage = {}
+    for st in stats:
+        evs = st["events"]
+        for (a, ea), (b, eb) in zip(evs, evs[1:]):
+            stage.setdefault(b, []).append(ea.elapsed_time(eb))
+    stage_ms = {k: statistics.mean(v) for k, v in stage.items()}
+    pairs_in = statistics.mean(st["pairs_in"] for st in stats)
+    bytes_out = statistics.mean((st["rows_out"] + st["pairs_out"]) * HIDDEN * 2 for st in stats)
+    ctx.check_device()
+
+    # end to end: pinned bf16 host batch -> device, layer, result -> pinned host, every step
+    x_host = [x.cpu().pin_memory() for x in xs]
+    o_host = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device="cuda")
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(K):
+        x_dev.copy_(x_host[s % 4], non_blocking=True)
+        o_host.copy_(moe.moe_forward_ep(store, 0, x_dev, lw), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    dist.barrier()
+    experts_ms = stage_ms.get("experts", float("nan"))
+    a2a_ms = stage_ms.get("dispatch_a2a", 0.0) + stage_ms.get("combine_a2a", 0.0)
+    times = torch.tensor([ms, e2e_ms, experts_ms, a2a_ms], dtype=torch.float64, device="cuda")
+    dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, experts_ms_max, a2a_ms_max = times.tolist()
+    _, bf16, peak_kind = peaks()
+    flops = (pairs_in + T) * 6_291_456  # this rank's expert products: received pairs + its shared-expert rows
+    tflops = flops / (experts_ms * 1e-3) / 1e12
+    link = 770.0  # GB/s per direction per GPU, measured peer copy on this pool
+    result = {
+        "metric": METRIC_PREFILL, "value": world * T * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 accumulation",
+        "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks with the config-0 distributions; bf16 N(0,1) tokens)",
+        "config": {"workload": "configs[3]: prefill 4096 tokens per rank through one MoE layer, uniform routing",
+                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T * world,
+                   "parallelism": f"ep{world}", "experts_per_rank": per,
+                   "l2": "inputs larger than L2: ~500 MB of activations per rank per step"},
+        "roofline": {"bound": "tensor", "kernel": "expert stage (dispatch + gather + grouped GEMMs), rank 0",
+                     "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16, "traffic": None,
+                     "peak_kind": peak_kind, "algorithmic_flops_per_launch": flops, "launch_ms": experts_ms},
+        "exchange": {"bytes_out_per_step": bytes_out, "a2a_ms_max": a2a_ms_max,
+                     "link_frac": bytes_out * (world - 1) / world / (a2a_ms_max * 1e-3) / 1e9 / link
+                     if a2a_ms_max > 0 else None, "link_gbs_ref": link},
+        "stage_ms_rank0": stage_ms,
+        "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 2,
+                "d2h_bytes_per_step": T * HIDDEN * 2},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks.summary(),
+    }
+    return result, (ctx, store, lw)
+
+
 def run_prefill4096(args, rank: int, world: int, dist):
     import torch
     from willow_v2_b200 import lib as L
     from willow_v2_b200 import moe, synth
+    if world > 1:
+        return run_prefill4096_ep(args, rank, world, dist)
     device = torch.cuda.current_device()
     ctx, store, layers = setup_model(device, 1)
     lw = layers[0].prepare(ctx, decode=False)

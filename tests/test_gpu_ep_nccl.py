@@ -1,0 +1,85 @@
+"""Expert parallelism across real GPUs: one process per GPU (spawned), NCCL all-to-all exchanges through
+moe_forward_ep, each rank holding its block of experts. Every rank's output must equal the single-GPU result for its
+tokens bit for bit. Skipped with fewer than two GPUs (the emulated-rank test covers the kernels on one GPU)."""
+import datetime
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+from willow_v2_b200 import synth
+
+pytestmark = pytest.mark.gpu
+SEED, LAYER, TOKENS_PER_RANK = 0, 0, 1024
+
+
+def _weights(moe, torch, ctx, zipf):
+    return moe.LayerWeights(
+        router_w=torch.from_numpy(synth.router_weight(SEED, LAYER)).cuda(),
+        shared_gate=torch.from_numpy(synth.shared_gate_weight(SEED, LAYER)).cuda(),
+        shared_gate_up=torch.from_numpy(synth.expert_gate_up(SEED, LAYER, 256).reshape(-1)).cuda(),
+        shared_down=torch.from_numpy(synth.expert_down(SEED, LAYER, 256).reshape(-1)).cuda(),
+        router_bias=torch.from_numpy(synth.zipf_bias(SEED)).cuda() if zipf else None).prepare(ctx)
+
+
+def _rank(rank, world, port, outdir, zipf):
+    import torch
+    import torch.distributed as dist
+    from willow_v2_b200 import moe
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        ctx = moe.Context(rank)
+        per = 256 // world
+        store = moe.ExpertStore(1, ctx=ctx, expert_range=(rank * per, (rank + 1) * per))
+        store.fill_synthetic(SEED)
+        lw = _weights(moe, torch, ctx, zipf)
+        x = torch.from_numpy(synth.hidden(SEED, TOKENS_PER_RANK * world, step=33)).to(torch.bfloat16)
+        mine = x[rank * TOKENS_PER_RANK:(rank + 1) * TOKENS_PER_RANK].cuda()
+        outs = [moe.moe_forward_ep(store, LAYER, mine, lw, out_dtype=torch.float32) for _ in range(2)]
+        torch.cuda.synchronize()
+        ctx.check_device()
+        assert torch.equal(outs[0], outs[1])
+        np.save(os.path.join(outdir, f"out{rank}.npy"), outs[0].cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("zipf", [False, True])
+def test_ep_over_nccl_matches_single_gpu(zipf):
+    import torch
+    import torch.multiprocessing as mp
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = 8 if n >= 8 else (4 if n >= 4 else 2)
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rank, args=(world, _free_port(), d, zipf), nprocs=world, start_method="spawn")
+        outs = [np.load(os.path.join(d, f"out{r}.npy")) for r in range(world)]
+    from willow_v2_b200 import moe
+    from willow_v2_b200.lib import lib
+    torch.cuda.set_device(0)
+    ctx = moe.Context(0)
+    full = moe.ExpertStore(1, ctx=ctx)
+    full.fill_synthetic(SEED)
+    lw = _weights(moe, torch, ctx, zipf)
+    x = torch.from_numpy(synth.hidden(SEED, TOKENS_PER_RANK * world, step=33)).to(torch.bfloat16).cuda()
+    prev = lib.wmoe_set_prefill_threshold(ctx.handle, 1)
+    try:
+        ref = moe.moe_forward(full, LAYER, x, lw, out_dtype=torch.float32).cpu().numpy()
+    finally:
+        lib.wmoe_set_prefill_threshold(ctx.handle, prev)
+    for r in range(world):
+        assert np.array_equal(outs[r], ref[r * TOKENS_PER_RANK:(r + 1) * TOKENS_PER_RANK]), r

@@ -353,18 +353,30 @@ class GpuEPOps:
 
 
 def moe_forward_ep(store, layer: int, x: torch.Tensor, lw: LayerWeights, group=None, top_k: int = 8,
-                   out_dtype: Optional[torch.dtype] = None, return_routing: bool = False, ops=GpuEPOps):
+                   out_dtype: Optional[torch.dtype] = None, return_routing: bool = False, ops=GpuEPOps,
+                   stats: Optional[dict] = None):
     """One MoE block on this rank's tokens x [T, H] with the experts split over the ranks of `group`
     (torch.distributed; NCCL on GPUs): store holds this rank's block (ExpertStore(expert_range=...)). Same result
     as moe_forward on one GPU with every expert. The exchange: counts, then rows and pair lists, then result rows
-    back, each one all_to_all_single."""
+    back, each one all_to_all_single. stats (optional dict, GPU only): CUDA events recorded after each stage
+    (stats["events"]: [(stage, event)], the first "start") and the rows / pairs sent and received."""
     import torch.distributed as dist
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     per = store.experts // world
     if tuple(store.expert_range) != (rank * per, (rank + 1) * per):
         raise ValueError(f"rank {rank} of {world} must hold experts [{rank * per}, {(rank + 1) * per})")
+    events = [] if stats is not None else None
+
+    def mark(name):
+        if events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            events.append((name, ev))
+
     x = x.contiguous()
+    mark("start")
     plan = ops.route_plan(store, x, lw, world, top_k)
+    mark("route_plan")
     # counts: what this rank sends to each rank -> what each rank sends here (one host read for the sizes)
     send_counts = plan.counts.t().contiguous()  # [world, (rows, pairs)]
     recv_counts = torch.empty_like(send_counts)
@@ -372,6 +384,7 @@ def moe_forward_ep(store, layer: int, x: torch.Tensor, lw: LayerWeights, group=N
     c = torch.cat([send_counts, recv_counts]).cpu()
     s_rows, s_pairs = c[:world, 0].tolist(), c[:world, 1].tolist()
     r_rows, r_pairs = c[world:, 0].tolist(), c[world:, 1].tolist()
+    mark("counts")
     H = x.shape[1]
     recv_buf = plan.send_buf.new_empty(sum(r_rows), *plan.send_buf.shape[1:])
     recv_pairs = plan.pair_list.new_empty(sum(r_pairs), 2)
@@ -379,12 +392,19 @@ def moe_forward_ep(store, layer: int, x: torch.Tensor, lw: LayerWeights, group=N
                            input_split_sizes=s_rows, group=group)
     dist.all_to_all_single(recv_pairs, plan.pair_list[:sum(s_pairs)], output_split_sizes=r_pairs,
                            input_split_sizes=s_pairs, group=group)
+    mark("dispatch_a2a")
     y = ops.experts(store, layer, world, r_rows, r_pairs, recv_buf, recv_pairs, x, lw)
+    mark("experts")
     P_r = sum(r_pairs)
     y_ret = y.new_empty(sum(s_pairs), H)
     dist.all_to_all_single(y_ret, y[:P_r].contiguous(), output_split_sizes=s_pairs, input_split_sizes=r_pairs,
                            group=group)
+    mark("combine_a2a")
     out = ops.combine(store, plan, y_ret, y[P_r:], out_dtype or x.dtype)
+    mark("combine")
+    if stats is not None:
+        stats.update(events=events, rows_out=sum(s_rows), pairs_out=sum(s_pairs), rows_in=sum(r_rows),
+                     pairs_in=P_r, tokens=x.shape[0])
     return (out, plan.topk_w, plan.topk_idx) if return_routing else out
 
 
