@@ -36,8 +36,10 @@ ROUTER_BYTES = EXPERTS * HIDDEN * 4 + HIDDEN * 4                           # rou
 # DRAM bytes (read + write) per layer of decode_kernel, measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on a 4-layer launch: 82,234,880 + 1,487,360 bytes; traffic grows with the layers
 TRAFFIC_PER_LAYER = (82_234_880 + 1_487_360) / 4
-# DRAM bytes (read + write) of one grouped_gemm_kernel<0> launch at 4096 tokens, measured by ncu; None until captured
-PREFILL_GATE_UP_TRAFFIC = None
+# DRAM bytes (read + write) of one grouped_gemm_kernel<0> launch at 4096 tokens, measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum = 454,209,280 + 31,324,928): the gathered activations (151 MB) and the
+# Q4_K weights (303 MB) read once, h written
+PREFILL_GATE_UP_TRAFFIC = 454_209_280 + 31_324_928
 LAYERS = 40
 SEED = 0
 METRIC = "MoE decode tokens/s (40-layer qwen35moe stack, 1 token per step)"
