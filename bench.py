@@ -209,7 +209,8 @@ def run_decode40(args, rank: int, world: int, dist):
 
 def run_prefill4096_ep(args, rank: int, world: int, dist):
     """configs[3] expert-parallel: rank r holds experts [r * 256 / N, (r + 1) * 256 / N) and routes its own 4096
-    tokens per step (weak scaling); dispatch and combine are NCCL all-to-alls (moe_forward_ep)."""
+    tokens per step (weak scaling); dispatch and combine are NCCL all-to-alls issued by the library
+    (moe_forward_ep_native), with its per-phase CUDA events."""
     import torch
     from willow_v2_b200 import moe, synth
     device = torch.cuda.current_device()
@@ -226,33 +227,40 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
     T = PREFILL_T
     xs = [torch.from_numpy(synth.hidden(SEED + 1000 * rank, T, step=b)).to(torch.bfloat16).cuda() for b in range(4)]
     stream = torch.cuda.current_stream()
+    from willow_v2_b200 import lib as L
+    moe.ep_init(ctx)
     for s in range(W):
-        moe.moe_forward_ep(store, 0, xs[s % 4], lw)
+        moe.moe_forward_ep_native(store, 0, xs[s % 4], lw)
     torch.cuda.synchronize()
     ctx.check_device()
+    # one step through the torch.distributed orchestration for the transfer sizes (not timed)
+    sizes = dict()
+    moe.moe_forward_ep(store, 0, xs[0], lw, stats=sizes)
+    pairs_in = sizes["pairs_in"]
+    bytes_out = (sizes["rows_out"] + sizes["pairs_out"]) * HIDDEN * 2
     dist.barrier()
     torch.cuda.synchronize()
+    L.check(ctx.handle, L.lib.wmoe_set_profiling(ctx.handle, K))
     launches0 = ctx.launches
-    stats = [dict() for _ in range(K)]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device) as clocks:
         ev0.record(stream)
         for s in range(K):
-            moe.moe_forward_ep(store, 0, xs[s % 4], lw, stats=stats[s])
+            moe.moe_forward_ep_native(store, 0, xs[s % 4], lw)
         ev1.record(stream)
         torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
     gpu_launches = ctx.launches - launches0
     ms = ev0.elapsed_time(ev1) / K
-    stage = {}
-    for st in stats:
-        evs = st["events"]
-        for (a, ea), (b, eb) in zip(evs, evs[1:]):
-            stage.setdefault(b, []).append(ea.elapsed_time(eb))
+    stage = {name: [] for name in L.EP_PHASES}
+    for ago in range(K):
+        for p, name in enumerate(L.EP_PHASES):
+            v = L.ctypes.c_float()
+            L.check(ctx.handle, L.lib.wmoe_phase_ms(ctx.handle, ago, p, L.ctypes.byref(v)))
+            stage[name].append(v.value)
+    L.check(ctx.handle, L.lib.wmoe_set_profiling(ctx.handle, 0))
     stage_ms = {k: statistics.mean(v) for k, v in stage.items()}
-    pairs_in = statistics.mean(st["pairs_in"] for st in stats)
-    bytes_out = statistics.mean((st["rows_out"] + st["pairs_out"]) * HIDDEN * 2 for st in stats)
     ctx.check_device()
 
     # end to end: pinned bf16 host batch -> device, layer, result -> pinned host, every step
@@ -265,10 +273,11 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
     e0.record(stream)
     for s in range(K):
         x_dev.copy_(x_host[s % 4], non_blocking=True)
-        o_host.copy_(moe.moe_forward_ep(store, 0, x_dev, lw), non_blocking=True)
+        o_host.copy_(moe.moe_forward_ep_native(store, 0, x_dev, lw), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / K
+    ctx.ep_finalize()
     dist.barrier()
     experts_ms = stage_ms.get("experts", float("nan"))
     a2a_ms = stage_ms.get("dispatch_a2a", 0.0) + stage_ms.get("combine_a2a", 0.0)

@@ -37,6 +37,7 @@ extern "C" {
 #define WMOE_ERR_DEVICE (-4)      /* a kernel reported a bad index or a wait that ran out (device status) */
 #define WMOE_ERR_UNSUPPORTED (-5) /* shape or type this build has no kernel for */
 #define WMOE_ERR_IO (-6)          /* a host-side copy into the store failed or was short */
+#define WMOE_ERR_NCCL (-7)        /* an NCCL call of the expert-parallel path failed */
 
 /* element types of activations */
 #define WMOE_F32 0
@@ -137,7 +138,8 @@ int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, 
  * boundaries on its own stream into slot (call number % calls); calls = 0 turns it off and frees the events.
  * wmoe_phase_ms gives phase `phase` of the call `ago` calls back (0 = the latest): 0 router + top-k, 1 dispatch,
  * 2 gather (GEMM path) or activation quantisation (GEMV path), 3 gate_up, 4 down, 5 combine. It waits for that
- * call's events. */
+ * call's events. wmoe_moe_forward_ep records its own six: 0 route + plan + rows, 1 count exchange and read-back,
+ * 2 dispatch exchange, 3 expert stage, 4 result exchange, 5 combine. */
 #define WMOE_PHASES 6
 int wmoe_set_profiling(wmoe_ctx* ctx, int calls);
 int wmoe_phase_ms(wmoe_ctx* ctx, int ago, int phase, float* ms);
@@ -212,6 +214,21 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
                        int32_t* send_tok /* [T * min(top_k, world)] */, int32_t* pair_list /* [T * top_k, 2] */,
                        int32_t* ret_index /* [T, top_k] */, uint16_t* send_buf /* fp16 [T * min(top_k, world), hidden] */,
                        void* stream);
+/* The same layer in one call over the library's own NCCL communicator (grouped ncclSend/ncclRecv for every
+ * exchange, one host read of the transfer sizes per layer): each rank passes its own tokens and gets their outputs,
+ * identical to wmoe_moe_forward on one GPU. wmoe_ep_unique_id (one rank) makes the id every rank passes to
+ * wmoe_ep_init(ctx, id, rank, world), which creates the communicator (collectively); wmoe_ep_finalize (or
+ * wmoe_destroy) frees it. NCCL is loaded at run time (libnccl.so.2); without it wmoe_ep_init returns
+ * WMOE_ERR_UNSUPPORTED. Arguments of wmoe_moe_forward_ep as in wmoe_moe_forward_layer; store from
+ * wmoe_store_create_range holding this rank's block. */
+int wmoe_ep_unique_id(void* out /* WMOE_EP_ID_BYTES */);
+#define WMOE_EP_ID_BYTES 128
+int wmoe_ep_init(wmoe_ctx* ctx, const void* unique_id, int rank, int world);
+int wmoe_ep_finalize(wmoe_ctx* ctx);
+int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                        const wmoe_layer_weights* weights, void* out, int out_dtype, int32_t* topk_idx_out,
+                        float* topk_w_out, void* stream);
+
 /* recv_rows / recv_pairs: HOST arrays [world] (what each rank sent here); recv_buf fp16 [sum recv_rows, hidden];
  * recv_pair_list [sum recv_pairs, 2]; x [T, hidden] this rank's own tokens; y fp16 [sum recv_pairs + T, hidden]. */
 int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, const int32_t* recv_rows,

@@ -1,6 +1,8 @@
 """Expert parallelism across real GPUs: one process per GPU (spawned), NCCL all-to-all exchanges through
 moe_forward_ep, each rank holding its block of experts. Every rank's output must equal the single-GPU result for its
-tokens bit for bit. Skipped with fewer than two GPUs (the emulated-rank test covers the kernels on one GPU)."""
+tokens bit for bit, through the torch.distributed orchestration (moe_forward_ep) and through the library's own NCCL
+communicator (moe_forward_ep_native). Skipped with fewer than two GPUs (the emulated-rank test covers the kernels on
+one GPU)."""
 import datetime
 import os
 import socket
@@ -24,7 +26,7 @@ def _weights(moe, torch, ctx, zipf):
         router_bias=torch.from_numpy(synth.zipf_bias(SEED)).cuda() if zipf else None).prepare(ctx)
 
 
-def _rank(rank, world, port, outdir, zipf):
+def _rank(rank, world, port, outdir, zipf, native):
     import torch
     import torch.distributed as dist
     from willow_v2_b200 import moe
@@ -41,9 +43,19 @@ def _rank(rank, world, port, outdir, zipf):
         lw = _weights(moe, torch, ctx, zipf)
         x = torch.from_numpy(synth.hidden(SEED, TOKENS_PER_RANK * world, step=33)).to(torch.bfloat16)
         mine = x[rank * TOKENS_PER_RANK:(rank + 1) * TOKENS_PER_RANK].cuda()
-        outs = [moe.moe_forward_ep(store, LAYER, mine, lw, out_dtype=torch.float32) for _ in range(2)]
+        if native:
+            moe.ep_init(ctx)
+            outs = [moe.moe_forward_ep_native(store, LAYER, mine, lw, out_dtype=torch.float32) for _ in range(2)]
+            # a rank with no tokens still takes part in every exchange
+            empty = moe.moe_forward_ep_native(store, LAYER, mine[:0], lw, out_dtype=torch.float32) if rank == 1 \
+                else moe.moe_forward_ep_native(store, LAYER, mine, lw, out_dtype=torch.float32)
+            assert empty.shape[0] == (0 if rank == 1 else TOKENS_PER_RANK)
+        else:
+            outs = [moe.moe_forward_ep(store, LAYER, mine, lw, out_dtype=torch.float32) for _ in range(2)]
         torch.cuda.synchronize()
         ctx.check_device()
+        if native:
+            ctx.ep_finalize()
         assert torch.equal(outs[0], outs[1])
         np.save(os.path.join(outdir, f"out{rank}.npy"), outs[0].cpu().numpy())
         dist.barrier()
@@ -57,8 +69,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("zipf", [False, True])
-def test_ep_over_nccl_matches_single_gpu(zipf):
+@pytest.mark.parametrize("zipf,native", [(False, False), (True, False), (False, True), (True, True)])
+def test_ep_over_nccl_matches_single_gpu(zipf, native):
     import torch
     import torch.multiprocessing as mp
     n = torch.cuda.device_count()
@@ -66,7 +78,7 @@ def test_ep_over_nccl_matches_single_gpu(zipf):
         pytest.skip("needs at least two GPUs")
     world = 8 if n >= 8 else (4 if n >= 4 else 2)
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_rank, args=(world, _free_port(), d, zipf), nprocs=world, start_method="spawn")
+        mp.start_processes(_rank, args=(world, _free_port(), d, zipf, native), nprocs=world, start_method="spawn")
         outs = [np.load(os.path.join(d, f"out{r}.npy")) for r in range(world)]
     from willow_v2_b200 import moe
     from willow_v2_b200.lib import lib

@@ -1,5 +1,9 @@
 // The C ABI of include/wmoe.h: argument checks, scratch planning and the order of launches. Kernels live in
 // dequant.cu, route.cu, dispatch.cu, gemv.cu, decode.cu and store.cu.
+#include <dlfcn.h>
+#include <cstring>
+#include <nccl.h>
+
 #include <algorithm>
 #include <string>
 #include <vector>
@@ -89,12 +93,14 @@ int wmoe_init(int device, wmoe_ctx** out) {
 }
 
 static void free_profiling(wmoe_ctx* ctx);
+static void ep_release(wmoe_ctx* ctx);
 
 void wmoe_destroy(wmoe_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
   free_profiling(ctx);
+  ep_release(ctx);
   cudaFree(ctx->scratch);
   cudaFree(ctx->d_status);
   delete ctx;
@@ -552,6 +558,7 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
   const bool tc = use_router_tc(w->router_split, x_dtype, T, hidden, experts);
   Plan plan;
   const size_t o_logits = plan.take<float>(router_logit_floats(tc, T, experts));
+  const size_t o_plan = plan.take<char>(ep_plan_scratch_bytes(T, world));
   if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
   int n = 0;
   WMOE_CHECK_CUDA(ctx,
@@ -561,7 +568,7 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
                   "router");
   WMOE_CHECK_CUDA(ctx,
                   ep_plan(topk_idx, T, top_k, experts, world, send_rows, send_pairs, send_tok, pair_list, ret_index,
-                          ctx->d_status, st, &n),
+                          at<void>(ctx, o_plan), ctx->d_status, st, &n),
                   "wmoe_ep_route_plan: plan");
   WMOE_CHECK_CUDA(ctx,
                   ep_pack(x, x_dtype, hidden, send_tok, send_rows, world, T * std::min(top_k, world), send_buf, st, &n),
@@ -570,30 +577,34 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
   return WMOE_OK;
 }
 
-int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, const int32_t* recv_rows,
-                    const int32_t* recv_pairs, const uint16_t* recv_buf, const int32_t* recv_pair_list,
-                    const void* x, int x_dtype, int T, const wmoe_layer_weights* w, uint16_t* y, void* stream) {
-  if (!ctx) return WMOE_ERR_INVALID;
-  if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad store");
-  if (world < 1 || world > kMaxRanks || !recv_rows || !recv_pairs || layer < 0 || layer >= store->layers || T < 0 ||
-      (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16))
-    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad arguments");
-  if (int rc = check_layer(ctx, w, "wmoe_ep_experts")) return rc;
+// Scratch of the expert stage of an expert-parallel layer: P_r received pairs, T own tokens.
+static size_t ep_experts_scratch_bytes(int P_r, int T, int E, int H, int F) {
+  Plan plan;
+  const size_t P = size_t(P_r) + size_t(T);
+  plan.take<int32_t>(size_t(P_r));                   // pair_row
+  plan.take<int32_t>(size_t(P_r));                   // pair_exp
+  plan.take<int32_t>(size_t(E));                     // counts
+  plan.take<int32_t>(size_t(E) + 1);                 // offsets
+  plan.take<int32_t>(size_t(P_r));                   // perm
+  plan.take<int32_t>(size_t(P_r));                   // pos
+  plan.take<int32_t>(size_t(E) + 1);                 // used
+  plan.take<int32_t>(size_t(E) + 2);                 // seg
+  plan.take<int32_t>(1);                             // n_used
+  plan.take<char>(dispatch_scratch_bytes(P_r, E));   // dispatch
+  plan.take<uint16_t>(P * H);                        // xg
+  plan.take<char>(prefill_gemm_scratch_bytes(P, E, H, F));
+  return plan.bytes;
+}
+
+static int ep_experts_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, const int32_t* recv_rows,
+                           const int32_t* recv_pairs, const uint16_t* recv_buf, const int32_t* recv_pair_list,
+                           const void* x, int x_dtype, int T, const wmoe_layer_weights* w, uint16_t* y,
+                           char* scratch, cudaStream_t st) {
   const int H = store->hidden, F = store->ffn, E = store->experts;
-  if (H != 2048 || F != 512) return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_ep_experts: this build runs hidden 2048, ffn 512");
-  long long R = 0, Pr = 0;
-  for (int s = 0; s < world; ++s) {
-    if (recv_rows[s] < 0 || recv_pairs[s] < 0) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad counts");
-    R += recv_rows[s];
-    Pr += recv_pairs[s];
-  }
-  if (Pr + T > (1ll << 30) || Pr > R * 8) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad counts");
-  if (Pr + T == 0) return WMOE_OK;
-  if (!y || (T > 0 && !x) || (Pr > 0 && (!recv_buf || !recv_pair_list)))
-    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: null pointer");
-  const int P_r = int(Pr);
-  const size_t P = size_t(Pr) + size_t(T);
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int P_r = 0;
+  for (int s = 0; s < world; ++s) P_r += recv_pairs[s];
+  const size_t P = size_t(P_r) + size_t(T);
+  if (P == 0) return WMOE_OK;
   Plan plan;
   const size_t o_row = plan.take<int32_t>(size_t(P_r));
   const size_t o_exp = plan.take<int32_t>(size_t(P_r));
@@ -607,12 +618,12 @@ int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, cons
   const size_t o_disp = plan.take<char>(dispatch_scratch_bytes(P_r, E));
   const size_t o_xg = plan.take<uint16_t>(P * H);
   const size_t o_gemm = plan.take<char>(prefill_gemm_scratch_bytes(P, E, H, F));
-  if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
+  auto sp = [&](size_t off) { return static_cast<void*>(scratch + off); };
   int n = 0;
-  int32_t* pair_row = at<int32_t>(ctx, o_row);
-  int32_t* pair_exp = at<int32_t>(ctx, o_exp);
+  int32_t* pair_row = static_cast<int32_t*>(sp(o_row));
+  int32_t* pair_exp = static_cast<int32_t*>(sp(o_exp));
   WMOE_CHECK_CUDA(ctx, ep_fixup(recv_pair_list, P_r, world, recv_rows, recv_pairs, pair_row, pair_exp, st, &n),
-                  "wmoe_ep_experts: pair lists");
+                  "expert stage: pair lists");
   std::vector<int32_t> experts_used;
   if (store->capped && P_r > 0) {
     // the store must copy the received pairs' experts in first: one wait for the pair list
@@ -629,29 +640,65 @@ int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, cons
   pm.T = P_r;
   pm.k = 1;
   pm.E = E;
-  pm.perm = at<int32_t>(ctx, o_perm);
-  pm.pos = at<int32_t>(ctx, o_pos);
-  pm.used = at<int32_t>(ctx, o_used);
-  pm.seg = at<int32_t>(ctx, o_seg);
-  pm.n_used = at<int32_t>(ctx, o_nused);
+  pm.perm = static_cast<int32_t*>(sp(o_perm));
+  pm.pos = static_cast<int32_t*>(sp(o_pos));
+  pm.used = static_cast<int32_t*>(sp(o_used));
+  pm.seg = static_cast<int32_t*>(sp(o_seg));
+  pm.n_used = static_cast<int32_t*>(sp(o_nused));
   WMOE_CHECK_CUDA(ctx,
-                  dispatch_rows(pair_exp, P_r, 1, E, T, at<void>(ctx, o_disp), at<int32_t>(ctx, o_counts),
-                                at<int32_t>(ctx, o_offsets), at<int32_t>(ctx, o_perm), at<int32_t>(ctx, o_pos),
-                                at<int32_t>(ctx, o_used), at<int32_t>(ctx, o_seg), at<int32_t>(ctx, o_nused), nullptr,
-                                ctx->d_status, st, &n),
-                  "wmoe_ep_experts: dispatch");
-  __half* xg = at<__half>(ctx, o_xg);
+                  dispatch_rows(pair_exp, P_r, 1, E, T, sp(o_disp), static_cast<int32_t*>(sp(o_counts)),
+                                static_cast<int32_t*>(sp(o_offsets)), const_cast<int32_t*>(pm.perm),
+                                const_cast<int32_t*>(pm.pos), const_cast<int32_t*>(pm.used),
+                                const_cast<int32_t*>(pm.seg), const_cast<int32_t*>(pm.n_used), nullptr, ctx->d_status,
+                                st, &n),
+                  "expert stage: dispatch");
+  __half* xg = static_cast<__half*>(sp(o_xg));
   WMOE_CHECK_CUDA(ctx, ep_gather(pm.perm, pair_row, P_r, recv_buf, x, x_dtype, T, H, xg, st, &n),
-                  "wmoe_ep_experts: gather");
+                  "expert stage: gather");
   const ExpertSource src = store_source(store, w->shared_gate_up, w->shared_down);
   WMOE_CHECK_CUDA(ctx,
-                  prefill_gemms(src, layer, pm, P, H, F, xg, reinterpret_cast<__half*>(y), pm.perm, P_r,
-                                at<void>(ctx, o_gemm), ctx->sm_count, ctx->d_status, nullptr, st, &n),
-                  "wmoe_ep_experts: grouped GEMM");
+                  prefill_gemms(src, layer, pm, P, H, F, xg, reinterpret_cast<__half*>(y), pm.perm, P_r, sp(o_gemm),
+                                ctx->sm_count, ctx->d_status, nullptr, st, &n),
+                  "expert stage: grouped GEMM");
   ctx->launches += uint64_t(n);
   if (store->capped && !experts_used.empty())
     if (int rc = store_mark_used(store, layer, experts_used.data(), int(experts_used.size()), st)) return rc;
   return WMOE_OK;
+}
+
+static int check_ep_counts(wmoe_ctx* ctx, int world, const int32_t* recv_rows, const int32_t* recv_pairs, int T,
+                           const char* fn) {
+  long long R = 0, Pr = 0;
+  for (int s = 0; s < world; ++s) {
+    if (recv_rows[s] < 0 || recv_pairs[s] < 0) return ctx_fail(ctx, WMOE_ERR_INVALID, std::string(fn) + ": bad counts");
+    R += recv_rows[s];
+    Pr += recv_pairs[s];
+  }
+  if (Pr + T > (1ll << 30) || Pr > R * 8) return ctx_fail(ctx, WMOE_ERR_INVALID, std::string(fn) + ": bad counts");
+  return WMOE_OK;
+}
+
+int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, const int32_t* recv_rows,
+                    const int32_t* recv_pairs, const uint16_t* recv_buf, const int32_t* recv_pair_list,
+                    const void* x, int x_dtype, int T, const wmoe_layer_weights* w, uint16_t* y, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad store");
+  if (world < 1 || world > kMaxRanks || !recv_rows || !recv_pairs || layer < 0 || layer >= store->layers || T < 0 ||
+      (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: bad arguments");
+  if (int rc = check_layer(ctx, w, "wmoe_ep_experts")) return rc;
+  if (store->hidden != 2048 || store->ffn != 512)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_ep_experts: this build runs hidden 2048, ffn 512");
+  if (int rc = check_ep_counts(ctx, world, recv_rows, recv_pairs, T, "wmoe_ep_experts")) return rc;
+  int P_r = 0, R = 0;
+  for (int s = 0; s < world; ++s) P_r += recv_pairs[s], R += recv_rows[s];
+  if (P_r + T == 0) return WMOE_OK;
+  if (!y || (T > 0 && !x) || (P_r > 0 && (!recv_buf || !recv_pair_list)))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_experts: null pointer");
+  if (int rc = ensure_scratch(ctx, ep_experts_scratch_bytes(P_r, T, store->experts, store->hidden, store->ffn)))
+    return rc;
+  return ep_experts_impl(ctx, store, layer, world, recv_rows, recv_pairs, recv_buf, recv_pair_list, x, x_dtype, T, w, y,
+                         static_cast<char*>(ctx->scratch), static_cast<cudaStream_t>(stream));
 }
 
 int wmoe_ep_combine(wmoe_ctx* ctx, int T, int top_k, int hidden, const int32_t* topk_idx, const float* topk_w,
@@ -669,6 +716,263 @@ int wmoe_ep_combine(wmoe_ctx* ctx, int T, int top_k, int hidden, const int32_t* 
                                reinterpret_cast<const __half*>(y_returned), reinterpret_cast<const __half*>(y_shared),
                                out, out_dtype, static_cast<cudaStream_t>(stream), &n),
                   "wmoe_ep_combine");
+  ctx->launches += uint64_t(n);
+  return WMOE_OK;
+}
+
+// ---- expert parallelism over the library's own NCCL communicator ----------------------------------------------
+// NCCL is resolved at run time (dlopen of libnccl.so.2, reusing the copy already loaded in the process, e.g. by
+// torch), so the library loads without it and only wmoe_ep_init needs it.
+struct NcclApi {
+  bool tried = false, ok = false;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+static NcclApi& nccl() {
+  static NcclApi api;
+  if (!api.tried) {
+    api.tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      auto get = [&](const char* n) { return dlsym(h, n); };
+      api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(get("ncclGetUniqueId"));
+      api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(get("ncclCommInitRank"));
+      api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(get("ncclCommDestroy"));
+      api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(get("ncclGroupStart"));
+      api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(get("ncclGroupEnd"));
+      api.Send = reinterpret_cast<decltype(api.Send)>(get("ncclSend"));
+      api.Recv = reinterpret_cast<decltype(api.Recv)>(get("ncclRecv"));
+      api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(get("ncclGetErrorString"));
+      api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.GroupStart && api.GroupEnd && api.Send &&
+               api.Recv && api.GetErrorString;
+    }
+  }
+  return api;
+}
+
+static int nccl_fail(wmoe_ctx* ctx, ncclResult_t r, const char* where) {
+  return ctx_fail(ctx, WMOE_ERR_NCCL, std::string(where) + ": " + nccl().GetErrorString(r));
+}
+
+#define WMOE_CHECK_NCCL(ctx, call, where)                   \
+  do {                                                      \
+    const ncclResult_t r_ = (call);                         \
+    if (r_ != ncclSuccess) return nccl_fail(ctx, r_, where); \
+  } while (0)
+
+int wmoe_ep_unique_id(void* out) {
+  if (!out) return WMOE_ERR_INVALID;
+  if (!nccl().ok) return WMOE_ERR_UNSUPPORTED;
+  ncclUniqueId id;
+  if (nccl().GetUniqueId(&id) != ncclSuccess) return WMOE_ERR_NCCL;
+  memcpy(out, &id, sizeof(id));
+  return WMOE_OK;
+}
+
+int wmoe_ep_init(wmoe_ctx* ctx, const void* unique_id, int rank, int world) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!unique_id || world < 1 || world > WMOE_MAX_RANKS || rank < 0 || rank >= world)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_init: bad rank / world");
+  if (!nccl().ok) return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_ep_init: libnccl.so.2 not available");
+  if (ctx->nccl_comm) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_init: already initialised");
+  WMOE_CHECK_CUDA(ctx, cudaSetDevice(ctx->device), "wmoe_ep_init");
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  ncclComm_t comm = nullptr;
+  WMOE_CHECK_NCCL(ctx, nccl().CommInitRank(&comm, world, id, rank), "wmoe_ep_init");
+  ctx->nccl_comm = comm;
+  ctx->ep_rank = rank;
+  ctx->ep_world = world;
+  return WMOE_OK;
+}
+
+static void ep_release(wmoe_ctx* ctx) {
+  if (ctx->nccl_comm) nccl().CommDestroy(static_cast<ncclComm_t>(ctx->nccl_comm));
+  ctx->nccl_comm = nullptr;
+  ctx->ep_world = 0;
+  cudaFree(ctx->ep_buf);
+  ctx->ep_buf = nullptr;
+  ctx->ep_buf_bytes = 0;
+}
+
+int wmoe_ep_finalize(wmoe_ctx* ctx) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  WMOE_CHECK_CUDA(ctx, cudaDeviceSynchronize(), "wmoe_ep_finalize");
+  ep_release(ctx);
+  return WMOE_OK;
+}
+
+static int ensure_ep_buf(wmoe_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->ep_buf_bytes) return WMOE_OK;
+  if (ctx->ep_buf) {
+    WMOE_CHECK_CUDA(ctx, cudaDeviceSynchronize(), "EP buffer resize");
+    cudaFree(ctx->ep_buf);
+    ctx->ep_buf = nullptr;
+    ctx->ep_buf_bytes = 0;
+  }
+  const size_t grown = std::max(bytes + bytes / 4, size_t(1) << 24);
+  WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->ep_buf, grown), "EP buffer allocation");
+  ctx->ep_buf_bytes = grown;
+  return WMOE_OK;
+}
+
+// One all-to-all-v round on the communicator: block d of `send` (send_n[d] elements) goes to rank d, block s of `recv`
+// (recv_n[s] elements) comes from rank s; blocks in rank order, counts in elements of `type`.
+static int ep_alltoallv(wmoe_ctx* ctx, const void* send, const int64_t* send_n, void* recv, const int64_t* recv_n,
+                        ncclDataType_t type, size_t elem, cudaStream_t st, const char* where) {
+  const NcclApi& api = nccl();
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
+  size_t so = 0, ro = 0;
+  WMOE_CHECK_NCCL(ctx, api.GroupStart(), where);
+  for (int d = 0; d < ctx->ep_world; ++d) {
+    if (send_n[d] > 0)
+      WMOE_CHECK_NCCL(ctx, api.Send(static_cast<const char*>(send) + so * elem, size_t(send_n[d]), type, d, comm, st), where);
+    if (recv_n[d] > 0)
+      WMOE_CHECK_NCCL(ctx, api.Recv(static_cast<char*>(recv) + ro * elem, size_t(recv_n[d]), type, d, comm, st), where);
+    so += size_t(send_n[d]);
+    ro += size_t(recv_n[d]);
+  }
+  WMOE_CHECK_NCCL(ctx, api.GroupEnd(), where);
+  return WMOE_OK;
+}
+
+int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                        const wmoe_layer_weights* w, void* out, int out_dtype, int32_t* topk_idx_out,
+                        float* topk_w_out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!ctx->nccl_comm) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: call wmoe_ep_init first");
+  if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: bad store");
+  const int world = ctx->ep_world, rank = ctx->ep_rank, E = store->experts, H = store->hidden, F = store->ffn;
+  if (E % world || store->expert_begin != rank * (E / world) || store->expert_end != (rank + 1) * (E / world))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: the store must hold this rank's block of experts");
+  if (layer < 0 || layer >= store->layers || T < 0 || top_k != 8 || H != 2048 || F != 512 ||
+      (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16) || (out_dtype != WMOE_F32 && out_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: bad layer, shape or dtype");
+  if (int rc = check_layer(ctx, w, "wmoe_moe_forward_ep")) return rc;
+  if (T > 0 && (!x || !out)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: null pointer");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int k = top_k, max_rows = T * std::min(k, world);
+  // stage A (sized by T) in the context scratch
+  const bool tc = use_router_tc(w->router_split, x_dtype, T, H, E);
+  Plan pa;
+  const size_t o_logits = pa.take<float>(std::max<size_t>(router_logit_floats(tc, T, E), 1));
+  const size_t o_w = pa.take<float>(size_t(T) * k + 1);
+  const size_t o_idx = pa.take<int32_t>(size_t(T) * k + 1);
+  const size_t o_s = pa.take<float>(size_t(T) + 1);
+  const size_t o_cnt = pa.take<int32_t>(size_t(4) * world);  // send rows, send pairs, recv rows, recv pairs
+  const size_t o_tok = pa.take<int32_t>(size_t(max_rows) + 1);
+  const size_t o_pl = pa.take<int32_t>(size_t(T) * k * 2 + 2);
+  const size_t o_ret = pa.take<int32_t>(size_t(T) * k + 1);
+  const size_t o_send = pa.take<uint16_t>(size_t(max_rows) * H + 8);
+  const size_t o_plan = pa.take<char>(ep_plan_scratch_bytes(std::max(T, 1), world));
+  if (int rc = ensure_scratch(ctx, pa.bytes)) return rc;
+  int n = 0;
+  // opt-in phase marks (wmoe_set_profiling): start, planned, counts known, rows arrived, experts, rows back, combined
+  cudaEvent_t* marks = ctx->profile_calls > 0
+                           ? &ctx->prof_events[size_t(ctx->profile_seq % uint64_t(ctx->profile_calls)) *
+                                               wmoe_ctx::kProfMarks]
+                           : nullptr;
+  auto mark = [&](int i) {
+    if (marks) cudaEventRecord(marks[i], st);
+  };
+  mark(0);
+  float* topk_w = at<float>(ctx, o_w);
+  int32_t* topk_idx = at<int32_t>(ctx, o_idx);
+  float* shared_s = at<float>(ctx, o_s);
+  int32_t* cnt = at<int32_t>(ctx, o_cnt);
+  int32_t* pair_list = at<int32_t>(ctx, o_pl);
+  int32_t* ret_index = at<int32_t>(ctx, o_ret);
+  uint16_t* send_buf = at<uint16_t>(ctx, o_send);
+  if (T > 0) {
+    WMOE_CHECK_CUDA(ctx,
+                    route_tokens(tc, x, x_dtype, T, H, E, k, w->router_w, w->router_bias, w->shared_gate,
+                                 w->router_split, at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status,
+                                 st, &n),
+                    "router");
+    WMOE_CHECK_CUDA(ctx,
+                    ep_plan(topk_idx, T, k, E, world, cnt, cnt + world, at<int32_t>(ctx, o_tok), pair_list, ret_index,
+                            at<void>(ctx, o_plan), ctx->d_status, st, &n),
+                    "EP plan");
+    WMOE_CHECK_CUDA(ctx, ep_pack(x, x_dtype, H, at<int32_t>(ctx, o_tok), cnt, world, max_rows, send_buf, st, &n),
+                    "EP rows");
+  } else {
+    WMOE_CHECK_CUDA(ctx, cudaMemsetAsync(cnt, 0, 2 * world * sizeof(int32_t), st), "EP plan");
+  }
+  mark(1);
+  // counts: (rows, pairs) to each rank -> from each rank; one read of all four arrays for the transfer sizes
+  {
+    std::vector<int64_t> one(static_cast<size_t>(world), 1);
+    if (int rc = ep_alltoallv(ctx, cnt, one.data(), cnt + 2 * world, one.data(), ncclInt32, 4, st, "EP counts"))
+      return rc;
+    if (int rc = ep_alltoallv(ctx, cnt + world, one.data(), cnt + 3 * world, one.data(), ncclInt32, 4, st, "EP counts"))
+      return rc;
+  }
+  std::vector<int32_t> c(size_t(4) * world);
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(c.data(), cnt, c.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+                  "EP counts read-back");
+  WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "EP counts read-back");
+  mark(2);
+  const int32_t *s_rows = c.data(), *s_pairs = c.data() + world, *r_rows = c.data() + 2 * world,
+                *r_pairs = c.data() + 3 * world;
+  if (int rc = check_ep_counts(ctx, world, r_rows, r_pairs, T, "wmoe_moe_forward_ep")) return rc;
+  long long R = 0, P_r = 0, S_pairs = 0;
+  for (int d = 0; d < world; ++d) R += r_rows[d], P_r += r_pairs[d], S_pairs += s_pairs[d];
+  // stage B (sized by what arrives) in the EP buffer; growing it only after the read-back above is safe
+  Plan pb;
+  const size_t o_recv = pb.take<uint16_t>(size_t(R) * H + 8);
+  const size_t o_rpl = pb.take<int32_t>(size_t(P_r) * 2 + 2);
+  const size_t o_y = pb.take<uint16_t>((size_t(P_r) + T) * H + 8);
+  const size_t o_yret = pb.take<uint16_t>(size_t(S_pairs) * H + 8);
+  const size_t o_es = pb.take<char>(ep_experts_scratch_bytes(int(P_r), T, E, H, F));
+  if (int rc = ensure_ep_buf(ctx, pb.bytes)) return rc;
+  char* eb = static_cast<char*>(ctx->ep_buf);
+  uint16_t* recv_buf = reinterpret_cast<uint16_t*>(eb + o_recv);
+  int32_t* recv_pl = reinterpret_cast<int32_t*>(eb + o_rpl);
+  uint16_t* y = reinterpret_cast<uint16_t*>(eb + o_y);
+  uint16_t* y_ret = reinterpret_cast<uint16_t*>(eb + o_yret);
+  std::vector<int64_t> sn(static_cast<size_t>(world)), rn(static_cast<size_t>(world));
+  for (int d = 0; d < world; ++d) sn[d] = int64_t(s_rows[d]) * H, rn[d] = int64_t(r_rows[d]) * H;
+  if (int rc = ep_alltoallv(ctx, send_buf, sn.data(), recv_buf, rn.data(), ncclHalf, 2, st, "EP dispatch rows"))
+    return rc;
+  for (int d = 0; d < world; ++d) sn[d] = int64_t(s_pairs[d]) * 2, rn[d] = int64_t(r_pairs[d]) * 2;
+  if (int rc = ep_alltoallv(ctx, pair_list, sn.data(), recv_pl, rn.data(), ncclInt32, 4, st, "EP dispatch pairs"))
+    return rc;
+  mark(3);
+  ctx->launches += uint64_t(n);
+  n = 0;
+  if (int rc = ep_experts_impl(ctx, store, layer, world, r_rows, r_pairs, recv_buf, recv_pl, x, x_dtype, T, w, y,
+                               eb + o_es, st))
+    return rc;
+  mark(4);
+  // result rows back: block s of y (r_pairs[s] rows) to rank s; block d of y_ret (s_pairs[d] rows) from rank d
+  for (int d = 0; d < world; ++d) sn[d] = int64_t(r_pairs[d]) * H, rn[d] = int64_t(s_pairs[d]) * H;
+  if (int rc = ep_alltoallv(ctx, y, sn.data(), y_ret, rn.data(), ncclHalf, 2, st, "EP combine rows")) return rc;
+  mark(5);
+  if (T > 0) {
+    WMOE_CHECK_CUDA(ctx,
+                    combine_rows(T, k, H, topk_idx, topk_w, ret_index, shared_s, reinterpret_cast<const __half*>(y_ret),
+                                 reinterpret_cast<const __half*>(y) + size_t(P_r) * H, out, out_dtype, st, &n),
+                    "EP combine");
+    if (topk_idx_out)
+      WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_idx_out, topk_idx, size_t(T) * k * sizeof(int32_t),
+                                           cudaMemcpyDeviceToDevice, st),
+                      "routing copy");
+    if (topk_w_out)
+      WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_w_out, topk_w, size_t(T) * k * sizeof(float), cudaMemcpyDeviceToDevice,
+                                           st),
+                      "routing copy");
+  }
+  mark(6);
+  if (marks) ++ctx->profile_seq;
   ctx->launches += uint64_t(n);
   return WMOE_OK;
 }

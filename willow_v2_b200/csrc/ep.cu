@@ -5,7 +5,7 @@
 // on one GPU, so the result does not depend on the number of ranks. willow runs on one device and has no
 // counterpart; the exchange is the dispatch/combine all-to-all of the expert-parallel configurations.
 //
-// Home side:  ep_plan (counts, send order, pair lists, where each pick's result row comes back) and ep_pack (rows).
+// Home side:  ep_plan (three passes over tiles of 256 tokens: counts, a scan over tiles, placement) and ep_pack.
 // Expert side: ep_fixup (received pair lists -> global row numbers), dispatch by expert, ep_gather, the GEMMs with
 // the down output written in the order the pairs arrived.
 #include <algorithm>
@@ -17,13 +17,12 @@ namespace wmoe {
 
 namespace {
 
-constexpr int kPlanThreads = 512;
+constexpr int kPlanTile = 256;  // tokens per CTA of the plan's counting and placing passes
 
-// Exclusive scan of one value per thread over a block of kPlanThreads threads (16 warps).
-__device__ int plan_scan(int v, int* total) {
-  __shared__ int warp_tot[32];
+// Inclusive scan of one value per thread over a block of kPlanTile threads (8 warps); *total = block sum.
+__device__ int tile_scan_incl(int v, int* total) {
+  __shared__ int warp_tot[kPlanTile / 32];
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-  constexpr int nwarps = kPlanThreads / 32;
   int incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -32,107 +31,143 @@ __device__ int plan_scan(int v, int* total) {
   }
   if (lane == 31) warp_tot[warp] = incl;
   __syncthreads();
-  if (warp == 0) {
-    const int w = lane < nwarps ? warp_tot[lane] : 0;
-    int wi = w;
+  int before = 0, sum = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += n;
-    }
-    if (lane < nwarps) warp_tot[lane] = wi - w;
-    if (lane == nwarps - 1) warp_tot[31] = wi;
+  for (int w = 0; w < kPlanTile / 32; ++w) {
+    before += w < warp ? warp_tot[w] : 0;
+    sum += warp_tot[w];
   }
   __syncthreads();
-  const int r = warp_tot[warp] + incl - v;
-  *total = warp_tot[31];
-  __syncthreads();
-  return r;
+  *total = sum;
+  return before + incl;
 }
 
-// One CTA. Thread i takes tokens [i * chunk, (i + 1) * chunk). Rows to rank d are its tokens with a pick on d, in
-// token order; pairs to d are those picks in (token, slot) order, which is also the order of the result rows d
-// sends back. ret_index[t][j]: position of pick (t, j)'s result row among all result rows this rank receives
-// (blocks of send_pairs[d] in rank order).
-__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __restrict__ idx, int T, int k, int E,
-                                                               int world, int32_t* __restrict__ send_rows,
-                                                               int32_t* __restrict__ send_pairs,
-                                                               int32_t* __restrict__ send_tok,
-                                                               int2* __restrict__ pair_list,
-                                                               int32_t* __restrict__ ret_index, int* status) {
-  __shared__ int base_r[kMaxRanks], base_p[kMaxRanks];
-  const int per = E / world;
-  const int chunk = (T + kPlanThreads - 1) / kPlanThreads;
-  const int t0 = min(T, int(threadIdx.x) * chunk), t1 = min(T, t0 + chunk);
-  int rows[kMaxRanks], pairs[kMaxRanks];
+// Pass 1: per tile of 256 tokens and destination rank d, the tokens with a pick on d (rows) and those picks
+// (pairs): tile_counts[tile][d] = rows | pairs << 12 (a tile has <= 256 rows and <= 2048 pairs per rank).
+__global__ void __launch_bounds__(kPlanTile) ep_count_kernel(const int32_t* __restrict__ idx, int T, int k, int E,
+                                                             int world, int32_t* __restrict__ tile_counts,
+                                                             int* status) {
+  const int t = blockIdx.x * kPlanTile + threadIdx.x, per = E / world;
+  int packed[kMaxRanks];
 #pragma unroll
-  for (int d = 0; d < kMaxRanks; ++d) rows[d] = pairs[d] = 0;
-  for (int t = t0; t < t1; ++t) {
-    unsigned mask = 0;
-    for (int j = 0; j < k; ++j) {
-      const int e = idx[size_t(t) * k + j];
-      if (e < 0 || e >= E) continue;
-      mask |= 1u << (e / per);
-    }
-#pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) rows[d] += (mask >> d) & 1u;
-    for (int j = 0; j < k; ++j) {
-      const int e = idx[size_t(t) * k + j];
-      if (e < 0 || e >= E) continue;
-#pragma unroll
-      for (int d = 0; d < kMaxRanks; ++d) pairs[d] += e / per == d;
-    }
-  }
-  int rb[kMaxRanks], pb[kMaxRanks];
-#pragma unroll
-  for (int d = 0; d < kMaxRanks; ++d) {
-    int tr, tp;
-    rb[d] = plan_scan(rows[d], &tr);
-    pb[d] = plan_scan(pairs[d], &tp);
-    if (threadIdx.x == 0) {
-      base_r[d] = tr;
-      base_p[d] = tp;
-      if (d < world) {
-        send_rows[d] = tr;
-        send_pairs[d] = tp;
-      }
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int r = 0, p = 0;
-    for (int d = 0; d < kMaxRanks; ++d) {
-      const int nr = base_r[d], np = base_p[d];
-      base_r[d] = r;
-      base_p[d] = p;
-      r += nr;
-      p += np;
-    }
-  }
-  __syncthreads();
-  for (int t = t0; t < t1; ++t) {
+  for (int d = 0; d < kMaxRanks; ++d) packed[d] = 0;
+  if (t < T) {
     unsigned mask = 0;
     for (int j = 0; j < k; ++j) {
       const int e = idx[size_t(t) * k + j];
       if (e < 0 || e >= E) {
         set_status(status, kStatusBadExpert);
+        continue;
+      }
+      const int d = e / per;
+      mask |= 1u << d;
+#pragma unroll
+      for (int dd = 0; dd < kMaxRanks; ++dd) packed[dd] += dd == d ? 1 << 12 : 0;
+    }
+#pragma unroll
+    for (int d = 0; d < kMaxRanks; ++d) packed[d] += (mask >> d) & 1u;
+  }
+#pragma unroll
+  for (int d = 0; d < kMaxRanks; ++d) {
+    if (d >= world) break;
+    int total;
+    tile_scan_incl(packed[d], &total);
+    if (threadIdx.x == 0) tile_counts[size_t(blockIdx.x) * world + d] = total;
+  }
+}
+
+// Pass 2 (one warp per rank d): exclusive scan over tiles -> per-tile bases; totals -> send_rows / send_pairs; the
+// bases include the offsets of the earlier ranks' blocks.
+__global__ void ep_scan_kernel(const int32_t* __restrict__ tile_counts, int ntiles, int world,
+                               int32_t* __restrict__ tile_base, int32_t* __restrict__ send_rows,
+                               int32_t* __restrict__ send_pairs) {
+  __shared__ int tot_r[kMaxRanks], tot_p[kMaxRanks];
+  const int d = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int run_r = 0, run_p = 0;
+  if (d < world) {
+    for (int t0 = 0; t0 < ntiles; t0 += 32) {
+      const int t = t0 + lane;
+      const int v = t < ntiles ? tile_counts[size_t(t) * world + d] : 0;
+      int r = v & 0xFFF, p = v >> 12;
+      int ir = r, ip = p;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int nr = __shfl_up_sync(0xffffffffu, ir, o), np = __shfl_up_sync(0xffffffffu, ip, o);
+        if (lane >= o) ir += nr, ip += np;
+      }
+      if (t < ntiles) tile_base[size_t(t) * world * 2 + 2 * d] = run_r + ir - r;
+      if (t < ntiles) tile_base[size_t(t) * world * 2 + 2 * d + 1] = run_p + ip - p;
+      run_r += __shfl_sync(0xffffffffu, ir, 31);
+      run_p += __shfl_sync(0xffffffffu, ip, 31);
+    }
+    if (lane == 0) {
+      tot_r[d] = run_r;
+      tot_p[d] = run_p;
+      send_rows[d] = run_r;
+      send_pairs[d] = run_p;
+    }
+  }
+  __syncthreads();
+  if (d < world) {  // add the start of rank d's block (earlier ranks' totals)
+    int br = 0, bp = 0;
+    for (int q = 0; q < d; ++q) br += tot_r[q], bp += tot_p[q];
+    for (int t = lane; t < ntiles; t += 32) {
+      tile_base[size_t(t) * world * 2 + 2 * d] += br;
+      tile_base[size_t(t) * world * 2 + 2 * d + 1] += bp;
+    }
+    if (lane == 0) {
+      // per-rank block starts for pass 3's row numbers within a block (stored after the tile bases)
+      tile_base[size_t(ntiles) * world * 2 + 2 * d] = br;
+      tile_base[size_t(ntiles) * world * 2 + 2 * d + 1] = bp;
+    }
+  }
+}
+
+// Pass 3: each token's place. Rows to rank d: tokens with a pick on d, in token order; pairs to d: those picks in
+// (token, slot) order, which is also the order of the result rows d sends back. ret_index[t][j]: position of pick
+// (t, j)'s result row among all result rows this rank receives (blocks of send_pairs[d] in rank order).
+__global__ void __launch_bounds__(kPlanTile) ep_place_kernel(const int32_t* __restrict__ idx, int T, int k, int E,
+                                                             int world, const int32_t* __restrict__ tile_base,
+                                                             int32_t* __restrict__ send_tok, int2* __restrict__ pair_list,
+                                                             int32_t* __restrict__ ret_index) {
+  const int t = blockIdx.x * kPlanTile + threadIdx.x, per = E / world;
+  const int ntiles = gridDim.x;
+  int packed[kMaxRanks];
+  unsigned mask = 0;
+#pragma unroll
+  for (int d = 0; d < kMaxRanks; ++d) packed[d] = 0;
+  if (t < T) {
+    for (int j = 0; j < k; ++j) {
+      const int e = idx[size_t(t) * k + j];
+      if (e < 0 || e >= E) {
         ret_index[size_t(t) * k + j] = 0;
         continue;
       }
-      mask |= 1u << (e / per);
+      const int d = e / per;
+      mask |= 1u << d;
+#pragma unroll
+      for (int dd = 0; dd < kMaxRanks; ++dd) packed[dd] += dd == d ? 1 << 12 : 0;
     }
 #pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) {
-      if (!((mask >> d) & 1u)) continue;
-      const int local_row = rb[d]++;
-      send_tok[base_r[d] + local_row] = t;
-      for (int j = 0; j < k; ++j) {
-        const int e = idx[size_t(t) * k + j];
-        if (e < 0 || e >= E || e / per != d) continue;
-        const int q = base_p[d] + pb[d]++;
-        pair_list[q] = make_int2(local_row, e);
-        ret_index[size_t(t) * k + j] = q;
-      }
+    for (int d = 0; d < kMaxRanks; ++d) packed[d] += (mask >> d) & 1u;
+  }
+#pragma unroll
+  for (int d = 0; d < kMaxRanks; ++d) {
+    if (d >= world) break;
+    int total;
+    const int incl = tile_scan_incl(packed[d], &total);
+    if (t >= T || !((mask >> d) & 1u)) continue;
+    const int excl = incl - packed[d];
+    const int row = tile_base[size_t(blockIdx.x) * world * 2 + 2 * d] + (excl & 0xFFF);
+    int q = tile_base[size_t(blockIdx.x) * world * 2 + 2 * d + 1] + (excl >> 12);
+    const int local_row = row - tile_base[size_t(ntiles) * world * 2 + 2 * d];
+    send_tok[row] = t;
+    for (int j = 0; j < k; ++j) {
+      const int e = idx[size_t(t) * k + j];
+      if (e < 0 || e >= E || e / per != d) continue;
+      pair_list[q] = make_int2(local_row, e);
+      ret_index[size_t(t) * k + j] = q;
+      ++q;
     }
   }
 }
@@ -195,13 +230,23 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const int32_t* __restric
 
 }  // namespace
 
+size_t ep_plan_scratch_bytes(int T, int world) {
+  const size_t ntiles = (size_t(T) + kPlanTile - 1) / kPlanTile;
+  return (ntiles * world + (ntiles + 1) * world * 2) * sizeof(int32_t);
+}
+
 cudaError_t ep_plan(const int32_t* topk_idx, int T, int k, int E, int world, int32_t* send_rows, int32_t* send_pairs,
-                    int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, int* status, cudaStream_t st,
-                    int* launches) {
-  if (world < 1 || world > kMaxRanks || E % world) return cudaErrorInvalidValue;
-  ep_plan_kernel<<<1, kPlanThreads, 0, st>>>(topk_idx, T, k, E, world, send_rows, send_pairs, send_tok,
-                                             reinterpret_cast<int2*>(pair_list), ret_index, status);
-  ++*launches;
+                    int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, void* scratch, int* status,
+                    cudaStream_t st, int* launches) {
+  if (world < 1 || world > kMaxRanks || E % world || k > 8 || T < 1) return cudaErrorInvalidValue;
+  const int ntiles = (T + kPlanTile - 1) / kPlanTile;
+  int32_t* tile_counts = static_cast<int32_t*>(scratch);
+  int32_t* tile_base = tile_counts + size_t(ntiles) * world;
+  ep_count_kernel<<<ntiles, kPlanTile, 0, st>>>(topk_idx, T, k, E, world, tile_counts, status);
+  ep_scan_kernel<<<1, 32 * kMaxRanks, 0, st>>>(tile_counts, ntiles, world, tile_base, send_rows, send_pairs);
+  ep_place_kernel<<<ntiles, kPlanTile, 0, st>>>(topk_idx, T, k, E, world, tile_base, send_tok,
+                                                reinterpret_cast<int2*>(pair_list), ret_index);
+  *launches += 3;
   return cudaGetLastError();
 }
 

@@ -381,16 +381,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const int n = min(32, t.ncols - c0);
+        // output row of column c0 + lane (remapped rows of the down launch fetched once per chunk)
+        int lane_row = prow0 + c0 + lane;
+        if (MODE == 1 && p.out_rows && lane < n && lane_row < p.n_routed) lane_row = p.out_rows[lane_row];
         constexpr int pieces = 32 * orows / 8;  // 16-byte pieces of the chunk
 #pragma unroll
         for (int q = e; q < pieces; q += 128) {
           const int c = q / (orows / 8), g = q % (orows / 8);
-          if (c < n) {
-            int row = prow0 + c0 + c;
-            if (MODE == 1 && p.out_rows && row < p.n_routed) row = p.out_rows[row];
+          const int row = __shfl_sync(0xffffffffu, lane_row, c);
+          if (c < n)
             *reinterpret_cast<uint4*>(gout + size_t(row) * ld + 8 * g) =
                 *reinterpret_cast<const uint4*>(obuf + c * orows + 8 * g);
-          }
         }
         if (MODE == 1) asm volatile("bar.sync 1, 128;" ::: "memory");  // obuf is rewritten by the next chunk
       }

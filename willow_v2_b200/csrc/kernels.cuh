@@ -104,9 +104,10 @@ cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const flo
 
 // ep.cu: expert parallelism over up to kMaxRanks ranks (contiguous expert blocks)
 constexpr int kMaxRanks = 8;
+size_t ep_plan_scratch_bytes(int T, int world);
 cudaError_t ep_plan(const int32_t* topk_idx, int T, int k, int E, int world, int32_t* send_rows, int32_t* send_pairs,
-                    int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, int* status, cudaStream_t st,
-                    int* launches);
+                    int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, void* scratch, int* status,
+                    cudaStream_t st, int* launches);
 cudaError_t ep_pack(const void* x, int x_dtype, int H, const int32_t* send_tok, const int32_t* send_rows, int world,
                     int max_rows, void* send_buf, cudaStream_t st, int* launches);
 cudaError_t ep_fixup(const int32_t* pair_list, int P, int world, const int32_t* recv_rows, const int32_t* recv_pairs,

@@ -24,6 +24,11 @@ struct wmoe_ctx {
   int prefill_threshold = 256;  // token count from which wmoe_moe_forward uses the tcgen05 grouped GEMMs
   uint64_t* trace = nullptr;  // decode phase timestamps (device), or null
   size_t trace_entries = 0;
+  // expert parallelism over the library's own NCCL communicator (wmoe_ep_init)
+  void* nccl_comm = nullptr;  // ncclComm_t
+  int ep_rank = 0, ep_world = 0;
+  void* ep_buf = nullptr;     // received rows, pair lists, result rows and the expert stage's scratch (grown)
+  size_t ep_buf_bytes = 0;
   // per-phase CUDA events of the last profile_calls multi-token MoE calls (opt-in): [profile_calls][kProfMarks]
   static constexpr int kProfMarks = 7;
   std::vector<cudaEvent_t> prof_events;

@@ -7,7 +7,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libwmoe.so")
 
 OK = 0
-ERR_INVALID, ERR_CUDA, ERR_CAPACITY, ERR_DEVICE, ERR_UNSUPPORTED, ERR_IO = -1, -2, -3, -4, -5, -6
+ERR_INVALID, ERR_CUDA, ERR_CAPACITY, ERR_DEVICE, ERR_UNSUPPORTED, ERR_IO, ERR_NCCL = -1, -2, -3, -4, -5, -6, -7
 F32, BF16, F16 = 0, 1, 2
 GGML_Q4_K, GGML_Q6_K = 12, 14
 STATUS_NAMES = {1: "expert id out of range", 2: "expert not resident", 3: "grid barrier timed out",
@@ -52,6 +52,10 @@ SIGNATURES = {
     "wmoe_ep_route_plan": (_i, [_p, _i, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "wmoe_ep_experts": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p]),
     "wmoe_ep_combine": (_i, [_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _i, _p]),
+    "wmoe_ep_unique_id": (_i, [_p]),
+    "wmoe_ep_init": (_i, [_p, _p, _i, _i]),
+    "wmoe_ep_finalize": (_i, [_p]),
+    "wmoe_moe_forward_ep": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _i, _p, _p, _p]),
 }
 
 
@@ -64,7 +68,9 @@ class LayerWeights(ctypes.Structure):
 
 ROUTER_STRIDE = 264  # WMOE_ROUTER_STRIDE
 PHASES = ("router", "dispatch", "gather", "gate_up", "down", "combine")  # WMOE_PHASES, in order
+EP_PHASES = ("route_plan", "counts", "dispatch_a2a", "experts", "combine_a2a", "combine")  # wmoe_moe_forward_ep
 MAX_RANKS = 8  # WMOE_MAX_RANKS
+EP_ID_BYTES = 128  # WMOE_EP_ID_BYTES
 
 
 def _load():

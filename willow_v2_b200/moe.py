@@ -62,6 +62,10 @@ class Context:
         if v:
             raise _lib.WmoeError(_lib.ERR_DEVICE, _lib.STATUS_NAMES.get(v, f"device status {v}"))
 
+    def ep_finalize(self):
+        """Frees the NCCL communicator of ep_init (every rank, before the process group goes away)."""
+        check(self.handle, lib.wmoe_ep_finalize(self.handle))
+
     def close(self):
         if self.handle:
             lib.wmoe_destroy(self.handle)
@@ -406,6 +410,37 @@ def moe_forward_ep(store, layer: int, x: torch.Tensor, lw: LayerWeights, group=N
         stats.update(events=events, rows_out=sum(s_rows), pairs_out=sum(s_pairs), rows_in=sum(r_rows),
                      pairs_in=P_r, tokens=x.shape[0])
     return (out, plan.topk_w, plan.topk_idx) if return_routing else out
+
+
+def ep_init(ctx: Context, group=None):
+    """Creates the library's own NCCL communicator over the ranks of a torch.distributed group (wmoe_ep_init): rank 0
+    makes the id, every rank receives it through the group. Needed once per context before moe_forward_ep_native."""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    buf = (ctypes.c_uint8 * _lib.EP_ID_BYTES)()
+    if rank == 0:
+        check(ctx.handle, lib.wmoe_ep_unique_id(buf))
+    obj = [bytes(buf)]
+    dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    uid = (ctypes.c_uint8 * _lib.EP_ID_BYTES).from_buffer_copy(obj[0])
+    check(ctx.handle, lib.wmoe_ep_init(ctx.handle, uid, rank, world))
+
+
+def moe_forward_ep_native(store: ExpertStore, layer: int, x: torch.Tensor, lw: LayerWeights, top_k: int = 8,
+                          out_dtype: Optional[torch.dtype] = None, return_routing: bool = False):
+    """moe_forward_ep in one library call (wmoe_moe_forward_ep) over the communicator of ep_init: the exchanges are
+    grouped ncclSend/ncclRecv issued from C++ on the current stream."""
+    ctx = store.ctx
+    x = x.contiguous()
+    T = x.shape[0]
+    out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    sel = torch.empty(T, top_k, dtype=torch.int32, device=x.device) if return_routing else None
+    w = torch.empty(T, top_k, dtype=torch.float32, device=x.device) if return_routing else None
+    weights = lw.as_struct()
+    check(ctx.handle, lib.wmoe_moe_forward_ep(ctx.handle, store.handle, layer, _ptr(x), _DTYPES[x.dtype], T, top_k,
+                                              ctypes.byref(weights), _ptr(out), _DTYPES[out.dtype], _ptr(sel),
+                                              _ptr(w), _stream()))
+    return (out, w, sel) if return_routing else out
 
 
 def decode_stack(store: ExpertStore, layers: list, h: torch.Tensor, eps: float = 1e-6, layer_begin: int = 0,
