@@ -229,6 +229,9 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
     stream = torch.cuda.current_stream()
     from willow_v2_b200 import lib as L
     moe.ep_init(ctx)
+    # tokens per expert grow with N (weak scaling): chunks of ~256 tokens per expert overlap exchanges and GEMMs
+    chunks = max(1, world // 2)
+    L.lib.wmoe_ep_set_chunks(ctx.handle, chunks)
     for s in range(W):
         moe.moe_forward_ep_native(store, 0, xs[s % 4], lw)
     torch.cuda.synchronize()
@@ -280,7 +283,7 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
     ctx.ep_finalize()
     dist.barrier()
     experts_ms = stage_ms.get("experts", float("nan"))
-    a2a_ms = stage_ms.get("dispatch_a2a", 0.0) + stage_ms.get("combine_a2a", 0.0)
+    a2a_ms = stage_ms.get("first_rows", 0.0) + stage_ms.get("last_results", 0.0)  # exchange time not overlapped
     times = torch.tensor([ms, e2e_ms, experts_ms, a2a_ms], dtype=torch.float64, device="cuda")
     dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms, e2e_ms, experts_ms_max, a2a_ms_max = times.tolist()
@@ -297,12 +300,12 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
                    "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T * world,
                    "parallelism": f"ep{world}", "experts_per_rank": per,
                    "l2": "inputs larger than L2: ~500 MB of activations per rank per step"},
-        "roofline": {"bound": "tensor", "kernel": "expert stage (dispatch + gather + grouped GEMMs), rank 0",
+        "roofline": {"bound": "tensor", "kernel": "expert stages (dispatch + gather + grouped GEMMs, all chunks), rank 0",
                      "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16, "traffic": None,
                      "peak_kind": peak_kind, "algorithmic_flops_per_launch": flops, "launch_ms": experts_ms},
-        "exchange": {"bytes_out_per_step": bytes_out, "a2a_ms_max": a2a_ms_max,
-                     "link_frac": bytes_out * (world - 1) / world / (a2a_ms_max * 1e-3) / 1e9 / link
-                     if a2a_ms_max > 0 else None, "link_gbs_ref": link},
+        "exchange": {"bytes_out_per_step": bytes_out, "exposed_ms_max": a2a_ms_max,
+                     "link_gbs_ref": link, "chunks": chunks,
+                     "note": "exchanges run on a second stream overlapping the expert stages; exposed = waits"},
         "stage_ms_rank0": stage_ms,
         "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 2,
                 "d2h_bytes_per_step": T * HIDDEN * 2},

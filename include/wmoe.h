@@ -138,8 +138,9 @@ int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, 
  * boundaries on its own stream into slot (call number % calls); calls = 0 turns it off and frees the events.
  * wmoe_phase_ms gives phase `phase` of the call `ago` calls back (0 = the latest): 0 router + top-k, 1 dispatch,
  * 2 gather (GEMM path) or activation quantisation (GEMV path), 3 gate_up, 4 down, 5 combine. It waits for that
- * call's events. wmoe_moe_forward_ep records its own six: 0 route + plan + rows, 1 count exchange and read-back,
- * 2 dispatch exchange, 3 expert stage, 4 result exchange, 5 combine. */
+ * call's events. wmoe_moe_forward_ep records its own six on the caller's stream: 0 route + plan + rows, 1 count
+ * exchange and read-back, 2 wait for the first chunk's rows, 3 expert stages (the other exchanges overlap them),
+ * 4 wait for the last results, 5 combine. */
 #define WMOE_PHASES 6
 int wmoe_set_profiling(wmoe_ctx* ctx, int calls);
 int wmoe_phase_ms(wmoe_ctx* ctx, int ago, int phase, float* ms);
@@ -225,6 +226,12 @@ int wmoe_ep_unique_id(void* out /* WMOE_EP_ID_BYTES */);
 #define WMOE_EP_ID_BYTES 128
 int wmoe_ep_init(wmoe_ctx* ctx, const void* unique_id, int rank, int world);
 int wmoe_ep_finalize(wmoe_ctx* ctx);
+/* wmoe_moe_forward_ep runs the rank's tokens in this many chunks (1..16, default 1) so that the exchanges of one
+ * chunk overlap the expert stage of another (the exchanges then run on a stream of the context, and the GEMMs leave
+ * SMs free for them). Every rank must use the same value: the count exchange carries it, and a mismatch makes every
+ * rank's call return WMOE_ERR_INVALID. The result does not depend on it. Chunks pay off when each expert still gets
+ * ~256 tokens per chunk (the tensor cores' cost per instruction is fixed up to N = 192). Returns the previous value. */
+int wmoe_ep_set_chunks(wmoe_ctx* ctx, int chunks);
 int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
                         const wmoe_layer_weights* weights, void* out, int out_dtype, int32_t* topk_idx_out,
                         float* topk_w_out, void* stream);

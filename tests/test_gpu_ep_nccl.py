@@ -44,8 +44,12 @@ def _rank(rank, world, port, outdir, zipf, native):
         x = torch.from_numpy(synth.hidden(SEED, TOKENS_PER_RANK * world, step=33)).to(torch.bfloat16)
         mine = x[rank * TOKENS_PER_RANK:(rank + 1) * TOKENS_PER_RANK].cuda()
         if native:
+            from willow_v2_b200.lib import lib
             moe.ep_init(ctx)
-            outs = [moe.moe_forward_ep_native(store, LAYER, mine, lw, out_dtype=torch.float32) for _ in range(2)]
+            outs = []
+            for chunks in (4, 1, 3):  # the result does not depend on the chunking
+                lib.wmoe_ep_set_chunks(ctx.handle, chunks)
+                outs.append(moe.moe_forward_ep_native(store, LAYER, mine, lw, out_dtype=torch.float32))
             # a rank with no tokens still takes part in every exchange
             empty = moe.moe_forward_ep_native(store, LAYER, mine[:0], lw, out_dtype=torch.float32) if rank == 1 \
                 else moe.moe_forward_ep_native(store, LAYER, mine, lw, out_dtype=torch.float32)
@@ -56,7 +60,7 @@ def _rank(rank, world, port, outdir, zipf, native):
         ctx.check_device()
         if native:
             ctx.ep_finalize()
-        assert torch.equal(outs[0], outs[1])
+        assert all(torch.equal(outs[0], o) for o in outs[1:])
         np.save(os.path.join(outdir, f"out{rank}.npy"), outs[0].cpu().numpy())
         dist.barrier()
     finally:
@@ -95,3 +99,51 @@ def test_ep_over_nccl_matches_single_gpu(zipf, native):
         lib.wmoe_set_prefill_threshold(ctx.handle, prev)
     for r in range(world):
         assert np.array_equal(outs[r], ref[r * TOKENS_PER_RANK:(r + 1) * TOKENS_PER_RANK]), r
+
+
+def _mismatch_rank(rank, world, port, outdir):
+    import torch
+    import torch.distributed as dist
+    from willow_v2_b200 import moe
+    from willow_v2_b200.lib import WmoeError, lib
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        ctx = moe.Context(rank)
+        per = 256 // world
+        store = moe.ExpertStore(1, ctx=ctx, expert_range=(rank * per, (rank + 1) * per))
+        store.fill_synthetic(SEED)
+        lw = _weights(moe, torch, ctx, False)
+        x = torch.from_numpy(synth.hidden(SEED, 256, step=44)).to(torch.bfloat16).cuda()
+        moe.ep_init(ctx)
+        lib.wmoe_ep_set_chunks(ctx.handle, 1 + rank % 2)  # ranks disagree
+        try:
+            moe.moe_forward_ep_native(store, LAYER, x, lw)
+            raised = False
+        except WmoeError as e:
+            raised = "chunk counts" in str(e)
+        lib.wmoe_ep_set_chunks(ctx.handle, 2)  # agree again: the communicator is still usable
+        out = moe.moe_forward_ep_native(store, LAYER, x, lw)
+        torch.cuda.synchronize()
+        ctx.ep_finalize()
+        np.save(os.path.join(outdir, f"ok{rank}.npy"), np.array([raised, bool(torch.isfinite(out.float()).all())]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_chunk_mismatch_is_an_error_on_every_rank():
+    """Ranks configured with different chunk counts get WMOE_ERR_INVALID from the same call (the fixed-size count
+    exchange carries the count) instead of mismatched exchanges; the next agreeing call works."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_mismatch_rank, args=(2, _free_port(), d), nprocs=2, start_method="spawn")
+        for r in range(2):
+            raised, finite = np.load(os.path.join(d, f"ok{r}.npy"))
+            assert raised and finite, r

@@ -567,11 +567,12 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
                                st, &n),
                   "router");
   WMOE_CHECK_CUDA(ctx,
-                  ep_plan(topk_idx, T, top_k, experts, world, send_rows, send_pairs, send_tok, pair_list, ret_index,
-                          at<void>(ctx, o_plan), ctx->d_status, st, &n),
+                  ep_plan(topk_idx, T, top_k, experts, world, send_rows, send_pairs, 1, send_tok, pair_list,
+                          ret_index, at<void>(ctx, o_plan), ctx->d_status, st, &n),
                   "wmoe_ep_route_plan: plan");
   WMOE_CHECK_CUDA(ctx,
-                  ep_pack(x, x_dtype, hidden, send_tok, send_rows, world, T * std::min(top_k, world), send_buf, st, &n),
+                  ep_pack(x, x_dtype, hidden, send_tok, send_rows, 1, world, T * std::min(top_k, world), send_buf, st,
+                          &n),
                   "wmoe_ep_route_plan: rows");
   ctx->launches += uint64_t(n);
   return WMOE_OK;
@@ -599,7 +600,7 @@ static size_t ep_experts_scratch_bytes(int P_r, int T, int E, int H, int F) {
 static int ep_experts_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, const int32_t* recv_rows,
                            const int32_t* recv_pairs, const uint16_t* recv_buf, const int32_t* recv_pair_list,
                            const void* x, int x_dtype, int T, const wmoe_layer_weights* w, uint16_t* y,
-                           char* scratch, cudaStream_t st) {
+                           char* scratch, cudaStream_t st, int gemm_ctas) {
   const int H = store->hidden, F = store->ffn, E = store->experts;
   int P_r = 0;
   for (int s = 0; s < world; ++s) P_r += recv_pairs[s];
@@ -658,7 +659,7 @@ static int ep_experts_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, int worl
   const ExpertSource src = store_source(store, w->shared_gate_up, w->shared_down);
   WMOE_CHECK_CUDA(ctx,
                   prefill_gemms(src, layer, pm, P, H, F, xg, reinterpret_cast<__half*>(y), pm.perm, P_r, sp(o_gemm),
-                                ctx->sm_count, ctx->d_status, nullptr, st, &n),
+                                gemm_ctas, ctx->d_status, nullptr, st, &n),
                   "expert stage: grouped GEMM");
   ctx->launches += uint64_t(n);
   if (store->capped && !experts_used.empty())
@@ -698,7 +699,7 @@ int wmoe_ep_experts(wmoe_ctx* ctx, wmoe_store* store, int layer, int world, cons
   if (int rc = ensure_scratch(ctx, ep_experts_scratch_bytes(P_r, T, store->experts, store->hidden, store->ffn)))
     return rc;
   return ep_experts_impl(ctx, store, layer, world, recv_rows, recv_pairs, recv_buf, recv_pair_list, x, x_dtype, T, w, y,
-                         static_cast<char*>(ctx->scratch), static_cast<cudaStream_t>(stream));
+                         static_cast<char*>(ctx->scratch), static_cast<cudaStream_t>(stream), ctx->sm_count);
 }
 
 int wmoe_ep_combine(wmoe_ctx* ctx, int T, int top_k, int hidden, const int32_t* topk_idx, const float* topk_w,
@@ -791,12 +792,21 @@ int wmoe_ep_init(wmoe_ctx* ctx, const void* unique_id, int rank, int world) {
   ctx->nccl_comm = comm;
   ctx->ep_rank = rank;
   ctx->ep_world = world;
+  WMOE_CHECK_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->ep_stream, cudaStreamNonBlocking), "wmoe_ep_init");
+  ctx->ep_events.assign(1 + 3 * kMaxEpChunks, nullptr);
+  for (cudaEvent_t& e : ctx->ep_events)
+    WMOE_CHECK_CUDA(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "wmoe_ep_init");
   return WMOE_OK;
 }
 
 static void ep_release(wmoe_ctx* ctx) {
   if (ctx->nccl_comm) nccl().CommDestroy(static_cast<ncclComm_t>(ctx->nccl_comm));
   ctx->nccl_comm = nullptr;
+  for (cudaEvent_t e : ctx->ep_events)
+    if (e) cudaEventDestroy(e);
+  ctx->ep_events.clear();
+  if (ctx->ep_stream) cudaStreamDestroy(ctx->ep_stream);
+  ctx->ep_stream = nullptr;
   ctx->ep_world = 0;
   cudaFree(ctx->ep_buf);
   ctx->ep_buf = nullptr;
@@ -829,6 +839,8 @@ static int ensure_ep_buf(wmoe_ctx* ctx, size_t bytes) {
 // (recv_n[s] elements) comes from rank s; blocks in rank order, counts in elements of `type`.
 static int ep_alltoallv(wmoe_ctx* ctx, const void* send, const int64_t* send_n, void* recv, const int64_t* recv_n,
                         ncclDataType_t type, size_t elem, cudaStream_t st, const char* where) {
+  // the rank's own block goes through NCCL too: inside one group its copy runs alongside the peer transfers
+  // (a separate cudaMemcpyAsync after the group measured slower)
   const NcclApi& api = nccl();
   ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
   size_t so = 0, ro = 0;
@@ -845,6 +857,16 @@ static int ep_alltoallv(wmoe_ctx* ctx, const void* send, const int64_t* send_n, 
   return WMOE_OK;
 }
 
+int wmoe_ep_set_chunks(wmoe_ctx* ctx, int chunks) {
+  if (!ctx || chunks < 1 || chunks > kMaxEpChunks) return WMOE_ERR_INVALID;
+  const int prev = ctx->ep_chunks;
+  ctx->ep_chunks = chunks;
+  return prev;
+}
+
+// The layer in C chunks of the rank's tokens so that the exchanges of some chunks overlap the expert stage of
+// others: the exchanges run on the context's communication stream, the rest on the caller's stream, ordered by
+// events. Chunks are planned first and their counts exchanged together (one host read of the transfer sizes).
 int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
                         const wmoe_layer_weights* w, void* out, int out_dtype, int32_t* topk_idx_out,
                         float* topk_w_out, void* stream) {
@@ -859,24 +881,30 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: bad layer, shape or dtype");
   if (int rc = check_layer(ctx, w, "wmoe_moe_forward_ep")) return rc;
   if (T > 0 && (!x || !out)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: null pointer");
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int k = top_k, max_rows = T * std::min(k, world);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream), cs = ctx->ep_stream;
+  const int k = top_k, kw = std::min(k, world);
+  // the chunk count is the context's setting only (never derived from local data): every rank must run the same
+  // exchanges; the count exchange below checks it
+  const int C = ctx->ep_chunks;
+  auto chunk_begin = [&](int c) { return int(int64_t(T) * c / C); };
+  const size_t xsz = x_dtype == WMOE_F32 ? 4 : 2, osz = out_dtype == WMOE_F32 ? 4 : 2;
   // stage A (sized by T) in the context scratch
   const bool tc = use_router_tc(w->router_split, x_dtype, T, H, E);
+  const int max_chunk = (T + C - 1) / C + 1;
   Plan pa;
   const size_t o_logits = pa.take<float>(std::max<size_t>(router_logit_floats(tc, T, E), 1));
   const size_t o_w = pa.take<float>(size_t(T) * k + 1);
   const size_t o_idx = pa.take<int32_t>(size_t(T) * k + 1);
   const size_t o_s = pa.take<float>(size_t(T) + 1);
-  const size_t o_cnt = pa.take<int32_t>(size_t(4) * world);  // send rows, send pairs, recv rows, recv pairs
-  const size_t o_tok = pa.take<int32_t>(size_t(max_rows) + 1);
+  // [send | recv][world][kCountWords]: per rank the chunk count, then (rows, pairs) of each chunk
+  const size_t o_cnt = pa.take<int32_t>(size_t(2) * world * kCountWords);
+  const size_t o_tok = pa.take<int32_t>(size_t(T) * kw + 1);
   const size_t o_pl = pa.take<int32_t>(size_t(T) * k * 2 + 2);
   const size_t o_ret = pa.take<int32_t>(size_t(T) * k + 1);
-  const size_t o_send = pa.take<uint16_t>(size_t(max_rows) * H + 8);
-  const size_t o_plan = pa.take<char>(ep_plan_scratch_bytes(std::max(T, 1), world));
+  const size_t o_send = pa.take<uint16_t>(size_t(T) * kw * H + 8);
+  const size_t o_plan = pa.take<char>(ep_plan_scratch_bytes(max_chunk, world));
   if (int rc = ensure_scratch(ctx, pa.bytes)) return rc;
   int n = 0;
-  // opt-in phase marks (wmoe_set_profiling): start, planned, counts known, rows arrived, experts, rows back, combined
   cudaEvent_t* marks = ctx->profile_calls > 0
                            ? &ctx->prof_events[size_t(ctx->profile_seq % uint64_t(ctx->profile_calls)) *
                                                wmoe_ctx::kProfMarks]
@@ -888,80 +916,132 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   float* topk_w = at<float>(ctx, o_w);
   int32_t* topk_idx = at<int32_t>(ctx, o_idx);
   float* shared_s = at<float>(ctx, o_s);
-  int32_t* cnt = at<int32_t>(ctx, o_cnt);
+  int32_t* cnt_send = at<int32_t>(ctx, o_cnt);                    // [world][kCountWords]
+  int32_t* cnt_recv = cnt_send + size_t(world) * kCountWords;      // [world][kCountWords]
+  int32_t* send_tok = at<int32_t>(ctx, o_tok);
   int32_t* pair_list = at<int32_t>(ctx, o_pl);
   int32_t* ret_index = at<int32_t>(ctx, o_ret);
   uint16_t* send_buf = at<uint16_t>(ctx, o_send);
-  if (T > 0) {
+  WMOE_CHECK_CUDA(ctx, ep_count_header(cnt_send, world, kCountWords, C, st, &n), "EP plan");
+  if (T > 0)
     WMOE_CHECK_CUDA(ctx,
                     route_tokens(tc, x, x_dtype, T, H, E, k, w->router_w, w->router_bias, w->shared_gate,
                                  w->router_split, at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status,
                                  st, &n),
                     "router");
+  for (int c = 0; c < C; ++c) {
+    const int t0 = chunk_begin(c), tn = chunk_begin(c + 1) - t0;
+    if (tn == 0) continue;
     WMOE_CHECK_CUDA(ctx,
-                    ep_plan(topk_idx, T, k, E, world, cnt, cnt + world, at<int32_t>(ctx, o_tok), pair_list, ret_index,
+                    ep_plan(topk_idx + size_t(t0) * k, tn, k, E, world, cnt_send + 1 + 2 * c, cnt_send + 2 + 2 * c,
+                            kCountWords,
+                            send_tok + size_t(t0) * kw, pair_list + size_t(t0) * k * 2, ret_index + size_t(t0) * k,
                             at<void>(ctx, o_plan), ctx->d_status, st, &n),
                     "EP plan");
-    WMOE_CHECK_CUDA(ctx, ep_pack(x, x_dtype, H, at<int32_t>(ctx, o_tok), cnt, world, max_rows, send_buf, st, &n),
+    WMOE_CHECK_CUDA(ctx,
+                    ep_pack(static_cast<const char*>(x) + size_t(t0) * H * xsz, x_dtype, H, send_tok + size_t(t0) * kw,
+                            cnt_send + 1 + 2 * c, kCountWords, world, tn * kw, send_buf + size_t(t0) * kw * H, st, &n),
                     "EP rows");
-  } else {
-    WMOE_CHECK_CUDA(ctx, cudaMemsetAsync(cnt, 0, 2 * world * sizeof(int32_t), st), "EP plan");
   }
   mark(1);
-  // counts: (rows, pairs) to each rank -> from each rank; one read of all four arrays for the transfer sizes
+  // every chunk's counts in one fixed-size exchange (kCountWords ints to and from each rank, whatever the chunk
+  // count), then one read of the transfer sizes
   {
-    std::vector<int64_t> one(static_cast<size_t>(world), 1);
-    if (int rc = ep_alltoallv(ctx, cnt, one.data(), cnt + 2 * world, one.data(), ncclInt32, 4, st, "EP counts"))
-      return rc;
-    if (int rc = ep_alltoallv(ctx, cnt + world, one.data(), cnt + 3 * world, one.data(), ncclInt32, 4, st, "EP counts"))
-      return rc;
+    std::vector<int64_t> nn(static_cast<size_t>(world), kCountWords);
+    if (int rc = ep_alltoallv(ctx, cnt_send, nn.data(), cnt_recv, nn.data(), ncclInt32, 4, st, "EP counts")) return rc;
   }
-  std::vector<int32_t> c(size_t(4) * world);
-  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(c.data(), cnt, c.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+  std::vector<int32_t> cnt(size_t(2) * world * kCountWords);
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(cnt.data(), cnt_send, cnt.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
                   "EP counts read-back");
   WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "EP counts read-back");
   mark(2);
-  const int32_t *s_rows = c.data(), *s_pairs = c.data() + world, *r_rows = c.data() + 2 * world,
-                *r_pairs = c.data() + 3 * world;
-  if (int rc = check_ep_counts(ctx, world, r_rows, r_pairs, T, "wmoe_moe_forward_ep")) return rc;
-  long long R = 0, P_r = 0, S_pairs = 0;
-  for (int d = 0; d < world; ++d) R += r_rows[d], P_r += r_pairs[d], S_pairs += s_pairs[d];
-  // stage B (sized by what arrives) in the EP buffer; growing it only after the read-back above is safe
+  const int32_t* cr = cnt.data() + size_t(world) * kCountWords;
+  for (int s = 0; s < world; ++s)
+    if (cr[size_t(s) * kCountWords] != C)
+      return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: ranks use different chunk counts (wmoe_ep_set_chunks)");
+  auto sr = [&](int d, int c) { return cnt[size_t(d) * kCountWords + 1 + 2 * c]; };  // rows of chunk c to d
+  auto sp = [&](int d, int c) { return cnt[size_t(d) * kCountWords + 2 + 2 * c]; };  // pairs of chunk c to d
+  auto rr = [&](int s, int c) { return cr[size_t(s) * kCountWords + 1 + 2 * c]; };   // rows from s
+  auto rp = [&](int s, int c) { return cr[size_t(s) * kCountWords + 2 + 2 * c]; };   // pairs from s
+  // stage B: per-chunk receive, result and return buffers, and one expert-stage scratch, in the EP buffer
+  std::vector<size_t> o_recv(C), o_rpl(C), o_y(C), o_yret(C);
+  std::vector<int> Pc(C), Rc(C), Sc(C), Tc(C), T0(C);
   Plan pb;
-  const size_t o_recv = pb.take<uint16_t>(size_t(R) * H + 8);
-  const size_t o_rpl = pb.take<int32_t>(size_t(P_r) * 2 + 2);
-  const size_t o_y = pb.take<uint16_t>((size_t(P_r) + T) * H + 8);
-  const size_t o_yret = pb.take<uint16_t>(size_t(S_pairs) * H + 8);
-  const size_t o_es = pb.take<char>(ep_experts_scratch_bytes(int(P_r), T, E, H, F));
+  size_t es = 0;
+  for (int c = 0; c < C; ++c) {
+    T0[c] = chunk_begin(c);
+    Tc[c] = chunk_begin(c + 1) - T0[c];
+    long long R = 0, P = 0, S = 0;
+    std::vector<int32_t> rrow(static_cast<size_t>(world)), rpair(static_cast<size_t>(world));
+    for (int d = 0; d < world; ++d) {
+      R += rr(d, c), P += rp(d, c), S += sp(d, c);
+      rrow[d] = rr(d, c), rpair[d] = rp(d, c);
+    }
+    if (int rc = check_ep_counts(ctx, world, rrow.data(), rpair.data(), Tc[c], "wmoe_moe_forward_ep")) return rc;
+    Rc[c] = int(R), Pc[c] = int(P), Sc[c] = int(S);
+    o_recv[c] = pb.take<uint16_t>(size_t(R) * H + 8);
+    o_rpl[c] = pb.take<int32_t>(size_t(P) * 2 + 2);
+    o_y[c] = pb.take<uint16_t>((size_t(P) + Tc[c]) * H + 8);
+    o_yret[c] = pb.take<uint16_t>(size_t(S) * H + 8);
+    es = std::max(es, ep_experts_scratch_bytes(Pc[c], Tc[c], E, H, F));
+  }
+  const size_t o_es = pb.take<char>(es);
   if (int rc = ensure_ep_buf(ctx, pb.bytes)) return rc;
   char* eb = static_cast<char*>(ctx->ep_buf);
-  uint16_t* recv_buf = reinterpret_cast<uint16_t*>(eb + o_recv);
-  int32_t* recv_pl = reinterpret_cast<int32_t*>(eb + o_rpl);
-  uint16_t* y = reinterpret_cast<uint16_t*>(eb + o_y);
-  uint16_t* y_ret = reinterpret_cast<uint16_t*>(eb + o_yret);
+  cudaEvent_t* ev = ctx->ep_events.data();  // [0] planned, then per chunk: rows arrived, results made, results back
+  WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[0], st), "EP ordering");
+  WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ev[0], 0), "EP ordering");
   std::vector<int64_t> sn(static_cast<size_t>(world)), rn(static_cast<size_t>(world));
-  for (int d = 0; d < world; ++d) sn[d] = int64_t(s_rows[d]) * H, rn[d] = int64_t(r_rows[d]) * H;
-  if (int rc = ep_alltoallv(ctx, send_buf, sn.data(), recv_buf, rn.data(), ncclHalf, 2, st, "EP dispatch rows"))
-    return rc;
-  for (int d = 0; d < world; ++d) sn[d] = int64_t(s_pairs[d]) * 2, rn[d] = int64_t(r_pairs[d]) * 2;
-  if (int rc = ep_alltoallv(ctx, pair_list, sn.data(), recv_pl, rn.data(), ncclInt32, 4, st, "EP dispatch pairs"))
-    return rc;
-  mark(3);
+  // dispatch exchanges of every chunk, in order, on the communication stream
+  for (int c = 0; c < C; ++c) {
+    const size_t t0 = size_t(T0[c]);
+    for (int d = 0; d < world; ++d) sn[d] = int64_t(sr(d, c)) * H, rn[d] = int64_t(rr(d, c)) * H;
+    if (int rc = ep_alltoallv(ctx, send_buf + t0 * kw * H, sn.data(), eb + o_recv[c], rn.data(), ncclHalf, 2, cs,
+                              "EP dispatch rows"))
+      return rc;
+    for (int d = 0; d < world; ++d) sn[d] = int64_t(sp(d, c)) * 2, rn[d] = int64_t(rp(d, c)) * 2;
+    if (int rc = ep_alltoallv(ctx, pair_list + t0 * k * 2, sn.data(), eb + o_rpl[c], rn.data(), ncclInt32, 4, cs,
+                              "EP dispatch pairs"))
+      return rc;
+    WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[1 + 3 * c], cs), "EP ordering");
+  }
   ctx->launches += uint64_t(n);
   n = 0;
-  if (int rc = ep_experts_impl(ctx, store, layer, world, r_rows, r_pairs, recv_buf, recv_pl, x, x_dtype, T, w, y,
-                               eb + o_es, st))
-    return rc;
+  // expert stage of each chunk once its rows are in; its results go back while the next chunk computes
+  for (int c = 0; c < C; ++c) {
+    WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(st, ev[1 + 3 * c], 0), "EP ordering");
+    if (c == 0) mark(3);
+    std::vector<int32_t> rrow(static_cast<size_t>(world)), rpair(static_cast<size_t>(world));
+    for (int d = 0; d < world; ++d) rrow[d] = rr(d, c), rpair[d] = rp(d, c);
+    uint16_t* y = reinterpret_cast<uint16_t*>(eb + o_y[c]);
+    if (int rc = ep_experts_impl(ctx, store, layer, world, rrow.data(), rpair.data(),
+                                 reinterpret_cast<const uint16_t*>(eb + o_recv[c]),
+                                 reinterpret_cast<const int32_t*>(eb + o_rpl[c]),
+                                 static_cast<const char*>(x) + size_t(T0[c]) * H * xsz, x_dtype, Tc[c], w, y, eb + o_es,
+                                 st, world > 1 && C > 1 ? std::max(1, ctx->sm_count - kEpCommSms) : ctx->sm_count))
+      return rc;
+    WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[2 + 3 * c], st), "EP ordering");
+    WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ev[2 + 3 * c], 0), "EP ordering");
+    for (int d = 0; d < world; ++d) sn[d] = int64_t(rp(d, c)) * H, rn[d] = int64_t(sp(d, c)) * H;
+    if (int rc = ep_alltoallv(ctx, y, sn.data(), eb + o_yret[c], rn.data(), ncclHalf, 2, cs, "EP combine rows"))
+      return rc;
+    WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[3 + 3 * c], cs), "EP ordering");
+  }
   mark(4);
-  // result rows back: block s of y (r_pairs[s] rows) to rank s; block d of y_ret (s_pairs[d] rows) from rank d
-  for (int d = 0; d < world; ++d) sn[d] = int64_t(r_pairs[d]) * H, rn[d] = int64_t(s_pairs[d]) * H;
-  if (int rc = ep_alltoallv(ctx, y, sn.data(), y_ret, rn.data(), ncclHalf, 2, st, "EP combine rows")) return rc;
-  mark(5);
-  if (T > 0) {
+  for (int c = 0; c < C; ++c) {
+    WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(st, ev[3 + 3 * c], 0), "EP ordering");
+    if (c == C - 1) mark(5);
+    if (Tc[c] == 0) continue;
+    const size_t t0 = size_t(T0[c]);
+    const uint16_t* y = reinterpret_cast<const uint16_t*>(eb + o_y[c]);
     WMOE_CHECK_CUDA(ctx,
-                    combine_rows(T, k, H, topk_idx, topk_w, ret_index, shared_s, reinterpret_cast<const __half*>(y_ret),
-                                 reinterpret_cast<const __half*>(y) + size_t(P_r) * H, out, out_dtype, st, &n),
+                    combine_rows(Tc[c], k, H, topk_idx + t0 * k, topk_w + t0 * k, ret_index + t0 * k, shared_s + t0,
+                                 reinterpret_cast<const __half*>(eb + o_yret[c]),
+                                 reinterpret_cast<const __half*>(y) + size_t(Pc[c]) * H,
+                                 static_cast<char*>(out) + t0 * H * osz, out_dtype, st, &n),
                     "EP combine");
+  }
+  if (T > 0) {
     if (topk_idx_out)
       WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_idx_out, topk_idx, size_t(T) * k * sizeof(int32_t),
                                            cudaMemcpyDeviceToDevice, st),

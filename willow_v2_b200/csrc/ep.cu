@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(kPlanTile) ep_count_kernel(const int32_t* __re
 // bases include the offsets of the earlier ranks' blocks.
 __global__ void ep_scan_kernel(const int32_t* __restrict__ tile_counts, int ntiles, int world,
                                int32_t* __restrict__ tile_base, int32_t* __restrict__ send_rows,
-                               int32_t* __restrict__ send_pairs) {
+                               int32_t* __restrict__ send_pairs, int count_stride) {
   __shared__ int tot_r[kMaxRanks], tot_p[kMaxRanks];
   const int d = threadIdx.x / 32, lane = threadIdx.x % 32;
   int run_r = 0, run_p = 0;
@@ -103,8 +103,8 @@ __global__ void ep_scan_kernel(const int32_t* __restrict__ tile_counts, int ntil
     if (lane == 0) {
       tot_r[d] = run_r;
       tot_p[d] = run_p;
-      send_rows[d] = run_r;
-      send_pairs[d] = run_p;
+      send_rows[d * count_stride] = run_r;
+      send_pairs[d * count_stride] = run_p;
     }
   }
   __syncthreads();
@@ -175,10 +175,10 @@ __global__ void __launch_bounds__(kPlanTile) ep_place_kernel(const int32_t* __re
 // send_buf[r] = x[send_tok[r]] as an fp16 row in run-of-8 order; blocks past the total row count return.
 template <typename XT>
 __global__ void __launch_bounds__(256) ep_pack_kernel(const XT* __restrict__ x, int H, const int32_t* __restrict__ send_tok,
-                                                      const int32_t* __restrict__ send_rows, int world,
-                                                      __half* __restrict__ send_buf) {
+                                                      const int32_t* __restrict__ send_rows, int count_stride,
+                                                      int world, __half* __restrict__ send_buf) {
   int total = 0;
-  for (int d = 0; d < world; ++d) total += send_rows[d];
+  for (int d = 0; d < world; ++d) total += send_rows[d * count_stride];
   const int r = blockIdx.x;
   if (r >= total) return;
   const XT* src = x + size_t(send_tok[r]) * H;
@@ -228,7 +228,18 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const int32_t* __restric
   }
 }
 
+// The send side of the EP count exchange: per rank `words` ints, the chunk count first, zeros after.
+__global__ void ep_count_header_kernel(int32_t* __restrict__ cnt, int world, int words, int chunks) {
+  for (int i = threadIdx.x; i < world * words; i += blockDim.x) cnt[i] = i % words == 0 ? chunks : 0;
+}
+
 }  // namespace
+
+cudaError_t ep_count_header(int32_t* cnt, int world, int words, int chunks, cudaStream_t st, int* launches) {
+  ep_count_header_kernel<<<1, 256, 0, st>>>(cnt, world, words, chunks);
+  ++*launches;
+  return cudaGetLastError();
+}
 
 size_t ep_plan_scratch_bytes(int T, int world) {
   const size_t ntiles = (size_t(T) + kPlanTile - 1) / kPlanTile;
@@ -236,31 +247,32 @@ size_t ep_plan_scratch_bytes(int T, int world) {
 }
 
 cudaError_t ep_plan(const int32_t* topk_idx, int T, int k, int E, int world, int32_t* send_rows, int32_t* send_pairs,
-                    int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, void* scratch, int* status,
-                    cudaStream_t st, int* launches) {
+                    int count_stride, int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, void* scratch,
+                    int* status, cudaStream_t st, int* launches) {
   if (world < 1 || world > kMaxRanks || E % world || k > 8 || T < 1) return cudaErrorInvalidValue;
   const int ntiles = (T + kPlanTile - 1) / kPlanTile;
   int32_t* tile_counts = static_cast<int32_t*>(scratch);
   int32_t* tile_base = tile_counts + size_t(ntiles) * world;
   ep_count_kernel<<<ntiles, kPlanTile, 0, st>>>(topk_idx, T, k, E, world, tile_counts, status);
-  ep_scan_kernel<<<1, 32 * kMaxRanks, 0, st>>>(tile_counts, ntiles, world, tile_base, send_rows, send_pairs);
+  ep_scan_kernel<<<1, 32 * kMaxRanks, 0, st>>>(tile_counts, ntiles, world, tile_base, send_rows, send_pairs,
+                                               count_stride);
   ep_place_kernel<<<ntiles, kPlanTile, 0, st>>>(topk_idx, T, k, E, world, tile_base, send_tok,
                                                 reinterpret_cast<int2*>(pair_list), ret_index);
   *launches += 3;
   return cudaGetLastError();
 }
 
-cudaError_t ep_pack(const void* x, int x_dtype, int H, const int32_t* send_tok, const int32_t* send_rows, int world,
-                    int max_rows, void* send_buf, cudaStream_t st, int* launches) {
+cudaError_t ep_pack(const void* x, int x_dtype, int H, const int32_t* send_tok, const int32_t* send_rows,
+                    int count_stride, int world, int max_rows, void* send_buf, cudaStream_t st, int* launches) {
   if (H % 8 || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(send_buf) % 16)
     return cudaErrorInvalidValue;
   if (max_rows <= 0) return cudaSuccess;
   if (x_dtype == kF32)
     ep_pack_kernel<float><<<unsigned(max_rows), 256, 0, st>>>(static_cast<const float*>(x), H, send_tok, send_rows,
-                                                              world, static_cast<__half*>(send_buf));
+                                                              count_stride, world, static_cast<__half*>(send_buf));
   else
     ep_pack_kernel<__nv_bfloat16><<<unsigned(max_rows), 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), H, send_tok, send_rows, world, static_cast<__half*>(send_buf));
+        static_cast<const __nv_bfloat16*>(x), H, send_tok, send_rows, count_stride, world, static_cast<__half*>(send_buf));
   ++*launches;
   return cudaGetLastError();
 }

@@ -104,12 +104,18 @@ cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const flo
 
 // ep.cu: expert parallelism over up to kMaxRanks ranks (contiguous expert blocks)
 constexpr int kMaxRanks = 8;
+constexpr int kMaxEpChunks = 16;
+constexpr int kCountWords = 1 + 2 * kMaxEpChunks;  // per rank in the EP count exchange: chunks, then rows / pairs
+// SMs the persistent GEMMs leave free while exchanges overlap them, so that NCCL's kernels find room
+constexpr int kEpCommSms = 16;
 size_t ep_plan_scratch_bytes(int T, int world);
+cudaError_t ep_count_header(int32_t* cnt, int world, int words, int chunks, cudaStream_t st, int* launches);
+// send_rows[d * count_stride], send_pairs[d * count_stride]: rows and pairs to rank d
 cudaError_t ep_plan(const int32_t* topk_idx, int T, int k, int E, int world, int32_t* send_rows, int32_t* send_pairs,
-                    int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, void* scratch, int* status,
-                    cudaStream_t st, int* launches);
-cudaError_t ep_pack(const void* x, int x_dtype, int H, const int32_t* send_tok, const int32_t* send_rows, int world,
-                    int max_rows, void* send_buf, cudaStream_t st, int* launches);
+                    int count_stride, int32_t* send_tok, int32_t* pair_list, int32_t* ret_index, void* scratch,
+                    int* status, cudaStream_t st, int* launches);
+cudaError_t ep_pack(const void* x, int x_dtype, int H, const int32_t* send_tok, const int32_t* send_rows,
+                    int count_stride, int world, int max_rows, void* send_buf, cudaStream_t st, int* launches);
 cudaError_t ep_fixup(const int32_t* pair_list, int P, int world, const int32_t* recv_rows, const int32_t* recv_pairs,
                      int32_t* pair_row, int32_t* pair_expert, cudaStream_t st, int* launches);
 cudaError_t ep_gather(const int32_t* perm, const int32_t* pair_row, int P_r, const void* recv, const void* x,

@@ -29,6 +29,9 @@ struct wmoe_ctx {
   int ep_rank = 0, ep_world = 0;
   void* ep_buf = nullptr;     // received rows, pair lists, result rows and the expert stage's scratch (grown)
   size_t ep_buf_bytes = 0;
+  cudaStream_t ep_stream = nullptr;     // the exchanges (overlapping the expert stage on the caller's stream)
+  std::vector<cudaEvent_t> ep_events;   // ordering between the two streams
+  int ep_chunks = 1;                    // token chunks per layer (wmoe_ep_set_chunks), the same on every rank
   // per-phase CUDA events of the last profile_calls multi-token MoE calls (opt-in): [profile_calls][kProfMarks]
   static constexpr int kProfMarks = 7;
   std::vector<cudaEvent_t> prof_events;

@@ -55,6 +55,7 @@ SIGNATURES = {
     "wmoe_ep_unique_id": (_i, [_p]),
     "wmoe_ep_init": (_i, [_p, _p, _i, _i]),
     "wmoe_ep_finalize": (_i, [_p]),
+    "wmoe_ep_set_chunks": (_i, [_p, _i]),
     "wmoe_moe_forward_ep": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _i, _p, _p, _p]),
 }
 
@@ -68,7 +69,7 @@ class LayerWeights(ctypes.Structure):
 
 ROUTER_STRIDE = 264  # WMOE_ROUTER_STRIDE
 PHASES = ("router", "dispatch", "gather", "gate_up", "down", "combine")  # WMOE_PHASES, in order
-EP_PHASES = ("route_plan", "counts", "dispatch_a2a", "experts", "combine_a2a", "combine")  # wmoe_moe_forward_ep
+EP_PHASES = ("route_plan", "counts", "first_rows", "experts", "last_results", "combine")  # wmoe_moe_forward_ep
 MAX_RANKS = 8  # WMOE_MAX_RANKS
 EP_ID_BYTES = 128  # WMOE_EP_ID_BYTES
 
