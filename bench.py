@@ -9,6 +9,9 @@ At N > 1 GPUs (torchrun) every rank serves its own token stream with its own ful
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode40|prefill4096]
 
+--workload batch64: 64 f32 tokens through one MoE layer with Zipf-biased routing (the
+dequant-GEMV path); tokens/s and HBM GB/s over the distinct experts each step touches.
+
 --workload prefill4096: one MoE layer on 4096 bf16 tokens with uniform routing (~128
 tokens per expert) through the tcgen05 grouped GEMMs; tokens/s, with the dominant GEMM launch against the measured
 bf16 tensor peak. At N > 1 it is expert-parallel (rank r holds 256/N experts, 4096 tokens per rank per step,
@@ -31,7 +34,8 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 HIDDEN, FFN, EXPERTS, TOP_K = 2048, 512, 256, 8
-EXPERT_BYTES = 2 * FFN * HIDDEN // 256 * 144 + HIDDEN * FFN // 256 * 210   # 2,039,808
+GATE_UP_Q4_BYTES = 2 * FFN * HIDDEN // 256 * 144                              # 1,179,648
+EXPERT_BYTES = GATE_UP_Q4_BYTES + HIDDEN * FFN // 256 * 210                    # 2,039,808
 ROUTER_BYTES = EXPERTS * HIDDEN * 4 + HIDDEN * 4                           # router + shared gate, fp32
 # DRAM bytes (read + write) per layer of decode_kernel, measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on a 4-layer launch: 82,234,880 + 1,487,360 bytes; traffic grows with the layers
@@ -43,6 +47,8 @@ PREFILL_GATE_UP_TRAFFIC = 454_209_280 + 31_324_928
 LAYERS = 40
 SEED = 0
 METRIC = "MoE decode tokens/s (40-layer qwen35moe stack, 1 token per step)"
+BATCH_T = 64
+METRIC_BATCH = "MoE batched-decode tokens/s (one qwen35moe MoE layer, 64 f32 tokens per step, Zipf routing)"
 PREFILL_T = 4096
 METRIC_PREFILL = "MoE prefill tokens/s (one qwen35moe MoE layer, 4096 bf16 tokens per step)"
 # useful expert-product FLOPs of one prefill layer: every token through 8 routed experts + the shared expert,
@@ -205,6 +211,137 @@ def run_decode40(args, rank: int, world: int, dist):
         "clocks": clocks.summary(),
     }
     return result, (ctx, store, layers)
+
+
+def run_batch64(args, rank: int, world: int, dist):
+    """64 independent f32 tokens through one MoE layer with the Zipf(s=1.1) routing bias: the split-K
+    float32 router, the dispatch sort and the tcgen05 grouped GEMMs (64 tokens is above the default GEMM threshold of
+    16). HBM roofline over the distinct experts hit by each step's routing (each expert's bytes counted once, however
+    many tokens use it), plus the router."""
+    import torch
+    from willow_v2_b200 import lib as L
+    from willow_v2_b200 import moe, synth
+    device = torch.cuda.current_device()
+    ctx, store, layers = setup_model(device, 1)
+    lw = layers[0]
+    lw.router_bias = torch.from_numpy(synth.zipf_bias(SEED)).cuda()
+    K, W = args.steps, args.warmup
+    T = BATCH_T
+    nb = 16  # batches cycled; each step re-routes
+    xs = [torch.from_numpy(synth.hidden(SEED + 1000 * rank, T, step=b)).cuda() for b in range(nb)]
+    out = torch.empty(T, HIDDEN, dtype=torch.float32, device="cuda")
+    sel = torch.empty(T, TOP_K, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+    weights = lw.as_struct()
+
+    def step(x, o, s):
+        L.check(ctx.handle, L.lib.wmoe_moe_forward_layer(ctx.handle, store.handle, 0, x.data_ptr(), L.F32, T, TOP_K,
+                                                         L.ctypes.byref(weights), o.data_ptr(), L.F32,
+                                                         None if s is None else s.data_ptr(), None,
+                                                         stream.cuda_stream))
+
+    # distinct experts per batch (the algorithmic bytes), from the same routing the timed steps use
+    distinct = []
+    for b in range(nb):
+        step(xs[b], out, sel)
+        distinct.append(int(torch.unique(sel).numel()))
+    for s in range(W):
+        step(xs[s % nb], out, None)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    L.check(ctx.handle, L.lib.wmoe_set_profiling(ctx.handle, K))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        ev0.record(stream)
+        for s in range(K):
+            step(xs[s % nb], out, None)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    gpu_launches = ctx.launches - launches0
+    ms = ev0.elapsed_time(ev1) / K
+    phase = {name: [] for name in L.PHASES}
+    for ago in range(K):
+        for p, name in enumerate(L.PHASES):
+            v = L.ctypes.c_float()
+            L.check(ctx.handle, L.lib.wmoe_phase_ms(ctx.handle, ago, p, L.ctypes.byref(v)))
+            phase[name].append(v.value)
+    L.check(ctx.handle, L.lib.wmoe_set_profiling(ctx.handle, 0))
+    phase_ms = {name: statistics.mean(v) for name, v in phase.items()}
+    ctx.check_device()
+    x_host = [x.cpu().pin_memory() for x in xs]
+    o_host = torch.empty(T, HIDDEN, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty(T, HIDDEN, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(K):
+        x_dev.copy_(x_host[s % nb], non_blocking=True)
+        step(x_dev, out, None)
+        o_host.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    times = torch.tensor([ms, e2e_ms, phase_ms["gate_up"]], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, gu_ms = times.tolist()
+    hbm, _, peak_kind = peaks()
+    mean_u = statistics.mean(distinct[s % nb] for s in range(K))
+    nbytes = (mean_u + 1) * EXPERT_BYTES + ROUTER_BYTES
+    # the gate_up launch: Q4_K blocks of the hit experts + shared, gathered fp16 rows in, fp16 h rows out
+    rows = T * (TOP_K + 1)
+    gu_bytes = (mean_u + 1) * GATE_UP_Q4_BYTES + rows * HIDDEN * 2 + rows * FFN * 2
+    gu_gbs = gu_bytes / (gu_ms * 1e-3) / 1e9
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    result = {
+        "metric": METRIC_BATCH, "value": world * T * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks; f32 N(0,1) tokens; Zipf(1.1) routing bias)",
+        "config": {"workload": "configs[2]: 64 tokens through one MoE layer, Zipf-biased routing",
+                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T,
+                   "distinct_experts_mean": mean_u,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": f"{nb} batches cycled: each step re-routes; ~{nbytes / 1e6:.0f} MB of weights per step"},
+        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel<0> (gate_up + SwiGLU)", "achieved": gu_gbs,
+                     "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms},
+        "roofline_step": {"achieved": achieved, "frac": achieved / hbm, "algorithmic_bytes": nbytes,
+                          "note": "whole step (all launches); bytes = distinct experts hit + shared + router"},
+        "phase_ms": phase_ms,
+        "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 4,
+                "d2h_bytes_per_step": T * HIDDEN * 4},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks.summary(),
+    }
+    return result, (ctx, store, layers)
+
+
+def cpu_baseline_batch(sample_experts: int = 256):
+    """The oracle port for configs[2]: router on the 64 tokens, then a sample of the hit experts dequantised and run on
+    their tokens, scaled to all hit experts + the shared expert."""
+    import oracle.moe_oracle as ora
+    from willow_v2_b200 import synth
+    x = synth.hidden(SEED, BATCH_T, step=777)
+    t0 = time.perf_counter()
+    w, sel = ora.route(x @ synth.router_weight(SEED, 0).T + synth.zipf_bias(SEED))
+    t_route = time.perf_counter() - t0
+    hit = sorted(set(int(e) for e in sel.reshape(-1)))
+    t_exp = 0.0
+    for e in hit[:sample_experts]:
+        rows = x[(sel == e).any(axis=1)]
+        gu, dn = synth.expert_gate_up(SEED, 0, e), synth.expert_down(SEED, 0, e)
+        t1 = time.perf_counter()
+        ora.expert_gate(rows @ ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN)).T) @ ora.dequantize(dn, "Q6_K", (HIDDEN, FFN)).T
+        t_exp += time.perf_counter() - t1
+    n = min(sample_experts, len(hit))
+    sec = t_route + t_exp / n * (len(hit) + 1)
+    return {"value": BATCH_T / sec, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"router on the 64 tokens; {n} of the {len(hit)} hit experts dequantised and run on their tokens "
+                      f"(numpy float32), scaled to all hit experts + the shared expert"}
 
 
 def run_prefill4096_ep(args, rank: int, world: int, dist):
@@ -537,7 +674,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode40", choices=["decode40", "prefill4096"])
+    ap.add_argument("--workload", default="decode40", choices=["decode40", "batch64", "prefill4096"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="stack depth (40 = the benchmark; fewer = profiling)")
     args = ap.parse_args()
@@ -564,6 +701,10 @@ def main():
         result, _keep = run_prefill4096(args, rank, world, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline_prefill()
+    elif args.workload == "batch64":
+        result, _keep = run_batch64(args, rank, world, dist)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_batch()
     else:
         result, _keep = run_decode40(args, rank, world, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

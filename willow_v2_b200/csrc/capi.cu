@@ -197,6 +197,36 @@ int wmoe_dequant(wmoe_ctx* ctx, int ggml_type, const uint8_t* blocks, size_t nbl
   return WMOE_OK;
 }
 
+// Router + top-k + shared gate of T tokens into caller buffers: for bf16 tokens with the split router, logits on the
+// tensor cores (partial sums of a K split); otherwise float32 on the CUDA cores, through the sliced router above 8
+// tokens (the same bits per token whatever the call's size). logits: router_logit_floats() floats of scratch.
+static bool use_router_tc(const void* router_split, int x_dtype, int T, int H, int E) {
+  return router_split && x_dtype == WMOE_BF16 && T >= 16 && router_tc_supported(T, H, E);
+}
+static size_t router_logit_floats(bool tc, int T, int E, int H) {
+  if (tc) return size_t(kRouterKSplit) * T * E;
+  if (T > 8) return size_t(router_slice_outputs(T, H)) * T * E;
+  return size_t(T) * (E + 1);
+}
+static cudaError_t route_tokens(bool tc, const void* x, int x_dtype, int T, int H, int E, int k, const float* router_w,
+                                const float* router_bias, const float* shared_gate, const void* router_split,
+                                float* logits, float* topk_w, int32_t* topk_idx, float* shared_s, int* status,
+                                cudaStream_t st, int* n, float* logits_out = nullptr) {
+  cudaError_t e;
+  if (tc) {
+    if ((e = router_logits_tc(x, T, H, E, router_split, logits, status, st, n)) != cudaSuccess) return e;
+    return router_topk_split(logits, kRouterKSplit, T, E, k, router_bias, topk_w, topk_idx, shared_s, logits_out, x,
+                             x_dtype, shared_gate, H, st, n);
+  }
+  if (T > 8) {
+    if ((e = router_logits_sliced(x, x_dtype, T, H, E, router_w, logits, st, n)) != cudaSuccess) return e;
+    return router_topk_split(logits, router_slice_outputs(T, H), T, E, k, router_bias, topk_w, topk_idx, shared_s,
+                             logits_out, x, x_dtype, shared_gate, H, st, n);
+  }
+  if ((e = router_logits(x, x_dtype, T, H, E, router_w, shared_gate, logits, st, n)) != cudaSuccess) return e;
+  return router_topk(logits, T, E, k, router_bias, topk_w, topk_idx, shared_s, logits_out, st, n);
+}
+
 int wmoe_route(wmoe_ctx* ctx, const void* x, int x_dtype, int T, int hidden, int experts, int top_k,
                const float* router_w, const float* router_bias, const float* shared_gate, float* topk_w,
                int32_t* topk_idx, float* shared_s, float* logits, void* stream) {
@@ -209,14 +239,15 @@ int wmoe_route(wmoe_ctx* ctx, const void* x, int x_dtype, int T, int hidden, int
   if (!x || !router_w || !topk_w || !topk_idx || (shared_s && !shared_gate))
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_route: null pointer");
   Plan plan;
-  const size_t o_logits = plan.take<float>(size_t(T) * (experts + 1));
+  const size_t o_logits = plan.take<float>(router_logit_floats(false, T, experts, hidden));
   if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   int n = 0;
-  float* lg = at<float>(ctx, o_logits);
-  WMOE_CHECK_CUDA(ctx, router_logits(x, x_dtype, T, hidden, experts, router_w, shared_gate, lg, st, &n), "router");
-  WMOE_CHECK_CUDA(ctx, router_topk(lg, T, experts, top_k, router_bias, topk_w, topk_idx, shared_s, logits, st, &n),
-                  "top-k");
+  WMOE_CHECK_CUDA(ctx,
+                  route_tokens(false, x, x_dtype, T, hidden, experts, top_k, router_w, router_bias, shared_gate,
+                               nullptr, at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status, st, &n,
+                               logits),
+                  "router");
   ctx->launches += uint64_t(n);
   return WMOE_OK;
 }
@@ -340,28 +371,6 @@ int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, 
   return WMOE_OK;
 }
 
-// Router + top-k + shared gate of T tokens into caller buffers: for bf16 tokens with the split router, logits on the
-// tensor cores (partial sums of a K split); otherwise float32 on the CUDA cores. logits: router_logit_floats().
-static bool use_router_tc(const void* router_split, int x_dtype, int T, int H, int E) {
-  return router_split && x_dtype == WMOE_BF16 && T >= 16 && router_tc_supported(T, H, E);
-}
-static size_t router_logit_floats(bool tc, int T, int E) {
-  return tc ? size_t(kRouterKSplit) * T * E : size_t(T) * (E + 1);
-}
-static cudaError_t route_tokens(bool tc, const void* x, int x_dtype, int T, int H, int E, int k, const float* router_w,
-                                const float* router_bias, const float* shared_gate, const void* router_split,
-                                float* logits, float* topk_w, int32_t* topk_idx, float* shared_s, int* status,
-                                cudaStream_t st, int* n) {
-  cudaError_t e;
-  if (tc) {
-    if ((e = router_logits_tc(x, T, H, E, router_split, logits, status, st, n)) != cudaSuccess) return e;
-    return router_topk_split(logits, kRouterKSplit, T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr, x,
-                             x_dtype, shared_gate, H, st, n);
-  }
-  if ((e = router_logits(x, x_dtype, T, H, E, router_w, shared_gate, logits, st, n)) != cudaSuccess) return e;
-  return router_topk(logits, T, E, k, router_bias, topk_w, topk_idx, shared_s, nullptr, st, n);
-}
-
 static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T,
                             int top_k, const float* router_w, const float* router_bias, const float* shared_gate,
                             const uint8_t* shared_gate_up, const uint8_t* shared_down, const float* router_packed,
@@ -399,7 +408,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   // router logits on the tensor cores for bf16 tokens when the split router is given (partial sums of a K split),
   // else float32 on the CUDA cores ([T][E + 1] with the shared gate as column E)
   const bool router_tc = use_router_tc(router_split, x_dtype, T, H, E);
-  const size_t o_logits = plan.take<float>(router_logit_floats(router_tc, T, E));
+  const size_t o_logits = plan.take<float>(router_logit_floats(router_tc, T, E, H));
   const size_t o_w = plan.take<float>(size_t(T) * k);
   const size_t o_idx = plan.take<int32_t>(size_t(T) * k);
   const size_t o_s = plan.take<float>(size_t(T));
@@ -557,7 +566,7 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
   }
   const bool tc = use_router_tc(w->router_split, x_dtype, T, hidden, experts);
   Plan plan;
-  const size_t o_logits = plan.take<float>(router_logit_floats(tc, T, experts));
+  const size_t o_logits = plan.take<float>(router_logit_floats(tc, T, experts, hidden));
   const size_t o_plan = plan.take<char>(ep_plan_scratch_bytes(T, world));
   if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
   int n = 0;
@@ -892,7 +901,7 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   const bool tc = use_router_tc(w->router_split, x_dtype, T, H, E);
   const int max_chunk = (T + C - 1) / C + 1;
   Plan pa;
-  const size_t o_logits = pa.take<float>(std::max<size_t>(router_logit_floats(tc, T, E), 1));
+  const size_t o_logits = pa.take<float>(std::max<size_t>(router_logit_floats(tc, T, E, H), 1));
   const size_t o_w = pa.take<float>(size_t(T) * k + 1);
   const size_t o_idx = pa.take<int32_t>(size_t(T) * k + 1);
   const size_t o_s = pa.take<float>(size_t(T) + 1);

@@ -41,7 +41,7 @@ __device__ __forceinline__ int pair_token(const PairMap& m, int p) {
 // dequant.cu
 cudaError_t dequant(int type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype, cudaStream_t st);
 
-// route.cu: logits [T, E+1] (column E = shared gate) then top-k
+// route.cu: at most 8 tokens, logits [T, E+1] (column E = shared gate); then top-k
 cudaError_t router_logits(const void* x, int x_dtype, int T, int H, int E, const float* router_w,
                           const float* shared_gate, float* logits, cudaStream_t st, int* launches);
 cudaError_t router_topk(const float* logits, int T, int E, int k, const float* bias, float* topk_w,
@@ -49,6 +49,13 @@ cudaError_t router_topk(const float* logits, int T, int E, int k, const float* b
 cudaError_t router_topk_split(const float* logits, int splits, int T, int E, int k, const float* bias, float* topk_w,
                               int32_t* topk_idx, float* shared_s, float* logits_out, const void* x, int x_dtype,
                               const float* g, int H, cudaStream_t st, int* launches);
+
+// More than 8 tokens: float32 logits without the shared gate as router_slice_outputs(T, H) partial sums [n][T][E]
+// over 128-wide K slices (one sum of all slices for large T), added in order by router_topk_split, which also forms
+// the shared-gate logit. A token's logits do not depend on the other tokens of the call. H a multiple of 128.
+int router_slice_outputs(int T, int H);
+cudaError_t router_logits_sliced(const void* x, int x_dtype, int T, int H, int E, const float* R, float* out,
+                                 cudaStream_t st, int* launches);
 
 // router_sm100.cu: bf16 tokens x (float32 router as three bf16 terms) on the tensor cores, K split kRouterKSplit
 // ways into partial logits [kRouterKSplit][T][E]

@@ -55,58 +55,77 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const XT* __restrict__
   }
 }
 
-// Many tokens: a 64 x 64 tile of logits per CTA (256 threads, 4 x 4 each), K in steps of 32 through shared memory.
+// More than 8 tokens: the router logits without the shared gate (the top-k kernel forms that one from x). Every logit
+// is a sequential fma chain over each kRouterSlice-wide K slice, and the slices are added in ascending order, whether
+// one CTA walks all of them (`slices_per_cta` = H / kRouterSlice, one output [T][E]) or each CTA takes one slice and
+// writes it as a partial sum ([H / kRouterSlice][T][E], added in order by the top-k kernel). A token's logits are
+// therefore the same bits whatever other tokens share its call.
+// CTA: 64 tokens x 64 router rows, 256 threads with 4 x 4 logits each; K in steps of 32 through two shared-memory
+// buffers, the next step's global loads held in registers while the current step computes.
+constexpr int kRouterSlice = 128, kRouterSplitMaxT = 1024;
+
 template <typename XT>
-__global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__ x, int T, int H, int E,
-                                                          const float* __restrict__ R,
-                                                          const float* __restrict__ g,
-                                                          float* __restrict__ logits) {
-  constexpr int BM = 64, BN = 64, BK = 32;
-  __shared__ float xs[BK][BM + 4];
-  __shared__ float ws[BK][BN + 4];
+__global__ void __launch_bounds__(256) router_slices_kernel(const XT* __restrict__ x, int T, int H, int E,
+                                                            const float* __restrict__ R, int slices_per_cta,
+                                                            float* __restrict__ out) {
+  constexpr int BM = 64, BN = 64, BK = 32, kSteps = kRouterSlice / BK;
+  __shared__ __align__(16) float xs[2][BK][BM + 4];
+  __shared__ __align__(16) float ws[2][BK][BN + 4];
   const int t0 = blockIdx.x * BM, e0 = blockIdx.y * BN;
-  const int tid = threadIdx.x;
-  const int rows = E + (g != nullptr ? 1 : 0);
-  const int ty = tid / 16, tx = tid % 16;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < H; k0 += BK) {
-    // 64 rows x 32 columns of x and of the weights: 2048 values each, 8 per thread (two float4)
+  const int k_begin = blockIdx.z * slices_per_cta * kRouterSlice;
+  const int nsteps = slices_per_cta * kSteps;
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  float4 xv[2], wv[2];
+  auto fetch = [&](int k0) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const int idx = tid + i * 256;  // 0..511 float4 slots
-      const int r = idx / 8, c = (idx % 8) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t0 + r < T) v = load4<XT>(x + size_t(t0 + r) * H + k0 + c);
-      xs[c + 0][r] = v.x;
-      xs[c + 1][r] = v.y;
-      xs[c + 2][r] = v.z;
-      xs[c + 3][r] = v.w;
-      float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
-      const int e = e0 + r;
-      if (e < E)
-        w = __ldg(reinterpret_cast<const float4*>(R + size_t(e) * H + k0 + c));
-      else if (e < rows)
-        w = __ldg(reinterpret_cast<const float4*>(g + k0 + c));
-      ws[c + 0][r] = w.x;
-      ws[c + 1][r] = w.y;
-      ws[c + 2][r] = w.z;
-      ws[c + 3][r] = w.w;
+      const int idx = tid + i * 256, r = idx / 8, c = (idx % 8) * 4;
+      xv[i] = t0 + r < T ? load4<XT>(x + size_t(t0 + r) * H + k0 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      wv[i] = e0 + r < E ? __ldg(reinterpret_cast<const float4*>(R + size_t(e0 + r) * H + k0 + c))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    __syncthreads();
+  };
+  auto stash = [&](int b) {
 #pragma unroll
-    for (int kk = 0; kk < BK; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx * 4 + j];
+    for (int i = 0; i < 2; ++i) {
+      const int idx = tid + i * 256, r = idx / 8, c = (idx % 8) * 4;
+      xs[b][c][r] = xv[i].x, xs[b][c + 1][r] = xv[i].y, xs[b][c + 2][r] = xv[i].z, xs[b][c + 3][r] = xv[i].w;
+      ws[b][c][r] = wv[i].x, ws[b][c + 1][r] = wv[i].y, ws[b][c + 2][r] = wv[i].z, ws[b][c + 3][r] = wv[i].w;
+    }
+  };
+  float acc[4][4], total[4][4];
+  fetch(k_begin);
+  stash(0);
+  __syncthreads();
+  for (int s = 0; s < nsteps; ++s) {
+    const int b = s & 1;
+    if (s + 1 < nsteps) fetch(k_begin + (s + 1) * BK);
+    if (s % kSteps == 0) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
     }
+#pragma unroll 8
+    for (int kk = 0; kk < BK; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(&xs[b][kk][ty * 4]);
+      const float4 w = *reinterpret_cast<const float4*>(&ws[b][kk][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, wv4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv4[j], acc[i][j]);
+    }
+    if (s % kSteps == kSteps - 1) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) total[i][j] = s < kSteps ? acc[i][j] : total[i][j] + acc[i][j];
+    }
+    if (s + 1 < nsteps) stash(b ^ 1);
     __syncthreads();
   }
+  float* o = out + size_t(blockIdx.z) * T * E;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int t = t0 + ty * 4 + i;
@@ -114,28 +133,37 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const XT* __restrict__
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int e = e0 + tx * 4 + j;
-      if (e < rows) logits[size_t(t) * (E + 1) + e] = acc[i][j];
+      if (e < E) o[size_t(t) * E + e] = total[i][j];
     }
   }
 }
 
+int router_slice_outputs(int T, int H) { return T <= kRouterSplitMaxT ? H / kRouterSlice : 1; }
+
+cudaError_t router_logits_sliced(const void* x, int x_dtype, int T, int H, int E, const float* R, float* out,
+                                 cudaStream_t st, int* launches) {
+  if (T <= 0 || H % kRouterSlice) return cudaErrorInvalidValue;
+  const int outputs = router_slice_outputs(T, H);
+  const dim3 grid(unsigned((T + 63) / 64), unsigned((E + 63) / 64), unsigned(outputs));
+  const int per_cta = H / kRouterSlice / outputs;
+  if (x_dtype == kF32)
+    router_slices_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), T, H, E, R, per_cta, out);
+  else
+    router_slices_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, E, R,
+                                                              per_cta, out);
+  ++*launches;
+  return cudaGetLastError();
+}
+
 cudaError_t router_logits(const void* x, int x_dtype, int T, int H, int E, const float* R, const float* g,
                           float* logits, cudaStream_t st, int* launches) {
-  if (T <= 8) {
-    const unsigned grid = unsigned((E + 1 + 7) / 8);
-    if (x_dtype == kF32)
-      router_gemv_kernel<float, 8><<<grid, 256, 0, st>>>(static_cast<const float*>(x), T, H, E, R, g, logits);
-    else
-      router_gemv_kernel<__nv_bfloat16, 8><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, E, R,
-                                                                   g, logits);
-  } else {
-    const dim3 grid(unsigned((T + 63) / 64), unsigned((E + 1 + 63) / 64));
-    if (x_dtype == kF32)
-      router_gemm_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), T, H, E, R, g, logits);
-    else
-      router_gemm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, E, R, g,
-                                                               logits);
-  }
+  if (T > 8) return cudaErrorInvalidValue;  // router_logits_sliced
+  const unsigned grid = unsigned((E + 1 + 7) / 8);
+  if (x_dtype == kF32)
+    router_gemv_kernel<float, 8><<<grid, 256, 0, st>>>(static_cast<const float*>(x), T, H, E, R, g, logits);
+  else
+    router_gemv_kernel<__nv_bfloat16, 8><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, H, E, R, g,
+                                                                 logits);
   ++*launches;
   return cudaGetLastError();
 }

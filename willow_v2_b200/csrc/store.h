@@ -21,7 +21,7 @@ struct wmoe_ctx {
   size_t scratch_bytes = 0;
   int decode_ctas = 0;      // CTAs of the persistent decode kernel (all co-resident)
   bool use_decode_kernel = true;
-  int prefill_threshold = 256;  // token count from which wmoe_moe_forward uses the tcgen05 grouped GEMMs
+  int prefill_threshold = 16;  // token count from which wmoe_moe_forward uses the tcgen05 grouped GEMMs
   uint64_t* trace = nullptr;  // decode phase timestamps (device), or null
   size_t trace_entries = 0;
   // expert parallelism over the library's own NCCL communicator (wmoe_ep_init)
