@@ -72,7 +72,7 @@ int wmoe_set_prefill_threshold(wmoe_ctx* ctx, int tokens);
  * engines/base.py:384-390): with trace non-null, each CTA writes %globaltimer nanoseconds at WMOE_TRACE_POINTS
  * points of every layer into trace[(layer * WMOE_TRACE_POINTS + point) * ctas + cta] (device memory of at least
  * layers * WMOE_TRACE_POINTS * ctas entries; ctas from wmoe_decode_ctas). Null turns it off. */
-#define WMOE_TRACE_POINTS 12
+#define WMOE_TRACE_POINTS 16
 int wmoe_set_trace(wmoe_ctx* ctx, uint64_t* trace, size_t entries);
 int wmoe_decode_ctas(const wmoe_ctx* ctx);
 /* Reads and clears the device status word: 0, or the first WMOE_ERR_DEVICE cause a kernel recorded

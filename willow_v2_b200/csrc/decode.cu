@@ -9,9 +9,9 @@
 //   B   every CTA reads x_l (its own RMS scale r = 1/sqrt(mean(x^2) + eps) from it), sums the replicas in a
 //       fixed order and quantises x to int16; warp 0 forms logits r*S + bias and the same top-k routing on every
 //       CTA and its lanes at once issue TMA bulk copies (cp.async.bulk, mbarrier completion) of this CTA's 32
-//       gate/up row pairs in two chunks. CTA c < 144 owns h block c: 32 consecutive h values of one expert slot.
-//       Once the first chunk lands, this CTA's slice of down rows of all k+1 experts follows, streaming while
-//       gate_up computes. Warps compute gate and up rows (dp2a on the 4-bit codes) -> SwiGLU; warp 0 quantises
+//       gate/up row pairs in two chunks, and right behind them of its slice of down rows of all k+1 experts, so
+//       that the layer's whole expert stream is in flight together. CTA c < 144 owns h block c: 32 consecutive h
+//       values of one expert slot. Warps compute gate and up rows (dp2a on the 4-bit codes) -> SwiGLU; warp 0 quantises
 //       the block's 32 h values to int16 once and writes them to global memory in the order the down lanes read;
 //       the other warps unpack their Q6_K down codes into registers (independent of h).
 //   S2  all h blocks complete.
@@ -47,7 +47,7 @@ constexpr int kSaccStride = 264;                  // doubles per replica (>= kE 
 constexpr int kSaccRot = kReplicas * kSaccStride;  // doubles per rotation buffer
 constexpr int kMaxPairs = 2;                      // (row, slot) down pairs per 8-lane group
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
-constexpr int kTracePoints = 12;  // WMOE_TRACE_POINTS
+constexpr int kTracePoints = 16;  // WMOE_TRACE_POINTS
 
 struct DecodeParams {
   ExpertSource src;
@@ -165,10 +165,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       : "memory");
 }
 
+// An L2 prefetch of one line: used to have an address translation cached before a bulk copy needs it.
+__device__ __forceinline__ void touch(const void* ptr) { asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr)); }
+
 // ---------------------------------------------------------------- shared memory layout
 
 struct Small {
   uint64_t mbar_gu[2], mbar_dn, mbar_rs;
+  DecodeLayer layers[kMaxLayers];  // the layer table, copied once (parameter reads by layer index miss the cache)
   alignas(16) float x[kH];        // x_l as read (raw residual for a stack)
   alignas(16) int16_t xq[kH];     // quantised x, in gate_up lane order (see xq_offset)
   float xs[kH / 32];
@@ -184,7 +188,6 @@ struct Small {
   float bias[2][kE];              // the routing bias (zero without one), by layer parity
   float hblk[32];                 // this CTA's 32 h values
   float red[kWarps];
-  const uint8_t* dn_ptr[kSlots];
   int sel[kSlots];
   float w[kSlots];
   int order[kK];
@@ -193,27 +196,61 @@ struct Small {
   int dn_off;                     // offset of row r0 within each slot's down chunk
 };
 
-__device__ __forceinline__ float q4_dot_smem(const uint8_t* block, int g, const uint32_t* xw, float sx0, float sx1,
-                                             float sum0, float sum1) {
-  const uint4 hd = *reinterpret_cast<const uint4*>(block);
-  const uint4 q0 = *reinterpret_cast<const uint4*>(block + 16 + 32 * g);
-  const uint4 q1 = *reinterpret_cast<const uint4*>(block + 32 + 32 * g);
-  const float d = f16_to_f32(uint16_t(hd.x & 0xFFFF)), dmin = f16_to_f32(uint16_t(hd.x >> 16));
-  int sc0, mn0, sc1, mn1;
-  q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * g, sc0, mn0);
-  q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * g + 1, sc1, mn1);
-  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  int a0 = 0, a1 = 0;
+// Scale and min of sub-blocks j = 2g and 2g + 1 of a Q4_K super-block (6-bit values packed in the 12 bytes s0..s2,
+// ggml's get_scale_min_k4 layout), without a branch on g: byte k = j % 4 of each word, and for j >= 4 the high two
+// bits of the first eight bytes complete the 4-bit halves of the last four.
+__device__ __forceinline__ void q4k_scales_pair(uint32_t s0, uint32_t s1, uint32_t s2, int g, int& sc0, int& mn0,
+                                                int& sc1, int& mn1) {
+  const int k = (2 * g) & 3;
+  const bool hi = g >= 2;
+  const uint32_t a = __byte_perm(s0, 0, 0x4440 + k) | (__byte_perm(s0, 0, 0x4440 + k + 1) << 16);  // b[k], b[k+1]
+  const uint32_t b = __byte_perm(s1, 0, 0x4440 + k) | (__byte_perm(s1, 0, 0x4440 + k + 1) << 16);
+  const uint32_t c = __byte_perm(s2, 0, 0x4440 + k) | (__byte_perm(s2, 0, 0x4440 + k + 1) << 16);
+  // two 16-bit lanes at once: (sub-block 2g, sub-block 2g + 1)
+  const uint32_t sc = hi ? ((c & 0x000F000Fu) | ((a >> 2) & 0x00300030u)) : (a & 0x003F003Fu);
+  const uint32_t mn = hi ? (((c >> 4) & 0x000F000Fu) | ((b >> 2) & 0x00300030u)) : (b & 0x003F003Fu);
+  sc0 = int(sc & 0xFFFF), sc1 = int(sc >> 16), mn0 = int(mn & 0xFFFF), mn1 = int(mn >> 16);
+}
+
+// One lane's share of a gate row and an up row: 64 weights of each (super-block sb, nibble group g = sub-blocks 2g
+// and 2g + 1) against the int16 x codes in xw, with four independent accumulators per row.
+__device__ __forceinline__ float2 q4_dot_pair(const uint8_t* gate, const uint8_t* up, int g, const uint32_t* xw,
+                                              float sx0, float sx1, float sum0, float sum1) {
+  const uint4 hg = *reinterpret_cast<const uint4*>(gate), hu = *reinterpret_cast<const uint4*>(up);
+  const uint4 g0 = *reinterpret_cast<const uint4*>(gate + 16 + 32 * g);
+  const uint4 g1 = *reinterpret_cast<const uint4*>(gate + 32 + 32 * g);
+  const uint4 u0 = *reinterpret_cast<const uint4*>(up + 16 + 32 * g);
+  const uint4 u1 = *reinterpret_cast<const uint4*>(up + 32 + 32 * g);
+  const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const uint32_t uw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  int ga0 = 0, ga1 = 0, gb0 = 0, gb1 = 0, ua0 = 0, ua1 = 0, ub0 = 0, ub1 = 0;  // a: runs m even, b: m odd
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    const uint32_t lo = qw[m] & 0x0F0F0F0Fu, hi = (qw[m] >> 4) & 0x0F0F0F0Fu;
-    a0 = dp2a_lo(xw[2 * m], lo, a0);
-    a0 = dp2a_hi(xw[2 * m + 1], lo, a0);
-    a1 = dp2a_lo(xw[16 + 2 * m], hi, a1);
-    a1 = dp2a_hi(xw[17 + 2 * m], hi, a1);
+  for (int m = 0; m < 8; m += 2) {
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      const int mm = m + o;
+      const uint32_t glo = gw[mm] & 0x0F0F0F0Fu, ghi = (gw[mm] >> 4) & 0x0F0F0F0Fu;
+      const uint32_t ulo = uw[mm] & 0x0F0F0F0Fu, uhi = (uw[mm] >> 4) & 0x0F0F0F0Fu;
+      int& g_lo = o ? gb0 : ga0;
+      int& g_hi = o ? gb1 : ga1;
+      int& u_lo = o ? ub0 : ua0;
+      int& u_hi = o ? ub1 : ua1;
+      g_lo = dp2a_hi(xw[2 * mm + 1], glo, dp2a_lo(xw[2 * mm], glo, g_lo));
+      u_lo = dp2a_hi(xw[2 * mm + 1], ulo, dp2a_lo(xw[2 * mm], ulo, u_lo));
+      g_hi = dp2a_hi(xw[17 + 2 * mm], ghi, dp2a_lo(xw[16 + 2 * mm], ghi, g_hi));
+      u_hi = dp2a_hi(xw[17 + 2 * mm], uhi, dp2a_lo(xw[16 + 2 * mm], uhi, u_hi));
+    }
   }
-  return sx0 * ((d * float(sc0)) * float(a0) - (dmin * float(mn0)) * sum0) +
-         sx1 * ((d * float(sc1)) * float(a1) - (dmin * float(mn1)) * sum1);
+  int gsc0, gmn0, gsc1, gmn1, usc0, umn0, usc1, umn1;
+  q4k_scales_pair(hg.y, hg.z, hg.w, g, gsc0, gmn0, gsc1, gmn1);
+  q4k_scales_pair(hu.y, hu.z, hu.w, g, usc0, umn0, usc1, umn1);
+  const float gd = f16_to_f32(uint16_t(hg.x & 0xFFFF)), gdm = f16_to_f32(uint16_t(hg.x >> 16));
+  const float ud = f16_to_f32(uint16_t(hu.x & 0xFFFF)), udm = f16_to_f32(uint16_t(hu.x >> 16));
+  const int gs0 = ga0 + gb0, gs1 = ga1 + gb1, us0 = ua0 + ub0, us1 = ua1 + ub1;
+  return make_float2(sx0 * ((gd * float(gsc0)) * float(gs0) - (gdm * float(gmn0)) * sum0) +
+                         sx1 * ((gd * float(gsc1)) * float(gs1) - (gdm * float(gmn1)) * sum1),
+                     sx0 * ((ud * float(usc0)) * float(us0) - (udm * float(umn0)) * sum0) +
+                         sx1 * ((ud * float(usc1)) * float(us1) - (udm * float(umn1)) * sum1));
 }
 
 // Where x position pos lives in sm.xq: the gate_up lane (super-block pos/256, nibble group (pos%256)/64) reads its
@@ -285,7 +322,7 @@ __device__ void fetch_layer_meta(Small& sm, const DecodeParams& p, int li) {
   if (t < kE)
     sm.slot_row[li % 2][t] = p.src.slot_of[size_t(layer) * kE + t];
   else if (t < 2 * kE)
-    sm.bias[li % 2][t - kE] = p.layers[li].router_bias ? p.layers[li].router_bias[t - kE] : 0.f;
+    sm.bias[li % 2][t - kE] = sm.layers[li].router_bias ? sm.layers[li].router_bias[t - kE] : 0.f;
 }
 
 // int16 quantisation of 2048 values by 512 threads, 4 each (thread t holds positions 4t..4t+3 in v): a 32-value
@@ -372,11 +409,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sm.dn_off = int(unsigned(r0) * kRowBytesQ6 % 16);
   }
+  {
+    constexpr int kWords = int(sizeof(DecodeLayer) / sizeof(uint64_t));
+    static_assert(sizeof(DecodeLayer) % sizeof(uint64_t) == 0, "DecodeLayer holds pointers only");
+    for (int i = tid; i < p.n_layers * kWords; i += kThreads)
+      reinterpret_cast<uint64_t*>(sm.layers)[i] = reinterpret_cast<const uint64_t*>(p.layers)[i];
+  }
   __syncthreads();
 
   // ---------------- prologue: the first layer's router sums from the input rows of this CTA
   {
-    const DecodeLayer& L = p.layers[0];
+    const DecodeLayer& L = sm.layers[0];
     for (int i = tid; i < nrows; i += kThreads) {
       float v;
       if (p.x_dtype == kF32)
@@ -397,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
   for (int li = 0; li < p.n_layers; ++li) {
     const int layer = p.layer_begin + li;
-    const DecodeLayer& L = p.layers[li];
+    const DecodeLayer& L = sm.layers[li];
     const unsigned parity = unsigned(li & 1);
     const double* S = p.sacc + (li % 3) * kSaccRot;
     const bool last = li + 1 == p.n_layers;
@@ -414,17 +457,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         const float* xi = li == 0 ? static_cast<const float*>(p.x_in) : p.xbuf + (li % 2) * kH;
         v = __ldcg(reinterpret_cast<const float4*>(xi) + tid);
       }
-      reinterpret_cast<float4*>(sm.x)[tid] = v;
-      float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      ss = warp_sum(ss);
-      if (lane == 0) sm.red[warp] = ss;
-      quant_x(v, sm.xq, sm.xs, sm.xsum);  // the RMS factor is applied to the scales later
+      // the router-sum replicas are read while x is in flight (one L2 round trip for both) and summed first
       if (tid <= kE) {
         double acc = 0.0;
 #pragma unroll
         for (int r = 0; r < kReplicas; ++r) acc += __ldcg(S + r * kSaccStride + tid);
         sm.logit[tid] = float(acc);
       }
+      reinterpret_cast<float4*>(sm.x)[tid] = v;
+      float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      ss = warp_sum(ss);
+      if (lane == 0) sm.red[warp] = ss;
+      quant_x(v, sm.xq, sm.xs, sm.xsum);  // the RMS factor is applied to the scales later
       if (c == 0)  // this rotation buffer is next added into two layers on
         for (int i = tid; i < kSaccRot; i += kThreads) p.sacc[((li + 2) % 3) * kSaccRot + i] = 0.0;
     }
@@ -436,12 +480,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       const int layer1 = layer + 1;
       if (tid < kE)
         next_meta = p.src.slot_of[size_t(layer1) * kE + tid];
-      else if (tid < 2 * kE && p.layers[li + 1].router_bias)
-        next_meta = __float_as_int(p.layers[li + 1].router_bias[tid - kE]);
+      else if (tid < 2 * kE && sm.layers[li + 1].router_bias)
+        next_meta = __float_as_int(sm.layers[li + 1].router_bias[tid - kE]);
     }
     if (warp == 0) {
-      float t = 0.f;
-      for (int i = 0; i < kWarps; ++i) t += sm.red[i];
+      const float t = warp_sum(lane < kWarps ? sm.red[lane] : 0.f);
       const float rsc = p.stack ? 1.0f / sqrtf(t / float(kH) + p.eps) : 1.0f;
       // top-k by k rounds of two single-instruction warp reductions: the largest logit, then the smallest expert
       // id holding it (ties go to the lower id)
@@ -473,12 +516,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
           my_e = be;
         }
       }
-      // renormalised weights of the k picks: exp(l_i - l_0) / sum_j exp(l_j - l_0)
-      const float top0 = unordered(__shfl_sync(0xffffffffu, my_key, 0));
-      const float my_ex = lane < kK ? expf(unordered(my_key) - top0) : 0.f;
-      float sum = my_ex;
-#pragma unroll
-      for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);  // lanes 0..7
       WMOE_TRACE(li, 2);
       // expert addresses of the k+1 slots (lane s holds slot s)
       const uint8_t *gu = nullptr, *dn = nullptr;
@@ -495,7 +532,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             set_status(p.status, kStatusNotResident);
           }
         }
-        sm.dn_ptr[lane] = dn;
         sm.sel[lane] = my_e;
       }
       // this CTA's 32 gate/up row pairs: lanes 0-3 issue the four copies at once (chunk = 16 pairs)
@@ -509,7 +545,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                              size_t(up * kF + blk_j0 + 16 * ch) * kRowBytesQ4;
         bulk_g2s(gu_buf + ch * kChunkBytes + up * (kChunkBytes / 2), src, kChunkBytes / 2, &sm.mbar_gu[ch]);
       }
+      // right behind them, down rows [r0, r1) of every slot (aligned outward to 16 bytes): the whole layer's stream
+      // is in flight at once (issuing the down rows only after the first gate_up chunk had landed left HBM half idle)
+      {
+        const unsigned lo = unsigned(r0) * kRowBytesQ6 / 16 * 16;
+        const unsigned hi = (unsigned(r1) * kRowBytesQ6 + 15) / 16 * 16;
+        const unsigned present = __popc(__ballot_sync(0xffffffffu, lane < kSlots && dn != nullptr));
+        if (lane == 0) mbar_arrive_expect_tx(&sm.mbar_dn, present * (hi - lo));
+        __syncwarp();
+        if (lane < kSlots && dn) bulk_g2s(dn_buf + size_t(lane) * dn_chunk, dn + lo, hi - lo, &sm.mbar_dn);
+      }
       WMOE_TRACE(li, 3);
+      // renormalised weights of the k picks: exp(l_i - l_0) / sum_j exp(l_j - l_0)
+      const float top0 = unordered(__shfl_sync(0xffffffffu, my_key, 0));
+      const float my_ex = lane < kK ? expf(unordered(my_key) - top0) : 0.f;
+      float sum = my_ex;
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);  // lanes 0..7
       if (lane < kK) {
         sm.w[lane] = my_ex / sum;
         if (c == 0 && p.topk_idx_out) p.topk_idx_out[li * kK + lane] = my_e;
@@ -526,19 +578,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     __syncthreads();
     WMOE_TRACE(li, 4);
     // the next layer's router slice, overlapping the copies (waited for before it is used in phase C)
-    const bool rs_copy = p.stack && !last && fetch_router_slice(sm, p.layers[li + 1], r0, nrows);
+    const bool rs_copy = p.stack && !last && fetch_router_slice(sm, sm.layers[li + 1], r0, nrows);
     if (!mbar_wait(&sm.mbar_gu[0], parity, p.status, &sm.abort_flag)) return;
     WMOE_TRACE(li, 5);
-    if (tid == 0) {
-      // down rows [r0, r1) of every slot, aligned outward to 16 bytes, after the first gate_up chunk
-      const unsigned lo = unsigned(r0) * kRowBytesQ6 / 16 * 16;
-      const unsigned hi = (unsigned(r1) * kRowBytesQ6 + 15) / 16 * 16;
-      int present = 0;
-      for (int s = 0; s < kSlots; ++s) present += sm.dn_ptr[s] ? 1 : 0;
-      mbar_arrive_expect_tx(&sm.mbar_dn, unsigned(present) * (hi - lo));
-      for (int s = 0; s < kSlots; ++s)
-        if (sm.dn_ptr[s]) bulk_g2s(dn_buf + size_t(s) * dn_chunk, sm.dn_ptr[s] + lo, hi - lo, &sm.mbar_dn);
-    }
     if (has_block) {
       const int sb = lane / 4, g = lane % 4;
       uint32_t xw[32];
@@ -554,18 +596,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       const float sum1 = float(sm.xsum[sb * 16 + 4 * g + 2] + sm.xsum[sb * 16 + 4 * g + 3]);
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) {
-        if (ch == 1 && !mbar_wait(&sm.mbar_gu[1], parity, p.status, &sm.abort_flag)) return;
+        if (ch == 1) {
+          WMOE_TRACE(li, 6);
+          if (!mbar_wait(&sm.mbar_gu[1], parity, p.status, &sm.abort_flag)) return;
+          WMOE_TRACE(li, 7);
+        }
         const uint8_t* gate = gu_buf + ch * kChunkBytes + warp * kRowBytesQ4 + sb * Q4K_BYTES;
         const uint8_t* up = gate + kChunkBytes / 2;
-        float gs = q4_dot_smem(gate, g, xw, sx0, sx1, sum0, sum1);
-        float us = q4_dot_smem(up, g, xw, sx0, sx1, sum0, sum1);
-        gs = warp_sum(gs);
-        us = warp_sum(us);
+        const float2 gu = q4_dot_pair(gate, up, g, xw, sx0, sx1, sum0, sum1);
+        float gs = gu.x, us = gu.y;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          gs += __shfl_xor_sync(0xffffffffu, gs, o);
+          us += __shfl_xor_sync(0xffffffffu, us, o);
+        }
         if (lane == 0) sm.hblk[16 * ch + warp] = silu(gs) * us;
       }
     }
+    if (!has_block) {
+      WMOE_TRACE(li, 6);
+      WMOE_TRACE(li, 7);
+    }
     __syncthreads();
-    WMOE_TRACE(li, 6);
+    WMOE_TRACE(li, 8);
     // the block's h, quantised once, in the order the down lanes read it; then this CTA arrives at S2
     if (warp == 0) {
       if (has_block) {
@@ -582,18 +635,40 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int sb = t8 / 4, hh = (t8 / 2) % 2, pq = 16 * (t8 % 2);
     const int base = sb * 256 + hh * 128 + pq;
     DownPair dp[kMaxPairs];
+    WMOE_TRACE(li, 9);
     if (!mbar_wait(&sm.mbar_dn, parity, p.status, &sm.abort_flag)) return;
+    WMOE_TRACE(li, 10);
 #pragma unroll
     for (int k = 0; k < kMaxPairs; ++k) {
       const int pr = grp + k * (kThreads / 8);
       if (pr < nrows * kSlots) {
         const int rl = pr / kSlots, slot = pr % kSlots;
         down_unpack(dn_buf + size_t(slot) * dn_chunk + sm.dn_off + rl * kRowBytesQ6 + sb * Q6K_BYTES, hh, pq, dp[k]);
+      } else {
+        dp[k] = DownPair{};  // past the CTA's rows: computed on, never stored
       }
     }
-    WMOE_TRACE(li, 7);
+    // while S2 completes: the address translations of the next layer's experts. A layer's copies come from 9 of
+    // 20 GB of expert pages, and a translation miss delays a bulk copy at issue and again at completion; each CTA
+    // touches both pages that each expert blob of its share (expert e on CTA e % nc) can span, and the shared
+    // expert's.
+    if (!last) {
+      if (tid < kE && tid % nc == c && next_meta >= 0) {
+        const uint8_t* b = p.src.slab + size_t(next_meta) * p.src.slot_bytes;
+        touch(b);
+        touch(b + p.src.slot_bytes - 1);
+      }
+      if (tid == kE && c == nc - 1) {
+        const DecodeLayer& N = sm.layers[li + 1];
+        touch(N.shared_gate_up);
+        touch(N.shared_gate_up + 2 * kF * kRowBytesQ4 - 1);
+        touch(N.shared_down);
+        touch(N.shared_down + kH * kRowBytesQ6 - 1);
+      }
+    }
+    WMOE_TRACE(li, 11);
     if (!grid_wait(p.bar, epoch, p.status, &sm.abort_flag)) return;
-    WMOE_TRACE(li, 8);
+    WMOE_TRACE(li, 12);
 
     // ---------------- phase C: h, down rows of this CTA, combine, next layer's router sums
     if (!last) {  // the next layer's slot row and bias (read by its top-k after S1)
@@ -603,46 +678,62 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         sm.bias[(li + 1) % 2][tid - kE] = __int_as_float(next_meta);
     }
     {
-      constexpr int kVec = kSlots * kF / 8;  // 576 runs of 8 int16
+      // every load issued before any store: one L2 round trip
+      constexpr int kVec = kSlots * kF / 8, kScales = kSlots * kF / 32, kSums = kSlots * kF / 16;
+      static_assert(kVec > kThreads && kVec <= 2 * kThreads && kScales <= kThreads && kSums <= kThreads, "h sizes");
       const uint4* src = reinterpret_cast<const uint4*>(p.hq);
       uint4* dst = reinterpret_cast<uint4*>(&sm.hq[0][0]);
-      for (int i = tid; i < kVec; i += kThreads) dst[i] = __ldcg(src + i);
-      for (int i = tid; i < kSlots * kF / 32; i += kThreads) (&sm.hs[0][0])[i] = __ldcg(p.hs + i);
-      for (int i = tid; i < kSlots * kF / 16; i += kThreads) (&sm.hsum[0][0])[i] = __ldcg(p.hsum + i);
+      const bool two = tid + kThreads < kVec;
+      const uint4 v0 = __ldcg(src + tid);
+      const uint4 v1 = two ? __ldcg(src + tid + kThreads) : make_uint4(0u, 0u, 0u, 0u);
+      const float hs = tid < kScales ? __ldcg(p.hs + tid) : 0.f;
+      const int hsum = tid < kSums ? __ldcg(p.hsum + tid) : 0;
+      dst[tid] = v0;
+      if (two) dst[tid + kThreads] = v1;
+      if (tid < kScales) (&sm.hs[0][0])[tid] = hs;
+      if (tid < kSums) (&sm.hsum[0][0])[tid] = hsum;
     }
     __syncthreads();
-    WMOE_TRACE(li, 9);
+    WMOE_TRACE(li, 13);
     {
+      // both pairs of the thread at once (a pair past the CTA's rows computes on unused codes and is not stored);
+      // the four quarters of a pair summed as a tree
       const unsigned gmask = 0xFFu << (8 * (lane / 8));
+      float part[kMaxPairs];
 #pragma unroll
       for (int k = 0; k < kMaxPairs; ++k) {
         const int pr = grp + k * (kThreads / 8);
-        if (pr >= nrows * kSlots) break;  // uniform within the 8-lane group
-        const int rl = pr / kSlots, slot = pr % kSlots;
-        float part = 0.f;
+        const int slot = pr % kSlots;
+        float t[4];
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
           // runs of 8 of this lane task: (s, 0) and (s, 1), each group's eight tasks adjacent
           const uint4* xp = reinterpret_cast<const uint4*>(sm.hq[slot]) + (s * 2) * 8 + t8;
           const uint4 xa = xp[0], xb = xp[8];
           const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-          int acc = 0;
+          int acc0 = 0, acc1 = 0;
 #pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            acc = dp2a_lo(xw[2 * m], dp[k].q[s][m], acc);
-            acc = dp2a_hi(xw[2 * m + 1], dp[k].q[s][m], acc);
+          for (int m = 0; m < 4; m += 2) {
+            acc0 = dp2a_hi(xw[2 * m + 1], dp[k].q[s][m], dp2a_lo(xw[2 * m], dp[k].q[s][m], acc0));
+            acc1 = dp2a_hi(xw[2 * m + 3], dp[k].q[s][m + 1], dp2a_lo(xw[2 * m + 2], dp[k].q[s][m + 1], acc1));
           }
           const int pos = base + 32 * s;
-          part += sm.hs[slot][pos / 32] * (dp[k].D[s] * float(acc - 32 * sm.hsum[slot][pos / 16]));
+          t[s] = sm.hs[slot][pos / 32] * (dp[k].D[s] * float(acc0 + acc1 - 32 * sm.hsum[slot][pos / 16]));
         }
-        part += __shfl_xor_sync(gmask, part, 4);
-        part += __shfl_xor_sync(gmask, part, 2);
-        part += __shfl_xor_sync(gmask, part, 1);
-        if (t8 == 0) sm.ys[rl][slot] = part;
+        part[k] = (t[0] + t[1]) + (t[2] + t[3]);
+      }
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+        for (int k = 0; k < kMaxPairs; ++k) part[k] += __shfl_xor_sync(gmask, part[k], o);
+#pragma unroll
+      for (int k = 0; k < kMaxPairs; ++k) {
+        const int pr = grp + k * (kThreads / 8);
+        if (t8 == 0 && pr < nrows * kSlots) sm.ys[pr / kSlots][pr % kSlots] = part[k];
       }
     }
     __syncthreads();
-    WMOE_TRACE(li, 10);
+    WMOE_TRACE(li, 14);
     if (tid < nrows) {
       const int r = r0 + tid;
       float acc = 0.f;
@@ -667,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       if (rs_copy) rs_phase ^= 1u;
       __syncthreads();
       add_router_part(sm, p.sacc + ((li + 1) % 3) * kSaccRot + replica * kSaccStride, nrows);
-      WMOE_TRACE(li, 11);
+      WMOE_TRACE(li, 15);
       if (!grid_barrier(p.bar, ++epoch, p.status, &sm.abort_flag)) return;
     }
   }

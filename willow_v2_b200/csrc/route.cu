@@ -180,23 +180,24 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
-  const float* row = logits + size_t(t) * (E + 1);
+  const float* row = splits == 0 ? logits + size_t(t) * (E + 1) : logits + size_t(t) * E;
   float v[PER_LANE];
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) v[i] = lane + 32 * i < E ? row[lane + 32 * i] : -INFINITY;
+  // partial sums added in order, each pass issuing the loads of all of a lane's logits at once
+  for (int s = 1; s < splits; ++s) {
+    const float* part = logits + (size_t(s) * T + t) * E;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i)
+      if (lane + 32 * i < E) v[i] += part[lane + 32 * i];
+  }
 #pragma unroll
   for (int i = 0; i < PER_LANE; ++i) {
     const int e = lane + 32 * i;
-    float l = -INFINITY;
     if (e < E) {
-      if (splits == 0) {
-        l = row[e];
-      } else {
-        l = logits[size_t(t) * E + e];
-        for (int s = 1; s < splits; ++s) l += logits[(size_t(s) * T + t) * E + e];
-      }
-      if (bias) l += bias[e];
-      if (logits_out) logits_out[size_t(t) * E + e] = l;
+      if (bias) v[i] += bias[e];
+      if (logits_out) logits_out[size_t(t) * E + e] = v[i];
     }
-    v[i] = l;
   }
   float top0 = 0.f, sum = 0.f;
   float sel_l = 0.f;
@@ -243,6 +244,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
       sl = row[E];
     } else {
       float acc = 0.f;
+#pragma unroll 4
       for (int h = lane * 4; h < H; h += 128) {
         const float4 w = __ldg(reinterpret_cast<const float4*>(g + h));
         const float4 xv = x_dtype == kF32 ? load4<float>(static_cast<const float*>(x) + size_t(t) * H + h)

@@ -14,8 +14,9 @@ from . import moe, synth
 from .lib import lib
 
 POINTS = ["layer start", "x + router sums read", "top-k done (warp 0)", "gate_up copies issued (warp 0)",
-          "x quantised, routing published", "gate_up chunk 0 landed", "gate_up done", "down codes unpacked",
-          "after S2", "h copied in", "down dot products", "combine + router sums"]
+          "x quantised, routing published", "gate_up chunk 0 landed", "gate_up chunk 0 computed",
+          "gate_up chunk 1 landed", "gate_up done", "h published (S2 arrive)", "down rows landed",
+          "down codes unpacked", "after S2", "h copied in", "down dot products", "combine + router sums"]
 
 
 def synthetic_stack(layers: int, seed: int = 0, ctx=None):
