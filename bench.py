@@ -7,10 +7,16 @@ Metric: tokens/s; the roofline line reports the expert-weight HBM bandwidth agai
 At N > 1 GPUs (torchrun) every rank serves its own token stream with its own full store (decode does not shard:
 "replicas only"), value = total tokens/s over all ranks, time = max over ranks.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode40|prefill4096]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload decode40|batch64|prefill4096|prefill32k]
 
 --workload batch64: 64 f32 tokens through one MoE layer with Zipf-biased routing (the
-dequant-GEMV path); tokens/s and HBM GB/s over the distinct experts each step touches.
+sliced router, the dispatch sort and the grouped GEMMs); tokens/s and HBM GB/s over the distinct experts each step
+touches.
+
+--workload prefill32k: 32768 bf16 tokens through 40 layers with Zipf routing and a 4 GiB
+expert store per GPU (experts over the cap stream from pinned host memory, the next layer prefetched); expert
+parallel under torchrun. Run with few steps: `--steps 3 --warmup 3`.
 
 --workload prefill4096: one MoE layer on 4096 bf16 tokens with uniform routing (~128
 tokens per expert) through the tcgen05 grouped GEMMs; tokens/s, with the dominant GEMM launch against the measured
@@ -53,6 +59,10 @@ PREFILL_T = 4096
 METRIC_PREFILL = "MoE prefill tokens/s (one qwen35moe MoE layer, 4096 bf16 tokens per step)"
 # useful expert-product FLOPs of one prefill layer: every token through 8 routed experts + the shared expert,
 # gate_up [2F x H] then down [H x F]
+PF32_T = 32768
+PF32_CAP = 4 << 30  # expert-store cap per GPU
+METRIC_PF32 = ("MoE prefill tokens/s (40-layer qwen35moe stack, 32768 bf16 tokens per step, Zipf routing, "
+               "4 GiB expert store per GPU)")
 GATE_UP_FLOPS = 2 * PREFILL_T * (TOP_K + 1) * (2 * FFN) * HIDDEN   # 154.6 GFLOP
 DOWN_FLOPS = 2 * PREFILL_T * (TOP_K + 1) * HIDDEN * FFN             # 77.3 GFLOP
 
@@ -452,6 +462,147 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
     return result, (ctx, store, lw)
 
 
+def run_prefill32k(args, rank: int, world: int, dist):
+    """32768 bf16 tokens (32768 / N per rank) through 40 MoE layers with Zipf(1.1)-biased routing (a
+    per-layer permutation), experts partitioned 256/N per GPU, each GPU's expert store capped at 4 GiB: the experts
+    over the cap live in pinned host memory and stream in on the store's side stream. While layer l runs, layer
+    l + 1's experts are prefetched (a prefill batch reads most of them); after the first warm-up pass, 75% of the
+    slots keep the hot set chosen by token counts (store.py:464-484). Residual + RMSNorm between layers
+    (wmoe_add_rmsnorm). Strong scaling: the 32768 tokens are split over the ranks."""
+    import torch
+    from willow_v2_b200 import lib as L
+    from willow_v2_b200 import moe, synth
+    device = torch.cuda.current_device()
+    ctx = moe.Context(device)
+    per = EXPERTS // world
+    n_layers = args.layers
+    store = moe.ExpertStore(n_layers, EXPERTS, HIDDEN, FFN, cap_bytes=PF32_CAP, ctx=ctx,
+                            expert_range=(rank * per, (rank + 1) * per))
+    store.fill_synthetic(SEED)
+    lws = [moe.LayerWeights(router_w=torch.from_numpy(synth.router_weight(SEED, l)).cuda(),
+                            shared_gate=torch.from_numpy(synth.shared_gate_weight(SEED, l)).cuda(),
+                            shared_gate_up=torch.from_numpy(synth.expert_gate_up(SEED, l, EXPERTS).reshape(-1)).cuda(),
+                            shared_down=torch.from_numpy(synth.expert_down(SEED, l, EXPERTS).reshape(-1)).cuda(),
+                            router_bias=torch.from_numpy(synth.zipf_bias(SEED + l)).cuda()).prepare(ctx, decode=False)
+           for l in range(n_layers)]
+    T = PF32_T // world
+    h0 = torch.from_numpy(synth.hidden(SEED, PF32_T, step=99)[rank * T:(rank + 1) * T]).cuda()
+    h = torch.empty_like(h0)
+    stream = torch.cuda.current_stream()
+    if world > 1:
+        moe.ep_init(ctx)
+        L.lib.wmoe_ep_set_chunks(ctx.handle, max(1, world // 2))
+        fwd = moe.moe_forward_ep_native
+    else:
+        fwd = moe.moe_forward
+
+    def stack(h):
+        out = None
+        for l in range(n_layers):
+            h, hn = moe.add_rmsnorm(h, out, out_dtype=torch.bfloat16)
+            out = fwd(store, l, hn, lws[l], out_dtype=torch.bfloat16)
+            store.prefetch((l + 1) % n_layers)  # copies overlap layer l's experts
+        return moe.add_rmsnorm(h, out, out_dtype=torch.bfloat16)[0]
+
+    K, W = args.steps, args.warmup
+    for s in range(W):
+        h.copy_(h0)
+        stack(h)
+        if s == 0:
+            store.choose_hot(0.75)  # usage of the first pass
+    torch.cuda.synchronize()
+    ctx.check_device()
+    # pinned host -> device bandwidth of this GPU, for the H2D roofline
+    pin = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    dev.copy_(pin, non_blocking=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    dev.copy_(pin, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    h2d_peak = (1 << 30) / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    del pin, dev
+    st0 = store.stats()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        ev0.record(stream)
+        for s in range(K):
+            h.copy_(h0)
+            stack(h)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    gpu_launches = ctx.launches - launches0
+    ms = ev0.elapsed_time(ev1) / K
+    st1 = store.stats()
+    ctx.check_device()
+    # end to end through the public calls: the step's tokens from pinned host memory, the result back, every step
+    h_host = h0.cpu().pin_memory()
+    o_host = torch.empty_like(h_host).pin_memory()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for s in range(K):
+        h.copy_(h_host, non_blocking=True)
+        o_host.copy_(stack(h), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    ctx.check_device()
+    if world > 1:
+        ctx.ep_finalize()
+    bytes_in = (st1["bytes_in"] - st0["bytes_in"]) / K
+    calls = (st1["hits"] + st1["misses"]) - (st0["hits"] + st0["misses"])
+    hit_rate = (st1["hits"] - st0["hits"]) / calls if calls else 1.0
+    times = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = times.tolist()
+    _, bf16, peak_kind = peaks()
+    flops = n_layers * PF32_T * (TOP_K + 1) * 6_291_456 // world  # this rank's share of the expert products
+    tflops = flops / (ms * 1e-3) / 1e12
+    h2d_gbs = bytes_in / (ms * 1e-3) / 1e9
+    result = {
+        "metric": METRIC_PF32, "value": PF32_T * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 accumulation",
+        "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks; bf16 N(0,1) tokens; per-layer Zipf(1.1) routing bias)",
+        "config": {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, 4 GiB cap",
+                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": n_layers,
+                   "tokens_per_step": PF32_T, "tokens_per_rank": T,
+                   "parallelism": f"ep{world}" if world > 1 else "single GPU", "experts_per_rank": per,
+                   "store_cap_bytes": PF32_CAP, "store_slots": int(PF32_CAP // ((EXPERT_BYTES + 255) // 256 * 256)),
+                   "hot_share": 0.75,
+                   "l2": "inputs larger than L2: 268 MB residual stream per rank and up to 21 GB of experts"},
+        "roofline": {"bound": "tensor", "kernel": "whole 40-layer step (expert products / step time), rank 0",
+                     "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16, "traffic": None,
+                     "peak_kind": peak_kind, "algorithmic_flops_per_launch": flops, "launch_ms": ms},
+        "h2d": {"bytes_per_step": bytes_in, "achieved_gbs": h2d_gbs, "peak_gbs_measured": h2d_peak,
+                "frac": h2d_gbs / h2d_peak if h2d_peak else None, "store_hit_rate": hit_rate,
+                "prefetched_per_step": (st1["prefetched"] - st0["prefetched"]) / K,
+                "prefetch_used_per_step": (st1["prefetch_used"] - st0["prefetch_used"]) / K,
+                "note": "rank 0; expert blobs copied from pinned host memory per step (misses and prefetches)"},
+        "e2e": {"value": PF32_T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 4,
+                "d2h_bytes_per_step": T * HIDDEN * 4},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks.summary(),
+    }
+    return result, (ctx, store, lws)
+
+
+def cpu_baseline_prefill32k():
+    """The oracle port timed as for configs[3] (router + dequantised expert FFNs, 9 experts a token): per-token work
+    does not depend on the routing skew, so the 40-layer rate is the one-layer rate / 40."""
+    base = cpu_baseline_prefill()
+    return {"value": base["value"] / LAYERS, "unit": "tokens/s", "cores": base["cores"], "kind": "port",
+            "sample": base["sample"] + "; divided by 40 layers"}
+
+
 def run_prefill4096(args, rank: int, world: int, dist):
     import torch
     from willow_v2_b200 import lib as L
@@ -618,6 +769,20 @@ def run_reference(args, rank, world):
     """The reference arm: the CPU restatement of willow's CPU path on the host cores, rank 0 only."""
     if rank != 0:
         return None
+    if args.workload == "prefill32k":
+        K, W = args.steps, args.warmup
+        vals = [cpu_baseline_prefill(sample_experts=8)["value"] / LAYERS for _ in range(W + K)][W:]
+        value = statistics.mean(vals)
+        base = cpu_baseline_prefill(sample_experts=8)
+        return {"metric": METRIC_PF32, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": PF32_T / value * 1e3, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, 4 GiB cap",
+                           "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": LAYERS,
+                           "tokens_per_step": PF32_T},
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                 "sample": "each step: " + base["sample"] + "; divided by 40 layers"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload == "prefill4096":
         K, W = args.steps, args.warmup
         vals = [cpu_baseline_prefill(sample_experts=8)["value"] for _ in range(W + K)][W:]
@@ -674,7 +839,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode40", choices=["decode40", "batch64", "prefill4096"])
+    ap.add_argument("--workload", default="decode40", choices=["decode40", "batch64", "prefill4096", "prefill32k"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="stack depth (40 = the benchmark; fewer = profiling)")
     args = ap.parse_args()
@@ -701,6 +866,10 @@ def main():
         result, _keep = run_prefill4096(args, rank, world, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline_prefill()
+    elif args.workload == "prefill32k":
+        result, _keep = run_prefill32k(args, rank, world, dist)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_prefill32k()
     elif args.workload == "batch64":
         result, _keep = run_batch64(args, rank, world, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

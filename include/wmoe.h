@@ -126,6 +126,18 @@ size_t wmoe_store_blob_bytes(const wmoe_store* store);
 /* Makes the given experts of a layer resident (copies misses from the host copy on the store's side stream;
  * the compute stream waits for them). Returns WMOE_ERR_CAPACITY if they cannot all fit at once. */
 int wmoe_store_prepare(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream);
+/* Starts copying the given experts of a coming layer (experts null: every expert of the layer the store holds,
+ * as a prefill batch reads most of them) without making the compute stream wait; the call that uses them waits
+ * for those copies only. Takes only slots that neither the last call nor a pending prefetch holds, and copies as
+ * many as fit; unused ones become ordinary cached slots once their layer runs. Replaces ExpertStore.prefetch and
+ * collect_prefetches (gguf/store.py:204-232). No-op on an uncapped store. */
+int wmoe_store_prefetch(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream);
+/* Picks the hot set: the `share` of the slots (0..1) that go to the experts routed the most tokens so far (counted
+ * by every call on a capped store); they are evicted only when no other slot can go. Replaces
+ * ExpertStore.choose_hot and record_usage (gguf/store.py:464-484). */
+int wmoe_store_choose_hot(wmoe_store* store, double share);
+/* Counters: experts copied by prefetches, and how many of those a call read before they were evicted. */
+int wmoe_store_prefetch_stats(const wmoe_store* store, uint64_t* prefetched, uint64_t* prefetch_used);
 /* Copies one blob back to host memory (from its slot, or the host copy of a capped store); synchronous. */
 int wmoe_store_download(wmoe_store* store, int layer, int expert, void* host_dst, void* stream);
 /* Device address of a resident blob, or null. */
@@ -277,6 +289,12 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
 int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
                               const wmoe_layer_weights* layers, float eps, const float* h_in, float* h_out,
                               int32_t* topk_idx_out, void* stream);
+
+/* Residual add + RMS normalisation between MoE layers (engines/qwen36/model.py:17-22, engines/base.py:27-32,
+ * weight 1): x_out = x + y (y optional, f32 or bf16), xn_out = x_out / sqrt(mean(x_out^2) + eps) as f32 or bf16.
+ * x, x_out f32 [T, hidden]; x_out may be x. 16-byte aligned buffers, hidden % 4 == 0. */
+int wmoe_add_rmsnorm(wmoe_ctx* ctx, const float* x, const void* y, int y_dtype, int T, int hidden, float eps,
+                     float* x_out, void* xn_out, int xn_dtype, void* stream);
 
 /* Several experts' [rows, k] Q4_K or Q6_K weights times one token: y[i] = W_i x for i < n.
  * weights: device array of n device pointers; x f32 [k]; y f32 [n, rows]. */

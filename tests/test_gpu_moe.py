@@ -338,6 +338,87 @@ def test_capped_store_matches_resident(model):
     capped.close()
 
 
+def test_prefetch_matches_resident(model):
+    """Prefetching the next layer's experts (all of them, as for a prefill batch) while a layer runs: results stay
+    bit-identical to the resident store, and calls read the prefetched copies."""
+    import torch
+    from willow_v2_b200 import moe
+    ctx, store, layers = model
+    blob = (store.blob_bytes + 255) // 256 * 256
+    capped = moe.ExpertStore(LAYERS, cap_bytes=300 * blob, ctx=ctx)
+    capped.fill_synthetic(SEED)
+    x = torch.from_numpy(synth.hidden(SEED, 16, step=6)).cuda()
+    for _ in range(2):
+        for layer in range(LAYERS):
+            a = moe.moe_forward(store, layer, x, layers[layer])
+            b = moe.moe_forward(capped, layer, x, layers[layer])
+            capped.prefetch((layer + 1) % LAYERS)
+            torch.cuda.synchronize()
+            assert torch.equal(a, b), layer
+    st = capped.stats()
+    assert st["prefetched"] > 0 and 0 < st["prefetch_used"] <= st["prefetched"], st
+    assert st["bytes_in"] == st["misses"] * store.blob_bytes
+    ctx.check_device()
+    capped.close()
+
+
+def test_hot_set_survives_a_scan(model):
+    """After one pass over the layers, choose_hot(0.5) keeps the experts routed the most tokens (store.py:464-480):
+    a second pass evicts from the other slots, so every hot expert is still resident after it."""
+    import torch
+    from willow_v2_b200 import moe
+    ctx, store, layers = model
+    blob = (store.blob_bytes + 255) // 256 * 256
+    cap_slots = 200
+    capped = moe.ExpertStore(LAYERS, cap_bytes=cap_slots * blob, ctx=ctx)
+    capped.fill_synthetic(SEED)
+    x = torch.from_numpy(synth.hidden(SEED, 16, step=7)).cuda()
+    usage = np.zeros(LAYERS * 256, dtype=np.int64)
+    for layer in range(LAYERS):
+        _, _, sel = moe.moe_forward(capped, layer, x, layers[layer], return_routing=True)
+        usage[layer * 256:(layer + 1) * 256] += np.bincount(sel.cpu().numpy().reshape(-1), minlength=256)
+    capped.choose_hot(0.5)
+    used = np.flatnonzero(usage)
+    hot = used[np.argsort(-usage[used], kind="stable")][:cap_slots // 2]
+    for layer in range(LAYERS):
+        moe.moe_forward(capped, layer, x, layers[layer])
+    torch.cuda.synchronize()
+    missing = [int(k) for k in hot if capped.blob_ptr(int(k) // 256, int(k) % 256) is None]
+    assert not missing, missing
+    ctx.check_device()
+    capped.close()
+
+
+def test_add_rmsnorm_matches_oracle(model):
+    """The layer glue x <- x + y, xn = rms_norm(x) (engines/qwen36/model.py:17-22, engines/base.py:27-32): x in
+    place (f32), xn as f32 and bf16; then a 3-layer prefill stack through it against the oracle's stack."""
+    import torch
+    from willow_v2_b200 import moe
+    ctx, store, layers = model
+    rng = np.random.default_rng(5)
+    x0 = rng.standard_normal((300, 2048)).astype(np.float32)
+    y = torch.from_numpy(rng.standard_normal((300, 2048)).astype(np.float32)).to(torch.bfloat16)
+    x = torch.from_numpy(x0.copy()).cuda()
+    x, xn = moe.add_rmsnorm(x, y.cuda(), out_dtype=torch.float32)
+    ref_x = x0 + y.float().numpy()
+    np.testing.assert_array_equal(x.cpu().numpy(), ref_x)
+    np.testing.assert_allclose(xn.cpu().numpy(), ora.rms_norm(ref_x), rtol=2e-6, atol=1e-6)
+    _, xb = moe.add_rmsnorm(torch.from_numpy(x0.copy()).cuda(), None, out_dtype=torch.bfloat16)
+    np.testing.assert_allclose(xb.float().cpu().numpy(), ora.rms_norm(x0), rtol=8e-3, atol=1e-6)
+    # the stack of engines/qwen36/model.py:17-22 for 64 tokens: h <- h + moe(rms_norm(h))
+    h0 = synth.hidden(SEED, 64, step=13)
+    h = torch.from_numpy(h0.copy()).cuda()
+    out = None
+    for layer in range(LAYERS):
+        h, hn = moe.add_rmsnorm(h, out, out_dtype=torch.float32)
+        out = moe.moe_forward(store, layer, hn, layers[layer], out_dtype=torch.float32)
+    h, _ = moe.add_rmsnorm(h, out, out_dtype=torch.float32)
+    ref = ora.moe_stack(h0, [oracle_layer(l) for l in range(LAYERS)])
+    # each grouped-GEMM layer adds ~4e-4 (fp16 operands) and the residual stack compounds it (measured 1.3e-3)
+    assert rel_l2(h.cpu().numpy(), ref) < TOL
+    ctx.check_device()
+
+
 def test_cap_too_small_is_an_error(model):
     import torch
     from willow_v2_b200 import moe

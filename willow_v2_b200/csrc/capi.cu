@@ -361,6 +361,52 @@ const uint8_t* wmoe_store_blob(const wmoe_store* store, int layer, int expert) {
   return slot < 0 ? nullptr : store->d_slab + size_t(slot) * store->slot_stride;
 }
 
+int wmoe_store_prefetch(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream) {
+  if (!store) return WMOE_ERR_INVALID;
+  if (n < 0 || (n > 0 && !experts))
+    return ctx_fail(store->ctx, WMOE_ERR_INVALID, "wmoe_store_prefetch: bad expert list");
+  std::vector<int32_t> all;
+  if (!experts) {  // every expert of the layer the store holds (a prefill batch reads most of them)
+    for (int e = store->expert_begin; e < store->expert_end; ++e) all.push_back(e);
+    experts = all.data();
+    n = int(all.size());
+  }
+  return store_prefetch(store, layer, experts, n, static_cast<cudaStream_t>(stream));
+}
+
+int wmoe_store_choose_hot(wmoe_store* store, double share) {
+  if (!store) return WMOE_ERR_INVALID;
+  return store_choose_hot(store, share);
+}
+
+int wmoe_store_prefetch_stats(const wmoe_store* store, uint64_t* prefetched, uint64_t* prefetch_used) {
+  if (!store) return WMOE_ERR_INVALID;
+  if (prefetched) *prefetched = store->prefetched;
+  if (prefetch_used) *prefetch_used = store->prefetch_used;
+  return WMOE_OK;
+}
+
+int wmoe_add_rmsnorm(wmoe_ctx* ctx, const float* x, const void* y, int y_dtype, int T, int hidden, float eps,
+                     float* x_out, void* xn_out, int xn_dtype, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (T < 0 || hidden <= 0 || hidden % 4 || !(eps >= 0.f))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_add_rmsnorm: bad shape or eps");
+  if ((y && y_dtype != WMOE_F32 && y_dtype != WMOE_BF16) || (xn_dtype != WMOE_F32 && xn_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_add_rmsnorm: bad dtype");
+  if (T == 0) return WMOE_OK;
+  if (!x || !x_out || !xn_out) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_add_rmsnorm: null pointer");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(x_out) |
+       reinterpret_cast<uintptr_t>(xn_out)) % 16)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_add_rmsnorm: buffers must be 16-byte aligned");
+  int n = 0;
+  WMOE_CHECK_CUDA(ctx,
+                  add_rmsnorm(x, y, y_dtype, T, hidden, eps, x_out, xn_out, xn_dtype,
+                              static_cast<cudaStream_t>(stream), &n),
+                  "wmoe_add_rmsnorm");
+  ctx->launches += uint64_t(n);
+  return WMOE_OK;
+}
+
 int wmoe_store_stats(const wmoe_store* store, uint64_t* hits, uint64_t* misses, uint64_t* bytes_in,
                      uint64_t* evictions) {
   if (!store) return WMOE_ERR_INVALID;
@@ -461,6 +507,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
     WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(sel.data(), topk_idx, sel.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
                     "routing read-back");
     WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "routing read-back");
+    store_record_usage(store, layer, sel.data(), sel.size());
     experts_used = sel;
     std::sort(experts_used.begin(), experts_used.end());
     experts_used.erase(std::unique(experts_used.begin(), experts_used.end()), experts_used.end());
@@ -641,6 +688,7 @@ static int ep_experts_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, int worl
     WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(ex.data(), pair_exp, ex.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
                     "pair read-back");
     WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "pair read-back");
+    store_record_usage(store, layer, ex.data(), ex.size());
     std::sort(ex.begin(), ex.end());
     ex.erase(std::unique(ex.begin(), ex.end()), ex.end());
     experts_used = ex;

@@ -20,6 +20,7 @@ enum DeviceStatus : int {
   kStatusNotResident = 2,
   kStatusBarrierTimeout = 3,
   kStatusBadSegment = 4,
+  kStatusRange = 5,  // a value left the range of its fp16 intermediate (h or y of the grouped GEMMs)
 };
 
 __device__ __forceinline__ void set_status(int* status, int cause) {

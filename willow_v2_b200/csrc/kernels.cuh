@@ -41,6 +41,10 @@ __device__ __forceinline__ int pair_token(const PairMap& m, int p) {
 // dequant.cu
 cudaError_t dequant(int type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype, cudaStream_t st);
 
+// norm.cu: x_out = x + y (y optional), xn = x_out * rsqrt(mean(x_out^2) + eps), per token row (H % 4 == 0)
+cudaError_t add_rmsnorm(const float* x, const void* y, int y_dtype, int T, int H, float eps, float* x_out, void* xn,
+                        int xn_dtype, cudaStream_t st, int* launches);
+
 // route.cu: at most 8 tokens, logits [T, E+1] (column E = shared gate); then top-k
 cudaError_t router_logits(const void* x, int x_dtype, int T, int H, int E, const float* router_w,
                           const float* shared_gate, float* logits, cudaStream_t st, int* launches);

@@ -5,7 +5,9 @@
 // 40-layer store (~21 GB) fits in HBM, so the default is every (layer, expert) blob resident in one slab and an
 // identity slot table. With a cap, the slab holds cap/blob slots; every blob lives in pinned host memory and a
 // miss is one cudaMemcpyAsync on a side stream, ordered against the compute stream by events, least recently
-// used slot evicted first. Kernels find a blob through the device slot table [layers, experts] (-1: absent).
+// used slot evicted first, slots of the usage-driven hot set only when nothing else can go. A prefetch starts the
+// copies of a coming layer without making the compute stream wait; the call that uses them waits for that batch
+// of copies only. Kernels find a blob through the device slot table [layers, experts] (-1: absent).
 #include <algorithm>
 #include <cstring>
 #include <list>
@@ -137,10 +139,12 @@ int store_create(wmoe_ctx* ctx, int layers, int experts, int expert_begin, int e
   cudaError_t e = cudaMalloc(&s->d_slab, size_t(s->n_slots) * s->slot_stride);
   if (e == cudaSuccess) e = cudaMalloc(&s->d_slot_of, total * sizeof(int32_t));
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking);
-  for (int i = 0; i < wmoe_store::kRing && e == cudaSuccess; ++i)
+  for (int i = 0; i < wmoe_store::kRing && e == cudaSuccess; ++i) {
     e = cudaEventCreateWithFlags(&s->ring[i], cudaEventDisableTiming);
-  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->copied, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->batch_ev[i], cudaEventDisableTiming);
+  }
   s->slot_of.assign(total, -1);
+  s->usage.assign(total, 0);
   if (e == cudaSuccess && s->capped) e = cudaHostAlloc(&s->h_master, held * s->blob_bytes, cudaHostAllocDefault);
   if (e != cudaSuccess) {
     const std::string msg = std::string("expert store allocation: ") + cudaGetErrorString(e);
@@ -153,6 +157,10 @@ int store_create(wmoe_ctx* ctx, int layers, int experts, int expert_begin, int e
   } else {
     s->slot_key.assign(size_t(s->n_slots), -1);
     s->slot_use.assign(size_t(s->n_slots), 0);
+    s->slot_batch.assign(size_t(s->n_slots), 0);
+    s->slot_prefetched.assign(size_t(s->n_slots), 0);
+    s->slot_from_prefetch.assign(size_t(s->n_slots), 0);
+    s->hot.assign(total, 0);
     s->lru_pos.resize(size_t(s->n_slots));
     for (int i = 0; i < s->n_slots; ++i) s->lru_pos[size_t(i)] = s->lru.insert(s->lru.end(), i);
   }
@@ -173,7 +181,8 @@ void store_destroy(wmoe_store* s) {
   if (s->h_master) cudaFreeHost(s->h_master);
   for (auto& ev : s->ring)
     if (ev) cudaEventDestroy(ev);
-  if (s->copied) cudaEventDestroy(s->copied);
+  for (auto& ev : s->batch_ev)
+    if (ev) cudaEventDestroy(ev);
   if (s->side) cudaStreamDestroy(s->side);
   delete s;
 }
@@ -257,46 +266,33 @@ int store_fill_synthetic(wmoe_store* s, uint64_t seed, int layer_begin, int laye
   return 0;
 }
 
-int store_prepare(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st) {
-  if (layer < 0 || layer >= s->layers || n < 0) return store_fail(s, -1, "wmoe_store_prepare: bad layer");
-  for (int i = 0; i < n; ++i) {
-    if (experts[i] < 0 || experts[i] >= s->experts) return store_fail(s, -1, "wmoe_store_prepare: bad expert id");
-    if (!s->owns(experts[i])) return store_fail(s, -1, "wmoe_store_prepare: expert outside the store's range");
-  }
-  if (!s->capped) {
-    s->hits += uint64_t(n);
-    return 0;
-  }
-  if (n > s->n_slots) return store_fail(s, -3, "expert store cap holds fewer experts than one layer call needs");
+// Copies the listed missing experts of a layer into slots on the side stream, as one batch with its own event
+// (returned in *batch). Victims are the least recently used slots that this request does not need and that hold
+// no pending prefetch, slots of hot experts only when no other slot can go (store.py:348). Before overwriting a
+// slot, the side stream waits for the compute work that last read it; the slot table entries are published on
+// the compute stream.
+static int copy_in(wmoe_store* s, int layer, const std::vector<int>& misses, std::vector<char>& needed, bool prefetch,
+                   cudaStream_t st, uint64_t* batch) {
   const size_t E = size_t(s->experts);
-  std::vector<int> wanted(experts, experts + n);
-  std::sort(wanted.begin(), wanted.end());
-  wanted.erase(std::unique(wanted.begin(), wanted.end()), wanted.end());
-  std::vector<char> needed(size_t(s->n_slots), 0);
-  std::vector<int> misses;
-  for (int x : wanted) {
-    const size_t key = size_t(layer) * E + size_t(x);
-    const int slot = s->slot_of[key];
-    if (slot >= 0) {
-      ++s->hits;
+  std::vector<int> victims;
+  victims.reserve(misses.size());
+  for (int pass = 0; pass < 2 && victims.size() < misses.size(); ++pass) {
+    for (auto it = s->lru.begin(); it != s->lru.end() && victims.size() < misses.size(); ++it) {
+      const int slot = *it;
+      if (needed[size_t(slot)] || s->slot_prefetched[size_t(slot)]) continue;
+      const int64_t key = s->slot_key[size_t(slot)];
+      const bool is_hot = key >= 0 && s->hot[size_t(key)];
+      if (is_hot != (pass == 1)) continue;
       needed[size_t(slot)] = 1;
-      s->lru.splice(s->lru.end(), s->lru, s->lru_pos[size_t(slot)]);  // most recently used at the back
-    } else {
-      misses.push_back(x);
+      victims.push_back(slot);
     }
   }
-  if (misses.empty()) return 0;
-  // the side stream must not overwrite a slot before the compute work that read it has finished, and must
-  // see the compute stream's earlier slot-table updates
+  if (victims.size() < misses.size()) return store_fail(s, -3, "expert store: no evictable slot");
+  const uint64_t b = ++s->batches;
   cudaError_t e = cudaSuccess;
   SlotUpdates u{};
-  auto it = s->lru.begin();
-  for (int x : misses) {
-    while (it != s->lru.end() && needed[size_t(*it)]) ++it;
-    if (it == s->lru.end()) return store_fail(s, -3, "expert store: no evictable slot");
-    const int slot = *it;
-    ++it;
-    needed[size_t(slot)] = 1;
+  for (size_t i = 0; i < misses.size() && e == cudaSuccess; ++i) {
+    const int slot = victims[i], x = misses[i];
     const int64_t old = s->slot_key[size_t(slot)];
     if (old >= 0) {
       ++s->evictions;
@@ -304,32 +300,139 @@ int store_prepare(wmoe_store* s, int layer, const int32_t* experts, int n, cudaS
       push_update(s, u, int(old), -1, st);
     }
     const uint64_t last = s->slot_use[size_t(slot)];
-    if (last > 0) {
+    // a compute event still holding that call (the ring has not wrapped past it) orders the overwrite
+    if (last > 0 && s->ring_seq[last % wmoe_store::kRing] == last)
       e = cudaStreamWaitEvent(s->side, s->ring[last % wmoe_store::kRing], 0);
-      if (e != cudaSuccess) break;
-    }
+    if (e != cudaSuccess) break;
     const size_t key = size_t(layer) * E + size_t(x);
     e = cudaMemcpyAsync(s->d_slab + size_t(slot) * s->slot_stride, s->h_master + s->blob_index(layer, x) * s->blob_bytes,
                         s->blob_bytes, cudaMemcpyHostToDevice, s->side);
     if (e != cudaSuccess) break;
     ++s->misses;
     s->bytes_in += s->blob_bytes;
+    if (prefetch) ++s->prefetched;
     s->slot_key[size_t(slot)] = int64_t(key);
     s->slot_of[key] = slot;
+    s->slot_batch[size_t(slot)] = b;
+    s->slot_prefetched[size_t(slot)] = prefetch ? 1 : 0;
+    s->slot_from_prefetch[size_t(slot)] = prefetch ? 1 : 0;
     push_update(s, u, int(key), slot, st);
     s->lru.splice(s->lru.end(), s->lru, s->lru_pos[size_t(slot)]);
   }
+  if (e == cudaSuccess) e = cudaEventRecord(s->batch_ev[b % wmoe_store::kRing], s->side);
   if (e != cudaSuccess) return store_fail(s, -6, std::string("expert copy: ") + cudaGetErrorString(e));
-  // the compute stream waits for the copies, then publishes the new slot table entries
-  e = cudaEventRecord(s->copied, s->side);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, s->copied, 0);
-  if (e != cudaSuccess) return store_fail(s, -2, std::string("expert copy ordering: ") + cudaGetErrorString(e));
+  *batch = b;
   return flush_updates(s, u, st);
+}
+
+static int check_request(wmoe_store* s, int layer, const int32_t* experts, int n, const char* fn) {
+  if (layer < 0 || layer >= s->layers || n < 0) return store_fail(s, -1, std::string(fn) + ": bad layer");
+  for (int i = 0; i < n; ++i) {
+    if (experts[i] < 0 || experts[i] >= s->experts) return store_fail(s, -1, std::string(fn) + ": bad expert id");
+    if (!s->owns(experts[i])) return store_fail(s, -1, std::string(fn) + ": expert outside the store's range");
+  }
+  return 0;
+}
+
+int store_prepare(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st) {
+  if (int rc = check_request(s, layer, experts, n, "wmoe_store_prepare")) return rc;
+  if (!s->capped) {
+    s->hits += uint64_t(n);
+    return 0;
+  }
+  if (n > s->n_slots) return store_fail(s, -3, "expert store cap holds fewer experts than one layer call needs");
+  const size_t E = size_t(s->experts);
+  // this layer's prefetches that the call does not use become ordinary cached slots (store.py:221-232)
+  for (int slot = 0; slot < s->n_slots; ++slot)
+    if (s->slot_prefetched[size_t(slot)] && s->slot_key[size_t(slot)] / int64_t(E) == layer)
+      s->slot_prefetched[size_t(slot)] = 0;
+  std::vector<int> wanted(experts, experts + n);
+  std::sort(wanted.begin(), wanted.end());
+  wanted.erase(std::unique(wanted.begin(), wanted.end()), wanted.end());
+  std::vector<char> needed(size_t(s->n_slots), 0);
+  std::vector<int> misses;
+  uint64_t wait_for = 0;  // the latest copy batch this call's slots came from
+  for (int x : wanted) {
+    const size_t key = size_t(layer) * E + size_t(x);
+    const int slot = s->slot_of[key];
+    if (slot >= 0) {
+      ++s->hits;
+      needed[size_t(slot)] = 1;
+      if (s->slot_from_prefetch[size_t(slot)]) {
+        ++s->prefetch_used;
+        s->slot_from_prefetch[size_t(slot)] = 0;
+      }
+      wait_for = std::max(wait_for, s->slot_batch[size_t(slot)]);
+      s->lru.splice(s->lru.end(), s->lru, s->lru_pos[size_t(slot)]);  // most recently used at the back
+    } else {
+      misses.push_back(x);
+    }
+  }
+  if (!misses.empty()) {
+    uint64_t b = 0;
+    if (int rc = copy_in(s, layer, misses, needed, false, st, &b)) return rc;
+    wait_for = b;
+  }
+  // the compute stream waits for the copies (side-stream batches complete in order); once is enough
+  if (wait_for > s->waited) {
+    const cudaError_t e = cudaStreamWaitEvent(st, s->batch_ev[wait_for % wmoe_store::kRing], 0);
+    if (e != cudaSuccess) return store_fail(s, -2, std::string("expert copy ordering: ") + cudaGetErrorString(e));
+    s->waited = wait_for;
+  }
+  return 0;
+}
+
+int store_prefetch(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st) {
+  if (int rc = check_request(s, layer, experts, n, "wmoe_store_prefetch")) return rc;
+  if (!s->capped) return 0;
+  const size_t E = size_t(s->experts);
+  std::vector<int> wanted(experts, experts + n);
+  std::sort(wanted.begin(), wanted.end());
+  wanted.erase(std::unique(wanted.begin(), wanted.end()), wanted.end());
+  std::vector<char> needed(size_t(s->n_slots), 0);
+  std::vector<int> misses;
+  for (int x : wanted) {
+    const int slot = s->slot_of[size_t(layer) * E + size_t(x)];
+    if (slot >= 0)
+      needed[size_t(slot)] = 1;
+    else
+      misses.push_back(x);
+  }
+  // a prefetch never takes the slots the last call read or pending prefetches: it fills at most the slots left
+  for (int slot = 0; slot < s->n_slots; ++slot)
+    if (s->seq > 0 && s->slot_use[size_t(slot)] == s->seq) needed[size_t(slot)] = 1;
+  size_t room = 0;
+  for (int slot = 0; slot < s->n_slots; ++slot) room += !needed[size_t(slot)] && !s->slot_prefetched[size_t(slot)];
+  if (misses.size() > room) misses.resize(room);
+  if (misses.empty()) return 0;
+  uint64_t b = 0;
+  return copy_in(s, layer, misses, needed, true, st, &b);
+}
+
+void store_record_usage(wmoe_store* s, int layer, const int32_t* experts, size_t n) {
+  const size_t base = size_t(layer) * size_t(s->experts);
+  for (size_t i = 0; i < n; ++i)
+    if (experts[i] >= 0 && experts[i] < s->experts) ++s->usage[base + size_t(experts[i])];
+}
+
+int store_choose_hot(wmoe_store* s, double share) {
+  if (!s->capped) return 0;
+  if (!(share >= 0.0 && share <= 1.0)) return store_fail(s, -1, "wmoe_store_choose_hot: share outside [0, 1]");
+  std::fill(s->hot.begin(), s->hot.end(), 0);
+  const size_t room = size_t(double(s->n_slots) * share);
+  std::vector<uint32_t> keys;
+  for (size_t k = 0; k < s->usage.size(); ++k)
+    if (s->usage[k] > 0) keys.push_back(uint32_t(k));
+  // most used first; ties in (layer, expert) order
+  std::stable_sort(keys.begin(), keys.end(), [&](uint32_t a, uint32_t b) { return s->usage[a] > s->usage[b]; });
+  for (size_t i = 0; i < keys.size() && i < room; ++i) s->hot[keys[i]] = 1;
+  return 0;
 }
 
 int store_mark_used(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st) {
   if (!s->capped) return 0;
   const uint64_t seq = ++s->seq;
+  s->ring_seq[seq % wmoe_store::kRing] = seq;
   const cudaError_t e = cudaEventRecord(s->ring[seq % wmoe_store::kRing], st);
   if (e != cudaSuccess) return store_fail(s, -2, std::string("store event: ") + cudaGetErrorString(e));
   for (int i = 0; i < n; ++i) {

@@ -40,7 +40,7 @@ struct wmoe_ctx {
 };
 
 struct wmoe_store {
-  static constexpr int kRing = 64;
+  static constexpr int kRing = 256;
   wmoe_ctx* ctx = nullptr;
   int layers = 0, experts = 0, hidden = 0, ffn = 0;
   int expert_begin = 0, expert_end = 0;  // the experts of each layer this store holds (expert parallelism)
@@ -57,13 +57,20 @@ struct wmoe_store {
   uint8_t* h_master = nullptr;    // pinned host copy of every blob (capped stores)
   std::vector<int64_t> slot_key;  // (layer * experts + expert) held by each slot, -1 free
   std::vector<uint64_t> slot_use; // sequence number of the last call that read the slot
+  std::vector<uint64_t> slot_batch;       // side-stream copy batch that filled the slot (0: none)
+  std::vector<char> slot_prefetched;      // filled by a prefetch whose layer has not run yet (not evictable)
+  std::vector<char> slot_from_prefetch;   // filled by a prefetch and not yet read by a call (counter only)
   std::list<int> lru;             // slots, least recently used first
   std::vector<std::list<int>::iterator> lru_pos;
+  std::vector<uint64_t> usage;    // [layers * experts] tokens routed to each expert (store.py:482-484)
+  std::vector<char> hot;          // [layers * experts] the hot set: evicted only when no other slot can go
   cudaStream_t side = nullptr;
-  cudaEvent_t ring[kRing] = {};
-  cudaEvent_t copied = nullptr;
+  cudaEvent_t ring[kRing] = {};       // compute-stream event of call seq at [seq % kRing]
+  uint64_t ring_seq[kRing] = {};
+  cudaEvent_t batch_ev[kRing] = {};   // side-stream event of copy batch b at [b % kRing]
   uint64_t seq = 0;
-  uint64_t hits = 0, misses = 0, bytes_in = 0, evictions = 0;
+  uint64_t batches = 0, waited = 0;   // copy batches issued; the last one the compute stream has waited for
+  uint64_t hits = 0, misses = 0, bytes_in = 0, evictions = 0, prefetched = 0, prefetch_used = 0;
 };
 
 int ctx_fail(wmoe_ctx* ctx, int code, const std::string& msg);
@@ -75,5 +82,8 @@ void store_destroy(wmoe_store* s);
 int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cudaStream_t st);
 int store_fill_synthetic(wmoe_store* s, uint64_t seed, int layer_begin, int layer_end, cudaStream_t st);
 int store_prepare(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st);
+int store_prefetch(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st);
 int store_mark_used(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st);
+void store_record_usage(wmoe_store* s, int layer, const int32_t* experts, size_t n);
+int store_choose_hot(wmoe_store* s, double share);
 wmoe::ExpertSource store_source(const wmoe_store* s, const uint8_t* shared_gate_up, const uint8_t* shared_down);

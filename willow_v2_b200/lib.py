@@ -11,7 +11,7 @@ ERR_INVALID, ERR_CUDA, ERR_CAPACITY, ERR_DEVICE, ERR_UNSUPPORTED, ERR_IO, ERR_NC
 F32, BF16, F16 = 0, 1, 2
 GGML_Q4_K, GGML_Q6_K = 12, 14
 STATUS_NAMES = {1: "expert id out of range", 2: "expert not resident", 3: "grid barrier timed out",
-                4: "bad segment"}
+                4: "bad segment", 5: "value out of the range of an fp16 intermediate"}
 
 # every symbol include/wmoe.h declares, with (restype, argtypes)
 _p, _i, _sz, _u64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_float
@@ -40,6 +40,10 @@ SIGNATURES = {
     "wmoe_store_fill_synthetic": (_i, [_p, _u64, _i, _i, _p]),
     "wmoe_store_blob_bytes": (_sz, [_p]),
     "wmoe_store_prepare": (_i, [_p, _i, _p, _i, _p]),
+    "wmoe_store_prefetch": (_i, [_p, _i, _p, _i, _p]),
+    "wmoe_store_choose_hot": (_i, [_p, ctypes.c_double]),
+    "wmoe_store_prefetch_stats": (_i, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
+    "wmoe_add_rmsnorm": (_i, [_p, _p, _p, _i, _i, _i, ctypes.c_float, _p, _p, _i, _p]),
     "wmoe_store_download": (_i, [_p, _i, _i, _p, _p]),
     "wmoe_store_blob": (_p, [_p, _i, _i]),
     "wmoe_store_stats": (_i, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_u64), ctypes.POINTER(_u64),

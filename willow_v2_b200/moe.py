@@ -181,6 +181,21 @@ class ExpertStore:
         check(self.ctx.handle, lib.wmoe_store_prepare(self.handle, layer, ids.ctypes.data_as(ctypes.c_void_p),
                                                       int(ids.size), _stream()))
 
+    def prefetch(self, layer: int, experts=None):
+        """Starts copying experts of a coming layer (store.py:204-219) without making the compute stream wait;
+        experts None: every expert of the layer this store holds (a prefill batch reads most of them). A no-op
+        when nothing is capped."""
+        if experts is None:
+            check(self.ctx.handle, lib.wmoe_store_prefetch(self.handle, layer, None, 0, _stream()))
+            return
+        ids = np.ascontiguousarray(np.asarray(list(experts), dtype=np.int32))
+        check(self.ctx.handle, lib.wmoe_store_prefetch(self.handle, layer, ids.ctypes.data_as(ctypes.c_void_p),
+                                                       int(ids.size), _stream()))
+
+    def choose_hot(self, share: float = 0.75):
+        """Keeps `share` of the slots for the experts routed the most tokens so far (store.py:464-480, HOT_SHARE)."""
+        check(self.ctx.handle, lib.wmoe_store_choose_hot(self.handle, float(share)))
+
     def download(self, layer: int, expert: int) -> np.ndarray:
         """The expert's bytes as the store holds them (uint8 [blob_bytes])."""
         out = np.empty(self.blob_bytes, dtype=np.uint8)
@@ -192,9 +207,11 @@ class ExpertStore:
         return lib.wmoe_store_blob(self.handle, layer, expert)
 
     def stats(self) -> dict:
-        vals = [ctypes.c_uint64() for _ in range(4)]
-        check(self.ctx.handle, lib.wmoe_store_stats(self.handle, *[ctypes.byref(v) for v in vals]))
-        return dict(zip(("hits", "misses", "bytes_in", "evictions"), (v.value for v in vals)))
+        vals = [ctypes.c_uint64() for _ in range(6)]
+        check(self.ctx.handle, lib.wmoe_store_stats(self.handle, *[ctypes.byref(v) for v in vals[:4]]))
+        check(self.ctx.handle, lib.wmoe_store_prefetch_stats(self.handle, *[ctypes.byref(v) for v in vals[4:]]))
+        return dict(zip(("hits", "misses", "bytes_in", "evictions", "prefetched", "prefetch_used"),
+                        (v.value for v in vals)))
 
     def close(self):
         if self.handle:
@@ -206,6 +223,22 @@ class ExpertStore:
             self.close()
         except Exception:
             pass
+
+
+def add_rmsnorm(x: torch.Tensor, y: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                out_dtype: torch.dtype = torch.bfloat16, ctx: Optional[Context] = None):
+    """The layer glue of engines/qwen36/model.py:17-22 (rms_norm of engines/base.py:27-32, weight 1): returns
+    (x + y as float32, rms_norm(x + y) as out_dtype); y (the previous MoE output, f32 or bf16) may be None. x is
+    updated in place (float32 [T, H])."""
+    ctx = ctx or default_context()
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("add_rmsnorm: x must be a contiguous float32 tensor")
+    T, H = x.shape
+    xn = torch.empty(T, H, dtype=out_dtype, device=x.device)
+    y_c = None if y is None else y.contiguous()
+    check(ctx.handle, lib.wmoe_add_rmsnorm(ctx.handle, _ptr(x), _ptr(y_c), _DTYPES[y.dtype] if y is not None else 0,
+                                           T, H, float(eps), _ptr(x), _ptr(xn), _DTYPES[out_dtype], _stream()))
+    return x, xn
 
 
 def pack_router(router_w: torch.Tensor, shared_gate: torch.Tensor, ctx: Optional[Context] = None) -> torch.Tensor:
