@@ -486,8 +486,9 @@ def run_prefill32k(args, rank: int, world: int, dist):
                             router_bias=torch.from_numpy(synth.zipf_bias(SEED + l)).cuda()).prepare(ctx, decode=False)
            for l in range(n_layers)]
     T = PF32_T // world
-    h0 = torch.from_numpy(synth.hidden(SEED, PF32_T, step=99)[rank * T:(rank + 1) * T]).cuda()
-    h = torch.empty_like(h0)
+    # two token batches cycled: each step routes a different batch (the prefetch guess sees only earlier steps)
+    h0s = [torch.from_numpy(synth.hidden(SEED, PF32_T, step=99 + b)[rank * T:(rank + 1) * T]).cuda() for b in range(2)]
+    h = torch.empty_like(h0s[0])
     stream = torch.cuda.current_stream()
     if world > 1:
         moe.ep_init(ctx)
@@ -506,7 +507,7 @@ def run_prefill32k(args, rank: int, world: int, dist):
 
     K, W = args.steps, args.warmup
     for s in range(W):
-        h.copy_(h0)
+        h.copy_(h0s[s % 2])
         stack(h)
         if s == 0:
             store.choose_hot(0.75)  # usage of the first pass
@@ -532,7 +533,7 @@ def run_prefill32k(args, rank: int, world: int, dist):
     with ClockSampler(device) as clocks:
         ev0.record(stream)
         for s in range(K):
-            h.copy_(h0)
+            h.copy_(h0s[(W + s) % 2])
             stack(h)
         ev1.record(stream)
         torch.cuda.synchronize()
@@ -541,14 +542,14 @@ def run_prefill32k(args, rank: int, world: int, dist):
     st1 = store.stats()
     ctx.check_device()
     # end to end through the public calls: the step's tokens from pinned host memory, the result back, every step
-    h_host = h0.cpu().pin_memory()
-    o_host = torch.empty_like(h_host).pin_memory()
+    h_host = [x.cpu().pin_memory() for x in h0s]
+    o_host = torch.empty_like(h_host[0]).pin_memory()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     for s in range(K):
-        h.copy_(h_host, non_blocking=True)
+        h.copy_(h_host[s % 2], non_blocking=True)
         o_host.copy_(stack(h), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
@@ -577,7 +578,7 @@ def run_prefill32k(args, rank: int, world: int, dist):
                    "tokens_per_step": PF32_T, "tokens_per_rank": T,
                    "parallelism": f"ep{world}" if world > 1 else "single GPU", "experts_per_rank": per,
                    "store_cap_bytes": PF32_CAP, "store_slots": int(PF32_CAP // ((EXPERT_BYTES + 255) // 256 * 256)),
-                   "hot_share": 0.75,
+                   "hot_share": 0.75, "batches_cycled": 2,
                    "l2": "inputs larger than L2: 268 MB residual stream per rank and up to 21 GB of experts"},
         "roofline": {"bound": "tensor", "kernel": "whole 40-layer step (expert products / step time), rank 0",
                      "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16, "traffic": None,

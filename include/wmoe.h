@@ -126,11 +126,12 @@ size_t wmoe_store_blob_bytes(const wmoe_store* store);
 /* Makes the given experts of a layer resident (copies misses from the host copy on the store's side stream;
  * the compute stream waits for them). Returns WMOE_ERR_CAPACITY if they cannot all fit at once. */
 int wmoe_store_prepare(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream);
-/* Starts copying the given experts of a coming layer (experts null: every expert of the layer the store holds,
- * as a prefill batch reads most of them) without making the compute stream wait; the call that uses them waits
- * for those copies only. Takes only slots that neither the last call nor a pending prefetch holds, and copies as
- * many as fit; unused ones become ordinary cached slots once their layer runs. Replaces ExpertStore.prefetch and
- * collect_prefetches (gguf/store.py:204-232). No-op on an uncapped store. */
+/* Starts copying the given experts of a coming layer without making the compute stream wait; the call that uses
+ * them waits for those copies only. experts null: the experts this layer has been routed to before, most used
+ * first (every expert of the layer the store holds when there is no history yet). Takes only slots that neither
+ * the last call nor a pending prefetch holds, and copies as many as fit, in the order given; unused ones become
+ * ordinary cached slots once their layer runs. Replaces ExpertStore.prefetch and collect_prefetches
+ * (gguf/store.py:204-232). No-op on an uncapped store. */
 int wmoe_store_prefetch(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream);
 /* Picks the hot set: the `share` of the slots (0..1) that go to the experts routed the most tokens so far (counted
  * by every call on a capped store); they are evicted only when no other slot can go. Replaces

@@ -366,8 +366,16 @@ int wmoe_store_prefetch(wmoe_store* store, int layer, const int32_t* experts, in
   if (n < 0 || (n > 0 && !experts))
     return ctx_fail(store->ctx, WMOE_ERR_INVALID, "wmoe_store_prefetch: bad expert list");
   std::vector<int32_t> all;
-  if (!experts) {  // every expert of the layer the store holds (a prefill batch reads most of them)
-    for (int e = store->expert_begin; e < store->expert_end; ++e) all.push_back(e);
+  if (!experts) {
+    // the guess: the experts this layer has been routed to before (the usage table), most used first; with no
+    // history, every expert of the layer the store holds (a prefill batch reads most of them)
+    const size_t base = size_t(layer >= 0 && layer < store->layers ? layer : 0) * size_t(store->experts);
+    for (int e = store->expert_begin; e < store->expert_end; ++e)
+      if (store->usage[base + size_t(e)] > 0) all.push_back(e);
+    std::stable_sort(all.begin(), all.end(),
+                     [&](int32_t a, int32_t b) { return store->usage[base + size_t(a)] > store->usage[base + size_t(b)]; });
+    if (all.empty())
+      for (int e = store->expert_begin; e < store->expert_end; ++e) all.push_back(e);
     experts = all.data();
     n = int(all.size());
   }

@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c0 = 0; c0 < t.ncols; c0 += 32) {
         float v[32];
         tmem_ld32(taddr + uint32_t(c0), v);
+        const int nv = min(32, t.ncols - c0);  // columns past the chunk's tokens hold padding or stale values
         if (MODE == 0) {
           // gate rows are quadrants 0-1, up rows quadrants 2-3; h index 64 mt + trow, stored in run-of-8 order
           if (quad >= 2) {
@@ -377,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 32; ++c) {
               const float g = v[c];
               const float hv = __fdividef(g, 1.0f + __expf(-g)) * xbuf[c * 64 + trow] * (1.0f / kHScale);
-              vmax = fmaxf(vmax, fabsf(hv));
+              if (c < nv) vmax = fmaxf(vmax, fabsf(hv));
               obuf[c * 64 + j] = __float2half_rn(hv);
             }
             if (!(vmax <= 65504.f)) set_status(p.status, kStatusRange);
@@ -388,13 +389,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
             const float yv = v[c] * (kHScale / kYScale);
-            vmax = fmaxf(vmax, fabsf(yv));
+            if (c < nv) vmax = fmaxf(vmax, fabsf(yv));
             obuf[c * kBM + trow] = __float2half_rn(yv);
           }
           if (!(vmax <= 65504.f)) set_status(p.status, kStatusRange);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        const int n = min(32, t.ncols - c0);
+        const int n = nv;
         // output row of column c0 + lane (remapped rows of the down launch fetched once per chunk)
         int lane_row = prow0 + c0 + lane;
         if (MODE == 1 && p.out_rows && lane < n && lane_row < p.n_routed) lane_row = p.out_rows[lane_row];

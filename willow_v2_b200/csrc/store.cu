@@ -386,9 +386,14 @@ int store_prefetch(wmoe_store* s, int layer, const int32_t* experts, int n, cuda
   if (int rc = check_request(s, layer, experts, n, "wmoe_store_prefetch")) return rc;
   if (!s->capped) return 0;
   const size_t E = size_t(s->experts);
-  std::vector<int> wanted(experts, experts + n);
-  std::sort(wanted.begin(), wanted.end());
-  wanted.erase(std::unique(wanted.begin(), wanted.end()), wanted.end());
+  // in the order given (the first ones get the room when it runs out), each expert once
+  std::vector<int> wanted;
+  std::vector<char> seen(E, 0);
+  for (int i = 0; i < n; ++i)
+    if (!seen[size_t(experts[i])]) {
+      seen[size_t(experts[i])] = 1;
+      wanted.push_back(experts[i]);
+    }
   std::vector<char> needed(size_t(s->n_slots), 0);
   std::vector<int> misses;
   for (int x : wanted) {

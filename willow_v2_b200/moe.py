@@ -183,8 +183,8 @@ class ExpertStore:
 
     def prefetch(self, layer: int, experts=None):
         """Starts copying experts of a coming layer (store.py:204-219) without making the compute stream wait;
-        experts None: every expert of the layer this store holds (a prefill batch reads most of them). A no-op
-        when nothing is capped."""
+        experts None: the experts the layer has been routed to before, most used first (all of the layer's experts
+        this store holds when there is no history). A no-op when nothing is capped."""
         if experts is None:
             check(self.ctx.handle, lib.wmoe_store_prefetch(self.handle, layer, None, 0, _stream()))
             return
