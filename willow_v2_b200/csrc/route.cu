@@ -184,7 +184,9 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
   float v[PER_LANE];
 #pragma unroll
   for (int i = 0; i < PER_LANE; ++i) v[i] = lane + 32 * i < E ? row[lane + 32 * i] : -INFINITY;
-  // partial sums added in order, each pass issuing the loads of all of a lane's logits at once
+  // partial sums added in order, each pass issuing the loads of all of a lane's logits at once (four passes' loads
+  // in flight)
+#pragma unroll 4
   for (int s = 1; s < splits; ++s) {
     const float* part = logits + (size_t(s) * T + t) * E;
 #pragma unroll
