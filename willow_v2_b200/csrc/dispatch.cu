@@ -5,6 +5,9 @@
 //   pass 2  one CTA: per-expert totals, exclusive scan -> offsets, per-(tile, expert) bases, used-expert list
 //   pass 3  per tile: each pick's rank among earlier tokens of the tile that picked the same expert, from a
 //           [expert][256-bit] token mask and popcounts; position = base + rank
+// Up to 256 tokens (one tile) the three passes run in one CTA (dispatch_small_kernel).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -129,6 +132,71 @@ __global__ void __launch_bounds__(kTile) scatter_kernel(const int32_t* __restric
   }
 }
 
+// One tile (T <= kTile): the three passes in one CTA of max(kTile, E) threads, the per-expert counts and token masks
+// in shared memory. Same ranks, offsets and used-expert list as the three launches, for two launches fewer.
+__global__ void __launch_bounds__(992) dispatch_small_kernel(const int32_t* __restrict__ idx, int T, int k, int E,
+                                                              int shared_rows, int32_t* __restrict__ counts,
+                                                              int32_t* __restrict__ offsets, int32_t* __restrict__ perm,
+                                                              int32_t* __restrict__ pos, int32_t* __restrict__ used,
+                                                              int32_t* __restrict__ seg, int32_t* __restrict__ n_used,
+                                                              int64_t* __restrict__ usage, int* status) {
+  constexpr int W = kTile / 32;
+  extern __shared__ int32_t sm[];
+  int32_t* hist = sm;                                         // [E]
+  int32_t* base = sm + E;                                     // [E] offsets
+  uint32_t* mask = reinterpret_cast<uint32_t*>(sm + 2 * E);  // [E][W]
+  const int tid = threadIdx.x;
+  for (int i = tid; i < E; i += blockDim.x) hist[i] = 0;
+  for (int i = tid; i < E * W; i += blockDim.x) mask[i] = 0;
+  __syncthreads();
+  if (tid < T)
+    for (int s = 0; s < k; ++s) {
+      const int e = idx[size_t(tid) * k + s];
+      if (e < 0 || e >= E) {
+        set_status(status, kStatusBadExpert);
+        continue;
+      }
+      atomicAdd(&hist[e], 1);
+      atomicOr(&mask[e * W + tid / 32], 1u << (tid % 32));
+    }
+  __syncthreads();
+  const int e = tid;
+  const int total = e < E ? hist[e] : 0;
+  int grand = 0;
+  const int off = block_exclusive_scan(total, &grand);
+  int nflag = 0;
+  const int slot = block_exclusive_scan(e < E && total > 0 ? 1 : 0, &nflag);
+  if (e < E) {
+    counts[e] = total;
+    offsets[e] = off;
+    base[e] = off;
+    if (usage) usage[e] += total;
+    if (total > 0) {
+      used[slot] = e;
+      seg[slot] = off;
+    }
+  }
+  if (e == 0) {
+    offsets[E] = T * k;
+    used[nflag] = E;  // the shared expert's segment: shared_rows rows (one per token)
+    seg[nflag] = T * k;
+    seg[nflag + 1] = T * k + shared_rows;
+    *n_used = nflag + 1;
+  }
+  __syncthreads();
+  if (tid >= T) return;
+  for (int s = 0; s < k; ++s) {
+    const int x = idx[size_t(tid) * k + s];
+    if (x < 0 || x >= E) continue;
+    const uint32_t* m = mask + x * W;
+    int rank = __popc(m[tid / 32] & ((1u << (tid % 32)) - 1u));
+    for (int w = 0; w < tid / 32; ++w) rank += __popc(m[w]);
+    const int p = base[x] + rank;
+    perm[p] = tid * k + s;
+    pos[size_t(tid) * k + s] = p;
+  }
+}
+
 cudaError_t dispatch(const int32_t* topk_idx, int T, int k, int E, void* scratch, int32_t* counts,
                      int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* used, int32_t* seg, int32_t* n_used,
                      int64_t* usage, int* status, cudaStream_t st, int* launches) {
@@ -141,6 +209,13 @@ cudaError_t dispatch_rows(const int32_t* topk_idx, int T, int k, int E, int shar
                           int32_t* seg, int32_t* n_used, int64_t* usage, int* status, cudaStream_t st,
                           int* launches) {
   const int ntiles = (T + kTile - 1) / kTile;
+  if (ntiles <= 1 && (E + 31) / 32 * 32 <= 992) {  // block_exclusive_scan: at most 31 warps
+    const int threads = std::max(kTile, (E + 31) / 32 * 32);
+    dispatch_small_kernel<<<1, threads, size_t(E) * (2 + kTile / 32) * sizeof(int32_t), st>>>(
+        topk_idx, T, k, E, shared_rows, counts, offsets, perm, pos, used, seg, n_used, usage, status);
+    ++*launches;
+    return cudaGetLastError();
+  }
   int32_t* tile_counts = static_cast<int32_t*>(scratch);
   int32_t* tile_base = tile_counts + size_t(ntiles) * E;
   if (T > 0) {
