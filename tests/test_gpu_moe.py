@@ -362,6 +362,45 @@ def test_prefetch_matches_resident(model):
     capped.close()
 
 
+def test_decode_with_next_layer_guess(model):
+    """Single-token decode over a capped store with willow's next-layer guess (engines/base.py:392-406): while layer
+    l runs, layer l + 1's router on the current residual picks experts to prefetch. Outputs stay bit-identical to
+    the resident store, and layers use guessed copies."""
+    from willow_v2_b200 import moe
+    ctx, store, layers = model
+    blob = (store.blob_bytes + 255) // 256 * 256
+    capped = moe.ExpertStore(LAYERS, cap_bytes=40 * blob, ctx=ctx)
+    capped.fill_synthetic(SEED)
+    prev = ctx.set_decode_kernel(False)  # both stores on the GEMV path (a capped store never runs the decode kernel)
+    try:
+        _guess_loop(store, capped, layers)
+    finally:
+        ctx.set_decode_kernel(prev)
+    st = capped.stats()
+    assert st["prefetched"] > 0 and st["prefetch_used"] > 0, st
+    ctx.check_device()
+    capped.close()
+
+
+def _guess_loop(store, capped, layers):
+    import torch
+    from willow_v2_b200 import moe
+    for step in range(3):
+        ha = torch.from_numpy(synth.hidden(SEED, 1, step=40 + step)).cuda()
+        hb = ha.clone()
+        for layer in range(LAYERS):
+            ha, na = moe.add_rmsnorm(ha, None, out_dtype=torch.float32)
+            hb, nb = moe.add_rmsnorm(hb, None, out_dtype=torch.float32)
+            if layer + 1 < LAYERS:
+                guess = moe.guess_next_layer(capped, hb, layers[layer + 1], layer + 1)
+                assert 0 < len(guess) <= 8
+            a = moe.moe_forward(store, layer, na, layers[layer])
+            b = moe.moe_forward(capped, layer, nb, layers[layer])
+            torch.cuda.synchronize()
+            assert torch.equal(a, b), (step, layer)
+            ha, hb = ha + a, hb + b
+
+
 def test_hot_set_survives_a_scan(model):
     """After one pass over the layers, choose_hot(0.5) keeps the experts routed the most tokens (store.py:464-480):
     a second pass evicts from the other slots, so every hot expert is still resident after it."""

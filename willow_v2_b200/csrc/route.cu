@@ -168,39 +168,11 @@ cudaError_t router_logits(const void* x, int x_dtype, int T, int H, int E, const
   return cudaGetLastError();
 }
 
-// One warp per token: k rounds of warp arg-max (larger value first, then the smaller expert id).
-// splits == 0: logits [T][E + 1], column E the shared-expert gate logit. splits > 0: `splits` partial sums
-// [splits][T][E] added in order, and the shared-expert gate logit is x[t] . g computed here.
+// k rounds of warp arg-max over a lane's PER_LANE logits (lane + 32 i): the larger value first, then the smaller
+// expert id; the renormalised weights exp(l_i - l_0) / sum_j exp(l_j - l_0) of the picks, in pick order.
 template <int PER_LANE>
-__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int splits, int T, int E, int k,
-                                                   const float* __restrict__ bias, float* __restrict__ topk_w,
-                                                   int32_t* __restrict__ topk_idx, float* __restrict__ shared_s,
-                                                   float* __restrict__ logits_out, const void* __restrict__ x,
-                                                   int x_dtype, const float* __restrict__ g, int H) {
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= T) return;
-  const float* row = splits == 0 ? logits + size_t(t) * (E + 1) : logits + size_t(t) * E;
-  float v[PER_LANE];
-#pragma unroll
-  for (int i = 0; i < PER_LANE; ++i) v[i] = lane + 32 * i < E ? row[lane + 32 * i] : -INFINITY;
-  // partial sums added in order, each pass issuing the loads of all of a lane's logits at once (four passes' loads
-  // in flight)
-#pragma unroll 4
-  for (int s = 1; s < splits; ++s) {
-    const float* part = logits + (size_t(s) * T + t) * E;
-#pragma unroll
-    for (int i = 0; i < PER_LANE; ++i)
-      if (lane + 32 * i < E) v[i] += part[lane + 32 * i];
-  }
-#pragma unroll
-  for (int i = 0; i < PER_LANE; ++i) {
-    const int e = lane + 32 * i;
-    if (e < E) {
-      if (bias) v[i] += bias[e];
-      if (logits_out) logits_out[size_t(t) * E + e] = v[i];
-    }
-  }
+__device__ __forceinline__ void select_topk(float (&v)[PER_LANE], int lane, int E, int k, float* __restrict__ w_out,
+                                            int32_t* __restrict__ idx_out) {
   float top0 = 0.f, sum = 0.f;
   float sel_l = 0.f;
   int sel_e = 0;
@@ -237,17 +209,108 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     }
   }
   if (lane < k) {
-    topk_w[size_t(t) * k + lane] = sel_l / sum;
-    topk_idx[size_t(t) * k + lane] = sel_e;
+    w_out[lane] = sel_l / sum;
+    idx_out[lane] = sel_e;
   }
+}
+
+// One warp per token: k rounds of warp arg-max (larger value first, then the smaller expert id).
+// splits == 0: logits [T][E + 1], column E the shared-expert gate logit. splits > 0: `splits` partial sums
+// [splits][T][E] added in order, and the shared-expert gate logit is x[t] . g computed here.
+template <int PER_LANE>
+__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int splits, int T, int E, int k,
+                                                   const float* __restrict__ bias, float* __restrict__ topk_w,
+                                                   int32_t* __restrict__ topk_idx, float* __restrict__ shared_s,
+                                                   float* __restrict__ logits_out, const void* __restrict__ x,
+                                                   int x_dtype, const float* __restrict__ g, int H) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const float* row = splits == 0 ? logits + size_t(t) * (E + 1) : logits + size_t(t) * E;
+  float v[PER_LANE];
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) v[i] = lane + 32 * i < E ? row[lane + 32 * i] : -INFINITY;
+  // partial sums added in order, each pass issuing the loads of all of a lane's logits at once (four passes' loads
+  // in flight)
+#pragma unroll 4
+  for (int s = 1; s < splits; ++s) {
+    const float* part = logits + (size_t(s) * T + t) * E;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i)
+      if (lane + 32 * i < E) v[i] += part[lane + 32 * i];
+  }
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      if (bias) v[i] += bias[e];
+      if (logits_out) logits_out[size_t(t) * E + e] = v[i];
+    }
+  }
+  select_topk<PER_LANE>(v, lane, E, k, topk_w + size_t(t) * k, topk_idx + size_t(t) * k);
   if (shared_s) {
     float sl;
     if (splits == 0) {
       sl = row[E];
     } else {
-      float acc = 0.f;
+      // four quarter sums of H / 4, each a lane-strided fma chain and a warp tree, added as ((q0 + q1) + (q2 + q3)):
+      // the same bits as topk_split_kernel's four warps
+      const int quarters = H % 512 == 0 ? 4 : 1;
+      float gq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (q >= quarters) break;
+        const int h0 = q * (H / quarters), h1 = (q + 1) * (H / quarters);
+        float acc = 0.f;
 #pragma unroll 4
-      for (int h = lane * 4; h < H; h += 128) {
+        for (int h = h0 + lane * 4; h < h1; h += 128) {
+          const float4 w = __ldg(reinterpret_cast<const float4*>(g + h));
+          const float4 xv = x_dtype == kF32 ? load4<float>(static_cast<const float*>(x) + size_t(t) * H + h)
+                                            : load4<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x) + size_t(t) * H + h);
+          acc = fmaf(w.x, xv.x, acc);
+          acc = fmaf(w.y, xv.y, acc);
+          acc = fmaf(w.z, xv.z, acc);
+          acc = fmaf(w.w, xv.w, acc);
+        }
+        gq[q] = warp_sum(acc);
+      }
+      sl = quarters == 4 ? (gq[0] + gq[1]) + (gq[2] + gq[3]) : gq[0];
+    }
+    if (lane == 0) shared_s[t] = 1.0f / (1.0f + expf(-sl));
+  }
+}
+
+// Top-k from 1..16 partial logit sums with E <= 256 and H a multiple of 512 (the sliced and tensor-core routers):
+// two tokens per CTA, four warps per token. Warp q adds, for experts [64q, 64q + 64), every partial in order with
+// all of them loaded at once, and forms a quarter of the shared-gate dot product; one warp per token then selects.
+// Per-logit arithmetic and the shared-gate sum ((q0 + q1) + (q2 + q3)) are those of topk_kernel.
+constexpr int kFastSplits = 16;
+
+__global__ void __launch_bounds__(256) topk_split_kernel(const float* __restrict__ logits, int splits, int T, int E,
+                                                         int k, const float* __restrict__ bias,
+                                                         float* __restrict__ topk_w, int32_t* __restrict__ topk_idx,
+                                                         float* __restrict__ shared_s, float* __restrict__ logits_out,
+                                                         const void* __restrict__ x, int x_dtype,
+                                                         const float* __restrict__ g, int H) {
+  __shared__ float lg[2][256];
+  __shared__ float gq[2][4];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tl = warp / 4, q = warp % 4;
+  const int t = blockIdx.x * 2 + tl;
+  if (t < T) {
+    float p[2][kFastSplits];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const int e = 64 * q + 32 * m + lane;
+#pragma unroll
+      for (int s = 0; s < kFastSplits; ++s)
+        p[m][s] = s < splits && e < E ? logits[(size_t(s) * T + t) * E + e] : 0.f;
+    }
+    float acc = 0.f;
+    if (shared_s) {
+      const int h1 = (q + 1) * (H / 4);
+#pragma unroll 4
+      for (int h = q * (H / 4) + lane * 4; h < h1; h += 128) {
         const float4 w = __ldg(reinterpret_cast<const float4*>(g + h));
         const float4 xv = x_dtype == kF32 ? load4<float>(static_cast<const float*>(x) + size_t(t) * H + h)
                                           : load4<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x) + size_t(t) * H + h);
@@ -256,9 +319,34 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
         acc = fmaf(w.z, xv.z, acc);
         acc = fmaf(w.w, xv.w, acc);
       }
-      sl = warp_sum(acc);
     }
-    if (lane == 0) shared_s[t] = 1.0f / (1.0f + expf(-sl));
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const int e = 64 * q + 32 * m + lane;
+      float v = p[m][0];
+#pragma unroll
+      for (int s = 1; s < kFastSplits; ++s)
+        if (s < splits) v += p[m][s];
+      if (e < E) {
+        if (bias) v += bias[e];
+        if (logits_out) logits_out[size_t(t) * E + e] = v;
+      }
+      lg[tl][e] = e < E ? v : -INFINITY;
+    }
+    if (shared_s) {
+      acc = warp_sum(acc);
+      if (lane == 0) gq[tl][q] = acc;
+    }
+  }
+  __syncthreads();
+  if (t >= T || q != 0) return;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = lg[tl][lane + 32 * i];
+  select_topk<8>(v, lane, E, k, topk_w + size_t(t) * k, topk_idx + size_t(t) * k);
+  if (shared_s && lane == 0) {
+    const float sl = (gq[tl][0] + gq[tl][1]) + (gq[tl][2] + gq[tl][3]);
+    shared_s[t] = 1.0f / (1.0f + expf(-sl));
   }
 }
 
@@ -289,6 +377,14 @@ cudaError_t pack_router(const float* router_w, const float* shared_gate, int E, 
 cudaError_t router_topk_split(const float* logits, int splits, int T, int E, int k, const float* bias, float* topk_w,
                               int32_t* topk_idx, float* shared_s, float* logits_out, const void* x, int x_dtype,
                               const float* g, int H, cudaStream_t st, int* launches) {
+  // up to 1024 tokens four warps per token (topk_kernel has too few CTAs there); above, one warp per token keeps
+  // more selecting warps per SM. Both give the same bits.
+  if (splits >= 1 && splits <= kFastSplits && E <= 256 && H % 512 == 0 && k <= 32 && T <= 1024) {
+    topk_split_kernel<<<unsigned((T + 1) / 2), 256, 0, st>>>(logits, splits, T, E, k, bias, topk_w, topk_idx, shared_s,
+                                                             logits_out, x, x_dtype, g, H);
+    ++*launches;
+    return cudaGetLastError();
+  }
   const unsigned grid = unsigned((T + 7) / 8);
   if (E <= 256)
     topk_kernel<8><<<grid, 256, 0, st>>>(logits, splits, T, E, k, bias, topk_w, topk_idx, shared_s, logits_out, x,

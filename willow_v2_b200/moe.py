@@ -241,6 +241,22 @@ def add_rmsnorm(x: torch.Tensor, y: Optional[torch.Tensor] = None, eps: float = 
     return x, xn
 
 
+def guess_next_layer(store: ExpertStore, residual: torch.Tensor, lw_next: "LayerWeights", layer_next: int,
+                     top_k: int = 8, eps: float = 1e-6) -> list:
+    """Decode on a capped store (engines/base.py:392-406, with engines/qwen36/model.py:30-31's guess input): runs
+    the next layer's router on rms_norm(residual), the residual stream before the current layer's experts, and
+    starts copying the experts it picks for every token (ExpertStore.prefetch), so they are resident or on their
+    way when that layer runs; the current layer's experts compute meanwhile. Returns the guessed expert ids (those
+    this store holds). Usually most of them are the experts the layer then picks."""
+    x = residual.float().contiguous().clone()
+    _, xn = add_rmsnorm(x, None, eps, out_dtype=torch.float32, ctx=store.ctx)
+    _, sel, _, _ = route(xn, lw_next.router_w, top_k, bias=lw_next.router_bias, ctx=store.ctx)
+    lo, hi = store.expert_range
+    guess = [e for e in torch.unique(sel).tolist() if lo <= e < hi]
+    store.prefetch(layer_next, guess)
+    return guess
+
+
 def pack_router(router_w: torch.Tensor, shared_gate: torch.Tensor, ctx: Optional[Context] = None) -> torch.Tensor:
     """The router [E, H] and shared gate [H] transposed into one f32 [H, 264] matrix (wmoe_pack_router): the
     decode kernel reads each CTA's rows of it as one contiguous block."""
