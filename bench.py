@@ -784,6 +784,20 @@ def run_reference(args, rank, world):
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                                  "sample": "each step: " + base["sample"] + "; divided by 40 layers"},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload == "batch64":
+        K, W = args.steps, args.warmup
+        vals = [cpu_baseline_batch(sample_experts=8)["value"] for _ in range(W + K)][W:]
+        value = statistics.mean(vals)
+        base = cpu_baseline_batch(sample_experts=8)
+        return {"metric": METRIC_BATCH, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": BATCH_T / value * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": "configs[2]: 64 tokens through one MoE layer, Zipf-biased routing",
+                           "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
+                           "tokens_per_step": BATCH_T},
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                 "sample": "each step: " + base["sample"]},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload == "prefill4096":
         K, W = args.steps, args.warmup
         vals = [cpu_baseline_prefill(sample_experts=8)["value"] for _ in range(W + K)][W:]
