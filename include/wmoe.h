@@ -123,6 +123,13 @@ int wmoe_store_upload(wmoe_store* store, int layer, int expert, const void* host
  * willow_v2_b200/synth.py), in the store's resident slots or its host copy when capped. */
 int wmoe_store_fill_synthetic(wmoe_store* store, uint64_t seed, int layer_begin, int layer_end, void* stream);
 size_t wmoe_store_blob_bytes(const wmoe_store* store);
+/* Sets a layer's down-matrix type (routed experts and the shared expert): 14 Q6_K (the default) or 12 Q4_K, as
+ * llama.cpp's Q4_K_M files store some layers (gguf/compiler.py:42-44 records the type per layer). Set it before
+ * uploading the layer: a Q4_K layer's blob is gate_up then H rows of 288 bytes (wmoe_store_layer_blob_bytes). The
+ * grouped GEMMs and dequant-GEMV kernels run both; the persistent decode kernel runs Q6_K layers only (single-token
+ * calls on a Q4_K layer take the GEMV kernels, wmoe_decode_stack refuses such a layer). */
+int wmoe_store_set_down_type(wmoe_store* store, int layer, int ggml_type);
+size_t wmoe_store_layer_blob_bytes(const wmoe_store* store, int layer);
 /* Makes the given experts of a layer resident (copies misses from the host copy on the store's side stream;
  * the compute stream waits for them). Returns WMOE_ERR_CAPACITY if they cannot all fit at once. */
 int wmoe_store_prepare(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream);

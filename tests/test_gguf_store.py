@@ -93,6 +93,23 @@ def test_expert_blobs_are_the_pack_layout(tmp_path, fused, files):
         files_.close()
 
 
+def test_q4k_down_layers_are_read(tmp_path):
+    """llama.cpp's Q4_K_M files store some layers' ffn_down_exps as Q4_K: such a layer's blob is gate ‖ up ‖ down
+    rows of 288 bytes."""
+    path, arrays = write_model(str(tmp_path), down_type=Q.Q4_K)
+    meta, tensors = gguf_store.read_gguf(path)
+    lay = gguf_store.expert_layout(meta, tensors)
+    assert lay.down_type(0) == "Q4_K" and lay.blob_bytes(0) == 2 * 256 * 512 // 256 * 144 + 512 * 256 // 256 * 144
+    files_ = gguf_store._Files()
+    try:
+        blob = gguf_store.expert_blob(files_, lay, 1, 3)
+        a = arrays[1]
+        np.testing.assert_array_equal(blob, np.concatenate([a["gate"][3].ravel(), a["up"][3].ravel(),
+                                                            a["down"][3].ravel()]))
+    finally:
+        files_.close()
+
+
 def test_unsupported_layout_is_an_error(tmp_path):
     path, _ = write_model(str(tmp_path), down_type=Q.Q8_0)
     meta, tensors = gguf_store.read_gguf(path)

@@ -458,6 +458,54 @@ def test_add_rmsnorm_matches_oracle(model):
     ctx.check_device()
 
 
+def test_q4k_down_layer_matches_oracle(model):
+    """A layer whose down matrices (routed and shared) are Q4_K, as llama.cpp's Q4_K_M files store some layers:
+    the dequant-GEMV kernels (4 tokens, and one token, which may not take the Q6_K decode kernel) and the grouped
+    GEMMs (64 tokens) against the float32 oracle; wmoe_decode_stack refuses such a layer."""
+    import torch
+    from willow_v2_b200 import moe
+    from willow_v2_b200.lib import WmoeError, lib
+    ctx, store, layers = model
+    gu_bytes = store.gate_up_bytes
+    dn_bytes = 2048 * 512 // 256 * 144
+    q4 = moe.ExpertStore(1, ctx=ctx)
+    q4.set_down_type(0, "Q4_K")
+    assert q4.layer_blob_bytes(0) == gu_bytes + dn_bytes
+    gate_up = {e: store.download(0, e)[:gu_bytes] for e in range(256)}
+    down = {e: store.download(1, e)[:dn_bytes] for e in range(256)}  # valid Q4_K super-blocks
+    for e in range(256):
+        q4.upload(0, e, np.concatenate([gate_up[e], down[e]]))
+    sgu = synth.expert_gate_up(SEED, 0, 256).reshape(-1)
+    sdn = synth.expert_gate_up(SEED, 1, 256).reshape(-1)[:dn_bytes]
+    lw = moe.LayerWeights(router_w=torch.from_numpy(synth.router_weight(SEED, 0)).cuda(),
+                          shared_gate=torch.from_numpy(synth.shared_gate_weight(SEED, 0)).cuda(),
+                          shared_gate_up=torch.from_numpy(sgu).cuda(),
+                          shared_down=torch.from_numpy(np.ascontiguousarray(sdn)).cuda()).prepare(ctx)
+
+    def experts(e):
+        g, d = (gate_up[e], down[e]) if e < 256 else (sgu, sdn)
+        return ora.dequantize(g, "Q4_K", (1024, 2048)), ora.dequantize(d, "Q4_K", (2048, 512))
+
+    ref_args = dict(router_w=synth.router_weight(SEED, 0), expert_weights=experts, shared=experts(256),
+                    shared_gate_w=synth.shared_gate_weight(SEED, 0))
+    for T, path, tol in ((4, "gemv", 1e-4), (1, "gemv", 1e-4), (64, "gemm", 1e-3)):
+        x = torch.from_numpy(synth.hidden(SEED, T, step=80 + T)).cuda()
+        prev = lib.wmoe_set_prefill_threshold(ctx.handle, 1 if path == "gemm" else 1 << 30)
+        try:
+            out = moe.moe_forward(q4, 0, x, lw)
+            torch.cuda.synchronize()
+        finally:
+            lib.wmoe_set_prefill_threshold(ctx.handle, prev)
+        idx = list(range(T)) if T <= 4 else [0, 31, 63]
+        ref = ora.moe(x[idx].cpu().numpy(), **ref_args)[0]
+        err = rel_l2(out[idx].cpu().numpy(), ref)
+        assert err < tol, (T, path, err)
+    with pytest.raises(WmoeError, match="Q6_K"):
+        moe.decode_stack(q4, [lw], torch.from_numpy(synth.hidden(SEED, 1)).cuda())
+    ctx.check_device()
+    q4.close()
+
+
 def test_cap_too_small_is_an_error(model):
     import torch
     from willow_v2_b200 import moe

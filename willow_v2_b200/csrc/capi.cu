@@ -327,6 +327,16 @@ int wmoe_store_fill_synthetic(wmoe_store* store, uint64_t seed, int layer_begin,
 
 size_t wmoe_store_blob_bytes(const wmoe_store* store) { return store ? store->blob_bytes : 0; }
 
+int wmoe_store_set_down_type(wmoe_store* store, int layer, int ggml_type) {
+  if (!store) return WMOE_ERR_INVALID;
+  return store_set_down_type(store, layer, ggml_type);
+}
+
+size_t wmoe_store_layer_blob_bytes(const wmoe_store* store, int layer) {
+  if (!store || layer < 0 || layer >= store->layers) return 0;
+  return store->layer_blob_bytes(layer);
+}
+
 int wmoe_store_prepare(wmoe_store* store, int layer, const int32_t* experts, int n, void* stream) {
   if (!store || (n > 0 && !experts)) return WMOE_ERR_INVALID;
   return store_prepare(store, layer, experts, n, static_cast<cudaStream_t>(stream));
@@ -343,12 +353,13 @@ int wmoe_store_download(wmoe_store* store, int layer, int expert, void* host_dst
   if (!store->owns(expert)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_download: expert outside the store's range");
   if (slot >= 0) {
     WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(host_dst, store->d_slab + size_t(slot) * store->slot_stride,
-                                         store->blob_bytes, cudaMemcpyDeviceToHost, st),
+                                         store->layer_blob_bytes(layer), cudaMemcpyDeviceToHost, st),
                     "wmoe_store_download");
     WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "wmoe_store_download");
   } else if (store->h_master) {
     WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "wmoe_store_download");
-    memcpy(host_dst, store->h_master + store->blob_index(layer, expert) * store->blob_bytes, store->blob_bytes);
+    memcpy(host_dst, store->h_master + store->blob_index(layer, expert) * store->blob_bytes,
+           store->layer_blob_bytes(layer));
   } else {
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_store_download: blob not present");
   }
@@ -444,12 +455,13 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   if (!x || !router_w || !shared_gate || !shared_gate_up || !shared_down || !out)
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: null pointer");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (T == 1 && !store->capped && ctx->use_decode_kernel && ctx->decode_ctas > 0 && E == 256) {
+  if (T == 1 && !store->capped && ctx->use_decode_kernel && ctx->decode_ctas > 0 && E == 256 &&
+      store->down_type[size_t(layer)] == kGgmlQ6K) {
     // one token, every expert resident: the persistent decode kernel (one launch, no host synchronisation)
     if (int rc = ensure_scratch(ctx, decode_scratch_bytes(H, F, E, ctx->decode_ctas))) return rc;
     DecodeLayer dl{router_w, router_bias, shared_gate, shared_gate_up, shared_down, router_packed, router_split};
     int n = 0;
-    const cudaError_t e = decode_persistent(store_source(store, shared_gate_up, shared_down), layer, 1, &dl, H, F, E,
+    const cudaError_t e = decode_persistent(store_source(store, layer, shared_gate_up, shared_down), layer, 1, &dl, H, F, E,
                                             top_k, 0.f, false, x, x_dtype, out, out_dtype, topk_idx_out, topk_w_out,
                                             ctx->scratch, ctx->decode_ctas, ctx->d_status, ctx->trace,
                                             ctx->trace_entries, st, &n);
@@ -537,7 +549,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
                            ctx->d_status, st, &n),
                   "dispatch");
   mark(2);
-  const ExpertSource src = store_source(store, shared_gate_up, shared_down);
+  const ExpertSource src = store_source(store, layer, shared_gate_up, shared_down);
   if (gemm_path) {
     WMOE_CHECK_CUDA(ctx,
                     prefill_experts(src, layer, pm, topk_idx, H, F, x, x_dtype, topk_w, shared_s, out, out_dtype,
@@ -721,7 +733,7 @@ static int ep_experts_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, int worl
   __half* xg = static_cast<__half*>(sp(o_xg));
   WMOE_CHECK_CUDA(ctx, ep_gather(pm.perm, pair_row, P_r, recv_buf, x, x_dtype, T, H, xg, st, &n),
                   "expert stage: gather");
-  const ExpertSource src = store_source(store, w->shared_gate_up, w->shared_down);
+  const ExpertSource src = store_source(store, layer, w->shared_gate_up, w->shared_down);
   WMOE_CHECK_CUDA(ctx,
                   prefill_gemms(src, layer, pm, P, H, F, xg, reinterpret_cast<__half*>(y), pm.perm, P_r, sp(o_gemm),
                                 gemm_ctas, ctx->d_status, nullptr, st, &n),
@@ -1137,10 +1149,15 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
   for (int i = 0; i < n_layers; ++i)
     if (!layers[i].router_w || !layers[i].shared_gate || !layers[i].shared_gate_up || !layers[i].shared_down)
       return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack: null weight pointer in layers[]");
+  for (int i = 0; i < n_layers; ++i)
+    if (store->down_type[size_t(layer_begin + i)] != kGgmlQ6K)
+      return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED,
+                      "wmoe_decode_stack: the persistent kernel runs Q6_K down matrices; call wmoe_moe_forward per "
+                      "layer for Q4_K ones");
   const size_t need = decode_scratch_bytes(store->hidden, store->ffn, store->experts, ctx->decode_ctas);
   if (int rc = ensure_scratch(ctx, need)) return rc;
   int n = 0;
-  const ExpertSource src = store_source(store, nullptr, nullptr);
+  const ExpertSource src = store_source(store, layer_begin, nullptr, nullptr);
   const cudaError_t e = decode_persistent(src, layer_begin, n_layers, reinterpret_cast<const DecodeLayer*>(layers),
                                           store->hidden, store->ffn, store->experts, 8, eps, true, h_in, WMOE_F32,
                                           h_out, WMOE_F32, topk_idx_out, nullptr, ctx->scratch, ctx->decode_ctas,
@@ -1169,6 +1186,10 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
     return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED,
                     "wmoe_decode_stack_noalloc: the persistent kernel cannot be co-resident here");
   for (int i = 0; i < n_layers; ++i)
+    if (store->down_type[size_t(layer_begin + i)] != kGgmlQ6K)
+      return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_decode_stack_noalloc: the persistent kernel runs Q6_K down "
+                                                 "matrices; call wmoe_moe_forward per layer for Q4_K ones");
+  for (int i = 0; i < n_layers; ++i)
     if (!layers[i].router_w || !layers[i].shared_gate || !layers[i].shared_gate_up || !layers[i].shared_down)
       return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: null weight pointer in layers[]");
   const size_t need = decode_scratch_bytes(store->hidden, store->ffn, store->experts, ctx->decode_ctas);
@@ -1183,7 +1204,7 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
   void* scratch = nullptr;
   WMOE_CHECK_CUDA(ctx, static_scratch(ctx->device, &scratch), "wmoe_decode_stack_noalloc: static scratch address");
   int n = 0;
-  const ExpertSource src = store_source(store, nullptr, nullptr);
+  const ExpertSource src = store_source(store, layer_begin, nullptr, nullptr);
   const cudaError_t e = decode_persistent(src, layer_begin, n_layers, reinterpret_cast<const DecodeLayer*>(layers),
                                           store->hidden, store->ffn, store->experts, 8, eps, true, h_in, WMOE_F32,
                                           h_out, WMOE_F32, topk_idx_out, nullptr, scratch, ctx->decode_ctas,

@@ -59,20 +59,24 @@ constexpr int kTileB = kBN * kBK * 2;                 // 24 KB fp16 tokens
 constexpr int kQ4Row = 144;                           // one Q4_K super-block of a row
 constexpr int kQ4Unit = kBM * kQ4Row;                 // 18,432 B: one super-block column of the tile
 constexpr int kQ6Unit = kBM * 2 * Q6K_BYTES;          // 53,760 B: 128 down rows of F = 512
+constexpr int kQ4DRow = 2 * Q4K_BYTES;                // a Q4_K down row of F = 512
+constexpr int kQ4DUnit = kBM * kQ4DRow;               // 36,864 B: 128 Q4_K down rows
 constexpr int kXbufBytes = 32 * 64 * 4;               // gate/up exchange of 32 columns (fp32)
 constexpr int kOutBytes = 32 * kBM * 2;                // one 32-column chunk of the output, token-major fp16
 
+// MODE 0: gate_up (Q4_K) + SwiGLU; 1: down with Q6_K rows; 2: down with Q4_K rows
 template <int MODE>
 struct Layout {
   static constexpr int bstages = MODE == 0 ? 6 : 4;      // token tile ring
-  static constexpr int depth = MODE == 0 ? 3 : 2;        // weight byte ring
-  static constexpr int unit = MODE == 0 ? kQ4Unit : kQ6Unit;
+  static constexpr int depth = MODE == 1 ? 2 : 3;        // weight byte ring
+  static constexpr int unit = MODE == 0 ? kQ4Unit : (MODE == 1 ? kQ6Unit : kQ4DUnit);
   static constexpr int raw = bstages * kTileB;           // weight ring offset (1024-aligned)
   static constexpr int xbuf = raw + depth * unit;        // gate_up only
   static constexpr int obuf = xbuf + (MODE == 0 ? kXbufBytes : 0);
   static constexpr int bytes = obuf + kOutBytes + 1024;  // + alignment slack
 };
-static_assert(Layout<0>::bytes <= 232448 && Layout<1>::bytes <= 232448, "shared memory");
+static_assert(Layout<0>::bytes <= 232448 && Layout<1>::bytes <= 232448 && Layout<2>::bytes <= 232448, "shared memory");
+static_assert(Layout<2>::bstages <= kMaxBStages && Layout<2>::depth <= 3 && kQ4DUnit % 1024 == 0, "Q4_K down ring");
 static_assert(Layout<0>::bstages <= kMaxBStages && Layout<1>::bstages <= kMaxBStages, "barrier arrays");
 static_assert(kTileB % 1024 == 0 && kQ4Unit % 1024 == 0, "TMA destinations stay 1024-aligned");
 
@@ -329,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint8_t* w = slot == kSharedSlot
                                    ? p.src.shared_down
                                    : p.src.slab + size_t(slot) * p.src.slot_bytes + p.src.gate_up_bytes;
-            bulk_g2s(dst, w + size_t(kQ6Unit) * t.mt, unsigned(kQ6Unit), &bars.raw_full[rs]);
+            bulk_g2s(dst, w + size_t(L::unit) * t.mt, unsigned(L::unit), &bars.raw_full[rs]);
           }
           issued_w = ru + 1;
         }
@@ -398,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n = nv;
         // output row of column c0 + lane (remapped rows of the down launch fetched once per chunk)
         int lane_row = prow0 + c0 + lane;
-        if (MODE == 1 && p.out_rows && lane < n && lane_row < p.n_routed) lane_row = p.out_rows[lane_row];
+        if (MODE != 0 && p.out_rows && lane < n && lane_row < p.n_routed) lane_row = p.out_rows[lane_row];
         constexpr int pieces = 32 * orows / 8;  // 16-byte pieces of the chunk
 #pragma unroll
         for (int q = e; q < pieces; q += 128) {
@@ -408,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4*>(gout + size_t(row) * ld + 8 * g) =
                 *reinterpret_cast<const uint4*>(obuf + c * orows + 8 * g);
         }
-        if (MODE == 1) asm volatile("bar.sync 1, 128;" ::: "memory");  // obuf is rewritten by the next chunk
+        if (MODE != 0) asm volatile("bar.sync 1, 128;" ::: "memory");  // obuf is rewritten by the next chunk
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -424,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int un = 0; un < units; ++un) {
         const int ru = it * units + un, rs = ru % L::depth;
         if (!mbar_wait_warp(&bars.raw_full[rs], unsigned((ru / L::depth) & 1), fail)) goto out;
-        const uint8_t* wrow = raw + rs * L::unit + r * (MODE == 0 ? kQ4Row : 2 * Q6K_BYTES);
+        const uint8_t* wrow = raw + rs * L::unit + r * (MODE == 0 ? kQ4Row : (MODE == 1 ? 2 * Q6K_BYTES : kQ4DRow));
         const int kb0 = MODE == 0 ? 4 * un : 0, kb1 = MODE == 0 ? 4 * un + 4 : nk;
         for (int kb = kb0 + j; kb < kb1; kb += 2) {
           const int kbg = it * nk + kb, s = kbg % kAStages;
@@ -435,8 +439,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ta = tlane + uint32_t(kACol0 + 32 * s);
           if (MODE == 0)
             dequant_q4k_block(wrow, kb % 4, ta);
-          else
+          else if (MODE == 1)
             dequant_q6k_block(wrow, kb, ta);
+          else  // K block kb: nibble group kb % 4 of super-block kb / 4
+            dequant_q4k_block(wrow + (kb / 4) * Q4K_BYTES, kb % 4, ta);
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
@@ -651,6 +657,9 @@ cudaError_t prefill_gemms(const ExpertSource& src, int layer, const PairMap& pm,
     if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   Layout<1>::bytes)) != cudaSuccess)
       return e;
+    if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Layout<2>::bytes)) != cudaSuccess)
+      return e;
     attr_set = true;
   }
   const uint64_t q4_row = uint64_t(H / QK) * Q4K_BYTES;
@@ -680,7 +689,10 @@ cudaError_t prefill_gemms(const ExpertSource& src, int layer, const PairMap& pm,
   gp.out = y;
   gp.out_rows = out_rows;
   gp.n_routed = n_routed;
-  grouped_gemm_kernel<1><<<unsigned(num_sms), kThreads, Layout<1>::bytes, st>>>(map_h, map_w, map_ws, gp);
+  if (src.down_type == kGgmlQ4K)
+    grouped_gemm_kernel<2><<<unsigned(num_sms), kThreads, Layout<2>::bytes, st>>>(map_h, map_w, map_ws, gp);
+  else
+    grouped_gemm_kernel<1><<<unsigned(num_sms), kThreads, Layout<1>::bytes, st>>>(map_h, map_w, map_ws, gp);
   if (marks) cudaEventRecord(marks[1], st);
   *launches += 2;
   return cudaGetLastError();

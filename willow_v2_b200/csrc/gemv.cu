@@ -294,11 +294,54 @@ __global__ void __launch_bounds__(256) down_gemv_kernel(ExpertSource src, int la
   }
 }
 
+// Q4_K down rows (F = 512: 2 super-blocks x 144 B, as some layers of llama.cpp's Q4_K_M files store them): 8 lanes
+// per row, lane task t = (super-block t / 4, nibble group t % 4), the Q4_K lane arithmetic of gate_up.
+template <int F>
+__global__ void __launch_bounds__(256) down_q4k_gemv_kernel(ExpertSource src, int layer, PairMap pm, int H,
+                                                            const int16_t* __restrict__ hq,
+                                                            const float* __restrict__ hs,
+                                                            const int32_t* __restrict__ hsum16,
+                                                            float* __restrict__ y, int* status) {
+  constexpr int LPR = F / 256 * 4, RPW = 32 / LPR, kRowBytes = F / 256 * Q4K_BYTES;
+  const int u = blockIdx.y;
+  if (u >= *pm.n_used) return;
+  const int e = pm.used[u], p0 = pm.seg[u], p1 = pm.seg[u + 1];
+  const uint8_t* w = down_of(src, layer, e, status);
+  if (w == nullptr) return;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int r = (blockIdx.x * 8 + warp) * RPW + lane / LPR;
+  const int task = lane % LPR, sb = task / 4, g = task % 4;
+  const bool valid = r < H;
+  const Q4Lane wl = q4_lane_load(w + size_t(valid ? r : 0) * kRowBytes + sb * Q4K_BYTES, g);
+  for (int p = p0; p < p1; ++p) {
+    const uint4* xr = reinterpret_cast<const uint4*>(hq + size_t(p) * F + sb * 256 + 64 * g);
+    uint4 x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = xr[i];
+    const int xb = p * (F / 32) + sb * 8 + 2 * g;
+    const float sx0 = hs[xb], sx1 = hs[xb + 1];
+    const int* s16 = hsum16 + size_t(p) * (F / 16) + sb * 16 + 4 * g;
+    const float sum0 = float(s16[0] + s16[1]), sum1 = float(s16[2] + s16[3]);
+    int a0 = 0, a1 = 0;
+    q4_lane_dot(wl, x, a0, a1);
+    float part = sx0 * (wl.A0 * float(a0) - wl.B0 * sum0) + sx1 * (wl.A1 * float(a1) - wl.B1 * sum1);
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (task == 0 && valid) y[size_t(p) * H + r] = part;
+  }
+}
+
 cudaError_t down_gemv(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const int16_t* hq,
                       const float* hs, const int32_t* hsum16, float* y, int* status, cudaStream_t st,
                       int* launches) {
   if (F != 512) return cudaErrorInvalidValue;
   constexpr int rows_per_cta = 8 * (32 / 8);
+  if (src.down_type == kGgmlQ4K) {
+    const dim3 grid(unsigned((H + rows_per_cta - 1) / rows_per_cta), unsigned(std::min(pm.E, pm.T * pm.k) + 1));
+    down_q4k_gemv_kernel<512><<<grid, 256, 0, st>>>(src, layer, pm, H, hq, hs, hsum16, y, status);
+    ++*launches;
+    return cudaGetLastError();
+  }
   const dim3 grid(unsigned((H + rows_per_cta - 1) / rows_per_cta), unsigned(std::min(pm.E, pm.T * pm.k) + 1));
   down_gemv_kernel<512><<<grid, 256, 0, st>>>(src, layer, pm, H, hq, hs, hsum16, y, status);
   ++*launches;

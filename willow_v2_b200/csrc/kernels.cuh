@@ -20,6 +20,7 @@ struct ExpertSource {
   int n_slots;             // slots in the slab
   const uint8_t* shared_gate_up;
   const uint8_t* shared_down;
+  int down_type;           // ggml type of the layer's down matrices, routed and shared: 14 Q6_K or 12 Q4_K
 };
 
 // Result of dispatch for T tokens with top-k routing, plus the shared expert as an extra segment.

@@ -145,6 +145,7 @@ int store_create(wmoe_ctx* ctx, int layers, int experts, int expert_begin, int e
   }
   s->slot_of.assign(total, -1);
   s->usage.assign(total, 0);
+  s->down_type.assign(size_t(layers), kGgmlQ6K);
   if (e == cudaSuccess && s->capped) e = cudaHostAlloc(&s->h_master, held * s->blob_bytes, cudaHostAllocDefault);
   if (e != cudaSuccess) {
     const std::string msg = std::string("expert store allocation: ") + cudaGetErrorString(e);
@@ -197,7 +198,7 @@ int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cud
     // the host copy is the master; drop any resident copy so the next prepare reloads it
     e = cudaStreamSynchronize(st);
     if (e == cudaSuccess) {
-      memcpy(s->h_master + s->blob_index(layer, expert) * s->blob_bytes, host_src, s->blob_bytes);
+      memcpy(s->h_master + s->blob_index(layer, expert) * s->blob_bytes, host_src, s->layer_blob_bytes(layer));
       const int slot = s->slot_of[key];
       if (slot >= 0) {
         SlotUpdates u{};
@@ -208,7 +209,7 @@ int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cud
       }
     }
   } else {
-    e = cudaMemcpyAsync(s->d_slab + size_t(s->slot_of[key]) * s->slot_stride, host_src, s->blob_bytes,
+    e = cudaMemcpyAsync(s->d_slab + size_t(s->slot_of[key]) * s->slot_stride, host_src, s->layer_blob_bytes(layer),
                         cudaMemcpyHostToDevice, st);
   }
   if (e != cudaSuccess) return store_fail(s, -6, std::string("wmoe_store_upload: ") + cudaGetErrorString(e));
@@ -218,6 +219,9 @@ int store_upload(wmoe_store* s, int layer, int expert, const void* host_src, cud
 int store_fill_synthetic(wmoe_store* s, uint64_t seed, int layer_begin, int layer_end, cudaStream_t st) {
   if (layer_begin < 0 || layer_end > s->layers || layer_begin > layer_end)
     return store_fail(s, -1, "wmoe_store_fill_synthetic: bad layer range");
+  for (int l = layer_begin; l < layer_end; ++l)
+    if (s->down_type[size_t(l)] != kGgmlQ6K)
+      return store_fail(s, -1, "wmoe_store_fill_synthetic: the generator makes Q6_K down matrices only");
   const int E = s->experts, n = int(s->owned());
   std::vector<int32_t> le(size_t(2) * n);
   int32_t* d_le = nullptr;
@@ -447,8 +451,17 @@ int store_mark_used(wmoe_store* s, int layer, const int32_t* experts, int n, cud
   return 0;
 }
 
-ExpertSource store_source(const wmoe_store* s, const uint8_t* shared_gate_up, const uint8_t* shared_down) {
+int store_set_down_type(wmoe_store* s, int layer, int ggml_type) {
+  if (layer < 0 || layer >= s->layers) return store_fail(s, -1, "wmoe_store_set_down_type: bad layer");
+  if (ggml_type != kGgmlQ6K && ggml_type != kGgmlQ4K)
+    return store_fail(s, -1, "wmoe_store_set_down_type: down matrices run as Q6_K (14) or Q4_K (12)");
+  s->down_type[size_t(layer)] = ggml_type;
+  return 0;
+}
+
+ExpertSource store_source(const wmoe_store* s, int layer, const uint8_t* shared_gate_up, const uint8_t* shared_down) {
   ExpertSource src;
+  src.down_type = s->down_type[size_t(layer >= 0 && layer < s->layers ? layer : 0)];
   src.slab = s->d_slab;
   src.slot_of = s->d_slot_of;
   src.slot_bytes = s->slot_stride;

@@ -49,6 +49,12 @@ struct wmoe_store {
   // index of an owned blob among the store's blobs (layer-major), e.g. into the pinned host copy
   size_t blob_index(int layer, int e) const { return size_t(layer) * owned() + size_t(e - expert_begin); }
   size_t gate_up_bytes = 0, down_bytes = 0, blob_bytes = 0, slot_stride = 0;
+  // ggml type of each layer's down matrices (Q6_K, or Q4_K as some layers of llama.cpp's Q4_K_M files), and the
+  // layer's blob size (gate_up then down; a Q4_K layer's blob is shorter than blob_bytes, the slot stride)
+  std::vector<int> down_type;
+  size_t layer_blob_bytes(int layer) const {
+    return down_type[size_t(layer)] == 12 ? gate_up_bytes + size_t(hidden) * ffn / 256 * 144 : blob_bytes;
+  }
   bool capped = false;
   int n_slots = 0;
   uint8_t* d_slab = nullptr;
@@ -86,4 +92,7 @@ int store_prefetch(wmoe_store* s, int layer, const int32_t* experts, int n, cuda
 int store_mark_used(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st);
 void store_record_usage(wmoe_store* s, int layer, const int32_t* experts, size_t n);
 int store_choose_hot(wmoe_store* s, double share);
-wmoe::ExpertSource store_source(const wmoe_store* s, const uint8_t* shared_gate_up, const uint8_t* shared_down);
+// the source of one layer: its down type comes with it
+wmoe::ExpertSource store_source(const wmoe_store* s, int layer, const uint8_t* shared_gate_up,
+                                const uint8_t* shared_down);
+int store_set_down_type(wmoe_store* s, int layer, int ggml_type);

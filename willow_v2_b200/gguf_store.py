@@ -157,8 +157,12 @@ class ExpertLayout:
     gate_up: Dict[int, Tuple[Tensor, ...]] = field(default_factory=dict)
     down: Dict[int, Tensor] = field(default_factory=dict)
 
-    def blob_bytes(self) -> int:
-        return 2 * self.ffn * self.hidden // 256 * 144 + self.hidden * self.ffn // 256 * 210
+    def down_type(self, layer: int) -> str:
+        return self.down[layer].type
+
+    def blob_bytes(self, layer: int = 0) -> int:
+        per = 144 if self.down_type(layer) == "Q4_K" else 210
+        return 2 * self.ffn * self.hidden // 256 * 144 + self.hidden * self.ffn // 256 * per
 
 
 def num_layers(meta: dict) -> int:
@@ -169,8 +173,9 @@ def num_layers(meta: dict) -> int:
 
 def expert_layout(meta: dict, tensors: Dict[str, Tensor]) -> ExpertLayout:
     """Finds every layer's blk.N.ffn_{gate,up,down}_exps (or a fused ffn_gate_up_exps) and checks what this library's
-    kernels run: gate/up Q4_K [E, F, H], down Q6_K [E, H, F], the same E, F, H on every layer, H and F multiples of
-    256. Raises GGUFError naming the first tensor that does not fit."""
+    kernels run: gate/up Q4_K [E, F, H], down Q6_K or Q4_K [E, H, F] (the type may differ per layer, as in llama.cpp's
+    Q4_K_M files), the same E, F, H on every layer, H and F multiples of 256. Raises GGUFError naming the first
+    tensor that does not fit."""
     n_layers = num_layers(meta)
     parts: Dict[int, Dict[str, Tensor]] = {}
     for name, t in tensors.items():
@@ -198,8 +203,9 @@ def expert_layout(meta: dict, tensors: Dict[str, Tensor]) -> ExpertLayout:
             if t.type != "Q4_K" or len(t.shape) != 3:
                 raise GGUFError(f"{t.name}: {t.type} {t.shape}; the kernels run Q4_K [experts, ffn, hidden]")
         down = p["down"]
-        if down.type != "Q6_K" or len(down.shape) != 3:
-            raise GGUFError(f"{down.name}: {down.type} {down.shape}; the kernels run Q6_K [experts, hidden, ffn]")
+        if down.type not in ("Q6_K", "Q4_K") or len(down.shape) != 3:
+            raise GGUFError(f"{down.name}: {down.type} {down.shape}; the kernels run Q6_K or Q4_K "
+                            "[experts, hidden, ffn]")
         E, rows, H = gu[0].shape
         F = rows // 2 if len(gu) == 1 else rows
         if len(gu) == 2 and gu[1].shape != gu[0].shape:
@@ -263,6 +269,7 @@ def load_experts(path: str, ctx=None, cap_bytes: int = 0, expert_range: Optional
     files = _Files()
     try:
         for layer in range(lay.layers):
+            store.set_down_type(layer, lay.down_type(layer))
             for e in range(lo, hi):
                 store.upload(layer, e, expert_blob(files, lay, layer, e))
     finally:
@@ -285,7 +292,7 @@ def _float_tensor(files: _Files, t: Tensor) -> np.ndarray:
 def layer_weights(path: str, ctx=None, prepare: bool = True, tensors_of=None):
     """moe.LayerWeights for every layer: router blk.N.ffn_gate_inp.weight [E, H] and shared-expert gate
     ffn_gate_inp_shexp.weight [H] as float32, the shared expert's ffn_{gate,up}_shexp (Q4_K [F, H]) fused into
-    gate_up bytes and ffn_down_shexp (Q6_K [H, F]) (the names of engines/qwen36/loader.py:37-41)."""
+    gate_up bytes and ffn_down_shexp ([H, F], of the layer's down type) (the names of engines/qwen36/loader.py:37-41)."""
     import torch
     from . import moe
     meta, tensors = tensors_of or read_gguf(path)
@@ -306,8 +313,9 @@ def layer_weights(path: str, ctx=None, prepare: bool = True, tensors_of=None):
                 raise GGUFError(f"layer {layer}: router {router.shape} / shared gate {gate_vec.shape}, expected "
                                 f"{(lay.experts, lay.hidden)} / {(lay.hidden,)}")
             sg, su, sd = (tensors[p + n] for n in need[2:])
+            # the kernels read the shared expert's down matrix with the layer's down type
             for t, typ, shape in ((sg, "Q4_K", (lay.ffn, lay.hidden)), (su, "Q4_K", (lay.ffn, lay.hidden)),
-                                  (sd, "Q6_K", (lay.hidden, lay.ffn))):
+                                  (sd, lay.down_type(layer), (lay.hidden, lay.ffn))):
                 if t.type != typ or tuple(t.shape) != shape:
                     raise GGUFError(f"{t.name}: {t.type} {t.shape}; the kernels run {typ} {shape}")
             gate_up = np.concatenate([files.view(sg, 0, sg.nbytes), files.view(su, 0, su.nbytes)])

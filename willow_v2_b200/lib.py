@@ -41,6 +41,8 @@ SIGNATURES = {
     "wmoe_store_blob_bytes": (_sz, [_p]),
     "wmoe_store_prepare": (_i, [_p, _i, _p, _i, _p]),
     "wmoe_store_prefetch": (_i, [_p, _i, _p, _i, _p]),
+    "wmoe_store_set_down_type": (_i, [_p, _i, _i]),
+    "wmoe_store_layer_blob_bytes": (_sz, [_p, _i]),
     "wmoe_store_choose_hot": (_i, [_p, ctypes.c_double]),
     "wmoe_store_prefetch_stats": (_i, [_p, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
     "wmoe_add_rmsnorm": (_i, [_p, _p, _p, _i, _i, _i, ctypes.c_float, _p, _p, _i, _p]),

@@ -160,12 +160,21 @@ class ExpertStore:
         self.gate_up_bytes = 2 * ffn * hidden // 256 * 144
         self.capped = cap_bytes != 0 and cap_bytes < layers * held * ((self.blob_bytes + 255) // 256 * 256)
 
+    def set_down_type(self, layer: int, type_name: str):
+        """The layer's down-matrix type: "Q6_K" (default) or "Q4_K" (some layers of llama.cpp's Q4_K_M files).
+        Set before uploading the layer; its blob is then layer_blob_bytes(layer) long."""
+        check(self.ctx.handle, lib.wmoe_store_set_down_type(self.handle, layer, _GGML[type_name][0]))
+
+    def layer_blob_bytes(self, layer: int) -> int:
+        return int(lib.wmoe_store_layer_blob_bytes(self.handle, layer))
+
     def upload(self, layer: int, expert: int, blob):
-        """blob: the expert's bytes (numpy uint8 / bytes, or a CPU uint8 tensor), blob_bytes long."""
+        """blob: the expert's bytes (numpy uint8 / bytes, or a CPU uint8 tensor), layer_blob_bytes(layer) long."""
         arr = np.ascontiguousarray(np.frombuffer(blob, dtype=np.uint8) if isinstance(blob, (bytes, bytearray))
                                    else (blob.numpy() if isinstance(blob, torch.Tensor) else blob), dtype=np.uint8)
-        if arr.size != self.blob_bytes:
-            raise ValueError(f"expert blob is {arr.size} bytes, expected {self.blob_bytes}")
+        want = self.layer_blob_bytes(layer)
+        if arr.size != want:
+            raise ValueError(f"expert blob is {arr.size} bytes, expected {want}")
         check(self.ctx.handle, lib.wmoe_store_upload(self.handle, layer, expert,
                                                      arr.ctypes.data_as(ctypes.c_void_p), _stream()))
         torch.cuda.current_stream().synchronize()  # the host buffer may be freed after this returns
@@ -197,8 +206,8 @@ class ExpertStore:
         check(self.ctx.handle, lib.wmoe_store_choose_hot(self.handle, float(share)))
 
     def download(self, layer: int, expert: int) -> np.ndarray:
-        """The expert's bytes as the store holds them (uint8 [blob_bytes])."""
-        out = np.empty(self.blob_bytes, dtype=np.uint8)
+        """The expert's bytes as the store holds them (uint8 [layer_blob_bytes(layer)])."""
+        out = np.empty(self.layer_blob_bytes(layer), dtype=np.uint8)
         check(self.ctx.handle, lib.wmoe_store_download(self.handle, layer, expert,
                                                        out.ctypes.data_as(ctypes.c_void_p), _stream()))
         return out
