@@ -8,7 +8,7 @@ At N > 1 GPUs (torchrun) every rank serves its own token stream with its own ful
 "replicas only"), value = total tokens/s over all ranks, time = max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload decode40|batch64|prefill4096|prefill32k]
+                  [--workload decode40|batch64|prefill4096|prefill32k|typed-decode] [--ggml-type T|all]
 
 --workload batch64: 64 f32 tokens through one MoE layer with Zipf-biased routing (the
 sliced router, the dispatch sort and the grouped GEMMs); tokens/s and HBM GB/s over the distinct experts each step
@@ -22,6 +22,10 @@ parallel under torchrun. Run with few steps: `--steps 3 --warmup 3`.
 tokens per expert) through the tcgen05 grouped GEMMs; tokens/s, with the dominant GEMM launch against the measured
 bf16 tensor peak. At N > 1 it is expert-parallel (rank r holds 256/N experts, 4096 tokens per rank per step,
 NCCL all-to-all dispatch and combine).
+
+--workload typed-decode (the row of the other expert quant types): one token's 8 routed experts in a ggml type of
+willow's Metal path (gguf/metal.py:295), through gemv_batch + SwiGLU + gemv_combine as engines/base.py:492-532 runs
+them; one JSON line per type (1 GPU), with the gate_up launch against the measured HBM copy peak.
 
 --impl reference times the CPU restatement of willow's own CPU path (the oracle port; willow's code cannot run
 on the GPU box) on the host cores, on a bounded sample of the same workload.
@@ -848,13 +852,180 @@ def run_reference(args, rank, world):
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+TYPED_D_AT = {"Q6_K": 208}  # byte offset of the fp16 scale in a block (0 for the other types)
+
+
+def run_typed_decode(args, type_name: str):
+    """willow's batched decode of one token's routed experts in another ggml type (engines/base.py:492-532 with
+    gguf/metal.py's kernels): gemv_batch over 8 experts' gate_up [1024, 2048], SwiGLU, gemv_combine over their down
+    [2048, 512] with bf16 routing weights. Each step's 8 experts are drawn from a pool of at least 2 GB of experts
+    (L2 holds under 7% of it). Steps are captured in CUDA graphs of G steps (each on other experts) and replayed,
+    so the device time is not the host's launch rate; two more graphs hold only the gemv_batch or only the combine
+    launches, for their per-launch times."""
+    import torch
+    import torch.nn.functional as F
+    from willow_v2_b200 import ggml, moe
+    from willow_v2_b200 import lib as L
+    ctx = moe.default_context()
+    K, W = args.steps, args.warmup
+    elements, size = ggml.BLOCKS[type_name]
+    gu_b = 2 * FFN * ggml.row_bytes(type_name, HIDDEN)
+    dn_b = HIDDEN * ggml.row_bytes(type_name, FFN)
+    eb = gu_b + dn_b
+    pool = max(EXPERTS, -(-(2 << 30) // eb))
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+    slab = torch.randint(0, 256, (pool * eb,), dtype=torch.uint8, device="cuda", generator=g)
+    blocks = slab.view(-1, size)
+    d_at = TYPED_D_AT.get(type_name, 0)
+    nb = blocks.shape[0]
+    for off in ((d_at, 2) if type_name == "Q4_K" else (d_at,)):
+        d = torch.empty(nb, dtype=torch.float16, device="cuda").uniform_(1e-3, 4e-3, generator=g)
+        blocks[:, off:off + 2] = d.view(torch.uint8).view(nb, 2)
+    del d
+    G = 50  # steps per graph
+    rng = np.random.default_rng(SEED)
+    sels = [rng.choice(pool, TOP_K, replace=False) for _ in range(G)]
+    base = slab.data_ptr()
+    gu_ptrs = [torch.tensor([base + int(e) * eb for e in s], dtype=torch.int64, device="cuda") for s in sels]
+    dn_ptrs = [torch.tensor([base + int(e) * eb + gu_b for e in s], dtype=torch.int64, device="cuda") for s in sels]
+    pos = torch.arange(TOP_K, dtype=torch.int64, device="cuda")
+    x = torch.randn(HIDDEN, generator=g, device="cuda").to(torch.bfloat16)
+    route = torch.rand(TOP_K, generator=g, device="cuda")
+    route = (route / route.sum()).to(torch.bfloat16)
+    gate_up = torch.empty(TOP_K, 2 * FFN, dtype=torch.bfloat16, device="cuda")
+    h = torch.empty(TOP_K, FFN, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(HIDDEN, dtype=torch.bfloat16, device="cuda")
+    tid = L.GGML_TYPES[type_name]
+
+    def up(i):
+        st = torch.cuda.current_stream().cuda_stream
+        L.check(ctx.handle, L.lib.wmoe_gemv_batch(ctx.handle, tid, gu_ptrs[i].data_ptr(), pos.data_ptr(), TOP_K, TOP_K,
+                                                  2 * FFN, HIDDEN, x.data_ptr(), L.BF16, gate_up.data_ptr(), L.BF16,
+                                                  st))
+
+    def act():
+        h.copy_((F.silu(gate_up[:, :FFN].float()) * gate_up[:, FFN:].float()).to(torch.bfloat16))
+
+    def down(i):
+        st = torch.cuda.current_stream().cuda_stream
+        L.check(ctx.handle, L.lib.wmoe_gemv_combine(ctx.handle, tid, dn_ptrs[i].data_ptr(), pos.data_ptr(), TOP_K,
+                                                    TOP_K, HIDDEN, FFN, h.data_ptr(), route.data_ptr(), L.BF16,
+                                                    y.data_ptr(), st))
+
+    for s in range(W):
+        up(s % G), act(), down(s % G)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    graphs = {}
+    for name, body in (("step", lambda i: (up(i), act(), down(i))), ("up", up), ("down", down)):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(G):
+                body(i)
+        graphs[name] = graph
+    reps = max(-(-K // G), 400)  # at least 20,000 steps (~0.7 s): the clock sampler sees the timed region
+    stream = torch.cuda.current_stream()
+
+    def timed(name):
+        graphs[name].replay()  # untimed replay: warm instruction caches and the graph itself
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graphs[name].replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (reps * G)
+
+    launches0 = ctx.launches
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        step_ms = timed("step")
+    gpu_launches = 2 * reps * G  # the graph's replays launch the captured kernels; ctx counts captures, not replays
+    gu_ms, dn_ms = timed("up"), timed("down")
+    ctx.check_device()
+    del launches0
+    # e2e through the public Python API (willow_v2_b200.ggml), no graph: x from pinned host memory in, y back out
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(HIDDEN, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    offs = [[int(e) * eb for e in s] for s in sels]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for s in range(K):
+        x_dev.copy_(x_host, non_blocking=True)
+        ggml.gemv_batch(slab, type_name, (2 * FFN, HIDDEN), x_dev, offs[s % G], list(range(TOP_K)), gate_up,
+                        ctx=ctx)
+        hh = (F.silu(gate_up[:, :FFN].float()) * gate_up[:, FFN:].float()).to(torch.bfloat16)
+        out = ggml.gemv_combine(slab, type_name, (HIDDEN, FFN), hh, [o + gu_b for o in offs[s % G]], route,
+                                list(range(TOP_K)), ctx=ctx)
+        y_host.copy_(out.reshape(-1), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    hbm, _, peak_kind = peaks()
+    gu_gbs = TOP_K * gu_b / (gu_ms * 1e-3) / 1e9
+    dn_gbs = TOP_K * dn_b / (dn_ms * 1e-3) / 1e9
+    step_gbs = TOP_K * eb / (step_ms * 1e-3) / 1e9
+    return {
+        "metric": f"typed batched-decode tokens/s (8 routed experts of one MoE layer, {type_name} weights)",
+        "value": 1e3 / step_ms, "unit": "tokens/s", "n_gpus": 1, "steps": reps * G, "warmup": W,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 (f32 sums)",
+        "data": f"synthetic: random {type_name} blocks with fp16 scales U[1e-3, 4e-3]; bf16 N(0,1) token",
+        "config": {"workload": f"typed-decode {type_name}: gemv_batch (gate_up [1024, 2048]) + SwiGLU + gemv_combine "
+                               "(down [2048, 512]) for 8 experts per step",
+                   "ggml_type": type_name, "expert_bytes": eb, "pool_experts": pool, "pool_bytes": pool * eb,
+                   "l2": "inputs larger than L2: each step reads 8 other experts of the >= 2 GB pool",
+                   "timing": f"CUDA graphs of {G} steps replayed {reps} times; events around the replays"},
+        "roofline": {"bound": "hbm", "kernel": "ggml_gemv_kernel (gemv_batch of the 8 gate_up matrices)",
+                     "achieved": gu_gbs, "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": None,
+                     "peak_kind": peak_kind, "algorithmic_bytes_per_launch": TOP_K * gu_b, "launch_ms": gu_ms},
+        "combine": {"kernel": "ggml_combine_kernel (8 down matrices + bf16 weighted sum)", "launch_ms": dn_ms,
+                    "achieved_gbs": dn_gbs, "frac": dn_gbs / hbm},
+        "roofline_step": {"achieved": step_gbs, "frac": step_gbs / hbm, "algorithmic_bytes": TOP_K * eb},
+        "e2e": {"value": 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": HIDDEN * 2,
+                "d2h_bytes_per_step": HIDDEN * 2, "path": "willow_v2_b200.ggml.gemv_batch / gemv_combine"},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clocks.summary(),
+    }
+
+
+def cpu_baseline_typed(type_name: str):
+    """The oracle port of the same step on the host cores: dequantise the 8 experts' matrices and multiply (numpy,
+    the BLAS threads numpy has)."""
+    from oracle import ggml_types as G
+    elements, size = G.BLOCKS[type_name]
+    rng = np.random.default_rng(SEED)
+    gu = rng.integers(0, 256, (2 * FFN * HIDDEN // elements, size), dtype=np.uint8)
+    dn = rng.integers(0, 256, (HIDDEN * FFN // elements, size), dtype=np.uint8)
+    d_at = TYPED_D_AT.get(type_name, 0)
+    for b in (gu, dn):
+        for off in ((d_at, 2) if type_name == "Q4_K" else (d_at,)):
+            b[:, off:off + 2] = rng.uniform(1e-3, 4e-3, b.shape[0]).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    x = rng.standard_normal(HIDDEN).astype(np.float32)
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 1 or time.perf_counter() - t0 < 2.0:
+        for _ in range(TOP_K):
+            a = G.dequantize(gu, type_name, (2 * FFN, HIDDEN)) @ x
+            h = a[:FFN] / (1 + np.exp(-np.clip(a[:FFN], -80, 80))) * a[FFN:]
+            _ = G.dequantize(dn, type_name, (HIDDEN, FFN)) @ h
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": 1.0 / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{reps} tokens x 8 experts ({type_name}), same shapes, ~2 s"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode40", choices=["decode40", "batch64", "prefill4096", "prefill32k"])
+    ap.add_argument("--workload", default="decode40",
+                    choices=["decode40", "batch64", "prefill4096", "prefill32k", "typed-decode"])
+    ap.add_argument("--ggml-type", default="all", help="typed-decode: one ggml type, or all (one JSON line each)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="stack depth (40 = the benchmark; fewer = profiling)")
     args = ap.parse_args()
@@ -877,6 +1048,14 @@ def main():
         d.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                              device_id=torch.device("cuda", local))
         dist = d
+    if args.workload == "typed-decode":
+        from willow_v2_b200 import ggml
+        for t in (ggml.TYPES if args.ggml_type == "all" else [args.ggml_type]):
+            result = run_typed_decode(args, t)
+            if not args.no_cpu_baseline:
+                result["cpu_baseline"] = cpu_baseline_typed(t)
+            print(json.dumps(result), flush=True)
+        return
     if args.workload == "prefill4096":
         result, _keep = run_prefill4096(args, rank, world, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

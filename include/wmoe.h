@@ -6,7 +6,8 @@
  * aborts or exits. A context is used from one host thread.
  *
  * Each entry point names the willow interface it replaces (paths within the willow-v2 project):
- *   wmoe_dequant             gguf/quants.py:207-227 dequantize (Q4_K 73-92, Q6_K 104-116);
+ *   wmoe_dequant             gguf/quants.py:207-227 dequantize (Q4_K 73-92, Q6_K 104-116, the other types
+ *                            27-195);
  *                            gguf/metal.py:217-228,357-363 dequant_<type> / dequantize_gpu
  *   wmoe_route               engines/base.py:91-97 route (+ the router linear, base.py:305-306,448,
  *                            and the shared-expert gate of base.py:104-107)
@@ -18,7 +19,11 @@
  *                            x + moe(rms_norm(x)) for one decode token, all layers in one launch
  *   wmoe_store_*             gguf/store.py:41-536 ExpertStore (slabs, LRU, load_batches, prefetch,
  *                            record_usage) and gguf/mps_shared.mm:10-20 shared_empty (host staging)
+ *   wmoe_ggml_row_bytes      gguf/metal.py:323-325 row_bytes
+ *   wmoe_gemv                gguf/metal.py:189-215,327-334 gemv_<type> / gemv (GGMLWeight.linear, 365-408)
  *   wmoe_gemv_batch          gguf/metal.py:239-261,336-343 gemv_batch (several experts x one token)
+ *   wmoe_gemv_combine        gguf/metal.py:263-291,345-355 gemv_combine (down + routing-weighted sum,
+ *                            engines/base.py:492-532 batched_decode_experts)
  */
 #ifndef WMOE_H
 #define WMOE_H
@@ -44,9 +49,18 @@ extern "C" {
 #define WMOE_BF16 1
 #define WMOE_F16 2
 
-/* ggml type ids (gguf/reader.py:14-48) */
+/* ggml type ids (gguf/reader.py:14-48). The MoE block runs Q4_K gate_up with Q6_K or Q4_K down; wmoe_dequant and
+ * the typed kernels (wmoe_gemv*) run every type of willow's Metal path (gguf/metal.py:295). */
+#define WMOE_GGML_Q5_0 6
+#define WMOE_GGML_Q8_0 8
 #define WMOE_GGML_Q4_K 12
 #define WMOE_GGML_Q6_K 14
+#define WMOE_GGML_IQ3_XXS 18
+#define WMOE_GGML_IQ4_NL 20
+#define WMOE_GGML_IQ3_S 21
+#define WMOE_GGML_IQ2_S 22
+#define WMOE_GGML_IQ4_XS 23
+#define WMOE_GGML_Q2_0 42
 
 typedef struct wmoe_ctx wmoe_ctx;
 typedef struct wmoe_store wmoe_store;
@@ -81,7 +95,8 @@ int wmoe_device_status(wmoe_ctx* ctx, int* status, void* stream);
 
 /* ---- quantised weights ------------------------------------------------------------------------------ */
 
-/* Dequantises nblocks ggml super-blocks (Q4_K: 144 B, Q6_K: 210 B each, 256 values) to out_dtype.
+/* Dequantises nblocks ggml blocks of any WMOE_GGML_* type (Q4_K: 144 B, Q6_K: 210 B, IQ2_S: 82 B ... per block of
+ * 256 values; Q5_0, Q8_0, IQ4_NL: 32 values; Q2_0: 64) to out_dtype, nblocks x elements values.
  * F32 output is bit-identical to gguf/quants.py:dequantize; BF16/F16 are that value rounded to nearest even. */
 int wmoe_dequant(wmoe_ctx* ctx, int ggml_type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype,
                  void* stream);
@@ -304,10 +319,32 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
 int wmoe_add_rmsnorm(wmoe_ctx* ctx, const float* x, const void* y, int y_dtype, int T, int hidden, float eps,
                      float* x_out, void* xn_out, int xn_dtype, void* stream);
 
-/* Several experts' [rows, k] Q4_K or Q6_K weights times one token: y[i] = W_i x for i < n.
- * weights: device array of n device pointers; x f32 [k]; y f32 [n, rows]. */
-int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, int n, int rows, int k,
-                    const float* x, float* y, void* stream);
+/* ---- typed expert kernels (gguf/metal.py) ----------------------------------------------------------- */
+/* Matrices are [rows, k] ggml blocks, rows back to back (a row is wmoe_ggml_row_bytes(type, k) bytes) at an even
+ * address; k is a multiple of 32 and of the type's block. Sums are float32; x, y, route_w are f32 or bf16 (16-byte
+ * aligned). An out-of-range position or perm entry, or an odd matrix address, sets the device status
+ * (wmoe_device_status) and that matrix is skipped. */
+
+/* Bytes of one row of k values; 0 for a type these kernels do not run or a k that is not a whole number of blocks. */
+size_t wmoe_ggml_row_bytes(int ggml_type, int k);
+
+/* y [tokens, rows] = x [tokens, k] . W^T for 1 <= tokens <= 8 (gguf/metal.py:189-215 gemv_<type>). */
+int wmoe_gemv(wmoe_ctx* ctx, int ggml_type, const uint8_t* w, int rows, int k, const void* x, int x_dtype,
+              int tokens, void* y, int y_dtype, void* stream);
+
+/* Several matrices times one token: y[positions[i]] = W_i x for i < n (gguf/metal.py:239-261 gemv_batch_<type>).
+ * weights: device array of n device pointers; positions: device int64 [n] with entries < n_out, or null for i
+ * (n_out >= n); x [k]; y [n_out, rows]. */
+int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, const int64_t* positions, int n,
+                    int n_out, int rows, int k, const void* x, int x_dtype, void* y, int y_dtype, void* stream);
+
+/* y [rows] = sum over i < n, in order, of route_w[perm[i]] * (W_i x_i) (gguf/metal.py:263-291 gemv_combine_<type>).
+ * dtype WMOE_BF16: x [n, k], route_w and y are bf16, and each W_i x_i, each scaled product and the running sum are
+ * rounded to bf16 as engines/base.py:431-443 combine_decode_experts does; WMOE_F32: all float32, no rounding.
+ * weights: device array of n device pointers; perm: device int64 [n] with entries < n_route. */
+int wmoe_gemv_combine(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, const int64_t* perm, int n,
+                      int n_route, int rows, int k, const void* x, const void* route_w, int dtype, void* y,
+                      void* stream);
 
 #ifdef __cplusplus
 }

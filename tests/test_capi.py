@@ -74,7 +74,7 @@ def test_fp16_rounding_of_generator_matches_numpy():
 def test_header_cites_reference_for_each_entry_point():
     text = open(HEADER).read()
     for sym in ("wmoe_dequant", "wmoe_route", "wmoe_dispatch", "wmoe_moe_forward", "wmoe_decode_stack",
-                "wmoe_store_*", "wmoe_gemv_batch"):
+                "wmoe_store_*", "wmoe_gemv_batch", "wmoe_gemv", "wmoe_gemv_combine", "wmoe_ggml_row_bytes"):
         assert re.search(re.escape(sym) + r"\s+\S+\.py:\d+", text), sym
 
 

@@ -525,15 +525,15 @@ def test_gemv_batch_matches_oracle(model):
     import ctypes
     import torch
     from willow_v2_b200 import moe
-    from willow_v2_b200.lib import lib, check, GGML_Q4_K
+    from willow_v2_b200.lib import lib, check, GGML_Q4_K, F32
     ctx, store, _ = model
     x = synth.hidden(SEED, 1, step=2)[0]
     ptrs = (ctypes.c_void_p * 2)(store.blob_ptr(0, 3), store.blob_ptr(0, 200))
     dptrs = torch.tensor([store.blob_ptr(0, 3), store.blob_ptr(0, 200)], dtype=torch.int64).cuda()
     y = torch.empty(2, 1024, dtype=torch.float32, device="cuda")
-    check(ctx.handle, lib.wmoe_gemv_batch(ctx.handle, GGML_Q4_K, ctypes.c_void_p(dptrs.data_ptr()), 2, 1024, 2048,
-                                          ctypes.c_void_p(torch.from_numpy(x).cuda().data_ptr()),
-                                          ctypes.c_void_p(y.data_ptr()), moe._stream()))
+    check(ctx.handle, lib.wmoe_gemv_batch(ctx.handle, GGML_Q4_K, ctypes.c_void_p(dptrs.data_ptr()), None, 2, 2, 1024,
+                                          2048, ctypes.c_void_p(torch.from_numpy(x).cuda().data_ptr()), F32,
+                                          ctypes.c_void_p(y.data_ptr()), F32, moe._stream()))
     torch.cuda.synchronize()
     for i, e in enumerate((3, 200)):
         ref = ora.dequantize(synth.expert_gate_up(SEED, 0, e), "Q4_K", (1024, 2048)) @ x

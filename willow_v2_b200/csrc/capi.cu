@@ -186,13 +186,17 @@ int wmoe_device_status(wmoe_ctx* ctx, int* status, void* stream) {
 int wmoe_dequant(wmoe_ctx* ctx, int ggml_type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype,
                  void* stream) {
   if (!ctx) return WMOE_ERR_INVALID;
-  if (ggml_type != WMOE_GGML_Q4_K && ggml_type != WMOE_GGML_Q6_K)
-    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_dequant: only Q4_K and Q6_K are supported");
+  if (ggml_row_bytes(ggml_type, 256) == 0)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_dequant: type " + std::to_string(ggml_type) +
+                                                   " is not one of the WMOE_GGML_* types");
   if (out_dtype != WMOE_F32 && out_dtype != WMOE_BF16 && out_dtype != WMOE_F16)
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_dequant: bad output dtype");
   if (nblocks && (!blocks || !out)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_dequant: null pointer");
-  WMOE_CHECK_CUDA(ctx, dequant(ggml_type, blocks, nblocks, out, out_dtype, static_cast<cudaStream_t>(stream)),
-                  "wmoe_dequant");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (ggml_type == WMOE_GGML_Q4_K || ggml_type == WMOE_GGML_Q6_K)
+    WMOE_CHECK_CUDA(ctx, dequant(ggml_type, blocks, nblocks, out, out_dtype, st), "wmoe_dequant");
+  else
+    WMOE_CHECK_CUDA(ctx, ggml_dequant(ggml_type, blocks, nblocks, out, out_dtype, st), "wmoe_dequant");
   ctx->launches += nblocks ? 1 : 0;
   return WMOE_OK;
 }
@@ -1214,18 +1218,76 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
   return WMOE_OK;
 }
 
-int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, int n, int rows, int k,
-                    const float* x, float* y, void* stream) {
+size_t wmoe_ggml_row_bytes(int ggml_type, int k) { return ggml_row_bytes(ggml_type, k); }
+
+// the checks every typed-kernel call shares; 0 when the call may go on
+static int typed_args(wmoe_ctx* ctx, const char* fn, int type, int rows, int k) {
+  if (ggml_row_bytes(type, k) == 0 || k % 32)
+    return ctx_fail(ctx, ggml_row_bytes(type, 32 * 256) ? WMOE_ERR_INVALID : WMOE_ERR_UNSUPPORTED,
+                    std::string(fn) + ": type " + std::to_string(type) + " with k = " + std::to_string(k) +
+                        " is not a whole number of its blocks (or not a type of these kernels)");
+  if (rows < 0) return ctx_fail(ctx, WMOE_ERR_INVALID, std::string(fn) + ": rows < 0");
+  return 0;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int wmoe_gemv(wmoe_ctx* ctx, int ggml_type, const uint8_t* w, int rows, int k, const void* x, int x_dtype,
+              int tokens, void* y, int y_dtype, void* stream) {
   if (!ctx) return WMOE_ERR_INVALID;
-  if (ggml_type != WMOE_GGML_Q4_K && ggml_type != WMOE_GGML_Q6_K)
-    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv_batch: only Q4_K and Q6_K");
-  if (n < 0 || rows < 0 || k <= 0 || k % 256) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: bad shape");
+  if (int rc = typed_args(ctx, "wmoe_gemv", ggml_type, rows, k)) return rc;
+  if (tokens < 1 || tokens > 8) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv: tokens must be 1..8");
+  if ((x_dtype != WMOE_F32 && x_dtype != WMOE_BF16) || (y_dtype != WMOE_F32 && y_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv: x and y are f32 or bf16");
+  if (rows == 0) return WMOE_OK;
+  if (!w || !x || !y) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv: null pointer");
+  if ((reinterpret_cast<uintptr_t>(w) & 1) || !aligned16(x))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv: w must be 2-byte and x 16-byte aligned");
+  WMOE_CHECK_CUDA(ctx,
+                  ggml_gemv(ggml_type, nullptr, w, nullptr, 1, 1, rows, k, x, x_dtype, tokens, y, y_dtype,
+                            ctx->d_status, static_cast<cudaStream_t>(stream)),
+                  "wmoe_gemv");
+  ctx->launches += 1;
+  return WMOE_OK;
+}
+
+int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, const int64_t* positions, int n,
+                    int n_out, int rows, int k, const void* x, int x_dtype, void* y, int y_dtype, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (int rc = typed_args(ctx, "wmoe_gemv_batch", ggml_type, rows, k)) return rc;
+  if (n < 0 || (!positions && n_out < n))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: n < 0, or n_out < n without positions");
+  if ((x_dtype != WMOE_F32 && x_dtype != WMOE_BF16) || (y_dtype != WMOE_F32 && y_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: x and y are f32 or bf16");
   if (n == 0 || rows == 0) return WMOE_OK;
   if (!weights || !x || !y) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: null pointer");
-  int c = 0;
-  WMOE_CHECK_CUDA(ctx, gemv_batch(ggml_type, weights, n, rows, k, x, y, static_cast<cudaStream_t>(stream), &c),
+  if (!aligned16(x)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: x must be 16-byte aligned");
+  WMOE_CHECK_CUDA(ctx,
+                  ggml_gemv(ggml_type, weights, nullptr, positions, n, positions ? n_out : n, rows, k, x, x_dtype, 1,
+                            y, y_dtype, ctx->d_status, static_cast<cudaStream_t>(stream)),
                   "wmoe_gemv_batch");
-  ctx->launches += uint64_t(c);
+  ctx->launches += 1;
+  return WMOE_OK;
+}
+
+int wmoe_gemv_combine(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, const int64_t* perm, int n,
+                      int n_route, int rows, int k, const void* x, const void* route_w, int dtype, void* y,
+                      void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (int rc = typed_args(ctx, "wmoe_gemv_combine", ggml_type, rows, k)) return rc;
+  if (n < 1 || n_route < 1) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_combine: n and n_route must be >= 1");
+  if (dtype != WMOE_F32 && dtype != WMOE_BF16)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_combine: dtype is f32 or bf16");
+  if (rows == 0) return WMOE_OK;
+  if (!weights || !perm || !x || !route_w || !y)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_combine: null pointer");
+  if (!aligned16(x)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_combine: x must be 16-byte aligned");
+  const cudaError_t e = ggml_combine(ggml_type, weights, perm, n, n_route, rows, k, x, route_w, dtype, y,
+                                     ctx->d_status, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv_combine: a row tile of this k does not fit shared memory");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_gemv_combine");
+  ctx->launches += 1;
   return WMOE_OK;
 }
 

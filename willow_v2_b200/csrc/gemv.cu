@@ -402,53 +402,4 @@ cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* 
   return cudaGetLastError();
 }
 
-// ---------------------------------------------------------------- several weights x one f32 vector
-
-// y[i, row] = W_i[row] . x with the exact dequantised values (one warp per row, each lane a 32-value chunk).
-__global__ void __launch_bounds__(256) gemv_batch_kernel(int type, const uint8_t* const* __restrict__ weights,
-                                                         int n, int rows, int k, const float* __restrict__ x,
-                                                         float* __restrict__ y) {
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int row = blockIdx.x * 8 + warp, i = blockIdx.y;
-  if (row >= rows || i >= n) return;
-  const int nb = k / QK;
-  const uint8_t* w = weights[i] + size_t(row) * nb * (type == kGgmlQ4K ? Q4K_BYTES : Q6K_BYTES);
-  float acc = 0.f;
-  for (int c = lane; c < nb * 8; c += 32) {
-    const float* xc = x + c * 32;
-    if (type == kGgmlQ4K) {
-      const uint8_t* b = w + (c / 8) * Q4K_BYTES;
-      const int j = c % 8;
-      const float d = f16_to_f32(uint16_t(b[0] | (b[1] << 8))), dmin = f16_to_f32(uint16_t(b[2] | (b[3] << 8)));
-      int sc, mn;
-      q4k_scale_min(b + 4, j, sc, mn);
-      const float scale = __fmul_rn(d, float(sc)), m = __fmul_rn(dmin, float(mn));
-      const uint8_t* qs = b + 16 + 32 * (j / 2);
-      const int sh = 4 * (j % 2);
-      for (int l = 0; l < 32; ++l) acc = fmaf(__fsub_rn(__fmul_rn(scale, float((qs[l] >> sh) & 0xF)), m), xc[l], acc);
-    } else {
-      const uint8_t* b = w + (c / 8) * Q6K_BYTES;
-      const int cc = c % 8, hh = cc / 4, s = cc % 4;
-      const float d = f16_to_f32(uint16_t(b[208] | (b[209] << 8)));
-      const float s0 = __fmul_rn(d, float(int8_t(b[192 + 2 * cc]))), s1 = __fmul_rn(d, float(int8_t(b[193 + 2 * cc])));
-      const uint8_t* ql = b + 64 * hh + 32 * (s % 2);
-      const uint8_t* qh = b + 128 + 32 * hh;
-      for (int l = 0; l < 32; ++l) {
-        const int q = int(((ql[l] >> (4 * (s / 2))) & 0xF) | (((qh[l] >> (2 * s)) & 3) << 4)) - 32;
-        acc = fmaf(__fmul_rn(l < 16 ? s0 : s1, float(q)), xc[l], acc);
-      }
-    }
-  }
-  acc = warp_sum(acc);
-  if (lane == 0) y[size_t(i) * rows + row] = acc;
-}
-
-cudaError_t gemv_batch(int type, const uint8_t* const* weights, int n, int rows, int k, const float* x, float* y,
-                       cudaStream_t st, int* launches) {
-  const dim3 grid(unsigned((rows + 7) / 8), unsigned(n));
-  gemv_batch_kernel<<<grid, 256, 0, st>>>(type, weights, n, rows, k, x, y);
-  ++*launches;
-  return cudaGetLastError();
-}
-
 }  // namespace wmoe

@@ -1,0 +1,429 @@
+// Typed expert kernels over ggml blocks: every type of willow's Metal path (gguf/metal.py:295: Q5_0, Q8_0, IQ4_NL,
+// IQ4_XS, IQ3_XXS, IQ3_S, IQ2_S, Q2_0, Q4_K, Q6_K).
+//   ggml_dequant_kernel   blocks -> f32 / bf16 / f16, bit-identical to gguf/quants.py:dequantize
+//                         (gguf/metal.py:217-228 dequant_<type>, 357-363 dequantize_gpu)
+//   ggml_gemv_kernel      y[pos_i * tokens + t] = W_i x_t for up to 8 tokens and n matrices
+//                         (gguf/metal.py:189-215 gemv_<type>, 239-261 gemv_batch_<type>)
+//   ggml_combine_kernel   y = sum_i w[perm[i]] * (W_i x_i) in order of i, with engines/base.py:431-443's bf16
+//                         rounding at every step, or in float32 (gguf/metal.py:263-291 gemv_combine_<type>)
+//
+// A CTA owns a tile of consecutive rows of one matrix: those rows are one contiguous byte range, staged into shared
+// memory by 16-byte cp.async copies (the unaligned head and tail by 16-bit copies), so HBM sees full coalesced
+// sectors whatever the block size. Warps then decode from shared memory: a row is spread over L lanes (L = the
+// row's 32-value chunks, at most 32), so short rows (k = 512: 16 chunks) still keep every lane busy. The chunk
+// decoders are in ggml_types.cuh; the codebooks (generated from gguf-py at build time) are copied to shared memory.
+#include <algorithm>
+#include <type_traits>
+
+#include "ggml_types.cuh"
+
+#include "ggml_tables.inc"
+
+namespace wmoe {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kCombineThreads = 128;  // combine: 4 warps, so a [2048, 512] matrix spreads over 256 CTAs
+constexpr int kGemvTileRows = 16;     // gemv: rows per CTA (8 x 1024 rows -> 512 CTAs, whatever the block size)
+
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// Copies bytes [src, src + len) (src 2-aligned, len even) to shared memory at dst, where dst is 16-aligned plus
+// (src % 16), so the 16-byte-aligned middle of the source lands 16-byte aligned. Returns without waiting; the
+// caller waits with cp_async_wait_all() and a barrier.
+__device__ __forceinline__ void stage_bytes(uint8_t* dst, const uint8_t* src, size_t len) {
+  const uintptr_t s = reinterpret_cast<uintptr_t>(src), e = s + len;
+  const uintptr_t a = (s + 15) & ~uintptr_t(15), z = e & ~uintptr_t(15);
+  if (a < z) {
+    const size_t n16 = (z - a) / 16;
+    for (size_t i = threadIdx.x; i < n16; i += blockDim.x)
+      cp_async16(dst + (a - s) + 16 * i, reinterpret_cast<const uint8_t*>(a) + 16 * i);
+    for (uintptr_t p = s + 2 * threadIdx.x; p < a; p += 2 * blockDim.x)
+      *reinterpret_cast<uint16_t*>(dst + (p - s)) = *reinterpret_cast<const uint16_t*>(p);
+    for (uintptr_t p = z + 2 * threadIdx.x; p < e; p += 2 * blockDim.x)
+      *reinterpret_cast<uint16_t*>(dst + (p - s)) = *reinterpret_cast<const uint16_t*>(p);
+  } else {
+    for (uintptr_t p = s + 2 * threadIdx.x; p < e; p += 2 * blockDim.x)
+      *reinterpret_cast<uint16_t*>(dst + (p - s)) = *reinterpret_cast<const uint16_t*>(p);
+  }
+}
+
+// The type's codebook into shared memory at tab (16-byte aligned); returns the table view.
+template <int T>
+__device__ __forceinline__ GgmlTables load_tables(uint8_t* tab) {
+  GgmlTables tb{nullptr, nullptr, nullptr};
+  if constexpr (T == kGgmlIQ4NL || T == kGgmlIQ4XS) {
+    float* lv = reinterpret_cast<float*>(tab);
+    if (threadIdx.x < 16) lv[threadIdx.x] = float(kIq4nlLevels[threadIdx.x]);
+    tb.levels = lv;
+  } else if constexpr (T == kGgmlIQ3XXS || T == kGgmlIQ3S) {
+    constexpr int n = T == kGgmlIQ3XXS ? 256 : 512;
+    const uint32_t* src = T == kGgmlIQ3XXS ? kIq3xxsGrid : kIq3sGrid;
+    uint32_t* g = reinterpret_cast<uint32_t*>(tab);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) g[i] = src[i];
+    tb.grid32 = g;
+  } else if constexpr (T == kGgmlIQ2S) {
+    uint2* g = reinterpret_cast<uint2*>(tab);
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
+      g[i] = make_uint2(uint32_t(kIq2sGrid[i]), uint32_t(kIq2sGrid[i] >> 32));
+    tb.grid64 = g;
+  }
+  return tb;
+}
+
+template <typename OutT>
+__device__ __forceinline__ OutT to_out(float v);
+template <>
+__device__ __forceinline__ float to_out<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
+
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// 32 activations of token row xt (f32 or bf16) starting at element 32 * c, dotted with v
+__device__ __forceinline__ float dot32(const float (&v)[32], const void* x, int x_dtype, size_t off) {
+  float s = 0.f;
+  if (x_dtype == kF32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 q = __ldg(p + i);
+      s = fmaf(v[4 * i], q.x, s);
+      s = fmaf(v[4 * i + 1], q.y, s);
+      s = fmaf(v[4 * i + 2], q.z, s);
+      s = fmaf(v[4 * i + 3], q.w, s);
+    }
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 q = __ldg(p + i);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s = fmaf(v[8 * i + 2 * j], __uint_as_float(w[j] << 16), s);
+        s = fmaf(v[8 * i + 2 * j + 1], __uint_as_float(w[j] & 0xFFFF0000u), s);
+      }
+    }
+  }
+  return s;
+}
+
+// sum over the L lanes of a row group (L a power of two, groups aligned to L)
+template <int L>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------------------------------------------ dequant
+
+template <int T, typename OutT>
+__global__ void __launch_bounds__(kThreads) ggml_dequant_kernel(const uint8_t* __restrict__ blocks, size_t nblocks,
+                                                                OutT* __restrict__ out) {
+  __shared__ __align__(16) uint8_t tab[table_bytes(T) > 0 ? table_bytes(T) : 16];
+  const GgmlTables tb = load_tables<T>(tab);
+  __syncthreads();
+  constexpr BlockGeom g = block_geom(T);
+  constexpr int per = g.elements / 32;
+  const size_t chunk = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  if (chunk >= nblocks * per) return;
+  float v[32];
+  decode_chunk<T>(blocks + (chunk / per) * g.bytes, int(chunk % per), tb, v);
+  OutT* o = out + chunk * 32;
+#pragma unroll
+  for (int l = 0; l < 32; ++l) o[l] = to_out<OutT>(v[l]);
+}
+
+// ------------------------------------------------------------------------------------------------ gemv
+
+struct GemvArgs {
+  const uint8_t* const* weights;  // n device pointers to [rows, k] matrices, or null: the one matrix `single`
+  const uint8_t* single;
+  const int64_t* positions;       // nullable: output slot of matrix i (default i); checked against n_out
+  int n, n_out, rows, k, tokens, tile_rows;
+  size_t row_bytes;
+  const void* x;  // [tokens, k]
+  int x_dtype;
+  void* y;        // [n_out * tokens, rows]
+  int y_dtype;
+  int* status;
+};
+
+// L lanes per row, MAXT token accumulators
+template <int T, int L, int MAXT>
+__global__ void __launch_bounds__(kThreads) ggml_gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const GgmlTables tb = load_tables<T>(smem);
+  uint8_t* stage = smem + ((table_bytes(T) + 15) & ~15);
+  const int i = blockIdx.y, r0 = blockIdx.x * a.tile_rows;
+  const int nr = min(a.tile_rows, a.rows - r0);
+  const uint8_t* mat = a.weights ? a.weights[i] : a.single;
+  const int64_t pos64 = a.positions ? a.positions[i] : i;
+  // an output slot out of range or an odd matrix address: flag it and touch nothing (uniform over the CTA)
+  if (pos64 < 0 || pos64 >= a.n_out || (reinterpret_cast<uintptr_t>(mat) & 1)) {
+    if (threadIdx.x == 0) atomicCAS(a.status, kStatusOk, kStatusBadExpert);
+    return;
+  }
+  const int pos = int(pos64);
+  const uint8_t* src = mat + size_t(r0) * a.row_bytes;
+  uint8_t* base = stage + (reinterpret_cast<uintptr_t>(src) & 15);
+  stage_bytes(base, src, size_t(nr) * a.row_bytes);
+  cp_async_wait_all();
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr int kRowsPerWarp = 32 / L;
+  const int chunks = a.k / 32;
+  for (int rr = warp * kRowsPerWarp + lane / L; rr - lane / L < nr; rr += kWarps * kRowsPerWarp) {
+    const bool valid = rr < nr;
+    const uint8_t* row = base + size_t(valid ? rr : 0) * a.row_bytes;
+    float acc[MAXT];
+#pragma unroll
+    for (int t = 0; t < MAXT; ++t) acc[t] = 0.f;
+    if (valid) {
+      for (int c = lane % L; c < chunks; c += L) {
+        float v[32];
+        decode_row_chunk<T>(row, c, tb, v);
+#pragma unroll
+        for (int t = 0; t < MAXT; ++t)
+          if (t < a.tokens) acc[t] += dot32(v, a.x, a.x_dtype, size_t(t) * a.k + 32 * size_t(c));
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < MAXT; ++t) {
+      if (t >= a.tokens) break;
+      const float s = group_sum<L>(acc[t]);
+      if (valid && lane % L == 0) {
+        const size_t o = (size_t(pos) * a.tokens + t) * a.rows + r0 + rr;
+        if (a.y_dtype == kF32)
+          static_cast<float*>(a.y)[o] = s;
+        else
+          static_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(s);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ combine
+
+struct CombineArgs {
+  const uint8_t* const* weights;  // n device pointers to [rows, k] matrices
+  const int64_t* perm;            // [n]: index of matrix i's routing weight in route_w (checked against n_route)
+  int n, n_route, rows, k, tile_rows, group;  // group: matrices staged at once
+  size_t row_bytes;
+  const void* x;        // [n, k]: matrix i's input row
+  const void* route_w;  // [n_route]
+  int dtype;            // kBF16: bf16 x, weights, y and rounding at each step; kF32: all float32
+  void* y;              // [rows]
+  int* status;
+};
+
+// One CTA (kCombineThreads) per tile of rows_per_pass rows (each group of L lanes owns one row), all matrices of a
+// group staged at once, then summed in order.
+template <int T, int L>
+__global__ void __launch_bounds__(kCombineThreads) ggml_combine_kernel(CombineArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const GgmlTables tb = load_tables<T>(smem);
+  uint8_t* stage = smem + ((table_bytes(T) + 15) & ~15);
+  const int r0 = blockIdx.x * a.tile_rows, nr = min(a.tile_rows, a.rows - r0);
+  const size_t tile_bytes = size_t(nr) * a.row_bytes;
+  const size_t slot = ((size_t(a.tile_rows) * a.row_bytes + 15) & ~size_t(15)) + 16;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int rr = warp * (32 / L) + lane / L;  // this lane group's row of the tile
+  const bool valid = rr < nr;
+  const int chunks = a.k / 32;
+  // a routing index out of range or an odd matrix address: flag it and touch nothing (uniform over the CTA)
+  for (int e = 0; e < a.n; ++e) {
+    const int64_t pe = a.perm[e];
+    if (pe < 0 || pe >= a.n_route || (reinterpret_cast<uintptr_t>(a.weights[e]) & 1)) {
+      if (threadIdx.x == 0) atomicCAS(a.status, kStatusOk, kStatusBadExpert);
+      return;
+    }
+  }
+  float total = 0.f;
+  for (int g0 = 0; g0 < a.n; g0 += a.group) {
+    const int gn = min(a.group, a.n - g0);
+    __syncthreads();  // the previous group's reads of the stage are done
+    for (int m = 0; m < gn; ++m) {
+      const uint8_t* src = a.weights[g0 + m] + size_t(r0) * a.row_bytes;
+      stage_bytes(stage + m * slot + (reinterpret_cast<uintptr_t>(src) & 15), src, tile_bytes);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    for (int m = 0; m < gn; ++m) {
+      const int e = g0 + m;
+      const int64_t pe = a.perm[e];
+      const float rw = a.dtype == kF32 ? static_cast<const float*>(a.route_w)[pe]
+                                       : __bfloat162float(static_cast<const __nv_bfloat16*>(a.route_w)[pe]);
+      const uint8_t* src = a.weights[e] + size_t(r0) * a.row_bytes;
+      const uint8_t* row = stage + m * slot + (reinterpret_cast<uintptr_t>(src) & 15) +
+                           size_t(valid ? rr : 0) * a.row_bytes;
+      float acc = 0.f;
+      if (valid) {
+        for (int c = lane % L; c < chunks; c += L) {
+          float v[32];
+          decode_row_chunk<T>(row, c, tb, v);
+          acc += dot32(v, a.x, a.dtype, size_t(e) * a.k + 32 * size_t(c));
+        }
+      }
+      const float p = group_sum<L>(acc);
+      if (a.dtype == kF32) {
+        total = e == 0 ? __fmul_rn(rw, p) : fmaf(rw, p, total);
+      } else {
+        const float scaled = round_bf16(__fmul_rn(round_bf16(p), rw));
+        total = e == 0 ? scaled : round_bf16(__fadd_rn(total, scaled));
+      }
+    }
+  }
+  if (valid && lane % L == 0) {
+    if (a.dtype == kF32)
+      static_cast<float*>(a.y)[r0 + rr] = total;
+    else
+      static_cast<__nv_bfloat16*>(a.y)[r0 + rr] = __float2bfloat16_rn(total);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ launch
+
+template <typename F>
+cudaError_t by_type(int type, F&& f) {
+  switch (type) {
+    case kGgmlQ5_0: return f(std::integral_constant<int, kGgmlQ5_0>{});
+    case kGgmlQ8_0: return f(std::integral_constant<int, kGgmlQ8_0>{});
+    case kGgmlIQ4NL: return f(std::integral_constant<int, kGgmlIQ4NL>{});
+    case kGgmlIQ4XS: return f(std::integral_constant<int, kGgmlIQ4XS>{});
+    case kGgmlIQ3XXS: return f(std::integral_constant<int, kGgmlIQ3XXS>{});
+    case kGgmlIQ3S: return f(std::integral_constant<int, kGgmlIQ3S>{});
+    case kGgmlIQ2S: return f(std::integral_constant<int, kGgmlIQ2S>{});
+    case kGgmlQ2_0: return f(std::integral_constant<int, kGgmlQ2_0>{});
+    case kGgmlQ4K: return f(std::integral_constant<int, kGgmlQ4K>{});
+    case kGgmlQ6K: return f(std::integral_constant<int, kGgmlQ6K>{});
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// lanes per row: the row's chunk count rounded down to a power of two, between 8 and 32 (rows of fewer than 8
+// chunks leave lanes idle)
+int lanes_for(int chunks) {
+  int l = 8;
+  while (l * 2 <= chunks && l < 32) l *= 2;
+  return l;
+}
+
+template <typename F>
+cudaError_t by_lanes(int lanes, F&& f) {
+  switch (lanes) {
+    case 32: return f(std::integral_constant<int, 32>{});
+    case 16: return f(std::integral_constant<int, 16>{});
+    default: return f(std::integral_constant<int, 8>{});
+  }
+}
+
+constexpr size_t kStageBudget = 32 * 1024;  // staged weight bytes per CTA of the gemv kernel
+constexpr size_t kMaxSmem = 200 * 1024;
+
+// Raises a kernel's dynamic shared-memory limit to kMaxSmem once per process (the launch's own size decides what it
+// gets), so launches inside CUDA-graph capture make no attribute call.
+template <auto Kernel>
+cudaError_t allow_max_smem() {
+  static const cudaError_t e =
+      cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxSmem));
+  return e;
+}
+
+}  // namespace
+
+size_t ggml_row_bytes(int type, int k) {
+  const BlockGeom g = block_geom(type);
+  if (g.elements == 0 || k <= 0 || k % g.elements) return 0;
+  return size_t(k / g.elements) * g.bytes;
+}
+
+cudaError_t ggml_dequant(int type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype,
+                         cudaStream_t st) {
+  if (nblocks == 0) return cudaSuccess;
+  return by_type(type, [&](auto tc) -> cudaError_t {
+    constexpr int T = decltype(tc)::value;
+    const size_t chunks = nblocks * (block_geom(T).elements / 32);
+    const unsigned grid = unsigned((chunks + kThreads - 1) / kThreads);
+    if (out_dtype == kF32)
+      ggml_dequant_kernel<T, float><<<grid, kThreads, 0, st>>>(blocks, nblocks, static_cast<float*>(out));
+    else if (out_dtype == kBF16)
+      ggml_dequant_kernel<T, __nv_bfloat16><<<grid, kThreads, 0, st>>>(blocks, nblocks,
+                                                                        static_cast<__nv_bfloat16*>(out));
+    else
+      ggml_dequant_kernel<T, __half><<<grid, kThreads, 0, st>>>(blocks, nblocks, static_cast<__half*>(out));
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t ggml_gemv(int type, const uint8_t* const* weights, const uint8_t* single, const int64_t* positions, int n,
+                      int n_out, int rows, int k, const void* x, int x_dtype, int tokens, void* y, int y_dtype,
+                      int* status, cudaStream_t st) {
+  const size_t rb = ggml_row_bytes(type, k);
+  if (rb == 0 || k % 32 || tokens < 1 || tokens > 8) return cudaErrorInvalidValue;
+  if (n == 0 || rows == 0) return cudaSuccess;
+  GemvArgs a{weights, single, positions, n, n_out, rows, k, tokens, 0, rb, x, x_dtype, y, y_dtype, status};
+  a.tile_rows = int(std::max<size_t>(1, std::min<size_t>(std::min<size_t>(size_t(rows), kGemvTileRows),
+                                                         kStageBudget / rb)));
+  const size_t smem = size_t((table_bytes(type) + 15) & ~15) + size_t(a.tile_rows) * rb + 16;
+  if (smem > kMaxSmem) return cudaErrorInvalidValue;
+  const dim3 grid(unsigned((rows + a.tile_rows - 1) / a.tile_rows), unsigned(n));
+  const int lanes = lanes_for(k / 32);
+  return by_type(type, [&](auto tc) -> cudaError_t {
+    constexpr int T = decltype(tc)::value;
+    return by_lanes(lanes, [&](auto lc) -> cudaError_t {
+      constexpr int L = decltype(lc)::value;
+      if (tokens == 1) {
+        if (cudaError_t e = allow_max_smem<ggml_gemv_kernel<T, L, 1>>()) return e;
+        ggml_gemv_kernel<T, L, 1><<<grid, kThreads, smem, st>>>(a);
+      } else {
+        if (cudaError_t e = allow_max_smem<ggml_gemv_kernel<T, L, 8>>()) return e;
+        ggml_gemv_kernel<T, L, 8><<<grid, kThreads, smem, st>>>(a);
+      }
+      return cudaGetLastError();
+    });
+  });
+}
+
+cudaError_t ggml_combine(int type, const uint8_t* const* weights, const int64_t* perm, int n, int n_route, int rows,
+                         int k, const void* x, const void* route_w, int dtype, void* y, int* status,
+                         cudaStream_t st) {
+  const size_t rb = ggml_row_bytes(type, k);
+  if (rb == 0 || k % 32 || n < 1) return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  const int lanes = lanes_for(k / 32);
+  const int rows_per_pass = kCombineThreads / 32 * (32 / lanes);  // one row per lane group: the tile is one pass
+  CombineArgs a{weights, perm, n, n_route, rows, k, 0, 0, rb, x, route_w, dtype, y, status};
+  a.tile_rows = std::min(rows, rows_per_pass);
+  const size_t slot = ((size_t(a.tile_rows) * rb + 15) & ~size_t(15)) + 16;
+  const size_t tab = size_t((table_bytes(type) + 15) & ~15);
+  if (tab + slot > kMaxSmem) return cudaErrorInvalidValue;
+  a.group = int(std::min<size_t>(size_t(n), (kMaxSmem - tab) / slot));
+  a.group = std::min(a.group, int(std::max<size_t>(1, (96 * 1024) / slot)));  // keep a few CTAs per SM
+  const size_t smem = tab + size_t(a.group) * slot;
+  const dim3 grid(unsigned((rows + a.tile_rows - 1) / a.tile_rows));
+  return by_type(type, [&](auto tc) -> cudaError_t {
+    constexpr int T = decltype(tc)::value;
+    return by_lanes(lanes, [&](auto lc) -> cudaError_t {
+      constexpr int L = decltype(lc)::value;
+      if (cudaError_t e = allow_max_smem<ggml_combine_kernel<T, L>>()) return e;
+      ggml_combine_kernel<T, L><<<grid, kCombineThreads, smem, st>>>(a);
+      return cudaGetLastError();
+    });
+  });
+}
+
+}  // namespace wmoe

@@ -92,8 +92,6 @@ cudaError_t down_gemv(const ExpertSource& src, int layer, const PairMap& pm, int
                       int* launches);
 cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* shared_s, const float* y,
                     const float* residual, void* out, int out_dtype, cudaStream_t st, int* launches);
-cudaError_t gemv_batch(int type, const uint8_t* const* weights, int n, int rows, int k, const float* x, float* y,
-                       cudaStream_t st, int* launches);
 
 // gemm_sm100.cu: tcgen05 grouped GEMMs for many tokens per expert (gate_up + SwiGLU, down) and the fp16 combine
 size_t prefill_scratch_bytes(int T, int k, int E, int H, int F);
@@ -161,5 +159,21 @@ cudaError_t fill_synthetic(uint8_t* dst, uint64_t seed, const int32_t* layer_exp
                            uint64_t dst_stride, int hidden, int ffn, cudaStream_t st);
 cudaError_t fill_synthetic_one(uint8_t* dst, uint64_t seed, int layer, int expert, int hidden, int ffn,
                                cudaStream_t st);
+
+// Typed expert kernels over ggml blocks (ggml_gemv.cu). Types: 6 Q5_0, 8 Q8_0, 12 Q4_K, 14 Q6_K, 18 IQ3_XXS,
+// 20 IQ4_NL, 21 IQ3_S, 22 IQ2_S, 23 IQ4_XS, 42 Q2_0. ggml_row_bytes is 0 for another type or a k that is not a
+// whole number of blocks.
+size_t ggml_row_bytes(int type, int k);
+cudaError_t ggml_dequant(int type, const uint8_t* blocks, size_t nblocks, void* out, int out_dtype, cudaStream_t st);
+// y[(pos_i * tokens + t) * rows + r] = W_i[r] . x[t]; W_i = weights[i] (device array) or `single` when weights is
+// null; pos_i = positions[i] (device, < n_out) or i
+cudaError_t ggml_gemv(int type, const uint8_t* const* weights, const uint8_t* single, const int64_t* positions, int n,
+                      int n_out, int rows, int k, const void* x, int x_dtype, int tokens, void* y, int y_dtype,
+                      int* status, cudaStream_t st);
+// y[r] = sum_i route_w[perm[i]] * (W_i[r] . x[i]) in order of i; dtype kBF16 rounds each product, scaled product
+// and running sum to bf16 (engines/base.py:431-443), kF32 keeps float32
+cudaError_t ggml_combine(int type, const uint8_t* const* weights, const int64_t* perm, int n, int n_route, int rows,
+                         int k, const void* x, const void* route_w, int dtype, void* y, int* status,
+                         cudaStream_t st);
 
 }  // namespace wmoe

@@ -1,0 +1,206 @@
+"""Typed expert kernels over ggml blocks: the B200 counterpart of willow's gguf/metal.py, for every type its Metal
+path runs (gguf/metal.py:295: Q5_0, Q8_0, IQ4_NL, IQ4_XS, IQ3_XXS, IQ3_S, IQ2_S, Q2_0, Q4_K, Q6_K).
+
+  row_bytes(type_name, k)                                   gguf/metal.py:323-325
+  gemv(raw, type_name, shape, x)                            gguf/metal.py:327-334 (tokens <= MAX_TOKENS)
+  gemv_batch(base, type_name, shape, x, offsets, positions, out)    gguf/metal.py:336-343
+  gemv_combine(base, type_name, shape, x, offsets, weights, perm)   gguf/metal.py:345-355
+  dequantize_gpu(raw, type_name, shape)                     gguf/metal.py:357-363
+  GGMLWeight                                                gguf/metal.py:365-408 (F.linear on ggml blocks)
+
+Arguments mean what they mean there. bf16 in and out, summed in float32; gemv_combine rounds to bf16 at every
+step like engines/base.py:431-443. The kernels are CUDA (libwmoe.so, csrc/ggml_gemv.cu); a missing library raises
+on import, and a type outside TYPES raises NotImplementedError as willow's quants.dequantize does.
+"""
+import ctypes
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import lib as _lib
+from .lib import check, lib
+
+MAX_TOKENS = 8  # gemv handles up to this many tokens; more are dequantized to bf16 and multiplied by torch
+TYPES = ("Q5_0", "Q8_0", "IQ4_NL", "IQ4_XS", "IQ3_XXS", "IQ3_S", "IQ2_S", "Q2_0", "Q4_K", "Q6_K")
+# (elements, bytes) per block (gguf/reader.py:14-48)
+BLOCKS = {"Q5_0": (32, 22), "Q8_0": (32, 34), "IQ4_NL": (32, 18), "IQ4_XS": (256, 136), "IQ3_XXS": (256, 98),
+          "IQ3_S": (256, 110), "IQ2_S": (256, 82), "Q2_0": (64, 18), "Q4_K": (256, 144), "Q6_K": (256, 210)}
+_DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+
+
+def _type_id(type_name: str) -> int:
+    if type_name not in _lib.GGML_TYPES:
+        raise NotImplementedError(f"ggml type {type_name} has no CUDA kernel (supported: {', '.join(TYPES)})")
+    return _lib.GGML_TYPES[type_name]
+
+
+def _ctx():
+    from .moe import default_context
+    return default_context()
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _act(x: torch.Tensor) -> torch.Tensor:
+    """Activations as the kernels take them: bf16 or f32, contiguous (16-byte aligned rows)."""
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        x = x.to(torch.bfloat16)
+    return x.contiguous()
+
+
+def _on_gpu(*tensors):
+    """The kernels read these through device addresses: every one must be a CUDA tensor on one device."""
+    devs = {t.device for t in tensors}
+    if any(not t.is_cuda for t in tensors) or len(devs) != 1:
+        raise ValueError(f"expected CUDA tensors on one device, got {sorted(str(d) for d in devs)}")
+
+
+def _pointers(base: torch.Tensor, offsets) -> torch.Tensor:
+    """Device array of base + offset for each offset (the kernels take matrix addresses)."""
+    ptrs = torch.tensor([base.data_ptr() + int(o) for o in offsets], dtype=torch.int64)
+    return ptrs.to(base.device, non_blocking=False)
+
+
+def available() -> bool:
+    return torch.cuda.is_available()
+
+
+def row_bytes(type_name: str, k: int) -> int:
+    elements, size = BLOCKS[type_name]
+    return k // elements * size
+
+
+def dequantize_gpu(raw: torch.Tensor, type_name: str, shape: tuple, dtype: torch.dtype = torch.bfloat16,
+                   ctx=None) -> torch.Tensor:
+    """raw (uint8, on the GPU) -> dtype [shape] on the GPU; float32 bit-identical to gguf/quants.py:dequantize."""
+    ctx = ctx or _ctx()
+    gtype = _type_id(type_name)
+    elements, size = BLOCKS[type_name]
+    _on_gpu(raw)
+    assert raw.dtype == torch.uint8 and raw.is_contiguous()
+    nblocks = raw.numel() // size
+    numel = 1
+    for s in shape:
+        numel *= int(s)
+    if nblocks * size != raw.numel() or nblocks * elements != numel:
+        raise ValueError(f"{raw.numel()} bytes of {type_name} do not hold a tensor of shape {tuple(shape)}")
+    out = torch.empty(tuple(shape), dtype=dtype, device=raw.device)
+    check(ctx.handle, lib.wmoe_dequant(ctx.handle, gtype, _p(raw), nblocks, _p(out), _DTYPES[dtype], _stream()))
+    return out
+
+
+def gemv(raw: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+         ctx=None) -> torch.Tensor:
+    """raw: the weight's bytes (uint8, on the GPU); x: [tokens <= MAX_TOKENS, k] -> out_dtype [tokens, rows]."""
+    ctx = ctx or _ctx()
+    rows, k = shape
+    x = _act(x.reshape(-1, k))
+    if not 1 <= x.shape[0] <= MAX_TOKENS:
+        raise ValueError(f"gemv takes 1..{MAX_TOKENS} tokens, got {x.shape[0]}")
+    if raw.numel() < rows * row_bytes(type_name, k):
+        raise ValueError("raw holds fewer bytes than the [rows, k] matrix")
+    _on_gpu(raw, x)
+    y = torch.empty(x.shape[0], rows, dtype=out_dtype, device=raw.device)
+    check(ctx.handle, lib.wmoe_gemv(ctx.handle, _type_id(type_name), _p(raw), rows, k, _p(x), _DTYPES[x.dtype],
+                                    x.shape[0], _p(y), _DTYPES[out_dtype], _stream()))
+    return y
+
+
+def gemv_batch(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor, offsets: list, positions: list,
+               out: torch.Tensor, ctx=None):
+    """Several experts' weights, all [rows, k] of type_name at byte offsets in base (uint8, on the GPU), times one
+    token x ([1, k] or [k]): writes expert i's result to row positions[i] of out ([n, rows], bf16 or f32)."""
+    ctx = ctx or _ctx()
+    rows, k = shape
+    if len(offsets) != len(positions):
+        raise ValueError("one position per offset")
+    if not offsets:
+        return
+    rb = row_bytes(type_name, k)
+    for o in offsets:
+        if o < 0 or o + rows * rb > base.numel():
+            raise ValueError(f"offset {o} puts a [{rows}, {k}] {type_name} matrix outside base")
+    if any(not 0 <= p < out.shape[0] for p in positions):
+        raise ValueError("a position outside out")
+    assert out.is_contiguous() and out.shape[-1] == rows
+    x = _act(x.reshape(k))
+    _on_gpu(base, x, out)
+    ptrs = _pointers(base, offsets)
+    pos = torch.tensor(list(positions), dtype=torch.int64).to(base.device)
+    check(ctx.handle, lib.wmoe_gemv_batch(ctx.handle, _type_id(type_name), _p(ptrs), _p(pos), len(offsets),
+                                          out.shape[0], rows, k, _p(x), _DTYPES[x.dtype], _p(out),
+                                          _DTYPES[out.dtype], _stream()))
+
+
+def gemv_combine(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor, offsets: list,
+                 weights: torch.Tensor, perm: list, ctx=None) -> torch.Tensor:
+    """sum over i of weights[perm[i]] * (W_i x[i]), in order of i, rounded to bf16 at each step like torch's bf16
+    ops. W_i: [rows, k] of type_name at byte offsets[i] in base; x: bf16 [n, k]; weights: bf16 [top_k], on the GPU.
+    -> bf16 [1, rows]."""
+    ctx = ctx or _ctx()
+    rows, k = shape
+    n = len(offsets)
+    if n == 0 or len(perm) != n:
+        raise ValueError("one perm entry per offset, at least one")
+    rb = row_bytes(type_name, k)
+    for o in offsets:
+        if o < 0 or o + rows * rb > base.numel():
+            raise ValueError(f"offset {o} puts a [{rows}, {k}] {type_name} matrix outside base")
+    if any(not 0 <= p < weights.numel() for p in perm):
+        raise ValueError("a perm entry outside weights")
+    x = x.reshape(n, k).to(torch.bfloat16).contiguous()
+    w = weights.reshape(-1).to(torch.bfloat16).contiguous()
+    _on_gpu(base, x, w)
+    ptrs = _pointers(base, offsets)
+    pm = torch.tensor(list(perm), dtype=torch.int64).to(base.device)
+    y = torch.empty(1, rows, dtype=torch.bfloat16, device=base.device)
+    check(ctx.handle, lib.wmoe_gemv_combine(ctx.handle, _type_id(type_name), _p(ptrs), _p(pm), n, w.numel(), rows, k,
+                                            _p(x), _p(w), _lib.BF16, _p(y), _stream()))
+    return y
+
+
+class GGMLWeight:
+    """A [rows, k] weight kept as its ggml blocks on the GPU, used in place of a bf16 tensor: F.linear(x, weight)
+    runs the CUDA kernels above (through __torch_function__). raw is a uint8 tensor; a CPU tensor is copied to the
+    GPU on first use."""
+
+    @classmethod
+    def __torch_function__(cls, func, types, args=(), kwargs=None):
+        bias = (kwargs or {}).get("bias", args[2] if len(args) > 2 else None)
+        if func is F.linear and len(args) > 1 and isinstance(args[1], GGMLWeight) and bias is None:
+            return args[1].linear(args[0])
+        return NotImplemented
+
+    def __init__(self, raw: torch.Tensor, type_name: str, shape: tuple):
+        _type_id(type_name)
+        self.raw, self.type_name, self.shape = raw, type_name, tuple(shape)
+        self.nbytes = raw.numel()
+
+    def to_gpu(self, device=None):
+        if not self.raw.is_cuda:
+            self.raw = self.raw.to(device or torch.device("cuda", torch.cuda.current_device()), non_blocking=True)
+
+    def location(self):
+        """(the GPU buffer holding this weight's bytes, as a uint8 tensor; their byte offset in it), for the
+        batched kernels."""
+        self.to_gpu()
+        base = self.raw if self.raw._base is None else self.raw._base
+        return base, self.raw.storage_offset() - base.storage_offset()
+
+    def linear(self, x: torch.Tensor) -> torch.Tensor:
+        self.to_gpu()
+        flat = x.reshape(-1, x.shape[-1])
+        if not flat.is_cuda:
+            flat = flat.to(self.raw.device)
+        if flat.shape[0] <= MAX_TOKENS:
+            y = gemv(self.raw, self.type_name, self.shape, flat).to(x.dtype)
+        else:
+            y = F.linear(flat.to(torch.bfloat16), dequantize_gpu(self.raw, self.type_name, self.shape)).to(x.dtype)
+        return y.view(*x.shape[:-1], y.shape[-1]).to(x.device)

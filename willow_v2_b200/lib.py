@@ -10,6 +10,9 @@ OK = 0
 ERR_INVALID, ERR_CUDA, ERR_CAPACITY, ERR_DEVICE, ERR_UNSUPPORTED, ERR_IO, ERR_NCCL = -1, -2, -3, -4, -5, -6, -7
 F32, BF16, F16 = 0, 1, 2
 GGML_Q4_K, GGML_Q6_K = 12, 14
+# ggml type ids of every type wmoe_dequant and the typed kernels (wmoe_gemv*) run (gguf/reader.py:14-48)
+GGML_TYPES = {"Q5_0": 6, "Q8_0": 8, "Q4_K": 12, "Q6_K": 14, "IQ3_XXS": 18, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22,
+              "IQ4_XS": 23, "Q2_0": 42}
 STATUS_NAMES = {1: "expert id out of range", 2: "expert not resident", 3: "grid barrier timed out",
                 4: "bad segment", 5: "value out of the range of an fp16 intermediate"}
 
@@ -54,7 +57,10 @@ SIGNATURES = {
     "wmoe_moe_forward_layer": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _i, _p, _p, _p]),
     "wmoe_decode_stack": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
     "wmoe_decode_stack_noalloc": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
-    "wmoe_gemv_batch": (_i, [_p, _i, _p, _i, _i, _i, _p, _p, _p]),
+    "wmoe_ggml_row_bytes": (_sz, [_i, _i]),
+    "wmoe_gemv": (_i, [_p, _i, _p, _i, _i, _p, _i, _i, _p, _i, _p]),
+    "wmoe_gemv_batch": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _i, _p, _i, _p]),
+    "wmoe_gemv_combine": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _p, _i, _p, _p]),
     "wmoe_ep_route_plan": (_i, [_p, _i, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "wmoe_ep_experts": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p]),
     "wmoe_ep_combine": (_i, [_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _i, _p]),

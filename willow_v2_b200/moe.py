@@ -1,7 +1,7 @@
 """The host side of the B200 MoE block: thin PyTorch-facing wrappers over libwmoe.so that mirror willow's own
 interfaces, so willow's engine can call them unchanged.
 
-  dequantize(raw, type_name, shape, dtype)   gguf/quants.py:207-227 (Q4_K, Q6_K), on the GPU
+  dequantize(raw, type_name, shape, dtype)   gguf/quants.py:207-227 (every type of ggml.TYPES), on the GPU
   route(x, router_w, top_k, ...)             engines/base.py:91-97 route, after the router linear (base.py:448)
   dispatch(selected, experts)                engines/base.py:456-467 grouping + store.py:482-484 record_usage
   ExpertStore                                gguf/store.py:41-536 (HBM slots; capped LRU over pinned host memory)
@@ -90,18 +90,10 @@ def default_context() -> Context:
 
 def dequantize(raw: torch.Tensor, type_name: str, shape: tuple, dtype: torch.dtype = torch.bfloat16,
                ctx: Optional[Context] = None) -> torch.Tensor:
-    """raw: uint8 CUDA tensor holding one Q4_K or Q6_K tensor's bytes -> a new tensor of shape and dtype
-    (float32 bit-identical to gguf/quants.py:dequantize; bf16/f16 rounded to nearest even from it)."""
-    ctx = ctx or default_context()
-    if type_name not in _GGML:
-        raise NotImplementedError(f"ggml type {type_name} is not supported (supported: Q4_K, Q6_K)")
-    gtype, block = _GGML[type_name]
-    assert raw.is_cuda and raw.dtype == torch.uint8 and raw.is_contiguous()
-    nblocks = raw.numel() // block
-    assert nblocks * block == raw.numel() and nblocks * 256 == int(np.prod(shape)), (type_name, shape, raw.shape)
-    out = torch.empty(shape, dtype=dtype, device=raw.device)
-    check(ctx.handle, lib.wmoe_dequant(ctx.handle, gtype, _ptr(raw), nblocks, _ptr(out), _DTYPES[dtype], _stream()))
-    return out
+    """raw: uint8 CUDA tensor holding one ggml tensor's bytes (any type of ggml.TYPES) -> a new tensor of shape and
+    dtype (float32 bit-identical to gguf/quants.py:dequantize; bf16/f16 rounded to nearest even from it)."""
+    from .ggml import dequantize_gpu
+    return dequantize_gpu(raw, type_name, shape, dtype, ctx)
 
 
 def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int = 8, bias: Optional[torch.Tensor] = None,
