@@ -1034,6 +1034,23 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and args.workload == "typed-decode":
+        if rank == 0:
+            from willow_v2_b200.ggml import TYPES
+            for t in (TYPES if args.ggml_type == "all" else [args.ggml_type]):
+                base = cpu_baseline_typed(t)
+                v = base["value"]
+                print(json.dumps({
+                    "metric": f"typed batched-decode tokens/s (8 routed experts of one MoE layer, {t} weights)",
+                    "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "dtype": "f32", "data": "synthetic", "impl": "reference",
+                    "config": {"workload": f"typed-decode {t}: 8 experts' gate_up [1024, 2048] + SwiGLU + down "
+                                           "[2048, 512]", "ggml_type": t},
+                    "cpu_baseline": base,
+                    "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                    flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:

@@ -3,8 +3,9 @@
 CPU: the numpy restatement (oracle/ggml_types.py) reproduces the golden values willow's own gguf/quants.py
 produced (tests/golden/make_golden_types.py) bit for bit, and the library's row sizes match the block table.
 GPU: wmoe_dequant is bit-identical to the oracle for every type (f32; bf16 = its round-to-nearest-even);
-wmoe_gemv / gemv_batch / gemv_combine (through willow_v2_b200.ggml, the mirror of gguf/metal.py) match the oracle's
-float32 products within the stated tolerances; GGMLWeight runs F.linear on both paths (gemv, dequant + matmul)."""
+wmoe_gemv / gemv_batch / gemv_combine (through willow_v2_b200.ggml, the mirror of gguf/metal.py; integer dot
+products on int16 activations) match the oracle's float32 products within the stated tolerances; GGMLWeight runs
+F.linear on both paths (gemv, dequant + matmul)."""
 import os
 
 import numpy as np
@@ -16,6 +17,9 @@ from oracle import ggml_types as G
 GOLDEN = os.path.join(REPO, "tests", "golden", "ggml_types.npz")
 SEED = 5
 TOL_F32 = 2e-5   # relative L2 of float32 outputs (same products, another summation order)
+# the GEMV kernels take activations as int16 with a power-of-two scale per 32 values (exact for bf16 values within
+# 2^6 of their block's largest; smaller ones round at 2^-14 of it): float32 outputs within this relative L2
+TOL_GEMV = 1e-4
 TOL_BF16 = 5e-3  # relative L2 of bf16 outputs (one bf16 rounding: <= 2^-9 relative per element)
 
 
@@ -137,7 +141,7 @@ def test_gemv_matches_oracle(ctx, type_name):
             xb = G.bf16(x32)
             y = ggml.gemv(raw, type_name, (rows, k), torch.from_numpy(xb).cuda().to(torch.bfloat16),
                           out_dtype=torch.float32, ctx=ctx)
-            assert rel_l2(y.cpu().numpy(), xb @ w.T) < TOL_F32, (rows, k, tokens)
+            assert rel_l2(y.cpu().numpy(), xb @ w.T) < TOL_GEMV, (rows, k, tokens)
             yb = ggml.gemv(raw, type_name, (rows, k), torch.from_numpy(x32).cuda(), ctx=ctx)
             assert yb.dtype == torch.bfloat16
             assert rel_l2(yb.float().cpu().numpy(), x32 @ w.T) < TOL_BF16, (rows, k, tokens)
@@ -168,7 +172,7 @@ def test_gemv_batch_positions_and_combine(ctx, type_name):
                     out, ctx=ctx)
     got = out.cpu().numpy()
     for i, m in enumerate(mats):
-        assert rel_l2(got[positions[i]], G.dequantize(m, type_name, (rows, k)) @ x) < TOL_F32, i
+        assert rel_l2(got[positions[i]], G.dequantize(m, type_name, (rows, k)) @ x) < TOL_GEMV, i
     assert not got[2].any() and not got[4].any()  # untouched positions
 
     xs = G.bf16(rng.standard_normal((n, k)).astype(np.float32))
@@ -190,7 +194,7 @@ def test_gemv_batch_positions_and_combine(ctx, type_name):
                                             rows, k, ggml._p(xs_t), ggml._p(rw_t), F32, ggml._p(y32),
                                             ggml._stream()))
     ref32 = sum(route[perm[i]] * (G.dequantize(m, type_name, (rows, k)) @ xs[i]) for i, m in enumerate(mats))
-    assert rel_l2(y32.cpu().numpy(), ref32) < TOL_F32
+    assert rel_l2(y32.cpu().numpy(), ref32) < TOL_GEMV
     ctx.check_device()
 
 

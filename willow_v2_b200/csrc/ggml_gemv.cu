@@ -9,9 +9,11 @@
 //
 // A CTA owns a tile of consecutive rows of one matrix: those rows are one contiguous byte range, staged into shared
 // memory by 16-byte cp.async copies (the unaligned head and tail by 16-bit copies), so HBM sees full coalesced
-// sectors whatever the block size. Warps then decode from shared memory: a row is spread over L lanes (L = the
-// row's 32-value chunks, at most 32), so short rows (k = 512: 16 chunks) still keep every lane busy. The chunk
-// decoders are in ggml_types.cuh; the codebooks (generated from gguf-py at build time) are copied to shared memory.
+// sectors whatever the block size. While the copies are in flight the CTA quantises its activations into shared
+// memory (int16, a power-of-two scale per 32 values). Warps then take the rows from shared memory: a row is spread
+// over L lanes (L = the row's 32-value chunks, 8 to 32), each chunk becomes 8 words of int8 weights (ggml_types.cuh
+// int_words) and two dp2a instructions cover 4 weights. The dequant kernel uses the float decoders instead, which
+// are bit-identical to willow's. The codebooks (generated from gguf-py at build time) are copied to shared memory.
 #include <algorithm>
 #include <type_traits>
 
@@ -80,6 +82,120 @@ __device__ __forceinline__ GgmlTables load_tables(uint8_t* tab) {
   return tb;
 }
 
+// The integer kernels' tables: IQ4 levels as int8 bytes, the grids as for the float decoders.
+template <int T>
+__device__ __forceinline__ void stage_int_tables(uint8_t* tab) {
+  if constexpr (T == kGgmlIQ4NL || T == kGgmlIQ4XS) {
+    if (threadIdx.x < 16) tab[threadIdx.x] = uint8_t(kIq4nlLevels[threadIdx.x]);
+  } else {
+    load_tables<T>(tab);
+  }
+}
+
+template <int T>
+__device__ __forceinline__ IntTables int_tables(const uint8_t* tab) {  // after the barrier that follows staging
+  IntTables it{0, 0, 0, 0, nullptr, nullptr};
+  if constexpr (T == kGgmlIQ4NL || T == kGgmlIQ4XS) {
+    const uint32_t* lv = reinterpret_cast<const uint32_t*>(tab);
+    it.lv0 = lv[0];
+    it.lv1 = lv[1];
+    it.lv2 = lv[2];
+    it.lv3 = lv[3];
+  } else if constexpr (T == kGgmlIQ3XXS || T == kGgmlIQ3S) {
+    it.grid32 = reinterpret_cast<const uint32_t*>(tab);
+  } else if constexpr (T == kGgmlIQ2S) {
+    it.grid64 = reinterpret_cast<const uint2*>(tab);
+  }
+  return it;
+}
+
+// Activations in shared memory: n rows of k values as int16 with one power-of-two scale per 32 values and the sums
+// of the int16 values per 16. A chunk's 64 bytes are stored as 4 quarters of 16 bytes, quarter-major
+// ([n][4][chunks] of 16 bytes), so the lanes of a warp, which read consecutive chunks, read consecutive 16-byte
+// words (no bank conflicts). Region sizes, each rounded up to 16 bytes.
+struct XQ {
+  uint4* q;      // [n][4][k / 32]
+  float* scale;  // [n, k / 32]
+  int* sum16;    // [n, k / 16]
+};
+
+__host__ __device__ constexpr size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+__host__ __device__ constexpr size_t xq_bytes(int n, int k) {
+  return align16(size_t(n) * k * 2) + align16(size_t(n) * (k / 32) * 4) + align16(size_t(n) * (k / 16) * 4);
+}
+// the combine's per-matrix addresses and routing weights, and a flag
+__host__ __device__ constexpr size_t combine_meta_bytes(int n) { return align16(size_t(n) * 12 + 4); }
+
+__device__ __forceinline__ XQ xq_view(uint8_t* p, int n, int k) {
+  XQ v;
+  v.q = reinterpret_cast<uint4*>(p);
+  v.scale = reinterpret_cast<float*>(p + align16(size_t(n) * k * 2));
+  v.sum16 = reinterpret_cast<int*>(p + align16(size_t(n) * k * 2) + align16(size_t(n) * (k / 32) * 4));
+  return v;
+}
+
+// Quantises x [n, k] (f32 or bf16, global) into xq: 8 lanes per 32-value block, 4 values per lane. The scale of a
+// block is 2^(E - 14) for its largest magnitude m = f * 2^E (f in [0.5, 1)), so |q| < 2^14 and every value within
+// 2^6 of m that a bf16 can hold is exact; blocks with m below 2^-107 are zero.
+__device__ __forceinline__ void quantize_x(const void* x, int x_dtype, int n, int k, XQ xq) {
+  const int nblk = n * (k / 32);
+  const int sub = threadIdx.x % 8, group = threadIdx.x / 8, groups = blockDim.x / 8;
+  for (int b0 = 0; b0 < nblk; b0 += groups) {  // the bound is uniform across each warp: shuffles stay converged
+    const int b = b0 + group;
+    const bool on = b < nblk;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (on) {
+      const size_t at = size_t(b) * 32 + 4 * sub;
+      if (x_dtype == kF32) {
+        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + at);
+        v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+      } else {
+        const uint2 h = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + at);
+        v[0] = __uint_as_float(h.x << 16), v[1] = __uint_as_float(h.x & 0xFFFF0000u);
+        v[2] = __uint_as_float(h.y << 16), v[3] = __uint_as_float(h.y & 0xFFFF0000u);
+      }
+    }
+    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    const int eb = int(__float_as_uint(m) >> 23);  // biased exponent; m = 1.f * 2^(eb - 127)
+    const bool zero = eb < 20;
+    const float inv = zero ? 0.f : __uint_as_float(uint32_t(267 - eb) << 23);  // 2^(140 - eb)
+    int q[4], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[i] = __float2int_rn(v[i] * inv);
+      sum += q[i];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (on) {
+      const uint2 packed = make_uint2((uint32_t(q[0]) & 0xFFFFu) | (uint32_t(q[1]) << 16),
+                                      (uint32_t(q[2]) & 0xFFFFu) | (uint32_t(q[3]) << 16));
+      const int chunks = k / 32, r = b / chunks, c = b % chunks;
+      reinterpret_cast<uint2*>(xq.q + (size_t(r) * 4 + sub / 2) * chunks + c)[sub % 2] = packed;
+      if (sub == 0) xq.scale[b] = zero ? 0.f : __uint_as_float(uint32_t(eb - 13) << 23);  // 2^(eb - 140)
+      if (sub % 4 == 0) xq.sum16[2 * b + sub / 4] = sum;
+    }
+  }
+}
+
+// the 32 int16 activations of chunk c of row r, their scale and half sums
+__device__ __forceinline__ float chunk_x(const XQ& xq, int k, int r, int c, uint32_t (&xw)[16], int& s0, int& s1) {
+  const int chunks = k / 32;
+  const uint4* p = xq.q + size_t(r) * 4 * chunks + c;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 u = p[i * chunks];
+    xw[4 * i] = u.x, xw[4 * i + 1] = u.y, xw[4 * i + 2] = u.z, xw[4 * i + 3] = u.w;
+  }
+  const int blk = r * (k / 32) + c;
+  s0 = xq.sum16[2 * blk];
+  s1 = xq.sum16[2 * blk + 1];
+  return xq.scale[blk];
+}
+
 template <typename OutT>
 __device__ __forceinline__ OutT to_out(float v);
 template <>
@@ -90,35 +206,6 @@ template <>
 __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
 
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-
-// 32 activations of token row xt (f32 or bf16) starting at element 32 * c, dotted with v
-__device__ __forceinline__ float dot32(const float (&v)[32], const void* x, int x_dtype, size_t off) {
-  float s = 0.f;
-  if (x_dtype == kF32) {
-    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 q = __ldg(p + i);
-      s = fmaf(v[4 * i], q.x, s);
-      s = fmaf(v[4 * i + 1], q.y, s);
-      s = fmaf(v[4 * i + 2], q.z, s);
-      s = fmaf(v[4 * i + 3], q.w, s);
-    }
-  } else {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + off);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 q = __ldg(p + i);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        s = fmaf(v[8 * i + 2 * j], __uint_as_float(w[j] << 16), s);
-        s = fmaf(v[8 * i + 2 * j + 1], __uint_as_float(w[j] & 0xFFFF0000u), s);
-      }
-    }
-  }
-  return s;
-}
 
 // sum over the L lanes of a row group (L a power of two, groups aligned to L)
 template <int L>
@@ -162,12 +249,14 @@ struct GemvArgs {
   int* status;
 };
 
-// L lanes per row, MAXT token accumulators
+// L lanes per row, MAXT token accumulators. Shared memory: the type's table, the quantised activations, then the
+// staged rows of the tile.
 template <int T, int L, int MAXT>
 __global__ void __launch_bounds__(kThreads) ggml_gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const GgmlTables tb = load_tables<T>(smem);
-  uint8_t* stage = smem + ((table_bytes(T) + 15) & ~15);
+  uint8_t* tab = smem;
+  const XQ xq = xq_view(smem + align16(table_bytes(T)), a.tokens, a.k);
+  uint8_t* stage = smem + align16(table_bytes(T)) + xq_bytes(a.tokens, a.k);
   const int i = blockIdx.y, r0 = blockIdx.x * a.tile_rows;
   const int nr = min(a.tile_rows, a.rows - r0);
   const uint8_t* mat = a.weights ? a.weights[i] : a.single;
@@ -180,9 +269,12 @@ __global__ void __launch_bounds__(kThreads) ggml_gemv_kernel(GemvArgs a) {
   const int pos = int(pos64);
   const uint8_t* src = mat + size_t(r0) * a.row_bytes;
   uint8_t* base = stage + (reinterpret_cast<uintptr_t>(src) & 15);
-  stage_bytes(base, src, size_t(nr) * a.row_bytes);
+  stage_bytes(base, src, size_t(nr) * a.row_bytes);  // in flight while x is quantised
+  stage_int_tables<T>(tab);
+  quantize_x(a.x, a.x_dtype, a.tokens, a.k, xq);
   cp_async_wait_all();
   __syncthreads();
+  const IntTables it = int_tables<T>(tab);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   constexpr int kRowsPerWarp = 32 / L;
   const int chunks = a.k / 32;
@@ -194,11 +286,18 @@ __global__ void __launch_bounds__(kThreads) ggml_gemv_kernel(GemvArgs a) {
     for (int t = 0; t < MAXT; ++t) acc[t] = 0.f;
     if (valid) {
       for (int c = lane % L; c < chunks; c += L) {
-        float v[32];
-        decode_row_chunk<T>(row, c, tb, v);
+        uint32_t w[8];
+        ChunkScale cs;
+        int_row_words<T>(row, c, it, w, cs);
 #pragma unroll
-        for (int t = 0; t < MAXT; ++t)
-          if (t < a.tokens) acc[t] += dot32(v, a.x, a.x_dtype, size_t(t) * a.k + 32 * size_t(c));
+        for (int t = 0; t < MAXT; ++t) {
+          if (t < a.tokens) {
+            uint32_t xw[16];
+            int s0, s1;
+            const float xs = chunk_x(xq, a.k, t, c, xw, s0, s1);
+            acc[t] += chunk_apply(w, cs, xw, xs, s0, s1);
+          }
+        }
       }
     }
 #pragma unroll
@@ -231,51 +330,72 @@ struct CombineArgs {
 };
 
 // One CTA (kCombineThreads) per tile of rows_per_pass rows (each group of L lanes owns one row), all matrices of a
-// group staged at once, then summed in order.
+// group staged at once, then summed in order. Shared memory: table, the n quantised input rows, the stage.
 template <int T, int L>
 __global__ void __launch_bounds__(kCombineThreads) ggml_combine_kernel(CombineArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const GgmlTables tb = load_tables<T>(smem);
-  uint8_t* stage = smem + ((table_bytes(T) + 15) & ~15);
+  uint8_t* tab = smem;
+  const XQ xq = xq_view(smem + align16(table_bytes(T)), a.n, a.k);
+  // the matrices' addresses, routing weights and a bad-entry flag, read from global memory once, in parallel
+  const uint8_t** mats = reinterpret_cast<const uint8_t**>(smem + align16(table_bytes(T)) + xq_bytes(a.n, a.k));
+  float* rws = reinterpret_cast<float*>(mats + a.n);
+  int* bad = reinterpret_cast<int*>(rws + a.n);
+  uint8_t* stage = smem + align16(table_bytes(T)) + xq_bytes(a.n, a.k) + combine_meta_bytes(a.n);
   const int r0 = blockIdx.x * a.tile_rows, nr = min(a.tile_rows, a.rows - r0);
   const size_t tile_bytes = size_t(nr) * a.row_bytes;
-  const size_t slot = ((size_t(a.tile_rows) * a.row_bytes + 15) & ~size_t(15)) + 16;
+  const size_t slot = align16(size_t(a.tile_rows) * a.row_bytes) + 16;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int rr = warp * (32 / L) + lane / L;  // this lane group's row of the tile
   const bool valid = rr < nr;
   const int chunks = a.k / 32;
-  // a routing index out of range or an odd matrix address: flag it and touch nothing (uniform over the CTA)
-  for (int e = 0; e < a.n; ++e) {
+  if (threadIdx.x == 0) *bad = 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < a.n; e += blockDim.x) {
     const int64_t pe = a.perm[e];
-    if (pe < 0 || pe >= a.n_route || (reinterpret_cast<uintptr_t>(a.weights[e]) & 1)) {
-      if (threadIdx.x == 0) atomicCAS(a.status, kStatusOk, kStatusBadExpert);
-      return;
+    const uint8_t* w = a.weights[e];
+    mats[e] = w;
+    if (pe < 0 || pe >= a.n_route || (reinterpret_cast<uintptr_t>(w) & 1)) {
+      *bad = 1;
+      rws[e] = 0.f;
+    } else {
+      rws[e] = a.dtype == kF32 ? static_cast<const float*>(a.route_w)[pe]
+                               : __bfloat162float(static_cast<const __nv_bfloat16*>(a.route_w)[pe]);
     }
   }
+  __syncthreads();
+  // a routing index out of range or an odd matrix address: flag it and touch nothing (uniform over the CTA)
+  if (*bad) {
+    if (threadIdx.x == 0) atomicCAS(a.status, kStatusOk, kStatusBadExpert);
+    return;
+  }
+  stage_int_tables<T>(tab);
   float total = 0.f;
   for (int g0 = 0; g0 < a.n; g0 += a.group) {
     const int gn = min(a.group, a.n - g0);
     __syncthreads();  // the previous group's reads of the stage are done
     for (int m = 0; m < gn; ++m) {
-      const uint8_t* src = a.weights[g0 + m] + size_t(r0) * a.row_bytes;
+      const uint8_t* src = mats[g0 + m] + size_t(r0) * a.row_bytes;
       stage_bytes(stage + m * slot + (reinterpret_cast<uintptr_t>(src) & 15), src, tile_bytes);
     }
+    if (g0 == 0) quantize_x(a.x, a.dtype, a.n, a.k, xq);  // while the first group's copies are in flight
     cp_async_wait_all();
     __syncthreads();
+    const IntTables it = int_tables<T>(tab);
     for (int m = 0; m < gn; ++m) {
       const int e = g0 + m;
-      const int64_t pe = a.perm[e];
-      const float rw = a.dtype == kF32 ? static_cast<const float*>(a.route_w)[pe]
-                                       : __bfloat162float(static_cast<const __nv_bfloat16*>(a.route_w)[pe]);
-      const uint8_t* src = a.weights[e] + size_t(r0) * a.row_bytes;
+      const float rw = rws[e];
+      const uint8_t* src = mats[e] + size_t(r0) * a.row_bytes;
       const uint8_t* row = stage + m * slot + (reinterpret_cast<uintptr_t>(src) & 15) +
                            size_t(valid ? rr : 0) * a.row_bytes;
       float acc = 0.f;
       if (valid) {
         for (int c = lane % L; c < chunks; c += L) {
-          float v[32];
-          decode_row_chunk<T>(row, c, tb, v);
-          acc += dot32(v, a.x, a.dtype, size_t(e) * a.k + 32 * size_t(c));
+          uint32_t w[8], xw[16];
+          ChunkScale cs;
+          int s0, s1;
+          int_row_words<T>(row, c, it, w, cs);
+          const float xs = chunk_x(xq, a.k, e, c, xw, s0, s1);
+          acc += chunk_apply(w, cs, xw, xs, s0, s1);
         }
       }
       const float p = group_sum<L>(acc);
@@ -378,7 +498,7 @@ cudaError_t ggml_gemv(int type, const uint8_t* const* weights, const uint8_t* si
   GemvArgs a{weights, single, positions, n, n_out, rows, k, tokens, 0, rb, x, x_dtype, y, y_dtype, status};
   a.tile_rows = int(std::max<size_t>(1, std::min<size_t>(std::min<size_t>(size_t(rows), kGemvTileRows),
                                                          kStageBudget / rb)));
-  const size_t smem = size_t((table_bytes(type) + 15) & ~15) + size_t(a.tile_rows) * rb + 16;
+  const size_t smem = align16(table_bytes(type)) + xq_bytes(tokens, k) + size_t(a.tile_rows) * rb + 16;
   if (smem > kMaxSmem) return cudaErrorInvalidValue;
   const dim3 grid(unsigned((rows + a.tile_rows - 1) / a.tile_rows), unsigned(n));
   const int lanes = lanes_for(k / 32);
@@ -408,8 +528,8 @@ cudaError_t ggml_combine(int type, const uint8_t* const* weights, const int64_t*
   const int rows_per_pass = kCombineThreads / 32 * (32 / lanes);  // one row per lane group: the tile is one pass
   CombineArgs a{weights, perm, n, n_route, rows, k, 0, 0, rb, x, route_w, dtype, y, status};
   a.tile_rows = std::min(rows, rows_per_pass);
-  const size_t slot = ((size_t(a.tile_rows) * rb + 15) & ~size_t(15)) + 16;
-  const size_t tab = size_t((table_bytes(type) + 15) & ~15);
+  const size_t slot = align16(size_t(a.tile_rows) * rb) + 16;
+  const size_t tab = align16(table_bytes(type)) + xq_bytes(n, k) + combine_meta_bytes(n);
   if (tab + slot > kMaxSmem) return cudaErrorInvalidValue;
   a.group = int(std::min<size_t>(size_t(n), (kMaxSmem - tab) / slot));
   a.group = std::min(a.group, int(std::max<size_t>(1, (96 * 1024) / slot)));  // keep a few CTAs per SM

@@ -246,6 +246,241 @@ __device__ __forceinline__ void decode_chunk<kGgmlQ6K>(const uint8_t* b, int c, 
   }
 }
 
+// ------------------------------------------------------------------------------------------------ integer form
+// The typed GEMV kernels take a chunk as 8 words of 4 signed int8 weights (word i = values 4i .. 4i+3) and its
+// scales: chunk . x = xs * (s0 * acc0 + s1 * acc1 - m0 * xsum0 - m1 * xsum1), where x ~ xs * xq (int16, one
+// power-of-two scale per 32 values), acc0 / acc1 = the integer dot products of words 0-3 / 4-7 with xq, and
+// xsum0 / xsum1 = the sums of xq over values 0-15 / 16-31 (offsets and mins: Q5_0 q - 16, Q2_0 q - 1, Q6_K q - 32,
+// Q4_K's dmin * mn). Products of small integers are exact, so the only differences from the float path are the
+// rounding of x to int16 (exact for bf16 values within 2^6 of their block's maximum) and the summation order.
+
+struct ChunkScale {
+  float s0, s1, m0, m1;
+};
+
+struct IntTables {
+  uint32_t lv0, lv1, lv2, lv3;  // IQ4_NL / IQ4_XS: the 16 int8 levels, 4 per word
+  const uint32_t* grid32;       // IQ3_XXS / IQ3_S
+  const uint2* grid64;          // IQ2_S
+};
+
+__device__ __forceinline__ int dp2a_lo_s(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp2a_hi_s(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// bit i of a 4-bit value -> byte i of the result (0 or 1)
+__device__ __forceinline__ uint32_t spread4(uint32_t b) { return (b * 0x00204081u) & 0x01010101u; }
+
+// bytes of g (each 1..127) negated where the matching bit of the 4-bit s is set: (g ^ 0xFF) + 1 per byte, which
+// carries into no neighbour because no byte is 0
+__device__ __forceinline__ uint32_t with_signs(uint32_t g, uint32_t s) {
+  const uint32_t one = spread4(s);
+  return (g ^ (one * 0xFFu)) + one;
+}
+
+// the IQ4 level of each of 4 nibbles (one per byte of nb) as int8 bytes, by byte permutes of the 16-level table
+__device__ __forceinline__ uint32_t iq4_levels(uint32_t nb, const IntTables& it) {
+  const uint32_t t = nb | (nb >> 4);
+  const uint32_t sel = __byte_perm(t, 0, 0x4420);  // n0 | n1 << 4 | n2 << 8 | n3 << 12
+  const uint32_t lo = __byte_perm(it.lv0, it.lv1, sel & 0x7777), hi = __byte_perm(it.lv2, it.lv3, sel & 0x7777);
+  const uint32_t m = spread4((nb >> 3) & 1 | (nb >> 10) & 2 | (nb >> 17) & 4 | (nb >> 24) & 8) * 0xFFu;
+  return (lo & ~m) | (hi & m);
+}
+
+template <int T>
+__device__ __forceinline__ void int_words(const uint8_t* b, int c, const IntTables& it, uint32_t (&w)[8],
+                                          ChunkScale& cs);
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlQ5_0>(const uint8_t* b, int, const IntTables&, uint32_t (&w)[8],
+                                                     ChunkScale& cs) {
+  const float d = half_at(b, 0);
+  const uint32_t qh = rd32(b, 2);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t q = rd32(b, 6 + 4 * i);
+    w[i] = (q & 0x0F0F0F0Fu) | (spread4((qh >> (4 * i)) & 0xF) << 4);
+    w[i + 4] = ((q >> 4) & 0x0F0F0F0Fu) | (spread4((qh >> (16 + 4 * i)) & 0xF) << 4);
+  }
+  cs = {d, d, 16.f * d, 16.f * d};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlQ8_0>(const uint8_t* b, int, const IntTables&, uint32_t (&w)[8],
+                                                     ChunkScale& cs) {
+  const float d = half_at(b, 0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = rd32(b, 2 + 4 * i);
+  cs = {d, d, 0.f, 0.f};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlIQ4NL>(const uint8_t* b, int, const IntTables& it, uint32_t (&w)[8],
+                                                      ChunkScale& cs) {
+  const float d = half_at(b, 0);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t q = rd32(b, 2 + 4 * i);
+    w[i] = iq4_levels(q & 0x0F0F0F0Fu, it);
+    w[i + 4] = iq4_levels((q >> 4) & 0x0F0F0F0Fu, it);
+  }
+  cs = {d, d, 0.f, 0.f};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlIQ4XS>(const uint8_t* b, int c, const IntTables& it, uint32_t (&w)[8],
+                                                      ChunkScale& cs) {
+  const float d = half_at(b, 0);
+  const uint32_t high = (rd16(b, 2) >> (2 * c)) & 3;
+  const uint32_t low = (rd16(b, 4 + 2 * (c / 4)) >> (4 * (c % 4))) & 0xF;
+  const float dl = __fmul_rn(d, float(int(low | (high << 4)) - 32));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t q = rd32(b, 8 + 16 * c + 4 * i);
+    w[i] = iq4_levels(q & 0x0F0F0F0Fu, it);
+    w[i + 4] = iq4_levels((q >> 4) & 0x0F0F0F0Fu, it);
+  }
+  cs = {dl, dl, 0.f, 0.f};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlIQ3XXS>(const uint8_t* b, int c, const IntTables& it,
+                                                       uint32_t (&w)[8], ChunkScale& cs) {
+  const float d = half_at(b, 0);
+  const uint32_t aux = rd32(b, 66 + 4 * c);
+  const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, float(aux >> 28))), 0.5f);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t two = rd16(b, 2 + 8 * c + 2 * l);
+    const uint32_t s = ksigns((aux >> (7 * l)) & 0x7F);
+    w[2 * l] = with_signs(it.grid32[two & 0xFF], s & 0xF);
+    w[2 * l + 1] = with_signs(it.grid32[two >> 8], s >> 4);
+  }
+  cs = {db, db, 0.f, 0.f};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlIQ2S>(const uint8_t* b, int c, const IntTables& it, uint32_t (&w)[8],
+                                                     ChunkScale& cs) {
+  const float d = half_at(b, 0);
+  const uint32_t qs = rd32(b, 2 + 4 * c), sg = rd32(b, 34 + 4 * c);
+  const uint32_t qh = (rd16(b, 66 + 2 * (c / 2)) >> (8 * (c % 2))) & 0xFF;
+  const uint32_t sc = (rd16(b, 74 + 2 * (c / 2)) >> (8 * (c % 2))) & 0xFF;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint2 g = it.grid64[((qs >> (8 * e)) & 0xFF) | (((qh >> (2 * e)) & 3) << 8)];
+    const uint32_t s = (sg >> (8 * e)) & 0xFF;
+    w[2 * e] = with_signs(g.x, s & 0xF);
+    w[2 * e + 1] = with_signs(g.y, s >> 4);
+  }
+  const float db0 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, float(sc & 0xF))), 0.25f);
+  const float db1 = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, float(sc >> 4))), 0.25f);
+  cs = {db0, db1, 0.f, 0.f};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlIQ3S>(const uint8_t* b, int c, const IntTables& it, uint32_t (&w)[8],
+                                                     ChunkScale& cs) {
+  const float d = half_at(b, 0);
+  const uint32_t qh = (rd16(b, 66 + 2 * (c / 2)) >> (8 * (c % 2))) & 0xFF;
+  const uint32_t sg = rd32(b, 74 + 4 * c);
+  const uint32_t sc = (rd16(b, 106 + 2 * (c / 4)) >> (4 * (c % 4))) & 0xF;
+  const float db = __fmul_rn(d, float(1 + 2 * int(sc)));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t two = rd16(b, 2 + 8 * c + 2 * i);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int e = 2 * i + h;
+      const uint32_t g = it.grid32[((two >> (8 * h)) & 0xFF) | (((qh >> e) & 1) << 8)];
+      w[e] = with_signs(g, (sg >> (4 * e)) & 0xF);
+    }
+  }
+  cs = {db, db, 0.f, 0.f};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlQ2_0>(const uint8_t* b, int c, const IntTables&, uint32_t (&w)[8],
+                                                     ChunkScale& cs) {
+  const float d = half_at(b, 0);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t q = rd32(b, 2 + 8 * c + 4 * h);  // values 16h .. 16h+15, 2 bits each
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t y = (q >> (8 * m)) & 0xFF;   // values 4m .. 4m+3 of this half
+      w[4 * h + m] = (y & 3) | ((y & 0xC) << 6) | ((y & 0x30) << 12) | ((y & 0xC0) << 18);
+    }
+  }
+  cs = {d, d, d, d};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlQ4K>(const uint8_t* b, int c, const IntTables&, uint32_t (&w)[8],
+                                                    ChunkScale& cs) {
+  const float d = half_at(b, 0), dmin = half_at(b, 2);
+  uint8_t s12[12];
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    const uint32_t two = rd16(b, 4 + 2 * i);
+    s12[2 * i] = uint8_t(two);
+    s12[2 * i + 1] = uint8_t(two >> 8);
+  }
+  int sc, mn;
+  q4k_scale_min(s12, c, sc, mn);
+  const float scale = __fmul_rn(d, float(sc)), m = __fmul_rn(dmin, float(mn));
+  const int shift = 4 * (c % 2);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = (rd32(b, 16 + 32 * (c / 2) + 4 * i) >> shift) & 0x0F0F0F0Fu;
+  cs = {scale, scale, m, m};
+}
+
+template <>
+__device__ __forceinline__ void int_words<kGgmlQ6K>(const uint8_t* b, int c, const IntTables&, uint32_t (&w)[8],
+                                                    ChunkScale& cs) {
+  const float d = half_at(b, 208);
+  const uint32_t sc2 = rd16(b, 192 + 2 * c);
+  const float s0 = __fmul_rn(d, float(int8_t(sc2 & 0xFF))), s1 = __fmul_rn(d, float(int8_t(sc2 >> 8)));
+  const int h = c / 4, s = c % 4, lshift = 4 * (s / 2), hshift = 2 * s;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t lo = rd32(b, 64 * h + 32 * (s % 2) + 4 * i), hi = rd32(b, 128 + 32 * h + 4 * i);
+    w[i] = ((lo >> lshift) & 0x0F0F0F0Fu) | (((hi >> hshift) & 0x03030303u) << 4);
+  }
+  cs = {s0, s1, 32.f * s0, 32.f * s1};
+}
+
+template <int T>
+__device__ __forceinline__ void int_row_words(const uint8_t* row, int c, const IntTables& it, uint32_t (&w)[8],
+                                              ChunkScale& cs) {
+  constexpr BlockGeom g = block_geom(T);
+  constexpr int per = g.elements / 32;
+  int_words<T>(row + (c / per) * g.bytes, c % per, it, w, cs);
+}
+
+// chunk . x for one token: xw = the chunk's 32 int16 activations as 16 words, xs their scale, xsum0 / xsum1 the
+// sums of values 0-15 / 16-31
+__device__ __forceinline__ float chunk_apply(const uint32_t (&w)[8], const ChunkScale& cs, const uint32_t (&xw)[16],
+                                             float xs, int xsum0, int xsum1) {
+  int a0 = 0, a1 = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a0 = dp2a_lo_s(xw[2 * i], w[i], a0);
+    a0 = dp2a_hi_s(xw[2 * i + 1], w[i], a0);
+    a1 = dp2a_lo_s(xw[8 + 2 * i], w[4 + i], a1);
+    a1 = dp2a_hi_s(xw[8 + 2 * i + 1], w[4 + i], a1);
+  }
+  const float t = cs.s0 * float(a0) + cs.s1 * float(a1) - cs.m0 * float(xsum0) - cs.m1 * float(xsum1);
+  return xs * t;
+}
+
 // Value chunk c of a row (32 values each) for any block size: block c / (elements / 32), chunk within it.
 template <int T>
 __device__ __forceinline__ void decode_row_chunk(const uint8_t* row, int c, const GgmlTables& tb, float (&v)[32]) {
