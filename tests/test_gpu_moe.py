@@ -537,7 +537,8 @@ def test_gemv_batch_matches_oracle(model):
     torch.cuda.synchronize()
     for i, e in enumerate((3, 200)):
         ref = ora.dequantize(synth.expert_gate_up(SEED, 0, e), "Q4_K", (1024, 2048)) @ x
-        assert rel_l2(y[i].cpu().numpy(), ref) < 1e-5
+        # the typed kernels take x as int16 per 32 values (2^-15 of each block's largest): 2e-4 relative L2
+        assert rel_l2(y[i].cpu().numpy(), ref) < 2e-4
 
 
 def test_device_status_clean(model):

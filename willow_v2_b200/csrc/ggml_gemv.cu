@@ -10,7 +10,7 @@
 // A CTA owns a tile of consecutive rows of one matrix: those rows are one contiguous byte range, staged into shared
 // memory by 16-byte cp.async copies (the unaligned head and tail by 16-bit copies), so HBM sees full coalesced
 // sectors whatever the block size. While the copies are in flight the CTA quantises its activations into shared
-// memory (int16, a power-of-two scale per 32 values). Warps then take the rows from shared memory: a row is spread
+// memory (int16, a power-of-two scale per 32 values, 15 bits of range). Warps then take the rows from shared memory: a row is spread
 // over L lanes (L = the row's 32-value chunks, 8 to 32), each chunk becomes 8 words of int8 weights (ggml_types.cuh
 // int_words) and two dp2a instructions cover 4 weights. The dequant kernel uses the float decoders instead, which
 // are bit-identical to willow's. The codebooks (generated from gguf-py at build time) are copied to shared memory.
@@ -135,8 +135,9 @@ __device__ __forceinline__ XQ xq_view(uint8_t* p, int n, int k) {
 }
 
 // Quantises x [n, k] (f32 or bf16, global) into xq: 8 lanes per 32-value block, 4 values per lane. The scale of a
-// block is 2^(E - 14) for its largest magnitude m = f * 2^E (f in [0.5, 1)), so |q| < 2^14 and every value within
-// 2^6 of m that a bf16 can hold is exact; blocks with m below 2^-107 are zero.
+// block is 2^(E - 15) for its largest magnitude m = f * 2^E (f in [0.5, 1)), so |q| <= 32767 (the one value that
+// rounds to 2^15 is clamped) and every value within 2^7 of m that a bf16 can hold is exact; blocks with m below
+// 2^-107 are zero. With int8 weights a chunk's dp2a sum stays below 32 * 32767 * 127 < 2^31.
 __device__ __forceinline__ void quantize_x(const void* x, int x_dtype, int n, int k, XQ xq) {
   const int nblk = n * (k / 32);
   const int sub = threadIdx.x % 8, group = threadIdx.x / 8, groups = blockDim.x / 8;
@@ -161,11 +162,11 @@ __device__ __forceinline__ void quantize_x(const void* x, int x_dtype, int n, in
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
     const int eb = int(__float_as_uint(m) >> 23);  // biased exponent; m = 1.f * 2^(eb - 127)
     const bool zero = eb < 20;
-    const float inv = zero ? 0.f : __uint_as_float(uint32_t(267 - eb) << 23);  // 2^(140 - eb)
+    const float inv = zero ? 0.f : __uint_as_float(uint32_t(268 - eb) << 23);  // 2^(141 - eb)
     int q[4], sum = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      q[i] = __float2int_rn(v[i] * inv);
+      q[i] = max(-32767, min(32767, __float2int_rn(v[i] * inv)));
       sum += q[i];
     }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
@@ -175,7 +176,7 @@ __device__ __forceinline__ void quantize_x(const void* x, int x_dtype, int n, in
                                       (uint32_t(q[2]) & 0xFFFFu) | (uint32_t(q[3]) << 16));
       const int chunks = k / 32, r = b / chunks, c = b % chunks;
       reinterpret_cast<uint2*>(xq.q + (size_t(r) * 4 + sub / 2) * chunks + c)[sub % 2] = packed;
-      if (sub == 0) xq.scale[b] = zero ? 0.f : __uint_as_float(uint32_t(eb - 13) << 23);  // 2^(eb - 140)
+      if (sub == 0) xq.scale[b] = zero ? 0.f : __uint_as_float(uint32_t(eb - 14) << 23);  // 2^(eb - 141)
       if (sub % 4 == 0) xq.sum16[2 * b + sub / 4] = sum;
     }
   }

@@ -252,7 +252,7 @@ __device__ __forceinline__ void decode_chunk<kGgmlQ6K>(const uint8_t* b, int c, 
 // power-of-two scale per 32 values), acc0 / acc1 = the integer dot products of words 0-3 / 4-7 with xq, and
 // xsum0 / xsum1 = the sums of xq over values 0-15 / 16-31 (offsets and mins: Q5_0 q - 16, Q2_0 q - 1, Q6_K q - 32,
 // Q4_K's dmin * mn). Products of small integers are exact, so the only differences from the float path are the
-// rounding of x to int16 (exact for bf16 values within 2^6 of their block's maximum) and the summation order.
+// rounding of x to int16 (exact for bf16 values within 2^7 of their block's maximum) and the summation order.
 
 struct ChunkScale {
   float s0, s1, m0, m1;
