@@ -77,6 +77,39 @@ def test_unsupported_types_are_refused_without_a_gpu():
     assert lib.wmoe_gemv_combine(None, 8, None, None, 1, 1, 1, 256, None, None, 1, None, None) == ERR_INVALID
 
 
+def test_wrappers_refuse_bad_arguments_without_a_gpu():
+    """The Python mirror of gguf/metal.py checks its arguments before any CUDA call: host tensors, too many tokens,
+    short buffers, offsets, positions and perm entries outside their arrays."""
+    import torch
+    from willow_v2_b200 import ggml
+    raw = torch.zeros(64 * ggml.row_bytes("Q8_0", 256), dtype=torch.uint8)
+    x = torch.zeros(1, 256, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ggml.gemv(raw, "Q8_0", (64, 256), x)
+    with pytest.raises(ValueError, match="1..8 tokens"):
+        ggml.gemv(raw, "Q8_0", (64, 256), torch.zeros(9, 256))
+    with pytest.raises(ValueError, match="fewer bytes"):
+        ggml.gemv(raw[:100], "Q8_0", (64, 256), x)
+    out = torch.zeros(2, 64)
+    with pytest.raises(ValueError, match="one position per offset"):
+        ggml.gemv_batch(raw, "Q8_0", (64, 256), x, [0], [0, 1], out)
+    with pytest.raises(ValueError, match="outside base"):
+        ggml.gemv_batch(raw, "Q8_0", (64, 256), x, [2], [0], out)
+    with pytest.raises(ValueError, match="position outside out"):
+        ggml.gemv_batch(raw, "Q8_0", (64, 256), x, [0], [2], out)
+    with pytest.raises(ValueError, match="CUDA"):
+        ggml.gemv_batch(raw, "Q8_0", (64, 256), x, [0], [1], out)
+    w = torch.ones(4, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="at least one"):
+        ggml.gemv_combine(raw, "Q8_0", (64, 256), x, [], w, [])
+    with pytest.raises(ValueError, match="perm entry outside"):
+        ggml.gemv_combine(raw, "Q8_0", (64, 256), x, [0], w, [4])
+    with pytest.raises(ValueError, match="CUDA"):
+        ggml.dequantize_gpu(raw, "Q8_0", (64, 256))
+    with pytest.raises(NotImplementedError, match="Q4_0"):
+        ggml.dequantize_gpu(raw, "Q4_0", (64, 256))
+
+
 def test_combine_oracle_rounds_like_torch_bf16():
     """The oracle's bf16 combine agrees with the same steps done in torch bf16 (engines/base.py:431-443)."""
     import torch

@@ -80,7 +80,6 @@ def row_bytes(type_name: str, k: int) -> int:
 def dequantize_gpu(raw: torch.Tensor, type_name: str, shape: tuple, dtype: torch.dtype = torch.bfloat16,
                    ctx=None) -> torch.Tensor:
     """raw (uint8, on the GPU) -> dtype [shape] on the GPU; float32 bit-identical to gguf/quants.py:dequantize."""
-    ctx = ctx or _ctx()
     gtype = _type_id(type_name)
     elements, size = BLOCKS[type_name]
     _on_gpu(raw)
@@ -92,6 +91,7 @@ def dequantize_gpu(raw: torch.Tensor, type_name: str, shape: tuple, dtype: torch
     if nblocks * size != raw.numel() or nblocks * elements != numel:
         raise ValueError(f"{raw.numel()} bytes of {type_name} do not hold a tensor of shape {tuple(shape)}")
     out = torch.empty(tuple(shape), dtype=dtype, device=raw.device)
+    ctx = ctx or _ctx()
     check(ctx.handle, lib.wmoe_dequant(ctx.handle, gtype, _p(raw), nblocks, _p(out), _DTYPES[dtype], _stream()))
     return out
 
@@ -99,7 +99,6 @@ def dequantize_gpu(raw: torch.Tensor, type_name: str, shape: tuple, dtype: torch
 def gemv(raw: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
          ctx=None) -> torch.Tensor:
     """raw: the weight's bytes (uint8, on the GPU); x: [tokens <= MAX_TOKENS, k] -> out_dtype [tokens, rows]."""
-    ctx = ctx or _ctx()
     rows, k = shape
     x = _act(x.reshape(-1, k))
     if not 1 <= x.shape[0] <= MAX_TOKENS:
@@ -108,6 +107,7 @@ def gemv(raw: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor, out_d
         raise ValueError("raw holds fewer bytes than the [rows, k] matrix")
     _on_gpu(raw, x)
     y = torch.empty(x.shape[0], rows, dtype=out_dtype, device=raw.device)
+    ctx = ctx or _ctx()
     check(ctx.handle, lib.wmoe_gemv(ctx.handle, _type_id(type_name), _p(raw), rows, k, _p(x), _DTYPES[x.dtype],
                                     x.shape[0], _p(y), _DTYPES[out_dtype], _stream()))
     return y
@@ -117,7 +117,6 @@ def gemv_batch(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor
                out: torch.Tensor, ctx=None):
     """Several experts' weights, all [rows, k] of type_name at byte offsets in base (uint8, on the GPU), times one
     token x ([1, k] or [k]): writes expert i's result to row positions[i] of out ([n, rows], bf16 or f32)."""
-    ctx = ctx or _ctx()
     rows, k = shape
     if len(offsets) != len(positions):
         raise ValueError("one position per offset")
@@ -134,6 +133,7 @@ def gemv_batch(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor
     _on_gpu(base, x, out)
     ptrs = _pointers(base, offsets)
     pos = torch.tensor(list(positions), dtype=torch.int64).to(base.device)
+    ctx = ctx or _ctx()
     check(ctx.handle, lib.wmoe_gemv_batch(ctx.handle, _type_id(type_name), _p(ptrs), _p(pos), len(offsets),
                                           out.shape[0], rows, k, _p(x), _DTYPES[x.dtype], _p(out),
                                           _DTYPES[out.dtype], _stream()))
@@ -144,7 +144,6 @@ def gemv_combine(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tens
     """sum over i of weights[perm[i]] * (W_i x[i]), in order of i, rounded to bf16 at each step like torch's bf16
     ops. W_i: [rows, k] of type_name at byte offsets[i] in base; x: bf16 [n, k]; weights: bf16 [top_k], on the GPU.
     -> bf16 [1, rows]."""
-    ctx = ctx or _ctx()
     rows, k = shape
     n = len(offsets)
     if n == 0 or len(perm) != n:
@@ -161,6 +160,7 @@ def gemv_combine(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tens
     ptrs = _pointers(base, offsets)
     pm = torch.tensor(list(perm), dtype=torch.int64).to(base.device)
     y = torch.empty(1, rows, dtype=torch.bfloat16, device=base.device)
+    ctx = ctx or _ctx()
     check(ctx.handle, lib.wmoe_gemv_combine(ctx.handle, _type_id(type_name), _p(ptrs), _p(pm), n, w.numel(), rows, k,
                                             _p(x), _p(w), _lib.BF16, _p(y), _stream()))
     return y
