@@ -649,19 +649,19 @@ cudaError_t prefill_gemms(const ExpertSource& src, int layer, const PairMap& pm,
 
   chunk_list_kernel<<<1, 512, 0, st>>>(pm, chunks, n_chunks);
   ++*launches;
-  static bool attr_set = false;  // per process: the kernels' shared memory limit does not change
-  if (!attr_set) {
-    if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  static std::atomic<uint64_t> attr_done{0};  // the kernels' shared memory limit, once per device
+  e = once_per_device(attr_done, []() -> cudaError_t {
+    cudaError_t r;
+    if ((r = cudaFuncSetAttribute(grouped_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   Layout<0>::bytes)) != cudaSuccess)
-      return e;
-    if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      return r;
+    if ((r = cudaFuncSetAttribute(grouped_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   Layout<1>::bytes)) != cudaSuccess)
-      return e;
-    if ((e = cudaFuncSetAttribute(grouped_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  Layout<2>::bytes)) != cudaSuccess)
-      return e;
-    attr_set = true;
-  }
+      return r;
+    return cudaFuncSetAttribute(grouped_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Layout<2>::bytes);
+  });
+  if (e != cudaSuccess) return e;
   const uint64_t q4_row = uint64_t(H / QK) * Q4K_BYTES;
   CUtensorMap map_x, map_h, map_w, map_ws;
   if ((e = make_tmap_f16(&map_x, xg, P, uint64_t(H))) != cudaSuccess) return e;

@@ -455,13 +455,14 @@ cudaError_t by_lanes(int lanes, F&& f) {
 constexpr size_t kStageBudget = 32 * 1024;  // staged weight bytes per CTA of the gemv kernel
 constexpr size_t kMaxSmem = 200 * 1024;
 
-// Raises a kernel's dynamic shared-memory limit to kMaxSmem once per process (the launch's own size decides what it
-// gets), so launches inside CUDA-graph capture make no attribute call.
+// Raises a kernel's dynamic shared-memory limit to kMaxSmem once per device (the launch's own size decides what it
+// gets).
 template <auto Kernel>
 cudaError_t allow_max_smem() {
-  static const cudaError_t e =
-      cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxSmem));
-  return e;
+  static std::atomic<uint64_t> done{0};
+  return once_per_device(done, []() {
+    return cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxSmem));
+  });
 }
 
 }  // namespace

@@ -4,7 +4,24 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace wmoe {
+
+// Runs set() (kernel attribute calls) once per device of this process: function attributes belong to a device's
+// context, so a process that drives several GPUs sets them on each. `done` holds one bit per device (0-63); a
+// concurrent first call on one device sets the attributes twice, which is harmless. Only cudaGetDevice runs on
+// later calls, so launches inside CUDA-graph capture make no attribute call.
+template <typename F>
+inline cudaError_t once_per_device(std::atomic<uint64_t>& done, F&& set) {
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  const cudaError_t e = set();
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 constexpr int kF32 = 0, kBF16 = 1, kF16 = 2;  // WMOE_F32/BF16/F16
 constexpr int kGgmlQ4K = 12, kGgmlQ6K = 14;

@@ -168,14 +168,11 @@ cudaError_t router_split(const float* router_w, int E, int H, void* out, cudaStr
 cudaError_t router_logits_tc(const void* x_bf16, int T, int H, int E, const void* router_split3, float* partial,
                              int* status, cudaStream_t st, int* launches) {
   if (!router_tc_supported(T, H, E)) return cudaErrorInvalidValue;
-  static bool attr_set = false;
-  cudaError_t e;
-  if (!attr_set) {
-    if ((e = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmem)) !=
-        cudaSuccess)
-      return e;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};  // the kernel's shared memory limit, once per device
+  cudaError_t e = once_per_device(attr_done, []() {
+    return cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmem);
+  });
+  if (e != cudaSuccess) return e;
   CUtensorMap mx, mw;
   if ((e = make_tmap_bf16(&mx, x_bf16, uint64_t(T), uint64_t(H), kRT)) != cudaSuccess) return e;
   if ((e = make_tmap_bf16(&mw, router_split3, uint64_t(3) * E, uint64_t(H), kRE)) != cudaSuccess) return e;
