@@ -123,6 +123,29 @@ def test_unsupported_layout_is_an_error(tmp_path):
         gguf_store.read_gguf(str(tmp_path / "x-00001-of-00003.gguf"))
 
 
+def test_truncated_files_are_errors(tmp_path):
+    """A file cut inside its header, or inside a tensor's data, raises GGUFError naming the problem."""
+    path, _ = write_model(str(tmp_path), layers=1)
+    data = open(path, "rb").read()
+    head = tmp_path / "head.gguf"
+    head.write_bytes(data[:200])
+    with pytest.raises(gguf_store.GGUFError, match="truncated or corrupt header"):
+        gguf_store.read_gguf(str(head))
+    cut = tmp_path / "cut.gguf"
+    cut.write_bytes(data[:-1000])
+    with pytest.raises(gguf_store.GGUFError, match="runs past the end"):
+        gguf_store.read_gguf(str(cut))
+
+
+def test_typed_tensors_have_sizes(tmp_path):
+    """Tensors of the typed kernels' ggml types get their byte sizes (the store still loads Q4_K / Q6_K experts
+    only, and names the first tensor of another type)."""
+    path, arrays = write_model(str(tmp_path), layers=1, down_type=Q.Q8_0)
+    _, tensors = gguf_store.read_gguf(path)
+    down = tensors["blk.0.ffn_down_exps.weight"]
+    assert down.type == "Q8_0" and down.nbytes == arrays[0]["down"].size
+
+
 @pytest.mark.gpu
 def test_gguf_model_runs_like_the_store_it_came_from(tmp_path):
     """One full-size layer (256 experts of H 2048, F 512) written to a GGUF from the synthetic store and loaded back:

@@ -25,8 +25,11 @@ import numpy as np
 GGUF_MAGIC = b"GGUF"
 DEFAULT_ALIGNMENT = 32  # when the file does not set general.alignment
 
-# ggml type ids this loader reads, with (values per block, bytes per block)
-TYPES = {0: ("F32", 1, 4), 1: ("F16", 1, 2), 12: ("Q4_K", 256, 144), 14: ("Q6_K", 256, 210), 30: ("BF16", 1, 2)}
+# ggml type ids whose sizes this loader knows, with (values per block, bytes per block) (gguf/reader.py:14-48): the
+# store's Q4_K / Q6_K, the float types of routers and gates, and the other types the typed kernels run
+TYPES = {0: ("F32", 1, 4), 1: ("F16", 1, 2), 6: ("Q5_0", 32, 22), 8: ("Q8_0", 32, 34), 12: ("Q4_K", 256, 144),
+         14: ("Q6_K", 256, 210), 18: ("IQ3_XXS", 256, 98), 20: ("IQ4_NL", 32, 18), 21: ("IQ3_S", 256, 110),
+         22: ("IQ2_S", 256, 82), 23: ("IQ4_XS", 256, 136), 30: ("BF16", 1, 2), 42: ("Q2_0", 64, 18)}
 # other ids are still parsed (the header must be walked), their sizes unknown to this loader
 _SCALARS = {0: "B", 1: "b", 2: "H", 3: "h", 4: "I", 5: "i", 6: "f", 7: "?", 10: "Q", 11: "q", 12: "d"}
 _STRING, _ARRAY = 8, 9
@@ -59,8 +62,11 @@ class GGUFError(ValueError):
 
 
 def _read_header(path: str):
+    """(metadata, {name: Tensor}) of one file. A truncated or corrupt header, or tensor data that runs past the end of
+    the file, raises GGUFError."""
     with open(path, "rb") as f:
         mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+    file_size = len(mm)
     try:
         buf = memoryview(mm)
         pos = 0
@@ -97,20 +103,23 @@ def _read_header(path: str):
         if bytes(buf[:4]) != GGUF_MAGIC:
             raise GGUFError(f"{path} is not a GGUF file")
         pos = 4
-        version, n_tensors, n_kv = take("IQQ")
-        if version < 2:
-            raise GGUFError(f"{path} is GGUF version {version}; versions 2 and 3 are supported")
-        meta = {}
-        for _ in range(n_kv):
-            key = string()
-            meta[key] = value(take("I"))
-        infos = []
-        for _ in range(n_tensors):
-            name = string()
-            n_dims = take("I")
-            ne = take(f"{n_dims}Q") if n_dims > 1 else (take("Q"),)
-            type_id, offset = take("IQ")
-            infos.append((name, tuple(reversed(ne)), type_id, offset))
+        try:
+            version, n_tensors, n_kv = take("IQQ")
+            if version < 2:
+                raise GGUFError(f"{path} is GGUF version {version}; versions 2 and 3 are supported")
+            meta = {}
+            for _ in range(n_kv):
+                key = string()
+                meta[key] = value(take("I"))
+            infos = []
+            for _ in range(n_tensors):
+                name = string()
+                n_dims = take("I")
+                ne = take(f"{n_dims}Q") if n_dims > 1 else (take("Q"),)
+                type_id, offset = take("IQ")
+                infos.append((name, tuple(reversed(ne)), type_id, offset))
+        except struct.error as e:
+            raise GGUFError(f"{path}: truncated or corrupt header ({e})") from None
         align = int(meta.get("general.alignment", DEFAULT_ALIGNMENT))
         data_start = (pos + align - 1) // align * align
     finally:
@@ -119,7 +128,10 @@ def _read_header(path: str):
     tensors = {}
     for name, shape, type_id, offset in infos:
         type_name = TYPES[type_id][0] if type_id in TYPES else f"ggml{type_id}"
-        tensors[name] = Tensor(name, path, data_start + offset, type_name, shape)
+        t = Tensor(name, path, data_start + offset, type_name, shape)
+        if type_id in TYPES and t.offset + t.nbytes > file_size:
+            raise GGUFError(f"{name}: its data runs past the end of {path} ({t.offset + t.nbytes} > {file_size} bytes)")
+        tensors[name] = t
     return meta, tensors
 
 
