@@ -13,8 +13,8 @@ from gguf import GGMLQuantizationType as Q  # noqa: E402
 
 from willow_v2_b200 import gguf_store  # noqa: E402
 
-ROW = {Q.Q4_K: 144, Q.Q6_K: 210, Q.Q8_0: 34}
-PER = {Q.Q4_K: 256, Q.Q6_K: 256, Q.Q8_0: 32}
+ROW = {Q.Q4_K: 144, Q.Q6_K: 210, Q.Q8_0: 34, Q.IQ2_S: 82, Q.IQ4_NL: 18}
+PER = {Q.Q4_K: 256, Q.Q6_K: 256, Q.Q8_0: 32, Q.IQ2_S: 256, Q.IQ4_NL: 32}
 
 
 def _quant(rng, shape, qt):
@@ -22,7 +22,8 @@ def _quant(rng, shape, qt):
     return rng.integers(0, 256, (*outer, k // PER[qt] * ROW[qt]), dtype=np.uint8)
 
 
-def write_model(folder, layers=2, E=4, F=256, H=512, fused=False, files=1, down_type=Q.Q6_K, seed=0):
+def write_model(folder, layers=2, E=4, F=256, H=512, fused=False, files=1, down_type=Q.Q6_K, seed=0,
+                gate_type=Q.Q4_K):
     """A qwen35moe GGUF (or `files` split files) with random quant bytes; returns the arrays written per layer."""
     rng = np.random.default_rng(seed)
     arrays = []
@@ -35,17 +36,17 @@ def write_model(folder, layers=2, E=4, F=256, H=512, fused=False, files=1, down_
         w = gguf.GGUFWriter(path, "qwen35moe")
         w.add_block_count(layers)
         for layer in range(f * per_file, min(layers, (f + 1) * per_file)):
-            a = dict(gate=_quant(rng, (E, F, H), Q.Q4_K), up=_quant(rng, (E, F, H), Q.Q4_K),
+            a = dict(gate=_quant(rng, (E, F, H), gate_type), up=_quant(rng, (E, F, H), gate_type),
                      down=_quant(rng, (E, H, F), down_type), router=rng.standard_normal((E, H)).astype(np.float32),
                      sgate=rng.standard_normal(H).astype(np.float32), sg=_quant(rng, (F, H), Q.Q4_K),
                      su=_quant(rng, (F, H), Q.Q4_K), sd=_quant(rng, (H, F), Q.Q6_K))
             p = f"blk.{layer}."
             if fused:
                 w.add_tensor(p + "ffn_gate_up_exps.weight", np.concatenate([a["gate"], a["up"]], axis=1),
-                             raw_dtype=Q.Q4_K)
+                             raw_dtype=gate_type)
             else:
-                w.add_tensor(p + "ffn_gate_exps.weight", a["gate"], raw_dtype=Q.Q4_K)
-                w.add_tensor(p + "ffn_up_exps.weight", a["up"], raw_dtype=Q.Q4_K)
+                w.add_tensor(p + "ffn_gate_exps.weight", a["gate"], raw_dtype=gate_type)
+                w.add_tensor(p + "ffn_up_exps.weight", a["up"], raw_dtype=gate_type)
             w.add_tensor(p + "ffn_down_exps.weight", a["down"], raw_dtype=down_type)
             w.add_tensor(p + "ffn_gate_inp.weight", a["router"])
             w.add_tensor(p + "ffn_gate_inp_shexp.weight", a["sgate"])
@@ -121,6 +122,26 @@ def test_unsupported_layout_is_an_error(tmp_path):
         gguf_store.read_gguf(str(bad))
     with pytest.raises(gguf_store.GGUFError, match="missing"):
         gguf_store.read_gguf(str(tmp_path / "x-00001-of-00003.gguf"))
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_typed_layer_views(tmp_path, fused):
+    """A layer of IQ2_S gate/up and IQ4_NL down experts read into one buffer: each expert's GGMLWeight views hold its
+    gate ‖ up rows and its down rows, at byte offsets of one base (what gemv_batch / gemv_combine take)."""
+    path, arrays = write_model(str(tmp_path), gate_type=Q.IQ2_S, down_type=Q.IQ4_NL, fused=fused)
+    tl = gguf_store.typed_layer(path, 1, device="cpu")
+    a = arrays[1]
+    assert (tl.gate_up_type, tl.down_type, tl.hidden, tl.ffn) == ("IQ2_S", "IQ4_NL", 512, 256)
+    assert tl.expert_bytes == 2 * 256 * 512 // 256 * 82 + 512 * 256 // 32 * 18
+    for e, (gu, dn) in enumerate(tl.experts):
+        assert (gu.type_name, gu.shape, dn.type_name, dn.shape) == ("IQ2_S", (512, 512), "IQ4_NL", (512, 256))
+        np.testing.assert_array_equal(gu.raw.numpy(), np.concatenate([a["gate"][e].ravel(), a["up"][e].ravel()]))
+        np.testing.assert_array_equal(dn.raw.numpy(), a["down"][e].ravel())
+        base_gu, off_gu = gu.raw._base, gu.raw.storage_offset()
+        assert base_gu is not None and base_gu.data_ptr() == tl.base.data_ptr()
+        assert off_gu == e * tl.expert_bytes and dn.raw.storage_offset() == off_gu + gu.raw.numel()
+    with pytest.raises(gguf_store.GGUFError, match="no ffn_down_exps|expected ffn_gate_exps"):
+        gguf_store.typed_layer(path, 7, device="cpu")
 
 
 def test_truncated_files_are_errors(tmp_path):

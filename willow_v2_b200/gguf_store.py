@@ -130,7 +130,8 @@ def _read_header(path: str):
         type_name = TYPES[type_id][0] if type_id in TYPES else f"ggml{type_id}"
         t = Tensor(name, path, data_start + offset, type_name, shape)
         if type_id in TYPES and t.offset + t.nbytes > file_size:
-            raise GGUFError(f"{name}: its data runs past the end of {path} ({t.offset + t.nbytes} > {file_size} bytes)")
+            raise GGUFError(f"{name}: its data runs past the end of {path} "
+                            f"({t.offset + t.nbytes} > {file_size} bytes)")
         tensors[name] = t
     return meta, tensors
 
@@ -304,7 +305,8 @@ def _float_tensor(files: _Files, t: Tensor) -> np.ndarray:
 def layer_weights(path: str, ctx=None, prepare: bool = True, tensors_of=None):
     """moe.LayerWeights for every layer: router blk.N.ffn_gate_inp.weight [E, H] and shared-expert gate
     ffn_gate_inp_shexp.weight [H] as float32, the shared expert's ffn_{gate,up}_shexp (Q4_K [F, H]) fused into
-    gate_up bytes and ffn_down_shexp ([H, F], of the layer's down type) (the names of engines/qwen36/loader.py:37-41)."""
+    gate_up bytes and ffn_down_shexp ([H, F], of the layer's down type) (the names of
+    engines/qwen36/loader.py:37-41)."""
     import torch
     from . import moe
     meta, tensors = tensors_of or read_gguf(path)
@@ -340,6 +342,79 @@ def layer_weights(path: str, ctx=None, prepare: bool = True, tensors_of=None):
     finally:
         files.close()
     return out
+
+
+# the ggml types of the typed expert kernels (willow_v2_b200/ggml.py, gguf/metal.py:295)
+TYPED = ("Q5_0", "Q8_0", "IQ4_NL", "IQ4_XS", "IQ3_XXS", "IQ3_S", "IQ2_S", "Q2_0", "Q4_K", "Q6_K")
+
+
+@dataclass
+class TypedLayer:
+    """One layer's routed experts, of any type the typed kernels run, in one uint8 buffer in the pack layout (per
+    expert: gate rows, up rows, down rows; gguf/compiler.py:69-88), and each expert's (gate_up, down) as
+    ggml.GGMLWeight views of that buffer. One buffer with byte offsets is what the batched decode kernels take
+    (gemv_batch, gemv_combine; engines/base.py:492-532), as willow's store hands out GGMLWeight views of its GPU
+    slots (gguf/store.py:425-437)."""
+    base: object                 # torch uint8 tensor [experts * expert_bytes]
+    experts: list                # [(gate_up GGMLWeight [2F, H], down GGMLWeight [H, F])] per expert
+    gate_up_type: str
+    down_type: str
+    hidden: int
+    ffn: int
+    expert_bytes: int
+
+
+def typed_layer(path: str, layer: int, device="cuda", parsed=None) -> TypedLayer:
+    """Reads one layer's ffn_{gate,up,down}_exps (or ffn_gate_up_exps) whatever their type among TYPED into one
+    buffer on `device`. Raises GGUFError naming a tensor of another type or shape."""
+    import torch
+    from .ggml import GGMLWeight
+    meta, tensors = parsed or read_gguf(path)
+    parts = {}
+    for name, t in tensors.items():
+        m = _EXPERT.match(name)
+        if m and int(m.group(1)) == layer:
+            parts[m.group(2)] = t
+    if "gate_up" in parts:
+        gu = (parts["gate_up"],)
+    elif "gate" in parts and "up" in parts:
+        gu = (parts["gate"], parts["up"])
+    else:
+        raise GGUFError(f"layer {layer}: expected ffn_gate_exps and ffn_up_exps (or ffn_gate_up_exps)")
+    if "down" not in parts:
+        raise GGUFError(f"layer {layer}: no ffn_down_exps")
+    down = parts["down"]
+    for t in (*gu, down):
+        if t.type not in TYPED or len(t.shape) != 3:
+            raise GGUFError(f"{t.name}: {t.type} {t.shape}; the typed kernels run {', '.join(TYPED)} "
+                            "[experts, rows, k]")
+    if len(gu) == 2 and (gu[0].type != gu[1].type or gu[0].shape != gu[1].shape):
+        raise GGUFError(f"layer {layer}: gate {gu[0].type} {gu[0].shape} and up {gu[1].type} {gu[1].shape} differ")
+    E, rows, H = gu[0].shape
+    F = rows // 2 if len(gu) == 1 else rows
+    if down.shape != (E, H, F):
+        raise GGUFError(f"{down.name}: shape {down.shape}, expected {(E, H, F)}")
+    if H % 32 or F % 32:
+        raise GGUFError(f"layer {layer}: hidden {H} and ffn {F} must be multiples of 32")
+    gu_b = sum(t.nbytes for t in gu) // E
+    dn_b = down.nbytes // E
+    eb = gu_b + dn_b
+    host = np.empty(E * eb, dtype=np.uint8)
+    files = _Files()
+    try:
+        for e in range(E):
+            at = e * eb
+            for t in gu:
+                per = t.nbytes // E
+                host[at:at + per] = files.view(t, e * per, per)
+                at += per
+            host[at:at + dn_b] = files.view(down, e * dn_b, dn_b)
+    finally:
+        files.close()
+    base = torch.from_numpy(host).to(device)
+    experts = [(GGMLWeight(base[e * eb:e * eb + gu_b], gu[0].type, (2 * F, H)),
+                GGMLWeight(base[e * eb + gu_b:(e + 1) * eb], down.type, (H, F))) for e in range(E)]
+    return TypedLayer(base, experts, gu[0].type, down.type, H, F, eb)
 
 
 def load(path: str, ctx=None, cap_bytes: int = 0, expert_range: Optional[Tuple[int, int]] = None):
