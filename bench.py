@@ -853,6 +853,10 @@ def run_reference(args, rank, world):
 
 
 TYPED_D_AT = {"Q6_K": 208}  # byte offset of the fp16 scale in a block (0 for the other types)
+# DRAM bytes (read + write) of one gemv_batch launch over 8 Q8_0 gate_up matrices, measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum = 17,845,760 + 0): the algorithmic 17,825,792 plus the activations
+# and addresses. The other types were not captured.
+TYPED_TRAFFIC = {"Q8_0": 17_845_760}
 
 
 def run_typed_decode(args, type_name: str):
@@ -979,8 +983,9 @@ def run_typed_decode(args, type_name: str):
                    "l2": "inputs larger than L2: each step reads 8 other experts of the >= 2 GB pool",
                    "timing": f"CUDA graphs of {G} steps replayed {reps} times; events around the replays"},
         "roofline": {"bound": "hbm", "kernel": "ggml_gemv_kernel (gemv_batch of the 8 gate_up matrices)",
-                     "achieved": gu_gbs, "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": None,
-                     "peak_kind": peak_kind, "algorithmic_bytes_per_launch": TOP_K * gu_b, "launch_ms": gu_ms},
+                     "achieved": gu_gbs, "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm,
+                     "traffic": TYPED_TRAFFIC.get(type_name), "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": TOP_K * gu_b, "launch_ms": gu_ms},
         "combine": {"kernel": "ggml_combine_kernel (8 down matrices + bf16 weighted sum)", "launch_ms": dn_ms,
                     "achieved_gbs": dn_gbs, "frac": dn_gbs / hbm},
         "roofline_step": {"achieved": step_gbs, "frac": step_gbs / hbm, "algorithmic_bytes": TOP_K * eb},
