@@ -108,6 +108,9 @@ def test_wrappers_refuse_bad_arguments_without_a_gpu():
         ggml.dequantize_gpu(raw, "Q8_0", (64, 256))
     with pytest.raises(NotImplementedError, match="Q4_0"):
         ggml.dequantize_gpu(raw, "Q4_0", (64, 256))
+    # f16 activations widen to f32 (exact) rather than rounding to bf16
+    h = torch.tensor([1.0 + 2.0 ** -10, -3.0009765625], dtype=torch.float16)
+    assert ggml._act(h).dtype == torch.float32 and torch.equal(ggml._act(h), h.float())
 
 
 def test_combine_oracle_rounds_like_torch_bf16():

@@ -49,9 +49,10 @@ def _p(t: Optional[torch.Tensor]):
 
 
 def _act(x: torch.Tensor) -> torch.Tensor:
-    """Activations as the kernels take them: bf16 or f32, contiguous (16-byte aligned rows)."""
+    """Activations as the kernels take them: bf16 or f32, contiguous (16-byte aligned rows). Other float types widen
+    to f32, which holds every f16 value exactly."""
     if x.dtype not in (torch.bfloat16, torch.float32):
-        x = x.to(torch.bfloat16)
+        x = x.to(torch.float32)
     return x.contiguous()
 
 
