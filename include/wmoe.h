@@ -323,7 +323,9 @@ int wmoe_add_rmsnorm(wmoe_ctx* ctx, const float* x, const void* y, int y_dtype, 
 /* Matrices are [rows, k] ggml blocks, rows back to back (a row is wmoe_ggml_row_bytes(type, k) bytes) at an even
  * address; k is a multiple of 32 and of the type's block. Sums are float32; x, y, route_w are f32 or bf16 (16-byte
  * aligned). An out-of-range position or perm entry, or an odd matrix address, sets the device status
- * (wmoe_device_status) and that matrix is skipped. */
+ * (wmoe_device_status) and that matrix is skipped. A CTA holds its activations (about 2.3 bytes per value: tokens x k
+ * for gemv, n x k for the combine) and a tile of rows in at most 200 KB of shared memory; calls beyond that return
+ * WMOE_ERR_UNSUPPORTED. */
 
 /* Bytes of one row of k values; 0 for a type these kernels do not run or a k that is not a whole number of blocks. */
 size_t wmoe_ggml_row_bytes(int ggml_type, int k);

@@ -1243,10 +1243,12 @@ int wmoe_gemv(wmoe_ctx* ctx, int ggml_type, const uint8_t* w, int rows, int k, c
   if (!w || !x || !y) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv: null pointer");
   if ((reinterpret_cast<uintptr_t>(w) & 1) || !aligned16(x))
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv: w must be 2-byte and x 16-byte aligned");
-  WMOE_CHECK_CUDA(ctx,
-                  ggml_gemv(ggml_type, nullptr, w, nullptr, 1, 1, rows, k, x, x_dtype, tokens, y, y_dtype,
-                            ctx->d_status, static_cast<cudaStream_t>(stream)),
-                  "wmoe_gemv");
+  const cudaError_t e = ggml_gemv(ggml_type, nullptr, w, nullptr, 1, 1, rows, k, x, x_dtype, tokens, y, y_dtype,
+                                  ctx->d_status, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv: the activations and a row tile of this k do not fit shared "
+                                               "memory");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_gemv");
   ctx->launches += 1;
   return WMOE_OK;
 }
@@ -1262,10 +1264,12 @@ int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights,
   if (n == 0 || rows == 0) return WMOE_OK;
   if (!weights || !x || !y) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: null pointer");
   if (!aligned16(x)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: x must be 16-byte aligned");
-  WMOE_CHECK_CUDA(ctx,
-                  ggml_gemv(ggml_type, weights, nullptr, positions, n, positions ? n_out : n, rows, k, x, x_dtype, 1,
-                            y, y_dtype, ctx->d_status, static_cast<cudaStream_t>(stream)),
-                  "wmoe_gemv_batch");
+  const cudaError_t e = ggml_gemv(ggml_type, weights, nullptr, positions, n, positions ? n_out : n, rows, k, x,
+                                  x_dtype, 1, y, y_dtype, ctx->d_status, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv_batch: the activations and a row tile of this k do not "
+                                               "fit shared memory");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_gemv_batch");
   ctx->launches += 1;
   return WMOE_OK;
 }
