@@ -334,28 +334,134 @@ def run_batch64(args, rank: int, world: int, dist):
     return result, (ctx, store, layers)
 
 
-def cpu_baseline_batch(sample_experts: int = 256):
-    """The oracle port for configs[2]: router on the 64 tokens, then a sample of the hit experts dequantised and run on
-    their tokens, scaled to all hit experts + the shared expert."""
+# ---------------------------------------------------------------------------------------------- CPU baseline pool
+# The CPU baseline and the reference arm run the oracle port (numpy float32) on every host core: a process pool with
+# one BLAS thread per worker, each expert's dequantisation + FFN one task, timed by the wall clock around the pool.
+# The pool is spawned (no GPU state is inherited). Dequantisation costs the same whatever the bytes are, so each
+# worker generates a few synthetic expert blobs once (untimed) and a task names one by index: the per-task IPC is
+# the activation rows only.
+N_BLOBS = 16
+_POOL = None
+_BLOBS = {}
+
+
+def cpu_baseline_pool():
+    """(pool, workers): the spawned process pool of the CPU baseline, started once per process."""
+    global _POOL
+    n = os.cpu_count() or 1
+    if _POOL is None:
+        import concurrent.futures
+        import multiprocessing
+        keys = ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")
+        saved = {k: os.environ.get(k) for k in keys}
+        os.environ.update({k: "1" for k in keys})  # inherited by the workers spawned below, not by this process
+        try:
+            _POOL = concurrent.futures.ProcessPoolExecutor(n, mp_context=multiprocessing.get_context("spawn"),
+                                                           initializer=_worker_init)
+            list(_POOL.map(_warm, range(4 * n)))  # every worker started (and its blobs made) before any timing
+        finally:
+            for k, v in saved.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
+    return _POOL, n
+
+
+def _worker_init():
+    from oracle import ggml_types as G
+    from willow_v2_b200 import synth
+    for i in range(N_BLOBS):
+        _BLOBS[("Q4_K/Q6_K", i)] = (synth.expert_gate_up(SEED, 0, i), synth.expert_down(SEED, 0, i))
+    for t in G.TYPES:  # one expert per type for the typed baseline (tasks of a type all name blob 0)
+        _typed_blob(t, 0)
+
+
+def _typed_blob(type_name: str, i: int):
+    key = (type_name, i)
+    if key not in _BLOBS:
+        from oracle import ggml_types as G
+        elements, size = G.BLOCKS[type_name]
+        rng = np.random.default_rng(SEED + i)
+        gu = rng.integers(0, 256, (2 * FFN * HIDDEN // elements, size), dtype=np.uint8)
+        dn = rng.integers(0, 256, (HIDDEN * FFN // elements, size), dtype=np.uint8)
+        d_at = TYPED_D_AT.get(type_name, 0)
+        for b in (gu, dn):
+            for off in ((d_at, 2) if type_name == "Q4_K" else (d_at,)):
+                b[:, off:off + 2] = rng.uniform(1e-3, 4e-3, b.shape[0]).astype(np.float16).view(np.uint8).reshape(-1, 2)
+        _BLOBS[key] = (gu, dn)
+    return _BLOBS[key]
+
+
+def _ffn_task(task):
+    """One expert of the oracle port: dequantise its gate_up / down blocks and run its FFN on `rows` (float32
+    [n, H]). Returns the output rows when `keep`, else their sum."""
+    kind, i, rows, keep = task
+    if kind == "Q4_K/Q6_K":
+        import oracle.moe_oracle as ora
+        gu, dn = _BLOBS[(kind, i)]
+        wg, wd = ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN)), ora.dequantize(dn, "Q6_K", (HIDDEN, FFN))
+    else:
+        from oracle import ggml_types as G
+        gu, dn = _typed_blob(kind, i)
+        wg, wd = G.dequantize(gu, kind, (2 * FFN, HIDDEN)), G.dequantize(dn, kind, (HIDDEN, FFN))
+    a = rows @ wg.T
+    g = a[:, :FFN]
+    y = (g / (1 + np.exp(-np.clip(g, -80, 80))) * a[:, FFN:]) @ wd.T
+    return y if keep else float(y.sum())
+
+
+def _warm(_):
+    return os.getpid()
+
+
+def cpu_baseline_wall(tasks):
+    """Runs the tasks on the pool; (wall seconds, results)."""
+    pool, _ = cpu_baseline_pool()
+    t0 = time.perf_counter()
+    out = list(pool.map(_ffn_task, tasks))
+    return time.perf_counter() - t0, out
+
+
+def cpu_baseline_decode_layer(x_norm, router, layer_step: int):
+    """One decode layer of the oracle port on the pool: router + top-8 in this process, the 8 routed experts and the
+    shared expert in parallel, then the combine in ascending expert id. Returns the seconds it took."""
+    import oracle.moe_oracle as ora
+    t0 = time.perf_counter()
+    w, sel = ora.route(x_norm @ router.T)
+    order = np.argsort(sel[0], kind="stable")
+    t_route = time.perf_counter() - t0
+    tasks = [("Q4_K/Q6_K", (int(sel[0, j]) + layer_step) % N_BLOBS, x_norm, True) for j in order]
+    tasks.append(("Q4_K/Q6_K", layer_step % N_BLOBS, x_norm, True))  # the shared expert
+    t_pool, ys = cpu_baseline_wall(tasks)
+    t1 = time.perf_counter()
+    out = np.zeros_like(x_norm)
+    for j, y in zip(order, ys[:-1]):
+        out += w[0, j] * y
+    out += ys[-1]  # the shared expert (its sigmoid gate is a dot product: negligible)
+    return t_route + t_pool + (time.perf_counter() - t1)
+
+
+def cpu_baseline_batch():
+    """The oracle port for configs[2] on every host core: the router on the 64 tokens, then every hit expert (and the
+    shared expert) dequantised and run on its tokens, in parallel on the pool."""
     import oracle.moe_oracle as ora
     from willow_v2_b200 import synth
+    _, workers = cpu_baseline_pool()
     x = synth.hidden(SEED, BATCH_T, step=777)
+    router = synth.router_weight(SEED, 0)
+    bias = synth.zipf_bias(SEED)
     t0 = time.perf_counter()
-    w, sel = ora.route(x @ synth.router_weight(SEED, 0).T + synth.zipf_bias(SEED))
+    w, sel = ora.route(x @ router.T + bias)
     t_route = time.perf_counter() - t0
     hit = sorted(set(int(e) for e in sel.reshape(-1)))
-    t_exp = 0.0
-    for e in hit[:sample_experts]:
-        rows = x[(sel == e).any(axis=1)]
-        gu, dn = synth.expert_gate_up(SEED, 0, e), synth.expert_down(SEED, 0, e)
-        t1 = time.perf_counter()
-        ora.expert_gate(rows @ ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN)).T) @ ora.dequantize(dn, "Q6_K", (HIDDEN, FFN)).T
-        t_exp += time.perf_counter() - t1
-    n = min(sample_experts, len(hit))
-    sec = t_route + t_exp / n * (len(hit) + 1)
-    return {"value": BATCH_T / sec, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"router on the 64 tokens; {n} of the {len(hit)} hit experts dequantised and run on their tokens "
-                      f"(numpy float32), scaled to all hit experts + the shared expert"}
+    tasks = [("Q4_K/Q6_K", e % N_BLOBS, x[(sel == e).any(axis=1)], False) for e in hit]
+    tasks.append(("Q4_K/Q6_K", 0, x, False))  # the shared expert on every token
+    t_pool, _ = cpu_baseline_wall(tasks)
+    sec = t_route + t_pool
+    return {"value": BATCH_T / sec, "unit": "tokens/s", "cores": workers, "kind": "port",
+            "sample": f"router on the 64 tokens; the {len(hit)} hit experts + the shared expert dequantised and run "
+                      f"on their tokens in parallel on {workers} worker processes (numpy float32)"}
 
 
 def run_prefill4096_ep(args, rank: int, world: int, dist):
@@ -710,64 +816,46 @@ def run_prefill4096(args, rank: int, world: int, dist):
     return result, (ctx, store, layers)
 
 
-def cpu_baseline_prefill(sample_experts: int = 128, tokens_per_expert: int = 144):
-    """willow's CPU path restated (the oracle port) for the prefill layer, timed on the host cores: the router on
-    all 4096 tokens, and for a sample of experts the dequantisation of their GGUF bytes plus their FFN on 128
-    tokens each, scaled to the 257 experts (256 routed + shared) and 36,864 (token, expert) rows of the layer."""
+def cpu_baseline_prefill(sample_experts: int = 0, tokens_per_expert: int = 144):
+    """willow's CPU path restated (the oracle port) for the prefill layer on every host core: the router on all 4096
+    tokens, then a sample of experts (default 4 per worker) dequantised with their FFN on 144 tokens each, in
+    parallel on the pool, scaled to the 257 experts (256 routed + shared) of the layer (36,864 token-expert rows)."""
     import oracle.moe_oracle as ora
     from willow_v2_b200 import synth
+    _, workers = cpu_baseline_pool()
+    n = sample_experts or 4 * workers
     x = synth.hidden(SEED, PREFILL_T, step=321)
     router = synth.router_weight(SEED, 0)
     t0 = time.perf_counter()
     ora.route(x @ router.T)
     t_route = time.perf_counter() - t0
-    t_deq = t_ffn = 0.0
-    for e in range(sample_experts):
-        gu, dn = synth.expert_gate_up(SEED, 0, e), synth.expert_down(SEED, 0, e)
-        t0 = time.perf_counter()
-        wg = ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN))
-        wd = ora.dequantize(dn, "Q6_K", (HIDDEN, FFN))
-        t1 = time.perf_counter()
-        xe = x[e * tokens_per_expert:(e + 1) * tokens_per_expert]
-        ora.expert_gate(xe @ wg.T) @ wd.T
-        t_ffn += time.perf_counter() - t1
-        t_deq += t1 - t0
+    tasks = [("Q4_K/Q6_K", e % N_BLOBS, x[(e % 28) * tokens_per_expert:(e % 28 + 1) * tokens_per_expert], False)
+             for e in range(n)]
+    t_pool, _ = cpu_baseline_wall(tasks)
     rows = PREFILL_T * (TOP_K + 1)
-    sec = t_route + t_deq / sample_experts * (EXPERTS + 1) + t_ffn / (sample_experts * tokens_per_expert) * rows
-    return {"value": PREFILL_T / sec, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"router on all {PREFILL_T} tokens; {sample_experts} experts dequantised from GGUF bytes with "
-                      f"their FFN on {tokens_per_expert} tokens each (numpy float32); scaled to 257 experts and "
-                      f"{rows} token-expert rows"}
+    sec = t_route + t_pool / (n * tokens_per_expert) * rows
+    return {"value": PREFILL_T / sec, "unit": "tokens/s", "cores": workers, "kind": "port",
+            "sample": f"router on all {PREFILL_T} tokens; {n} experts dequantised from GGUF bytes with their FFN on "
+                      f"{tokens_per_expert} tokens each, in parallel on {workers} worker processes (numpy float32); "
+                      f"scaled to {rows} token-expert rows"}
 
 
-def cpu_baseline(sample_layers: int = 2):
-    """willow's CPU path restated (the oracle port) timed on the host cores: dequantise the token's routed and
-    shared experts from their GGUF bytes and run route / expert FFN / combine in float32, one layer at a time.
-    Returns tokens/s scaled to the 40-layer token from the sampled layers."""
+def cpu_baseline(sample_layers: int = 4):
+    """willow's CPU path restated (the oracle port) on every host core: per layer the router + top-8, the 9 experts'
+    dequantisation from GGUF bytes and FFN in parallel on the pool, the combine; tokens/s scaled to the 40-layer
+    token from the sampled layers."""
     import oracle.moe_oracle as ora
     from willow_v2_b200 import synth
+    _, workers = cpu_baseline_pool()
     h = synth.hidden(SEED, 1, step=123)
     total = 0.0
     for l in range(sample_layers):
-        x = ora.rms_norm(h)
-        router = synth.router_weight(SEED, l)
-        sel = ora.route(x @ router.T)[1][0]
-        raw = {int(e): (synth.expert_gate_up(SEED, l, int(e)), synth.expert_down(SEED, l, int(e)))
-               for e in list(sel) + [EXPERTS]}  # bytes as the store would hold them (not timed)
-        gate = synth.shared_gate_weight(SEED, l)
-
-        def experts(e):
-            gu, dn = raw[e]
-            return ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN)), ora.dequantize(dn, "Q6_K", (HIDDEN, FFN))
-
-        t0 = time.perf_counter()
-        out = ora.moe(x, router, experts, experts(EXPERTS), gate)[0]
-        total += time.perf_counter() - t0
-        h = h + out
+        total += cpu_baseline_decode_layer(ora.rms_norm(h), synth.router_weight(SEED, l), l)
     per_layer = total / sample_layers
-    return {"value": 1.0 / (per_layer * LAYERS), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{sample_layers} of the 40 layers of one decode token (dequantise 9 experts + route + FFN + "
-                      f"combine per layer, float32 numpy), scaled to 40 layers"}
+    return {"value": 1.0 / (per_layer * LAYERS), "unit": "tokens/s", "cores": workers, "kind": "port",
+            "sample": f"{sample_layers} of the 40 layers of one decode token (router + top-8; 9 experts dequantised "
+                      f"and run in parallel on {workers} worker processes; combine; float32 numpy), scaled to 40 "
+                      f"layers"}
 
 
 def run_reference(args, rank, world):
@@ -776,79 +864,75 @@ def run_reference(args, rank, world):
         return None
     if args.workload == "prefill32k":
         K, W = args.steps, args.warmup
-        vals = [cpu_baseline_prefill(sample_experts=8)["value"] / LAYERS for _ in range(W + K)][W:]
+        n = cpu_baseline_pool()[1]  # one expert per worker each step
+        vals = [cpu_baseline_prefill(sample_experts=n)["value"] / LAYERS for _ in range(W + K)][W:]
         value = statistics.mean(vals)
-        base = cpu_baseline_prefill(sample_experts=8)
+        base = cpu_baseline_prefill(sample_experts=n)
         return {"metric": METRIC_PF32, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": PF32_T / value * 1e3, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
                 "config": {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, 4 GiB cap",
                            "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": LAYERS,
                            "tokens_per_step": PF32_T},
-                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"], "kind": "port",
                                  "sample": "each step: " + base["sample"] + "; divided by 40 layers"},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload == "batch64":
         K, W = args.steps, args.warmup
-        vals = [cpu_baseline_batch(sample_experts=8)["value"] for _ in range(W + K)][W:]
+        vals = [cpu_baseline_batch()["value"] for _ in range(W + K)][W:]
         value = statistics.mean(vals)
-        base = cpu_baseline_batch(sample_experts=8)
+        base = cpu_baseline_batch()
         return {"metric": METRIC_BATCH, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": BATCH_T / value * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
                 "config": {"workload": "configs[2]: 64 tokens through one MoE layer, Zipf-biased routing",
                            "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
                            "tokens_per_step": BATCH_T},
-                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"], "kind": "port",
                                  "sample": "each step: " + base["sample"]},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload == "prefill4096":
         K, W = args.steps, args.warmup
-        vals = [cpu_baseline_prefill(sample_experts=8)["value"] for _ in range(W + K)][W:]
+        n = cpu_baseline_pool()[1]  # one expert per worker each step
+        vals = [cpu_baseline_prefill(sample_experts=n)["value"] for _ in range(W + K)][W:]
         value = statistics.mean(vals)
-        base = cpu_baseline_prefill(sample_experts=8)
+        base = cpu_baseline_prefill(sample_experts=n)
         return {"metric": METRIC_PREFILL, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": PREFILL_T / value * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
                 "config": {"workload": "configs[3]: prefill 4096 tokens through one MoE layer, uniform routing",
                            "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
                            "tokens_per_step": PREFILL_T},
-                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"], "kind": "port",
                                  "sample": "each step: " + base["sample"]},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     import oracle.moe_oracle as ora
     from willow_v2_b200 import synth
     K, W = args.steps, args.warmup
-    # each step: one layer's router + top-k on a new token, then one of that layer's 9 experts (8 routed + shared)
-    # dequantised from its GGUF bytes and run; a token = 40 x (router + 9 experts)
-    t_route, t_expert = [], []
-    routers = [synth.router_weight(SEED, l) for l in range(LAYERS)]
+    _, workers = cpu_baseline_pool()
+    # each step: one layer of one new token (router + top-8, its 9 experts in parallel on the pool, the combine);
+    # a token = 40 steps
+    routers = {}
+    times = []
     for s in range(W + K):
         layer = s % LAYERS
+        if layer not in routers:
+            routers[layer] = synth.router_weight(SEED, layer)
         x = ora.rms_norm(synth.hidden(SEED, 1, step=10_000 + s))
-        t0 = time.perf_counter()
-        w, sel = ora.route(x @ routers[layer].T)
-        t1 = time.perf_counter()
-        e = int(sel[0, s % TOP_K]) if s % (TOP_K + 1) != TOP_K else EXPERTS
-        gu, dn = synth.expert_gate_up(SEED, layer, e), synth.expert_down(SEED, layer, e)  # the store's bytes
-        t2 = time.perf_counter()
-        y = ora.expert_gate(x @ ora.dequantize(gu, "Q4_K", (2 * FFN, HIDDEN)).T) @ ora.dequantize(dn, "Q6_K", (HIDDEN, FFN)).T
-        y = y * w[0, 0]
-        t3 = time.perf_counter()
+        dt = cpu_baseline_decode_layer(x, routers[layer], s)
         if s >= W:
-            t_route.append(t1 - t0)
-            t_expert.append(t3 - t2)
-    sec = LAYERS * (statistics.mean(t_route) + (TOP_K + 1) * statistics.mean(t_expert))
+            times.append(dt)
+    sec = LAYERS * statistics.mean(times)
     value = 1.0 / sec
     return {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": "configs[1]: decode 1 token x 40 MoE layers", "hidden": HIDDEN, "experts": EXPERTS,
                        "ffn": FFN, "top_k": TOP_K, "layers": LAYERS},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": "each step: one layer's router + top-8 and one of its 9 experts dequantised "
-                                       "from GGUF bytes and run (numpy float32); token time = 40 x (router + "
-                                       "9 x expert)"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
+                             "sample": f"each step: one layer of a new token: router + top-8, the 9 experts "
+                                       f"dequantised from GGUF bytes and run in parallel on {workers} worker "
+                                       f"processes, combine (numpy float32); token time = 40 x the mean step"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -997,29 +1081,18 @@ def run_typed_decode(args, type_name: str):
 
 
 def cpu_baseline_typed(type_name: str):
-    """The oracle port of the same step on the host cores: dequantise the 8 experts' matrices and multiply (numpy,
-    the BLAS threads numpy has)."""
-    from oracle import ggml_types as G
-    elements, size = G.BLOCKS[type_name]
-    rng = np.random.default_rng(SEED)
-    gu = rng.integers(0, 256, (2 * FFN * HIDDEN // elements, size), dtype=np.uint8)
-    dn = rng.integers(0, 256, (HIDDEN * FFN // elements, size), dtype=np.uint8)
-    d_at = TYPED_D_AT.get(type_name, 0)
-    for b in (gu, dn):
-        for off in ((d_at, 2) if type_name == "Q4_K" else (d_at,)):
-            b[:, off:off + 2] = rng.uniform(1e-3, 4e-3, b.shape[0]).astype(np.float16).view(np.uint8).reshape(-1, 2)
-    x = rng.standard_normal(HIDDEN).astype(np.float32)
-    t0 = time.perf_counter()
-    reps = 0
-    while reps < 1 or time.perf_counter() - t0 < 2.0:
-        for _ in range(TOP_K):
-            a = G.dequantize(gu, type_name, (2 * FFN, HIDDEN)) @ x
-            h = a[:FFN] / (1 + np.exp(-np.clip(a[:FFN], -80, 80))) * a[FFN:]
-            _ = G.dequantize(dn, type_name, (HIDDEN, FFN)) @ h
-        reps += 1
-    dt = (time.perf_counter() - t0) / reps
-    return {"value": 1.0 / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{reps} tokens x 8 experts ({type_name}), same shapes, ~2 s"}
+    """The oracle port of the same step on every host core: one token's 8 experts (dequantise gate_up and down,
+    SwiGLU, down product) in parallel on the pool, for about 2 s of tokens."""
+    _, workers = cpu_baseline_pool()
+    x = np.random.default_rng(SEED).standard_normal((1, HIDDEN)).astype(np.float32)
+    tasks = [(type_name, 0, x, False) for _ in range(TOP_K)]
+    times = []
+    while not times or sum(times) < 2.0:
+        times.append(cpu_baseline_wall(tasks)[0])
+    dt = statistics.mean(times)
+    return {"value": 1.0 / dt, "unit": "tokens/s", "cores": workers, "kind": "port",
+            "sample": f"{len(times)} tokens x 8 experts ({type_name}) in parallel on {workers} worker processes, same "
+                      f"shapes, ~2 s"}
 
 
 def main():
