@@ -348,7 +348,11 @@ _BLOBS = {}
 def cpu_baseline_pool():
     """(pool, workers): the spawned process pool of the CPU baseline, started once per process."""
     global _POOL
-    n = os.cpu_count() or 1
+    try:
+        n = len(os.sched_getaffinity(0))  # the cores this process may run on
+    except AttributeError:
+        n = os.cpu_count() or 1
+    n = max(1, min(n, 64))  # each worker holds ~60 MB of expert blobs
     if _POOL is None:
         import concurrent.futures
         import multiprocessing
