@@ -362,7 +362,9 @@ def cpu_baseline_pool():
         try:
             _POOL = concurrent.futures.ProcessPoolExecutor(n, mp_context=multiprocessing.get_context("spawn"),
                                                            initializer=_worker_init)
-            list(_POOL.map(_warm, range(4 * n)))  # every worker started (and its blobs made) before any timing
+            pids = set(_POOL.map(_warm, range(4 * n)))  # every worker started (its blobs made) before any timing
+            if len(pids) < n:
+                pids |= set(_POOL.map(_warm, range(8 * n)))
         finally:
             for k, v in saved.items():
                 if v is None:
@@ -416,6 +418,7 @@ def _ffn_task(task):
 
 
 def _warm(_):
+    time.sleep(0.05)  # long enough that the 4n warm-up tasks spread over every worker (each past its initializer)
     return os.getpid()
 
 
