@@ -181,7 +181,8 @@ def run_decode40(args, rank: int, world: int, dist):
     ctx.check_device()
 
     # end to end through the public API: pinned host input -> device, decode, result -> pinned host, every step
-    h_host = torch.from_numpy(np.concatenate([synth.hidden(SEED + 7 + 1000 * rank, 1, step=s) for s in range(K)])).pin_memory()
+    h_host = torch.from_numpy(np.concatenate([synth.hidden(SEED + 7 + 1000 * rank, 1, step=s)
+                                              for s in range(K)])).pin_memory()
     o_host = torch.empty(K, HIDDEN, dtype=torch.float32).pin_memory()
     h_dev = torch.empty(HIDDEN, dtype=torch.float32, device="cuda")
     if dist:
@@ -213,7 +214,8 @@ def run_decode40(args, rank: int, world: int, dist):
                    "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": n_layers,
                    "tokens_per_step": 1,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2: 734 MB of expert weights per step, a new token (new routing) each step"},
+                   "l2": "inputs larger than L2: 734 MB of expert weights per step, a new token (new routing) each "
+                         "step"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": n_layers * TRAFFIC_PER_LAYER, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": expert_bytes,
@@ -564,7 +566,8 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
                    "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T * world,
                    "parallelism": f"ep{world}", "experts_per_rank": per,
                    "l2": "inputs larger than L2: ~500 MB of activations per rank per step"},
-        "roofline": {"bound": "tensor", "kernel": "expert stages (dispatch + gather + grouped GEMMs, all chunks), rank 0",
+        "roofline": {"bound": "tensor",
+                     "kernel": "expert stages (dispatch + gather + grouped GEMMs, all chunks), rank 0",
                      "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16, "traffic": None,
                      "peak_kind": peak_kind, "algorithmic_flops_per_launch": flops, "launch_ms": experts_ms},
         "exchange": {"bytes_out_per_step": bytes_out, "exposed_ms_max": a2a_ms_max,
@@ -878,7 +881,8 @@ def run_reference(args, rank, world):
         return {"metric": METRIC_PF32, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": PF32_T / value * 1e3, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-                "config": {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, 4 GiB cap",
+                "config": {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, "
+                                       "4 GiB cap",
                            "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": LAYERS,
                            "tokens_per_step": PF32_T},
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"], "kind": "port",

@@ -65,7 +65,8 @@ def test_fp16_rounding_of_generator_matches_numpy():
     u = rng.integers(0, 1 << 24, 20000).astype(np.float64)
     vals = u * (3e-3 / 16777216.0) + 1e-3
     # exact ties and values right at binade edges
-    vals = np.concatenate((vals, [2.0 ** -10, 2.0 ** -9, 2.0 ** -9 * (1 + 2.0 ** -11), 2.0 ** -9 * (1 + 3 * 2.0 ** -11)]))
+    vals = np.concatenate((vals, [2.0 ** -10, 2.0 ** -9, 2.0 ** -9 * (1 + 2.0 ** -11),
+                                  2.0 ** -9 * (1 + 3 * 2.0 ** -11)]))
     ref = vals.astype(np.float16).view(np.uint16)
     got = np.array([f64_to_f16_rne(float(v)) for v in vals], dtype=np.uint16)
     np.testing.assert_array_equal(got, ref)

@@ -77,7 +77,8 @@ def test_parser_matches_gguf_py(tmp_path):
 
 @pytest.mark.parametrize("fused,files", [(False, 1), (True, 1), (False, 2)])
 def test_expert_blobs_are_the_pack_layout(tmp_path, fused, files):
-    """blob(layer, e) = gate rows of e ‖ up rows of e ‖ down rows of e, for separate, fused and split-file models."""
+    """blob(layer, e) = gate rows of e ‖ up rows of e ‖ down rows of e, for separate, fused and split-file
+    models."""
     path, arrays = write_model(str(tmp_path), fused=fused, files=files)
     meta, tensors = gguf_store.read_gguf(path)
     lay = gguf_store.expert_layout(meta, tensors)

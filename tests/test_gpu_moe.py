@@ -77,7 +77,8 @@ def test_dequant_store_blob_matches_oracle(model):
     gu = moe.dequantize(blob[:store.gate_up_bytes].contiguous(), "Q4_K", (1024, 2048), torch.float32).cpu().numpy()
     dn = moe.dequantize(blob[store.gate_up_bytes:].contiguous(), "Q6_K", (2048, 512), torch.float32).cpu().numpy()
     np.testing.assert_array_equal(gu.view(np.uint32),
-                                  ora.dequantize(synth.expert_gate_up(SEED, 1, 77), "Q4_K", (1024, 2048)).view(np.uint32))
+                                  ora.dequantize(synth.expert_gate_up(SEED, 1, 77), "Q4_K",
+                                                 (1024, 2048)).view(np.uint32))
     np.testing.assert_array_equal(dn.view(np.uint32),
                                   ora.dequantize(synth.expert_down(SEED, 1, 77), "Q6_K", (2048, 512)).view(np.uint32))
 
@@ -157,7 +158,8 @@ def test_dispatch_is_a_stable_grouping(model, T):
     ref_perm = np.argsort(flat, kind="stable")
     np.testing.assert_array_equal(perm.cpu().numpy(), ref_perm)
     np.testing.assert_array_equal(counts.cpu().numpy(), np.bincount(flat, minlength=256))
-    np.testing.assert_array_equal(offsets.cpu().numpy()[:-1], np.concatenate(([0], np.cumsum(np.bincount(flat, minlength=256))[:-1])))
+    np.testing.assert_array_equal(offsets.cpu().numpy()[:-1],
+                                  np.concatenate(([0], np.cumsum(np.bincount(flat, minlength=256))[:-1])))
     assert offsets[-1].item() == T * 8
     np.testing.assert_array_equal(usage.cpu().numpy(), np.bincount(flat, minlength=256))
 

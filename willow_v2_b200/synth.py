@@ -112,7 +112,8 @@ def expert_down(seed: int, layer: int, expert: int, rows=None) -> np.ndarray:
 
 def expert_blob(seed: int, layer: int, expert: int) -> np.ndarray:
     """The expert's bytes as the store holds them: gate_up then down, uint8 [EXPERT_BYTES]."""
-    return np.concatenate((expert_gate_up(seed, layer, expert).reshape(-1), expert_down(seed, layer, expert).reshape(-1)))
+    return np.concatenate((expert_gate_up(seed, layer, expert).reshape(-1),
+                           expert_down(seed, layer, expert).reshape(-1)))
 
 
 def _rng(*key) -> np.random.Generator:
