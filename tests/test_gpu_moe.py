@@ -463,7 +463,8 @@ def test_add_rmsnorm_matches_oracle(model):
 def test_q4k_down_layer_matches_oracle(model):
     """A layer whose down matrices (routed and shared) are Q4_K, as llama.cpp's Q4_K_M files store some layers:
     the dequant-GEMV kernels (4 tokens, and one token, which may not take the Q6_K decode kernel) and the grouped
-    GEMMs (64 tokens) against the float32 oracle; wmoe_decode_stack refuses such a layer."""
+    GEMMs (64 tokens) and the persistent decode kernel (one token, and a one-layer stack) against the float32
+    oracle."""
     import torch
     from willow_v2_b200 import moe
     from willow_v2_b200.lib import WmoeError, lib
@@ -490,22 +491,65 @@ def test_q4k_down_layer_matches_oracle(model):
 
     ref_args = dict(router_w=synth.router_weight(SEED, 0), expert_weights=experts, shared=experts(256),
                     shared_gate_w=synth.shared_gate_weight(SEED, 0))
-    for T, path, tol in ((4, "gemv", 1e-4), (1, "gemv", 1e-4), (64, "gemm", 1e-3)):
+    for T, path, tol in ((4, "gemv", 1e-4), (1, "gemv", 1e-4), (1, "decode", 1e-4), (64, "gemm", 1e-3)):
         x = torch.from_numpy(synth.hidden(SEED, T, step=80 + T)).cuda()
         prev = lib.wmoe_set_prefill_threshold(ctx.handle, 1 if path == "gemm" else 1 << 30)
+        prev_d = ctx.set_decode_kernel(path == "decode")
         try:
             out = moe.moe_forward(q4, 0, x, lw)
             torch.cuda.synchronize()
         finally:
             lib.wmoe_set_prefill_threshold(ctx.handle, prev)
+            ctx.set_decode_kernel(prev_d)
         idx = list(range(T)) if T <= 4 else [0, 31, 63]
         ref = ora.moe(x[idx].cpu().numpy(), **ref_args)[0]
         err = rel_l2(out[idx].cpu().numpy(), ref)
         assert err < tol, (T, path, err)
-    with pytest.raises(WmoeError, match="Q6_K"):
-        moe.decode_stack(q4, [lw], torch.from_numpy(synth.hidden(SEED, 1)).cuda())
+    h0 = synth.hidden(SEED, 1, step=88)
+    out = moe.decode_stack(q4, [lw], torch.from_numpy(h0).cuda()).cpu().numpy()
+    assert rel_l2(out.reshape(1, -1), ora.moe_stack(h0, [ref_args])) < 5e-4  # the stack bound of the other tests
     ctx.check_device()
     q4.close()
+
+
+def test_decode_stack_mixed_down_types(model):
+    """A 3-layer stack whose middle layer has Q4_K down matrices (routed and shared) runs as one persistent launch
+    and matches the oracle's layer-by-layer stack (rms_norm, residual) within the stack bound."""
+    import torch
+    from willow_v2_b200 import moe
+    ctx, store, layers = model
+    dn_bytes = 2048 * 512 // 256 * 144
+    mixed = moe.ExpertStore(LAYERS, ctx=ctx)
+    mixed.set_down_type(1, "Q4_K")
+    q4_down = {e: synth.expert_gate_up(SEED, 2, e).reshape(-1)[:dn_bytes] for e in range(257)}
+    for layer in range(LAYERS):
+        for e in range(256):
+            blob = store.download(layer, e)
+            if layer == 1:
+                blob = np.concatenate([blob[:store.gate_up_bytes], q4_down[e]])
+            mixed.upload(layer, e, blob)
+    lws = list(layers)
+    lws[1] = moe.LayerWeights(router_w=layers[1].router_w, shared_gate=layers[1].shared_gate,
+                              shared_gate_up=layers[1].shared_gate_up,
+                              shared_down=torch.from_numpy(np.ascontiguousarray(q4_down[256])).cuda())
+
+    def oracle_mixed(layer):
+        if layer != 1:
+            return oracle_layer(layer)
+
+        def experts(e):
+            return (ora.dequantize(synth.expert_gate_up(SEED, 1, e), "Q4_K", (1024, 2048)),
+                    ora.dequantize(q4_down[e], "Q4_K", (2048, 512)))
+        return dict(router_w=synth.router_weight(SEED, 1), expert_weights=experts, shared=experts(256),
+                    shared_gate_w=synth.shared_gate_weight(SEED, 1))
+
+    h0 = synth.hidden(SEED, 1, step=21)
+    out, sel = moe.decode_stack(mixed, lws, torch.from_numpy(h0).cuda(), return_routing=True)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    ref = ora.moe_stack(h0, [oracle_mixed(l) for l in range(LAYERS)])
+    assert rel_l2(out.cpu().numpy().reshape(1, -1), ref) < 5e-4
+    mixed.close()
 
 
 def test_cap_too_small_is_an_error(model):

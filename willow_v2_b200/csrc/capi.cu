@@ -72,6 +72,8 @@ static T* at(wmoe_ctx* ctx, size_t off) {
   return reinterpret_cast<T*>(static_cast<char*>(ctx->scratch) + off);
 }
 
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 extern "C" {
 
 int wmoe_init(int device, wmoe_ctx** out) {
@@ -460,15 +462,16 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: null pointer");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (T == 1 && !store->capped && ctx->use_decode_kernel && ctx->decode_ctas > 0 && E == 256 &&
-      store->down_type[size_t(layer)] == kGgmlQ6K) {
+      aligned16(router_packed) && aligned16(x)) {
     // one token, every expert resident: the persistent decode kernel (one launch, no host synchronisation)
     if (int rc = ensure_scratch(ctx, decode_scratch_bytes(H, F, E, ctx->decode_ctas))) return rc;
     DecodeLayer dl{router_w, router_bias, shared_gate, shared_gate_up, shared_down, router_packed, router_split};
     int n = 0;
-    const cudaError_t e = decode_persistent(store_source(store, layer, shared_gate_up, shared_down), layer, 1, &dl, H, F, E,
-                                            top_k, 0.f, false, x, x_dtype, out, out_dtype, topk_idx_out, topk_w_out,
-                                            ctx->scratch, ctx->decode_ctas, ctx->d_status, ctx->trace,
-                                            ctx->trace_entries, st, &n);
+    const int down_type = store->down_type[size_t(layer)];
+    const cudaError_t e = decode_persistent(store_source(store, layer, shared_gate_up, shared_down), &down_type,
+                                            layer, 1, &dl, H, F, E, top_k, 0.f, false, x, x_dtype, out, out_dtype,
+                                            topk_idx_out, topk_w_out, ctx->scratch, ctx->decode_ctas,
+                                            ctx->d_status, ctx->trace, ctx->trace_entries, st, &n);
     ctx->launches += uint64_t(n);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel");
     return WMOE_OK;
@@ -1154,19 +1157,19 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
     if (!layers[i].router_w || !layers[i].shared_gate || !layers[i].shared_gate_up || !layers[i].shared_down)
       return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack: null weight pointer in layers[]");
   for (int i = 0; i < n_layers; ++i)
-    if (store->down_type[size_t(layer_begin + i)] != kGgmlQ6K)
-      return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED,
-                      "wmoe_decode_stack: the persistent kernel runs Q6_K down matrices; call wmoe_moe_forward per "
-                      "layer for Q4_K ones");
-  const size_t need = decode_scratch_bytes(store->hidden, store->ffn, store->experts, ctx->decode_ctas);
-  if (int rc = ensure_scratch(ctx, need)) return rc;
+    if (!aligned16(layers[i].router_packed))
+      return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack: a packed router must be 16-byte aligned");
+  if (!aligned16(h_in)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack: h_in must be 16-byte aligned");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = ensure_scratch(ctx, decode_scratch_bytes(store->hidden, store->ffn, store->experts, ctx->decode_ctas)))
+    return rc;
   int n = 0;
   const ExpertSource src = store_source(store, layer_begin, nullptr, nullptr);
-  const cudaError_t e = decode_persistent(src, layer_begin, n_layers, reinterpret_cast<const DecodeLayer*>(layers),
-                                          store->hidden, store->ffn, store->experts, 8, eps, true, h_in, WMOE_F32,
-                                          h_out, WMOE_F32, topk_idx_out, nullptr, ctx->scratch, ctx->decode_ctas,
-                                          ctx->d_status, ctx->trace, ctx->trace_entries,
-                                          static_cast<cudaStream_t>(stream), &n);
+  const cudaError_t e = decode_persistent(src, store->down_type.data() + layer_begin, layer_begin, n_layers,
+                                          reinterpret_cast<const DecodeLayer*>(layers), store->hidden, store->ffn,
+                                          store->experts, 8, eps, true, h_in, WMOE_F32, h_out, WMOE_F32, topk_idx_out,
+                                          nullptr, ctx->scratch, ctx->decode_ctas, ctx->d_status, ctx->trace,
+                                          ctx->trace_entries, st, &n);
   ctx->launches += uint64_t(n);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack");
   return WMOE_OK;
@@ -1190,12 +1193,13 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
     return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED,
                     "wmoe_decode_stack_noalloc: the persistent kernel cannot be co-resident here");
   for (int i = 0; i < n_layers; ++i)
-    if (store->down_type[size_t(layer_begin + i)] != kGgmlQ6K)
-      return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_decode_stack_noalloc: the persistent kernel runs Q6_K down "
-                                                 "matrices; call wmoe_moe_forward per layer for Q4_K ones");
-  for (int i = 0; i < n_layers; ++i)
     if (!layers[i].router_w || !layers[i].shared_gate || !layers[i].shared_gate_up || !layers[i].shared_down)
       return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: null weight pointer in layers[]");
+  for (int i = 0; i < n_layers; ++i)
+    if (!aligned16(layers[i].router_packed))
+      return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: a packed router must be 16-byte aligned");
+  if (!aligned16(h_in))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_decode_stack_noalloc: h_in must be 16-byte aligned");
   const size_t need = decode_scratch_bytes(store->hidden, store->ffn, store->experts, ctx->decode_ctas);
   if (need > static_scratch_bytes())
     return ctx_fail(ctx, WMOE_ERR_CAPACITY,
@@ -1209,10 +1213,11 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
   WMOE_CHECK_CUDA(ctx, static_scratch(ctx->device, &scratch), "wmoe_decode_stack_noalloc: static scratch address");
   int n = 0;
   const ExpertSource src = store_source(store, layer_begin, nullptr, nullptr);
-  const cudaError_t e = decode_persistent(src, layer_begin, n_layers, reinterpret_cast<const DecodeLayer*>(layers),
-                                          store->hidden, store->ffn, store->experts, 8, eps, true, h_in, WMOE_F32,
-                                          h_out, WMOE_F32, topk_idx_out, nullptr, scratch, ctx->decode_ctas,
-                                          ctx->d_status, nullptr, 0, static_cast<cudaStream_t>(stream), &n);
+  const cudaError_t e = decode_persistent(src, store->down_type.data() + layer_begin, layer_begin, n_layers,
+                                          reinterpret_cast<const DecodeLayer*>(layers), store->hidden, store->ffn,
+                                          store->experts, 8, eps, true, h_in, WMOE_F32, h_out, WMOE_F32, topk_idx_out,
+                                          nullptr, scratch, ctx->decode_ctas, ctx->d_status, nullptr, 0,
+                                          static_cast<cudaStream_t>(stream), &n);
   ctx->launches += uint64_t(n);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack_noalloc");
   return WMOE_OK;
@@ -1230,7 +1235,6 @@ static int typed_args(wmoe_ctx* ctx, const char* fn, int type, int rows, int k) 
   return 0;
 }
 
-static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int wmoe_gemv(wmoe_ctx* ctx, int ggml_type, const uint8_t* w, int rows, int k, const void* x, int x_dtype,
               int tokens, void* y, int y_dtype, void* stream) {

@@ -39,7 +39,8 @@ constexpr int kThreads = 512, kWarps = kThreads / 32;
 constexpr int kMaxLayers = 64;
 constexpr int kMaxRows = 32;                      // output rows per CTA
 constexpr int kRowBytesQ4 = kH / 256 * Q4K_BYTES;  // 1152
-constexpr int kRowBytesQ6 = kF / 256 * Q6K_BYTES;  // 420
+constexpr int kRowBytesQ6 = kF / 256 * Q6K_BYTES;  // 420: a Q6_K down row
+constexpr int kRowBytesQ4d = kF / 256 * Q4K_BYTES;  // 288: a Q4_K down row
 constexpr int kHBlocks = kSlots * kF / 32;        // 144 h blocks of 32 values: one per CTA
 constexpr int kChunkBytes = 16 * 2 * kRowBytesQ4;  // 16 gate rows + 16 up rows
 constexpr int kReplicas = 16;
@@ -69,6 +70,7 @@ struct DecodeParams {
   int* status;
   int dn_chunk;     // bytes reserved per slot for this CTA's down rows
   unsigned long long* trace;  // phase timestamps [layer][point][cta], or null
+  unsigned char down_q4[kMaxLayers];  // 1: the layer's down matrices are Q4_K (else Q6_K)
   DecodeLayer layers[kMaxLayers];
 };
 
@@ -173,6 +175,7 @@ __device__ __forceinline__ void touch(const void* ptr) { asm volatile("prefetch.
 struct Small {
   uint64_t mbar_gu[2], mbar_dn, mbar_rs;
   DecodeLayer layers[kMaxLayers];  // the layer table, copied once (parameter reads by layer index miss the cache)
+  unsigned char down_q4[kMaxLayers];
   alignas(16) float x[kH];        // x_l as read (raw residual for a stack)
   alignas(16) int16_t xq[kH];     // quantised x, in gate_up lane order (see xq_offset)
   float xs[kH / 32];
@@ -193,7 +196,6 @@ struct Small {
   int order[kK];
   float rscale;
   int abort_flag;
-  int dn_off;                     // offset of row r0 within each slot's down chunk
 };
 
 // Scale and min of sub-blocks j = 2g and 2g + 1 of a Q4_K super-block (6-bit values packed in the 12 bytes s0..s2,
@@ -267,6 +269,8 @@ __device__ __forceinline__ int hq_offset(int pos) {
   const int t8 = sb * 4 + hh * 2 + p / 16, e16 = p % 16;
   return ((s * 2 + e16 / 8) * 8 + t8) * 8 + e16 % 8;
 }
+// Start of run (quarter s, half-run j) of down lane task t8 within a slot's quantised h.
+__device__ __forceinline__ int hq_run(int s, int j, int t8) { return ((s * 2 + j) * 8 + t8) * 8; }
 
 // Warp-cooperative int16 quantisation of 32 values (lane i holds value i of the block): q[offset], the block's
 // scale and its two per-16 sums, with single-instruction warp reductions (redux.sync).
@@ -357,13 +361,17 @@ __device__ __forceinline__ float unordered(uint32_t u) {
   return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
 }
 
-// Unpacked Q6_K codes of one (row, slot) pair for one lane: quarter s, positions 4m..4m+3 in q[s][m].
+// Down codes of one (row, slot) pair for one lane, unpacked while the h exchange (S2) completes.
+// Q6_K: lane task t8 = (super-block t8/4, half (t8/2)%2, 16-run t8%2); q[s][m] holds quarter s, positions 4m..4m+3
+// of the run as 6-bit codes, D[s] = d * scale of the quarter's 16 values.
+// Q4_K: lane task t8 = (super-block t8/4, nibble group g = t8%4); q[0..1][*] hold the 8 words of quant bytes
+// 32g..32g+31 (low nibbles: sub-block 2g, high: 2g + 1), D = {d*sc0, dmin*mn0, d*sc1, dmin*mn1}.
 struct DownPair {
   uint32_t q[4][4];
   float D[4];
 };
 
-__device__ __forceinline__ void down_unpack(const uint8_t* blk, int hh, int pq, DownPair& dp) {
+__device__ __forceinline__ void down_unpack_q6(const uint8_t* blk, int hh, int pq, DownPair& dp) {
   const uint4 ql0 = lds_u2_16(blk + hh * 64 + pq), ql1 = lds_u2_16(blk + hh * 64 + 32 + pq);
   const uint4 qh = lds_u2_16(blk + 128 + hh * 32 + pq), sc = lds_u2_16(blk + 192);
   const float d = f16_to_f32(*reinterpret_cast<const uint16_t*>(blk + 208));
@@ -380,6 +388,63 @@ __device__ __forceinline__ void down_unpack(const uint8_t* blk, int hh, int pq, 
       dp.q[s][m] = ((lw >> (4 * (s / 2))) & 0x0F0F0F0Fu) | (((hw[m] >> (2 * s)) & 0x03030303u) << 4);
     }
   }
+}
+
+__device__ __forceinline__ void down_unpack_q4(const uint8_t* blk, int g, DownPair& dp) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * g);
+  int sc0, mn0, sc1, mn1;
+  q4k_scales_pair(hdr.y, hdr.z, hdr.w, g, sc0, mn0, sc1, mn1);
+  const float d = f16_to_f32(uint16_t(hdr.x & 0xFFFF)), dm = f16_to_f32(uint16_t(hdr.x >> 16));
+  dp.q[0][0] = q0.x, dp.q[0][1] = q0.y, dp.q[0][2] = q0.z, dp.q[0][3] = q0.w;
+  dp.q[1][0] = q1.x, dp.q[1][1] = q1.y, dp.q[1][2] = q1.z, dp.q[1][3] = q1.w;
+  dp.D[0] = d * float(sc0), dp.D[1] = dm * float(mn0), dp.D[2] = d * float(sc1), dp.D[3] = dm * float(mn1);
+}
+
+// One pair's down product for one lane, from the unpacked codes and the slot's quantised h in shared memory.
+__device__ __forceinline__ float down_dot_q6(const DownPair& dp, const Small& sm, int slot, int t8, int base) {
+  float t[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    // runs of 8 of this lane task: (s, 0) and (s, 1), each group's eight tasks adjacent
+    const uint4 xa = *reinterpret_cast<const uint4*>(&sm.hq[slot][hq_run(s, 0, t8)]);
+    const uint4 xb = *reinterpret_cast<const uint4*>(&sm.hq[slot][hq_run(s, 1, t8)]);
+    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    int acc0 = 0, acc1 = 0;
+#pragma unroll
+    for (int m = 0; m < 4; m += 2) {
+      acc0 = dp2a_hi(xw[2 * m + 1], dp.q[s][m], dp2a_lo(xw[2 * m], dp.q[s][m], acc0));
+      acc1 = dp2a_hi(xw[2 * m + 3], dp.q[s][m + 1], dp2a_lo(xw[2 * m + 2], dp.q[s][m + 1], acc1));
+    }
+    const int pos = base + 32 * s;
+    t[s] = sm.hs[slot][pos / 32] * (dp.D[s] * float(acc0 + acc1 - 32 * sm.hsum[slot][pos / 16]));
+  }
+  return (t[0] + t[1]) + (t[2] + t[3]);
+}
+
+// Q4_K: sub-block 2g is positions sb*256 + 64g + [0, 32) and lies in quarter s = 2 (g % 2) of half g / 2, tasks
+// t8b and t8b + 1 of the Q6_K lane layout (16 positions each); sub-block 2g + 1 is quarter s + 1 of the same tasks.
+__device__ __forceinline__ float down_dot_q4(const DownPair& dp, const Small& sm, int slot, int sb, int g) {
+  const int t8b = sb * 4 + (g >> 1) * 2, s = 2 * (g & 1);
+  int acc[2] = {0, 0};
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // 0: low nibbles (sub-block 2g), 1: high nibbles (2g + 1)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // run j: positions 8j..8j+7 of the sub-block = quant words 2j, 2j + 1
+      const int t8 = t8b + (j >> 1), jr = j & 1;
+      const uint4 xa = *reinterpret_cast<const uint4*>(&sm.hq[slot][hq_run(s + half, jr, t8)]);
+      const uint32_t w0 = dp.q[j >> 1][2 * (j & 1)], w1 = dp.q[j >> 1][2 * (j & 1) + 1];
+      const uint32_t n0 = (w0 >> (4 * half)) & 0x0F0F0F0Fu, n1 = (w1 >> (4 * half)) & 0x0F0F0F0Fu;
+      acc[half] = dp2a_hi(xa.y, n0, dp2a_lo(xa.x, n0, acc[half]));
+      acc[half] = dp2a_hi(xa.w, n1, dp2a_lo(xa.z, n1, acc[half]));
+    }
+  }
+  const int b0 = sb * 8 + 2 * g;  // 32-value block of sub-block 2g in h
+  const float h0 = float(sm.hsum[slot][2 * b0] + sm.hsum[slot][2 * b0 + 1]);
+  const float h1 = float(sm.hsum[slot][2 * b0 + 2] + sm.hsum[slot][2 * b0 + 3]);
+  return sm.hs[slot][b0] * (dp.D[0] * float(acc[0]) - dp.D[1] * h0) +
+         sm.hs[slot][b0 + 1] * (dp.D[2] * float(acc[1]) - dp.D[3] * h1);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
@@ -407,13 +472,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     mbar_init(&sm.mbar_dn, 1);
     mbar_init(&sm.mbar_rs, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    sm.dn_off = int(unsigned(r0) * kRowBytesQ6 % 16);
   }
   {
     constexpr int kWords = int(sizeof(DecodeLayer) / sizeof(uint64_t));
     static_assert(sizeof(DecodeLayer) % sizeof(uint64_t) == 0, "DecodeLayer holds pointers only");
     for (int i = tid; i < p.n_layers * kWords; i += kThreads)
       reinterpret_cast<uint64_t*>(sm.layers)[i] = reinterpret_cast<const uint64_t*>(p.layers)[i];
+    if (tid < kMaxLayers) sm.down_q4[tid] = p.down_q4[tid];
   }
   __syncthreads();
 
@@ -444,6 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const unsigned parity = unsigned(li & 1);
     const double* S = p.sacc + (li % 3) * kSaccRot;
     const bool last = li + 1 == p.n_layers;
+    const bool dq4 = sm.down_q4[li] != 0;
+    const int rb = dq4 ? kRowBytesQ4d : kRowBytesQ6;  // down row bytes of this layer
 
     // ---------------- phase B: x_l, RMS scale, router sums, routing, copies, gate_up
     WMOE_TRACE(li, 0);
@@ -548,8 +615,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       // right behind them, down rows [r0, r1) of every slot (aligned outward to 16 bytes): the whole layer's stream
       // is in flight at once (issuing the down rows only after the first gate_up chunk had landed left HBM half idle)
       {
-        const unsigned lo = unsigned(r0) * kRowBytesQ6 / 16 * 16;
-        const unsigned hi = (unsigned(r1) * kRowBytesQ6 + 15) / 16 * 16;
+        const unsigned lo = unsigned(r0) * unsigned(rb) / 16 * 16;
+        const unsigned hi = (unsigned(r1) * unsigned(rb) + 15) / 16 * 16;
         const unsigned present = __popc(__ballot_sync(0xffffffffu, lane < kSlots && dn != nullptr));
         if (lane == 0) mbar_arrive_expect_tx(&sm.mbar_dn, present * (hi - lo));
         __syncwarp();
@@ -632,20 +699,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     ++epoch;
     // down codes of this thread's (row, slot) pairs, unpacked while S2 completes
     const int grp = tid / 8, t8 = tid % 8;
-    const int sb = t8 / 4, hh = (t8 / 2) % 2, pq = 16 * (t8 % 2);
-    const int base = sb * 256 + hh * 128 + pq;
     DownPair dp[kMaxPairs];
     WMOE_TRACE(li, 9);
     if (!mbar_wait(&sm.mbar_dn, parity, p.status, &sm.abort_flag)) return;
     WMOE_TRACE(li, 10);
+    {
+      const int dn_off = (r0 * rb) % 16;  // row r0 within each slot's down chunk
 #pragma unroll
-    for (int k = 0; k < kMaxPairs; ++k) {
-      const int pr = grp + k * (kThreads / 8);
-      if (pr < nrows * kSlots) {
-        const int rl = pr / kSlots, slot = pr % kSlots;
-        down_unpack(dn_buf + size_t(slot) * dn_chunk + sm.dn_off + rl * kRowBytesQ6 + sb * Q6K_BYTES, hh, pq, dp[k]);
-      } else {
-        dp[k] = DownPair{};  // past the CTA's rows: computed on, never stored
+      for (int k = 0; k < kMaxPairs; ++k) {
+        const int pr = grp + k * (kThreads / 8);
+        if (pr < nrows * kSlots) {
+          const int rl = pr / kSlots, slot = pr % kSlots;
+          const uint8_t* row = dn_buf + size_t(slot) * dn_chunk + dn_off + rl * rb;
+          if (dq4)
+            down_unpack_q4(row + (t8 / 4) * Q4K_BYTES, t8 % 4, dp[k]);
+          else
+            down_unpack_q6(row + (t8 / 4) * Q6K_BYTES, (t8 / 2) % 2, 16 * (t8 % 2), dp[k]);
+        } else {
+          dp[k] = DownPair{};  // past the CTA's rows: computed on, never stored
+        }
       }
     }
     // while S2 completes: the address translations of the next layer's experts. A layer's copies come from 9 of
@@ -663,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         touch(N.shared_gate_up);
         touch(N.shared_gate_up + 2 * kF * kRowBytesQ4 - 1);
         touch(N.shared_down);
-        touch(N.shared_down + kH * kRowBytesQ6 - 1);
+        touch(N.shared_down + kH * (sm.down_q4[li + 1] ? kRowBytesQ4d : kRowBytesQ6) - 1);
       }
     }
     WMOE_TRACE(li, 11);
@@ -702,25 +774,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       float part[kMaxPairs];
 #pragma unroll
       for (int k = 0; k < kMaxPairs; ++k) {
-        const int pr = grp + k * (kThreads / 8);
-        const int slot = pr % kSlots;
-        float t[4];
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          // runs of 8 of this lane task: (s, 0) and (s, 1), each group's eight tasks adjacent
-          const uint4* xp = reinterpret_cast<const uint4*>(sm.hq[slot]) + (s * 2) * 8 + t8;
-          const uint4 xa = xp[0], xb = xp[8];
-          const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-          int acc0 = 0, acc1 = 0;
-#pragma unroll
-          for (int m = 0; m < 4; m += 2) {
-            acc0 = dp2a_hi(xw[2 * m + 1], dp[k].q[s][m], dp2a_lo(xw[2 * m], dp[k].q[s][m], acc0));
-            acc1 = dp2a_hi(xw[2 * m + 3], dp[k].q[s][m + 1], dp2a_lo(xw[2 * m + 2], dp[k].q[s][m + 1], acc1));
-          }
-          const int pos = base + 32 * s;
-          t[s] = sm.hs[slot][pos / 32] * (dp[k].D[s] * float(acc0 + acc1 - 32 * sm.hsum[slot][pos / 16]));
-        }
-        part[k] = (t[0] + t[1]) + (t[2] + t[3]);
+        const int slot = (grp + k * (kThreads / 8)) % kSlots;
+        if (dq4)
+          part[k] = down_dot_q4(dp[k], sm, slot, t8 / 4, t8 % 4);
+        else
+          part[k] = down_dot_q6(dp[k], sm, slot, t8, (t8 / 4) * 256 + ((t8 / 2) % 2) * 128 + 16 * (t8 % 2));
       }
 #pragma unroll
       for (int o = 4; o > 0; o >>= 1)
@@ -782,19 +840,36 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 size_t static_scratch_bytes() { return kStaticScratchBytes; }
 
-// Device address of g_static_scratch on the current device, looked up once per device (the first call on a device
-// must come before any stream capture). Returns the CUDA error of the lookup.
+// Device address of g_static_scratch on the current device, looked up once per (device, primary context) pair:
+// after a cudaDeviceReset the context is a new one and the address is looked up again. The first call on a device
+// must come before any stream capture. Returns the CUDA error of the lookup.
 cudaError_t static_scratch(int device, void** ptr) {
   constexpr int kMaxDevices = 64;
   static std::mutex mu;
   static void* addr[kMaxDevices] = {};
+  static void* owner[kMaxDevices] = {};  // the context the address belongs to
+  using GetCtx = int (*)(void**);        // cuCtxGetCurrent, reached through the runtime (no link to libcuda)
+  static GetCtx get_ctx = nullptr;
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[device]) {
+  if (!get_ctx) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_ctx = reinterpret_cast<GetCtx>(fn);
+  }
+  void* cur = nullptr;
+  if (get_ctx) {
+    cudaFree(nullptr);  // makes the device's primary context current if it is not yet
+    if (get_ctx(&cur) != 0) cur = nullptr;
+  }
+  if (!addr[device] || owner[device] != cur) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return e;
     addr[device] = p;
+    owner[device] = cur;
   }
   *ptr = addr[device];
   return cudaSuccess;
@@ -821,12 +896,17 @@ int decode_num_ctas(int device) {
   return per_sm >= 1 ? sms : 0;
 }
 
-cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_layers, const DecodeLayer* layers,
-                              int H, int F, int E, int k, float eps, bool stack, const void* x_in, int x_dtype,
-                              void* out, int out_dtype, int32_t* topk_idx_out, float* topk_w_out, void* scratch,
-                              int num_ctas, int* status, uint64_t* trace, size_t trace_entries, cudaStream_t st,
-                              int* launches) {
+cudaError_t decode_persistent(const ExpertSource& src, const int* down_types, int layer_begin, int n_layers,
+                              const DecodeLayer* layers, int H, int F, int E, int k, float eps, bool stack,
+                              const void* x_in, int x_dtype, void* out, int out_dtype, int32_t* topk_idx_out,
+                              float* topk_w_out, void* scratch, int num_ctas, int* status, uint64_t* trace,
+                              size_t trace_entries, cudaStream_t st, int* launches) {
   if (H != kH || F != kF || E != kE || k != kK || num_ctas < kHBlocks) return cudaErrorInvalidValue;
+  for (int i = 0; i < n_layers; ++i) {
+    if (down_types[i] != kGgmlQ6K && down_types[i] != kGgmlQ4K) return cudaErrorInvalidValue;
+    // a packed router is bulk-copied: 16-byte aligned
+    if (reinterpret_cast<uintptr_t>(layers[i].router_packed) & 15u) return cudaErrorMisalignedAddress;
+  }
   // the trace covers the first launch's layers when it is large enough, else it is off
   if (trace && trace_entries < size_t(std::min(n_layers, kMaxLayers)) * kTracePoints * size_t(num_ctas))
     trace = nullptr;
@@ -861,7 +941,10 @@ cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_la
     p.status = status;
     p.dn_chunk = down_chunk_bytes(num_ctas);
     p.trace = l0 == 0 ? reinterpret_cast<unsigned long long*>(trace) : nullptr;
-    for (int i = 0; i < p.n_layers; ++i) p.layers[i] = layers[l0 + i];
+    for (int i = 0; i < p.n_layers; ++i) {
+      p.layers[i] = layers[l0 + i];
+      p.down_q4[i] = down_types[l0 + i] == kGgmlQ4K ? 1 : 0;
+    }
     // barrier counter and the router sums start at zero for every launch
     e = cudaMemsetAsync(base, 0, 256, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(sacc, 0, 3 * size_t(kSaccRot) * sizeof(double), st);

@@ -164,12 +164,13 @@ size_t decode_scratch_bytes(int H, int F, int E, int num_ctas);
 size_t static_scratch_bytes();
 cudaError_t static_scratch(int device, void** ptr);  // the no-allocation entry point's scratch on a device
 int decode_num_ctas(int device);
-cudaError_t decode_persistent(const ExpertSource& src, int layer_begin, int n_layers, const DecodeLayer* layers,
-                              int H, int F, int E, int k, float eps, bool stack, const void* x_in, int x_dtype,
-                              void* out,
-                              int out_dtype, int32_t* topk_idx_out, float* topk_w_out, void* scratch,
-                              int num_ctas, int* status, uint64_t* trace, size_t trace_entries, cudaStream_t st,
-                              int* launches);
+// down_types[i]: ggml type of layer layer_begin + i's down matrices (kGgmlQ6K or kGgmlQ4K). The scratch holds
+// decode_scratch_bytes; each launch clears what it needs first.
+cudaError_t decode_persistent(const ExpertSource& src, const int* down_types, int layer_begin, int n_layers,
+                              const DecodeLayer* layers, int H, int F, int E, int k, float eps, bool stack,
+                              const void* x_in, int x_dtype, void* out, int out_dtype, int32_t* topk_idx_out,
+                              float* topk_w_out, void* scratch, int num_ctas, int* status, uint64_t* trace,
+                              size_t trace_entries, cudaStream_t st, int* launches);
 
 // store.cu: device generator
 cudaError_t fill_synthetic(uint8_t* dst, uint64_t seed, const int32_t* layer_expert /*[n][2]*/, int n,
