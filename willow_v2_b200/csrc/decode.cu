@@ -9,8 +9,8 @@
 //   B   every CTA reads x_l (its own RMS scale r = 1/sqrt(mean(x^2) + eps) from it), sums the replicas in a
 //       fixed order and quantises x to int16; warp 0 forms logits r*S + bias and the same top-k routing on every
 //       CTA and its lanes at once issue TMA bulk copies (cp.async.bulk, mbarrier completion) of this CTA's 32
-//       gate/up row pairs in two chunks, and right behind them of its slice of down rows of all k+1 experts, so
-//       that the layer's whole expert stream is in flight together. CTA c < 144 owns h block c: 32 consecutive h
+//       gate/up row pairs in two chunks; right after the routing barrier warp 1 issues its slice of down rows of
+//       all k+1 experts (off warp 0's path), so that the layer's whole expert stream is in flight together. CTA c < 144 owns h block c: 32 consecutive h
 //       values of one expert slot. Warps compute gate and up rows (dp2a on the 4-bit codes) -> SwiGLU; warp 0 quantises
 //       the block's 32 h values to int16 once and writes them to global memory in the order the down lanes read;
 //       the other warps unpack their Q6_K down codes into registers (independent of h).
@@ -43,7 +43,7 @@ constexpr int kRowBytesQ6 = kF / 256 * Q6K_BYTES;  // 420: a Q6_K down row
 constexpr int kRowBytesQ4d = kF / 256 * Q4K_BYTES;  // 288: a Q4_K down row
 constexpr int kHBlocks = kSlots * kF / 32;        // 144 h blocks of 32 values: one per CTA
 constexpr int kChunkBytes = 16 * 2 * kRowBytesQ4;  // 16 gate rows + 16 up rows
-constexpr int kReplicas = 16;
+constexpr int kReplicas = 4;
 constexpr int kSaccStride = 264;                  // doubles per replica (>= kE + 1)
 constexpr int kSaccRot = kReplicas * kSaccStride;  // doubles per rotation buffer
 constexpr int kMaxPairs = 2;                      // (row, slot) down pairs per 8-lane group
@@ -194,6 +194,7 @@ struct Small {
   int sel[kSlots];
   float w[kSlots];
   int order[kK];
+  const uint8_t* dn_ptr[kSlots];
   float rscale;
   int abort_flag;
 };
@@ -612,16 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                              size_t(up * kF + blk_j0 + 16 * ch) * kRowBytesQ4;
         bulk_g2s(gu_buf + ch * kChunkBytes + up * (kChunkBytes / 2), src, kChunkBytes / 2, &sm.mbar_gu[ch]);
       }
-      // right behind them, down rows [r0, r1) of every slot (aligned outward to 16 bytes): the whole layer's stream
-      // is in flight at once (issuing the down rows only after the first gate_up chunk had landed left HBM half idle)
-      {
-        const unsigned lo = unsigned(r0) * unsigned(rb) / 16 * 16;
-        const unsigned hi = (unsigned(r1) * unsigned(rb) + 15) / 16 * 16;
-        const unsigned present = __popc(__ballot_sync(0xffffffffu, lane < kSlots && dn != nullptr));
-        if (lane == 0) mbar_arrive_expect_tx(&sm.mbar_dn, present * (hi - lo));
-        __syncwarp();
-        if (lane < kSlots && dn) bulk_g2s(dn_buf + size_t(lane) * dn_chunk, dn + lo, hi - lo, &sm.mbar_dn);
-      }
+      if (lane < kSlots) sm.dn_ptr[lane] = dn;  // the down rows are issued by warp 1 after the routing barrier
       WMOE_TRACE(li, 3);
       // renormalised weights of the k picks: exp(l_i - l_0) / sum_j exp(l_j - l_0)
       const float top0 = unordered(__shfl_sync(0xffffffffu, my_key, 0));
@@ -644,6 +636,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     __syncthreads();
     WMOE_TRACE(li, 4);
+    if (warp == 1) {  // down rows [r0, r1) of every slot (aligned outward to 16 bytes), off warp 0's critical path
+      const uint8_t* dn = lane < kSlots ? sm.dn_ptr[lane] : nullptr;
+      const unsigned lo = unsigned(r0) * unsigned(rb) / 16 * 16;
+      const unsigned hi = (unsigned(r1) * unsigned(rb) + 15) / 16 * 16;
+      const unsigned present = __popc(__ballot_sync(0xffffffffu, dn != nullptr));
+      if (lane == 0) mbar_arrive_expect_tx(&sm.mbar_dn, present * (hi - lo));
+      __syncwarp();
+      if (dn) bulk_g2s(dn_buf + size_t(lane) * dn_chunk, dn + lo, hi - lo, &sm.mbar_dn);
+    }
     // the next layer's router slice, overlapping the copies (waited for before it is used in phase C)
     const bool rs_copy = p.stack && !last && fetch_router_slice(sm, sm.layers[li + 1], r0, nrows);
     if (!mbar_wait(&sm.mbar_gu[0], parity, p.status, &sm.abort_flag)) return;
