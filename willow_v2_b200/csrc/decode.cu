@@ -4,8 +4,9 @@
 // A layer has two grid-wide exchanges, the minimum its data flow allows (every logit needs all of x; every down
 // row needs all of an expert's h):
 //   S1  x_l is complete in global memory, and so are the router sums S_l[e] = sum_r R_l[e, r] x_l[r] (plus the
-//       shared-expert gate row), accumulated in float64 by the CTAs that produced the rows of x_l, into 16
-//       replicas (CTA c adds into replica c % 16) so that no cache line takes more than ~10 of the adds.
+//       shared-expert gate row), accumulated in float64 by the CTAs that produced the rows of x_l, into 4
+//       replicas (CTA c adds into replica c % 4; measured against 1, 2, 8 and 16 replicas, 4 balances the atomics'
+//       contention against the reads after S1).
 //   B   every CTA reads x_l (its own RMS scale r = 1/sqrt(mean(x^2) + eps) from it), sums the replicas in a
 //       fixed order and quantises x to int16; warp 0 forms logits r*S + bias and the same top-k routing on every
 //       CTA and its lanes at once issue TMA bulk copies (cp.async.bulk, mbarrier completion) of this CTA's 32
