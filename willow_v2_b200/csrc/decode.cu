@@ -11,10 +11,11 @@
 //       fixed order and quantises x to int16; warp 0 forms logits r*S + bias and the same top-k routing on every
 //       CTA and its lanes at once issue TMA bulk copies (cp.async.bulk, mbarrier completion) of this CTA's 32
 //       gate/up row pairs in two chunks; right after the routing barrier warp 1 issues its slice of down rows of
-//       all k+1 experts (off warp 0's path), so that the layer's whole expert stream is in flight together. CTA c < 144 owns h block c: 32 consecutive h
-//       values of one expert slot. Warps compute gate and up rows (dp2a on the 4-bit codes) -> SwiGLU; warp 0 quantises
-//       the block's 32 h values to int16 once and writes them to global memory in the order the down lanes read;
-//       the other warps unpack their Q6_K down codes into registers (independent of h).
+//       all k+1 experts (off warp 0's path), so that the layer's whole expert stream is in flight together.
+//       CTA c < 144 owns h block c: 32 consecutive h values of one expert slot. Warps compute gate and up rows
+//       (dp2a on the 4-bit codes) -> SwiGLU; warp 0 quantises the block's 32 h values to int16 once and writes
+//       them to global memory in the order the down lanes read; the other warps unpack their down codes (Q6_K, or
+//       Q4_K on a layer whose down matrices are Q4_K) into registers (independent of h).
 //   S2  all h blocks complete.
 //   C   every CTA copies the quantised h into shared memory, finishes its rows of the k+1 down products (dp2a on
 //       the unpacked codes), combines them in ascending expert id plus the gated shared expert (+ the residual),
