@@ -1,14 +1,20 @@
 """Benchmark of the qwen35moe MoE hot path on B200.
 
-Default workload: decode of one token through 40 stacked MoE layers of the config-0
-shapes (H 2048, 256 experts of FFN 512, top-8, Q4_K gate/up + Q6_K down, shared expert), residual + RMSNorm
-between layers, all 20.9 GB of expert weights resident in HBM. One step = one token through the 40 layers.
-Metric: tokens/s; the roofline line reports the expert-weight HBM bandwidth against the measured copy peak.
-At N > 1 GPUs (torchrun) every rank serves its own token stream with its own full store (decode does not shard:
-"replicas only"), value = total tokens/s over all ranks, time = max over ranks.
+Default workload (`--workload prefill4096`): one MoE layer on 4096 bf16 tokens with uniform
+routing (~128 tokens per expert) through the tensor-core router and the tcgen05 grouped GEMMs; tokens/s, with the
+gate_up GEMM launch against the measured bf16 tensor peak. At N > 1 GPUs (torchrun) it is expert-parallel: rank r
+holds 256/N experts and routes its own 4096 tokens per step (weak scaling), with the dispatch and combine
+all-to-alls over NCCL, so the scaling run measures the exchange. At N = 1 the line also carries "decode40", the
+configs[1] measurement below, taken on the same GPU in the same run.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload decode40|batch64|prefill4096|prefill32k|typed-decode] [--ggml-type T|all]
+                  [--workload prefill4096|decode40|batch64|prefill32k|typed-decode] [--ggml-type T|all]
+
+--workload decode40: decode of one token through 40 stacked MoE layers of the config-0
+shapes (H 2048, 256 experts of FFN 512, top-8, Q4_K gate/up + Q6_K down, shared expert), residual + RMSNorm between
+layers, all 20.9 GB of expert weights resident in HBM; one step = one token through the 40 layers; the roofline
+line reports the expert-weight HBM bandwidth against the measured copy peak. At N > 1 every rank serves its own
+token stream with its own full store (decode does not shard: "replicas only").
 
 --workload batch64: 64 f32 tokens through one MoE layer with Zipf-biased routing (the
 sliced router, the dispatch sort and the grouped GEMMs); tokens/s and HBM GB/s over the distinct experts each step
@@ -18,23 +24,18 @@ touches.
 expert store per GPU (experts over the cap stream from pinned host memory, the next layer prefetched); expert
 parallel under torchrun. Run with few steps: `--steps 3 --warmup 3`.
 
---workload prefill4096: one MoE layer on 4096 bf16 tokens with uniform routing (~128
-tokens per expert) through the tcgen05 grouped GEMMs; tokens/s, with the dominant GEMM launch against the measured
-bf16 tensor peak. At N > 1 it is expert-parallel (rank r holds 256/N experts, 4096 tokens per rank per step,
-NCCL all-to-all dispatch and combine).
-
 --workload typed-decode (the row of the other expert quant types): one token's 8 routed experts in a ggml type of
 willow's Metal path (gguf/metal.py:295), through gemv_batch + SwiGLU + gemv_combine as engines/base.py:492-532 runs
 them; one JSON line per type (1 GPU), with the gate_up launch against the measured HBM copy peak.
 
---impl reference times the CPU restatement of willow's own CPU path (the oracle port; willow's code cannot run
-on the GPU box) on the host cores, on a bounded sample of the same workload.
+--impl reference times the CPU restatement of willow's own CPU path (the oracle port) on the host cores, on rank 0;
+for prefill4096 and decode40 every step is the whole workload (a 4096-token layer, a 40-layer token), for batch64
+the whole 64-token block; it emits the same config as this arm. Defaults for it: 20 steps, 5 warm-up.
 """
 import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -80,53 +81,107 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def workload_config(workload: str, world: int, n_layers: int = LAYERS, type_name: str = "") -> dict:
+    """The `config` object of a workload's JSON line: the same dict for this GPU arm and for --impl reference at the
+    same N (it names the work, not what a run measured)."""
+    base = {"hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K}
+    if workload == "decode40":
+        return {"workload": ("configs[1]: decode 1 token x 40 MoE layers, all experts resident" if n_layers == LAYERS
+                             else f"profiling case: decode 1 token x {n_layers} layers (not the benchmark)"),
+                **base, "layers": n_layers, "tokens_per_step": 1,
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "l2": "inputs larger than L2: 734 MB of expert weights per step, a new token (new routing) each step"}
+    if workload == "batch64":
+        return {"workload": "configs[2]: 64 tokens through one MoE layer, Zipf-biased routing", **base,
+                "tokens_per_step": BATCH_T, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "l2": "16 batches cycled: each step re-routes (distinct experts per step in roofline_step)"}
+    if workload == "prefill4096":
+        if world == 1:
+            return {"workload": "configs[3]: prefill 4096 tokens through one MoE layer, uniform routing", **base,
+                    "tokens_per_step": PREFILL_T, "parallelism": "single GPU",
+                    "l2": "inputs larger than L2: 524 MB of expert weights and ~500 MB of activations per step"}
+        return {"workload": "configs[3]: prefill 4096 tokens per rank through one MoE layer, uniform routing", **base,
+                "tokens_per_step": PREFILL_T * world, "parallelism": f"ep{world}",
+                "experts_per_rank": EXPERTS // world,
+                "l2": "inputs larger than L2: ~500 MB of activations per rank per step"}
+    if workload == "prefill32k":
+        return {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, 4 GiB cap", **base,
+                "layers": n_layers, "tokens_per_step": PF32_T, "tokens_per_rank": PF32_T // world,
+                "parallelism": f"ep{world}" if world > 1 else "single GPU", "experts_per_rank": EXPERTS // world,
+                "store_cap_bytes": PF32_CAP, "store_slots": int(PF32_CAP // ((EXPERT_BYTES + 255) // 256 * 256)),
+                "hot_share": 0.75, "batches_cycled": 2,
+                "l2": "inputs larger than L2: 268 MB residual stream per rank and up to 21 GB of experts"}
+    if workload == "typed-decode":
+        return {"workload": f"typed-decode {type_name}: gemv_batch (gate_up [1024, 2048]) + SwiGLU + gemv_combine "
+                            "(down [2048, 512]) for 8 experts per step", "ggml_type": type_name,
+                "l2": "inputs larger than L2: each step reads 8 other experts of a >= 2 GB pool"}
+    raise ValueError(workload)
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+    """SM clocks and clock-event (throttle) reasons of the bench's GPU, read through NVML every ~2 ms on a thread
+    while the timed region runs, plus once on entry and once on exit, so that even a region of a few milliseconds
+    has samples. Reads only; no GPU setting is changed."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
     def __init__(self, device: int):
         self.device = device
-        self.proc = None
+        self.samples, self.max_mhz, self.reasons = [], None, set()
+        self.handle = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            prop = torch.cuda.get_device_properties(device)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except pynvml.NVMLError:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.nvml = pynvml
+        except Exception:
+            self.handle = None
+
+    def _sample(self):
+        n = self.nvml
+        self.samples.append(float(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)))
+        mask = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+        self.reasons |= {name for bit, name in self.REASONS.items() if mask & bit}
+
+    def _loop(self):
+        while not self.stop.wait(0.002):
+            try:
+                self._sample()
+            except Exception:
+                return
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.device)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+        if self.handle is not None:
+            import threading
+            try:
+                self.max_mhz = float(self.nvml.nvmlDeviceGetMaxClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+                self._sample()
+            except Exception:
+                self.handle = None
+                return self
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
+        if self.handle is not None:
+            self.stop.set()
+            self.thread.join()
             try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+                self._sample()
+            except Exception:
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = self.samples
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(sm), "source": "NVML, ~2 ms"}
 
 
 def setup_model(device: int, n_layers: int = LAYERS):
@@ -209,13 +264,7 @@ def run_decode40(args, rank: int, world: int, dist):
         "metric": METRIC, "value": world * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks with the config-0 distributions; random-init router)",
-        "config": {"workload": ("configs[1]: decode 1 token x 40 MoE layers, all experts resident" if n_layers == LAYERS
-                                else f"profiling case: decode 1 token x {n_layers} layers (not the benchmark)"),
-                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": n_layers,
-                   "tokens_per_step": 1,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2: 734 MB of expert weights per step, a new token (new routing) each "
-                         "step"},
+        "config": workload_config("decode40", world, n_layers),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": n_layers * TRAFFIC_PER_LAYER, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": expert_bytes,
@@ -317,15 +366,12 @@ def run_batch64(args, rank: int, world: int, dist):
         "metric": METRIC_BATCH, "value": world * T * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks; f32 N(0,1) tokens; Zipf(1.1) routing bias)",
-        "config": {"workload": "configs[2]: 64 tokens through one MoE layer, Zipf-biased routing",
-                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T,
-                   "distinct_experts_mean": mean_u,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": f"{nb} batches cycled: each step re-routes; ~{nbytes / 1e6:.0f} MB of weights per step"},
+        "config": workload_config("batch64", world),
         "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel<0> (gate_up + SwiGLU)", "achieved": gu_gbs,
                      "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": None, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms},
         "roofline_step": {"achieved": achieved, "frac": achieved / hbm, "algorithmic_bytes": nbytes,
+                          "distinct_experts_mean": mean_u,
                           "note": "whole step (all launches); bytes = distinct experts hit + shared + router"},
         "phase_ms": phase_ms,
         "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 4,
@@ -376,6 +422,14 @@ def cpu_baseline_pool():
     return _POOL, n
 
 
+def shutdown_cpu_pool():
+    """Stops the CPU-baseline pool before the interpreter exits (its exit hooks otherwise run on torn-down modules)."""
+    global _POOL
+    if _POOL is not None:
+        _POOL.shutdown(wait=True)
+        _POOL = None
+
+
 def _worker_init():
     from oracle import ggml_types as G
     from willow_v2_b200 import synth
@@ -419,6 +473,27 @@ def _ffn_task(task):
     return y if keep else float(y.sum())
 
 
+_SHM = {}
+
+
+def _shm_array(name: str, shape):
+    """A float32 array over a named shared-memory block (attached once per process)."""
+    from multiprocessing import shared_memory
+    if name not in _SHM:
+        _SHM[name] = shared_memory.SharedMemory(name=name)
+    return np.ndarray(shape, dtype=np.float32, buffer=_SHM[name].buf)
+
+
+def _prefill_task(task):
+    """One expert of a whole prefill layer: rows idx of the shared token matrix through its FFN, written to rows
+    [off, off + len(idx)) of the shared output matrix."""
+    blob, x_name, T, idx, y_name, P, off = task
+    x = _shm_array(x_name, (T, HIDDEN))
+    y = _shm_array(y_name, (P, HIDDEN))
+    y[off:off + len(idx)] = _ffn_task(("Q4_K/Q6_K", blob, x[idx], True))
+    return len(idx)
+
+
 def _warm(_):
     time.sleep(0.05)  # long enough that the 4n warm-up tasks spread over every worker (each past its initializer)
     return os.getpid()
@@ -434,7 +509,7 @@ def cpu_baseline_wall(tasks):
 
 def cpu_baseline_decode_layer(x_norm, router, layer_step: int):
     """One decode layer of the oracle port on the pool: router + top-8 in this process, the 8 routed experts and the
-    shared expert in parallel, then the combine in ascending expert id. Returns the seconds it took."""
+    shared expert in parallel, then the combine in ascending expert id. Returns (seconds it took, output)."""
     import oracle.moe_oracle as ora
     t0 = time.perf_counter()
     w, sel = ora.route(x_norm @ router.T)
@@ -448,7 +523,7 @@ def cpu_baseline_decode_layer(x_norm, router, layer_step: int):
     for j, y in zip(order, ys[:-1]):
         out += w[0, j] * y
     out += ys[-1]  # the shared expert (its sigmoid gate is a dot product: negligible)
-    return t_route + t_pool + (time.perf_counter() - t1)
+    return t_route + t_pool + (time.perf_counter() - t1), out
 
 
 def cpu_baseline_batch():
@@ -562,10 +637,7 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
         "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 accumulation",
         "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks with the config-0 distributions; bf16 N(0,1) tokens)",
-        "config": {"workload": "configs[3]: prefill 4096 tokens per rank through one MoE layer, uniform routing",
-                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T * world,
-                   "parallelism": f"ep{world}", "experts_per_rank": per,
-                   "l2": "inputs larger than L2: ~500 MB of activations per rank per step"},
+        "config": workload_config("prefill4096", world),
         "roofline": {"bound": "tensor",
                      "kernel": "expert stages (dispatch + gather + grouped GEMMs, all chunks), rank 0",
                      "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16, "traffic": None,
@@ -693,13 +765,7 @@ def run_prefill32k(args, rank: int, world: int, dist):
         "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 accumulation",
         "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks; bf16 N(0,1) tokens; per-layer Zipf(1.1) routing bias)",
-        "config": {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, 4 GiB cap",
-                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": n_layers,
-                   "tokens_per_step": PF32_T, "tokens_per_rank": T,
-                   "parallelism": f"ep{world}" if world > 1 else "single GPU", "experts_per_rank": per,
-                   "store_cap_bytes": PF32_CAP, "store_slots": int(PF32_CAP // ((EXPERT_BYTES + 255) // 256 * 256)),
-                   "hot_share": 0.75, "batches_cycled": 2,
-                   "l2": "inputs larger than L2: 268 MB residual stream per rank and up to 21 GB of experts"},
+        "config": workload_config("prefill32k", world, n_layers),
         "roofline": {"bound": "tensor", "kernel": "whole 40-layer step (expert products / step time), rank 0",
                      "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16, "traffic": None,
                      "peak_kind": peak_kind, "algorithmic_flops_per_launch": flops, "launch_ms": ms},
@@ -806,10 +872,7 @@ def run_prefill4096(args, rank: int, world: int, dist):
         "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 accumulation",
         "data": "synthetic (seeded GGUF Q4_K/Q6_K blocks with the config-0 distributions; bf16 N(0,1) tokens)",
-        "config": {"workload": "configs[3]: prefill 4096 tokens through one MoE layer, uniform routing",
-                   "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "tokens_per_step": T,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2: 524 MB of expert weights and ~500 MB of activations per step"},
+        "config": workload_config("prefill4096", world),
         "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel<0> (gate_up + SwiGLU)",
                      "achieved": gu_tflops, "peak": bf16, "unit": "TFLOP/s", "frac": gu_tflops / bf16,
                      "traffic": PREFILL_GATE_UP_TRAFFIC, "peak_kind": peak_kind,
@@ -850,6 +913,69 @@ def cpu_baseline_prefill(sample_experts: int = 0, tokens_per_expert: int = 144):
                       f"scaled to {rows} token-expert rows"}
 
 
+def cpu_decode_token(h, routers, step: int) -> float:
+    """One whole decode token of the oracle port: 40 layers of rms_norm, router + top-8, the 9 experts in parallel on
+    the pool, combine and residual, each layer fed by the last. Returns the seconds it took."""
+    import oracle.moe_oracle as ora
+    t = 0.0
+    for l, router in enumerate(routers):
+        t0 = time.perf_counter()
+        xn = ora.rms_norm(h)
+        t += time.perf_counter() - t0
+        dt, out = cpu_baseline_decode_layer(xn, router, step * LAYERS + l)
+        t0 = time.perf_counter()
+        h = h + out
+        t += dt + time.perf_counter() - t0
+    return t
+
+
+_PF_SHM = []
+
+
+def cpu_prefill_layer(x, router) -> float:
+    """One whole prefill layer of the oracle port on the pool (4096 tokens): the router and top-8 on every token, each
+    of the 256 routed experts on its tokens and the shared expert on all of them (split over the workers), every
+    expert dequantised from GGUF bytes (stand-in blobs of the same sizes), outputs in shared memory, then the
+    combine in ascending expert id plus the gated shared expert. Returns the seconds it took."""
+    import oracle.moe_oracle as ora
+    from multiprocessing import shared_memory
+    pool, workers = cpu_baseline_pool()
+    T = x.shape[0]
+    P = T * (TOP_K + 1)
+    if not _PF_SHM:
+        import atexit
+        for nbytes in (T * HIDDEN * 4, P * HIDDEN * 4):
+            _PF_SHM.append(shared_memory.SharedMemory(create=True, size=nbytes))
+        atexit.register(lambda: [(m.close(), m.unlink()) for m in _PF_SHM])
+    xs, ys = _PF_SHM
+    np.ndarray((T, HIDDEN), np.float32, buffer=xs.buf)[:] = x
+    y = np.ndarray((P, HIDDEN), np.float32, buffer=ys.buf)
+    t0 = time.perf_counter()
+    logits = x @ router.T
+    w, sel = ora.route(logits[:, :EXPERTS])
+    flat = sel.reshape(-1)
+    order = np.argsort(flat, kind="stable")  # pairs grouped by expert, tokens ascending within an expert
+    counts = np.bincount(flat, minlength=EXPERTS)
+    starts = np.concatenate([[0], np.cumsum(counts)])
+    tasks = [(e % N_BLOBS, xs.name, T, (order[starts[e]:starts[e + 1]] // TOP_K).astype(np.int32), ys.name, P,
+              int(starts[e])) for e in range(EXPERTS) if counts[e]]
+    chunk = -(-T // workers)
+    tasks += [(0, xs.name, T, np.arange(c, min(T, c + chunk), dtype=np.int32), ys.name, P, T * TOP_K + c)
+              for c in range(0, T, chunk)]
+    list(pool.map(_prefill_task, tasks))
+    pos = np.empty(T * TOP_K, np.int64)
+    pos[order] = np.arange(T * TOP_K)
+    pos = pos.reshape(T, TOP_K)
+    asc = np.argsort(sel, axis=1, kind="stable")
+    out = np.zeros((T, HIDDEN), np.float32)
+    rows = np.arange(T)
+    for j in range(TOP_K):
+        k = asc[:, j]
+        out += w[rows, k, None] * y[pos[rows, k]]
+    out += ora.sigmoid(logits[:, EXPERTS:EXPERTS + 1]) * y[T * TOP_K:]
+    return time.perf_counter() - t0
+
+
 def cpu_baseline(sample_layers: int = 4):
     """willow's CPU path restated (the oracle port) on every host core: per layer the router + top-8, the 9 experts'
     dequantisation from GGUF bytes and FFN in parallel on the pool, the combine; tokens/s scaled to the 40-layer
@@ -860,7 +986,7 @@ def cpu_baseline(sample_layers: int = 4):
     h = synth.hidden(SEED, 1, step=123)
     total = 0.0
     for l in range(sample_layers):
-        total += cpu_baseline_decode_layer(ora.rms_norm(h), synth.router_weight(SEED, l), l)
+        total += cpu_baseline_decode_layer(ora.rms_norm(h), synth.router_weight(SEED, l), l)[0]
     per_layer = total / sample_layers
     return {"value": 1.0 / (per_layer * LAYERS), "unit": "tokens/s", "cores": workers, "kind": "port",
             "sample": f"{sample_layers} of the 40 layers of one decode token (router + top-8; 9 experts dequantised "
@@ -881,10 +1007,7 @@ def run_reference(args, rank, world):
         return {"metric": METRIC_PF32, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": PF32_T / value * 1e3, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-                "config": {"workload": "configs[4]: prefill 32768 tokens through 40 MoE layers, Zipf routing, "
-                                       "4 GiB cap",
-                           "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K, "layers": LAYERS,
-                           "tokens_per_step": PF32_T},
+                "config": workload_config("prefill32k", world),
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"], "kind": "port",
                                  "sample": "each step: " + base["sample"] + "; divided by 40 layers"},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -896,54 +1019,56 @@ def run_reference(args, rank, world):
         return {"metric": METRIC_BATCH, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": BATCH_T / value * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-                "config": {"workload": "configs[2]: 64 tokens through one MoE layer, Zipf-biased routing",
-                           "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
-                           "tokens_per_step": BATCH_T},
+                "config": workload_config("batch64", world),
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"], "kind": "port",
                                  "sample": "each step: " + base["sample"]},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload == "prefill4096":
-        K, W = args.steps, args.warmup
-        n = cpu_baseline_pool()[1]  # one expert per worker each step
-        vals = [cpu_baseline_prefill(sample_experts=n)["value"] for _ in range(W + K)][W:]
-        value = statistics.mean(vals)
-        base = cpu_baseline_prefill(sample_experts=n)
-        return {"metric": METRIC_PREFILL, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
-                "warmup": W, "ms_per_step": PREFILL_T / value * 1e3, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-                "config": {"workload": "configs[3]: prefill 4096 tokens through one MoE layer, uniform routing",
-                           "hidden": HIDDEN, "experts": EXPERTS, "ffn": FFN, "top_k": TOP_K,
-                           "tokens_per_step": PREFILL_T},
-                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": base["cores"], "kind": "port",
-                                 "sample": "each step: " + base["sample"]},
-                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    import oracle.moe_oracle as ora
+        res = reference_prefill4096(args.steps, args.warmup, world)
+        if world == 1 and not args.no_decode40:
+            res["decode40"] = reference_decode40(min(args.steps, 8), 1, world)
+        return res
+    return reference_decode40(args.steps, args.warmup, world)
+
+
+def reference_decode40(K: int, W: int, world: int) -> dict:
+    """The reference arm for configs[1]: every step is one whole 40-layer token of the oracle port (cpu_decode_token),
+    so ms_per_step x steps is the time measured."""
     from willow_v2_b200 import synth
-    K, W = args.steps, args.warmup
     _, workers = cpu_baseline_pool()
-    # each step: one layer of one new token (router + top-8, its 9 experts in parallel on the pool, the combine);
-    # a token = 40 steps
-    routers = {}
-    times = []
-    for s in range(W + K):
-        layer = s % LAYERS
-        if layer not in routers:
-            routers[layer] = synth.router_weight(SEED, layer)
-        x = ora.rms_norm(synth.hidden(SEED, 1, step=10_000 + s))
-        dt = cpu_baseline_decode_layer(x, routers[layer], s)
-        if s >= W:
-            times.append(dt)
-    sec = LAYERS * statistics.mean(times)
+    routers = [synth.router_weight(SEED, l) for l in range(LAYERS)]
+    times = [cpu_decode_token(synth.hidden(SEED, 1, step=10_000 + s), routers, s) for s in range(W + K)][W:]
+    sec = statistics.mean(times)
     value = 1.0 / sec
     return {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "configs[1]: decode 1 token x 40 MoE layers", "hidden": HIDDEN, "experts": EXPERTS,
-                       "ffn": FFN, "top_k": TOP_K, "layers": LAYERS},
+            "dtype": "f32", "data": "synthetic", "impl": "reference", "config": workload_config("decode40", world),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
-                             "sample": f"each step: one layer of a new token: router + top-8, the 9 experts "
-                                       f"dequantised from GGUF bytes and run in parallel on {workers} worker "
-                                       f"processes, combine (numpy float32); token time = 40 x the mean step"},
+                             "sample": f"each step one whole token: 40 layers of rms_norm, router + top-8, the 9 "
+                                       f"experts dequantised from GGUF bytes (stand-in blobs of the same sizes) and "
+                                       f"run in parallel on {workers} worker processes, combine, residual (numpy "
+                                       f"float32)"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def reference_prefill4096(K: int, W: int, world: int) -> dict:
+    """The reference arm for configs[3]: every step is one whole 4096-token layer of the oracle port
+    (cpu_prefill_layer); 4 batches cycled like the GPU arm."""
+    from willow_v2_b200 import synth
+    _, workers = cpu_baseline_pool()
+    router = np.vstack([synth.router_weight(SEED, 0), synth.shared_gate_weight(SEED, 0).reshape(1, -1)])
+    xs = [synth.hidden(SEED, PREFILL_T, step=b) for b in range(4)]
+    times = [cpu_prefill_layer(xs[s % 4], router) for s in range(W + K)][W:]
+    sec = statistics.mean(times)
+    value = PREFILL_T / sec
+    return {"metric": METRIC_PREFILL, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference", "config": workload_config("prefill4096", world),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
+                             "sample": f"each step one whole layer of {PREFILL_T} tokens: router + top-8 on every "
+                                       f"token, the 256 routed experts on their tokens and the shared expert on all, "
+                                       f"each dequantised from GGUF bytes (stand-in blobs of the same sizes), in "
+                                       f"parallel on {workers} worker processes (numpy float32), combine"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -1072,11 +1197,9 @@ def run_typed_decode(args, type_name: str):
         "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 (f32 sums)",
         "data": f"synthetic: random {type_name} blocks with fp16 scales U[1e-3, 4e-3]; bf16 N(0,1) token",
-        "config": {"workload": f"typed-decode {type_name}: gemv_batch (gate_up [1024, 2048]) + SwiGLU + gemv_combine "
-                               "(down [2048, 512]) for 8 experts per step",
-                   "ggml_type": type_name, "expert_bytes": eb, "pool_experts": pool, "pool_bytes": pool * eb,
-                   "l2": "inputs larger than L2: each step reads 8 other experts of the >= 2 GB pool",
-                   "timing": f"CUDA graphs of {G} steps replayed {reps} times; events around the replays"},
+        "config": workload_config("typed-decode", 1, type_name=type_name),
+        "pool": {"expert_bytes": eb, "pool_experts": pool, "pool_bytes": pool * eb,
+                 "timing": f"CUDA graphs of {G} steps replayed {reps} times; events around the replays"},
         "roofline": {"bound": "hbm", "kernel": "ggml_gemv_kernel (gemv_batch of the 8 gate_up matrices)",
                      "achieved": gu_gbs, "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm,
                      "traffic": TYPED_TRAFFIC.get(type_name), "peak_kind": peak_kind,
@@ -1109,15 +1232,21 @@ def cpu_baseline_typed(type_name: str):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None, help="default 2000 (reference arm: 20)")
+    ap.add_argument("--warmup", type=int, default=None, help="default 50 (reference arm: 5)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode40",
+    ap.add_argument("--workload", default="prefill4096",
                     choices=["decode40", "batch64", "prefill4096", "prefill32k", "typed-decode"])
     ap.add_argument("--ggml-type", default="all", help="typed-decode: one ggml type, or all (one JSON line each)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS, help="stack depth (40 = the benchmark; fewer = profiling)")
+    ap.add_argument("--no-decode40", action="store_true",
+                    help="prefill4096 at N=1: skip the decode40 measurement attached to the line")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 20 if args.impl == "reference" else 2000
+    if args.warmup is None:
+        args.warmup = 5 if args.impl == "reference" else 50
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1134,16 +1263,17 @@ def main():
                     "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                     "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                     "dtype": "f32", "data": "synthetic", "impl": "reference",
-                    "config": {"workload": f"typed-decode {t}: 8 experts' gate_up [1024, 2048] + SwiGLU + down "
-                                           "[2048, 512]", "ggml_type": t},
+                    "config": workload_config("typed-decode", 1, type_name=t),
                     "cpu_baseline": base,
                     "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
                     flush=True)
+        shutdown_cpu_pool()
         return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
             print(json.dumps(res), flush=True)
+        shutdown_cpu_pool()
         return
     import torch
     torch.cuda.set_device(local)
@@ -1161,11 +1291,19 @@ def main():
             if not args.no_cpu_baseline:
                 result["cpu_baseline"] = cpu_baseline_typed(t)
             print(json.dumps(result), flush=True)
+        shutdown_cpu_pool()
         return
     if args.workload == "prefill4096":
         result, _keep = run_prefill4096(args, rank, world, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline_prefill()
+        if world == 1 and not args.no_decode40:
+            # configs[1] on the same GPU, its own line attached: the 40-layer single-token decode (HBM roofline)
+            del _keep
+            torch.cuda.empty_cache()
+            d40, _keep = run_decode40(args, rank, world, dist)
+            result["decode40"] = {k: d40[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "warmup",
+                                                     "config", "roofline", "e2e", "gpu_launches", "clocks")}
     elif args.workload == "prefill32k":
         result, _keep = run_prefill32k(args, rank, world, dist)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1180,6 +1318,7 @@ def main():
             result["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(result), flush=True)
+    shutdown_cpu_pool()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

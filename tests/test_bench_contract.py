@@ -36,10 +36,32 @@ def check_line(r):
 
 @pytest.mark.parametrize("workload", ["decode40", "batch64", "prefill4096", "prefill32k"])
 def test_reference_arm_line(workload):
-    lines = run_bench("--impl", "reference", "--workload", workload, "--steps", "1", "--warmup", "3")
+    import bench
+    args = ("--no-decode40",) if workload == "prefill4096" else ()
+    lines = run_bench("--impl", "reference", "--workload", workload, "--steps", "1", "--warmup", "3", *args)
     assert len(lines) == 1
     check_line(lines[0])
     assert lines[0]["unit"] == "tokens/s"
+    # the same config object as the GPU arm at the same N, so the two lines name the same work
+    assert lines[0]["config"] == json.loads(json.dumps(bench.workload_config(workload, 1)))
+
+
+def test_reference_arm_default_is_whole_steps():
+    """The default workload (prefill4096) at N=1 times one whole 4096-token layer per step and attaches the
+    decode40 arm (whole 40-layer tokens); the ms per step is what was measured (steps x ms fits the run)."""
+    import time
+    t0 = time.perf_counter()
+    lines = run_bench("--impl", "reference", "--steps", "1", "--warmup", "3")
+    wall = time.perf_counter() - t0
+    assert len(lines) == 1
+    r = lines[0]
+    check_line(r)
+    assert r["config"]["workload"].startswith("configs[3]")
+    d = r["decode40"]
+    check_line(d)
+    assert d["config"]["workload"].startswith("configs[1]")
+    assert (r["steps"] + r["warmup"]) * r["ms_per_step"] / 1e3 < wall
+    assert (d["steps"] + d["warmup"]) * d["ms_per_step"] / 1e3 < wall
 
 
 def test_reference_arm_typed_decode():
@@ -52,6 +74,6 @@ def test_reference_arm_typed_decode():
 
 def test_reference_arm_other_ranks_are_silent():
     """Under torchrun only rank 0 runs the reference arm; the others exit 0 without work."""
-    lines = run_bench("--impl", "reference", "--steps", "1", "--warmup", "3",
+    lines = run_bench("--impl", "reference", "--steps", "1", "--warmup", "3", "--no-decode40",
                       env={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert lines == []
