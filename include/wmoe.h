@@ -82,6 +82,12 @@ int wmoe_set_decode_kernel(wmoe_ctx* ctx, int enable);
  * weights for each of its tokens.)
  * Returns the previous value (or WMOE_ERR_INVALID for tokens < 1). */
 int wmoe_set_prefill_threshold(wmoe_ctx* ctx, int tokens);
+/* willow's --min-expert-weight (Engine.skip_small_experts, engines/base.py:413-429; main.py:37,108): with
+ * weight > 0 every routing of this context keeps each token's top pick and its picks of renormalised weight >=
+ * weight, scaled back up to the picks' former total; the others are dropped. Dropped picks come back as -1 in
+ * topk_idx_out and with weight 0 in topk_w_out (wmoe_route: weight 0, id kept); their experts' outputs are added
+ * with weight 0, which leaves the block's output what it is without them. weight in [0, 1); 0 (default) is off. */
+int wmoe_set_min_expert_weight(wmoe_ctx* ctx, float weight);
 /* Phase tracing of the persistent decode kernel (the role of willow's per-section Engine.tick timings,
  * engines/base.py:384-390): with trace non-null, each CTA writes %globaltimer nanoseconds at WMOE_TRACE_POINTS
  * points of every layer into trace[(layer * WMOE_TRACE_POINTS + point) * ctas + cta] (device memory of at least

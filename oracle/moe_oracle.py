@@ -15,6 +15,7 @@ What each function restates (paths within the willow-v2 project):
   shared_expert  engines/base.py:104-107 (shared_expert_gate.weight [1, H], engines/qwen36/loader.py:127-128)
   moe            engines/base.py:445-490 with each_expert's sum, base.py:534-591 (experts added in ascending id
                  order with index_add_, then the shared expert)
+  skip_small_experts  engines/base.py:413-429 (min_expert_weight; dropped picks become -1)
   rms_norm       engines/base.py:27-32 (zero-centred, weight 0 -> scale 1) and the residual wiring of
                  engines/qwen36/model.py:17-22
 """
@@ -109,18 +110,31 @@ def shared_expert(x, gate_w, up_w, down_w, shared_gate_w):
     return sigmoid(x @ shared_gate_w.reshape(1, -1).T) * h
 
 
-def moe(x, router_w, expert_weights, shared, shared_gate_w, router_bias=None, top_k=8):
+def skip_small_experts(w: np.ndarray, sel: np.ndarray, min_weight: float):
+    """engines/base.py:413-429: keeps each token's top pick (column 0, the largest) and the picks whose weight is
+    >= min_weight, scales the kept weights back up to the former total; dropped picks get selected -1."""
+    keep = w >= min_weight
+    keep[:, 0] = True
+    kept = w * keep
+    kept = kept * (w.sum(axis=-1, keepdims=True) / kept.sum(axis=-1, keepdims=True))
+    return kept.astype(np.float32), np.where(keep, sel, -1)
+
+
+def moe(x, router_w, expert_weights, shared, shared_gate_w, router_bias=None, top_k=8, min_expert_weight=0.0):
     """One MoE block, engines/base.py:445-490 on the CPU path (each_expert, base.py:534-591).
     x: float32 [T, H]. expert_weights(e) -> (gate_up float32 [2F, H], down float32 [H, F]).
     shared: (gate_up float32 [2F, H], down float32 [H, F]) of the shared expert.
+    min_expert_weight > 0: skip_small_experts first (base.py:463-464).
     Returns (out [T, H] float32, routing weights [T, k], selected [T, k])."""
     x = x.astype(np.float32)
     logits = x @ router_w.T
     if router_bias is not None:
         logits = logits + router_bias
     w, sel = route(logits, top_k)
+    if min_expert_weight:
+        w, sel = skip_small_experts(w, sel, min_expert_weight)
     out = np.zeros_like(x)
-    for e in np.unique(sel):  # ascending expert id, as each_expert sums them (base.py:580-586)
+    for e in np.unique(sel[sel >= 0]):  # ascending expert id, as each_expert sums them (base.py:580-586)
         tok, slot = np.nonzero(sel == e)
         gu, dn = expert_weights(int(e))
         h = expert_gate(x[tok] @ gu.T) @ dn.T

@@ -95,3 +95,18 @@ def test_synthetic_distributions():
     # partial-row generation is a slice of the whole tensor
     full = synth.expert_down(3, 1, 2)
     np.testing.assert_array_equal(synth.expert_down(3, 1, 2, rows=(100, 140)), full[100:140])
+
+
+def test_skip_small_experts_matches_reference():
+    """ora.skip_small_experts against willow's Engine.skip_small_experts (engines/base.py:413-429) on 256 routings
+    and four thresholds (tests/golden/make_golden_skip.py): the same picks dropped, the kept weights rescaled."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "skip.npz"))
+    dropped = 0
+    for m in (0.05, 0.1, 0.125, 0.2):
+        w, sel = ora.skip_small_experts(g["w"], g["sel"], m)
+        np.testing.assert_array_equal(sel, g[f"sel_{m}"])
+        np.testing.assert_allclose(w, g[f"w_{m}"], rtol=1e-6, atol=0)
+        dropped += int((sel < 0).sum())
+    assert dropped > 0
+

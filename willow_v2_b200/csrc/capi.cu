@@ -167,6 +167,14 @@ int wmoe_set_prefill_threshold(wmoe_ctx* ctx, int tokens) {
   return prev;
 }
 
+int wmoe_set_min_expert_weight(wmoe_ctx* ctx, float weight) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!(weight >= 0.f && weight < 1.f))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_set_min_expert_weight: the weight must lie in [0, 1)");
+  ctx->min_expert_weight = weight;
+  return WMOE_OK;
+}
+
 int wmoe_set_decode_kernel(wmoe_ctx* ctx, int enable) {
   if (!ctx) return WMOE_ERR_INVALID;
   const int prev = ctx->use_decode_kernel ? 1 : 0;
@@ -214,10 +222,10 @@ static size_t router_logit_floats(bool tc, int T, int E, int H) {
   if (T > 8) return size_t(router_slice_outputs(T, H)) * T * E;
   return size_t(T) * (E + 1);
 }
-static cudaError_t route_tokens(bool tc, const void* x, int x_dtype, int T, int H, int E, int k, const float* router_w,
-                                const float* router_bias, const float* shared_gate, const void* router_split,
-                                float* logits, float* topk_w, int32_t* topk_idx, float* shared_s, int* status,
-                                cudaStream_t st, int* n, float* logits_out = nullptr) {
+static cudaError_t route_topk(bool tc, const void* x, int x_dtype, int T, int H, int E, int k, const float* router_w,
+                              const float* router_bias, const float* shared_gate, const void* router_split,
+                              float* logits, float* topk_w, int32_t* topk_idx, float* shared_s, int* status,
+                              cudaStream_t st, int* n, float* logits_out) {
   cudaError_t e;
   if (tc) {
     if ((e = router_logits_tc(x, T, H, E, router_split, logits, status, st, n)) != cudaSuccess) return e;
@@ -231,6 +239,24 @@ static cudaError_t route_tokens(bool tc, const void* x, int x_dtype, int T, int 
   }
   if ((e = router_logits(x, x_dtype, T, H, E, router_w, shared_gate, logits, st, n)) != cudaSuccess) return e;
   return router_topk(logits, T, E, k, router_bias, topk_w, topk_idx, shared_s, logits_out, st, n);
+}
+// The routing of every multi-token path: route_topk, then willow's skip_small_experts when min_w > 0 (the dropped
+// picks keep their ids internally, with weight 0).
+static cudaError_t route_tokens(bool tc, const void* x, int x_dtype, int T, int H, int E, int k, const float* router_w,
+                                const float* router_bias, const float* shared_gate, const void* router_split,
+                                float* logits, float* topk_w, int32_t* topk_idx, float* shared_s, int* status,
+                                cudaStream_t st, int* n, float min_w, float* logits_out = nullptr) {
+  const cudaError_t e = route_topk(tc, x, x_dtype, T, H, E, k, router_w, router_bias, shared_gate, router_split, logits,
+                                   topk_w, topk_idx, shared_s, status, st, n, logits_out);
+  if (e != cudaSuccess) return e;
+  return skip_small_experts(topk_w, T, k, min_w, st, n);
+}
+
+// A caller's copy of the picks: -1 where skip_small_experts dropped one (as willow marks them), else the ids.
+static cudaError_t copy_picks(const int32_t* topk_idx, const float* topk_w, int32_t* out, int n, float min_w,
+                              cudaStream_t st, int* launches) {
+  if (min_w > 0.f) return mark_dropped(topk_idx, topk_w, out, n, st, launches);
+  return cudaMemcpyAsync(out, topk_idx, size_t(n) * sizeof(int32_t), cudaMemcpyDeviceToDevice, st);
 }
 
 int wmoe_route(wmoe_ctx* ctx, const void* x, int x_dtype, int T, int hidden, int experts, int top_k,
@@ -252,7 +278,7 @@ int wmoe_route(wmoe_ctx* ctx, const void* x, int x_dtype, int T, int hidden, int
   WMOE_CHECK_CUDA(ctx,
                   route_tokens(false, x, x_dtype, T, hidden, experts, top_k, router_w, router_bias, shared_gate,
                                nullptr, at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status, st, &n,
-                               logits),
+                               ctx->min_expert_weight, logits),
                   "router");
   ctx->launches += uint64_t(n);
   return WMOE_OK;
@@ -471,7 +497,8 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
     const cudaError_t e = decode_persistent(store_source(store, layer, shared_gate_up, shared_down), &down_type,
                                             layer, 1, &dl, H, F, E, top_k, 0.f, false, x, x_dtype, out, out_dtype,
                                             topk_idx_out, topk_w_out, ctx->scratch, ctx->decode_ctas,
-                                            ctx->d_status, ctx->trace, ctx->trace_entries, st, &n);
+                                            ctx->d_status, ctx->trace, ctx->trace_entries, st, &n,
+                                            ctx->min_expert_weight);
     ctx->launches += uint64_t(n);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel");
     return WMOE_OK;
@@ -523,7 +550,8 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   float* shared_s = at<float>(ctx, o_s);
   WMOE_CHECK_CUDA(ctx,
                   route_tokens(router_tc, x, x_dtype, T, H, E, k, router_w, router_bias, shared_gate, router_split,
-                               at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status, st, &n),
+                               at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status, st, &n,
+                               ctx->min_expert_weight),
                   "router");
   mark(1);
   std::vector<int32_t> experts_used;
@@ -584,8 +612,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   }
   if (marks) ++ctx->profile_seq;
   if (topk_idx_out)
-    WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_idx_out, topk_idx, size_t(T) * k * sizeof(int32_t),
-                                         cudaMemcpyDeviceToDevice, st),
+    WMOE_CHECK_CUDA(ctx, copy_picks(topk_idx, topk_w, topk_idx_out, T * k, ctx->min_expert_weight, st, &n),
                     "routing copy");
   if (topk_w_out)
     WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_w_out, topk_w, size_t(T) * k * sizeof(float), cudaMemcpyDeviceToDevice, st),
@@ -647,7 +674,7 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
   WMOE_CHECK_CUDA(ctx,
                   route_tokens(tc, x, x_dtype, T, hidden, experts, top_k, w->router_w, w->router_bias, w->shared_gate,
                                w->router_split, at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status,
-                               st, &n),
+                               st, &n, ctx->min_expert_weight),
                   "router");
   WMOE_CHECK_CUDA(ctx,
                   ep_plan(topk_idx, T, top_k, experts, world, send_rows, send_pairs, 1, send_tok, pair_list,
@@ -1011,7 +1038,7 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
     WMOE_CHECK_CUDA(ctx,
                     route_tokens(tc, x, x_dtype, T, H, E, k, w->router_w, w->router_bias, w->shared_gate,
                                  w->router_split, at<float>(ctx, o_logits), topk_w, topk_idx, shared_s, ctx->d_status,
-                                 st, &n),
+                                 st, &n, ctx->min_expert_weight),
                     "router");
   for (int c = 0; c < C; ++c) {
     const int t0 = chunk_begin(c), tn = chunk_begin(c + 1) - t0;
@@ -1127,8 +1154,7 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   }
   if (T > 0) {
     if (topk_idx_out)
-      WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_idx_out, topk_idx, size_t(T) * k * sizeof(int32_t),
-                                           cudaMemcpyDeviceToDevice, st),
+      WMOE_CHECK_CUDA(ctx, copy_picks(topk_idx, topk_w, topk_idx_out, T * k, ctx->min_expert_weight, st, &n),
                       "routing copy");
     if (topk_w_out)
       WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(topk_w_out, topk_w, size_t(T) * k * sizeof(float), cudaMemcpyDeviceToDevice,
@@ -1169,7 +1195,7 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
                                           reinterpret_cast<const DecodeLayer*>(layers), store->hidden, store->ffn,
                                           store->experts, 8, eps, true, h_in, WMOE_F32, h_out, WMOE_F32, topk_idx_out,
                                           nullptr, ctx->scratch, ctx->decode_ctas, ctx->d_status, ctx->trace,
-                                          ctx->trace_entries, st, &n);
+                                          ctx->trace_entries, st, &n, ctx->min_expert_weight);
   ctx->launches += uint64_t(n);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack");
   return WMOE_OK;
@@ -1217,7 +1243,7 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
                                           reinterpret_cast<const DecodeLayer*>(layers), store->hidden, store->ffn,
                                           store->experts, 8, eps, true, h_in, WMOE_F32, h_out, WMOE_F32, topk_idx_out,
                                           nullptr, scratch, ctx->decode_ctas, ctx->d_status, nullptr, 0,
-                                          static_cast<cudaStream_t>(stream), &n);
+                                          static_cast<cudaStream_t>(stream), &n, ctx->min_expert_weight);
   ctx->launches += uint64_t(n);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack_noalloc");
   return WMOE_OK;

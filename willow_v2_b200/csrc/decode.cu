@@ -73,6 +73,7 @@ struct DecodeParams {
   int dn_chunk;     // bytes reserved per slot for this CTA's down rows
   unsigned long long* trace;  // phase timestamps [layer][point][cta], or null
   unsigned char down_q4[kMaxLayers];  // 1: the layer's down matrices are Q4_K (else Q6_K)
+  float min_w;      // willow's min_expert_weight (0: off)
   DecodeLayer layers[kMaxLayers];
 };
 
@@ -623,10 +624,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       float sum = my_ex;
 #pragma unroll
       for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);  // lanes 0..7
+      // willow's skip_small_experts (engines/base.py:413-429): keep the top pick (lane 0) and the picks >= min_w,
+      // scaled back up to the former total; a dropped pick keeps its expert with weight 0
+      float my_w = lane < kK ? my_ex / sum : 0.f;
+      if (p.min_w > 0.f) {
+        const bool keep = lane == 0 || my_w >= p.min_w;
+        float total = my_w, kept = keep ? my_w : 0.f;
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+          total += __shfl_xor_sync(0xffffffffu, total, o);
+          kept += __shfl_xor_sync(0xffffffffu, kept, o);
+        }
+        my_w = keep ? my_w * (total / kept) : 0.f;
+      }
       if (lane < kK) {
-        sm.w[lane] = my_ex / sum;
-        if (c == 0 && p.topk_idx_out) p.topk_idx_out[li * kK + lane] = my_e;
-        if (c == 0 && p.topk_w_out) p.topk_w_out[li * kK + lane] = my_ex / sum;
+        sm.w[lane] = my_w;
+        if (c == 0 && p.topk_idx_out) p.topk_idx_out[li * kK + lane] = my_w == 0.f ? -1 : my_e;
+        if (c == 0 && p.topk_w_out) p.topk_w_out[li * kK + lane] = my_w;
         int rank = 0;
         for (int o = 0; o < kK; ++o) rank += __shfl_sync(0x000000ffu, my_e, o) < my_e ? 1 : 0;
         sm.order[rank] = lane;
@@ -903,7 +917,7 @@ cudaError_t decode_persistent(const ExpertSource& src, const int* down_types, in
                               const DecodeLayer* layers, int H, int F, int E, int k, float eps, bool stack,
                               const void* x_in, int x_dtype, void* out, int out_dtype, int32_t* topk_idx_out,
                               float* topk_w_out, void* scratch, int num_ctas, int* status, uint64_t* trace,
-                              size_t trace_entries, cudaStream_t st, int* launches) {
+                              size_t trace_entries, cudaStream_t st, int* launches, float min_w) {
   if (H != kH || F != kF || E != kE || k != kK || num_ctas < kHBlocks) return cudaErrorInvalidValue;
   for (int i = 0; i < n_layers; ++i) {
     if (down_types[i] != kGgmlQ6K && down_types[i] != kGgmlQ4K) return cudaErrorInvalidValue;
@@ -943,6 +957,7 @@ cudaError_t decode_persistent(const ExpertSource& src, const int* down_types, in
     p.bar = bar;
     p.status = status;
     p.dn_chunk = down_chunk_bytes(num_ctas);
+    p.min_w = min_w;
     p.trace = l0 == 0 ? reinterpret_cast<unsigned long long*>(trace) : nullptr;
     for (int i = 0; i < p.n_layers; ++i) {
       p.layers[i] = layers[l0 + i];

@@ -72,6 +72,12 @@ cudaError_t router_topk_split(const float* logits, int splits, int T, int E, int
                               int32_t* topk_idx, float* shared_s, float* logits_out, const void* x, int x_dtype,
                               const float* g, int H, cudaStream_t st, int* launches);
 
+// willow's skip_small_experts on topk_w [T, k] in place (no-op for min_w <= 0): each token keeps its top pick and
+// the picks of weight >= min_w, rescaled to the former total; dropped picks get weight 0 (their ids are kept).
+cudaError_t skip_small_experts(float* topk_w, int T, int k, float min_w, cudaStream_t st, int* launches);
+// out = idx with -1 where w == 0 (the picks skip_small_experts dropped)
+cudaError_t mark_dropped(const int32_t* idx, const float* w, int32_t* out, int n, cudaStream_t st, int* launches);
+
 // More than 8 tokens: float32 logits without the shared gate as router_slice_outputs(T, H) partial sums [n][T][E]
 // over 128-wide K slices (one sum of all slices for large T), added in order by router_topk_split, which also forms
 // the shared-gate logit. A token's logits do not depend on the other tokens of the call. H a multiple of 128.
@@ -170,7 +176,7 @@ cudaError_t decode_persistent(const ExpertSource& src, const int* down_types, in
                               const DecodeLayer* layers, int H, int F, int E, int k, float eps, bool stack,
                               const void* x_in, int x_dtype, void* out, int out_dtype, int32_t* topk_idx_out,
                               float* topk_w_out, void* scratch, int num_ctas, int* status, uint64_t* trace,
-                              size_t trace_entries, cudaStream_t st, int* launches);
+                              size_t trace_entries, cudaStream_t st, int* launches, float min_w = 0.f);
 
 // store.cu: device generator
 cudaError_t fill_synthetic(uint8_t* dst, uint64_t seed, const int32_t* layer_expert /*[n][2]*/, int n,

@@ -368,6 +368,45 @@ __global__ void pack_router_kernel(const float* __restrict__ R, const float* __r
   }
 }
 
+// willow's skip_small_experts (engines/base.py:413-429) on the renormalised weights of T tokens, one thread per
+// token: pick j of a token is kept when j == 0 (the largest weight; picks are in descending order) or its weight is
+// >= min_w; the kept weights are scaled so that they add up to the picks' former total, the dropped ones become 0.
+// The expert ids stay as they are: a dropped pick's expert is then added with weight 0, which leaves every sum
+// unchanged.
+__global__ void skip_small_kernel(float* __restrict__ topk_w, int T, int k, float min_w) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float* w = topk_w + size_t(t) * k;
+  float total = 0.f, kept = 0.f;
+  for (int j = 0; j < k; ++j) {
+    total += w[j];
+    if (j == 0 || w[j] >= min_w) kept += w[j];
+  }
+  const float scale = total / kept;
+  for (int j = 0; j < k; ++j) w[j] = (j == 0 || w[j] >= min_w) ? w[j] * scale : 0.f;
+}
+
+cudaError_t skip_small_experts(float* topk_w, int T, int k, float min_w, cudaStream_t st, int* launches) {
+  if (T <= 0 || !(min_w > 0.f)) return cudaSuccess;
+  skip_small_kernel<<<unsigned((T + 255) / 256), 256, 0, st>>>(topk_w, T, k, min_w);
+  ++*launches;
+  return cudaGetLastError();
+}
+
+// out[i] = idx[i], or -1 where the pick's weight is 0 (dropped by skip_small_experts), as willow marks them
+__global__ void mark_dropped_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w,
+                                    int32_t* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = w[i] == 0.f ? -1 : idx[i];
+}
+
+cudaError_t mark_dropped(const int32_t* idx, const float* w, int32_t* out, int n, cudaStream_t st, int* launches) {
+  if (n <= 0) return cudaSuccess;
+  mark_dropped_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(idx, w, out, n);
+  ++*launches;
+  return cudaGetLastError();
+}
+
 cudaError_t pack_router(const float* router_w, const float* shared_gate, int E, int H, float* out, cudaStream_t st) {
   const dim3 grid(unsigned((H + 31) / 32), unsigned((kRouterStride + 31) / 32));
   pack_router_kernel<<<grid, dim3(32, 8), 0, st>>>(router_w, shared_gate, E, H, out);

@@ -22,6 +22,7 @@ struct wmoe_ctx {
   int decode_ctas = 0;      // CTAs of the persistent decode kernel (all co-resident)
   bool use_decode_kernel = true;
   int prefill_threshold = 16;  // token count from which wmoe_moe_forward uses the tcgen05 grouped GEMMs
+  float min_expert_weight = 0.f;  // willow's --min-expert-weight (wmoe_set_min_expert_weight); 0: off
   uint64_t* trace = nullptr;  // decode phase timestamps (device), or null
   size_t trace_entries = 0;
   // expert parallelism over the library's own NCCL communicator (wmoe_ep_init)

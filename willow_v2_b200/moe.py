@@ -51,6 +51,12 @@ class Context:
     def set_decode_kernel(self, enable: bool) -> bool:
         return bool(lib.wmoe_set_decode_kernel(self.handle, int(enable)))
 
+    def set_min_expert_weight(self, weight: float):
+        """willow's min_expert_weight (engines/base.py:413-429): routings of this context drop each token's picks of
+        renormalised weight below `weight` except its top one, scaling the kept ones back to the former total;
+        dropped picks are returned as -1 (weight 0). 0 turns it off."""
+        check(self.handle, lib.wmoe_set_min_expert_weight(self.handle, float(weight)))
+
     def device_status(self) -> int:
         """Reads and clears the device status word (0 = fine; see lib.STATUS_NAMES)."""
         v = ctypes.c_int()
@@ -243,17 +249,22 @@ def add_rmsnorm(x: torch.Tensor, y: Optional[torch.Tensor] = None, eps: float = 
 
 
 def guess_next_layer(store: ExpertStore, residual: torch.Tensor, lw_next: "LayerWeights", layer_next: int,
-                     top_k: int = 8, eps: float = 1e-6) -> list:
+                     top_k: int = 8, eps: float = 1e-6, guess_input: Optional[torch.Tensor] = None) -> list:
     """Decode on a capped store (engines/base.py:392-406, with engines/qwen36/model.py:30-31's guess input): runs
-    the next layer's router on rms_norm(residual), the residual stream before the current layer's experts, and
-    starts copying the experts it picks for every token (ExpertStore.prefetch), so they are resident or on their
-    way when that layer runs; the current layer's experts compute meanwhile. Returns the guessed expert ids (those
-    this store holds). Usually most of them are the experts the layer then picks."""
-    x = residual.float().contiguous().clone()
-    _, xn = add_rmsnorm(x, None, eps, out_dtype=torch.float32, ctx=store.ctx)
-    _, sel, _, _ = route(xn, lw_next.router_w, top_k, bias=lw_next.router_bias, ctx=store.ctx)
+    the next layer's router on rms_norm(residual), the residual stream before the current layer's experts (or on
+    guess_input, the engine's own normalised form of it), and starts copying the experts it picks for every token
+    (ExpertStore.prefetch), so they are resident or on their way when that layer runs; the current layer's experts
+    compute meanwhile. Returns the guessed expert ids (those this store holds). Usually most of them are the experts
+    the layer then picks. Guesses the context's min_expert_weight drops are not copied (base.py:424-425)."""
+    if guess_input is None:
+        x = residual.float().contiguous().clone()
+        _, xn = add_rmsnorm(x, None, eps, out_dtype=torch.float32, ctx=store.ctx)
+    else:
+        xn = guess_input.float().contiguous()
+    w, sel, _, _ = route(xn, lw_next.router_w, top_k, bias=lw_next.router_bias, ctx=store.ctx)
     lo, hi = store.expert_range
-    guess = [e for e in torch.unique(sel).tolist() if lo <= e < hi]
+    picked = sel[w > 0]
+    guess = [e for e in torch.unique(picked).tolist() if lo <= e < hi]
     store.prefetch(layer_next, guess)
     return guess
 
@@ -516,31 +527,70 @@ class CudaMoE:
     """Mixin that replaces willow's Engine.moe (engines/base.py:445-490) with the B200 kernels:
 
         class B200Qwen35(CudaMoE, Qwen35MoEEngine): ...
+        engine = B200Qwen35(...)            # willow's loader as usual
+        engine.wmoe_attach(gguf_path)       # routed experts into HBM, shared experts' GGUF bytes
 
-    It reads the layer's weights by willow's names through self.w(...): the router
-    ``{prefix}layers.{L}.mlp.gate.weight`` and ``.mlp.shared_expert_gate.weight`` (f32, on the GPU), and the shared
-    expert as raw GGUF bytes on the GPU, ``.mlp.shared_expert.gate_up_proj.qweight`` (Q4_K, gate rows then up rows)
-    and ``.mlp.shared_expert.down_proj.qweight`` (Q6_K). Routed experts come from self.experts, an ExpertStore of
-    this module. ``.mlp.gate.bias`` (optional, f32 [E]) is added to the logits. Returns the block's output in x's
-    dtype, like Engine.moe; residual is accepted for the signature (the next-layer guess it feeds in willow only
-    drives SSD prefetching, which an HBM-resident store does not need)."""
+    Weights by willow's own names through self.w(...): the router ``{prefix}layers.{L}.mlp.gate.weight`` and the
+    shared-expert gate ``.mlp.shared_expert_gate.weight`` (willow keeps them dequantised, bf16 or f32: they are
+    widened to f32 exactly), and ``.mlp.gate.bias`` when present. willow's loader dequantises the shared expert, so
+    its GGUF bytes come from the file (wmoe_attach), or from ``.mlp.shared_expert.gate_up_proj.qweight`` (Q4_K,
+    gate rows then up rows) and ``.mlp.shared_expert.down_proj.qweight`` when the engine keeps them. Routed experts
+    come from self.experts, an ExpertStore of this module.
+
+    The engine's settings keep their meaning:
+    * min_expert_weight (main.py:37,108): routed picks below it are dropped as skip_small_experts does
+      (base.py:413-429);
+    * residual with prefetch_top_k (base.py:392-406,450,473-474): for a decode token on a capped store, the next
+      layer's router runs on the engine's router_guess_input(residual, layer + 1) and the experts it picks start
+      copying into HBM (ExpertStore.prefetch) while this layer computes.
+    Returns the block's output in x's dtype, like Engine.moe."""
 
     top_k = 8
+
+    def wmoe_attach(self, gguf_path: str, cap_bytes: int = 0, ctx: Optional[Context] = None):
+        """Reads the GGUF's routed experts into an ExpertStore (self.experts; capped at cap_bytes of HBM when given)
+        and keeps each layer's shared-expert bytes on the GPU for moe_layer_weights."""
+        from . import gguf_store
+        store, lws = gguf_store.load(gguf_path, ctx=ctx, cap_bytes=cap_bytes)
+        self.experts = store
+        self._wmoe_shared = {layer: (lw.shared_gate_up, lw.shared_down) for layer, lw in enumerate(lws)}
+        self.__dict__.pop("_wmoe_layers", None)
+        return store
 
     def moe_layer_weights(self, layer: int) -> LayerWeights:
         """The layer's weights with their prepared router forms, made on first use and kept."""
         cache = self.__dict__.setdefault("_wmoe_layers", {})
         if layer not in cache:
             p = f"{self.prefix}layers.{layer}.mlp"
-            cache[layer] = LayerWeights(router_w=self.w(p + ".gate.weight"),
-                                        shared_gate=self.w(p + ".shared_expert_gate.weight").reshape(-1),
-                                        shared_gate_up=self.w(p + ".shared_expert.gate_up_proj.qweight"),
-                                        shared_down=self.w(p + ".shared_expert.down_proj.qweight"),
-                                        router_bias=self.weights.get(p + ".gate.bias")).prepare(self.experts.ctx)
+            dev = torch.device("cuda", self.experts.ctx.device)
+            f32 = lambda t: t.to(device=dev, dtype=torch.float32).contiguous()
+            shared = getattr(self, "_wmoe_shared", {}).get(layer)
+            if shared is None:
+                shared = (self.w(p + ".shared_expert.gate_up_proj.qweight"),
+                          self.w(p + ".shared_expert.down_proj.qweight"))
+            bias = self.weights.get(p + ".gate.bias")
+            cache[layer] = LayerWeights(router_w=f32(self.w(p + ".gate.weight")),
+                                        shared_gate=f32(self.w(p + ".shared_expert_gate.weight").reshape(-1)),
+                                        shared_gate_up=shared[0].to(dev).contiguous(),
+                                        shared_down=shared[1].to(dev).contiguous(),
+                                        router_bias=None if bias is None else f32(bias)).prepare(self.experts.ctx)
         return cache[layer]
 
     def moe(self, x: torch.Tensor, layer: int, residual: torch.Tensor = None) -> torch.Tensor:
         lw = self.moe_layer_weights(layer)
+        ctx = self.experts.ctx
+        ctx.set_min_expert_weight(float(getattr(self, "min_expert_weight", 0.0) or 0.0))
         shape = x.shape
-        out = moe_forward(self.experts, layer, x.reshape(-1, shape[-1]), lw, self.top_k)
+        flat = x.reshape(-1, shape[-1])
+        out = moe_forward(self.experts, layer, flat, lw, self.top_k)
+        # willow starts the next layer's guessed reads after this layer's (base.py:471-474); here they are queued
+        # behind this layer's kernels on the same stream, and the copies run on the store's side stream
+        following = layer + 1
+        k = int(getattr(self, "prefetch_top_k", 0) or 0)
+        if (residual is not None and k and self.experts.capped and flat.shape[0] == 1
+                and following < getattr(self, "num_layers", self.experts.layers)):
+            guess_in = self.router_guess_input(residual.reshape(-1, shape[-1]), following) \
+                if hasattr(self, "router_guess_input") else None
+            guess_next_layer(self.experts, residual.reshape(-1, shape[-1]), self.moe_layer_weights(following),
+                             following, top_k=min(k, self.top_k), guess_input=guess_in)
         return out.view(shape)
