@@ -1275,7 +1275,7 @@ int wmoe_gemv(wmoe_ctx* ctx, int ggml_type, const uint8_t* w, int rows, int k, c
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv: w must be 2-byte and x 16-byte aligned");
   const cudaError_t e = ggml_gemv(ggml_type, nullptr, w, nullptr, 1, 1, rows, k, x, x_dtype, tokens, y, y_dtype,
                                   ctx->d_status, static_cast<cudaStream_t>(stream));
-  if (e == cudaErrorInvalidValue)
+  if (e == cudaErrorNotSupported)  // ggml_gemv / ggml_combine: the shared-memory budget, nothing else
     return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv: the activations and a row tile of this k do not fit shared "
                                                "memory");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_gemv");
@@ -1296,7 +1296,7 @@ int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights,
   if (!aligned16(x)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_batch: x must be 16-byte aligned");
   const cudaError_t e = ggml_gemv(ggml_type, weights, nullptr, positions, n, positions ? n_out : n, rows, k, x,
                                   x_dtype, 1, y, y_dtype, ctx->d_status, static_cast<cudaStream_t>(stream));
-  if (e == cudaErrorInvalidValue)
+  if (e == cudaErrorNotSupported)  // ggml_gemv / ggml_combine: the shared-memory budget, nothing else
     return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv_batch: the activations and a row tile of this k do not "
                                                "fit shared memory");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_gemv_batch");
@@ -1318,7 +1318,7 @@ int wmoe_gemv_combine(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weight
   if (!aligned16(x)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_gemv_combine: x must be 16-byte aligned");
   const cudaError_t e = ggml_combine(ggml_type, weights, perm, n, n_route, rows, k, x, route_w, dtype, y,
                                      ctx->d_status, static_cast<cudaStream_t>(stream));
-  if (e == cudaErrorInvalidValue)
+  if (e == cudaErrorNotSupported)  // ggml_gemv / ggml_combine: the shared-memory budget, nothing else
     return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv_combine: a row tile of this k does not fit shared memory");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_gemv_combine");
   ctx->launches += 1;

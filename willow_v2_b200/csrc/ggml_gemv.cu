@@ -491,6 +491,10 @@ cudaError_t ggml_dequant(int type, const uint8_t* blocks, size_t nblocks, void* 
   });
 }
 
+// The refusal of a call whose activations and row tile do not fit shared memory: a code no launch or attribute
+// call of these launchers returns, so that the C ABI can tell it apart (WMOE_ERR_UNSUPPORTED).
+constexpr cudaError_t kSmemRefusal = cudaErrorNotSupported;
+
 cudaError_t ggml_gemv(int type, const uint8_t* const* weights, const uint8_t* single, const int64_t* positions, int n,
                       int n_out, int rows, int k, const void* x, int x_dtype, int tokens, void* y, int y_dtype,
                       int* status, cudaStream_t st) {
@@ -501,7 +505,8 @@ cudaError_t ggml_gemv(int type, const uint8_t* const* weights, const uint8_t* si
   a.tile_rows = int(std::max<size_t>(1, std::min<size_t>(std::min<size_t>(size_t(rows), kGemvTileRows),
                                                          kStageBudget / rb)));
   const size_t smem = align16(table_bytes(type)) + xq_bytes(tokens, k) + size_t(a.tile_rows) * rb + 16;
-  if (smem > kMaxSmem) return cudaErrorInvalidValue;
+  if (smem > kMaxSmem) return kSmemRefusal;
+  (void)cudaGetLastError();  // an earlier call's non-sticky error must not read as this launch's
   const dim3 grid(unsigned((rows + a.tile_rows - 1) / a.tile_rows), unsigned(n));
   const int lanes = lanes_for(k / 32);
   return by_type(type, [&](auto tc) -> cudaError_t {
@@ -532,7 +537,8 @@ cudaError_t ggml_combine(int type, const uint8_t* const* weights, const int64_t*
   a.tile_rows = std::min(rows, rows_per_pass);
   const size_t slot = align16(size_t(a.tile_rows) * rb) + 16;
   const size_t tab = align16(table_bytes(type)) + xq_bytes(n, k) + combine_meta_bytes(n);
-  if (tab + slot > kMaxSmem) return cudaErrorInvalidValue;
+  if (tab + slot > kMaxSmem) return kSmemRefusal;
+  (void)cudaGetLastError();  // an earlier call's non-sticky error must not read as this launch's
   a.group = int(std::min<size_t>(size_t(n), (kMaxSmem - tab) / slot));
   a.group = std::min(a.group, int(std::max<size_t>(1, (96 * 1024) / slot)));  // keep a few CTAs per SM
   const size_t smem = tab + size_t(a.group) * slot;

@@ -304,9 +304,10 @@ static int copy_in(wmoe_store* s, int layer, const std::vector<int>& misses, std
       push_update(s, u, int(old), -1, st);
     }
     const uint64_t last = s->slot_use[size_t(slot)];
-    // a compute event still holding that call (the ring has not wrapped past it) orders the overwrite
-    if (last > 0 && s->ring_seq[last % wmoe_store::kRing] == last)
-      e = cudaStreamWaitEvent(s->side, s->ring[last % wmoe_store::kRing], 0);
+    // the compute event of the call that last read the slot orders the overwrite. When the ring has wrapped past
+    // that call, its entry holds a later call's event: a context issues its calls on one compute stream (it is
+    // single-stream), so that later call's completion implies the earlier one's, and waiting on it is still safe.
+    if (last > 0) e = cudaStreamWaitEvent(s->side, s->ring[last % wmoe_store::kRing], 0);
     if (e != cudaSuccess) break;
     const size_t key = size_t(layer) * E + size_t(x);
     e = cudaMemcpyAsync(s->d_slab + size_t(slot) * s->slot_stride, s->h_master + s->blob_index(layer, x) * s->blob_bytes,
@@ -441,7 +442,6 @@ int store_choose_hot(wmoe_store* s, double share) {
 int store_mark_used(wmoe_store* s, int layer, const int32_t* experts, int n, cudaStream_t st) {
   if (!s->capped) return 0;
   const uint64_t seq = ++s->seq;
-  s->ring_seq[seq % wmoe_store::kRing] = seq;
   const cudaError_t e = cudaEventRecord(s->ring[seq % wmoe_store::kRing], st);
   if (e != cudaSuccess) return store_fail(s, -2, std::string("store event: ") + cudaGetErrorString(e));
   for (int i = 0; i < n; ++i) {

@@ -73,7 +73,6 @@ struct wmoe_store {
   std::vector<char> hot;          // [layers * experts] the hot set: evicted only when no other slot can go
   cudaStream_t side = nullptr;
   cudaEvent_t ring[kRing] = {};       // compute-stream event of call seq at [seq % kRing]
-  uint64_t ring_seq[kRing] = {};
   cudaEvent_t batch_ev[kRing] = {};   // side-stream event of copy batch b at [b % kRing]
   uint64_t seq = 0;
   uint64_t batches = 0, waited = 0;   // copy batches issued; the last one the compute stream has waited for

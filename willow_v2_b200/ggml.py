@@ -63,10 +63,56 @@ def _on_gpu(*tensors):
         raise ValueError(f"expected CUDA tensors on one device, got {sorted(str(d) for d in devs)}")
 
 
-def _pointers(base: torch.Tensor, offsets) -> torch.Tensor:
-    """Device array of base + offset for each offset (the kernels take matrix addresses)."""
-    ptrs = torch.tensor([base.data_ptr() + int(o) for o in offsets], dtype=torch.int64)
-    return ptrs.to(base.device, non_blocking=False)
+class _Staging:
+    """The small int64 arrays the batched kernels take (matrix addresses, output positions, routing order) go to the
+    GPU through a ring of pinned host chunks, each copied asynchronously into its device chunk on the current
+    stream: a call makes no host synchronisation (a pageable torch.tensor(...).to(device) would wait for the GPU
+    on every call). A chunk is written again only after the event recorded behind the kernel that read its last
+    contents has completed; with 64 chunks that wait is all but never taken."""
+    CHUNKS, WORDS = 64, 1024
+
+    def __init__(self, device: torch.device):
+        self.host = torch.empty(self.CHUNKS, self.WORDS, dtype=torch.int64).pin_memory()
+        self.host_np = self.host.numpy()
+        self.dev = torch.empty(self.CHUNKS, self.WORDS, dtype=torch.int64, device=device)
+        self.events = [None] * self.CHUNKS
+        self.next = 0
+        self.chunk = -1
+
+    def put(self, *arrays):
+        """Device int64 views of the given integer sequences (one chunk for all of them)."""
+        sizes = [len(a) for a in arrays]
+        if sum(sizes) > self.WORDS:  # beyond a chunk: a plain (synchronising) upload
+            self.chunk = -1
+            return [torch.tensor(list(a), dtype=torch.int64).to(self.dev.device) for a in arrays]
+        c = self.chunk = self.next
+        self.next = (c + 1) % self.CHUNKS
+        if self.events[c] is not None:
+            self.events[c].synchronize()
+        h, off, views = self.host_np[c], 0, []
+        for a, n in zip(arrays, sizes):
+            h[off:off + n] = a
+            views.append((off, n))
+            off += n
+        self.dev[c, :off].copy_(self.host[c, :off], non_blocking=True)
+        return [self.dev[c, o:o + n] for o, n in views]
+
+    def done(self):
+        """Marks the chunk of the last put as read by the kernel just launched on the current stream."""
+        if self.chunk >= 0:
+            ev = torch.cuda.Event()
+            ev.record()
+            self.events[self.chunk] = ev
+
+
+_STAGING = {}
+
+
+def _staging(device: torch.device) -> _Staging:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _STAGING:
+        _STAGING[key] = _Staging(torch.device("cuda", key))
+    return _STAGING[key]
 
 
 def available() -> bool:
@@ -132,12 +178,16 @@ def gemv_batch(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor
     assert out.is_contiguous() and out.shape[-1] == rows
     x = _act(x.reshape(k))
     _on_gpu(base, x, out)
-    ptrs = _pointers(base, offsets)
-    pos = torch.tensor(list(positions), dtype=torch.int64).to(base.device)
+    stage = _staging(base.device)
+    b0 = base.data_ptr()
+    ptrs, pos = stage.put([b0 + int(o) for o in offsets], [int(q) for q in positions])
     ctx = ctx or _ctx()
-    check(ctx.handle, lib.wmoe_gemv_batch(ctx.handle, _type_id(type_name), _p(ptrs), _p(pos), len(offsets),
-                                          out.shape[0], rows, k, _p(x), _DTYPES[x.dtype], _p(out),
-                                          _DTYPES[out.dtype], _stream()))
+    try:
+        check(ctx.handle, lib.wmoe_gemv_batch(ctx.handle, _type_id(type_name), _p(ptrs), _p(pos), len(offsets),
+                                              out.shape[0], rows, k, _p(x), _DTYPES[x.dtype], _p(out),
+                                              _DTYPES[out.dtype], _stream()))
+    finally:
+        stage.done()
 
 
 def gemv_combine(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tensor, offsets: list,
@@ -158,12 +208,16 @@ def gemv_combine(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tens
     x = x.reshape(n, k).to(torch.bfloat16).contiguous()
     w = weights.reshape(-1).to(torch.bfloat16).contiguous()
     _on_gpu(base, x, w)
-    ptrs = _pointers(base, offsets)
-    pm = torch.tensor(list(perm), dtype=torch.int64).to(base.device)
+    stage = _staging(base.device)
+    b0 = base.data_ptr()
+    ptrs, pm = stage.put([b0 + int(o) for o in offsets], [int(q) for q in perm])
     y = torch.empty(1, rows, dtype=torch.bfloat16, device=base.device)
     ctx = ctx or _ctx()
-    check(ctx.handle, lib.wmoe_gemv_combine(ctx.handle, _type_id(type_name), _p(ptrs), _p(pm), n, w.numel(), rows, k,
-                                            _p(x), _p(w), _lib.BF16, _p(y), _stream()))
+    try:
+        check(ctx.handle, lib.wmoe_gemv_combine(ctx.handle, _type_id(type_name), _p(ptrs), _p(pm), n, w.numel(),
+                                                rows, k, _p(x), _p(w), _lib.BF16, _p(y), _stream()))
+    finally:
+        stage.done()
     return y
 
 
