@@ -258,9 +258,13 @@ int wmoe_ep_route_plan(wmoe_ctx* ctx, int world, const void* x, int x_dtype, int
                        int32_t* send_tok /* [T * min(top_k, world)] */, int32_t* pair_list /* [T * top_k, 2] */,
                        int32_t* ret_index /* [T, top_k] */, uint16_t* send_buf /* fp16 [T * min(top_k, world), hidden] */,
                        void* stream);
-/* The same layer in one call over the library's own NCCL communicator (grouped ncclSend/ncclRecv for every
- * exchange, one host read of the transfer sizes per layer): each rank passes its own tokens and gets their outputs,
- * identical to wmoe_moe_forward on one GPU. wmoe_ep_unique_id (one rank) makes the id every rank passes to
+/* The same layer in one call over the library's own NCCL communicator: each rank passes its own tokens and gets
+ * their outputs, identical to wmoe_moe_forward on one GPU. Per layer one all-gather of every rank's transfer counts
+ * (one bounded host read of them); the rows, pair lists and result rows are copied by the copy engines straight
+ * into the destination rank's exchange window (device memory every rank maps through CUDA IPC; made on first use
+ * and grown together by every rank), one stream per destination, each exchange closed by a one-int all-reduce as
+ * barrier. No kernel reads another GPU's memory. With WMOE_EP_NCCL_ROWS set in the environment at wmoe_ep_init
+ * the rows go through grouped ncclSend/ncclRecv instead. wmoe_ep_unique_id (one rank) makes the id every rank passes to
  * wmoe_ep_init(ctx, id, rank, world), which creates the communicator (collectively); wmoe_ep_finalize (or
  * wmoe_destroy) frees it. NCCL is loaded at run time (libnccl.so.2); without it wmoe_ep_init returns
  * WMOE_ERR_UNSUPPORTED. Arguments of wmoe_moe_forward_ep as in wmoe_moe_forward_layer; store from
@@ -269,6 +273,13 @@ int wmoe_ep_unique_id(void* out /* WMOE_EP_ID_BYTES */);
 #define WMOE_EP_ID_BYTES 128
 int wmoe_ep_init(wmoe_ctx* ctx, const void* unique_id, int rank, int world);
 int wmoe_ep_finalize(wmoe_ctx* ctx);
+/* Failure handling: the communicator is non-blocking, and every host wait on it (the creation, the count read-back
+ * of each wmoe_moe_forward_ep, the exchange windows' set-up) is bounded by this many milliseconds (default 30000)
+ * while the communicator is watched for asynchronous errors. A rank that left, or any NCCL error, aborts the
+ * communicator (its kernels in flight return) and the call returns WMOE_ERR_NCCL; every later EP call of the context
+ * does so too until wmoe_ep_finalize and a new wmoe_ep_init. Returns the previous value. No counterpart in willow,
+ * which runs on one device. */
+int wmoe_ep_set_timeout(wmoe_ctx* ctx, int ms);
 /* wmoe_moe_forward_ep runs the rank's tokens in this many chunks (1..16, default 1) so that the exchanges of one
  * chunk overlap the expert stage of another (the exchanges then run on a stream of the context, and the GEMMs leave
  * SMs free for them). Every rank must use the same value: the count exchange carries it, and a mismatch makes every

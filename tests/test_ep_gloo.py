@@ -124,3 +124,46 @@ def test_ep_exchange_on_two_gloo_ranks():
     want = ora.moe(x, ops.router, ops.weights, ops.weights(256), ops.gate)[0]
     err = float(np.linalg.norm(out - want) / np.linalg.norm(want))
     assert err < 1e-5, err
+
+
+def _leave_rank(rank, world, port, outdir):
+    """One step together, then rank 1 leaves between steps; rank 0's next exchange must fail within the process
+    group's short timeout instead of waiting for good."""
+    import datetime
+    import time
+    import types
+    import torch.distributed as dist
+    from willow_v2_b200.moe import moe_forward_ep
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    per = E // world
+    store = types.SimpleNamespace(experts=E, expert_range=(rank * per, (rank + 1) * per))
+    mine = torch.from_numpy(np.array_split(synth.hidden(SEED, TOKENS, step=9), world)[rank])
+    moe_forward_ep(store, LAYER, mine, None, ops=OracleEPOps(), out_dtype=torch.float32)
+    dist.barrier()
+    if rank == 1:
+        os._exit(0)
+    t0 = time.time()
+    failed = False
+    try:
+        moe_forward_ep(store, LAYER, mine, None, ops=OracleEPOps(), out_dtype=torch.float32)
+    except RuntimeError:
+        failed = True
+    np.save(os.path.join(outdir, "left.npy"), np.array([float(failed), time.time() - t0]))
+    os._exit(0)
+
+
+def test_ep_rank_leaving_fails_the_next_exchange():
+    """The exchange logic when a rank leaves between steps, on gloo ranks: the survivor's next layer raises from its
+    first exchange within the group's 3 s timeout."""
+    import time
+    with tempfile.TemporaryDirectory() as d:
+        ctxs = mp.start_processes(_leave_rank, args=(WORLD, _free_port(), d), nprocs=WORLD, start_method="spawn",
+                                  join=False)
+        deadline = time.time() + 120
+        while not ctxs.join(timeout=max(1.0, deadline - time.time())) and time.time() < deadline:
+            pass
+        failed, waited = np.load(os.path.join(d, "left.npy"))
+    assert failed == 1.0 and waited < 30.0, (failed, waited)
+

@@ -7,6 +7,7 @@ import datetime
 import os
 import socket
 import tempfile
+import time
 
 import numpy as np
 import pytest
@@ -101,6 +102,32 @@ def test_ep_over_nccl_matches_single_gpu(zipf, native):
         assert np.array_equal(outs[r], ref[r * TOKENS_PER_RANK:(r + 1) * TOKENS_PER_RANK]), r
 
 
+@pytest.mark.parametrize("zipf", [False, True])
+def test_ep_native_one_rank_matches_single_gpu(zipf):
+    """The library's own EP path on a one-rank communicator (one GPU): the count all-gather, the exchange window,
+    the copy-engine copies and the barriers all run; the output equals the single-GPU layer bit for bit for every
+    chunk count."""
+    import torch
+    import torch.multiprocessing as mp
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rank, args=(1, _free_port(), d, zipf, True), nprocs=1, start_method="spawn")
+        out = np.load(os.path.join(d, "out0.npy"))
+    from willow_v2_b200 import moe
+    from willow_v2_b200.lib import lib
+    torch.cuda.set_device(0)
+    ctx = moe.Context(0)
+    full = moe.ExpertStore(1, ctx=ctx)
+    full.fill_synthetic(SEED)
+    lw = _weights(moe, torch, ctx, zipf)
+    x = torch.from_numpy(synth.hidden(SEED, TOKENS_PER_RANK, step=33)).to(torch.bfloat16).cuda()
+    prev = lib.wmoe_set_prefill_threshold(ctx.handle, 1)
+    try:
+        ref = moe.moe_forward(full, LAYER, x, lw, out_dtype=torch.float32).cpu().numpy()
+    finally:
+        lib.wmoe_set_prefill_threshold(ctx.handle, prev)
+    assert np.array_equal(out, ref)
+
+
 def _mismatch_rank(rank, world, port, outdir):
     import torch
     import torch.distributed as dist
@@ -147,3 +174,69 @@ def test_ep_chunk_mismatch_is_an_error_on_every_rank():
         for r in range(2):
             raised, finite = np.load(os.path.join(d, f"ok{r}.npy"))
             assert raised and finite, r
+
+
+def _leave_rank(rank, world, port, outdir):
+    """Two ranks take one step together; rank 1 then leaves between steps (nothing of it in flight) and exits; rank
+    0's next layer must come back with WMOE_ERR_NCCL within the context's timeout, and its GPU stays usable."""
+    import time
+    import torch
+    import torch.distributed as dist
+    from willow_v2_b200 import moe
+    from willow_v2_b200.lib import ERR_NCCL, WmoeError
+    os.environ["NCCL_NVLS_ENABLE"] = "0"  # plain peer transfers: nothing of a leaving rank bound to a multicast object
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    # the test's own coordination over gloo, so that the survivor's teardown does not wait on the rank that left
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    ctx = moe.Context(rank)
+    per = 256 // world
+    store = moe.ExpertStore(1, ctx=ctx, expert_range=(rank * per, (rank + 1) * per))
+    store.fill_synthetic(SEED)
+    lw = _weights(moe, torch, ctx, False)
+    x = torch.from_numpy(synth.hidden(SEED, 512, step=55 + rank)).to(torch.bfloat16).cuda()
+    moe.ep_init(ctx)
+    ctx.ep_set_timeout(3000)
+    first = moe.moe_forward_ep_native(store, LAYER, x, lw)
+    torch.cuda.synchronize()
+    dist.barrier()
+    if rank == 1:
+        ctx.ep_finalize()
+        np.save(os.path.join(outdir, "left1.npy"), np.array([1.0]))
+        os._exit(0)  # leaves without a goodbye, as a failed rank would
+    time.sleep(1.0)
+    t0 = time.time()
+    code = 0
+    try:
+        moe.moe_forward_ep_native(store, LAYER, x, lw)
+        torch.cuda.synchronize()
+    except WmoeError as e:
+        code = e.code
+    waited = time.time() - t0
+    # the communicator is gone, the GPU is not: a single-GPU layer on this rank's experts still runs
+    ctx.ep_finalize()
+    again = moe.moe_forward(store, LAYER, x, lw)
+    torch.cuda.synchronize()
+    ok = bool(torch.isfinite(again.float()).all()) and bool(torch.isfinite(first.float()).all())
+    np.save(os.path.join(outdir, "left0.npy"), np.array([float(code == ERR_NCCL), waited, float(ok)]))
+    os._exit(0)
+
+
+def test_ep_rank_leaving_is_an_nccl_error():
+    """A rank that leaves between steps: the survivor's next wmoe_moe_forward_ep returns WMOE_ERR_NCCL within its
+    3 s timeout (the count exchange's bounded wait aborts the communicator) instead of hanging; no GPU is faulted
+    or left waiting."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        ctxs = mp.start_processes(_leave_rank, args=(2, _free_port(), d), nprocs=2, start_method="spawn", join=False)
+        deadline = time.time() + 120
+        while not ctxs.join(timeout=max(1.0, deadline - time.time())) and time.time() < deadline:
+            pass
+        assert os.path.exists(os.path.join(d, "left1.npy"))
+        nccl_error, waited, ok = np.load(os.path.join(d, "left0.npy"))
+        assert nccl_error == 1.0 and ok == 1.0
+        assert waited < 20.0, waited

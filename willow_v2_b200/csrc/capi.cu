@@ -1,7 +1,11 @@
 // The C ABI of include/wmoe.h: argument checks, scratch planning and the order of launches. Kernels live in
 // dequant.cu, route.cu, dispatch.cu, gemv.cu, decode.cu and store.cu.
 #include <dlfcn.h>
+
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
+#include <thread>
 #include <nccl.h>
 
 #include <algorithm>
@@ -836,49 +840,110 @@ int wmoe_ep_combine(wmoe_ctx* ctx, int T, int top_k, int hidden, const int32_t* 
 // NCCL is resolved at run time (dlopen of libnccl.so.2, reusing the copy already loaded in the process, e.g. by
 // torch), so the library loads without it and only wmoe_ep_init needs it.
 struct NcclApi {
-  bool tried = false, ok = false;
+  bool ok = false;
   ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
 static NcclApi& nccl() {
   static NcclApi api;
-  if (!api.tried) {
-    api.tried = true;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
     void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
     if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (h) {
-      auto get = [&](const char* n) { return dlsym(h, n); };
+      auto get = [&](const char* name) { return dlsym(h, name); };
       api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(get("ncclGetUniqueId"));
-      api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(get("ncclCommInitRank"));
+      api.CommInitRankConfig = reinterpret_cast<decltype(api.CommInitRankConfig)>(get("ncclCommInitRankConfig"));
+      api.CommGetAsyncError = reinterpret_cast<decltype(api.CommGetAsyncError)>(get("ncclCommGetAsyncError"));
+      api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(get("ncclCommAbort"));
       api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(get("ncclCommDestroy"));
       api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(get("ncclGroupStart"));
       api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(get("ncclGroupEnd"));
       api.Send = reinterpret_cast<decltype(api.Send)>(get("ncclSend"));
       api.Recv = reinterpret_cast<decltype(api.Recv)>(get("ncclRecv"));
+      api.AllGather = reinterpret_cast<decltype(api.AllGather)>(get("ncclAllGather"));
+      api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(get("ncclAllReduce"));
       api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(get("ncclGetErrorString"));
-      api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.GroupStart && api.GroupEnd && api.Send &&
-               api.Recv && api.GetErrorString;
+      api.ok = api.GetUniqueId && api.CommInitRankConfig && api.CommGetAsyncError && api.CommAbort &&
+               api.CommDestroy && api.GroupStart && api.GroupEnd && api.Send && api.Recv && api.AllGather &&
+               api.AllReduce && api.GetErrorString;
     }
   }
   return api;
 }
 
+static void ep_release(wmoe_ctx* ctx);
+
+// A failure of the communicator: the context aborts it (its kernels in flight return) and keeps no exchange state;
+// every later EP call fails until wmoe_ep_finalize and a new wmoe_ep_init.
 static int nccl_fail(wmoe_ctx* ctx, ncclResult_t r, const char* where) {
-  return ctx_fail(ctx, WMOE_ERR_NCCL, std::string(where) + ": " + nccl().GetErrorString(r));
+  std::string msg = std::string(where) + ": " + nccl().GetErrorString(r);
+  if (ctx->nccl_comm) {
+    nccl().CommAbort(static_cast<ncclComm_t>(ctx->nccl_comm));
+    ctx->nccl_comm = nullptr;
+    ctx->ep_dead = true;
+    msg += " (communicator aborted)";
+  }
+  return ctx_fail(ctx, WMOE_ERR_NCCL, msg);
 }
 
-#define WMOE_CHECK_NCCL(ctx, call, where)                   \
-  do {                                                      \
-    const ncclResult_t r_ = (call);                         \
-    if (r_ != ncclSuccess) return nccl_fail(ctx, r_, where); \
+static long long now_ms() {
+  return std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+// The communicator is non-blocking: a call may return ncclInProgress and finish in the background. Waits, for at
+// most the context's timeout, until its state is settled; an error or the timeout aborts it.
+static int nccl_settle(wmoe_ctx* ctx, ncclResult_t r, const char* where) {
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(ctx, r, where);
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
+  const long long t0 = now_ms();
+  for (;;) {
+    ncclResult_t state = ncclSuccess;
+    const ncclResult_t q = nccl().CommGetAsyncError(comm, &state);
+    if (q != ncclSuccess) return nccl_fail(ctx, q, where);
+    if (state == ncclSuccess) return WMOE_OK;
+    if (state != ncclInProgress) return nccl_fail(ctx, state, where);
+    if (now_ms() - t0 > ctx->ep_timeout_ms)
+      return nccl_fail(ctx, ncclRemoteError, (std::string(where) + ": timed out").c_str());
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+#define WMOE_CHECK_NCCL(ctx, call, where)                              \
+  do {                                                               \
+    if (int rc_ = nccl_settle(ctx, (call), where)) return rc_;       \
   } while (0)
+
+// A host wait for work on a stream that includes communicator kernels: bounded by the context's timeout, and
+// watching the communicator for an asynchronous error (a peer that left). Either aborts the communicator.
+static int ep_wait(wmoe_ctx* ctx, cudaStream_t st, const char* where) {
+  const long long t0 = now_ms();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) return WMOE_OK;
+    if (e != cudaErrorNotReady) return cuda_fail(ctx, e, where);
+    ncclResult_t state = ncclSuccess;
+    nccl().CommGetAsyncError(static_cast<ncclComm_t>(ctx->nccl_comm), &state);
+    if (state != ncclSuccess && state != ncclInProgress) return nccl_fail(ctx, state, where);
+    if (now_ms() - t0 > ctx->ep_timeout_ms)
+      return nccl_fail(ctx, ncclRemoteError, (std::string(where) + ": timed out waiting for the other ranks").c_str());
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
 
 int wmoe_ep_unique_id(void* out) {
   if (!out) return WMOE_ERR_INVALID;
@@ -889,30 +954,65 @@ int wmoe_ep_unique_id(void* out) {
   return WMOE_OK;
 }
 
+int wmoe_ep_set_timeout(wmoe_ctx* ctx, int ms) {
+  if (!ctx || ms < 1) return WMOE_ERR_INVALID;
+  const int prev = ctx->ep_timeout_ms;
+  ctx->ep_timeout_ms = ms;
+  return prev;
+}
+
+static int ep_setup_windows(wmoe_ctx* ctx);
+
 int wmoe_ep_init(wmoe_ctx* ctx, const void* unique_id, int rank, int world) {
   if (!ctx) return WMOE_ERR_INVALID;
   if (!unique_id || world < 1 || world > WMOE_MAX_RANKS || rank < 0 || rank >= world)
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_init: bad rank / world");
   if (!nccl().ok) return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_ep_init: libnccl.so.2 not available");
-  if (ctx->nccl_comm) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_init: already initialised");
+  if (ctx->nccl_comm || ctx->ep_dead)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_ep_init: already initialised (wmoe_ep_finalize first)");
   WMOE_CHECK_CUDA(ctx, cudaSetDevice(ctx->device), "wmoe_ep_init");
   ncclUniqueId id;
   memcpy(&id, unique_id, sizeof(id));
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
   ncclComm_t comm = nullptr;
-  WMOE_CHECK_NCCL(ctx, nccl().CommInitRank(&comm, world, id, rank), "wmoe_ep_init");
+  const ncclResult_t r = nccl().CommInitRankConfig(&comm, world, id, rank, &config);
   ctx->nccl_comm = comm;
+  if (int rc = nccl_settle(ctx, r, "wmoe_ep_init")) return rc;
   ctx->ep_rank = rank;
   ctx->ep_world = world;
   WMOE_CHECK_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->ep_stream, cudaStreamNonBlocking), "wmoe_ep_init");
   ctx->ep_events.assign(1 + 3 * kMaxEpChunks, nullptr);
   for (cudaEvent_t& e : ctx->ep_events)
     WMOE_CHECK_CUDA(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "wmoe_ep_init");
-  return WMOE_OK;
+  return ep_setup_windows(ctx);
+}
+
+static void ep_close_windows(wmoe_ctx* ctx) {
+  for (int d = 0; d < int(ctx->ep_peer_win.size()); ++d)
+    if (d != ctx->ep_rank && ctx->ep_peer_win[size_t(d)]) cudaIpcCloseMemHandle(ctx->ep_peer_win[size_t(d)]);
+  ctx->ep_peer_win.clear();
+  cudaFree(ctx->ep_win);
+  ctx->ep_win = nullptr;
+  ctx->ep_win_bytes = 0;
 }
 
 static void ep_release(wmoe_ctx* ctx) {
   if (ctx->nccl_comm) nccl().CommDestroy(static_cast<ncclComm_t>(ctx->nccl_comm));
   ctx->nccl_comm = nullptr;
+  ctx->ep_dead = false;
+  ep_close_windows(ctx);
+  for (cudaStream_t s : ctx->ep_peer_streams)
+    if (s) cudaStreamDestroy(s);
+  ctx->ep_peer_streams.clear();
+  for (cudaEvent_t e : ctx->ep_peer_events)
+    if (e) cudaEventDestroy(e);
+  ctx->ep_peer_events.clear();
+  cudaFree(ctx->ep_flag);
+  ctx->ep_flag = nullptr;
+  cudaFree(ctx->ep_handles);
+  ctx->ep_handles = nullptr;
+  ctx->ep_ipc = false;
   for (cudaEvent_t e : ctx->ep_events)
     if (e) cudaEventDestroy(e);
   ctx->ep_events.clear();
@@ -927,8 +1027,85 @@ static void ep_release(wmoe_ctx* ctx) {
 int wmoe_ep_finalize(wmoe_ctx* ctx) {
   if (!ctx) return WMOE_ERR_INVALID;
   cudaSetDevice(ctx->device);
-  WMOE_CHECK_CUDA(ctx, cudaDeviceSynchronize(), "wmoe_ep_finalize");
+  // after an abort the device may still hold the aborted kernels' streams: a bounded wait, then release anyway
+  const cudaError_t e = ctx->ep_dead ? cudaSuccess : cudaDeviceSynchronize();
   ep_release(ctx);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_ep_finalize");
+  return WMOE_OK;
+}
+
+// The exchange machinery beside the communicator: a stream and an event per destination rank, the barrier word and
+// the staging of the IPC handle all-gather. Windows themselves are made by ep_grow_windows when a call first
+// needs them. Without peer access between every pair of devices the rows go through NCCL send/recv instead.
+static int ep_setup_windows(wmoe_ctx* ctx) {
+  const int world = ctx->ep_world;
+  ctx->ep_peer_streams.assign(size_t(world), nullptr);
+  ctx->ep_peer_events.assign(size_t(world), nullptr);
+  for (int d = 0; d < world; ++d) {
+    WMOE_CHECK_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->ep_peer_streams[size_t(d)], cudaStreamNonBlocking),
+                    "wmoe_ep_init");
+    WMOE_CHECK_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_peer_events[size_t(d)], cudaEventDisableTiming),
+                    "wmoe_ep_init");
+  }
+  WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->ep_flag, 256), "wmoe_ep_init");
+  WMOE_CHECK_CUDA(ctx, cudaMemset(ctx->ep_flag, 0, 256), "wmoe_ep_init");
+  WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->ep_handles, size_t(world) * sizeof(cudaIpcMemHandle_t)), "wmoe_ep_init");
+  ctx->ep_ipc = std::getenv("WMOE_EP_NCCL_ROWS") == nullptr;  // the NCCL send/recv path, for comparison
+  return WMOE_OK;
+}
+
+// The exchanges' barrier: a one-int all-reduce on stream st. Every rank issues it after its copies into the peers'
+// windows (ordered on st), so when it completes on a rank, every copy into that rank's window has landed.
+static int ep_barrier(wmoe_ctx* ctx, cudaStream_t st, const char* where) {
+  WMOE_CHECK_NCCL(ctx, nccl().AllReduce(ctx->ep_flag, ctx->ep_flag, 1, ncclInt32, ncclSum,
+                                        static_cast<ncclComm_t>(ctx->nccl_comm), st),
+                  where);
+  return WMOE_OK;
+}
+
+// Windows of at least `need` bytes on every rank. Every rank calls this with the same `need` (it is computed from the
+// all-gathered counts), so all of them grow together: close the peers' old windows, free this one, allocate and
+// export the new one, all-gather the handles, open the peers'. Nothing writes into the old windows any more: a call's
+// copies into a rank's window end before that call's last barrier, and the growth comes after the next call's count
+// exchange.
+static int ep_grow_windows(wmoe_ctx* ctx, size_t need, cudaStream_t st) {
+  if (need <= ctx->ep_win_bytes) return WMOE_OK;
+  const int world = ctx->ep_world, rank = ctx->ep_rank;
+  WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "EP windows");
+  for (int d = 0; d < int(ctx->ep_peer_win.size()); ++d)
+    if (d != rank && ctx->ep_peer_win[size_t(d)]) cudaIpcCloseMemHandle(ctx->ep_peer_win[size_t(d)]);
+  ctx->ep_peer_win.clear();
+  // every rank has closed its mappings of the old windows before any frees one
+  if (int rc = ep_barrier(ctx, st, "EP windows")) return rc;
+  if (int rc = ep_wait(ctx, st, "EP windows")) return rc;
+  cudaFree(ctx->ep_win);
+  ctx->ep_win = nullptr;
+  const size_t bytes = std::max(need + need / 4, size_t(64) << 20);
+  WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->ep_win, bytes), "EP window allocation");
+  ctx->ep_win_bytes = bytes;
+  cudaIpcMemHandle_t mine;
+  WMOE_CHECK_CUDA(ctx, cudaIpcGetMemHandle(&mine, ctx->ep_win), "EP window export");
+  char* staged = static_cast<char*>(ctx->ep_handles);
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(staged + size_t(rank) * sizeof(mine), &mine, sizeof(mine),
+                                       cudaMemcpyHostToDevice, st),
+                  "EP windows");
+  WMOE_CHECK_NCCL(ctx, nccl().AllGather(staged + size_t(rank) * sizeof(mine), staged, sizeof(mine), ncclUint8,
+                                        static_cast<ncclComm_t>(ctx->nccl_comm), st),
+                  "EP windows");
+  std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(world));
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(all.data(), staged, size_t(world) * sizeof(mine), cudaMemcpyDeviceToHost, st),
+                  "EP windows");
+  if (int rc = ep_wait(ctx, st, "EP windows")) return rc;
+  ctx->ep_peer_win.assign(size_t(world), nullptr);
+  for (int d = 0; d < world; ++d) {
+    if (d == rank) {
+      ctx->ep_peer_win[size_t(d)] = ctx->ep_win;
+      continue;
+    }
+    WMOE_CHECK_CUDA(ctx, cudaIpcOpenMemHandle(&ctx->ep_peer_win[size_t(d)], all[size_t(d)],
+                                              cudaIpcMemLazyEnablePeerAccess),
+                    "EP window import");
+  }
   return WMOE_OK;
 }
 
@@ -955,16 +1132,20 @@ static int ep_alltoallv(wmoe_ctx* ctx, const void* send, const int64_t* send_n, 
   const NcclApi& api = nccl();
   ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
   size_t so = 0, ro = 0;
-  WMOE_CHECK_NCCL(ctx, api.GroupStart(), where);
-  for (int d = 0; d < ctx->ep_world; ++d) {
+  // calls inside the group only queue; the group's end settles them
+  auto queued = [](ncclResult_t r) { return r == ncclSuccess || r == ncclInProgress; };
+  ncclResult_t r = api.GroupStart();
+  for (int d = 0; d < ctx->ep_world && queued(r); ++d) {
     if (send_n[d] > 0)
-      WMOE_CHECK_NCCL(ctx, api.Send(static_cast<const char*>(send) + so * elem, size_t(send_n[d]), type, d, comm, st), where);
-    if (recv_n[d] > 0)
-      WMOE_CHECK_NCCL(ctx, api.Recv(static_cast<char*>(recv) + ro * elem, size_t(recv_n[d]), type, d, comm, st), where);
+      r = api.Send(static_cast<const char*>(send) + so * elem, size_t(send_n[d]), type, d, comm, st);
+    if (recv_n[d] > 0 && queued(r))
+      r = api.Recv(static_cast<char*>(recv) + ro * elem, size_t(recv_n[d]), type, d, comm, st);
     so += size_t(send_n[d]);
     ro += size_t(recv_n[d]);
   }
-  WMOE_CHECK_NCCL(ctx, api.GroupEnd(), where);
+  const ncclResult_t end = api.GroupEnd();
+  if (!queued(r)) return nccl_fail(ctx, r, where);
+  WMOE_CHECK_NCCL(ctx, end, where);
   return WMOE_OK;
 }
 
@@ -982,6 +1163,9 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
                         const wmoe_layer_weights* w, void* out, int out_dtype, int32_t* topk_idx_out,
                         float* topk_w_out, void* stream) {
   if (!ctx) return WMOE_ERR_INVALID;
+  if (ctx->ep_dead)
+    return ctx_fail(ctx, WMOE_ERR_NCCL, "wmoe_moe_forward_ep: the communicator was aborted after a failure; "
+                                        "wmoe_ep_finalize, then wmoe_ep_init again");
   if (!ctx->nccl_comm) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: call wmoe_ep_init first");
   if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: bad store");
   const int world = ctx->ep_world, rank = ctx->ep_rank, E = store->experts, H = store->hidden, F = store->ffn;
@@ -1007,8 +1191,9 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   const size_t o_w = pa.take<float>(size_t(T) * k + 1);
   const size_t o_idx = pa.take<int32_t>(size_t(T) * k + 1);
   const size_t o_s = pa.take<float>(size_t(T) + 1);
-  // [send | recv][world][kCountWords]: per rank the chunk count, then (rows, pairs) of each chunk
-  const size_t o_cnt = pa.take<int32_t>(size_t(2) * world * kCountWords);
+  // send [world][kCountWords] (per destination the chunk count, then (rows, pairs) of each chunk), then every rank's
+  // send table all-gathered [world][world][kCountWords]
+  const size_t o_cnt = pa.take<int32_t>(size_t(world + world * world) * kCountWords);
   const size_t o_tok = pa.take<int32_t>(size_t(T) * kw + 1);
   const size_t o_pl = pa.take<int32_t>(size_t(T) * k * 2 + 2);
   const size_t o_ret = pa.take<int32_t>(size_t(T) * k + 1);
@@ -1028,7 +1213,7 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   int32_t* topk_idx = at<int32_t>(ctx, o_idx);
   float* shared_s = at<float>(ctx, o_s);
   int32_t* cnt_send = at<int32_t>(ctx, o_cnt);                    // [world][kCountWords]
-  int32_t* cnt_recv = cnt_send + size_t(world) * kCountWords;      // [world][kCountWords]
+  int32_t* cnt_all = cnt_send + size_t(world) * kCountWords;       // [source][destination][kCountWords]
   int32_t* send_tok = at<int32_t>(ctx, o_tok);
   int32_t* pair_list = at<int32_t>(ctx, o_pl);
   int32_t* ret_index = at<int32_t>(ctx, o_ret);
@@ -1055,28 +1240,60 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
                     "EP rows");
   }
   mark(1);
-  // every chunk's counts in one fixed-size exchange (kCountWords ints to and from each rank, whatever the chunk
-  // count), then one read of the transfer sizes
-  {
-    std::vector<int64_t> nn(static_cast<size_t>(world), kCountWords);
-    if (int rc = ep_alltoallv(ctx, cnt_send, nn.data(), cnt_recv, nn.data(), ncclInt32, 4, st, "EP counts")) return rc;
-  }
-  std::vector<int32_t> cnt(size_t(2) * world * kCountWords);
-  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(cnt.data(), cnt_send, cnt.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+  // every rank's send table to every rank in one fixed-size all-gather, then one bounded read of all of it: each
+  // rank then knows every transfer, so every rank computes the same window layouts
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
+  WMOE_CHECK_NCCL(ctx, nccl().AllGather(cnt_send, cnt_all, size_t(world) * kCountWords, ncclInt32, comm, st),
+                  "EP counts");
+  std::vector<int32_t> cnt(size_t(world) * world * kCountWords);
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(cnt.data(), cnt_all, cnt.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
                   "EP counts read-back");
-  WMOE_CHECK_CUDA(ctx, cudaStreamSynchronize(st), "EP counts read-back");
+  if (int rc = ep_wait(ctx, st, "EP counts read-back")) return rc;
   mark(2);
-  const int32_t* cr = cnt.data() + size_t(world) * kCountWords;
-  for (int s = 0; s < world; ++s)
-    if (cr[size_t(s) * kCountWords] != C)
-      return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: ranks use different chunk counts (wmoe_ep_set_chunks)");
-  auto sr = [&](int d, int c) { return cnt[size_t(d) * kCountWords + 1 + 2 * c]; };  // rows of chunk c to d
-  auto sp = [&](int d, int c) { return cnt[size_t(d) * kCountWords + 2 + 2 * c]; };  // pairs of chunk c to d
-  auto rr = [&](int s, int c) { return cr[size_t(s) * kCountWords + 1 + 2 * c]; };   // rows from s
-  auto rp = [&](int s, int c) { return cr[size_t(s) * kCountWords + 2 + 2 * c]; };   // pairs from s
-  // stage B: per-chunk receive, result and return buffers, and one expert-stage scratch, in the EP buffer
-  std::vector<size_t> o_recv(C), o_rpl(C), o_y(C), o_yret(C);
-  std::vector<int> Pc(C), Rc(C), Sc(C), Tc(C), T0(C);
+  auto A = [&](int s_, int d_, int i) { return cnt[(size_t(s_) * world + d_) * kCountWords + i]; };
+  for (int s_ = 0; s_ < world; ++s_)
+    for (int d_ = 0; d_ < world; ++d_)
+      if (A(s_, d_, 0) != C)
+        return ctx_fail(ctx, WMOE_ERR_INVALID,
+                        "wmoe_moe_forward_ep: ranks use different chunk counts (wmoe_ep_set_chunks)");
+  auto sr = [&](int d, int c) { return A(rank, d, 1 + 2 * c); };  // rows of chunk c to d
+  auto sp = [&](int d, int c) { return A(rank, d, 2 + 2 * c); };  // pairs of chunk c to d
+  auto rr = [&](int s_, int c) { return A(s_, rank, 1 + 2 * c); };  // rows from s
+  auto rp = [&](int s_, int c) { return A(s_, rank, 2 + 2 * c); };  // pairs from s
+  auto a256 = [](size_t b) { return (b + 255) / 256 * 256; };
+  // rank q's window: per chunk the rows it receives, their pair lists, and the result rows that come back to it
+  struct Layout {
+    std::vector<size_t> rows, pairs, ret;
+    size_t total = 0;
+  };
+  auto layout = [&](int q) {
+    Layout L;
+    for (int c = 0; c < C; ++c) {
+      size_t R = 0, P = 0, S = 0;
+      for (int o = 0; o < world; ++o) R += size_t(A(o, q, 1 + 2 * c)), P += size_t(A(o, q, 2 + 2 * c)),
+                                      S += size_t(A(q, o, 2 + 2 * c));
+      L.rows.push_back(L.total);
+      L.total += a256(R * H * 2);
+      L.pairs.push_back(L.total);
+      L.total += a256(P * 8);
+      L.ret.push_back(L.total);
+      L.total += a256(S * H * 2);
+    }
+    return L;
+  };
+  std::vector<Layout> lay;
+  size_t need = 0;
+  for (int q = 0; q < world; ++q) {
+    lay.push_back(layout(q));
+    need = std::max(need, lay.back().total);
+  }
+  const bool ipc = ctx->ep_ipc;
+  if (ipc)
+    if (int rc = ep_grow_windows(ctx, need, st)) return rc;
+  // stage B in the EP buffer: per chunk the expert results (and, on the NCCL path, the received and returned rows),
+  // and one expert-stage scratch
+  std::vector<size_t> o_y(C), o_recv(C), o_rpl(C), o_yret(C);
+  std::vector<int> Pc(C), Tc(C), T0(C);
   Plan pb;
   size_t es = 0;
   for (int c = 0; c < C; ++c) {
@@ -1089,35 +1306,87 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
       rrow[d] = rr(d, c), rpair[d] = rp(d, c);
     }
     if (int rc = check_ep_counts(ctx, world, rrow.data(), rpair.data(), Tc[c], "wmoe_moe_forward_ep")) return rc;
-    Rc[c] = int(R), Pc[c] = int(P), Sc[c] = int(S);
-    o_recv[c] = pb.take<uint16_t>(size_t(R) * H + 8);
-    o_rpl[c] = pb.take<int32_t>(size_t(P) * 2 + 2);
+    Pc[c] = int(P);
     o_y[c] = pb.take<uint16_t>((size_t(P) + Tc[c]) * H + 8);
-    o_yret[c] = pb.take<uint16_t>(size_t(S) * H + 8);
+    if (!ipc) {
+      o_recv[c] = pb.take<uint16_t>(size_t(R) * H + 8);
+      o_rpl[c] = pb.take<int32_t>(size_t(P) * 2 + 2);
+      o_yret[c] = pb.take<uint16_t>(size_t(S) * H + 8);
+    }
     es = std::max(es, ep_experts_scratch_bytes(Pc[c], Tc[c], E, H, F));
   }
   const size_t o_es = pb.take<char>(es);
   if (int rc = ensure_ep_buf(ctx, pb.bytes)) return rc;
   char* eb = static_cast<char*>(ctx->ep_buf);
+  char* win = static_cast<char*>(ctx->ep_win);
+  auto recv_rows = [&](int c) { return ipc ? win + lay[rank].rows[c] : eb + o_recv[c]; };
+  auto recv_pairs = [&](int c) { return ipc ? win + lay[rank].pairs[c] : eb + o_rpl[c]; };
+  auto returned = [&](int c) { return ipc ? win + lay[rank].ret[c] : eb + o_yret[c]; };
   cudaEvent_t* ev = ctx->ep_events.data();  // [0] planned, then per chunk: rows arrived, results made, results back
   WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[0], st), "EP ordering");
   WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ev[0], 0), "EP ordering");
+  // copies of one exchange into the peers' windows, one stream per destination (the copy engines run them
+  // together and take no SM), joined on the communication stream, then the barrier
+  auto copy_out = [&](const std::vector<const char*>& src, const std::vector<char*>& dst,
+                      const std::vector<size_t>& bytes, cudaEvent_t after, const char* where) -> int {
+    for (int d = 0; d < world; ++d) {
+      if (!bytes[size_t(d)]) continue;
+      cudaStream_t ps = ctx->ep_peer_streams[size_t(d)];
+      WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(ps, after, 0), where);
+      WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(dst[size_t(d)], src[size_t(d)], bytes[size_t(d)], cudaMemcpyDeviceToDevice,
+                                           ps),
+                      where);
+      WMOE_CHECK_CUDA(ctx, cudaEventRecord(ctx->ep_peer_events[size_t(d)], ps), where);
+      WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ctx->ep_peer_events[size_t(d)], 0), where);
+    }
+    return ep_barrier(ctx, cs, where);
+  };
   std::vector<int64_t> sn(static_cast<size_t>(world)), rn(static_cast<size_t>(world));
-  // dispatch exchanges of every chunk, in order, on the communication stream
+  // dispatch exchanges of every chunk, in order
   for (int c = 0; c < C; ++c) {
     const size_t t0 = size_t(T0[c]);
-    for (int d = 0; d < world; ++d) sn[d] = int64_t(sr(d, c)) * H, rn[d] = int64_t(rr(d, c)) * H;
-    if (int rc = ep_alltoallv(ctx, send_buf + t0 * kw * H, sn.data(), eb + o_recv[c], rn.data(), ncclHalf, 2, cs,
-                              "EP dispatch rows"))
-      return rc;
-    for (int d = 0; d < world; ++d) sn[d] = int64_t(sp(d, c)) * 2, rn[d] = int64_t(rp(d, c)) * 2;
-    if (int rc = ep_alltoallv(ctx, pair_list + t0 * k * 2, sn.data(), eb + o_rpl[c], rn.data(), ncclInt32, 4, cs,
-                              "EP dispatch pairs"))
-      return rc;
+    if (ipc) {
+      std::vector<const char*> src(static_cast<size_t>(world));
+      std::vector<char*> dst(static_cast<size_t>(world));
+      std::vector<size_t> bytes(static_cast<size_t>(world));
+      size_t so = 0;
+      for (int d = 0; d < world; ++d) {  // rows: this rank's block sits after the blocks of lower ranks
+        size_t before = 0;
+        for (int o = 0; o < rank; ++o) before += size_t(A(o, d, 1 + 2 * c));
+        src[size_t(d)] = reinterpret_cast<const char*>(send_buf + (t0 * kw + so) * H);
+        dst[size_t(d)] = static_cast<char*>(ctx->ep_peer_win[size_t(d)]) + lay[d].rows[c] + before * H * 2;
+        bytes[size_t(d)] = size_t(sr(d, c)) * H * 2;
+        so += size_t(sr(d, c));
+      }
+      if (int rc = copy_out(src, dst, bytes, ev[0], "EP dispatch rows")) return rc;
+      so = 0;
+      for (int d = 0; d < world; ++d) {  // pair lists, laid out the same way
+        size_t before = 0;
+        for (int o = 0; o < rank; ++o) before += size_t(A(o, d, 2 + 2 * c));
+        src[size_t(d)] = reinterpret_cast<const char*>(pair_list + (t0 * k + so) * 2);
+        dst[size_t(d)] = static_cast<char*>(ctx->ep_peer_win[size_t(d)]) + lay[d].pairs[c] + before * 8;
+        bytes[size_t(d)] = size_t(sp(d, c)) * 8;
+        so += size_t(sp(d, c));
+      }
+      if (int rc = copy_out(src, dst, bytes, ev[0], "EP dispatch pairs")) return rc;
+    } else {
+      for (int d = 0; d < world; ++d) sn[d] = int64_t(sr(d, c)) * H, rn[d] = int64_t(rr(d, c)) * H;
+      if (int rc = ep_alltoallv(ctx, send_buf + t0 * kw * H, sn.data(), recv_rows(c), rn.data(), ncclHalf, 2, cs,
+                                "EP dispatch rows"))
+        return rc;
+      for (int d = 0; d < world; ++d) sn[d] = int64_t(sp(d, c)) * 2, rn[d] = int64_t(rp(d, c)) * 2;
+      if (int rc = ep_alltoallv(ctx, pair_list + t0 * k * 2, sn.data(), recv_pairs(c), rn.data(), ncclInt32, 4, cs,
+                                "EP dispatch pairs"))
+        return rc;
+    }
     WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[1 + 3 * c], cs), "EP ordering");
   }
   ctx->launches += uint64_t(n);
   n = 0;
+  // SMs the persistent GEMMs leave free while exchanges overlap them: NCCL's send/recv kernels need many; on the
+  // copy-engine path only the barriers' one-CTA all-reduces need room
+  const int gemm_sms = world > 1 && C > 1 ? std::max(1, ctx->sm_count - (ipc ? kEpBarrierSms : kEpCommSms))
+                                          : ctx->sm_count;
   // expert stage of each chunk once its rows are in; its results go back while the next chunk computes
   for (int c = 0; c < C; ++c) {
     WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(st, ev[1 + 3 * c], 0), "EP ordering");
@@ -1126,16 +1395,32 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
     for (int d = 0; d < world; ++d) rrow[d] = rr(d, c), rpair[d] = rp(d, c);
     uint16_t* y = reinterpret_cast<uint16_t*>(eb + o_y[c]);
     if (int rc = ep_experts_impl(ctx, store, layer, world, rrow.data(), rpair.data(),
-                                 reinterpret_cast<const uint16_t*>(eb + o_recv[c]),
-                                 reinterpret_cast<const int32_t*>(eb + o_rpl[c]),
+                                 reinterpret_cast<const uint16_t*>(recv_rows(c)),
+                                 reinterpret_cast<const int32_t*>(recv_pairs(c)),
                                  static_cast<const char*>(x) + size_t(T0[c]) * H * xsz, x_dtype, Tc[c], w, y, eb + o_es,
-                                 st, world > 1 && C > 1 ? std::max(1, ctx->sm_count - kEpCommSms) : ctx->sm_count))
+                                 st, gemm_sms))
       return rc;
     WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[2 + 3 * c], st), "EP ordering");
     WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ev[2 + 3 * c], 0), "EP ordering");
-    for (int d = 0; d < world; ++d) sn[d] = int64_t(rp(d, c)) * H, rn[d] = int64_t(sp(d, c)) * H;
-    if (int rc = ep_alltoallv(ctx, y, sn.data(), eb + o_yret[c], rn.data(), ncclHalf, 2, cs, "EP combine rows"))
-      return rc;
+    if (ipc) {
+      std::vector<const char*> src(static_cast<size_t>(world));
+      std::vector<char*> dst(static_cast<size_t>(world));
+      std::vector<size_t> bytes(static_cast<size_t>(world));
+      size_t yo = 0;
+      for (int s_ = 0; s_ < world; ++s_) {  // results for source s into its return block, after lower ranks' blocks
+        size_t before = 0;
+        for (int o = 0; o < rank; ++o) before += size_t(A(s_, o, 2 + 2 * c));
+        src[size_t(s_)] = reinterpret_cast<const char*>(y + yo * H);
+        dst[size_t(s_)] = static_cast<char*>(ctx->ep_peer_win[size_t(s_)]) + lay[s_].ret[c] + before * H * 2;
+        bytes[size_t(s_)] = size_t(rp(s_, c)) * H * 2;
+        yo += size_t(rp(s_, c));
+      }
+      if (int rc = copy_out(src, dst, bytes, ev[2 + 3 * c], "EP combine rows")) return rc;
+    } else {
+      for (int d = 0; d < world; ++d) sn[d] = int64_t(rp(d, c)) * H, rn[d] = int64_t(sp(d, c)) * H;
+      if (int rc = ep_alltoallv(ctx, y, sn.data(), returned(c), rn.data(), ncclHalf, 2, cs, "EP combine rows"))
+        return rc;
+    }
     WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[3 + 3 * c], cs), "EP ordering");
   }
   mark(4);
@@ -1147,7 +1432,7 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
     const uint16_t* y = reinterpret_cast<const uint16_t*>(eb + o_y[c]);
     WMOE_CHECK_CUDA(ctx,
                     combine_rows(Tc[c], k, H, topk_idx + t0 * k, topk_w + t0 * k, ret_index + t0 * k, shared_s + t0,
-                                 reinterpret_cast<const __half*>(eb + o_yret[c]),
+                                 reinterpret_cast<const __half*>(returned(c)),
                                  reinterpret_cast<const __half*>(y) + size_t(Pc[c]) * H,
                                  static_cast<char*>(out) + t0 * H * osz, out_dtype, st, &n),
                     "EP combine");

@@ -141,6 +141,8 @@ constexpr int kMaxEpChunks = 16;
 constexpr int kCountWords = 1 + 2 * kMaxEpChunks;  // per rank in the EP count exchange: chunks, then rows / pairs
 // SMs the persistent GEMMs leave free while exchanges overlap them, so that NCCL's kernels find room
 constexpr int kEpCommSms = 16;
+// the same on the copy-engine exchange path, where only the barriers' one-CTA all-reduces run beside the GEMMs
+constexpr int kEpBarrierSms = 4;
 size_t ep_plan_scratch_bytes(int T, int world);
 cudaError_t ep_count_header(int32_t* cnt, int world, int words, int chunks, cudaStream_t st, int* launches);
 // send_rows[d * count_stride], send_pairs[d * count_stride]: rows and pairs to rank d

@@ -33,6 +33,17 @@ struct wmoe_ctx {
   cudaStream_t ep_stream = nullptr;     // the exchanges (overlapping the expert stage on the caller's stream)
   std::vector<cudaEvent_t> ep_events;   // ordering between the two streams
   int ep_chunks = 1;                    // token chunks per layer (wmoe_ep_set_chunks), the same on every rank
+  int ep_timeout_ms = 30000;            // bound of every host wait on the communicator (wmoe_ep_set_timeout)
+  bool ep_dead = false;                 // the communicator was aborted after a failure; wmoe_ep_finalize, then init
+  // exchange windows: this rank's device buffer, written by the peers' copy engines through CUDA IPC
+  bool ep_ipc = false;                  // windows mapped on every rank (else the rows go through NCCL send/recv)
+  void* ep_win = nullptr;
+  size_t ep_win_bytes = 0;              // the same on every rank
+  std::vector<void*> ep_peer_win;       // [world]: every rank's window in this process (own one included)
+  std::vector<cudaStream_t> ep_peer_streams;  // one per destination rank: copies to different ranks run together
+  std::vector<cudaEvent_t> ep_peer_events;
+  int* ep_flag = nullptr;               // one int: the all-reduce that serves as the exchanges' barrier
+  void* ep_handles = nullptr;           // [world][sizeof(cudaIpcMemHandle_t)] device staging of the handle all-gather
   // per-phase CUDA events of the last profile_calls multi-token MoE calls (opt-in): [profile_calls][kProfMarks]
   static constexpr int kProfMarks = 7;
   std::vector<cudaEvent_t> prof_events;

@@ -28,6 +28,7 @@ SIGNATURES = {
     "wmoe_set_trace": (_i, [_p, _p, _sz]),
     "wmoe_set_prefill_threshold": (_i, [_p, _i]),
     "wmoe_set_min_expert_weight": (_i, [_p, _f]),
+    "wmoe_ep_set_timeout": (_i, [_p, _i]),
     "wmoe_set_profiling": (_i, [_p, _i]),
     "wmoe_phase_ms": (_i, [_p, _i, _i, ctypes.POINTER(_f)]),
     "wmoe_decode_ctas": (_i, [_p]),

@@ -68,6 +68,10 @@ class Context:
         if v:
             raise _lib.WmoeError(_lib.ERR_DEVICE, _lib.STATUS_NAMES.get(v, f"device status {v}"))
 
+    def ep_set_timeout(self, ms: int) -> int:
+        """Bound of every host wait on the expert-parallel communicator (wmoe_ep_set_timeout); returns the old one."""
+        return int(lib.wmoe_ep_set_timeout(self.handle, int(ms)))
+
     def ep_finalize(self):
         """Frees the NCCL communicator of ep_init (every rank, before the process group goes away)."""
         check(self.handle, lib.wmoe_ep_finalize(self.handle))
