@@ -142,8 +142,13 @@ def _leave_rank(rank, world, port, outdir):
     mine = torch.from_numpy(np.array_split(synth.hidden(SEED, TOKENS, step=9), world)[rank])
     moe_forward_ep(store, LAYER, mine, None, ops=OracleEPOps(), out_dtype=torch.float32)
     dist.barrier()
-    if rank == 1:
+    ready = os.path.join(outdir, "rank0_out_of_barrier")
+    if rank == 1:  # leaves once rank 0 is past the barrier (so that only the next exchange sees it gone)
+        while not os.path.exists(ready):
+            time.sleep(0.05)
         os._exit(0)
+    open(ready, "w").close()
+    time.sleep(1.0)
     t0 = time.time()
     failed = False
     try:
@@ -164,6 +169,9 @@ def test_ep_rank_leaving_fails_the_next_exchange():
         deadline = time.time() + 120
         while not ctxs.join(timeout=max(1.0, deadline - time.time())) and time.time() < deadline:
             pass
+        for p in ctxs.processes:
+            if p.is_alive():
+                p.kill()
         failed, waited = np.load(os.path.join(d, "left.npy"))
     assert failed == 1.0 and waited < 30.0, (failed, waited)
 

@@ -201,24 +201,39 @@ def _leave_rank(rank, world, port, outdir):
     first = moe.moe_forward_ep_native(store, LAYER, x, lw)
     torch.cuda.synchronize()
     dist.barrier()
+    ready = os.path.join(outdir, "rank0_out_of_barrier")
     if rank == 1:
-        ctx.ep_finalize()
+        torch.cuda.synchronize()  # nothing of it in flight
+        while not os.path.exists(ready):  # rank 0 is past the barrier: only its next layer sees this rank gone
+            time.sleep(0.05)
         np.save(os.path.join(outdir, "left1.npy"), np.array([1.0]))
-        os._exit(0)  # leaves without a goodbye, as a failed rank would
+        os._exit(0)  # leaves without a goodbye (no finalize, no destroy), as a failed rank would
+    open(ready, "w").close()
     time.sleep(1.0)
+
+    def say(what):
+        print(f"rank 0: {what} at {time.time() - t0:.2f} s", flush=True)
+
     t0 = time.time()
     code = 0
     try:
         moe.moe_forward_ep_native(store, LAYER, x, lw)
+        say("call returned")
         torch.cuda.synchronize()
     except WmoeError as e:
         code = e.code
+        say(f"error {e}")
     waited = time.time() - t0
-    # the communicator is gone, the GPU is not: a single-GPU layer on this rank's experts still runs
+    # the communicator is gone, the GPU is not: a single-GPU layer still runs, with a clean device status
     ctx.ep_finalize()
-    again = moe.moe_forward(store, LAYER, x, lw)
+    say("finalized")
+    full = moe.ExpertStore(1, ctx=ctx)
+    full.fill_synthetic(SEED)
+    again = moe.moe_forward(full, LAYER, x, lw)
     torch.cuda.synchronize()
     ok = bool(torch.isfinite(again.float()).all()) and bool(torch.isfinite(first.float()).all())
+    ok = ok and ctx.device_status() == 0
+    say("single-GPU layer ran")
     np.save(os.path.join(outdir, "left0.npy"), np.array([float(code == ERR_NCCL), waited, float(ok)]))
     os._exit(0)
 
@@ -236,6 +251,9 @@ def test_ep_rank_leaving_is_an_nccl_error():
         deadline = time.time() + 120
         while not ctxs.join(timeout=max(1.0, deadline - time.time())) and time.time() < deadline:
             pass
+        for p in ctxs.processes:  # a rank still running at the deadline is a failure; it must not outlive the test
+            if p.is_alive():
+                p.kill()
         assert os.path.exists(os.path.join(d, "left1.npy"))
         nccl_error, waited, ok = np.load(os.path.join(d, "left0.npy"))
         assert nccl_error == 1.0 and ok == 1.0

@@ -2,8 +2,10 @@
 // dequant.cu, route.cu, dispatch.cu, gemv.cu, decode.cu and store.cu.
 #include <dlfcn.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstdlib>
+#include <memory>
 #include <cstring>
 #include <thread>
 #include <nccl.h>
@@ -845,6 +847,7 @@ struct NcclApi {
   ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
@@ -869,6 +872,7 @@ static NcclApi& nccl() {
       api.CommInitRankConfig = reinterpret_cast<decltype(api.CommInitRankConfig)>(get("ncclCommInitRankConfig"));
       api.CommGetAsyncError = reinterpret_cast<decltype(api.CommGetAsyncError)>(get("ncclCommGetAsyncError"));
       api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(get("ncclCommAbort"));
+      api.CommFinalize = reinterpret_cast<decltype(api.CommFinalize)>(get("ncclCommFinalize"));
       api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(get("ncclCommDestroy"));
       api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(get("ncclGroupStart"));
       api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(get("ncclGroupEnd"));
@@ -878,7 +882,7 @@ static NcclApi& nccl() {
       api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(get("ncclAllReduce"));
       api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(get("ncclGetErrorString"));
       api.ok = api.GetUniqueId && api.CommInitRankConfig && api.CommGetAsyncError && api.CommAbort &&
-               api.CommDestroy && api.GroupStart && api.GroupEnd && api.Send && api.Recv && api.AllGather &&
+               api.CommFinalize && api.CommDestroy && api.GroupStart && api.GroupEnd && api.Send && api.Recv && api.AllGather &&
                api.AllReduce && api.GetErrorString;
     }
   }
@@ -887,22 +891,45 @@ static NcclApi& nccl() {
 
 static void ep_release(wmoe_ctx* ctx);
 
+static long long now_ms() {
+  return std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+// One step of a host poll: spins (yielding the core) for the first 5 ms of a wait, then sleeps 50 us at a time. A
+// sleep from the start would cost every settled call and every count read-back the timer slack (~50 us or more).
+static void poll_pause(long long t0) {
+  if (now_ms() - t0 < 5)
+    std::this_thread::yield();
+  else
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+}
+
+// ncclCommAbort on a helper thread, waited for at most timeout_ms: the abort makes the communicator's kernels
+// return and frees its resources; should it itself not return, the host is not held (the thread is left to it).
+// Returns whether it finished.
+static bool abort_comm(ncclComm_t comm, int timeout_ms) {
+  auto done = std::make_shared<std::atomic<bool>>(false);
+  std::thread([comm, done] {
+    nccl().CommAbort(comm);
+    done->store(true);
+  }).detach();
+  const long long t0 = now_ms();
+  while (!done->load() && now_ms() - t0 <= timeout_ms) poll_pause(t0);
+  return done->load();
+}
+
 // A failure of the communicator: the context aborts it (its kernels in flight return) and keeps no exchange state;
 // every later EP call fails until wmoe_ep_finalize and a new wmoe_ep_init.
 static int nccl_fail(wmoe_ctx* ctx, ncclResult_t r, const char* where) {
   std::string msg = std::string(where) + ": " + nccl().GetErrorString(r);
   if (ctx->nccl_comm) {
-    nccl().CommAbort(static_cast<ncclComm_t>(ctx->nccl_comm));
+    const bool aborted = abort_comm(static_cast<ncclComm_t>(ctx->nccl_comm), ctx->ep_timeout_ms);
     ctx->nccl_comm = nullptr;
     ctx->ep_dead = true;
-    msg += " (communicator aborted)";
+    msg += aborted ? " (communicator aborted)" : " (communicator abort did not finish in time)";
   }
   return ctx_fail(ctx, WMOE_ERR_NCCL, msg);
-}
-
-static long long now_ms() {
-  return std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now().time_since_epoch())
-      .count();
 }
 
 // The communicator is non-blocking: a call may return ncclInProgress and finish in the background. Waits, for at
@@ -919,7 +946,7 @@ static int nccl_settle(wmoe_ctx* ctx, ncclResult_t r, const char* where) {
     if (state != ncclInProgress) return nccl_fail(ctx, state, where);
     if (now_ms() - t0 > ctx->ep_timeout_ms)
       return nccl_fail(ctx, ncclRemoteError, (std::string(where) + ": timed out").c_str());
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+    poll_pause(t0);
   }
 }
 
@@ -941,7 +968,7 @@ static int ep_wait(wmoe_ctx* ctx, cudaStream_t st, const char* where) {
     if (state != ncclSuccess && state != ncclInProgress) return nccl_fail(ctx, state, where);
     if (now_ms() - t0 > ctx->ep_timeout_ms)
       return nccl_fail(ctx, ncclRemoteError, (std::string(where) + ": timed out waiting for the other ranks").c_str());
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+    poll_pause(t0);
   }
 }
 
@@ -997,9 +1024,36 @@ static void ep_close_windows(wmoe_ctx* ctx) {
   ctx->ep_win_bytes = 0;
 }
 
-static void ep_release(wmoe_ctx* ctx) {
-  if (ctx->nccl_comm) nccl().CommDestroy(static_cast<ncclComm_t>(ctx->nccl_comm));
+// Ends the communicator: ncclCommFinalize is collective (it waits for the other ranks' finalize), so its completion
+// is polled for at most the context's timeout, and a communicator whose finalize does not complete (a rank left) is
+// aborted instead of waited on.
+static void ep_end_comm(wmoe_ctx* ctx) {
+  if (!ctx->nccl_comm) return;
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
   ctx->nccl_comm = nullptr;
+  const ncclResult_t r = nccl().CommFinalize(comm);
+  bool done = r == ncclSuccess;
+  if (r == ncclInProgress) {
+    const long long t0 = now_ms();
+    for (;;) {
+      ncclResult_t state = ncclSuccess;
+      if (nccl().CommGetAsyncError(comm, &state) != ncclSuccess) break;
+      if (state == ncclSuccess) {
+        done = true;
+        break;
+      }
+      if (state != ncclInProgress || now_ms() - t0 > ctx->ep_timeout_ms) break;
+      poll_pause(t0);
+    }
+  }
+  if (done)
+    nccl().CommDestroy(comm);
+  else
+    abort_comm(comm, ctx->ep_timeout_ms);
+}
+
+static void ep_release(wmoe_ctx* ctx) {
+  ep_end_comm(ctx);
   ctx->ep_dead = false;
   ep_close_windows(ctx);
   for (cudaStream_t s : ctx->ep_peer_streams)
@@ -1012,6 +1066,10 @@ static void ep_release(wmoe_ctx* ctx) {
   ctx->ep_flag = nullptr;
   cudaFree(ctx->ep_handles);
   ctx->ep_handles = nullptr;
+  cudaFreeHost(ctx->ep_host_counts);
+  ctx->ep_host_counts = nullptr;
+  cudaFreeHost(ctx->ep_host_handles);
+  ctx->ep_host_handles = nullptr;
   ctx->ep_ipc = false;
   for (cudaEvent_t e : ctx->ep_events)
     if (e) cudaEventDestroy(e);
@@ -1027,10 +1085,28 @@ static void ep_release(wmoe_ctx* ctx) {
 int wmoe_ep_finalize(wmoe_ctx* ctx) {
   if (!ctx) return WMOE_ERR_INVALID;
   cudaSetDevice(ctx->device);
-  // after an abort the device may still hold the aborted kernels' streams: a bounded wait, then release anyway
-  const cudaError_t e = ctx->ep_dead ? cudaSuccess : cudaDeviceSynchronize();
+  if (!ctx->ep_dead) {
+    const cudaError_t e = cudaDeviceSynchronize();
+    ep_release(ctx);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_ep_finalize");
+    return WMOE_OK;
+  }
+  // after an abort: the aborted kernels return, so the EP streams drain; wait for that for at most the timeout
+  // (cudaFree and cudaDeviceSynchronize would block for good behind a stream that did not)
+  std::vector<cudaStream_t> streams(ctx->ep_peer_streams);
+  streams.push_back(ctx->ep_stream);
+  const long long t0 = now_ms();
+  bool drained = false;
+  while (!drained && now_ms() - t0 <= ctx->ep_timeout_ms) {
+    drained = true;
+    for (cudaStream_t s : streams)
+      if (s && cudaStreamQuery(s) == cudaErrorNotReady) drained = false;
+    if (!drained) poll_pause(t0);
+  }
+  if (!drained)
+    return ctx_fail(ctx, WMOE_ERR_NCCL, "wmoe_ep_finalize: the exchange streams did not drain after the abort; "
+                                        "their buffers are left allocated");
   ep_release(ctx);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_ep_finalize");
   return WMOE_OK;
 }
 
@@ -1050,6 +1126,10 @@ static int ep_setup_windows(wmoe_ctx* ctx) {
   WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->ep_flag, 256), "wmoe_ep_init");
   WMOE_CHECK_CUDA(ctx, cudaMemset(ctx->ep_flag, 0, 256), "wmoe_ep_init");
   WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->ep_handles, size_t(world) * sizeof(cudaIpcMemHandle_t)), "wmoe_ep_init");
+  WMOE_CHECK_CUDA(ctx, cudaMallocHost(&ctx->ep_host_counts, size_t(kMaxRanks) * kMaxRanks * kCountWords * 4),
+                  "wmoe_ep_init");
+  WMOE_CHECK_CUDA(ctx, cudaMallocHost(&ctx->ep_host_handles, size_t(kMaxRanks) * sizeof(cudaIpcMemHandle_t)),
+                  "wmoe_ep_init");
   ctx->ep_ipc = std::getenv("WMOE_EP_NCCL_ROWS") == nullptr;  // the NCCL send/recv path, for comparison
   return WMOE_OK;
 }
@@ -1092,8 +1172,8 @@ static int ep_grow_windows(wmoe_ctx* ctx, size_t need, cudaStream_t st) {
   WMOE_CHECK_NCCL(ctx, nccl().AllGather(staged + size_t(rank) * sizeof(mine), staged, sizeof(mine), ncclUint8,
                                         static_cast<ncclComm_t>(ctx->nccl_comm), st),
                   "EP windows");
-  std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(world));
-  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(all.data(), staged, size_t(world) * sizeof(mine), cudaMemcpyDeviceToHost, st),
+  cudaIpcMemHandle_t* all = static_cast<cudaIpcMemHandle_t*>(ctx->ep_host_handles);  // pinned: the copy is async
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(all, staged, size_t(world) * sizeof(mine), cudaMemcpyDeviceToHost, st),
                   "EP windows");
   if (int rc = ep_wait(ctx, st, "EP windows")) return rc;
   ctx->ep_peer_win.assign(size_t(world), nullptr);
@@ -1102,7 +1182,7 @@ static int ep_grow_windows(wmoe_ctx* ctx, size_t need, cudaStream_t st) {
       ctx->ep_peer_win[size_t(d)] = ctx->ep_win;
       continue;
     }
-    WMOE_CHECK_CUDA(ctx, cudaIpcOpenMemHandle(&ctx->ep_peer_win[size_t(d)], all[size_t(d)],
+    WMOE_CHECK_CUDA(ctx, cudaIpcOpenMemHandle(&ctx->ep_peer_win[size_t(d)], all[d],
                                               cudaIpcMemLazyEnablePeerAccess),
                     "EP window import");
   }
@@ -1245,10 +1325,13 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
   WMOE_CHECK_NCCL(ctx, nccl().AllGather(cnt_send, cnt_all, size_t(world) * kCountWords, ncclInt32, comm, st),
                   "EP counts");
-  std::vector<int32_t> cnt(size_t(world) * world * kCountWords);
-  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(cnt.data(), cnt_all, cnt.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+  const size_t n_cnt = size_t(world) * world * kCountWords;
+  // into pinned memory, so that the copy is asynchronous and the host's wait for it is ep_wait's bounded poll
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(ctx->ep_host_counts, cnt_all, n_cnt * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                       st),
                   "EP counts read-back");
   if (int rc = ep_wait(ctx, st, "EP counts read-back")) return rc;
+  const std::vector<int32_t> cnt(ctx->ep_host_counts, ctx->ep_host_counts + n_cnt);
   mark(2);
   auto A = [&](int s_, int d_, int i) { return cnt[(size_t(s_) * world + d_) * kCountWords + i]; };
   for (int s_ = 0; s_ < world; ++s_)
@@ -1327,15 +1410,20 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ev[0], 0), "EP ordering");
   // copies of one exchange into the peers' windows, one stream per destination (the copy engines run them
   // together and take no SM), joined on the communication stream, then the barrier
-  auto copy_out = [&](const std::vector<const char*>& src, const std::vector<char*>& dst,
-                      const std::vector<size_t>& bytes, cudaEvent_t after, const char* where) -> int {
+  struct Copy {
+    const char* src;
+    char* dst;
+    size_t bytes;
+  };
+  auto copy_out = [&](const std::vector<std::vector<Copy>>& per_dest, cudaEvent_t after, const char* where) -> int {
     for (int d = 0; d < world; ++d) {
-      if (!bytes[size_t(d)]) continue;
+      size_t total = 0;
+      for (const Copy& cp : per_dest[size_t(d)]) total += cp.bytes;
+      if (!total) continue;
       cudaStream_t ps = ctx->ep_peer_streams[size_t(d)];
       WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(ps, after, 0), where);
-      WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(dst[size_t(d)], src[size_t(d)], bytes[size_t(d)], cudaMemcpyDeviceToDevice,
-                                           ps),
-                      where);
+      for (const Copy& cp : per_dest[size_t(d)])
+        if (cp.bytes) WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(cp.dst, cp.src, cp.bytes, cudaMemcpyDeviceToDevice, ps), where);
       WMOE_CHECK_CUDA(ctx, cudaEventRecord(ctx->ep_peer_events[size_t(d)], ps), where);
       WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ctx->ep_peer_events[size_t(d)], 0), where);
     }
@@ -1346,29 +1434,22 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   for (int c = 0; c < C; ++c) {
     const size_t t0 = size_t(T0[c]);
     if (ipc) {
-      std::vector<const char*> src(static_cast<size_t>(world));
-      std::vector<char*> dst(static_cast<size_t>(world));
-      std::vector<size_t> bytes(static_cast<size_t>(world));
-      size_t so = 0;
-      for (int d = 0; d < world; ++d) {  // rows: this rank's block sits after the blocks of lower ranks
-        size_t before = 0;
-        for (int o = 0; o < rank; ++o) before += size_t(A(o, d, 1 + 2 * c));
-        src[size_t(d)] = reinterpret_cast<const char*>(send_buf + (t0 * kw + so) * H);
-        dst[size_t(d)] = static_cast<char*>(ctx->ep_peer_win[size_t(d)]) + lay[d].rows[c] + before * H * 2;
-        bytes[size_t(d)] = size_t(sr(d, c)) * H * 2;
-        so += size_t(sr(d, c));
+      // rows and pair lists of every destination in one exchange: this rank's blocks sit after those of lower ranks
+      std::vector<std::vector<Copy>> per_dest(static_cast<size_t>(world));
+      size_t so_rows = 0, so_pairs = 0;
+      for (int d = 0; d < world; ++d) {
+        size_t rows_before = 0, pairs_before = 0;
+        for (int o = 0; o < rank; ++o)
+          rows_before += size_t(A(o, d, 1 + 2 * c)), pairs_before += size_t(A(o, d, 2 + 2 * c));
+        char* w = static_cast<char*>(ctx->ep_peer_win[size_t(d)]);
+        per_dest[size_t(d)].push_back({reinterpret_cast<const char*>(send_buf + (t0 * kw + so_rows) * H),
+                                       w + lay[d].rows[c] + rows_before * H * 2, size_t(sr(d, c)) * H * 2});
+        per_dest[size_t(d)].push_back({reinterpret_cast<const char*>(pair_list + (t0 * k + so_pairs) * 2),
+                                       w + lay[d].pairs[c] + pairs_before * 8, size_t(sp(d, c)) * 8});
+        so_rows += size_t(sr(d, c));
+        so_pairs += size_t(sp(d, c));
       }
-      if (int rc = copy_out(src, dst, bytes, ev[0], "EP dispatch rows")) return rc;
-      so = 0;
-      for (int d = 0; d < world; ++d) {  // pair lists, laid out the same way
-        size_t before = 0;
-        for (int o = 0; o < rank; ++o) before += size_t(A(o, d, 2 + 2 * c));
-        src[size_t(d)] = reinterpret_cast<const char*>(pair_list + (t0 * k + so) * 2);
-        dst[size_t(d)] = static_cast<char*>(ctx->ep_peer_win[size_t(d)]) + lay[d].pairs[c] + before * 8;
-        bytes[size_t(d)] = size_t(sp(d, c)) * 8;
-        so += size_t(sp(d, c));
-      }
-      if (int rc = copy_out(src, dst, bytes, ev[0], "EP dispatch pairs")) return rc;
+      if (int rc = copy_out(per_dest, ev[0], "EP dispatch")) return rc;
     } else {
       for (int d = 0; d < world; ++d) sn[d] = int64_t(sr(d, c)) * H, rn[d] = int64_t(rr(d, c)) * H;
       if (int rc = ep_alltoallv(ctx, send_buf + t0 * kw * H, sn.data(), recv_rows(c), rn.data(), ncclHalf, 2, cs,
@@ -1403,19 +1484,18 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
     WMOE_CHECK_CUDA(ctx, cudaEventRecord(ev[2 + 3 * c], st), "EP ordering");
     WMOE_CHECK_CUDA(ctx, cudaStreamWaitEvent(cs, ev[2 + 3 * c], 0), "EP ordering");
     if (ipc) {
-      std::vector<const char*> src(static_cast<size_t>(world));
-      std::vector<char*> dst(static_cast<size_t>(world));
-      std::vector<size_t> bytes(static_cast<size_t>(world));
+      std::vector<std::vector<Copy>> per_dest(static_cast<size_t>(world));
       size_t yo = 0;
       for (int s_ = 0; s_ < world; ++s_) {  // results for source s into its return block, after lower ranks' blocks
         size_t before = 0;
         for (int o = 0; o < rank; ++o) before += size_t(A(s_, o, 2 + 2 * c));
-        src[size_t(s_)] = reinterpret_cast<const char*>(y + yo * H);
-        dst[size_t(s_)] = static_cast<char*>(ctx->ep_peer_win[size_t(s_)]) + lay[s_].ret[c] + before * H * 2;
-        bytes[size_t(s_)] = size_t(rp(s_, c)) * H * 2;
+        per_dest[size_t(s_)].push_back({reinterpret_cast<const char*>(y + yo * H),
+                                        static_cast<char*>(ctx->ep_peer_win[size_t(s_)]) + lay[s_].ret[c] +
+                                            before * H * 2,
+                                        size_t(rp(s_, c)) * H * 2});
         yo += size_t(rp(s_, c));
       }
-      if (int rc = copy_out(src, dst, bytes, ev[2 + 3 * c], "EP combine rows")) return rc;
+      if (int rc = copy_out(per_dest, ev[2 + 3 * c], "EP combine rows")) return rc;
     } else {
       for (int d = 0; d < world; ++d) sn[d] = int64_t(rp(d, c)) * H, rn[d] = int64_t(sp(d, c)) * H;
       if (int rc = ep_alltoallv(ctx, y, sn.data(), returned(c), rn.data(), ncclHalf, 2, cs, "EP combine rows"))

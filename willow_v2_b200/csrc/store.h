@@ -44,6 +44,10 @@ struct wmoe_ctx {
   std::vector<cudaEvent_t> ep_peer_events;
   int* ep_flag = nullptr;               // one int: the all-reduce that serves as the exchanges' barrier
   void* ep_handles = nullptr;           // [world][sizeof(cudaIpcMemHandle_t)] device staging of the handle all-gather
+  // pinned host copies of the all-gathered counts and handles: a device-to-host copy into pageable memory would
+  // block the host behind the communicator's kernels, outside the bounded waits
+  int32_t* ep_host_counts = nullptr;    // [kMaxRanks][kMaxRanks][kCountWords]
+  void* ep_host_handles = nullptr;      // [kMaxRanks][sizeof(cudaIpcMemHandle_t)]
   // per-phase CUDA events of the last profile_calls multi-token MoE calls (opt-in): [profile_calls][kProfMarks]
   static constexpr int kProfMarks = 7;
   std::vector<cudaEvent_t> prof_events;
