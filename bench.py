@@ -49,8 +49,8 @@ GATE_UP_Q4_BYTES = 2 * FFN * HIDDEN // 256 * 144                              # 
 EXPERT_BYTES = GATE_UP_Q4_BYTES + HIDDEN * FFN // 256 * 210                    # 2,039,808
 ROUTER_BYTES = EXPERTS * HIDDEN * 4 + HIDDEN * 4                           # router + shared gate, fp32
 # DRAM bytes (read + write) per layer of decode_kernel, measured by ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum) on a 4-layer launch: 82,234,880 + 1,487,360 bytes; traffic grows with the layers
-TRAFFIC_PER_LAYER = (82_234_880 + 1_487_360) / 4
+# dram__bytes_write.sum) on a 4-layer launch: 82,377,984 + 2,413,824 bytes; traffic grows with the layers
+TRAFFIC_PER_LAYER = (82_377_984 + 2_413_824) / 4
 # DRAM bytes (read + write) of one grouped_gemm_kernel<0> launch at 4096 tokens, measured by ncu
 # (dram__bytes_read.sum + dram__bytes_write.sum = 454,209,280 + 31,324,928): the gathered activations (151 MB) and the
 # Q4_K weights (303 MB) read once, h written
