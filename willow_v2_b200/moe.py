@@ -493,8 +493,10 @@ def ep_init(ctx: Context, group=None):
 
 def moe_forward_ep_native(store: ExpertStore, layer: int, x: torch.Tensor, lw: LayerWeights, top_k: int = 8,
                           out_dtype: Optional[torch.dtype] = None, return_routing: bool = False):
-    """moe_forward_ep in one library call (wmoe_moe_forward_ep) over the communicator of ep_init: the exchanges are
-    grouped ncclSend/ncclRecv issued from C++ on the current stream."""
+    """moe_forward_ep in one library call (wmoe_moe_forward_ep) over the communicator of ep_init: one all-gather of
+    the transfer counts, then the rows, pair lists and result rows copied by the copy engines into the peers'
+    exchange windows (CUDA IPC), each exchange closed by a one-int all-reduce. Raises WmoeError (WMOE_ERR_NCCL) when a
+    rank has left or NCCL failed; every later call of the context does so until ep_finalize and a new ep_init."""
     ctx = store.ctx
     x = x.contiguous()
     T = x.shape[0]
