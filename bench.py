@@ -659,8 +659,9 @@ def run_prefill32k(args, rank: int, world: int, dist):
     per-layer permutation), experts partitioned 256/N per GPU, each GPU's expert store capped at 4 GiB: the experts
     over the cap live in pinned host memory and stream in on the store's side stream. While layer l runs, layer
     l + 1's experts are prefetched (a prefill batch reads most of them); after the first warm-up pass, 75% of the
-    slots keep the hot set chosen by token counts (store.py:464-484). Residual + RMSNorm between layers
-    (wmoe_add_rmsnorm). Strong scaling: the 32768 tokens are split over the ranks."""
+    slots keep the hot set chosen by token counts (store.py:464-484). The whole stack is one wmoe_prefill_stack
+    call: residual + RMSNorm in each layer's combine kernel, the next layer's prefetch issued by the library. Strong
+    scaling: the 32768 tokens are split over the ranks."""
     import torch
     from willow_v2_b200 import lib as L
     from willow_v2_b200 import moe, synth
@@ -682,20 +683,12 @@ def run_prefill32k(args, rank: int, world: int, dist):
     h0s = [torch.from_numpy(synth.hidden(SEED, PF32_T, step=99 + b)[rank * T:(rank + 1) * T]).cuda() for b in range(2)]
     h = torch.empty_like(h0s[0])
     stream = torch.cuda.current_stream()
-    if world > 1:
+    if world > 1:  # every layer of the stack then runs over the library's communicator
         moe.ep_init(ctx)
         L.lib.wmoe_ep_set_chunks(ctx.handle, max(1, world // 2))
-        fwd = moe.moe_forward_ep_native
-    else:
-        fwd = moe.moe_forward
 
-    def stack(h):
-        out = None
-        for l in range(n_layers):
-            h, hn = moe.add_rmsnorm(h, out, out_dtype=torch.bfloat16)
-            out = fwd(store, l, hn, lws[l], out_dtype=torch.bfloat16)
-            store.prefetch((l + 1) % n_layers)  # copies overlap layer l's experts
-        return moe.add_rmsnorm(h, out, out_dtype=torch.bfloat16)[0]
+    def stack(h):  # h <- h + moe(rms_norm(h)) for every layer, in place; bf16 block inputs
+        return moe.prefill_stack(store, lws, h, x_dtype=torch.bfloat16, out=h)
 
     K, W = args.steps, args.warmup
     for s in range(W):

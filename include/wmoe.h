@@ -17,6 +17,8 @@
  *                            batched_decode_experts 492-532, combine_decode_experts 431-443)
  *   wmoe_decode_stack        engines/qwen36/model.py:17-22 MoEEngine.forward's per-layer
  *                            x + moe(rms_norm(x)) for one decode token, all layers in one launch
+ *   wmoe_prefill_stack       the same layer loop for a prompt of T tokens, residual + RMSNorm in each
+ *                            layer's combine
  *   wmoe_store_*             gguf/store.py:41-536 ExpertStore (slabs, LRU, load_batches, prefetch,
  *                            record_usage) and gguf/mps_shared.mm:10-20 shared_empty (host staging)
  *   wmoe_ggml_row_bytes      gguf/metal.py:323-325 row_bytes
@@ -146,9 +148,9 @@ int wmoe_store_fill_synthetic(wmoe_store* store, uint64_t seed, int layer_begin,
 size_t wmoe_store_blob_bytes(const wmoe_store* store);
 /* Sets a layer's down-matrix type (routed experts and the shared expert): 14 Q6_K (the default) or 12 Q4_K, as
  * llama.cpp's Q4_K_M files store some layers (gguf/compiler.py:42-44 records the type per layer). Set it before
- * uploading the layer: a Q4_K layer's blob is gate_up then H rows of 288 bytes (wmoe_store_layer_blob_bytes). The
- * grouped GEMMs and dequant-GEMV kernels run both; the persistent decode kernel runs Q6_K layers only (single-token
- * calls on a Q4_K layer take the GEMV kernels, wmoe_decode_stack refuses such a layer). */
+ * uploading the layer: a Q4_K layer's blob is gate_up then H rows of 288 bytes (wmoe_store_layer_blob_bytes).  Every
+ * kernel runs both: the grouped GEMMs, the dequant-GEMV kernels and the persistent decode kernel (stacks may mix
+ * the two types layer by layer). */
 int wmoe_store_set_down_type(wmoe_store* store, int layer, int ggml_type);
 size_t wmoe_store_layer_blob_bytes(const wmoe_store* store, int layer);
 /* Makes the given experts of a layer resident (copies misses from the host copy on the store's side stream;
@@ -329,6 +331,23 @@ int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_l
 int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
                               const wmoe_layer_weights* layers, float eps, const float* h_in, float* h_out,
                               int32_t* topk_idx_out, void* stream);
+
+/* T tokens through layers [layer_begin, layer_begin + n_layers) of the store: h <- h + moe_l(rms_norm(h)) per layer
+ * (eps, unit weight), MoEEngine.forward's layer loop (engines/qwen36/model.py:17-22) for a prompt. One residual +
+ * RMSNorm launch before the first layer; after it every layer's combine kernel adds the block output to h and
+ * writes the next layer's normalised input (no separate residual + RMSNorm pass between layers). Each block takes
+ * its input in x_dtype (WMOE_BF16: tensor-core router when layers[i].router_split is set, and the grouped GEMMs; or
+ * WMOE_F32) and computes as wmoe_moe_forward_layer does, min_expert_weight included. h_in / h_out: f32 [T, hidden]
+ * on the device, 16-byte aligned, may alias. layers: HOST array of n_layers entries of device pointers.
+ *   - After wmoe_ep_init every layer runs as wmoe_moe_forward_ep does, over the context's communicator: the store
+ *     holds this rank's block of the experts (wmoe_store_create_range) and every rank calls with its own tokens.
+ *   - A capped store starts copying the next layer's experts (wmoe_store_prefetch with its guess) once a layer is
+ *     issued, and the first layer's after the last.
+ *   - One f32 token on a resident store runs wmoe_decode_stack.
+ * The context keeps the T x hidden rows passed between layers (grown on first use). */
+int wmoe_prefill_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
+                       const wmoe_layer_weights* layers, float eps, const float* h_in, int T, int x_dtype,
+                       float* h_out, void* stream);
 
 /* Residual add + RMS normalisation between MoE layers (engines/qwen36/model.py:17-22, engines/base.py:27-32,
  * weight 1): x_out = x + y (y optional, f32 or bf16), xn_out = x_out / sqrt(mean(x_out^2) + eps) as f32 or bf16.

@@ -128,6 +128,92 @@ def test_ep_native_one_rank_matches_single_gpu(zipf):
     assert np.array_equal(out, ref)
 
 
+STACK_LAYERS, STACK_TOKENS = 3, 512
+
+
+def _stack_weights(moe, torch, ctx):
+    return [moe.LayerWeights(
+        router_w=torch.from_numpy(synth.router_weight(SEED, l)).cuda(),
+        shared_gate=torch.from_numpy(synth.shared_gate_weight(SEED, l)).cuda(),
+        shared_gate_up=torch.from_numpy(synth.expert_gate_up(SEED, l, 256).reshape(-1)).cuda(),
+        shared_down=torch.from_numpy(synth.expert_down(SEED, l, 256).reshape(-1)).cuda(),
+        router_bias=torch.from_numpy(synth.zipf_bias(SEED + l)).cuda()).prepare(ctx) for l in range(STACK_LAYERS)]
+
+
+def _stack_rank(rank, world, port, outdir):
+    """wmoe_prefill_stack after wmoe_ep_init: every layer over the library's communicator, the residual epilogue in
+    each chunk's combine."""
+    import torch
+    import torch.distributed as dist
+    from willow_v2_b200 import moe
+    from willow_v2_b200.lib import lib
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        ctx = moe.Context(rank)
+        per = 256 // world
+        store = moe.ExpertStore(STACK_LAYERS, ctx=ctx, expert_range=(rank * per, (rank + 1) * per))
+        store.fill_synthetic(SEED)
+        lws = _stack_weights(moe, torch, ctx)
+        h = torch.from_numpy(synth.hidden(SEED, STACK_TOKENS * world, step=77)[rank * STACK_TOKENS:
+                                                                                (rank + 1) * STACK_TOKENS]).cuda()
+        moe.ep_init(ctx)
+        outs = []
+        for chunks in (1, 2):  # the result does not depend on the chunking
+            lib.wmoe_ep_set_chunks(ctx.handle, chunks)
+            outs.append(moe.prefill_stack(store, lws, h))
+        torch.cuda.synchronize()
+        ctx.check_device()
+        ctx.ep_finalize()
+        assert torch.equal(outs[0], outs[1])
+        np.save(os.path.join(outdir, f"stack{rank}.npy"), outs[0].cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _stack_reference(world):
+    import torch
+    from willow_v2_b200 import moe
+    torch.cuda.set_device(0)
+    ctx = moe.Context(0)
+    full = moe.ExpertStore(STACK_LAYERS, ctx=ctx)
+    full.fill_synthetic(SEED)
+    h = torch.from_numpy(synth.hidden(SEED, STACK_TOKENS * world, step=77)).cuda()
+    out = moe.prefill_stack(full, _stack_weights(moe, torch, ctx), h).cpu().numpy()
+    full.close()
+    return out
+
+
+def test_ep_prefill_stack_one_rank_matches_single_gpu():
+    """The stack over a one-rank communicator (one GPU) gives the single-GPU stack bit for bit."""
+    import torch.multiprocessing as mp
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_stack_rank, args=(1, _free_port(), d), nprocs=1, start_method="spawn")
+        out = np.load(os.path.join(d, "stack0.npy"))
+    assert np.array_equal(out, _stack_reference(1))
+
+
+def test_ep_prefill_stack_matches_single_gpu():
+    """Three layers of Zipf-routed tokens through wmoe_prefill_stack on 2, 4 or 8 ranks: every rank's rows equal the
+    single-GPU stack's bit for bit."""
+    import torch
+    import torch.multiprocessing as mp
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = 8 if n >= 8 else (4 if n >= 4 else 2)
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_stack_rank, args=(world, _free_port(), d), nprocs=world, start_method="spawn")
+        outs = [np.load(os.path.join(d, f"stack{r}.npy")) for r in range(world)]
+    ref = _stack_reference(world)
+    for r in range(world):
+        assert np.array_equal(outs[r], ref[r * STACK_TOKENS:(r + 1) * STACK_TOKENS]), r
+
+
 def _mismatch_rank(rank, world, port, outdir):
     import torch
     import torch.distributed as dist

@@ -110,6 +110,7 @@ void wmoe_destroy(wmoe_ctx* ctx) {
   free_profiling(ctx);
   ep_release(ctx);
   cudaFree(ctx->scratch);
+  cudaFree(ctx->stack_xn);
   cudaFree(ctx->d_status);
   delete ctx;
 }
@@ -478,7 +479,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
                             int top_k, const float* router_w, const float* router_bias, const float* shared_gate,
                             const uint8_t* shared_gate_up, const uint8_t* shared_down, const float* router_packed,
                             const void* router_split, void* out, int out_dtype, int32_t* topk_idx_out,
-                            float* topk_w_out, void* stream) {
+                            float* topk_w_out, void* stream, const AddNorm* an = nullptr) {
   if (!ctx) return WMOE_ERR_INVALID;
   if (!store) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: null store");
   if (store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: store belongs to another context");
@@ -490,10 +491,11 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   if (H != 2048 || F != 512 || top_k != 8 || E > 512)
     return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_moe_forward: this build runs hidden 2048, ffn 512, top-8");
   if (T == 0) return WMOE_OK;
-  if (!x || !router_w || !shared_gate || !shared_gate_up || !shared_down || !out)
+  if (!x || !router_w || !shared_gate || !shared_gate_up || !shared_down || (!out && !an))
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward: null pointer");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (T == 1 && !store->capped && ctx->use_decode_kernel && ctx->decode_ctas > 0 && E == 256 &&
+  const AddNorm epi = an ? *an : AddNorm{};
+  if (T == 1 && !an && !store->capped && ctx->use_decode_kernel && ctx->decode_ctas > 0 && E == 256 &&
       aligned16(router_packed) && aligned16(x)) {
     // one token, every expert resident: the persistent decode kernel (one launch, no host synchronisation)
     if (int rc = ensure_scratch(ctx, decode_scratch_bytes(H, F, E, ctx->decode_ctas))) return rc;
@@ -594,7 +596,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
   if (gemm_path) {
     WMOE_CHECK_CUDA(ctx,
                     prefill_experts(src, layer, pm, topk_idx, H, F, x, x_dtype, topk_w, shared_s, out, out_dtype,
-                                    at<void>(ctx, o_region), ctx->sm_count, ctx->d_status, marks ? marks + 3 : nullptr,
+                                    epi, at<void>(ctx, o_region), ctx->sm_count, ctx->d_status, marks ? marks + 3 : nullptr,
                                     st, &n),
                     "grouped GEMM");
   } else {
@@ -613,7 +615,7 @@ static int moe_forward_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const v
     float* y = at<float>(ctx, o_y);
     WMOE_CHECK_CUDA(ctx, down_gemv(src, layer, pm, H, F, hq, hs, hsum, y, ctx->d_status, st, &n), "down");
     mark(5);
-    WMOE_CHECK_CUDA(ctx, combine(pm, H, topk_w, shared_s, y, nullptr, out, out_dtype, st, &n), "combine");
+    WMOE_CHECK_CUDA(ctx, combine(pm, H, topk_w, shared_s, y, out, out_dtype, epi, st, &n), "combine");
     mark(6);
   }
   if (marks) ++ctx->profile_seq;
@@ -832,7 +834,7 @@ int wmoe_ep_combine(wmoe_ctx* ctx, int T, int top_k, int hidden, const int32_t* 
   WMOE_CHECK_CUDA(ctx,
                   combine_rows(T, top_k, hidden, topk_idx, topk_w, ret_index, shared_s,
                                reinterpret_cast<const __half*>(y_returned), reinterpret_cast<const __half*>(y_shared),
-                               out, out_dtype, static_cast<cudaStream_t>(stream), &n),
+                               out, out_dtype, AddNorm{}, static_cast<cudaStream_t>(stream), &n),
                   "wmoe_ep_combine");
   ctx->launches += uint64_t(n);
   return WMOE_OK;
@@ -1239,9 +1241,9 @@ int wmoe_ep_set_chunks(wmoe_ctx* ctx, int chunks) {
 // The layer in C chunks of the rank's tokens so that the exchanges of some chunks overlap the expert stage of
 // others: the exchanges run on the context's communication stream, the rest on the caller's stream, ordered by
 // events. Chunks are planned first and their counts exchanged together (one host read of the transfer sizes).
-int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
-                        const wmoe_layer_weights* w, void* out, int out_dtype, int32_t* topk_idx_out,
-                        float* topk_w_out, void* stream) {
+static int moe_forward_ep_impl(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T,
+                               int top_k, const wmoe_layer_weights* w, void* out, int out_dtype,
+                               int32_t* topk_idx_out, float* topk_w_out, void* stream, const AddNorm* an) {
   if (!ctx) return WMOE_ERR_INVALID;
   if (ctx->ep_dead)
     return ctx_fail(ctx, WMOE_ERR_NCCL, "wmoe_moe_forward_ep: the communicator was aborted after a failure; "
@@ -1255,7 +1257,7 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
       (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16) || (out_dtype != WMOE_F32 && out_dtype != WMOE_BF16))
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: bad layer, shape or dtype");
   if (int rc = check_layer(ctx, w, "wmoe_moe_forward_ep")) return rc;
-  if (T > 0 && (!x || !out)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: null pointer");
+  if (T > 0 && (!x || (!out && !an))) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_moe_forward_ep: null pointer");
   const cudaStream_t st = static_cast<cudaStream_t>(stream), cs = ctx->ep_stream;
   const int k = top_k, kw = std::min(k, world);
   // the chunk count is the context's setting only (never derived from local data): every rank must run the same
@@ -1510,11 +1512,17 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
     if (Tc[c] == 0) continue;
     const size_t t0 = size_t(T0[c]);
     const uint16_t* y = reinterpret_cast<const uint16_t*>(eb + o_y[c]);
+    AddNorm epi;  // the chunk's rows of the residual epilogue
+    if (an) {
+      epi = *an;
+      epi.h += t0 * H;
+      if (epi.xn) epi.xn = static_cast<char*>(epi.xn) + t0 * H * (epi.xn_dtype == WMOE_F32 ? 4 : 2);
+    }
     WMOE_CHECK_CUDA(ctx,
                     combine_rows(Tc[c], k, H, topk_idx + t0 * k, topk_w + t0 * k, ret_index + t0 * k, shared_s + t0,
                                  reinterpret_cast<const __half*>(returned(c)),
                                  reinterpret_cast<const __half*>(y) + size_t(Pc[c]) * H,
-                                 static_cast<char*>(out) + t0 * H * osz, out_dtype, st, &n),
+                                 an ? nullptr : static_cast<char*>(out) + t0 * H * osz, out_dtype, epi, st, &n),
                     "EP combine");
   }
   if (T > 0) {
@@ -1530,6 +1538,13 @@ int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void*
   if (marks) ++ctx->profile_seq;
   ctx->launches += uint64_t(n);
   return WMOE_OK;
+}
+
+int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
+                        const wmoe_layer_weights* w, void* out, int out_dtype, int32_t* topk_idx_out,
+                        float* topk_w_out, void* stream) {
+  return moe_forward_ep_impl(ctx, store, layer, x, x_dtype, T, top_k, w, out, out_dtype, topk_idx_out, topk_w_out,
+                             stream, nullptr);
 }
 
 int wmoe_decode_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
@@ -1611,6 +1626,70 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
                                           static_cast<cudaStream_t>(stream), &n, ctx->min_expert_weight);
   ctx->launches += uint64_t(n);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_decode_stack_noalloc");
+  return WMOE_OK;
+}
+
+// The multi-token counterpart of wmoe_decode_stack. One residual + RMSNorm launch before the first layer; after
+// that each layer's combine kernel adds its output to h and writes the next layer's input (the residual epilogue),
+// so a layer is the router, dispatch and the expert kernels only.
+int wmoe_prefill_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_layers,
+                       const wmoe_layer_weights* layers, float eps, const float* h_in, int T, int x_dtype,
+                       float* h_out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (!store || store->ctx != ctx) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: bad store");
+  if (layer_begin < 0 || n_layers <= 0 || layer_begin + n_layers > store->layers || !layers || T < 0 ||
+      !(eps >= 0.f) || (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: bad arguments");
+  if (T == 0) return WMOE_OK;
+  if (!h_in || !h_out) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: null pointer");
+  if (!aligned16(h_in) || !aligned16(h_out))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: h_in and h_out must be 16-byte aligned");
+  for (int i = 0; i < n_layers; ++i)
+    if (int rc = check_layer(ctx, &layers[i], "wmoe_prefill_stack")) return rc;
+  // after wmoe_ep_init every layer runs over the context's expert-parallel communicator
+  const bool ep = ctx->nccl_comm != nullptr;
+  if (!ep && T == 1 && x_dtype == WMOE_F32 && !store->capped && ctx->use_decode_kernel &&
+      ctx->decode_ctas > 0 && store->experts == 256) {
+    bool packed = true;
+    for (int i = 0; i < n_layers; ++i) packed = packed && aligned16(layers[i].router_packed);
+    if (packed) return wmoe_decode_stack(ctx, store, layer_begin, n_layers, layers, eps, h_in, h_out, nullptr, stream);
+  }
+  const int H = store->hidden;
+  const size_t need = size_t(T) * H * (x_dtype == WMOE_F32 ? 4 : 2);
+  if (need > ctx->stack_xn_bytes) {
+    if (ctx->stack_xn) {
+      WMOE_CHECK_CUDA(ctx, cudaDeviceSynchronize(), "wmoe_prefill_stack: buffer resize");
+      cudaFree(ctx->stack_xn);
+      ctx->stack_xn = nullptr;
+      ctx->stack_xn_bytes = 0;
+    }
+    WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->stack_xn, need), "wmoe_prefill_stack: buffer allocation");
+    ctx->stack_xn_bytes = need;
+  }
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* xn = ctx->stack_xn;
+  int n = 0;
+  WMOE_CHECK_CUDA(ctx, add_rmsnorm(h_in, nullptr, WMOE_F32, T, H, eps, h_out, xn, x_dtype, st, &n),
+                  "wmoe_prefill_stack: first norm");
+  ctx->launches += uint64_t(n);
+  for (int i = 0; i < n_layers; ++i) {
+    const int l = layer_begin + i;
+    const wmoe_layer_weights& w = layers[i];
+    AddNorm an;
+    an.h = h_out;
+    an.xn = i + 1 < n_layers ? xn : nullptr;
+    an.xn_dtype = x_dtype;
+    an.eps = eps;
+    const int rc = ep ? moe_forward_ep_impl(ctx, store, l, xn, x_dtype, T, 8, &w, nullptr, x_dtype, nullptr, nullptr,
+                                            stream, &an)
+                      : moe_forward_impl(ctx, store, l, xn, x_dtype, T, 8, w.router_w, w.router_bias, w.shared_gate,
+                                         w.shared_gate_up, w.shared_down, w.router_packed, w.router_split, nullptr,
+                                         x_dtype, nullptr, nullptr, stream, &an);
+    if (rc) return rc;
+    // a capped store copies the next layer's experts while this one computes (gguf/store.py:204-219)
+    if (store->capped)
+      if (int rc2 = wmoe_store_prefetch(store, i + 1 < n_layers ? l + 1 : layer_begin, nullptr, 0, stream)) return rc2;
+  }
   return WMOE_OK;
 }
 

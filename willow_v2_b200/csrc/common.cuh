@@ -47,6 +47,42 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Sum of v over the CTA in a fixed order (a tree per warp, then warp 0 over the warp sums), returned to every
+// thread. Every thread of the CTA must call it; red is __shared__ float[32], free again on return.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x % 32, wid = threadIdx.x / 32;
+  v = warp_sum(v);
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    float t = lane < int((blockDim.x + 31) / 32) ? red[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// Eight consecutive floats to a float32 (f32) or bfloat16 row at element offset i (16-byte aligned), bf16 rounded
+// to nearest even
+__device__ __forceinline__ void store8(void* dst, bool f32, size_t i, const float* v) {
+  if (f32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(dst) + i);
+    o[0] = make_float4(v[0], v[1], v[2], v[3]);
+    o[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint32_t b[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      b[j] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dst) + i) = make_uint4(b[0], b[1], b[2], b[3]);
+  }
+}
+
 // d = c + a.lo16 * b.byte0 + a.hi16 * b.byte1  (signed 16-bit x unsigned 8-bit)
 __device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) {
   int d;

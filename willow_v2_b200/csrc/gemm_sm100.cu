@@ -518,7 +518,9 @@ __global__ void __launch_bounds__(256) gather_fp16_kernel(PairMap pm, const XT* 
 // Combine from the fp16 down outputs (stored / kYScale): out[t] = sum over the token's picks in ascending expert id
 // of w * kYScale * y_routed[rows[t][j]] (engines/base.py:580-586), + s_t * kYScale * y_shared[t] (base.py:481-489).
 // One CTA per token, 8 consecutive outputs per thread from 16-byte loads of each row. The token rows (x) are
-// converted to fp16 unscaled: callers pass normalised hidden states (|x| far below 65504).
+// converted to fp16 unscaled: callers pass normalised hidden states (|x| far below 65504). With the residual
+// epilogue (an.h set) the CTA adds its row to h[t] and, when an.xn is set, writes the next layer's normalised input
+// from the updated row it holds: the separate residual + RMSNorm pass over the activations goes away.
 template <int K>
 __global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t* __restrict__ topk_idx,
                                                            const float* __restrict__ topk_w,
@@ -526,7 +528,8 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t*
                                                            const float* __restrict__ shared_s,
                                                            const __half* __restrict__ y_routed,
                                                            const __half* __restrict__ y_shared,
-                                                           void* __restrict__ out, int out_dtype) {
+                                                           void* __restrict__ out, int out_dtype, AddNorm an) {
+  __shared__ float red[32];
   const int t = blockIdx.x;
   int ex[K], ps[K];
   float ws[K];
@@ -552,6 +555,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t*
         ws[j - 1] = tw;
       }
   const float s = shared_s[t] * kYScale;
+  float ss = 0.f;  // squares of the updated residual row (epilogue)
   for (int r = threadIdx.x * 8; r < H; r += blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -567,18 +571,27 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t*
         acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(f.y, wi));
       }
     }
-    if (out_dtype == kF32) {
-      float* o = static_cast<float*>(out) + size_t(t) * H + r;
-      *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      *reinterpret_cast<float4*>(o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    } else {
-      uint32_t b[4];
+    if (an.h) {  // h[t] += out[t] (x + moe(...), engines/qwen36/model.py:22)
+      float4* hp = reinterpret_cast<float4*>(an.h + size_t(t) * H + r);
+      const float4 a = hp[0], b = hp[1];
+      const float v[8] = {__fadd_rn(a.x, acc[0]), __fadd_rn(a.y, acc[1]), __fadd_rn(a.z, acc[2]),
+                          __fadd_rn(a.w, acc[3]), __fadd_rn(b.x, acc[4]), __fadd_rn(b.y, acc[5]),
+                          __fadd_rn(b.z, acc[6]), __fadd_rn(b.w, acc[7])};
+      hp[0] = make_float4(v[0], v[1], v[2], v[3]);
+      hp[1] = make_float4(v[4], v[5], v[6], v[7]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const __nv_bfloat162 v = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-        b[j] = *reinterpret_cast<const uint32_t*>(&v);
-      }
-      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + size_t(t) * H + r) = make_uint4(b[0], b[1], b[2], b[3]);
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+      continue;
+    }
+    store8(out, out_dtype == kF32, size_t(t) * H + r, acc);
+  }
+  if (an.h && an.xn) {  // uniform over the CTA: xn[t] = h[t] / sqrt(mean(h[t]^2) + eps) (engines/base.py:27-32)
+    const float rs = rsqrtf(block_sum(ss, red) / float(H) + an.eps);
+    for (int r = threadIdx.x * 8; r < H; r += blockDim.x * 8) {
+      const float4* hp = reinterpret_cast<const float4*>(an.h + size_t(t) * H + r);
+      const float4 a = hp[0], b = hp[1];
+      const float v[8] = {a.x * rs, a.y * rs, a.z * rs, a.w * rs, b.x * rs, b.y * rs, b.z * rs, b.w * rs};
+      store8(an.xn, an.xn_dtype == kF32, size_t(t) * H + r, v);
     }
   }
 }
@@ -700,11 +713,14 @@ cudaError_t prefill_gemms(const ExpertSource& src, int layer, const PairMap& pm,
 
 cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const float* topk_w, const int32_t* rows,
                          const float* shared_s, const __half* y_routed, const __half* y_shared, void* out,
-                         int out_dtype, cudaStream_t st, int* launches) {
-  if (k != 8 || H % 8 || reinterpret_cast<uintptr_t>(out) % 16) return cudaErrorInvalidValue;
+                         int out_dtype, const AddNorm& an, cudaStream_t st, int* launches) {
+  if (k != 8 || H % 8) return cudaErrorInvalidValue;
+  if (an.h ? (reinterpret_cast<uintptr_t>(an.h) % 16 || reinterpret_cast<uintptr_t>(an.xn) % 16)
+           : reinterpret_cast<uintptr_t>(out) % 16)
+    return cudaErrorInvalidValue;
   if (T > 0) {
     combine_rows_kernel<8><<<unsigned(T), 256, 0, st>>>(H, topk_idx, topk_w, rows, shared_s, y_routed, y_shared, out,
-                                                        out_dtype);
+                                                        out_dtype, an);
     ++*launches;
   }
   return cudaGetLastError();
@@ -712,11 +728,11 @@ cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const flo
 
 cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, const int32_t* topk_idx, int H,
                             int F, const void* x, int x_dtype, const float* topk_w, const float* shared_s, void* out,
-                            int out_dtype, void* scratch, int num_sms, int* status, const cudaEvent_t* marks,
-                            cudaStream_t st, int* launches) {
+                            int out_dtype, const AddNorm& an, void* scratch, int num_sms, int* status,
+                            const cudaEvent_t* marks, cudaStream_t st, int* launches) {
   if (pm.k != 8) return cudaErrorInvalidValue;
-  // activations are read and written 16 bytes at a time
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16) return cudaErrorInvalidValue;
+  // activations are read and written 16 bytes at a time (out, or the epilogue's rows, checked by combine_rows)
+  if (reinterpret_cast<uintptr_t>(x) % 16) return cudaErrorInvalidValue;
   const size_t P = size_t(pm.T) * (pm.k + 1);
   char* b = static_cast<char*>(scratch);
   __half* xg = reinterpret_cast<__half*>(b);
@@ -733,7 +749,7 @@ cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& p
                                 marks ? marks + 1 : nullptr, st, launches);
   if (e != cudaSuccess) return e;
   e = combine_rows(pm.T, pm.k, H, topk_idx, topk_w, pm.pos, shared_s, ybuf, ybuf + size_t(pm.T) * pm.k * H, out,
-                   out_dtype, st, launches);
+                   out_dtype, an, st, launches);
   if (marks) cudaEventRecord(marks[3], st);
   return e;
 }

@@ -351,13 +351,14 @@ cudaError_t down_gemv(const ExpertSource& src, int layer, const PairMap& pm, int
 // ---------------------------------------------------------------- combine
 
 // out[t] = sum over t's k picks in ascending expert id of w * y[pick] (engines/base.py:580-586: index_add_ in
-// expert order), then + s_t * shared(x_t) (base.py:481-489), then + residual when given.
+// expert order), then + s_t * shared(x_t) (base.py:481-489). With the residual epilogue (an.h set; the grid is then
+// one CTA per token) h[t] += out[t] and, when an.xn is set, xn[t] = rms_norm(h[t]) (engines/qwen36/model.py:17-22).
 template <int K>
 __global__ void __launch_bounds__(256) combine_kernel(PairMap pm, int H, const float* __restrict__ topk_w,
                                                       const float* __restrict__ shared_s,
-                                                      const float* __restrict__ y,
-                                                      const float* __restrict__ residual, void* __restrict__ out,
-                                                      int out_dtype) {
+                                                      const float* __restrict__ y, void* __restrict__ out,
+                                                      int out_dtype, AddNorm an) {
+  __shared__ float red[32];
   const int t = blockIdx.y;
   int ps[K];
   float ws[K];
@@ -380,24 +381,52 @@ __global__ void __launch_bounds__(256) combine_kernel(PairMap pm, int H, const f
       }
   const float s = shared_s[t];
   const size_t shared_row = size_t(pm.T) * K + t;
-  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {
+  auto value = [&](int r) {
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(y[size_t(ps[i]) * H + r], ws[i]));
-    acc = __fadd_rn(acc, __fmul_rn(s, y[shared_row * H + r]));
-    if (residual) acc = __fadd_rn(residual[size_t(t) * H + r], acc);
-    if (out_dtype == kF32)
-      static_cast<float*>(out)[size_t(t) * H + r] = acc;
-    else
-      static_cast<__nv_bfloat16*>(out)[size_t(t) * H + r] = __float2bfloat16_rn(acc);
+    return __fadd_rn(acc, __fmul_rn(s, y[shared_row * H + r]));
+  };
+  if (!an.h) {
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < H; r += gridDim.x * blockDim.x) {
+      const float acc = value(r);
+      if (out_dtype == kF32)
+        static_cast<float*>(out)[size_t(t) * H + r] = acc;
+      else
+        static_cast<__nv_bfloat16*>(out)[size_t(t) * H + r] = __float2bfloat16_rn(acc);
+    }
+    return;
+  }
+  // the residual epilogue: the CTA holds the whole row, 8 consecutive values per thread (the partition and
+  // summation order of add_rmsnorm_kernel)
+  float ss = 0.f;
+  float* hrow = an.h + size_t(t) * H;
+  for (int r = threadIdx.x * 8; r < H; r += blockDim.x * 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = __fadd_rn(hrow[r + j], value(r + j));
+      hrow[r + j] = v;
+      ss = fmaf(v, v, ss);
+    }
+  }
+  if (an.xn) {  // uniform over the CTA
+    const float rs = rsqrtf(block_sum(ss, red) / float(H) + an.eps);
+    for (int r = threadIdx.x * 8; r < H; r += blockDim.x * 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = hrow[r + j] * rs;
+      store8(an.xn, an.xn_dtype == kF32, size_t(t) * H + r, v);
+    }
   }
 }
 
-cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* shared_s, const float* y,
-                    const float* residual, void* out, int out_dtype, cudaStream_t st, int* launches) {
+cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* shared_s, const float* y, void* out,
+                    int out_dtype, const AddNorm& an, cudaStream_t st, int* launches) {
   if (pm.k != 8) return cudaErrorInvalidValue;
-  const dim3 grid(unsigned((H + 255) / 256), unsigned(pm.T));
-  combine_kernel<8><<<grid, 256, 0, st>>>(pm, H, topk_w, shared_s, y, residual, out, out_dtype);
+  if (an.h && (H % 8 || reinterpret_cast<uintptr_t>(an.xn) % 16)) return cudaErrorInvalidValue;
+  // the epilogue's norm needs the whole row in one CTA
+  const dim3 grid(an.h ? 1u : unsigned((H + 255) / 256), unsigned(pm.T));
+  combine_kernel<8><<<grid, 256, 0, st>>>(pm, H, topk_w, shared_s, y, out, out_dtype, an);
   ++*launches;
   return cudaGetLastError();
 }

@@ -104,6 +104,18 @@ cudaError_t dispatch_rows(const int32_t* topk_idx, int T, int k, int E, int shar
                           int32_t* seg, int32_t* n_used, int64_t* usage, int* status, cudaStream_t st,
                           int* launches);
 
+// The residual epilogue of a combine: between layers willow computes x + moe(rms_norm(x))
+// (engines/qwen36/model.py:17-22, engines/base.py:27-32 with weight 1). With h set the combine adds its output to the
+// residual row (h[t] += out[t], float32) instead of writing out, and when xn is set also writes the next layer's
+// input xn[t] = h[t] / sqrt(mean(h[t]^2) + eps) in xn_dtype. xn may be the call's own input x: every kernel that
+// reads x runs before the combine on the same stream.
+struct AddNorm {
+  float* h = nullptr;
+  void* xn = nullptr;
+  int xn_dtype = 0;
+  float eps = 0.f;
+};
+
 // gemv.cu (small token counts per expert)
 cudaError_t quant_rows(const void* x, int x_dtype, int rows, int K, int16_t* q, float* scale, int32_t* sum16,
                        cudaStream_t st, int* launches);
@@ -113,8 +125,8 @@ cudaError_t gate_up_gemv(const ExpertSource& src, int layer, const PairMap& pm, 
 cudaError_t down_gemv(const ExpertSource& src, int layer, const PairMap& pm, int H, int F, const int16_t* hq,
                       const float* hs, const int32_t* hsum16, float* y, int* status, cudaStream_t st,
                       int* launches);
-cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* shared_s, const float* y,
-                    const float* residual, void* out, int out_dtype, cudaStream_t st, int* launches);
+cudaError_t combine(const PairMap& pm, int H, const float* topk_w, const float* shared_s, const float* y, void* out,
+                    int out_dtype, const AddNorm& an, cudaStream_t st, int* launches);
 
 // gemm_sm100.cu: tcgen05 grouped GEMMs for many tokens per expert (gate_up + SwiGLU, down) and the fp16 combine
 size_t prefill_scratch_bytes(int T, int k, int E, int H, int F);
@@ -123,17 +135,18 @@ size_t prefill_gemm_scratch_bytes(size_t P, int E, int H, int F);
 // down, combine (or null).
 cudaError_t prefill_experts(const ExpertSource& src, int layer, const PairMap& pm, const int32_t* topk_idx, int H,
                             int F, const void* x, int x_dtype, const float* topk_w, const float* shared_s, void* out,
-                            int out_dtype, void* scratch, int num_sms, int* status, const cudaEvent_t* marks,
-                            cudaStream_t st, int* launches);
+                            int out_dtype, const AddNorm& an, void* scratch, int num_sms, int* status,
+                            const cudaEvent_t* marks, cudaStream_t st, int* launches);
 // The two GEMMs over P gathered fp16 rows xg (run-of-8 order): y [P][H] fp16 (= down output / 32); routed pair
 // positions p < n_routed are written at row out_rows[p] when out_rows is given. marks: 2 events (or null).
 cudaError_t prefill_gemms(const ExpertSource& src, int layer, const PairMap& pm, size_t P, int H, int F,
                           const __half* xg, __half* y, const int32_t* out_rows, int n_routed, void* scratch,
                           int num_sms, int* status, const cudaEvent_t* marks, cudaStream_t st, int* launches);
 // out[t] = sum over picks in ascending expert id of w * 32 * y_routed[rows[t][j]] + s_t * 32 * y_shared[t]
+// (or the residual epilogue an, when an.h is set)
 cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const float* topk_w, const int32_t* rows,
                          const float* shared_s, const __half* y_routed, const __half* y_shared, void* out,
-                         int out_dtype, cudaStream_t st, int* launches);
+                         int out_dtype, const AddNorm& an, cudaStream_t st, int* launches);
 
 // ep.cu: expert parallelism over up to kMaxRanks ranks (contiguous expert blocks)
 constexpr int kMaxRanks = 8;

@@ -20,46 +20,69 @@ __device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
       make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
 }
 
-template <typename YT, typename NT>
+// W consecutive values per thread (8 when H % 8 == 0: the partition and summation order of the combine kernels'
+// residual epilogue, so that a layer's fused and unfused glue give the same bits; else 4).
+template <int W>
+__device__ __forceinline__ void load_row(const float* p, float* v) {
+#pragma unroll
+  for (int j = 0; j < W; j += 4) {
+    const float4 a = ld4(p + j);
+    v[j] = a.x, v[j + 1] = a.y, v[j + 2] = a.z, v[j + 3] = a.w;
+  }
+}
+template <int W, typename YT>
+__device__ __forceinline__ void add_row(const YT* p, float* v) {
+#pragma unroll
+  for (int j = 0; j < W; j += 4) {
+    const float4 a = ld4(p + j);
+    v[j] += a.x, v[j + 1] += a.y, v[j + 2] += a.z, v[j + 3] += a.w;
+  }
+}
+template <int W, typename T>
+__device__ __forceinline__ void store_row(T* p, const float* v) {
+#pragma unroll
+  for (int j = 0; j < W; j += 4) st4(p + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+}
+
+template <int W, typename YT, typename NT>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const float* x, const YT* __restrict__ y, int H, float eps,
                                                           float* x_out, NT* __restrict__ xn) {  // x_out may be x
-  __shared__ float red[8];
+  __shared__ float red[32];
   const size_t row = size_t(blockIdx.x) * H;
-  const int tid = threadIdx.x;
   float ss = 0.f;
-  for (int h = tid * 4; h < H; h += 1024) {
-    float4 v = ld4(x + row + h);
-    if (y) {
-      const float4 a = ld4(y + row + h);
-      v.x += a.x, v.y += a.y, v.z += a.z, v.w += a.w;
-    }
-    st4(x_out + row + h, v);
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
+  for (int h = threadIdx.x * W; h < H; h += blockDim.x * W) {
+    float v[W];
+    load_row<W>(x + row + h, v);
+    if (y) add_row<W>(y + row + h, v);
+    store_row<W>(x_out + row + h, v);
+#pragma unroll
+    for (int j = 0; j < W; ++j) ss = fmaf(v[j], v[j], ss);
   }
-  ss = warp_sum(ss);
-  if (tid % 32 == 0) red[tid / 32] = ss;
-  __syncthreads();
-  float t = tid < 8 ? red[tid] : 0.f;
-  if (tid < 32) t = warp_sum(t);
-  if (tid == 0) red[0] = t;
-  __syncthreads();
-  const float r = rsqrtf(red[0] / float(H) + eps);
-  for (int h = tid * 4; h < H; h += 1024) {
-    const float4 v = ld4(x_out + row + h);
-    st4(xn + row + h, make_float4(v.x * r, v.y * r, v.z * r, v.w * r));
+  const float r = rsqrtf(block_sum(ss, red) / float(H) + eps);
+  for (int h = threadIdx.x * W; h < H; h += blockDim.x * W) {
+    float v[W];
+    load_row<W>(x_out + row + h, v);
+#pragma unroll
+    for (int j = 0; j < W; ++j) v[j] *= r;
+    store_row<W>(xn + row + h, v);
   }
 }
 
 template <typename YT>
 static void launch_norm(const float* x, const YT* y, int T, int H, float eps, float* x_out, void* xn, int xn_dtype,
                         cudaStream_t st) {
-  if (xn_dtype == kF32)
-    add_rmsnorm_kernel<YT, float><<<T, 256, 0, st>>>(x, y, H, eps, x_out, static_cast<float*>(xn));
-  else
-    add_rmsnorm_kernel<YT, __nv_bfloat16><<<T, 256, 0, st>>>(x, y, H, eps, x_out, static_cast<__nv_bfloat16*>(xn));
+  float* xf = static_cast<float*>(xn);
+  __nv_bfloat16* xb = static_cast<__nv_bfloat16*>(xn);
+  if (H % 8 == 0) {
+    if (xn_dtype == kF32)
+      add_rmsnorm_kernel<8, YT, float><<<T, 256, 0, st>>>(x, y, H, eps, x_out, xf);
+    else
+      add_rmsnorm_kernel<8, YT, __nv_bfloat16><<<T, 256, 0, st>>>(x, y, H, eps, x_out, xb);
+  } else if (xn_dtype == kF32) {
+    add_rmsnorm_kernel<4, YT, float><<<T, 256, 0, st>>>(x, y, H, eps, x_out, xf);
+  } else {
+    add_rmsnorm_kernel<4, YT, __nv_bfloat16><<<T, 256, 0, st>>>(x, y, H, eps, x_out, xb);
+  }
 }
 
 cudaError_t add_rmsnorm(const float* x, const void* y, int y_dtype, int T, int H, float eps, float* x_out, void* xn,

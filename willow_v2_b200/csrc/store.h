@@ -19,6 +19,8 @@ struct wmoe_ctx {
   int* d_status = nullptr;  // device status word (see wmoe::DeviceStatus)
   void* scratch = nullptr;  // grown on demand
   size_t scratch_bytes = 0;
+  void* stack_xn = nullptr;  // wmoe_prefill_stack: the normalised input rows passed from layer to layer
+  size_t stack_xn_bytes = 0;
   int decode_ctas = 0;      // CTAs of the persistent decode kernel (all co-resident)
   bool use_decode_kernel = true;
   int prefill_threshold = 16;  // token count from which wmoe_moe_forward uses the tcgen05 grouped GEMMs

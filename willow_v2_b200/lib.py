@@ -59,6 +59,7 @@ SIGNATURES = {
     "wmoe_moe_forward_layer": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _i, _p, _p, _p]),
     "wmoe_decode_stack": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
     "wmoe_decode_stack_noalloc": (_i, [_p, _p, _i, _i, _p, _f, _p, _p, _p, _p]),
+    "wmoe_prefill_stack": (_i, [_p, _p, _i, _i, _p, _f, _p, _i, _i, _p, _p]),
     "wmoe_ggml_row_bytes": (_sz, [_i, _i]),
     "wmoe_gemv": (_i, [_p, _i, _p, _i, _i, _p, _i, _i, _p, _i, _p]),
     "wmoe_gemv_batch": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _i, _p, _i, _p]),

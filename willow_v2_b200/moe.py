@@ -529,6 +529,25 @@ def decode_stack(store: ExpertStore, layers: list, h: torch.Tensor, eps: float =
     return (out, sel) if return_routing else out
 
 
+def prefill_stack(store: ExpertStore, layers: list, h: torch.Tensor, eps: float = 1e-6, layer_begin: int = 0,
+                  x_dtype: torch.dtype = torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """T tokens through len(layers) stacked blocks, h <- h + moe(rms_norm(h)) per layer (wmoe_prefill_stack): the
+    residual add and the next layer's RMSNorm run in each layer's combine kernel. h: f32 [T, H] on the GPU; each
+    block takes its input in x_dtype (bf16: the tensor-core router of LayerWeights.prepare). After ep_init each layer
+    runs over the context's communicator, the store holding this rank's block of the experts (every rank passes its
+    own tokens); a capped store prefetches each next layer. out may be h."""
+    ctx = store.ctx
+    h = h.contiguous()
+    if h.dtype != torch.float32 or h.dim() != 2:
+        raise ValueError("prefill_stack: h must be a float32 [T, H] tensor")
+    out = torch.empty_like(h) if out is None else out
+    arr = (_lib.LayerWeights * len(layers))(*[lw.as_struct() for lw in layers])
+    check(ctx.handle, lib.wmoe_prefill_stack(ctx.handle, store.handle, layer_begin, len(layers),
+                                             ctypes.cast(arr, ctypes.c_void_p), ctypes.c_float(eps), _ptr(h),
+                                             h.shape[0], _DTYPES[x_dtype], _ptr(out), _stream()))
+    return out
+
+
 class CudaMoE:
     """Mixin that replaces willow's Engine.moe (engines/base.py:445-490) with the B200 kernels:
 
