@@ -1080,7 +1080,6 @@ def run_typed_decode(args, type_name: str):
     so the device time is not the host's launch rate; two more graphs hold only the gemv_batch or only the combine
     launches, for their per-launch times."""
     import torch
-    import torch.nn.functional as F
     from willow_v2_b200 import ggml, moe
     from willow_v2_b200 import lib as L
     ctx = moe.default_context()
@@ -1120,8 +1119,9 @@ def run_typed_decode(args, type_name: str):
                                                   2 * FFN, HIDDEN, x.data_ptr(), L.BF16, gate_up.data_ptr(), L.BF16,
                                                   st))
 
-    def act():
-        h.copy_((F.silu(gate_up[:, :FFN].float()) * gate_up[:, FFN:].float()).to(torch.bfloat16))
+    def act():  # willow's expert_gate (engines/base.py:99-102) on the library's kernel
+        L.check(ctx.handle, L.lib.wmoe_expert_gate(ctx.handle, gate_up.data_ptr(), TOP_K, FFN, h.data_ptr(),
+                                                   torch.cuda.current_stream().cuda_stream))
 
     def down(i):
         st = torch.cuda.current_stream().cuda_stream
@@ -1157,26 +1157,30 @@ def run_typed_decode(args, type_name: str):
     launches0 = ctx.launches
     with ClockSampler(torch.cuda.current_device()) as clocks:
         step_ms = timed("step")
-    gpu_launches = 2 * reps * G  # the graph's replays launch the captured kernels; ctx counts captures, not replays
+    gpu_launches = 3 * reps * G  # the graph's replays launch the captured kernels; ctx counts captures, not replays
     gu_ms, dn_ms = timed("up"), timed("down")
     ctx.check_device()
     del launches0
-    # e2e through the public Python API (willow_v2_b200.ggml), no graph: x from pinned host memory in, y back out
+    # e2e through the public Python API, no graph: x from pinned host memory in, the token's experts in one
+    # ggml.batched_decode_experts call (engines/base.py:492-532), y back out
     x_host = x.cpu().pin_memory()
     y_host = torch.empty(HIDDEN, dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty_like(x)
     offs = [[int(e) * eb for e in s] for s in sels]
+    dn_offs = [[o + gu_b for o in s] for s in offs]
+    slots = list(range(TOP_K))
+    for s in range(W):
+        ggml.batched_decode_experts(slab, type_name, type_name, FFN, x_dev, offs[s % G], dn_offs[s % G], route,
+                                    slots, ctx=ctx)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
+    y_dev = torch.empty(1, HIDDEN, dtype=torch.bfloat16, device="cuda")
     for s in range(K):
         x_dev.copy_(x_host, non_blocking=True)
-        ggml.gemv_batch(slab, type_name, (2 * FFN, HIDDEN), x_dev, offs[s % G], list(range(TOP_K)), gate_up,
-                        ctx=ctx)
-        hh = (F.silu(gate_up[:, :FFN].float()) * gate_up[:, FFN:].float()).to(torch.bfloat16)
-        out = ggml.gemv_combine(slab, type_name, (HIDDEN, FFN), hh, [o + gu_b for o in offs[s % G]], route,
-                                list(range(TOP_K)), ctx=ctx)
-        y_host.copy_(out.reshape(-1), non_blocking=True)
+        ggml.batched_decode_experts(slab, type_name, type_name, FFN, x_dev, offs[s % G], dn_offs[s % G], route,
+                                    slots, ctx=ctx, out=y_dev)
+        y_host.copy_(y_dev.reshape(-1), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / K
@@ -1201,7 +1205,7 @@ def run_typed_decode(args, type_name: str):
                     "achieved_gbs": dn_gbs, "frac": dn_gbs / hbm},
         "roofline_step": {"achieved": step_gbs, "frac": step_gbs / hbm, "algorithmic_bytes": TOP_K * eb},
         "e2e": {"value": 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": HIDDEN * 2,
-                "d2h_bytes_per_step": HIDDEN * 2, "path": "willow_v2_b200.ggml.gemv_batch / gemv_combine"},
+                "d2h_bytes_per_step": HIDDEN * 2, "path": "willow_v2_b200.ggml.batched_decode_experts (one library call)"},
         "gpu_launches": int(gpu_launches),
         "clocks": clocks.summary(),
     }

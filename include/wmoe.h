@@ -26,6 +26,9 @@
  *   wmoe_gemv_batch          gguf/metal.py:239-261,336-343 gemv_batch (several experts x one token)
  *   wmoe_gemv_combine        gguf/metal.py:263-291,345-355 gemv_combine (down + routing-weighted sum,
  *                            engines/base.py:492-532 batched_decode_experts)
+ *   wmoe_expert_gate         engines/base.py:99-102 expert_gate (silu(gate) * up)
+ *   wmoe_batched_decode_experts  engines/base.py:492-532 batched_decode_experts in one call (gemv_batch,
+ *                            expert_gate, gemv_combine)
  */
 #ifndef WMOE_H
 #define WMOE_H
@@ -383,6 +386,21 @@ int wmoe_gemv_batch(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights,
 int wmoe_gemv_combine(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weights, const int64_t* perm, int n,
                       int n_route, int rows, int k, const void* x, const void* route_w, int dtype, void* y,
                       void* stream);
+
+/* willow's expert_gate (engines/base.py:99-102) on bf16 rows: out [n, ffn] = silu(gate) * up for gate_up [n, 2 * ffn]
+ * ([gate | up] per row), each step rounded to bf16 as torch's bf16 F.silu and product round it. */
+int wmoe_expert_gate(wmoe_ctx* ctx, const void* gate_up, int n, int ffn, void* out, void* stream);
+
+/* One decode token's routed experts in one call, as engines/base.py:492-532 batched_decode_experts runs them when
+ * every down matrix sits in one buffer: gate_up for all n experts (wmoe_gemv_batch: [2 * ffn, hidden] matrices of
+ * gate_up_type), willow's expert_gate silu(gate) * up in bf16 (engines/base.py:99-102), then the down matrices
+ * ([hidden, ffn] of down_type) and the routing-weighted sum in bf16 (wmoe_gemv_combine, perm[i] the slot of expert
+ * i's weight in route_w). gate_up_ptrs, down_ptrs, perm: HOST arrays of n (1..256) device addresses / slots, staged
+ * to the GPU by the context without a host synchronisation; x bf16 [hidden] (16-byte aligned), route_w bf16
+ * [n_route], y bf16 [hidden]. Two launches on stream: the combine applies expert_gate as it loads the gate_up rows. */
+int wmoe_batched_decode_experts(wmoe_ctx* ctx, int gate_up_type, int down_type, int hidden, int ffn,
+                                const uint64_t* gate_up_ptrs, const uint64_t* down_ptrs, const int64_t* perm, int n,
+                                int n_route, const void* x, const void* route_w, void* y, void* stream);
 
 #ifdef __cplusplus
 }

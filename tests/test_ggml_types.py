@@ -75,6 +75,8 @@ def test_unsupported_types_are_refused_without_a_gpu():
         ggml.GGMLWeight(np.zeros(1, np.uint8), "IQ1_S", (1, 256))
     assert lib.wmoe_gemv(None, 8, None, 1, 256, None, 1, 1, None, 1, None) == ERR_INVALID
     assert lib.wmoe_gemv_combine(None, 8, None, None, 1, 1, 1, 256, None, None, 1, None, None) == ERR_INVALID
+    assert lib.wmoe_batched_decode_experts(None, 12, 14, 2048, 512, None, None, None, 8, 8, None, None, None,
+                                           None) == ERR_INVALID
 
 
 def test_wrappers_refuse_bad_arguments_without_a_gpu():
@@ -232,6 +234,62 @@ def test_gemv_batch_positions_and_combine(ctx, type_name):
     ref32 = sum(route[perm[i]] * (G.dequantize(m, type_name, (rows, k)) @ xs[i]) for i, m in enumerate(mats))
     assert rel_l2(y32.cpu().numpy(), ref32) < TOL_GEMV
     ctx.check_device()
+
+
+@pytest.mark.gpu
+def test_expert_gate_rounds_like_torch(ctx):
+    """wmoe_expert_gate gives the bits of willow's expert_gate on bf16 tensors, F.silu(gate) * up
+    (engines/base.py:99-102), over a wide range of values (large negative and positive gates, tiny ups)."""
+    import torch
+    import torch.nn.functional as F
+    from willow_v2_b200 import ggml
+    g = torch.Generator().manual_seed(3)
+    gu = (torch.randn(64, 1024, generator=g) * torch.logspace(-3, 1.5, 1024)).to(torch.bfloat16).cuda()
+    got = ggml.expert_gate(gu, ctx=ctx)
+    want = F.silu(gu[:, :512]) * gu[:, 512:]
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gu_type,dn_type", [("Q4_K", "Q6_K"), ("IQ2_S", "IQ2_S"), ("Q8_0", "Q4_K")])
+def test_batched_decode_experts(ctx, gu_type, dn_type):
+    """wmoe_batched_decode_experts (engines/base.py:492-532 in one call) gives the bits of its three steps run
+    through the Python API one after another: gemv_batch into bf16 rows, willow's expert_gate F.silu(gate) * up on
+    bf16 tensors (engines/base.py:99-102), gemv_combine. The chain is also checked against the oracle's bf16
+    restatement (the last bf16 rounding of a float32 dot product summed in another order may differ by a step)."""
+    import torch
+    import torch.nn.functional as F
+    from willow_v2_b200 import ggml
+    H, Fd, n = 2048, 512, 8
+    gu_b = 2 * Fd * G.row_bytes(gu_type, H)
+    dn_b = H * G.row_bytes(dn_type, Fd)
+    gus = [matrix(gu_type, 2 * Fd, H, 300 + i) for i in range(n)]
+    dns = [matrix(dn_type, H, Fd, 400 + i) for i in range(n)]
+    slab_np = np.concatenate([np.concatenate([g, d]) for g, d in zip(gus, dns)])
+    slab = torch.from_numpy(slab_np).cuda()
+    offs = [i * (gu_b + dn_b) for i in range(n)]
+    rng = np.random.default_rng(21)
+    x = torch.from_numpy(rng.standard_normal(H).astype(np.float32)).to(torch.bfloat16).cuda()
+    route = torch.from_numpy(rng.uniform(0.02, 0.3, 8).astype(np.float32)).to(torch.bfloat16).cuda()
+    perm = [3, 0, 6, 1, 5, 2, 7, 4]
+    y = ggml.batched_decode_experts(slab, gu_type, dn_type, Fd, x, offs, [o + gu_b for o in offs], route, perm,
+                                    ctx=ctx)
+    gate_up = torch.empty(n, 2 * Fd, dtype=torch.bfloat16, device="cuda")
+    ggml.gemv_batch(slab, gu_type, (2 * Fd, H), x, offs, list(range(n)), gate_up, ctx=ctx)
+    hidden = (F.silu(gate_up[:, :Fd]) * gate_up[:, Fd:]).contiguous()
+    want = ggml.gemv_combine(slab, dn_type, (H, Fd), hidden, [o + gu_b for o in offs], route, perm, ctx=ctx)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    assert y.shape == (1, H) and y.dtype == torch.bfloat16
+    assert torch.equal(y, want)
+    # the oracle's chain
+    xb = x.float().cpu().numpy()
+    g = np.stack([G.bf16(G.dequantize(m, gu_type, (2 * Fd, H)) @ xb) for m in gus])
+    gt = torch.from_numpy(g).to(torch.bfloat16)
+    hid = (F.silu(gt[:, :Fd]) * gt[:, Fd:]).float().numpy()
+    ref = G.gemv_combine_bf16(dns, dn_type, (H, Fd), hid, route.float().cpu().numpy(), perm)
+    assert rel_l2(y.float().cpu().numpy().reshape(-1), ref) < 1e-2
 
 
 @pytest.mark.gpu

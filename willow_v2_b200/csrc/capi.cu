@@ -111,6 +111,10 @@ void wmoe_destroy(wmoe_ctx* ctx) {
   ep_release(ctx);
   cudaFree(ctx->scratch);
   cudaFree(ctx->stack_xn);
+  cudaFree(ctx->stage_dev);
+  cudaFreeHost(ctx->stage_host);
+  for (cudaEvent_t ev : ctx->stage_ev)
+    if (ev) cudaEventDestroy(ev);
   cudaFree(ctx->d_status);
   delete ctx;
 }
@@ -1766,6 +1770,75 @@ int wmoe_gemv_combine(wmoe_ctx* ctx, int ggml_type, const uint8_t* const* weight
     return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED, "wmoe_gemv_combine: a row tile of this k does not fit shared memory");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_gemv_combine");
   ctx->launches += 1;
+  return WMOE_OK;
+}
+
+int wmoe_expert_gate(wmoe_ctx* ctx, const void* gate_up, int n, int ffn, void* out, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (n < 0 || ffn < 1) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_expert_gate: n < 0 or ffn < 1");
+  if (n == 0) return WMOE_OK;
+  if (!gate_up || !out) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_expert_gate: null pointer");
+  WMOE_CHECK_CUDA(ctx, swiglu_bf16(gate_up, n, ffn, out, static_cast<cudaStream_t>(stream)), "wmoe_expert_gate");
+  ctx->launches += 1;
+  return WMOE_OK;
+}
+
+int wmoe_batched_decode_experts(wmoe_ctx* ctx, int gate_up_type, int down_type, int hidden, int ffn,
+                                const uint64_t* gate_up_ptrs, const uint64_t* down_ptrs, const int64_t* perm, int n,
+                                int n_route, const void* x, const void* route_w, void* y, void* stream) {
+  if (!ctx) return WMOE_ERR_INVALID;
+  if (int rc = typed_args(ctx, "wmoe_batched_decode_experts", gate_up_type, 2 * ffn, hidden)) return rc;
+  if (int rc = typed_args(ctx, "wmoe_batched_decode_experts", down_type, hidden, ffn)) return rc;
+  if (n < 1 || n > 256 || n_route < 1 || hidden < 1 || ffn < 1)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_batched_decode_experts: n must be 1..256, n_route >= 1");
+  if (!gate_up_ptrs || !down_ptrs || !perm || !x || !route_w || !y)
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_batched_decode_experts: null pointer");
+  for (int i = 0; i < n; ++i)
+    if (!gate_up_ptrs[i] || !down_ptrs[i] || perm[i] < 0 || perm[i] >= n_route)
+      return ctx_fail(ctx, WMOE_ERR_INVALID,
+                      "wmoe_batched_decode_experts: null matrix pointer or perm entry outside the routing weights");
+  if (!aligned16(x)) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_batched_decode_experts: x must be 16-byte aligned");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  constexpr int kSlots = wmoe_ctx::kStageSlots, kWords = wmoe_ctx::kStageWords;
+  if (!ctx->stage_host) {
+    WMOE_CHECK_CUDA(ctx, cudaHostAlloc(&ctx->stage_host, sizeof(int64_t) * kSlots * kWords, cudaHostAllocDefault),
+                    "wmoe_batched_decode_experts: staging");
+    WMOE_CHECK_CUDA(ctx, cudaMalloc(&ctx->stage_dev, sizeof(int64_t) * kSlots * kWords),
+                    "wmoe_batched_decode_experts: staging");
+    for (cudaEvent_t& ev : ctx->stage_ev)
+      WMOE_CHECK_CUDA(ctx, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "wmoe_batched_decode_experts");
+  }
+  Plan plan;
+  const size_t o_gu = plan.take<uint16_t>(size_t(n) * 2 * ffn);
+  if (int rc = ensure_scratch(ctx, plan.bytes)) return rc;
+  const int slot = ctx->stage_next;
+  ctx->stage_next = (slot + 1) % kSlots;
+  if (ctx->stage_used[slot])
+    WMOE_CHECK_CUDA(ctx, cudaEventSynchronize(ctx->stage_ev[slot]), "wmoe_batched_decode_experts: staging");
+  int64_t* host = ctx->stage_host + size_t(slot) * kWords;
+  int64_t* dev = ctx->stage_dev + size_t(slot) * kWords;
+  for (int i = 0; i < n; ++i) {
+    host[i] = int64_t(gate_up_ptrs[i]);
+    host[n + i] = int64_t(down_ptrs[i]);
+    host[2 * n + i] = perm[i];
+  }
+  WMOE_CHECK_CUDA(ctx, cudaMemcpyAsync(dev, host, sizeof(int64_t) * 3 * size_t(n), cudaMemcpyHostToDevice, st),
+                  "wmoe_batched_decode_experts: staging");
+  void* gu = at<void>(ctx, o_gu);
+  // gate_up, then the combine, which applies expert_gate as it loads the gate_up rows
+  cudaError_t e = ggml_gemv(gate_up_type, reinterpret_cast<const uint8_t* const*>(dev), nullptr, nullptr, n, n,
+                            2 * ffn, hidden, x, WMOE_BF16, 1, gu, WMOE_BF16, ctx->d_status, st);
+  if (e == cudaSuccess)
+    e = ggml_combine(down_type, reinterpret_cast<const uint8_t* const*>(dev + n), dev + 2 * n, n, n_route, hidden,
+                     ffn, gu, route_w, WMOE_BF16, y, ctx->d_status, st, true);
+  // the slot is released behind whatever was enqueued, also when a launch was refused
+  cudaEventRecord(ctx->stage_ev[slot], st);
+  ctx->stage_used[slot] = true;
+  if (e == cudaErrorNotSupported)
+    return ctx_fail(ctx, WMOE_ERR_UNSUPPORTED,
+                    "wmoe_batched_decode_experts: a row tile of this k does not fit shared memory");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "wmoe_batched_decode_experts");
+  ctx->launches += 2;
   return WMOE_OK;
 }
 

@@ -520,8 +520,9 @@ __global__ void __launch_bounds__(256) gather_fp16_kernel(PairMap pm, const XT* 
 // One CTA per token, 8 consecutive outputs per thread from 16-byte loads of each row. The token rows (x) are
 // converted to fp16 unscaled: callers pass normalised hidden states (|x| far below 65504). With the residual
 // epilogue (an.h set) the CTA adds its row to h[t] and, when an.xn is set, writes the next layer's normalised input
-// from the updated row it holds: the separate residual + RMSNorm pass over the activations goes away.
-template <int K>
+// from the updated row it holds: the separate residual + RMSNorm pass over the activations goes away. EPI selects
+// the epilogue at compile time (a run-time branch cost the plain combine 8%).
+template <int K, bool EPI>
 __global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t* __restrict__ topk_idx,
                                                            const float* __restrict__ topk_w,
                                                            const int32_t* __restrict__ rows,
@@ -571,7 +572,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t*
         acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(f.y, wi));
       }
     }
-    if (an.h) {  // h[t] += out[t] (x + moe(...), engines/qwen36/model.py:22)
+    if constexpr (EPI) {  // h[t] += out[t] (x + moe(...), engines/qwen36/model.py:22)
       float4* hp = reinterpret_cast<float4*>(an.h + size_t(t) * H + r);
       const float4 a = hp[0], b = hp[1];
       const float v[8] = {__fadd_rn(a.x, acc[0]), __fadd_rn(a.y, acc[1]), __fadd_rn(a.z, acc[2]),
@@ -581,11 +582,11 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(int H, const int32_t*
       hp[1] = make_float4(v[4], v[5], v[6], v[7]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
-      continue;
+    } else {
+      store8(out, out_dtype == kF32, size_t(t) * H + r, acc);
     }
-    store8(out, out_dtype == kF32, size_t(t) * H + r, acc);
   }
-  if (an.h && an.xn) {  // uniform over the CTA: xn[t] = h[t] / sqrt(mean(h[t]^2) + eps) (engines/base.py:27-32)
+  if (EPI && an.xn) {  // uniform over the CTA: xn[t] = h[t] / sqrt(mean(h[t]^2) + eps) (engines/base.py:27-32)
     const float rs = rsqrtf(block_sum(ss, red) / float(H) + an.eps);
     for (int r = threadIdx.x * 8; r < H; r += blockDim.x * 8) {
       const float4* hp = reinterpret_cast<const float4*>(an.h + size_t(t) * H + r);
@@ -719,8 +720,12 @@ cudaError_t combine_rows(int T, int k, int H, const int32_t* topk_idx, const flo
            : reinterpret_cast<uintptr_t>(out) % 16)
     return cudaErrorInvalidValue;
   if (T > 0) {
-    combine_rows_kernel<8><<<unsigned(T), 256, 0, st>>>(H, topk_idx, topk_w, rows, shared_s, y_routed, y_shared, out,
-                                                        out_dtype, an);
+    if (an.h)
+      combine_rows_kernel<8, true><<<unsigned(T), 256, 0, st>>>(H, topk_idx, topk_w, rows, shared_s, y_routed,
+                                                                y_shared, out, out_dtype, an);
+    else
+      combine_rows_kernel<8, false><<<unsigned(T), 256, 0, st>>>(H, topk_idx, topk_w, rows, shared_s, y_routed,
+                                                                 y_shared, out, out_dtype, an);
     ++*launches;
   }
   return cudaGetLastError();

@@ -138,6 +138,16 @@ __device__ __forceinline__ XQ xq_view(uint8_t* p, int n, int k) {
 // block is 2^(E - 15) for its largest magnitude m = f * 2^E (f in [0.5, 1)), so |q| <= 32767 (the one value that
 // rounds to 2^15 is clamped) and every value within 2^7 of m that a bf16 can hold is exact; blocks with m below
 // 2^-107 are zero. With int8 weights a chunk's dp2a sum stays below 32 * 32767 * 127 < 2^31.
+// willow's expert_gate (engines/base.py:99-102) on one bf16 gate / up pair, as torch computes it on bf16 tensors:
+// silu(g) = g / (1 + exp(-g)) in float rounded to bf16, then that times u in float rounded to bf16.
+__device__ __forceinline__ float expert_gate_bf16(float g, float u) {
+  const float s = __bfloat162float(__float2bfloat16_rn(g / (1.f + expf(-g))));
+  return __bfloat162float(__float2bfloat16_rn(s * u));
+}
+
+// x_dtype kGated: x is bf16 gate_up rows [n][2k] and row r's input is expert_gate(gate, up) of them
+constexpr int kGated = -1;
+
 __device__ __forceinline__ void quantize_x(const void* x, int x_dtype, int n, int k, XQ xq) {
   const int nblk = n * (k / 32);
   const int sub = threadIdx.x % 8, group = threadIdx.x / 8, groups = blockDim.x / 8;
@@ -150,6 +160,14 @@ __device__ __forceinline__ void quantize_x(const void* x, int x_dtype, int n, in
       if (x_dtype == kF32) {
         const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + at);
         v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+      } else if (x_dtype == kGated) {
+        const size_t r = at / size_t(k), j = at % size_t(k);
+        const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(x) + r * 2 * k + j;
+        const uint2 g = *reinterpret_cast<const uint2*>(gp), u = *reinterpret_cast<const uint2*>(gp + k);
+        v[0] = expert_gate_bf16(__uint_as_float(g.x << 16), __uint_as_float(u.x << 16));
+        v[1] = expert_gate_bf16(__uint_as_float(g.x & 0xFFFF0000u), __uint_as_float(u.x & 0xFFFF0000u));
+        v[2] = expert_gate_bf16(__uint_as_float(g.y << 16), __uint_as_float(u.y << 16));
+        v[3] = expert_gate_bf16(__uint_as_float(g.y & 0xFFFF0000u), __uint_as_float(u.y & 0xFFFF0000u));
       } else {
         const uint2 h = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + at);
         v[0] = __uint_as_float(h.x << 16), v[1] = __uint_as_float(h.x & 0xFFFF0000u);
@@ -323,9 +341,10 @@ struct CombineArgs {
   const int64_t* perm;            // [n]: index of matrix i's routing weight in route_w (checked against n_route)
   int n, n_route, rows, k, tile_rows, group;  // group: matrices staged at once
   size_t row_bytes;
-  const void* x;        // [n, k]: matrix i's input row
+  const void* x;        // [n, k]: matrix i's input row (gated: bf16 [n, 2k] gate_up rows, see kGated)
   const void* route_w;  // [n_route]
   int dtype;            // kBF16: bf16 x, weights, y and rounding at each step; kF32: all float32
+  int gated;            // x holds gate_up rows and the input is willow's expert_gate of them (kBF16 only)
   void* y;              // [rows]
   int* status;
 };
@@ -378,7 +397,7 @@ __global__ void __launch_bounds__(kCombineThreads) ggml_combine_kernel(CombineAr
       const uint8_t* src = mats[g0 + m] + size_t(r0) * a.row_bytes;
       stage_bytes(stage + m * slot + (reinterpret_cast<uintptr_t>(src) & 15), src, tile_bytes);
     }
-    if (g0 == 0) quantize_x(a.x, a.dtype, a.n, a.k, xq);  // while the first group's copies are in flight
+    if (g0 == 0) quantize_x(a.x, a.gated ? kGated : a.dtype, a.n, a.k, xq);  // while the first copies fly
     cp_async_wait_all();
     __syncthreads();
     const IntTables it = int_tables<T>(tab);
@@ -527,13 +546,13 @@ cudaError_t ggml_gemv(int type, const uint8_t* const* weights, const uint8_t* si
 
 cudaError_t ggml_combine(int type, const uint8_t* const* weights, const int64_t* perm, int n, int n_route, int rows,
                          int k, const void* x, const void* route_w, int dtype, void* y, int* status,
-                         cudaStream_t st) {
+                         cudaStream_t st, bool gated) {
   const size_t rb = ggml_row_bytes(type, k);
-  if (rb == 0 || k % 32 || n < 1) return cudaErrorInvalidValue;
+  if (rb == 0 || k % 32 || n < 1 || (gated && dtype != kBF16)) return cudaErrorInvalidValue;
   if (rows == 0) return cudaSuccess;
   const int lanes = lanes_for(k / 32);
   const int rows_per_pass = kCombineThreads / 32 * (32 / lanes);  // one row per lane group: the tile is one pass
-  CombineArgs a{weights, perm, n, n_route, rows, k, 0, 0, rb, x, route_w, dtype, y, status};
+  CombineArgs a{weights, perm, n, n_route, rows, k, 0, 0, rb, x, route_w, dtype, gated ? 1 : 0, y, status};
   a.tile_rows = std::min(rows, rows_per_pass);
   const size_t slot = align16(size_t(a.tile_rows) * rb) + 16;
   const size_t tab = align16(table_bytes(type)) + xq_bytes(n, k) + combine_meta_bytes(n);
@@ -552,6 +571,24 @@ cudaError_t ggml_combine(int type, const uint8_t* const* weights, const int64_t*
       return cudaGetLastError();
     });
   });
+}
+
+// willow's expert_gate on bf16 [n][2F] gate_up rows (expert_gate_bf16 per element)
+__global__ void __launch_bounds__(256) swiglu_bf16_kernel(const __nv_bfloat16* __restrict__ gu, int n, int F,
+                                                          __nv_bfloat16* __restrict__ out) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= size_t(n) * F) return;
+  const size_t e = i / size_t(F), j = i % size_t(F);
+  out[i] = __float2bfloat16_rn(expert_gate_bf16(__bfloat162float(gu[e * 2 * F + j]),
+                                                __bfloat162float(gu[e * 2 * F + F + j])));
+}
+
+cudaError_t swiglu_bf16(const void* gate_up, int n, int F, void* out, cudaStream_t st) {
+  const size_t total = size_t(n) * F;
+  if (total == 0) return cudaSuccess;
+  swiglu_bf16_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gate_up), n, F,
+                                                                   static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
 }
 
 }  // namespace wmoe

@@ -210,9 +210,13 @@ cudaError_t ggml_gemv(int type, const uint8_t* const* weights, const uint8_t* si
                       int n_out, int rows, int k, const void* x, int x_dtype, int tokens, void* y, int y_dtype,
                       int* status, cudaStream_t st);
 // y[r] = sum_i route_w[perm[i]] * (W_i[r] . x[i]) in order of i; dtype kBF16 rounds each product, scaled product
-// and running sum to bf16 (engines/base.py:431-443), kF32 keeps float32
+// and running sum to bf16 (engines/base.py:431-443), kF32 keeps float32. gated (kBF16 only): x holds bf16 gate_up
+// rows [n][2k] and x[i] is willow's expert_gate of row i (engines/base.py:99-102), as swiglu_bf16 computes it
+// willow's expert_gate on bf16 [n][2F] gate_up rows -> bf16 [n][F], rounded as torch's bf16 silu and product
+cudaError_t swiglu_bf16(const void* gate_up, int n, int F, void* out, cudaStream_t st);
 cudaError_t ggml_combine(int type, const uint8_t* const* weights, const int64_t* perm, int n, int n_route, int rows,
                          int k, const void* x, const void* route_w, int dtype, void* y, int* status,
-                         cudaStream_t st);
+                         cudaStream_t st,
+                         bool gated = false);
 
 }  // namespace wmoe

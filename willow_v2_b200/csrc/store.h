@@ -21,6 +21,14 @@ struct wmoe_ctx {
   size_t scratch_bytes = 0;
   void* stack_xn = nullptr;  // wmoe_prefill_stack: the normalised input rows passed from layer to layer
   size_t stack_xn_bytes = 0;
+  // wmoe_batched_decode_experts: the host pointer and order arrays go to the GPU through a ring of pinned slots; a
+  // slot is rewritten only after the event recorded behind the kernels that read it has completed
+  static constexpr int kStageSlots = 16, kStageWords = 3 * 256;
+  int64_t* stage_host = nullptr;
+  int64_t* stage_dev = nullptr;
+  cudaEvent_t stage_ev[kStageSlots] = {};
+  bool stage_used[kStageSlots] = {};
+  int stage_next = 0;
   int decode_ctas = 0;      // CTAs of the persistent decode kernel (all co-resident)
   bool use_decode_kernel = true;
   int prefill_threshold = 16;  // token count from which wmoe_moe_forward uses the tcgen05 grouped GEMMs

@@ -221,6 +221,63 @@ def gemv_combine(base: torch.Tensor, type_name: str, shape: tuple, x: torch.Tens
     return y
 
 
+def expert_gate(gate_up: torch.Tensor, ctx=None) -> torch.Tensor:
+    """willow's expert_gate (engines/base.py:99-102) on bf16 [n, 2 * ffn] rows -> bf16 [n, ffn] (wmoe_expert_gate),
+    rounded as torch's bf16 F.silu(gate) * up."""
+    if gate_up.dtype != torch.bfloat16 or gate_up.dim() != 2 or gate_up.shape[1] % 2:
+        raise ValueError("expert_gate takes bf16 [n, 2 * ffn]")
+    gate_up = gate_up.contiguous()
+    _on_gpu(gate_up)
+    n, ffn = gate_up.shape[0], gate_up.shape[1] // 2
+    out = torch.empty(n, ffn, dtype=torch.bfloat16, device=gate_up.device)
+    ctx = ctx or _ctx()
+    check(ctx.handle, lib.wmoe_expert_gate(ctx.handle, _p(gate_up), n, ffn, _p(out), _stream()))
+    return out
+
+
+def batched_decode_experts(base: torch.Tensor, gate_up_type: str, down_type: str, ffn: int, x: torch.Tensor,
+                           gate_up_offsets, down_offsets, routing_weights: torch.Tensor, perm,
+                           ctx=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One decode token's routed experts in one library call (wmoe_batched_decode_experts), as
+    engines/base.py:492-532 batched_decode_experts runs them when the experts sit in one buffer: gate_up_offsets[i]
+    is expert i's [2 * ffn, hidden] gate_up matrix of gate_up_type and down_offsets[i] its [hidden, ffn] down matrix
+    of down_type, byte offsets in base (uint8, on the GPU); x bf16 [hidden]; routing_weights bf16 [top_k], perm[i]
+    the slot of expert i's weight in it. Returns bf16 [1, hidden] (written into out when given), the value of
+    gemv_batch, expert_gate and gemv_combine run one after another. The library checks the perm entries."""
+    n = len(gate_up_offsets)
+    if n == 0 or len(down_offsets) != n or len(perm) != n:
+        raise ValueError("one down offset and one perm entry per gate_up offset, at least one")
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        x = x.to(torch.bfloat16).contiguous()
+    hidden = x.numel()
+    w = routing_weights
+    if w.dtype != torch.bfloat16 or not w.is_contiguous():
+        w = w.to(torch.bfloat16).contiguous()
+    gu_bytes = 2 * ffn * row_bytes(gate_up_type, hidden)
+    dn_bytes = hidden * row_bytes(down_type, ffn)
+    size = base.numel()
+    if min(gate_up_offsets) < 0 or max(gate_up_offsets) + gu_bytes > size:
+        raise ValueError("a gate_up offset puts its matrix outside base")
+    if min(down_offsets) < 0 or max(down_offsets) + dn_bytes > size:
+        raise ValueError("a down offset puts its matrix outside base")
+    dev = base.device
+    if not (base.is_cuda and x.device == dev and w.device == dev):
+        raise ValueError("base, x and routing_weights must be CUDA tensors on one device")
+    if out is None:
+        out = torch.empty(1, hidden, dtype=torch.bfloat16, device=dev)
+    elif out.dtype != torch.bfloat16 or out.numel() != hidden or not out.is_contiguous() or out.device != dev:
+        raise ValueError("out must be a contiguous bf16 tensor of hidden values on base's device")
+    b0 = base.data_ptr()
+    gu = (ctypes.c_uint64 * n)(*[b0 + o for o in gate_up_offsets])
+    dn = (ctypes.c_uint64 * n)(*[b0 + o for o in down_offsets])
+    pm = (ctypes.c_int64 * n)(*perm)
+    ctx = ctx or _ctx()
+    check(ctx.handle, lib.wmoe_batched_decode_experts(ctx.handle, _type_id(gate_up_type), _type_id(down_type), hidden,
+                                                      ffn, gu, dn, pm, n, w.numel(), x.data_ptr(), w.data_ptr(),
+                                                      out.data_ptr(), torch.cuda.current_stream(dev).cuda_stream))
+    return out
+
+
 class GGMLWeight:
     """A [rows, k] weight kept as its ggml blocks on the GPU, used in place of a bf16 tensor: F.linear(x, weight)
     runs the CUDA kernels above (through __torch_function__). raw is a uint8 tensor; a CPU tensor is copied to the

@@ -64,6 +64,8 @@ SIGNATURES = {
     "wmoe_gemv": (_i, [_p, _i, _p, _i, _i, _p, _i, _i, _p, _i, _p]),
     "wmoe_gemv_batch": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _i, _p, _i, _p]),
     "wmoe_gemv_combine": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _p, _i, _p, _p]),
+    "wmoe_expert_gate": (_i, [_p, _p, _i, _i, _p, _p]),
+    "wmoe_batched_decode_experts": (_i, [_p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _p, _p, _p]),
     "wmoe_ep_route_plan": (_i, [_p, _i, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "wmoe_ep_experts": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p]),
     "wmoe_ep_combine": (_i, [_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _i, _p]),
