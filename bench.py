@@ -118,6 +118,55 @@ def workload_config(workload: str, world: int, n_layers: int = LAYERS, type_name
     raise ValueError(workload)
 
 
+def pipelined_e2e(torch, run, x_hosts, K: int, dist=None) -> float:
+    """Milliseconds per step of K end-to-end steps whose copies overlap the compute of neighbouring steps, as a
+    serving loop double-buffers them: step s's input is copied in from pinned host memory on one copy stream and
+    its result read back into pinned host memory on another, while step s - 1 or s + 1 computes on the current
+    stream. Every step copies its whole input in and its whole result out inside the timed region; two device input
+    buffers and two pinned result buffers, ordered by events (an input buffer is rewritten only after the step that
+    read it, a result only after its read-back). run(x_dev, b) enqueues one step on the current stream and returns
+    its device result (buffer b of two, or a fresh tensor)."""
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    x_dev = [torch.empty_like(x_hosts[0], device="cuda") for _ in range(2)]
+    o_host = [None, None]
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # input b landed
+    ev_used = [torch.cuda.Event() for _ in range(2)]  # the step on input b is done
+    ev_out = [torch.cuda.Event() for _ in range(2)]   # result b read back
+    for b in range(2):
+        ev_used[b].record(comp)
+        ev_out[b].record(comp)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    h2d.wait_stream(comp)
+    d2h.wait_stream(comp)
+    for s in range(K):
+        b = s % 2
+        h2d.wait_event(ev_used[b])
+        with torch.cuda.stream(h2d):
+            x_dev[b].copy_(x_hosts[s % len(x_hosts)], non_blocking=True)
+        ev_in[b].record(h2d)
+        comp.wait_event(ev_in[b])
+        comp.wait_event(ev_out[b])
+        out = run(x_dev[b], b)
+        ev_used[b].record(comp)
+        out.record_stream(d2h)
+        if o_host[b] is None:
+            o_host[b] = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        d2h.wait_event(ev_used[b])
+        with torch.cuda.stream(d2h):
+            o_host[b].copy_(out, non_blocking=True)
+        ev_out[b].record(d2h)
+    comp.wait_stream(h2d)
+    comp.wait_stream(d2h)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / K
+
+
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons of the bench's GPU, read through NVML every ~2 ms on a thread
     while the timed region runs, plus once on entry and once on exit, so that even a region of a few milliseconds
@@ -550,8 +599,8 @@ def cpu_baseline_batch():
 
 def run_prefill4096_ep(args, rank: int, world: int, dist):
     """configs[3] expert-parallel: rank r holds experts [r * 256 / N, (r + 1) * 256 / N) and routes its own 4096
-    tokens per step (weak scaling); dispatch and combine are NCCL all-to-alls issued by the library
-    (moe_forward_ep_native), with its per-phase CUDA events."""
+    tokens per step (weak scaling); dispatch and combine are the library's exchanges (moe_forward_ep_native: count
+    all-gather, copy-engine copies into the peers' windows), with its per-phase CUDA events."""
     import torch
     from willow_v2_b200 import moe, synth
     device = torch.cuda.current_device()
@@ -607,20 +656,10 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
     stage_ms = {k: statistics.mean(v) for k, v in stage.items()}
     ctx.check_device()
 
-    # end to end: pinned bf16 host batch -> device, layer, result -> pinned host, every step
+    # end to end: pinned bf16 host batch -> device, layer, result -> pinned host, every step, the copies of
+    # neighbouring steps overlapping the layer (pipelined_e2e)
     x_host = [x.cpu().pin_memory() for x in xs]
-    o_host = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device="cuda")
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for s in range(K):
-        x_dev.copy_(x_host[s % 4], non_blocking=True)
-        o_host.copy_(moe.moe_forward_ep_native(store, 0, x_dev, lw), non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / K
+    e2e_ms = pipelined_e2e(torch, lambda x_dev, b: moe.moe_forward_ep_native(store, 0, x_dev, lw), x_host, K, dist)
     ctx.ep_finalize()
     dist.barrier()
     experts_ms = stage_ms.get("experts", float("nan"))
@@ -647,7 +686,9 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
                      "note": "exchanges run on a second stream overlapping the expert stages; exposed = waits"},
         "stage_ms_rank0": stage_ms,
         "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 2,
-                "d2h_bytes_per_step": T * HIDDEN * 2},
+                "d2h_bytes_per_step": T * HIDDEN * 2,
+                "copies": "every step's input in and result out inside the timed region, on two copy streams "
+                          "overlapping the neighbouring steps' compute (double buffers ordered by events)"},
         "gpu_launches": int(gpu_launches),
         "clocks": clocks.summary(),
     }
@@ -833,22 +874,16 @@ def run_prefill4096(args, rank: int, world: int, dist):
     phase_ms = {name: statistics.mean(v) for name, v in phase.items()}
     ctx.check_device()
 
-    # end to end through the public API: pinned bf16 host batch -> device, layer, result -> pinned host, every step
+    # end to end through the public API: pinned bf16 host batch -> device, layer, result -> pinned host, every step,
+    # the copies of neighbouring steps overlapping the layer (pipelined_e2e)
     x_host = [x.cpu().pin_memory() for x in xs]
-    o_host = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device="cuda")
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for s in range(K):
-        x_dev.copy_(x_host[s % 4], non_blocking=True)
-        step(x_dev, out)
-        o_host.copy_(out, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / K
+    outs = [out, torch.empty_like(out)]
+
+    def run(x_dev, b):
+        step(x_dev, outs[b])
+        return outs[b]
+
+    e2e_ms = pipelined_e2e(torch, run, x_host, K, dist)
     if dist:
         dist.barrier()
 
@@ -875,7 +910,9 @@ def run_prefill4096(args, rank: int, world: int, dist):
         "layer_tensor_frac": layer_tflops / bf16,
         "phase_ms": phase_ms,
         "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 2,
-                "d2h_bytes_per_step": T * HIDDEN * 2},
+                "d2h_bytes_per_step": T * HIDDEN * 2,
+                "copies": "every step's input in and result out inside the timed region, on two copy streams "
+                          "overlapping the neighbouring steps' compute (double buffers ordered by events)"},
         "gpu_launches": int(gpu_launches),
         "clocks": clocks.summary(),
     }
