@@ -618,10 +618,16 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
     xs = [torch.from_numpy(synth.hidden(SEED + 1000 * rank, T, step=b)).to(torch.bfloat16).cuda() for b in range(4)]
     stream = torch.cuda.current_stream()
     from willow_v2_b200 import lib as L
+    if args.ep_exchange == "nccl":
+        os.environ["WMOE_EP_NCCL_ROWS"] = "1"
+    elif args.ep_exchange == "copy":
+        os.environ.pop("WMOE_EP_NCCL_ROWS", None)
     moe.ep_init(ctx)
-    # tokens per expert grow with N (weak scaling): chunks of ~256 tokens per expert overlap exchanges and GEMMs
-    chunks = max(1, world // 2)
+    if args.ep_chunks is not None:
+        L.lib.wmoe_ep_set_chunks(ctx.handle, args.ep_chunks)
+    chunks = L.lib.wmoe_ep_set_chunks(ctx.handle, 1)  # read the setting back
     L.lib.wmoe_ep_set_chunks(ctx.handle, chunks)
+    rows = "copy engines into IPC windows" if L.lib.wmoe_ep_uses_copy_engines(ctx.handle) == 1 else "NCCL send/recv"
     for s in range(W):
         moe.moe_forward_ep_native(store, 0, xs[s % 4], lw)
     torch.cuda.synchronize()
@@ -683,6 +689,7 @@ def run_prefill4096_ep(args, rank: int, world: int, dist):
                      "peak_kind": peak_kind, "algorithmic_flops_per_launch": flops, "launch_ms": experts_ms},
         "exchange": {"bytes_out_per_step": bytes_out, "exposed_ms_max": a2a_ms_max,
                      "link_gbs_ref": link, "chunks": chunks,
+                     "rows": rows,
                      "note": "exchanges run on a second stream overlapping the expert stages; exposed = waits"},
         "stage_ms_rank0": stage_ms,
         "e2e": {"value": world * T * 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": T * HIDDEN * 2,
@@ -704,7 +711,6 @@ def run_prefill32k(args, rank: int, world: int, dist):
     call: residual + RMSNorm in each layer's combine kernel, the next layer's prefetch issued by the library. Strong
     scaling: the 32768 tokens are split over the ranks."""
     import torch
-    from willow_v2_b200 import lib as L
     from willow_v2_b200 import moe, synth
     device = torch.cuda.current_device()
     ctx = moe.Context(device)
@@ -724,9 +730,8 @@ def run_prefill32k(args, rank: int, world: int, dist):
     h0s = [torch.from_numpy(synth.hidden(SEED, PF32_T, step=99 + b)[rank * T:(rank + 1) * T]).cuda() for b in range(2)]
     h = torch.empty_like(h0s[0])
     stream = torch.cuda.current_stream()
-    if world > 1:  # every layer of the stack then runs over the library's communicator
+    if world > 1:  # every layer of the stack then runs over the library's communicator (its chunk count)
         moe.ep_init(ctx)
-        L.lib.wmoe_ep_set_chunks(ctx.handle, max(1, world // 2))
 
     def stack(h):  # h <- h + moe(rms_norm(h)) for every layer, in place; bf16 block inputs
         return moe.prefill_stack(store, lws, h, x_dtype=torch.bfloat16, out=h)
@@ -1276,6 +1281,10 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="stack depth (40 = the benchmark; fewer = profiling)")
     ap.add_argument("--no-decode40", action="store_true",
                     help="prefill4096 at N=1: skip the decode40 measurement attached to the line")
+    ap.add_argument("--ep-chunks", type=int, default=None,
+                    help="prefill4096 at N>1: token chunks per rank (default: the library's choice for N)")
+    ap.add_argument("--ep-exchange", choices=["auto", "copy", "nccl"], default="auto",
+                    help="prefill4096 at N>1: the rows' exchange (default: the library's choice for N)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 20 if args.impl == "reference" else 2000

@@ -285,12 +285,15 @@ int wmoe_ep_finalize(wmoe_ctx* ctx);
  * does so too until wmoe_ep_finalize and a new wmoe_ep_init. Returns the previous value. No counterpart in willow,
  * which runs on one device. */
 int wmoe_ep_set_timeout(wmoe_ctx* ctx, int ms);
-/* wmoe_moe_forward_ep runs the rank's tokens in this many chunks (1..16, default 1) so that the exchanges of one
- * chunk overlap the expert stage of another (the exchanges then run on a stream of the context, and the GEMMs leave
- * SMs free for them). Every rank must use the same value: the count exchange carries it, and a mismatch makes every
+/* wmoe_moe_forward_ep runs the rank's tokens in this many chunks (1..16; wmoe_ep_init sets 1 below four ranks and 2
+ * from four) so that the exchanges of one chunk overlap the expert stage of another (the exchanges then run on a
+ * stream of the context, and the GEMMs leave SMs free for them). Every rank must use the same value: the count exchange carries it, and a mismatch makes every
  * rank's call return WMOE_ERR_INVALID. The result does not depend on it. Chunks pay off when each expert still gets
  * ~256 tokens per chunk (the tensor cores' cost per instruction is fixed up to N = 192). Returns the previous value. */
 int wmoe_ep_set_chunks(wmoe_ctx* ctx, int chunks);
+/* 1 when the context's exchanges copy the rows with the copy engines into the peers' windows, 0 when they go through
+ * NCCL send/recv (WMOE_EP_NCCL_ROWS set at wmoe_ep_init), -1 without a communicator. */
+int wmoe_ep_uses_copy_engines(const wmoe_ctx* ctx);
 int wmoe_moe_forward_ep(wmoe_ctx* ctx, wmoe_store* store, int layer, const void* x, int x_dtype, int T, int top_k,
                         const wmoe_layer_weights* weights, void* out, int out_dtype, int32_t* topk_idx_out,
                         float* topk_w_out, void* stream);

@@ -1014,6 +1014,9 @@ int wmoe_ep_init(wmoe_ctx* ctx, const void* unique_id, int rank, int world) {
   if (int rc = nccl_settle(ctx, r, "wmoe_ep_init")) return rc;
   ctx->ep_rank = rank;
   ctx->ep_world = world;
+  // measured at 4096 tokens per rank: one chunk is fastest on two ranks, two on eight (one and four slower: the
+  // exchanges' fixed costs against the expert stage's overlap)
+  ctx->ep_chunks = world >= 4 ? 2 : 1;
   WMOE_CHECK_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->ep_stream, cudaStreamNonBlocking), "wmoe_ep_init");
   ctx->ep_events.assign(1 + 3 * kMaxEpChunks, nullptr);
   for (cudaEvent_t& e : ctx->ep_events)
@@ -1136,8 +1139,15 @@ static int ep_setup_windows(wmoe_ctx* ctx) {
                   "wmoe_ep_init");
   WMOE_CHECK_CUDA(ctx, cudaMallocHost(&ctx->ep_host_handles, size_t(kMaxRanks) * sizeof(cudaIpcMemHandle_t)),
                   "wmoe_ep_init");
-  ctx->ep_ipc = std::getenv("WMOE_EP_NCCL_ROWS") == nullptr;  // the NCCL send/recv path, for comparison
+  // the rows' exchange: copy engines into the peers' windows, or NCCL send/recv (WMOE_EP_NCCL_ROWS); the environment
+  // decides, read here once
+  ctx->ep_ipc = std::getenv("WMOE_EP_NCCL_ROWS") == nullptr;
   return WMOE_OK;
+}
+
+int wmoe_ep_uses_copy_engines(const wmoe_ctx* ctx) {
+  if (!ctx || !ctx->nccl_comm) return -1;
+  return ctx->ep_ipc ? 1 : 0;
 }
 
 // The exchanges' barrier: a one-int all-reduce on stream st. Every rank issues it after its copies into the peers'

@@ -73,6 +73,7 @@ SIGNATURES = {
     "wmoe_ep_init": (_i, [_p, _p, _i, _i]),
     "wmoe_ep_finalize": (_i, [_p]),
     "wmoe_ep_set_chunks": (_i, [_p, _i]),
+    "wmoe_ep_uses_copy_engines": (_i, [_p]),
     "wmoe_moe_forward_ep": (_i, [_p, _p, _i, _p, _i, _i, _i, _p, _p, _i, _p, _p, _p]),
 }
 
