@@ -33,6 +33,10 @@ def test_library_rejects_bad_arguments_without_a_gpu():
     # null output handle: refused before touching CUDA
     assert L.lib.wmoe_init(0, None) == L.ERR_INVALID
     assert L.lib.wmoe_dequant(None, L.GGML_Q4_K, None, 0, None, L.F32, None) == L.ERR_INVALID
+    assert L.lib.wmoe_prefill_stack(None, None, 0, 1, None, L.ctypes.c_float(1e-6), None, 4, L.BF16, None,
+                                    None) == L.ERR_INVALID
+    assert L.lib.wmoe_expert_gate(None, None, 1, 512, None, None) == L.ERR_INVALID
+    assert L.lib.wmoe_ep_uses_copy_engines(None) == -1
     assert L.lib.wmoe_store_blob_bytes(None) == 0
     assert L.lib.wmoe_launch_count(None) == 0
 

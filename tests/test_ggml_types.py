@@ -108,6 +108,24 @@ def test_wrappers_refuse_bad_arguments_without_a_gpu():
         ggml.gemv_combine(raw, "Q8_0", (64, 256), x, [0], w, [4])
     with pytest.raises(ValueError, match="CUDA"):
         ggml.dequantize_gpu(raw, "Q8_0", (64, 256))
+    # the one-call expert step (engines/base.py:492-532) and expert_gate
+    gu_b, dn_b = 2 * 128 * ggml.row_bytes("Q8_0", 256), 256 * ggml.row_bytes("Q8_0", 128)
+    slab = torch.zeros(2 * (gu_b + dn_b), dtype=torch.uint8)
+    xb = torch.zeros(256, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="at least one"):
+        ggml.batched_decode_experts(slab, "Q8_0", "Q8_0", 128, xb, [0], [], w, [0])
+    with pytest.raises(ValueError, match="gate_up offset"):
+        ggml.batched_decode_experts(slab, "Q8_0", "Q8_0", 128, xb, [slab.numel()], [gu_b], w, [0])
+    with pytest.raises(ValueError, match="down offset"):
+        ggml.batched_decode_experts(slab, "Q8_0", "Q8_0", 128, xb, [0], [slab.numel() - 1], w, [0])
+    with pytest.raises(ValueError, match="perm entry outside"):
+        ggml.batched_decode_experts(slab, "Q8_0", "Q8_0", 128, xb, [0], [gu_b], w, [4])
+    with pytest.raises(ValueError, match="CUDA"):
+        ggml.batched_decode_experts(slab, "Q8_0", "Q8_0", 128, xb, [0], [gu_b], w, [3])
+    with pytest.raises(ValueError, match="bf16"):
+        ggml.expert_gate(torch.zeros(2, 64))
+    with pytest.raises(ValueError, match="CUDA"):
+        ggml.expert_gate(torch.zeros(2, 64, dtype=torch.bfloat16))
     with pytest.raises(NotImplementedError, match="Q4_0"):
         ggml.dequantize_gpu(raw, "Q4_0", (64, 256))
     # f16 activations widen to f32 (exact) rather than rounding to bf16

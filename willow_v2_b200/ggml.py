@@ -243,7 +243,7 @@ def batched_decode_experts(base: torch.Tensor, gate_up_type: str, down_type: str
     is expert i's [2 * ffn, hidden] gate_up matrix of gate_up_type and down_offsets[i] its [hidden, ffn] down matrix
     of down_type, byte offsets in base (uint8, on the GPU); x bf16 [hidden]; routing_weights bf16 [top_k], perm[i]
     the slot of expert i's weight in it. Returns bf16 [1, hidden] (written into out when given), the value of
-    gemv_batch, expert_gate and gemv_combine run one after another. The library checks the perm entries."""
+    gemv_batch, expert_gate and gemv_combine run one after another."""
     n = len(gate_up_offsets)
     if n == 0 or len(down_offsets) != n or len(perm) != n:
         raise ValueError("one down offset and one perm entry per gate_up offset, at least one")
@@ -260,6 +260,8 @@ def batched_decode_experts(base: torch.Tensor, gate_up_type: str, down_type: str
         raise ValueError("a gate_up offset puts its matrix outside base")
     if min(down_offsets) < 0 or max(down_offsets) + dn_bytes > size:
         raise ValueError("a down offset puts its matrix outside base")
+    if min(perm) < 0 or max(perm) >= w.numel():
+        raise ValueError("a perm entry outside routing_weights")
     dev = base.device
     if not (base.is_cuda and x.device == dev and w.device == dev):
         raise ValueError("base, x and routing_weights must be CUDA tensors on one device")
