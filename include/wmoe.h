@@ -346,7 +346,8 @@ int wmoe_decode_stack_noalloc(wmoe_ctx* ctx, wmoe_store* store, int layer_begin,
  * WMOE_F32) and computes as wmoe_moe_forward_layer does, min_expert_weight included. h_in / h_out: f32 [T, hidden]
  * on the device, 16-byte aligned, may alias. layers: HOST array of n_layers entries of device pointers.
  *   - After wmoe_ep_init every layer runs as wmoe_moe_forward_ep does, over the context's communicator: the store
- *     holds this rank's block of the experts (wmoe_store_create_range) and every rank calls with its own tokens.
+ *     holds this rank's block of the experts (wmoe_store_create_range) and every rank calls with its own tokens
+ *     (T may be 0: the rank still takes part in every layer's exchanges).
  *   - A capped store starts copying the next layer's experts (wmoe_store_prefetch with its guess) once a layer is
  *     issued, and the first layer's after the last.
  *   - One f32 token on a resident store runs wmoe_decode_stack.

@@ -165,10 +165,13 @@ def _stack_rank(rank, world, port, outdir):
         for chunks in (1, 2):  # the result does not depend on the chunking
             lib.wmoe_ep_set_chunks(ctx.handle, chunks)
             outs.append(moe.prefill_stack(store, lws, h))
+        # a rank without tokens still takes part in every layer's exchanges; the other ranks' rows do not change
+        part = moe.prefill_stack(store, lws, h[:0] if rank == world - 1 and world > 1 else h)
         torch.cuda.synchronize()
         ctx.check_device()
         ctx.ep_finalize()
         assert torch.equal(outs[0], outs[1])
+        assert part.shape[0] == 0 if rank == world - 1 and world > 1 else torch.equal(part, outs[0])
         np.save(os.path.join(outdir, f"stack{rank}.npy"), outs[0].cpu().numpy())
         dist.barrier()
     finally:

@@ -1654,14 +1654,22 @@ int wmoe_prefill_stack(wmoe_ctx* ctx, wmoe_store* store, int layer_begin, int n_
   if (layer_begin < 0 || n_layers <= 0 || layer_begin + n_layers > store->layers || !layers || T < 0 ||
       !(eps >= 0.f) || (x_dtype != WMOE_F32 && x_dtype != WMOE_BF16))
     return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: bad arguments");
-  if (T == 0) return WMOE_OK;
-  if (!h_in || !h_out) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: null pointer");
-  if (!aligned16(h_in) || !aligned16(h_out))
-    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: h_in and h_out must be 16-byte aligned");
   for (int i = 0; i < n_layers; ++i)
     if (int rc = check_layer(ctx, &layers[i], "wmoe_prefill_stack")) return rc;
   // after wmoe_ep_init every layer runs over the context's expert-parallel communicator
   const bool ep = ctx->nccl_comm != nullptr;
+  if (T == 0) {
+    if (!ep) return WMOE_OK;
+    // a rank without tokens still takes part in every layer's exchanges
+    for (int i = 0; i < n_layers; ++i)
+      if (int rc = moe_forward_ep_impl(ctx, store, layer_begin + i, nullptr, x_dtype, 0, 8, &layers[i], nullptr,
+                                       x_dtype, nullptr, nullptr, stream, nullptr))
+        return rc;
+    return WMOE_OK;
+  }
+  if (!h_in || !h_out) return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: null pointer");
+  if (!aligned16(h_in) || !aligned16(h_out))
+    return ctx_fail(ctx, WMOE_ERR_INVALID, "wmoe_prefill_stack: h_in and h_out must be 16-byte aligned");
   if (!ep && T == 1 && x_dtype == WMOE_F32 && !store->capped && ctx->use_decode_kernel &&
       ctx->decode_ctas > 0 && store->experts == 256) {
     bool packed = true;
